@@ -1,0 +1,275 @@
+/*
+ * phyzb.h — C ABI of the B200 batched rigid-body stepper (libphyzb200.so).
+ *
+ * This is the drop-in boundary for phyz-gpu's batched-simulation path: one
+ * opaque handle owns every device buffer of N independent worlds of one
+ * articulated model, exactly as `phyz_gpu::cuda::BatchSim` does
+ * (crates/phyz-gpu/src/cuda/mod.rs:430-468), and each entry point below
+ * replaces one method of that type. Host arrays are caller-owned and copied
+ * in and out; world-major f64 rows, as phyz's `State` packs them
+ * (crates/phyz-gpu/src/layout.rs:340-372).
+ *
+ * Conventions (mirroring the reference's `Result<_, String>`):
+ *   - every function returns PHYZB_OK (0) or a negative PHYZB_ERR_* code;
+ *   - the message of the last failure on the calling thread is returned by
+ *     phyzb_last_error() (thread-local, valid until the next failing call);
+ *   - one handle is driven by one host thread at a time;
+ *   - nothing here allocates except phyzb_create / phyzb_enable_* (device
+ *     buffers) and the staging used by the *_host bulk copies;
+ *   - no call ever traps the GPU: device-side failures (non-finite state)
+ *     are recorded in a status word that phyzb_status() reads.
+ *
+ * Joint, geometry and DOF conventions are phyz's:
+ *   - joint types use the packed-body-table codes of layout.rs:23;
+ *   - free-joint q = [exp-coords(3), pos(3)], v = [angular(3), linear(3)]
+ *     (crates/phyz-model/src/joint.rs:278-306); nq == nv;
+ *   - bodies are topologically sorted (parent < child), body i owns joint i;
+ *   - ground contact is Z-up (phyz_kernels.cu:641-643).
+ */
+#ifndef PHYZB_H
+#define PHYZB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PHYZB_ABI_VERSION 1
+
+/* ── status codes ─────────────────────────────────────────────────────── */
+#define PHYZB_OK 0
+#define PHYZB_ERR_INVALID (-1)     /* bad argument or model */
+#define PHYZB_ERR_CUDA (-2)        /* CUDA runtime call failed */
+#define PHYZB_ERR_NO_DEVICE (-3)   /* no CUDA device / driver */
+#define PHYZB_ERR_STATE (-4)       /* call not valid in this state (e.g. contact off) */
+#define PHYZB_ERR_NONFINITE (-5)   /* a world's state went non-finite on device */
+#define PHYZB_ERR_TOO_LARGE (-6)   /* model does not fit the kernel's limits */
+#define PHYZB_ERR_UNSUPPORTED (-7) /* feature outside the implemented path */
+
+/* ── enums ────────────────────────────────────────────────────────────── */
+/* Joint codes: crates/phyz-gpu/src/layout.rs:23 ([1] joint_type). */
+#define PHYZB_JOINT_REVOLUTE 0
+#define PHYZB_JOINT_PRISMATIC 1
+#define PHYZB_JOINT_FIXED 2
+#define PHYZB_JOINT_BALL 3
+#define PHYZB_JOINT_FREE 4
+
+/* Geometry codes: crates/phyz-gpu/src/layout.rs:42 ([0] geom_type). */
+#define PHYZB_GEOM_NONE 0
+#define PHYZB_GEOM_SPHERE 1
+#define PHYZB_GEOM_BOX 2
+#define PHYZB_GEOM_CAPSULE 3
+#define PHYZB_GEOM_CYLINDER 4
+#define PHYZB_GEOM_MESH_AABB 5
+
+/* Device precision of a simulator. The host-side arrays stay f64. */
+#define PHYZB_F32 0
+#define PHYZB_F64 1
+
+/* Element type of a host bulk buffer (phyzb_step_with_controls). */
+#define PHYZB_HOST_F32 0
+#define PHYZB_HOST_F64 1
+
+/* Maximum bodies per world (layout.rs:100 MAX_BODIES). */
+#define PHYZB_MAX_BODIES 32
+/* Maximum DOFs per world (every body a free joint would be 192; the
+ * kernels bound nv by this). */
+#define PHYZB_MAX_DOFS 64
+
+/* Floats per body in phyzb_readback_contacts output: touching, depth,
+ * point[3], force[3] — the first 8 slots of layout.rs:68-80. */
+#define PHYZB_CONTACT_STRIDE 8
+
+/* ── model description ────────────────────────────────────────────────── */
+
+/* One body and the joint that attaches it to its parent. Field meanings are
+ * phyz's: phyz_model::Body (crates/phyz-model/src/body.rs:8-56) with its
+ * SpatialInertia about the COM, and phyz_model::Joint
+ * (crates/phyz-model/src/joint.rs:28-70). */
+typedef struct phyzb_body {
+    int32_t parent;     /* -1 for a root attached to the world */
+    int32_t joint_type; /* PHYZB_JOINT_* */
+    double mass;
+    double com[3];      /* centre of mass, body frame */
+    double inertia[6];  /* rotational inertia about the COM: xx, yy, zz, xy, xz, yz */
+    double ptj_rot[9];  /* parent->joint coordinate rotation, row-major */
+    double ptj_pos[3];  /* joint origin in parent coordinates */
+    double axis[3];     /* hinge / slide axis, joint frame */
+    double damping;     /* viscous: f = -damping * qd, implicit in D */
+    double stiffness;   /* passive spring (1-DOF): f = -k (q - spring_ref) */
+    double spring_ref;
+    double armature;    /* rotor inertia on the D diagonal */
+    int32_t has_limits; /* 1-DOF soft limits (joint.rs:184-230) */
+    double limit_lower, limit_upper;
+    double limit_stiffness, limit_damping;
+    double friction_loss; /* smoothed Coulomb: -mu tanh(qd / 1e-3) (joint.rs:240-245) */
+    /* primary collision shape (layout.rs:38-52 semantics) */
+    int32_t geom_type;          /* PHYZB_GEOM_* */
+    double geom_params[6];      /* sphere r | box hx,hy,hz | capsule r,len | cylinder r,h | mesh min[3],max[3] */
+    double geom_origin_pos[3];  /* shape origin, body frame */
+    double geom_origin_rot[9];  /* body -> shape coordinates, row-major */
+} phyzb_body;
+
+/* The model shared by every world: phyz_model::Model
+ * (crates/phyz-model/src/model.rs:124-150) restricted to what the batched
+ * path reads. */
+typedef struct phyzb_model {
+    int32_t nbodies;
+    double gravity[3];
+    double dt;
+    const phyzb_body* bodies; /* nbodies entries */
+} phyzb_model;
+
+/* One PD-servoed DOF: phyz_gpu::PdDof (crates/phyz-gpu/src/pd_pipeline.rs,
+ * packed by layout.rs:300-312). */
+typedef struct phyzb_pd_dof {
+    int32_t q_index;
+    int32_t v_index;
+    double kp, kd, max_force;
+} phyzb_pd_dof;
+
+typedef struct phyzb_sim phyzb_sim; /* opaque */
+
+/* Device view of a simulator's resident state, for zero-copy callers
+ * (torch tensors, other kernels). All arrays are structure-of-arrays:
+ * element (world w, dof j) of q lives at q[j * nworld + w]. */
+typedef struct phyzb_device_view {
+    void* q;        /* nv x nworld */
+    void* v;        /* nv x nworld */
+    void* ctrl;     /* nv x nworld */
+    void* qdd;      /* nv x nworld, accelerations of the last step */
+    int64_t nworld;
+    int32_t nv;
+    int32_t nbodies;
+    int32_t precision; /* PHYZB_F32 / PHYZB_F64 */
+    int32_t device;
+    void* stream;   /* cudaStream_t the simulator launches on */
+} phyzb_device_view;
+
+/* ── library ──────────────────────────────────────────────────────────── */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* phyzb_last_error(void);
+/* PHYZB_ABI_VERSION. */
+int phyzb_abi_version(void);
+/* Number of visible CUDA devices (0 without a driver; never fails). */
+int phyzb_device_count(void);
+
+/* ── lifecycle ────────────────────────────────────────────────────────── */
+
+/* BatchSim::on_device (cuda/mod.rs:482-485, 497-541): validate the model
+ * (nb <= PHYZB_MAX_BODIES, topological order, finite parameters), allocate
+ * q/v/ctrl/qdd for `nworld` worlds on `device`, zero them.
+ * Errors: PHYZB_ERR_NO_DEVICE without a driver, PHYZB_ERR_TOO_LARGE past
+ * the body limit, PHYZB_ERR_INVALID on a malformed model. */
+int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int precision,
+                 phyzb_sim** out);
+/* Drop (frees every device buffer). NULL is a no-op. */
+int phyzb_destroy(phyzb_sim* sim);
+/* BatchSim::set_model (cuda/mod.rs:573-594): same body count and DOF
+ * widths, new parameters. Re-run phyzb_enable_* after it if geometry or
+ * gains changed too. */
+int phyzb_set_model(phyzb_sim* sim, const phyzb_model* model);
+
+/* ── contact ──────────────────────────────────────────────────────────── */
+
+/* BatchSim::enable_ground_contact (cuda/mod.rs:601-621): penalty ground
+ * contact, one global stiffness/damping. Writes the collidable-body count;
+ * PHYZB_ERR_INVALID when no body has a supported shape
+ * (layout.rs:282-297). */
+int phyzb_enable_ground_contact(phyzb_sim* sim, double ground_height, double stiffness,
+                                double damping, double friction, int32_t* collidable_out);
+/* BatchSim::enable_ground_contact_per_body (cuda/mod.rs:627-634): per-body
+ * gains (nbodies entries each). */
+int phyzb_enable_ground_contact_per_body(phyzb_sim* sim, double ground_height,
+                                         double friction, const double* stiffness,
+                                         const double* damping, int32_t* collidable_out);
+/* Turn contact off again (ext forces zero). */
+int phyzb_disable_contact(phyzb_sim* sim);
+/* BatchSim::collidable_bodies (cuda/mod.rs:999-1001): 0 when disabled. */
+int phyzb_collidable_bodies(const phyzb_sim* sim);
+
+/* ── PD servos ────────────────────────────────────────────────────────── */
+
+/* BatchSim::enable_pd_control (cuda/mod.rs:771-790); check_pd_dofs
+ * (layout.rs:300-315) rules. */
+int phyzb_enable_pd(phyzb_sim* sim, const phyzb_pd_dof* dofs, int32_t n);
+/* BatchSim::set_position_targets (cuda/mod.rs:793-801): nworld x n rows. */
+int phyzb_set_position_targets(phyzb_sim* sim, const double* targets);
+
+/* ── state ────────────────────────────────────────────────────────────── */
+
+/* BatchSim::load_states (cuda/mod.rs:804-812): world-major q, v (nworld x
+ * nv) and ctrl (nworld x nv, NULL = zero). */
+int phyzb_load_states(phyzb_sim* sim, const double* q, const double* v, const double* ctrl);
+/* BatchSim::set_controls (cuda/mod.rs:815-821): nworld x nv, held across
+ * steps until replaced. */
+int phyzb_set_controls(phyzb_sim* sim, const double* ctrl);
+
+/* ── stepping ─────────────────────────────────────────────────────────── */
+
+/* BatchSim::step_many(n) (cuda/mod.rs:843-875): n steps of
+ * PD -> contact -> ABA -> integrate, run as one fused launch that keeps
+ * each world's state on chip across the n steps. Asynchronous on the
+ * simulator's stream; n == 0 is a no-op. */
+int phyzb_step(phyzb_sim* sim, int32_t n);
+/* n steps whose controls change every step: `ctrl` holds n x nworld x nv
+ * world-major rows of element type `host_dtype` (PHYZB_HOST_F32/F64) in
+ * host memory (pinned memory overlaps the copies with the kernels). Same
+ * result as n x (phyzb_set_controls(row t); phyzb_step(1)). On return the
+ * ctrl buffer holds the last row, as after that loop. */
+int phyzb_step_with_controls(phyzb_sim* sim, const void* ctrl, int host_dtype, int32_t n);
+/* Block until every launch on the simulator's stream has finished, then
+ * report the device status word (PHYZB_ERR_NONFINITE if any world went
+ * non-finite since the last phyzb_clear_status). */
+int phyzb_sync(phyzb_sim* sim);
+int phyzb_status(phyzb_sim* sim);
+int phyzb_clear_status(phyzb_sim* sim);
+
+/* ── readback ─────────────────────────────────────────────────────────── */
+
+/* BatchSim::readback_states (cuda/mod.rs:978-983): world-major q, v. */
+int phyzb_readback_states(phyzb_sim* sim, double* q, double* v);
+/* Joint accelerations of the last step, world-major (no reference
+ * counterpart: the reference keeps qdd on device; needed for qdd parity). */
+int phyzb_readback_qdd(phyzb_sim* sim, double* qdd);
+/* BatchSim::readback_contacts (cuda/mod.rs:987-996): nworld x nbodies x
+ * PHYZB_CONTACT_STRIDE of the last step. PHYZB_ERR_STATE if contact off. */
+int phyzb_readback_contacts(phyzb_sim* sim, double* contact_state);
+
+/* ── device-resident path ─────────────────────────────────────────────── */
+
+/* Device pointers and layout of the resident state (zero-copy). */
+int phyzb_device_view_get(phyzb_sim* sim, phyzb_device_view* out);
+/* Launch on a caller-provided stream (a cudaStream_t; NULL = the
+ * simulator's own stream). */
+int phyzb_set_stream(phyzb_sim* sim, void* stream);
+/* n fused steps whose per-step controls are read from a device-resident
+ * schedule laid out [n][nv][nworld] (SoA, the simulator's precision,
+ * `step_stride` elements between consecutive steps, >= nv*nworld).
+ * Asynchronous. The device-side equivalent of phyzb_step_with_controls. */
+int phyzb_step_device_controls(phyzb_sim* sim, const void* ctrl_schedule, int64_t step_stride,
+                               int32_t n);
+/* Sum over worlds of a per-world objective into a device scalar (the
+ * simulator's precision): kind 0 = kinetic energy 0.5 v.M(q).v computed
+ * body-wise, kind 1 = sum of squared joint positions. The value a
+ * multi-GPU job all-reduces at the end of a rollout. */
+int phyzb_objective_device(phyzb_sim* sim, int kind, void* out_device_scalar);
+
+/* ── measurement helpers (no reference counterpart) ───────────────────── */
+
+/* Algorithmic flop count of one world-step of this simulator's model and
+ * settings, as executed by the kernel's formulation (add/sub/mul = 1,
+ * fma = 2, div = 1), with transcendental calls tallied separately. */
+int phyzb_flops_per_world_step(const phyzb_sim* sim, double* flops, double* transcendentals);
+/* Launch configuration the fused kernel uses for this simulator. */
+int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
+                      int32_t* smem_bytes, int32_t* scratch_per_world);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PHYZB_H */

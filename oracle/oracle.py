@@ -1,0 +1,210 @@
+"""TEST INFRASTRUCTURE ONLY — ctypes face of the CPU checkers.
+
+* `Oracle`: the f64 C++ restatement of phyz's CPU path (phyz_oracle.hpp,
+  built into _build/libphyz_oracle.so).
+* `RefHost`: the reference's own crates/phyz-gpu/cuda/phyz_kernels.cu
+  compiled as host C++ (f32), built into _ref/libphyz_ref_host.so by the
+  Makefile from the reference tree; the prebuilt object travels with the
+  repository snapshot, the reference tree does not.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs use
+this module, and only as the checker / the timed CPU reference.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ORACLE_SO = HERE / "_build" / "libphyz_oracle.so"
+REF_SO = HERE / "_ref" / "libphyz_ref_host.so"
+
+_D = C.POINTER(C.c_double)
+_F = C.POINTER(C.c_float)
+_I = C.POINTER(C.c_int32)
+
+
+def build() -> None:
+    """Run the Makefile (oracle always; the reference build when its tree exists)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _d(a):
+    return None if a is None else a.ctypes.data_as(_D)
+
+
+def _f(a):
+    return None if a is None else a.ctypes.data_as(_F)
+
+
+class Oracle:
+    def __init__(self):
+        if not ORACLE_SO.exists():
+            build()
+        self.lib = C.CDLL(str(ORACLE_SO))
+        L = self.lib
+        MP = C.c_void_p
+        L.oracle_aba.argtypes = [MP, C.c_int64, _D, _D, _D, _D, _D]
+        L.oracle_rnea.argtypes = [MP, C.c_int64, _D, _D, _D, _D]
+        L.oracle_integrate_configuration.argtypes = [MP, C.c_int64, _D, _D, C.c_double]
+        L.oracle_forward_kinematics.argtypes = [MP, C.c_int64, _D, _D, _D, _D]
+        L.oracle_energy.argtypes = [MP, C.c_int64, _D, _D, _D, _D]
+        L.oracle_penalty_contact.argtypes = [MP, C.c_int64, _D, _D, C.c_double, C.c_double, _D, _D, _D, _D]
+        L.oracle_rollout.argtypes = [MP, C.c_int64, _D, _D, _D, C.c_int64, C.c_int32, C.c_int32, C.c_double,
+                                     C.c_double, _D, _D, C.c_int32, _I, _D, _D, _D, _D, C.c_int32]
+        for f in ("oracle_aba", "oracle_rnea", "oracle_integrate_configuration", "oracle_forward_kinematics",
+                  "oracle_energy", "oracle_penalty_contact", "oracle_rollout"):
+            getattr(L, f).restype = C.c_int
+
+    @staticmethod
+    def _m(model):
+        cm, keep = model.to_c()
+        return cm, keep
+
+    def aba(self, model, q, v, ctrl=None, ext=None):
+        cm, keep = self._m(model)
+        q, v = np.ascontiguousarray(q, np.float64), np.ascontiguousarray(v, np.float64)
+        ctrl = None if ctrl is None else np.ascontiguousarray(ctrl, np.float64)
+        ext = None if ext is None else np.ascontiguousarray(ext, np.float64)
+        out = np.zeros_like(q)
+        self.lib.oracle_aba(C.addressof(cm), q.shape[0], _d(q), _d(v), _d(ctrl), _d(ext), _d(out))
+        return out
+
+    def rnea(self, model, q, v, qdd):
+        cm, keep = self._m(model)
+        q, v, qdd = (np.ascontiguousarray(a, np.float64) for a in (q, v, qdd))
+        out = np.zeros_like(q)
+        self.lib.oracle_rnea(C.addressof(cm), q.shape[0], _d(q), _d(v), _d(qdd), _d(out))
+        return out
+
+    def integrate_configuration(self, model, q, v, dt):
+        cm, keep = self._m(model)
+        q = np.array(q, np.float64, copy=True, order="C")
+        v = np.ascontiguousarray(v, np.float64)
+        self.lib.oracle_integrate_configuration(C.addressof(cm), q.shape[0], _d(q), _d(v), dt)
+        return q
+
+    def forward_kinematics(self, model, q, v):
+        cm, keep = self._m(model)
+        q, v = np.ascontiguousarray(q, np.float64), np.ascontiguousarray(v, np.float64)
+        n, nb = q.shape[0], model.nbodies
+        xw = np.zeros((n, nb, 12))
+        vel = np.zeros((n, nb, 6))
+        self.lib.oracle_forward_kinematics(C.addressof(cm), n, _d(q), _d(v), _d(xw), _d(vel))
+        return xw, vel
+
+    def energy(self, model, q, v):
+        cm, keep = self._m(model)
+        q, v = np.ascontiguousarray(q, np.float64), np.ascontiguousarray(v, np.float64)
+        ke, pe = np.zeros(q.shape[0]), np.zeros(q.shape[0])
+        self.lib.oracle_energy(C.addressof(cm), q.shape[0], _d(q), _d(v), _d(ke), _d(pe))
+        return ke, pe
+
+    def penalty_contact(self, model, q, v, ground, friction, k, d):
+        cm, keep = self._m(model)
+        q, v = np.ascontiguousarray(q, np.float64), np.ascontiguousarray(v, np.float64)
+        n, nb = q.shape[0], model.nbodies
+        k = np.ascontiguousarray(np.broadcast_to(k, (nb,)), np.float64)
+        d = np.ascontiguousarray(np.broadcast_to(d, (nb,)), np.float64)
+        ext = np.zeros((n, nb, 6))
+        cs = np.zeros((n, nb, 8))
+        self.lib.oracle_penalty_contact(C.addressof(cm), n, _d(q), _d(v), ground, friction, _d(k), _d(d),
+                                        _d(ext), _d(cs))
+        return ext, cs
+
+    def rollout(self, model, q, v, ctrl=None, nsteps=1, schedule=False, contact=None, pd=None, targets=None,
+                nthreads=1):
+        """nsteps of [PD ->] [contact ->] ABA -> semi-implicit Euler.
+        ctrl: (nworld, nv) held, or with schedule=True (nsteps, nworld, nv).
+        contact: (ground, friction, k[nb], d[nb]); pd: list of PdDof."""
+        cm, keep = self._m(model)
+        q = np.array(q, np.float64, copy=True, order="C")
+        v = np.array(v, np.float64, copy=True, order="C")
+        n, nv, nb = q.shape[0], model.nv, model.nbodies
+        stride = 0
+        if ctrl is not None:
+            ctrl = np.ascontiguousarray(ctrl, np.float64)
+            stride = n * nv if schedule else 0
+        qdd = np.zeros((n, nv))
+        cs = np.zeros((n, nb, 8))
+        has_c = contact is not None
+        g, fr, k, d = (contact if has_c else (0.0, 0.0, None, None))
+        if has_c:
+            k = np.ascontiguousarray(np.broadcast_to(k, (nb,)), np.float64)
+            d = np.ascontiguousarray(np.broadcast_to(d, (nb,)), np.float64)
+        npd = 0
+        pidx = pg = tg = None
+        if pd:
+            npd = len(pd)
+            pidx = np.ascontiguousarray([[p.q_index, p.v_index] for p in pd], np.int32)
+            pg = np.ascontiguousarray([[p.kp, p.kd, p.max_force] for p in pd], np.float64)
+            tg = np.ascontiguousarray(targets, np.float64)
+        self.lib.oracle_rollout(C.addressof(cm), n, _d(q), _d(v), _d(ctrl), stride, nsteps, int(has_c), g, fr,
+                                _d(k), _d(d), npd, None if pidx is None else pidx.ctypes.data_as(_I), _d(pg),
+                                _d(tg), _d(qdd), _d(cs), nthreads)
+        return q, v, qdd, cs
+
+
+class RefHost:
+    """The reference's f32 kernels compiled as host C++ (phyz_host_*)."""
+
+    BODY_STRIDE, GEOM_STRIDE, PD_STRIDE = 36, 24, 8
+
+    def __init__(self):
+        if not REF_SO.exists():
+            build()
+        if not REF_SO.exists():
+            raise RuntimeError(f"{REF_SO} missing and the reference tree is not available to build it")
+        self.lib = C.CDLL(str(REF_SO))
+        L = self.lib
+        L.phyzref_pack_bodies.argtypes = [C.c_void_p, _F]
+        L.phyzref_pack_geometries.argtypes = [C.c_void_p, _D, _D, _F]
+        L.phyzref_rollout.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
+                                      C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, C.c_uint32, _F, _F,
+                                      _F, _F, _F, C.c_int64, C.c_int32, _F, _F]
+
+    def rollout(self, model, q, v, ctrl, nsteps=1, schedule=False, contact=None, pd=None, targets=None,
+                nthreads=1):
+        cm, keep = model.to_c()
+        nb, nv = model.nbodies, model.nv
+        bodies = np.zeros(nb * self.BODY_STRIDE, np.float32)
+        self.lib.phyzref_pack_bodies(C.addressof(cm), _f(bodies))
+        geom = None
+        ground = fr = 0.0
+        if contact is not None:
+            ground, fr, k, d = contact
+            k = np.ascontiguousarray(np.broadcast_to(k, (nb,)), np.float64)
+            d = np.ascontiguousarray(np.broadcast_to(d, (nb,)), np.float64)
+            geom = np.zeros(nb * self.GEOM_STRIDE, np.float32)
+            self.lib.phyzref_pack_geometries(C.addressof(cm), _d(k), _d(d), _f(geom))
+        n = q.shape[0]
+        qf = np.ascontiguousarray(q, np.float32).copy()
+        vf = np.ascontiguousarray(v, np.float32).copy()
+        cf = np.ascontiguousarray(ctrl, np.float32)
+        stride = n * nv if schedule else 0
+        npd = 0
+        tbl = tg = None
+        if pd:
+            npd = len(pd)
+            tbl = np.zeros(npd * self.PD_STRIDE, np.float32)
+            for i, p in enumerate(pd):
+                tbl[i * self.PD_STRIDE: i * self.PD_STRIDE + 5] = [p.q_index, p.v_index, p.kp, p.kd, p.max_force]
+            tg = np.ascontiguousarray(targets, np.float32)
+        qdd = np.zeros((n, nv), np.float32)
+        cs = np.zeros((n, nb, 8), np.float32)
+        gx, gy, gz = (float(x) for x in model.gravity)
+        self.lib.phyzref_rollout(nthreads, n, nv, nb, float(model.dt), gx, gy, gz, _f(bodies), _f(geom),
+                                 float(ground), float(fr), npd, _f(tbl), _f(tg), _f(qf), _f(vf), _f(cf), stride,
+                                 nsteps, _f(qdd), _f(cs))
+        return qf, vf, qdd, cs
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1

@@ -1,0 +1,8 @@
+"""phyz_b200 — a B200-native batched rigid-body stepper with phyz-gpu's
+batched-simulation API (BatchSim) over the C ABI of libphyzb200.so."""
+from ._lib import PhyzbError
+from .batch_sim import BatchSim, BodyContactGains, PdDof
+from .model import Geometry, Joint, Model, ModelBuilder, SpatialInertia, Transform
+
+__all__ = ["BatchSim", "BodyContactGains", "PdDof", "PhyzbError", "Geometry", "Joint", "Model",
+           "ModelBuilder", "SpatialInertia", "Transform"]

@@ -1,0 +1,176 @@
+"""ctypes binding of libphyzb200.so (include/phyzb.h).
+
+Loading fails loudly: there is no CPU fallback for any entry point. The
+struct layouts below mirror include/phyzb.h field for field.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libphyzb200.so"
+
+PHYZB_OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_NO_DEVICE = -3
+ERR_STATE = -4
+ERR_NONFINITE = -5
+ERR_TOO_LARGE = -6
+ERR_UNSUPPORTED = -7
+
+F32 = 0
+F64 = 1
+HOST_F32 = 0
+HOST_F64 = 1
+MAX_BODIES = 32
+MAX_DOFS = 64
+CONTACT_STRIDE = 8
+
+JOINT_REVOLUTE, JOINT_PRISMATIC, JOINT_FIXED, JOINT_BALL, JOINT_FREE = 0, 1, 2, 3, 4
+GEOM_NONE, GEOM_SPHERE, GEOM_BOX, GEOM_CAPSULE, GEOM_CYLINDER, GEOM_MESH_AABB = 0, 1, 2, 3, 4, 5
+
+
+class PhyzbBody(C.Structure):
+    _fields_ = [
+        ("parent", C.c_int32),
+        ("joint_type", C.c_int32),
+        ("mass", C.c_double),
+        ("com", C.c_double * 3),
+        ("inertia", C.c_double * 6),
+        ("ptj_rot", C.c_double * 9),
+        ("ptj_pos", C.c_double * 3),
+        ("axis", C.c_double * 3),
+        ("damping", C.c_double),
+        ("stiffness", C.c_double),
+        ("spring_ref", C.c_double),
+        ("armature", C.c_double),
+        ("has_limits", C.c_int32),
+        ("limit_lower", C.c_double),
+        ("limit_upper", C.c_double),
+        ("limit_stiffness", C.c_double),
+        ("limit_damping", C.c_double),
+        ("friction_loss", C.c_double),
+        ("geom_type", C.c_int32),
+        ("geom_params", C.c_double * 6),
+        ("geom_origin_pos", C.c_double * 3),
+        ("geom_origin_rot", C.c_double * 9),
+    ]
+
+
+class PhyzbModel(C.Structure):
+    _fields_ = [
+        ("nbodies", C.c_int32),
+        ("gravity", C.c_double * 3),
+        ("dt", C.c_double),
+        ("bodies", C.POINTER(PhyzbBody)),
+    ]
+
+
+class PhyzbPdDof(C.Structure):
+    _fields_ = [
+        ("q_index", C.c_int32),
+        ("v_index", C.c_int32),
+        ("kp", C.c_double),
+        ("kd", C.c_double),
+        ("max_force", C.c_double),
+    ]
+
+
+class PhyzbDeviceView(C.Structure):
+    _fields_ = [
+        ("q", C.c_void_p),
+        ("v", C.c_void_p),
+        ("ctrl", C.c_void_p),
+        ("qdd", C.c_void_p),
+        ("nworld", C.c_int64),
+        ("nv", C.c_int32),
+        ("nbodies", C.c_int32),
+        ("precision", C.c_int32),
+        ("device", C.c_int32),
+        ("stream", C.c_void_p),
+    ]
+
+
+_P = C.c_void_p
+_D = C.POINTER(C.c_double)
+_I32P = C.POINTER(C.c_int32)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "phyzb_last_error": (C.c_char_p, []),
+    "phyzb_abi_version": (C.c_int, []),
+    "phyzb_device_count": (C.c_int, []),
+    "phyzb_create": (C.c_int, [C.POINTER(PhyzbModel), C.c_int64, C.c_int, C.c_int, C.POINTER(_P)]),
+    "phyzb_destroy": (C.c_int, [_P]),
+    "phyzb_set_model": (C.c_int, [_P, C.POINTER(PhyzbModel)]),
+    "phyzb_enable_ground_contact": (C.c_int, [_P, C.c_double, C.c_double, C.c_double, C.c_double, _I32P]),
+    "phyzb_enable_ground_contact_per_body": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _I32P]),
+    "phyzb_disable_contact": (C.c_int, [_P]),
+    "phyzb_collidable_bodies": (C.c_int, [_P]),
+    "phyzb_enable_pd": (C.c_int, [_P, C.POINTER(PhyzbPdDof), C.c_int32]),
+    "phyzb_set_position_targets": (C.c_int, [_P, _D]),
+    "phyzb_load_states": (C.c_int, [_P, _D, _D, _D]),
+    "phyzb_set_controls": (C.c_int, [_P, _D]),
+    "phyzb_step": (C.c_int, [_P, C.c_int32]),
+    "phyzb_step_with_controls": (C.c_int, [_P, _P, C.c_int, C.c_int32]),
+    "phyzb_sync": (C.c_int, [_P]),
+    "phyzb_status": (C.c_int, [_P]),
+    "phyzb_clear_status": (C.c_int, [_P]),
+    "phyzb_readback_states": (C.c_int, [_P, _D, _D]),
+    "phyzb_readback_qdd": (C.c_int, [_P, _D]),
+    "phyzb_readback_contacts": (C.c_int, [_P, _D]),
+    "phyzb_device_view_get": (C.c_int, [_P, C.POINTER(PhyzbDeviceView)]),
+    "phyzb_set_stream": (C.c_int, [_P, _P]),
+    "phyzb_step_device_controls": (C.c_int, [_P, _P, C.c_int64, C.c_int32]),
+    "phyzb_objective_device": (C.c_int, [_P, C.c_int, _P]),
+    "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
+    "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P]),
+}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load the library (built by phyz_b200.build). Raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m phyz_b200.build` "
+            "(there is no CPU fallback for the stepper)"
+        )
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class PhyzbError(RuntimeError):
+    """A failing libphyzb200 call: `code` is the PHYZB_ERR_* value."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+def check(code: int) -> int:
+    if code < 0:
+        msg = load().phyzb_last_error().decode("utf-8", "replace")
+        raise PhyzbError(code, msg)
+    return code
+
+
+def dptr(a) -> C.POINTER(C.c_double):
+    """Pointer to a C-contiguous float64 numpy array."""
+    return a.ctypes.data_as(_D)
+
+
+def lib_path() -> str:
+    return os.fspath(LIB_PATH)

@@ -1,0 +1,239 @@
+"""BatchSim: the batched-simulation surface of phyz-gpu over libphyzb200.
+
+Method for method this mirrors phyz_gpu::cuda::BatchSim
+(crates/phyz-gpu/src/cuda/mod.rs:430-1377): build from a Model and a world
+count, optionally enable ground contact and PD servos, then
+load_states / set_controls / step / readback_states. Errors raise
+PhyzbError where the reference returns Err(String); `try_step` returns the
+error instead of raising, like the reference's try_step.
+
+Host arrays are numpy float64, world-major (nworld x width), as phyz's
+State rows (layout.rs:340-372).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import PhyzbError, check, dptr
+from .model import Model
+
+
+@dataclass
+class PdDof:
+    """phyz_gpu::PdDof (crates/phyz-gpu/src/pd_pipeline.rs)."""
+
+    q_index: int
+    v_index: int
+    kp: float
+    kd: float
+    max_force: float
+
+
+@dataclass
+class BodyContactGains:
+    """phyz_gpu::BodyContactGains (contact_pipeline.rs:277-305)."""
+
+    stiffness: float
+    damping: float
+
+    @staticmethod
+    def uniform_frequency(model: Model, omega: float, zeta: float) -> list:
+        return [
+            BodyContactGains(b.inertia.mass * omega * omega, 2.0 * zeta * b.inertia.mass * omega)
+            for b in model.bodies
+        ]
+
+
+def _rows(a, nworld: int, width: int) -> np.ndarray:
+    """pack_rows semantics (layout.rs:327-337): zero-pad / truncate rows."""
+    out = np.zeros((nworld, width), np.float64)
+    if a is None:
+        return out
+    if isinstance(a, np.ndarray) and a.ndim == 2:
+        r, c = min(a.shape[0], nworld), min(a.shape[1], width)
+        out[:r, :c] = a[:r, :c]
+        return out
+    for w, row in enumerate(list(a)[:nworld]):
+        row = np.asarray(row, np.float64).reshape(-1)[:width]
+        out[w, : row.size] = row
+    return out
+
+
+class BatchSim:
+    """N independent worlds of one model on one GPU."""
+
+    def __init__(self, model: Model, nworld: int, device: int = 0, precision: str = "f64"):
+        self._lib = _lib.load()
+        self.model = model
+        self.nworld = int(nworld)
+        self.device = int(device)
+        self.precision = precision
+        prec = {"f32": _lib.F32, "f64": _lib.F64}[precision]
+        self._cmodel, self._cbodies = model.to_c()
+        h = C.c_void_p()
+        check(self._lib.phyzb_create(C.byref(self._cmodel), self.nworld, self.device, prec, C.byref(h)))
+        self._h = h
+        self.nv = model.nv
+        self.nb = model.nbodies
+
+    # ── construction (cuda/mod.rs:470-498) ────────────────────────────────
+    @classmethod
+    def new(cls, model: Model, nworld: int, precision: str = "f64") -> "BatchSim":
+        return cls(model, nworld, 0, precision)
+
+    @classmethod
+    def on_device(cls, model: Model, nworld: int, ordinal: int, precision: str = "f64") -> "BatchSim":
+        return cls(model, nworld, ordinal, precision)
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self._lib.phyzb_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def set_model(self, model: Model) -> None:
+        cm, cb = model.to_c()
+        check(self._lib.phyzb_set_model(self._h, C.byref(cm)))
+        self.model, self._cmodel, self._cbodies = model, cm, cb
+
+    # ── contact (cuda/mod.rs:596-700) ─────────────────────────────────────
+    def enable_ground_contact(self, ground_height: float, stiffness: float, damping: float,
+                              friction: float) -> int:
+        n = C.c_int32()
+        check(self._lib.phyzb_enable_ground_contact(self._h, ground_height, stiffness, damping, friction,
+                                                    C.byref(n)))
+        return n.value
+
+    def enable_ground_contact_per_body(self, ground_height: float, friction: float, gains) -> int:
+        k = np.ascontiguousarray([g.stiffness for g in gains], np.float64)
+        d = np.ascontiguousarray([g.damping for g in gains], np.float64)
+        if k.size != self.nb:
+            raise PhyzbError(_lib.ERR_INVALID, f"need {self.nb} body gains, got {k.size}")
+        n = C.c_int32()
+        check(self._lib.phyzb_enable_ground_contact_per_body(self._h, ground_height, friction, dptr(k), dptr(d),
+                                                             C.byref(n)))
+        return n.value
+
+    def disable_contact(self) -> None:
+        check(self._lib.phyzb_disable_contact(self._h))
+
+    def collidable_bodies(self) -> int:
+        return self._lib.phyzb_collidable_bodies(self._h)
+
+    # ── PD (cuda/mod.rs:771-801) ───────────────────────────────────────────
+    def enable_pd_control(self, dofs) -> None:
+        arr = (_lib.PhyzbPdDof * max(len(dofs), 1))()
+        for i, d in enumerate(dofs):
+            arr[i] = _lib.PhyzbPdDof(d.q_index, d.v_index, d.kp, d.kd, d.max_force)
+        check(self._lib.phyzb_enable_pd(self._h, arr, len(dofs)))
+        self._npd = len(dofs)
+
+    def set_position_targets(self, targets) -> None:
+        t = _rows(targets, self.nworld, getattr(self, "_npd", 0))
+        check(self._lib.phyzb_set_position_targets(self._h, dptr(t)))
+
+    # ── state (cuda/mod.rs:804-821) ────────────────────────────────────────
+    def load_states(self, q, v, ctrl=None) -> None:
+        qa = _rows(q, self.nworld, self.nv)
+        va = _rows(v, self.nworld, self.nv)
+        ca = None if ctrl is None else _rows(ctrl, self.nworld, self.nv)
+        check(self._lib.phyzb_load_states(self._h, dptr(qa), dptr(va), None if ca is None else dptr(ca)))
+
+    def set_controls(self, controls) -> None:
+        c = _rows(controls, self.nworld, self.nv)
+        check(self._lib.phyzb_set_controls(self._h, dptr(c)))
+
+    # ── stepping (cuda/mod.rs:818-875) ─────────────────────────────────────
+    def step(self) -> None:
+        self.step_many(1)
+
+    def try_step(self):
+        try:
+            self.step_many(1)
+            return None
+        except PhyzbError as e:
+            return e
+
+    def step_many(self, n: int) -> None:
+        check(self._lib.phyzb_step(self._h, int(n)))
+
+    def step_with_controls(self, ctrl_seq: np.ndarray) -> None:
+        """len(ctrl_seq) steps, step t under controls ctrl_seq[t] (nworld x nv),
+        host float32 or float64 — the same as set_controls + step per row."""
+        a = np.ascontiguousarray(ctrl_seq)
+        if a.ndim != 3 or a.shape[1:] != (self.nworld, self.nv):
+            raise PhyzbError(_lib.ERR_INVALID, f"ctrl_seq must be (n, {self.nworld}, {self.nv})")
+        dt = {np.dtype(np.float32): _lib.HOST_F32, np.dtype(np.float64): _lib.HOST_F64}[a.dtype]
+        check(self._lib.phyzb_step_with_controls(self._h, a.ctypes.data_as(C.c_void_p), dt, a.shape[0]))
+
+    def step_with_controls_ptr(self, ptr: int, host_dtype: int, n: int) -> None:
+        """Raw form of step_with_controls for pinned host buffers (e.g. torch)."""
+        check(self._lib.phyzb_step_with_controls(self._h, C.c_void_p(ptr), host_dtype, int(n)))
+
+    def step_device_controls(self, ptr: int, step_stride: int, n: int) -> None:
+        check(self._lib.phyzb_step_device_controls(self._h, C.c_void_p(ptr), int(step_stride), int(n)))
+
+    def sync(self) -> None:
+        check(self._lib.phyzb_sync(self._h))
+
+    def status(self) -> None:
+        check(self._lib.phyzb_status(self._h))
+
+    def clear_status(self) -> None:
+        check(self._lib.phyzb_clear_status(self._h))
+
+    # ── readback (cuda/mod.rs:978-996) ─────────────────────────────────────
+    def readback_states(self):
+        q = np.zeros((self.nworld, self.nv))
+        v = np.zeros((self.nworld, self.nv))
+        check(self._lib.phyzb_readback_states(self._h, dptr(q), dptr(v)))
+        return q, v
+
+    def readback_qdd(self) -> np.ndarray:
+        qdd = np.zeros((self.nworld, self.nv))
+        check(self._lib.phyzb_readback_qdd(self._h, dptr(qdd)))
+        return qdd
+
+    def readback_contacts(self) -> np.ndarray:
+        """(nworld, nbodies, 8): touching, depth, point xyz, force xyz."""
+        cs = np.zeros((self.nworld, self.nb, _lib.CONTACT_STRIDE))
+        check(self._lib.phyzb_readback_contacts(self._h, dptr(cs)))
+        return cs
+
+    # ── device-resident path ───────────────────────────────────────────────
+    def device_view(self) -> dict:
+        v = _lib.PhyzbDeviceView()
+        check(self._lib.phyzb_device_view_get(self._h, C.byref(v)))
+        return {k: getattr(v, k) for k, _ in _lib.PhyzbDeviceView._fields_}
+
+    def set_stream(self, stream_ptr: int | None) -> None:
+        check(self._lib.phyzb_set_stream(self._h, C.c_void_p(stream_ptr or 0)))
+
+    def objective_device(self, kind: int, out_ptr: int) -> None:
+        check(self._lib.phyzb_objective_device(self._h, int(kind), C.c_void_p(out_ptr)))
+
+    def flops_per_world_step(self):
+        f, t = C.c_double(), C.c_double()
+        check(self._lib.phyzb_flops_per_world_step(self._h, C.byref(f), C.byref(t)))
+        return f.value, t.value
+
+    def launch_info(self) -> dict:
+        vals = [C.c_int32() for _ in range(4)]
+        check(self._lib.phyzb_launch_info(self._h, *[C.byref(x) for x in vals]))
+        return dict(zip(("worlds_per_block", "blocks", "smem_bytes", "scratch_per_world"),
+                        [x.value for x in vals]))

@@ -1,0 +1,642 @@
+// C ABI of libphyzb200 (include/phyzb.h): the BatchSim of phyz-gpu
+// (crates/phyz-gpu/src/cuda/mod.rs:430-1377) re-designed around one fused
+// multi-step kernel per launch. The handle owns every device buffer; host
+// arrays are copied in and out through a device staging buffer and
+// converted on the device between phyz's world-major f64 rows and the
+// simulator's structure-of-arrays state (f32 or f64).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/phyzb.h"
+#include "pz_launch.h"
+#include "pz_pack.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define PZ_CUDA(expr)                                                                           \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return fail(PHYZB_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));    \
+    } while (0)
+
+#define PZ_TRY(expr)                \
+    do {                            \
+        int r_ = (expr);            \
+        if (r_ != PHYZB_OK) return r_; \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+struct phyzb_sim {
+    int device = 0, precision = PHYZB_F64;
+    long long nworld = 0;
+    int nb = 0, nv = 0;
+    std::vector<phyzb_body> bodies;
+    phyzb_model model{};  // points into `bodies`
+    pz::PackCfg cfg;
+    double ground_h = 0.0, friction = 0.0;
+    int collidable = 0;
+
+    cudaStream_t own_stream = nullptr, stream = nullptr, copy_stream = nullptr;
+    void *q = nullptr, *v = nullptr, *ctrl = nullptr, *qdd = nullptr;
+    void *targets = nullptr, *cstate = nullptr;
+    int* status = nullptr;
+    void* blob = nullptr;
+    size_t blob_cap = 0;
+    pz::PackInfo info;
+    pz::LaunchCfg launch{};
+    void* staging = nullptr;  // device, AoS f64 rows for host copies
+    size_t staging_bytes = 0;
+    // bulk per-step control pipeline (phyzb_step_with_controls)
+    void* pipe_raw[2] = {nullptr, nullptr};
+    void* pipe_soa[2] = {nullptr, nullptr};
+    size_t pipe_raw_bytes = 0, pipe_soa_bytes = 0;
+    cudaEvent_t ev_copied[2] = {nullptr, nullptr}, ev_converted[2] = {nullptr, nullptr};
+
+    size_t esz() const { return precision == PHYZB_F64 ? 8 : 4; }
+    size_t state_bytes() const { return (size_t)nworld * nv * esz(); }
+};
+
+namespace {
+
+bool is_f64(const phyzb_sim* s) { return s->precision == PHYZB_F64; }
+
+int repack(phyzb_sim* s) {
+    std::vector<unsigned char> blob;
+    s->info = is_f64(s) ? pz::pack_model<double>(&s->model, s->nv, s->cfg, blob)
+                        : pz::pack_model<float>(&s->model, s->nv, s->cfg, blob);
+    s->collidable = s->info.collidable;
+    // kernels already queued may read the table: drain the stream first
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    if ((size_t)s->info.bytes > s->blob_cap) {
+        if (s->blob) cudaFree(s->blob);
+        s->blob = nullptr;
+        s->blob_cap = 0;
+        PZ_CUDA(cudaMalloc(&s->blob, s->info.bytes));
+        s->blob_cap = s->info.bytes;
+    }
+    PZ_CUDA(cudaMemcpy(s->blob, blob.data(), s->info.bytes, cudaMemcpyHostToDevice));
+    cudaError_t e = is_f64(s) ? pz::rollout_config<double>(s->info.scratch, s->info.bytes, s->nworld, &s->launch)
+                              : pz::rollout_config<float>(s->info.scratch, s->info.bytes, s->nworld, &s->launch);
+    if (e == cudaErrorInvalidConfiguration)
+        return fail(PHYZB_ERR_TOO_LARGE, "per-world scratch (" + std::to_string(s->info.scratch) +
+                                             " slots) does not fit shared memory at 32 worlds per block");
+    PZ_CUDA(e);
+    return PHYZB_OK;
+}
+
+void set_model_copy(phyzb_sim* s, const phyzb_model* m) {
+    s->bodies.assign(m->bodies, m->bodies + m->nbodies);
+    s->model = *m;
+    s->model.bodies = s->bodies.data();
+}
+
+template <class T>
+pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+    pz::RolloutArgs<T> a;
+    a.model_blob = s->blob;
+    a.model_bytes = s->info.bytes;
+    a.off_bi = s->info.off_bi;
+    a.off_pd = s->info.off_pd;
+    a.off_pdmap = s->info.off_pdmap;
+    a.nb = s->nb;
+    a.nv = s->nv;
+    a.npd = (int)s->cfg.pd.size();
+    a.contact = s->cfg.contact ? 1 : 0;
+    a.dt = s->model.dt;
+    a.gx = s->model.gravity[0];
+    a.gy = s->model.gravity[1];
+    a.gz = s->model.gravity[2];
+    a.ground_h = s->ground_h;
+    a.friction = s->friction;
+    a.q = (T*)s->q;
+    a.v = (T*)s->v;
+    a.ctrl = (const T*)ctrl;
+    a.ctrl_stride = stride;
+    a.targets = (const T*)s->targets;
+    a.qdd = (T*)s->qdd;
+    a.cstate = s->cfg.contact ? (T*)s->cstate : nullptr;
+    a.status = s->status;
+    a.nworld = s->nworld;
+    a.nsteps = nsteps;
+    a.scratch = s->info.scratch;
+    return a;
+}
+
+int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+    cudaError_t e = is_f64(s) ? pz::launch_rollout<double>(rollout_args<double>(s, ctrl, stride, nsteps), s->launch,
+                                                           s->stream)
+                              : pz::launch_rollout<float>(rollout_args<float>(s, ctrl, stride, nsteps), s->launch,
+                                                          s->stream);
+    PZ_CUDA(e);
+    return PHYZB_OK;
+}
+
+// host rows [nworld][width] f64 -> device SoA [width][nworld] in the sim precision
+int upload_rows(phyzb_sim* s, const double* host, int width, void* dst) {
+    const size_t bytes = (size_t)s->nworld * width * sizeof(double);
+    if (bytes == 0) return PHYZB_OK;
+    if (bytes > s->staging_bytes) return fail(PHYZB_ERR_INVALID, "internal: staging too small");
+    PZ_CUDA(cudaMemcpyAsync(s->staging, host, bytes, cudaMemcpyHostToDevice, s->stream));
+    cudaError_t e = is_f64(s) ? pz::launch_aos_to_soa<double, double>((const double*)s->staging, (double*)dst,
+                                                                      s->nworld, width, 1, s->stream)
+                              : pz::launch_aos_to_soa<double, float>((const double*)s->staging, (float*)dst,
+                                                                     s->nworld, width, 1, s->stream);
+    PZ_CUDA(e);
+    // the caller may reuse `host` as soon as this returns
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    return PHYZB_OK;
+}
+
+// device SoA [width][nworld] -> host rows [nworld][width] f64
+int download_rows(phyzb_sim* s, const void* src, int width, double* host) {
+    const size_t bytes = (size_t)s->nworld * width * sizeof(double);
+    if (bytes == 0) return PHYZB_OK;
+    cudaError_t e = is_f64(s) ? pz::launch_soa_to_aos<double, double>((const double*)src, (double*)s->staging,
+                                                                      s->nworld, width, s->stream)
+                              : pz::launch_soa_to_aos<float, double>((const float*)src, (double*)s->staging,
+                                                                     s->nworld, width, s->stream);
+    PZ_CUDA(e);
+    PZ_CUDA(cudaMemcpyAsync(host, s->staging, bytes, cudaMemcpyDeviceToHost, s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    return PHYZB_OK;
+}
+
+void free_ptr(void*& p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+int check_sim(const phyzb_sim* s) {
+    if (!s) return fail(PHYZB_ERR_INVALID, "simulator handle is null");
+    return PHYZB_OK;
+}
+
+int read_status(phyzb_sim* s) {
+    int st[2] = {0, 0};
+    PZ_CUDA(cudaMemcpyAsync(st, s->status, sizeof(st), cudaMemcpyDeviceToHost, s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    if (st[0] & 1)
+        return fail(PHYZB_ERR_NONFINITE, "state went non-finite on device (first world " + std::to_string(st[1]) + ")");
+    return PHYZB_OK;
+}
+
+int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d) {
+    int collidable = 0;
+    for (int i = 0; i < s->nb; i++)
+        if (s->bodies[i].geom_type != PHYZB_GEOM_NONE) collidable++;
+    if (collidable == 0) {
+        // layout.rs:282-297 no_collidable_geometry_error
+        std::string names;
+        for (int i = 0; i < s->nb; i++) names += (i ? ", body " : "body ") + std::to_string(i);
+        return fail(PHYZB_ERR_INVALID,
+                    "ground contact enabled but no body has GPU-collidable geometry (supported: sphere, box, "
+                    "capsule, cylinder, mesh); bodies without a supported shape: [" + names + "]");
+    }
+    if (!std::isfinite(ground) || !std::isfinite(friction))
+        return fail(PHYZB_ERR_INVALID, "contact parameters must be finite");
+    for (int i = 0; i < s->nb; i++)
+        if (!std::isfinite(k[i]) || !std::isfinite(d[i]))
+            return fail(PHYZB_ERR_INVALID, "contact gains must be finite");
+    if (!s->cstate) {
+        const size_t bytes = (size_t)s->nworld * s->nb * PHYZB_CONTACT_STRIDE * s->esz();
+        PZ_CUDA(cudaMalloc(&s->cstate, bytes > 0 ? bytes : 16));
+        PZ_CUDA(cudaMemsetAsync(s->cstate, 0, bytes, s->stream));
+    }
+    s->cfg.contact = true;
+    s->cfg.gk.assign(k, k + s->nb);
+    s->cfg.gd.assign(d, d + s->nb);
+    s->ground_h = ground;
+    s->friction = friction;
+    PZ_TRY(repack(s));
+    return PHYZB_OK;
+}
+
+int ensure_pipeline(phyzb_sim* s, size_t raw_bytes, size_t soa_bytes) {
+    if (raw_bytes > s->pipe_raw_bytes) {
+        for (int b = 0; b < 2; b++) {
+            free_ptr(s->pipe_raw[b]);
+            PZ_CUDA(cudaMalloc(&s->pipe_raw[b], raw_bytes));
+        }
+        s->pipe_raw_bytes = raw_bytes;
+    }
+    if (soa_bytes > s->pipe_soa_bytes) {
+        for (int b = 0; b < 2; b++) {
+            free_ptr(s->pipe_soa[b]);
+            PZ_CUDA(cudaMalloc(&s->pipe_soa[b], soa_bytes));
+        }
+        s->pipe_soa_bytes = soa_bytes;
+    }
+    for (int b = 0; b < 2; b++) {
+        if (!s->ev_copied[b]) PZ_CUDA(cudaEventCreateWithFlags(&s->ev_copied[b], cudaEventDisableTiming));
+        if (!s->ev_converted[b]) PZ_CUDA(cudaEventCreateWithFlags(&s->ev_converted[b], cudaEventDisableTiming));
+    }
+    if (!s->copy_stream) PZ_CUDA(cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking));
+    return PHYZB_OK;
+}
+
+void destroy_sim(phyzb_sim* s) {
+    if (!s) return;
+    DeviceGuard g(s->device);
+    if (s->stream) cudaStreamSynchronize(s->stream);
+    if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
+    free_ptr(s->q);
+    free_ptr(s->v);
+    free_ptr(s->ctrl);
+    free_ptr(s->qdd);
+    free_ptr(s->targets);
+    free_ptr(s->cstate);
+    void* st = s->status;
+    free_ptr(st);
+    free_ptr(s->blob);
+    free_ptr(s->staging);
+    for (int b = 0; b < 2; b++) {
+        free_ptr(s->pipe_raw[b]);
+        free_ptr(s->pipe_soa[b]);
+        if (s->ev_copied[b]) cudaEventDestroy(s->ev_copied[b]);
+        if (s->ev_converted[b]) cudaEventDestroy(s->ev_converted[b]);
+    }
+    if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
+    if (s->own_stream) cudaStreamDestroy(s->own_stream);
+    delete s;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* phyzb_last_error(void) { return g_err.c_str(); }
+
+int phyzb_abi_version(void) { return PHYZB_ABI_VERSION; }
+
+int phyzb_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int precision, phyzb_sim** out) {
+    if (!out) return fail(PHYZB_ERR_INVALID, "out pointer is null");
+    *out = nullptr;
+    int nv = 0;
+    const std::string why = pz::validate_model(model, &nv);
+    if (!why.empty()) {
+        const bool too_large = model && model->nbodies > PHYZB_MAX_BODIES;
+        return fail(too_large ? PHYZB_ERR_TOO_LARGE : PHYZB_ERR_INVALID, why);
+    }
+    if (nworld < 1) return fail(PHYZB_ERR_INVALID, "nworld must be >= 1");
+    if (precision != PHYZB_F32 && precision != PHYZB_F64) return fail(PHYZB_ERR_INVALID, "precision must be F32 or F64");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(PHYZB_ERR_NO_DEVICE, "no CUDA device is available");
+    }
+    if (device < 0 || device >= ndev)
+        return fail(PHYZB_ERR_NO_DEVICE, "device " + std::to_string(device) + " out of range (" + std::to_string(ndev) +
+                                             " visible)");
+    DeviceGuard g(device);
+    phyzb_sim* s = new phyzb_sim();
+    s->device = device;
+    s->precision = precision;
+    s->nworld = nworld;
+    s->nb = model->nbodies;
+    s->nv = nv;
+    set_model_copy(s, model);
+    auto bail = [&](int code) {
+        destroy_sim(s);
+        return code;
+    };
+    if (cudaStreamCreateWithFlags(&s->own_stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(PHYZB_ERR_CUDA, "cudaStreamCreate failed"));
+    s->stream = s->own_stream;
+    const size_t sb = s->state_bytes() > 0 ? s->state_bytes() : 16;
+    void** bufs[] = {&s->q, &s->v, &s->ctrl, &s->qdd};
+    for (void** b : bufs) {
+        cudaError_t e = cudaMalloc(b, sb);
+        if (e != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, std::string("cudaMalloc: ") + cudaGetErrorString(e)));
+        cudaMemsetAsync(*b, 0, sb, s->stream);
+    }
+    void* st = nullptr;
+    if (cudaMalloc(&st, 2 * sizeof(int)) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc status"));
+    s->status = (int*)st;
+    const int init[2] = {0, 0x7fffffff};
+    cudaMemcpy(s->status, init, sizeof(init), cudaMemcpyHostToDevice);
+    s->staging_bytes = (size_t)nworld * std::max(nv, s->nb * PHYZB_CONTACT_STRIDE) * sizeof(double);
+    if (cudaMalloc(&s->staging, s->staging_bytes > 0 ? s->staging_bytes : 16) != cudaSuccess)
+        return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc staging"));
+    int r = repack(s);
+    if (r != PHYZB_OK) {
+        std::string msg = g_err;
+        destroy_sim(s);
+        return fail(r, msg);
+    }
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "init sync failed"));
+    *out = s;
+    return PHYZB_OK;
+}
+
+int phyzb_destroy(phyzb_sim* sim) {
+    destroy_sim(sim);
+    return PHYZB_OK;
+}
+
+int phyzb_set_model(phyzb_sim* s, const phyzb_model* model) {
+    PZ_TRY(check_sim(s));
+    int nv = 0;
+    const std::string why = pz::validate_model(model, &nv);
+    if (!why.empty()) return fail(PHYZB_ERR_INVALID, why);
+    if (model->nbodies != s->nb || nv != s->nv)
+        return fail(PHYZB_ERR_INVALID, "set_model: shape changed (" + std::to_string(model->nbodies) + " bodies, nv " +
+                                           std::to_string(nv) + " vs " + std::to_string(s->nb) + " bodies, nv " +
+                                           std::to_string(s->nv) + "); build a new simulator");
+    for (int i = 0; i < s->nb; i++)
+        if (model->bodies[i].joint_type != s->bodies[i].joint_type || model->bodies[i].parent != s->bodies[i].parent)
+            return fail(PHYZB_ERR_INVALID, "set_model: topology or joint types changed; build a new simulator");
+    DeviceGuard g(s->device);
+    set_model_copy(s, model);
+    return repack(s);
+}
+
+int phyzb_enable_ground_contact(phyzb_sim* s, double ground_height, double stiffness, double damping, double friction,
+                                int32_t* collidable_out) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    std::vector<double> k(s->nb, stiffness), d(s->nb, damping);
+    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data()));
+    if (collidable_out) *collidable_out = s->collidable;
+    return PHYZB_OK;
+}
+
+int phyzb_enable_ground_contact_per_body(phyzb_sim* s, double ground_height, double friction,
+                                         const double* stiffness, const double* damping, int32_t* collidable_out) {
+    PZ_TRY(check_sim(s));
+    if (!stiffness || !damping) return fail(PHYZB_ERR_INVALID, "per-body gains are null");
+    DeviceGuard g(s->device);
+    PZ_TRY(set_contact(s, ground_height, friction, stiffness, damping));
+    if (collidable_out) *collidable_out = s->collidable;
+    return PHYZB_OK;
+}
+
+int phyzb_disable_contact(phyzb_sim* s) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    s->cfg.contact = false;
+    return repack(s);
+}
+
+int phyzb_collidable_bodies(const phyzb_sim* s) { return (s && s->cfg.contact) ? s->collidable : 0; }
+
+int phyzb_enable_pd(phyzb_sim* s, const phyzb_pd_dof* dofs, int32_t n) {
+    PZ_TRY(check_sim(s));
+    // layout.rs:300-315 check_pd_dofs
+    if (!dofs || n <= 0) return fail(PHYZB_ERR_INVALID, "PD pipeline needs at least one servoed DOF");
+    for (int k = 0; k < n; k++)
+        if (dofs[k].q_index < 0 || dofs[k].q_index >= s->nv || dofs[k].v_index < 0 || dofs[k].v_index >= s->nv)
+            return fail(PHYZB_ERR_INVALID, "PD DOF out of range: q_index " + std::to_string(dofs[k].q_index) +
+                                               " (nq " + std::to_string(s->nv) + "), v_index " +
+                                               std::to_string(dofs[k].v_index) + " (nv " + std::to_string(s->nv) +
+                                               ")");
+    DeviceGuard g(s->device);
+    const bool same = (int)s->cfg.pd.size() == n && s->targets;
+    s->cfg.pd.assign(dofs, dofs + n);
+    if (!same) {
+        free_ptr(s->targets);
+        const size_t bytes = (size_t)n * s->nworld * s->esz();
+        PZ_CUDA(cudaMalloc(&s->targets, bytes));
+        PZ_CUDA(cudaMemsetAsync(s->targets, 0, bytes, s->stream));
+    }
+    return repack(s);
+}
+
+int phyzb_set_position_targets(phyzb_sim* s, const double* targets) {
+    PZ_TRY(check_sim(s));
+    if (s->cfg.pd.empty()) return fail(PHYZB_ERR_STATE, "PD control not enabled — call enable_pd_control first");
+    if (!targets) return fail(PHYZB_ERR_INVALID, "targets is null");
+    DeviceGuard g(s->device);
+    return upload_rows(s, targets, (int)s->cfg.pd.size(), s->targets);
+}
+
+int phyzb_load_states(phyzb_sim* s, const double* q, const double* v, const double* ctrl) {
+    PZ_TRY(check_sim(s));
+    if (!q || !v) return fail(PHYZB_ERR_INVALID, "q and v must not be null");
+    DeviceGuard g(s->device);
+    PZ_TRY(upload_rows(s, q, s->nv, s->q));
+    PZ_TRY(upload_rows(s, v, s->nv, s->v));
+    if (ctrl) return upload_rows(s, ctrl, s->nv, s->ctrl);
+    PZ_CUDA(cudaMemsetAsync(s->ctrl, 0, s->state_bytes(), s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    return PHYZB_OK;
+}
+
+int phyzb_set_controls(phyzb_sim* s, const double* ctrl) {
+    PZ_TRY(check_sim(s));
+    if (!ctrl) return fail(PHYZB_ERR_INVALID, "ctrl is null");
+    DeviceGuard g(s->device);
+    return upload_rows(s, ctrl, s->nv, s->ctrl);
+}
+
+int phyzb_step(phyzb_sim* s, int32_t n) {
+    PZ_TRY(check_sim(s));
+    if (n < 0) return fail(PHYZB_ERR_INVALID, "step count must be >= 0");
+    if (n == 0) return PHYZB_OK;
+    DeviceGuard g(s->device);
+    return launch(s, s->ctrl, 0, n);
+}
+
+int phyzb_step_device_controls(phyzb_sim* s, const void* sched, int64_t step_stride, int32_t n) {
+    PZ_TRY(check_sim(s));
+    if (n < 0) return fail(PHYZB_ERR_INVALID, "step count must be >= 0");
+    if (n == 0) return PHYZB_OK;
+    if (!sched) return fail(PHYZB_ERR_INVALID, "control schedule is null");
+    if (step_stride < (int64_t)s->nv * s->nworld)
+        return fail(PHYZB_ERR_INVALID, "step_stride must be >= nv * nworld");
+    DeviceGuard g(s->device);
+    PZ_TRY(launch(s, sched, step_stride, n));
+    // leave the held controls equal to the last row, as n x (set_controls; step)
+    const char* last = (const char*)sched + (size_t)(n - 1) * step_stride * s->esz();
+    PZ_CUDA(cudaMemcpyAsync(s->ctrl, last, s->state_bytes(), cudaMemcpyDeviceToDevice, s->stream));
+    return PHYZB_OK;
+}
+
+int phyzb_step_with_controls(phyzb_sim* s, const void* ctrl, int host_dtype, int32_t n) {
+    PZ_TRY(check_sim(s));
+    if (n < 0) return fail(PHYZB_ERR_INVALID, "step count must be >= 0");
+    if (n == 0) return PHYZB_OK;
+    if (!ctrl) return fail(PHYZB_ERR_INVALID, "ctrl is null");
+    if (host_dtype != PHYZB_HOST_F32 && host_dtype != PHYZB_HOST_F64)
+        return fail(PHYZB_ERR_INVALID, "host_dtype must be PHYZB_HOST_F32 or PHYZB_HOST_F64");
+    DeviceGuard g(s->device);
+    const size_t hsz = host_dtype == PHYZB_HOST_F64 ? 8 : 4;
+    const size_t row = (size_t)s->nworld * s->nv;  // elements per step
+    // chunk: about 128 MB of host rows per copy, at least one step
+    size_t chunk = row ? std::max<size_t>(1, (128u << 20) / (row * hsz)) : 1;
+    chunk = std::min<size_t>(chunk, (size_t)n);
+    PZ_TRY(ensure_pipeline(s, chunk * row * hsz, chunk * row * s->esz()));
+    const char* host = (const char*)ctrl;
+    int done = 0, c = 0;
+    while (done < n) {
+        const int len = (int)std::min<size_t>(chunk, (size_t)(n - done));
+        const int b = c & 1;
+        if (c >= 2) PZ_CUDA(cudaStreamWaitEvent(s->copy_stream, s->ev_converted[b], 0));
+        PZ_CUDA(cudaMemcpyAsync(s->pipe_raw[b], host + (size_t)done * row * hsz, (size_t)len * row * hsz,
+                                cudaMemcpyHostToDevice, s->copy_stream));
+        PZ_CUDA(cudaEventRecord(s->ev_copied[b], s->copy_stream));
+        PZ_CUDA(cudaStreamWaitEvent(s->stream, s->ev_copied[b], 0));
+        cudaError_t e;
+        if (is_f64(s))
+            e = host_dtype == PHYZB_HOST_F64
+                    ? pz::launch_aos_to_soa<double, double>((const double*)s->pipe_raw[b], (double*)s->pipe_soa[b],
+                                                            s->nworld, s->nv, len, s->stream)
+                    : pz::launch_aos_to_soa<float, double>((const float*)s->pipe_raw[b], (double*)s->pipe_soa[b],
+                                                           s->nworld, s->nv, len, s->stream);
+        else
+            e = host_dtype == PHYZB_HOST_F64
+                    ? pz::launch_aos_to_soa<double, float>((const double*)s->pipe_raw[b], (float*)s->pipe_soa[b],
+                                                           s->nworld, s->nv, len, s->stream)
+                    : pz::launch_aos_to_soa<float, float>((const float*)s->pipe_raw[b], (float*)s->pipe_soa[b],
+                                                          s->nworld, s->nv, len, s->stream);
+        PZ_CUDA(e);
+        PZ_CUDA(cudaEventRecord(s->ev_converted[b], s->stream));
+        PZ_TRY(launch(s, s->pipe_soa[b], (long long)row, len));
+        if (done + len == n) {
+            const char* last = (const char*)s->pipe_soa[b] + (size_t)(len - 1) * row * s->esz();
+            PZ_CUDA(cudaMemcpyAsync(s->ctrl, last, row * s->esz(), cudaMemcpyDeviceToDevice, s->stream));
+        }
+        done += len;
+        c++;
+    }
+    // every host row has been read once the copy stream drains
+    PZ_CUDA(cudaStreamSynchronize(s->copy_stream));
+    return PHYZB_OK;
+}
+
+int phyzb_sync(phyzb_sim* s) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    return read_status(s);
+}
+
+int phyzb_status(phyzb_sim* s) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    return read_status(s);
+}
+
+int phyzb_clear_status(phyzb_sim* s) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    const int init[2] = {0, 0x7fffffff};
+    PZ_CUDA(cudaMemcpyAsync(s->status, init, sizeof(init), cudaMemcpyHostToDevice, s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    return PHYZB_OK;
+}
+
+int phyzb_readback_states(phyzb_sim* s, double* q, double* v) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    if (q) PZ_TRY(download_rows(s, s->q, s->nv, q));
+    if (v) PZ_TRY(download_rows(s, s->v, s->nv, v));
+    return PHYZB_OK;
+}
+
+int phyzb_readback_qdd(phyzb_sim* s, double* qdd) {
+    PZ_TRY(check_sim(s));
+    if (!qdd) return fail(PHYZB_ERR_INVALID, "qdd is null");
+    DeviceGuard g(s->device);
+    return download_rows(s, s->qdd, s->nv, qdd);
+}
+
+int phyzb_readback_contacts(phyzb_sim* s, double* cs) {
+    PZ_TRY(check_sim(s));
+    if (!s->cfg.contact || !s->cstate)
+        return fail(PHYZB_ERR_STATE, "ground contact not enabled — call enable_ground_contact first");
+    if (!cs) return fail(PHYZB_ERR_INVALID, "output is null");
+    DeviceGuard g(s->device);
+    return download_rows(s, s->cstate, s->nb * PHYZB_CONTACT_STRIDE, cs);
+}
+
+int phyzb_device_view_get(phyzb_sim* s, phyzb_device_view* out) {
+    PZ_TRY(check_sim(s));
+    if (!out) return fail(PHYZB_ERR_INVALID, "out is null");
+    out->q = s->q;
+    out->v = s->v;
+    out->ctrl = s->ctrl;
+    out->qdd = s->qdd;
+    out->nworld = s->nworld;
+    out->nv = s->nv;
+    out->nbodies = s->nb;
+    out->precision = s->precision;
+    out->device = s->device;
+    out->stream = (void*)s->stream;
+    return PHYZB_OK;
+}
+
+int phyzb_set_stream(phyzb_sim* s, void* stream) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    s->stream = stream ? (cudaStream_t)stream : s->own_stream;
+    return PHYZB_OK;
+}
+
+int phyzb_objective_device(phyzb_sim* s, int kind, void* out) {
+    PZ_TRY(check_sim(s));
+    if (kind != 0 && kind != 1) return fail(PHYZB_ERR_INVALID, "objective kind must be 0 or 1");
+    if (!out) return fail(PHYZB_ERR_INVALID, "output is null");
+    DeviceGuard g(s->device);
+    cudaError_t e = is_f64(s) ? pz::launch_objective<double>(rollout_args<double>(s, s->ctrl, 0, 1), s->launch, kind,
+                                                             (double*)out, s->stream)
+                              : pz::launch_objective<float>(rollout_args<float>(s, s->ctrl, 0, 1), s->launch, kind,
+                                                            (float*)out, s->stream);
+    PZ_CUDA(e);
+    return PHYZB_OK;
+}
+
+int phyzb_flops_per_world_step(const phyzb_sim* s, double* flops, double* transcendentals) {
+    PZ_TRY(check_sim(s));
+    const pz::FlopCount fc = pz::count_world_step(&s->model, s->nv, s->cfg);
+    if (flops) *flops = fc.flops;
+    if (transcendentals) *transcendentals = fc.transcendentals;
+    return PHYZB_OK;
+}
+
+int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t* smem, int32_t* scratch) {
+    PZ_TRY(check_sim(s));
+    if (wpb) *wpb = s->launch.W;
+    if (blocks) *blocks = s->launch.grid;
+    if (smem) *smem = s->launch.smem;
+    if (scratch) *scratch = s->info.scratch;
+    return PHYZB_OK;
+}
+
+}  // extern "C"

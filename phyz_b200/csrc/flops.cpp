@@ -1,0 +1,152 @@
+// Algorithmic flop count of one world-step, taken by running the kernel's
+// own world-step code (pz_world.cuh) on the host with a counting scalar.
+// This is a measurement helper only: the counting scalar carries values
+// so branches follow a real state, but nothing here is a way to step a
+// simulation on the CPU (no float/double host instantiation exists).
+//
+// Convention: +, -, *, / count one flop each (a fused multiply-add is the
+// two flops it replaces); sqrt, sin/cos, atan2 and tanh are tallied
+// separately as transcendental calls; min/max/abs/compares count nothing.
+#include <vector>
+
+#include "pz_pack.h"
+#include "pz_types.cuh"
+
+namespace pz {
+
+struct Tally {
+    double flops = 0, trans = 0;
+};
+static thread_local Tally g_tally;
+
+struct Cnt {
+    double v;
+    Cnt() = default;
+    Cnt(double x) : v(x) {}
+};
+inline Cnt operator+(Cnt a, Cnt b) {
+    g_tally.flops += 1;
+    return Cnt(a.v + b.v);
+}
+inline Cnt operator-(Cnt a, Cnt b) {
+    g_tally.flops += 1;
+    return Cnt(a.v - b.v);
+}
+inline Cnt operator*(Cnt a, Cnt b) {
+    g_tally.flops += 1;
+    return Cnt(a.v * b.v);
+}
+inline Cnt operator/(Cnt a, Cnt b) {
+    g_tally.flops += 1;
+    return Cnt(a.v / b.v);
+}
+inline Cnt operator-(Cnt a) { return Cnt(-a.v); }
+inline Cnt& operator+=(Cnt& a, Cnt b) { return a = a + b; }
+inline bool operator<(Cnt a, Cnt b) { return a.v < b.v; }
+inline bool operator>(Cnt a, Cnt b) { return a.v > b.v; }
+inline bool operator<=(Cnt a, Cnt b) { return a.v <= b.v; }
+inline bool operator>=(Cnt a, Cnt b) { return a.v >= b.v; }
+inline void pz_sincos(Cnt x, Cnt* s, Cnt* c) {
+    g_tally.trans += 1;
+    *s = Cnt(std::sin(x.v));
+    *c = Cnt(std::cos(x.v));
+}
+inline Cnt pz_sqrt(Cnt x) {
+    g_tally.trans += 1;
+    return Cnt(std::sqrt(x.v));
+}
+inline Cnt pz_atan2(Cnt y, Cnt x) {
+    g_tally.trans += 1;
+    return Cnt(std::atan2(y.v, x.v));
+}
+inline Cnt pz_tanh(Cnt x) {
+    g_tally.trans += 1;
+    return Cnt(std::tanh(x.v));
+}
+inline Cnt pz_abs(Cnt x) { return Cnt(std::fabs(x.v)); }
+inline Cnt pz_min(Cnt a, Cnt b) { return Cnt(std::fmin(a.v, b.v)); }
+inline Cnt pz_max(Cnt a, Cnt b) { return Cnt(std::fmax(a.v, b.v)); }
+
+template <>
+struct Eps<Cnt> {
+    static constexpr double quat = 2.220446049250313e-16;
+};
+
+}  // namespace pz
+
+#include "pz_world.cuh"
+
+namespace pz {
+
+namespace {
+struct HostScr {
+    Cnt* base;
+    Cnt& operator()(int s) const { return base[s]; }
+    void prefetch(int s, const Cnt* g) const { base[s] = *g; }
+    void commit() const {}
+    void wait() const {}
+};
+}  // namespace
+
+FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
+    std::vector<unsigned char> blob;
+    const PackInfo info = pack_model<double>(m, nv, cfg, blob);
+    const int nb = m->nbodies, npd = (int)cfg.pd.size();
+    // the same table in the counting scalar (BodyT<double> -> BodyT<Cnt>)
+    std::vector<BodyT<Cnt>> bt(nb);
+    const BodyT<double>* src = reinterpret_cast<const BodyT<double>*>(blob.data());
+    static_assert(sizeof(BodyT<double>) == sizeof(BodyT<Cnt>), "layout");
+    std::memcpy((void*)bt.data(), src, sizeof(BodyT<double>) * nb);
+    std::vector<PdT<Cnt>> pd(npd > 0 ? npd : 1);
+    const PdT<double>* psrc = reinterpret_cast<const PdT<double>*>(blob.data() + info.off_pd);
+    for (int k = 0; k < npd; k++) {
+        pd[k].kp = psrc[k].kp;
+        pd[k].kd = psrc[k].kd;
+        pd[k].maxf = psrc[k].maxf;
+        pd[k].qi = psrc[k].qi;
+        pd[k].vi = psrc[k].vi;
+    }
+    ModelView<Cnt> M;
+    M.bt = bt.data();
+    M.bi = reinterpret_cast<const BodyI*>(blob.data() + info.off_bi);
+    M.pd = pd.data();
+    M.pd_of_dof = reinterpret_cast<const int*>(blob.data() + info.off_pdmap);
+    M.nb = nb;
+    M.nv = nv;
+    M.npd = npd;
+    M.contact = cfg.contact ? 1 : 0;
+    M.dt = Cnt(m->dt);
+    M.gx = Cnt(m->gravity[0]);
+    M.gy = Cnt(m->gravity[1]);
+    M.gz = Cnt(m->gravity[2]);
+    // Ground far below: contact detection is counted, the force law is not
+    // (a lower bound on the work of a contact step).
+    M.ground_h = Cnt(-1e9);
+    M.friction = Cnt(1.0);
+    const double dtc = m->dt > 1e-9 ? m->dt : 1e-9;
+    M.inv_dt_c = Cnt(1.0 / dtc);
+    M.kstiff_c = Cnt(4.0 / (dtc * dtc));
+
+    std::vector<Cnt> scratch(info.scratch > 0 ? info.scratch : 1, Cnt(0.0));
+    HostScr S{scratch.data()};
+    // a generic state, away from the exp/log small-angle branches
+    for (int j = 0; j < nv; j++) {
+        scratch[j] = Cnt(0.1 + 0.01 * j);
+        scratch[nv + j] = Cnt(0.2 - 0.03 * j);
+    }
+    std::vector<Cnt> ctrl(nv > 0 ? nv : 1, Cnt(0.5)), targets(npd > 0 ? npd : 1, Cnt(0.0));
+    const WorldIO<Cnt> io{ctrl.data(), 0, targets.data(), 1, 0};
+    const Out<Cnt> none{nullptr, 0};
+    for (int i = 0; i < nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
+    pass1_all(M, S, false, none);
+    // steady state: one backward sweep + one fused finish/start sweep
+    g_tally = Tally{};
+    pass2(M, S);
+    pass3_next(M, S, io, 1, false, none, none);
+    FlopCount fc;
+    fc.flops = g_tally.flops;
+    fc.transcendentals = g_tally.trans;
+    return fc;
+}
+
+}  // namespace pz

@@ -1,0 +1,55 @@
+// Host-side launch interface of the stepper's kernels (stepper.cu), used by
+// the C ABI (capi.cu). No kernel here has a host implementation.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace pz {
+
+struct LaunchCfg {
+    int W;     // worlds (threads) per block
+    int grid;  // blocks
+    int smem;  // dynamic shared memory bytes per block
+};
+
+// One fused rollout launch: `nsteps` steps of every world.
+template <class T>
+struct RolloutArgs {
+    const void* model_blob;  // BodyT[nb] | BodyI[nb] | PdT[npd] | int pd_of_dof[nv]
+    int model_bytes;         // multiple of 16
+    int off_bi, off_pd, off_pdmap;
+    int nb, nv, npd, contact;
+    double dt, gx, gy, gz, ground_h, friction;
+    T* q;                  // [nv][nworld]
+    T* v;                  // [nv][nworld]
+    const T* ctrl;         // [nv][nworld] held, or schedule [nsteps][nv][nworld]
+    long long ctrl_stride; // elements between steps of the schedule (0: held)
+    const T* targets;      // [npd][nworld] or null
+    T* qdd;                // [nv][nworld], last step
+    T* cstate;             // [nb*8][nworld] contact state of the last step, or null
+    int* status;           // [0]: bit 0 = a world went non-finite; [1]: first such world
+    long long nworld;
+    int nsteps;
+    int scratch;           // scratch slots per world
+};
+
+template <class T>
+cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, LaunchCfg* out);
+template <class T>
+cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
+
+// Per-world kinetic energy (kind 0) or sum of q^2 (kind 1), summed over
+// worlds into *out (accumulated; caller zeroes it).
+template <class T>
+cudaError_t launch_objective(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out,
+                             cudaStream_t s);
+
+// Layout conversions between host-style world-major rows and the device SoA.
+// aos: [nworld][width] of Tin; soa: [width][nworld] of Tout.
+template <class Tin, class Tout>
+cudaError_t launch_aos_to_soa(const Tin* aos, Tout* soa, long long nworld, int width, int nrep,
+                              cudaStream_t s);
+template <class Tin, class Tout>
+cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int width, cudaStream_t s);
+
+}  // namespace pz

@@ -1,0 +1,85 @@
+// Device-side model table of the B200 stepper: one record per body, shared
+// by every world and staged into shared memory once per thread block.
+//
+// It carries what phyz's packed body table carries (parent, joint type,
+// DOF offset, mass/COM/inertia, parent->joint transform, axis, damping,
+// spring, armature: crates/phyz-gpu/src/layout.rs:18-37) plus what the
+// reference's CPU path applies and its GPU table drops (soft limits, dry
+// friction: crates/phyz-model/src/joint.rs:184-247), the contact geometry
+// of layout.rs:38-52, and precomputed quantities of this kernel's
+// formulation (inertia about the body origin, m*c, COM inverse inertia,
+// armature + dt*damping).
+//
+// The integer half names where each body's per-world scratch lives: the
+// per-world state is structure-of-arrays in shared memory, slot s of a
+// world at smem[s * worlds_per_block + thread].
+#pragma once
+
+namespace pz {
+
+enum JointCode { J_REVOLUTE = 0, J_PRISMATIC = 1, J_FIXED = 2, J_BALL = 3, J_FREE = 4 };
+
+enum BodyFlags {
+    F_PTJ_ROT = 1 << 0,   // parent->joint rotation is not the identity
+    F_PTJ_POS = 1 << 1,   // parent->joint translation is not zero
+    F_LIMITS = 1 << 2,    // soft joint limits (1-DOF)
+    F_FRICTION = 1 << 3,  // dry friction loss (1-DOF)
+    F_SPRING = 1 << 4,    // passive spring (1-DOF)
+    F_CONTACT = 1 << 5,   // collidable while contact is enabled (has an F slot)
+    F_CHAIN = 1 << 6,     // body i+1 has this body as parent (backward carry)
+    F_BRANCH = 1 << 7,    // parent of a child that is not i+1 (stored accumulators)
+};
+
+template <class T>
+struct alignas(16) BodyT {
+    T mass, mcom[3];          // m, m*c
+    T Io[6];                  // rotational inertia about the body origin (xx,yy,zz,xy,xz,yz)
+    T com[3];                 // centre of mass
+    T ptj_rot[9], ptj_pos[3]; // parent->joint transform (row-major rotation)
+    T axis[3];
+    T damping, stiffness, spring_ref, d_extra;  // d_extra = armature + dt * damping
+    T lim_lo, lim_hi, lim_k, lim_d, fric;
+    T Icinv[6];               // inverse of the COM inertia (0 if singular), for contact
+    T geom[6], gpos[3], grot[9];
+    T gk, gd;                 // penalty gains of this body
+    T armature;
+};
+
+struct alignas(16) BodyI {
+    int parent, jtype, off, ndof;
+    int axis_k;       // 0/1/2: axis is +e_k exactly (planar fast path); -1 general
+    int flags;        // BodyFlags
+    int s_xj;         // joint transform data: hinge (c, s); ball/free R_J (9)
+    int s_vw;         // body velocity (6) between passes 1 and 2, then W = U D^-1 (6*ndof)
+    int s_w0;         // control input of the step, then D^-1 u (ndof)
+    int s_f;          // contact wrench, body frame (6)
+    int s_acc;        // branch: accumulated child inertia (21) + bias force (6)
+    int s_vold;       // branch: velocity of the step being finished (6)
+    int s_acca;       // branch: acceleration (6)
+    int s_wx;         // branch: world frame for contact (up 3, height 1 | full R 9 + p 3)
+    int gtype;        // geometry code (0 none)
+    int npts;         // contact points (box 8, others 1)
+};
+
+template <class T>
+struct alignas(16) PdT {
+    T kp, kd, maxf;
+    int qi, vi;
+};
+
+// Everything a world-step needs besides its own state.
+template <class T>
+struct ModelView {
+    const BodyT<T>* bt;
+    const BodyI* bi;
+    const PdT<T>* pd;
+    const int* pd_of_dof;  // nv entries: PD entry driving this DOF, or -1
+    int nb, nv, npd;
+    int contact;           // 0/1
+    T dt, gx, gy, gz;
+    T ground_h, friction;
+    T inv_dt_c;            // 1 / max(dt, 1e-9)   (phyz_kernels.cu:574-578)
+    T kstiff_c;            // 4 / max(dt, 1e-9)^2
+};
+
+}  // namespace pz

@@ -1,0 +1,240 @@
+// Host-side packing of a phyzb_model into the device model table
+// (pz_model.cuh), including the per-world scratch layout. Host C++ only.
+//
+// The field semantics are those of phyz's pack_bodies / pack_geometries
+// (crates/phyz-gpu/src/layout.rs:103-279); values are kept in the
+// simulator's precision (f32 or f64) instead of always f32.
+#pragma once
+
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/phyzb.h"
+#include "pz_model.cuh"
+
+namespace pz {
+
+inline int ndof_of(int jt) {
+    switch (jt) {
+        case J_REVOLUTE:
+        case J_PRISMATIC: return 1;
+        case J_BALL: return 3;
+        case J_FREE: return 6;
+        default: return 0;
+    }
+}
+
+inline bool finite_all(const double* p, int n) {
+    for (int k = 0; k < n; k++)
+        if (!std::isfinite(p[k])) return false;
+    return true;
+}
+
+// Checks the reference applies at construction (cuda/mod.rs:499-510: body
+// limit, nq == nv) plus what this kernel relies on: topological order,
+// known codes, finite parameters. Returns "" when the model is usable.
+inline std::string validate_model(const phyzb_model* m, int* nv_out) {
+    if (!m || !m->bodies) return "model is null";
+    if (m->nbodies < 1) return "model has no bodies";
+    if (m->nbodies > PHYZB_MAX_BODIES)
+        return "model has " + std::to_string(m->nbodies) + " bodies but the kernels hold at most " +
+               std::to_string(PHYZB_MAX_BODIES) + " per world";
+    if (!finite_all(m->gravity, 3) || !std::isfinite(m->dt) || !(m->dt > 0.0))
+        return "gravity and dt must be finite, dt > 0";
+    int nv = 0;
+    for (int i = 0; i < m->nbodies; i++) {
+        const phyzb_body& b = m->bodies[i];
+        const std::string at = "body " + std::to_string(i) + ": ";
+        if (b.parent < -1 || b.parent >= i) return at + "parent must be -1 or an earlier body (topological order)";
+        if (b.joint_type < 0 || b.joint_type > 4) return at + "unknown joint type " + std::to_string(b.joint_type);
+        if (b.geom_type < 0 || b.geom_type > 5) return at + "unknown geometry type " + std::to_string(b.geom_type);
+        const double* groups[] = {b.com, b.inertia, b.ptj_rot, b.ptj_pos, b.axis, b.geom_params, b.geom_origin_pos,
+                                  b.geom_origin_rot};
+        const int sizes[] = {3, 6, 9, 3, 3, 6, 3, 9};
+        for (int g = 0; g < 8; g++)
+            if (!finite_all(groups[g], sizes[g])) return at + "non-finite parameter";
+        const double sc[] = {b.mass, b.damping, b.stiffness, b.spring_ref, b.armature, b.friction_loss};
+        if (!finite_all(sc, 6)) return at + "non-finite parameter";
+        if (b.has_limits &&
+            !(std::isfinite(b.limit_lower) && std::isfinite(b.limit_upper) && std::isfinite(b.limit_stiffness) &&
+              std::isfinite(b.limit_damping)))
+            return at + "non-finite joint limit";
+        nv += ndof_of(b.joint_type);
+    }
+    if (nv > PHYZB_MAX_DOFS)
+        return "model has " + std::to_string(nv) + " DOFs; at most " + std::to_string(PHYZB_MAX_DOFS) + " supported";
+    if (nv_out) *nv_out = nv;
+    return "";
+}
+
+struct PackInfo {
+    int off_bi = 0, off_pd = 0, off_pdmap = 0, bytes = 0;
+    int scratch = 0;     // scratch slots per world
+    int collidable = 0;  // bodies with a contact shape
+};
+
+inline int pad16(int b) { return (b + 15) & ~15; }
+
+// Contact and PD settings that change the table.
+struct PackCfg {
+    bool contact = false;
+    std::vector<double> gk, gd;          // per-body penalty gains (contact)
+    std::vector<phyzb_pd_dof> pd;        // PD servos
+};
+
+template <class T>
+inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std::vector<unsigned char>& blob) {
+    const int nb = m->nbodies;
+    const int npd = (int)cfg.pd.size();
+    PackInfo info;
+    const int szT = pad16((int)sizeof(BodyT<T>) * nb);
+    const int szI = pad16((int)sizeof(BodyI) * nb);
+    const int szP = pad16((int)sizeof(PdT<T>) * (npd > 0 ? npd : 1));
+    const int szM = pad16((int)sizeof(int) * (nv > 0 ? nv : 1));
+    info.off_bi = szT;
+    info.off_pd = szT + szI;
+    info.off_pdmap = szT + szI + szP;
+    info.bytes = szT + szI + szP + szM;
+    blob.assign(info.bytes, 0);
+    BodyT<T>* bt = reinterpret_cast<BodyT<T>*>(blob.data());
+    BodyI* bi = reinterpret_cast<BodyI*>(blob.data() + info.off_bi);
+    PdT<T>* pd = reinterpret_cast<PdT<T>*>(blob.data() + info.off_pd);
+    int* pdmap = reinterpret_cast<int*>(blob.data() + info.off_pdmap);
+
+    int next = 2 * nv;  // q, v
+    int off = 0;
+    for (int i = 0; i < nb; i++) {
+        const phyzb_body& b = m->bodies[i];
+        BodyT<T>& t = bt[i];
+        BodyI& d = bi[i];
+        const int nd = ndof_of(b.joint_type);
+        d.parent = b.parent;
+        d.jtype = b.joint_type;
+        d.off = off;
+        d.ndof = nd;
+        off += nd;
+        // mass properties: I_o = I_c + m (|c|^2 1 - c c^T)  (phyz_kernels.cu:332-359)
+        const double mass = b.mass, cx = b.com[0], cy = b.com[1], cz = b.com[2];
+        t.mass = T(mass);
+        t.mcom[0] = T(mass * cx);
+        t.mcom[1] = T(mass * cy);
+        t.mcom[2] = T(mass * cz);
+        t.Io[0] = T(b.inertia[0] + mass * (cy * cy + cz * cz));
+        t.Io[1] = T(b.inertia[1] + mass * (cx * cx + cz * cz));
+        t.Io[2] = T(b.inertia[2] + mass * (cx * cx + cy * cy));
+        t.Io[3] = T(b.inertia[3] - mass * cx * cy);
+        t.Io[4] = T(b.inertia[4] - mass * cx * cz);
+        t.Io[5] = T(b.inertia[5] - mass * cy * cz);
+        for (int k = 0; k < 3; k++) t.com[k] = T(b.com[k]);
+        for (int k = 0; k < 9; k++) t.ptj_rot[k] = T(b.ptj_rot[k]);
+        for (int k = 0; k < 3; k++) t.ptj_pos[k] = T(b.ptj_pos[k]);
+        for (int k = 0; k < 3; k++) t.axis[k] = T(b.axis[k]);
+        t.damping = T(b.damping);
+        t.stiffness = T(b.stiffness);
+        t.spring_ref = T(b.spring_ref);
+        t.armature = T(b.armature);
+        t.d_extra = T(b.armature + m->dt * b.damping);
+        t.lim_lo = T(b.limit_lower);
+        t.lim_hi = T(b.limit_upper);
+        t.lim_k = T(b.limit_stiffness);
+        t.lim_d = T(b.limit_damping);
+        t.fric = T(b.friction_loss);
+        // COM inverse inertia by cofactors (phyz_kernels.cu:545-561)
+        {
+            const double xx = b.inertia[0], yy = b.inertia[1], zz = b.inertia[2];
+            const double xy = b.inertia[3], xz = b.inertia[4], yz = b.inertia[5];
+            const double c00 = yy * zz - yz * yz, c01 = xz * yz - xy * zz, c02 = xy * yz - xz * yy;
+            const double det = xx * c00 + xy * c01 + xz * c02;
+            double inv[6] = {0, 0, 0, 0, 0, 0};
+            if (std::fabs(det) >= 1e-20) {
+                const double c11 = xx * zz - xz * xz, c12 = xy * xz - xx * yz, c22 = xx * yy - xy * xy;
+                const double r = 1.0 / det;
+                inv[0] = c00 * r;
+                inv[1] = c11 * r;
+                inv[2] = c22 * r;
+                inv[3] = c01 * r;
+                inv[4] = c02 * r;
+                inv[5] = c12 * r;
+            }
+            for (int k = 0; k < 6; k++) t.Icinv[k] = T(inv[k]);
+        }
+        for (int k = 0; k < 6; k++) t.geom[k] = T(b.geom_params[k]);
+        for (int k = 0; k < 3; k++) t.gpos[k] = T(b.geom_origin_pos[k]);
+        for (int k = 0; k < 9; k++) t.grot[k] = T(b.geom_origin_rot[k]);
+        t.gk = T(cfg.contact && (int)cfg.gk.size() > i ? cfg.gk[i] : 0.0);
+        t.gd = T(cfg.contact && (int)cfg.gd.size() > i ? cfg.gd[i] : 0.0);
+
+        // structure flags
+        int flags = 0;
+        const double* R = b.ptj_rot;
+        const bool rot_id = R[0] == 1.0 && R[1] == 0.0 && R[2] == 0.0 && R[3] == 0.0 && R[4] == 1.0 &&
+                            R[5] == 0.0 && R[6] == 0.0 && R[7] == 0.0 && R[8] == 1.0;
+        if (!rot_id) flags |= F_PTJ_ROT;
+        if (b.ptj_pos[0] != 0.0 || b.ptj_pos[1] != 0.0 || b.ptj_pos[2] != 0.0) flags |= F_PTJ_POS;
+        if (nd == 1 && b.has_limits) flags |= F_LIMITS;
+        if (nd == 1 && b.friction_loss > 0.0) flags |= F_FRICTION;
+        if (nd == 1 && b.stiffness != 0.0) flags |= F_SPRING;
+        d.axis_k = -1;
+        if (nd == 1)
+            for (int k = 0; k < 3; k++) {
+                bool unit = true;
+                for (int q = 0; q < 3; q++) unit = unit && (b.axis[q] == (q == k ? 1.0 : 0.0));
+                if (unit) d.axis_k = k;
+            }
+        if (i + 1 < nb && m->bodies[i + 1].parent == i) flags |= F_CHAIN;
+        for (int j = i + 2; j < nb; j++)
+            if (m->bodies[j].parent == i) flags |= F_BRANCH;
+        d.gtype = b.geom_type;
+        d.npts = b.geom_type == 2 ? 8 : 1;
+        if (b.geom_type != 0) info.collidable++;
+
+        // scratch layout of this body
+        d.s_xj = next;
+        next += b.joint_type == J_REVOLUTE ? 2 : ((b.joint_type == J_BALL || b.joint_type == J_FREE) ? 9 : 0);
+        d.s_vw = next;
+        next += nd > 1 ? 6 * nd : 6;
+        d.s_w0 = next;
+        next += nd;
+        d.s_f = -1;
+        if (cfg.contact && b.geom_type != 0) {
+            flags |= F_CONTACT;
+            d.s_f = next;
+            next += 6;
+        }
+        d.s_acc = d.s_vold = d.s_acca = d.s_wx = -1;
+        if (flags & F_BRANCH) {
+            d.s_acc = next;
+            next += 27;
+            d.s_vold = next;
+            next += 6;
+            d.s_acca = next;
+            next += 6;
+            if (cfg.contact) {
+                d.s_wx = next;
+                next += 12;
+            }
+        }
+        d.flags = flags;
+    }
+    for (int j = 0; j < nv; j++) pdmap[j] = -1;
+    for (int k = 0; k < npd; k++) {
+        pd[k].kp = T(cfg.pd[k].kp);
+        pd[k].kd = T(cfg.pd[k].kd);
+        pd[k].maxf = T(cfg.pd[k].max_force);
+        pd[k].qi = cfg.pd[k].q_index;
+        pd[k].vi = cfg.pd[k].v_index;
+        pdmap[cfg.pd[k].v_index] = k;
+    }
+    info.scratch = next;
+    return info;
+}
+
+// Algorithmic flop count of one steady-state world-step (flops.cpp).
+struct FlopCount {
+    double flops = 0, transcendentals = 0;
+};
+FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg);
+
+}  // namespace pz

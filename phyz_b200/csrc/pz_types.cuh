@@ -1,0 +1,385 @@
+// Spatial-algebra value types of the B200 stepper, in the reduced form the
+// kernel computes in:
+//
+//   * spatial vectors are [angular; linear] (Featherstone order, as phyz's
+//     tang::SpatialVec, crates/phyz-math/src/spatial.rs:3-12);
+//   * an articulated inertia is kept as its three distinct 3x3 blocks
+//     |Ia  H|        Ia, M symmetric (6 entries each), H full (9):
+//     |H^T M|        21 numbers instead of phyz's dense 36;
+//   * Plücker transforms (tang::SpatialTransform, spatial.rs:24-35) are
+//     applied as a rotation E followed by a translation r, never as 6x6
+//     matrices: X = [E 0; -E r^x E] (phyz_kernels.cu:180-200 builds the
+//     same matrix densely).
+//
+// Everything is templated on the scalar T: float and double on the device,
+// and a counting scalar on the host, which is how the algorithmic flop
+// count of a world-step is taken from this exact code.
+#pragma once
+
+#if defined(__CUDACC__)
+#define PZ_HD __host__ __device__ __forceinline__
+#define PZ_OUTLINE __host__ __device__ __noinline__
+#else
+#define PZ_HD inline
+#define PZ_OUTLINE inline
+#endif
+
+#if defined(__CUDA_ARCH__)
+#include <cuda_runtime.h>
+#endif
+
+namespace pz {
+
+// ── scalar shims (device versions; the host counting scalar overloads these) ──
+#if defined(__CUDA_ARCH__)
+__device__ __forceinline__ void pz_sincos(float x, float* s, float* c) { sincosf(x, s, c); }
+__device__ __forceinline__ void pz_sincos(double x, double* s, double* c) { sincos(x, s, c); }
+__device__ __forceinline__ float pz_sqrt(float x) { return sqrtf(x); }
+__device__ __forceinline__ double pz_sqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ float pz_atan2(float y, float x) { return atan2f(y, x); }
+__device__ __forceinline__ double pz_atan2(double y, double x) { return atan2(y, x); }
+__device__ __forceinline__ float pz_tanh(float x) { return tanhf(x); }
+__device__ __forceinline__ double pz_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float pz_abs(float x) { return fabsf(x); }
+__device__ __forceinline__ double pz_abs(double x) { return fabs(x); }
+__device__ __forceinline__ float pz_min(float a, float b) { return fminf(a, b); }
+__device__ __forceinline__ double pz_min(double a, double b) { return fmin(a, b); }
+__device__ __forceinline__ float pz_max(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ double pz_max(double a, double b) { return fmax(a, b); }
+__device__ __forceinline__ bool pz_finite(float x) { return isfinite(x); }
+__device__ __forceinline__ bool pz_finite(double x) { return isfinite(x); }
+#endif
+
+// Small-angle threshold of the exp/log maps: f64 uses f64::EPSILON like
+// crates/phyz-math/src/lib.rs:48,67; f32 uses the 1e-6 of the reference's
+// f32 kernels (phyz_kernels.cu:262,292).
+template <class T> struct Eps;
+template <> struct Eps<float> { static constexpr double quat = 1e-6; };
+template <> struct Eps<double> { static constexpr double quat = 2.220446049250313e-16; };
+
+// ── 3-vectors ──────────────────────────────────────────────────────────────
+template <class T>
+struct V3 {
+    T x, y, z;
+};
+template <class T>
+PZ_HD V3<T> mk3(T x, T y, T z) {
+    V3<T> r;
+    r.x = x;
+    r.y = y;
+    r.z = z;
+    return r;
+}
+template <class T>
+PZ_HD V3<T> zero3() {
+    return mk3<T>(T(0), T(0), T(0));
+}
+template <class T>
+PZ_HD V3<T> operator+(const V3<T>& a, const V3<T>& b) {
+    return mk3<T>(a.x + b.x, a.y + b.y, a.z + b.z);
+}
+template <class T>
+PZ_HD V3<T> operator-(const V3<T>& a, const V3<T>& b) {
+    return mk3<T>(a.x - b.x, a.y - b.y, a.z - b.z);
+}
+template <class T>
+PZ_HD V3<T> operator-(const V3<T>& a) {
+    return mk3<T>(-a.x, -a.y, -a.z);
+}
+template <class T>
+PZ_HD V3<T> operator*(const V3<T>& a, const T& s) {
+    return mk3<T>(a.x * s, a.y * s, a.z * s);
+}
+template <class T>
+PZ_HD T dot(const V3<T>& a, const V3<T>& b) {
+    return a.x * b.x + a.y * b.y + a.z * b.z;
+}
+template <class T>
+PZ_HD V3<T> cross(const V3<T>& a, const V3<T>& b) {
+    return mk3<T>(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
+}
+template <class T>
+PZ_HD T get(const V3<T>& a, int i) {
+    return i == 0 ? a.x : (i == 1 ? a.y : a.z);
+}
+template <int I, class T>
+PZ_HD T& at(V3<T>& a) {
+    return I == 0 ? a.x : (I == 1 ? a.y : a.z);
+}
+template <int I, class T>
+PZ_HD const T& at(const V3<T>& a) {
+    return I == 0 ? a.x : (I == 1 ? a.y : a.z);
+}
+
+// ── spatial vectors [angular; linear] ─────────────────────────────────────
+template <class T>
+struct SV {
+    V3<T> w, l;
+};
+template <class T>
+PZ_HD SV<T> mksv(const V3<T>& w, const V3<T>& l) {
+    SV<T> r;
+    r.w = w;
+    r.l = l;
+    return r;
+}
+template <class T>
+PZ_HD SV<T> zerosv() {
+    return mksv<T>(zero3<T>(), zero3<T>());
+}
+template <class T>
+PZ_HD SV<T> operator+(const SV<T>& a, const SV<T>& b) {
+    return mksv<T>(a.w + b.w, a.l + b.l);
+}
+template <class T>
+PZ_HD SV<T> operator-(const SV<T>& a, const SV<T>& b) {
+    return mksv<T>(a.w - b.w, a.l - b.l);
+}
+template <class T>
+PZ_HD T dot(const SV<T>& a, const SV<T>& b) {
+    return dot(a.w, b.w) + dot(a.l, b.l);
+}
+// motion cross v x m (phyz_kernels.cu:110-116)
+template <class T>
+PZ_HD SV<T> crm(const SV<T>& v, const SV<T>& m) {
+    return mksv<T>(cross(v.w, m.w), cross(v.w, m.l) + cross(v.l, m.w));
+}
+// force cross v x* f (phyz_kernels.cu:118-124)
+template <class T>
+PZ_HD SV<T> crf(const SV<T>& v, const SV<T>& f) {
+    return mksv<T>(cross(v.w, f.w) + cross(v.l, f.l), cross(v.w, f.l));
+}
+template <class T>
+PZ_HD T svget(const SV<T>& a, int i) {
+    return i < 3 ? get(a.w, i) : get(a.l, i - 3);
+}
+
+// symmetric 3x3 packed as xx, yy, zz, xy, xz, yz
+PZ_HD constexpr int sidx(int i, int j) {
+    return i == j ? i : (i + j == 1 ? 3 : (i + j == 2 ? 4 : 5));
+}
+
+// ── articulated inertia in three blocks ────────────────────────────────────
+template <class T>
+struct AI {
+    T a[6];  // angular-angular (symmetric)
+    T h[9];  // angular-linear, row-major
+    T m[6];  // linear-linear (symmetric)
+};
+
+template <class T>
+PZ_HD void ai_zero(AI<T>& I) {
+#pragma unroll
+    for (int k = 0; k < 6; k++) I.a[k] = T(0), I.m[k] = T(0);
+#pragma unroll
+    for (int k = 0; k < 9; k++) I.h[k] = T(0);
+}
+template <class T>
+PZ_HD void ai_add(AI<T>& I, const AI<T>& B) {
+#pragma unroll
+    for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + B.a[k], I.m[k] = I.m[k] + B.m[k];
+#pragma unroll
+    for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + B.h[k];
+}
+template <class T>
+PZ_HD V3<T> symv(const T* A, const V3<T>& x) {
+    return mk3<T>(A[0] * x.x + A[3] * x.y + A[4] * x.z, A[3] * x.x + A[1] * x.y + A[5] * x.z,
+                  A[4] * x.x + A[5] * x.y + A[2] * x.z);
+}
+template <class T>
+PZ_HD V3<T> m3v(const T* H, const V3<T>& x) {
+    return mk3<T>(H[0] * x.x + H[1] * x.y + H[2] * x.z, H[3] * x.x + H[4] * x.y + H[5] * x.z,
+                  H[6] * x.x + H[7] * x.y + H[8] * x.z);
+}
+template <class T>
+PZ_HD V3<T> m3tv(const T* H, const V3<T>& x) {
+    return mk3<T>(H[0] * x.x + H[3] * x.y + H[6] * x.z, H[1] * x.x + H[4] * x.y + H[7] * x.z,
+                  H[2] * x.x + H[5] * x.y + H[8] * x.z);
+}
+// I v = [Ia w + H l; H^T w + M l]
+template <class T>
+PZ_HD SV<T> ai_mul(const AI<T>& I, const SV<T>& v) {
+    return mksv<T>(symv(I.a, v.w) + m3v(I.h, v.l), m3tv(I.h, v.w) + symv(I.m, v.l));
+}
+
+// ── transforms ─────────────────────────────────────────────────────────────
+// A rotation E as a row-major 3x3.
+template <class T>
+struct R3 {
+    T m[9];
+};
+template <class T>
+PZ_HD V3<T> rmul(const R3<T>& E, const V3<T>& x) {
+    return m3v(E.m, x);
+}
+template <class T>
+PZ_HD V3<T> rtmul(const R3<T>& E, const V3<T>& x) {
+    return m3tv(E.m, x);
+}
+
+// apply_motion with E, r: [E w; E (l - r x w)] (phyz_kernels.cu:314-320)
+template <class T>
+PZ_HD SV<T> xm_apply(const R3<T>& E, const V3<T>& r, const SV<T>& m) {
+    return mksv<T>(rmul(E, m.w), rmul(E, m.l - cross(r, m.w)));
+}
+template <class T>
+PZ_HD SV<T> xm_apply_rot(const R3<T>& E, const SV<T>& m) {
+    return mksv<T>(rmul(E, m.w), rmul(E, m.l));
+}
+template <class T>
+PZ_HD SV<T> xm_apply_trans(const V3<T>& r, const SV<T>& m) {
+    return mksv<T>(m.w, m.l - cross(r, m.w));
+}
+// inv_apply_force: X^T f = [E^T t + r x E^T f; E^T f] (phyz_kernels.cu:322-329)
+template <class T>
+PZ_HD SV<T> xf_tapply_rot(const R3<T>& E, const SV<T>& f) {
+    return mksv<T>(rtmul(E, f.w), rtmul(E, f.l));
+}
+template <class T>
+PZ_HD SV<T> xf_tapply_trans(const V3<T>& r, const SV<T>& f) {
+    return mksv<T>(f.w + cross(r, f.l), f.l);
+}
+
+// Planar rotation about the coordinate axis K by the angle whose cosine
+// and sine are (c, s): E e_i = c e_i + s e_j, E e_j = -s e_i + c e_j with
+// (i, j, K) cyclic. This is revolute_rot of a unit coordinate axis
+// (phyz_kernels.cu:245-256 / joint.rs:259-266).
+template <int K, class T>
+PZ_HD V3<T> prot(const T& c, const T& s, const V3<T>& x) {
+    constexpr int I = (K + 1) % 3, J = (K + 2) % 3;
+    V3<T> r = x;
+    at<I>(r) = c * at<I>(x) - s * at<J>(x);
+    at<J>(r) = s * at<I>(x) + c * at<J>(x);
+    return r;
+}
+template <int K, class T>
+PZ_HD V3<T> prot_t(const T& c, const T& s, const V3<T>& x) {
+    constexpr int I = (K + 1) % 3, J = (K + 2) % 3;
+    V3<T> r = x;
+    at<I>(r) = c * at<I>(x) + s * at<J>(x);
+    at<J>(r) = -s * at<I>(x) + c * at<J>(x);
+    return r;
+}
+
+// Inertia congruence by a rotation: I <- X^T I X for X = [E 0; 0 E]:
+// Ia <- E^T Ia E, H <- E^T H E, M <- E^T M E.
+template <class T>
+PZ_HD void sym_rot(const R3<T>& E, T* A) {
+    // B = A E (full), A' = E^T B (symmetric part)
+    T B[9];
+#pragma unroll
+    for (int i = 0; i < 3; i++)
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            B[i * 3 + j] = A[sidx(i, 0)] * E.m[0 * 3 + j] + A[sidx(i, 1)] * E.m[1 * 3 + j] +
+                           A[sidx(i, 2)] * E.m[2 * 3 + j];
+#pragma unroll
+    for (int i = 0; i < 3; i++)
+#pragma unroll
+        for (int j = i; j < 3; j++)
+            A[sidx(i, j)] = E.m[0 * 3 + i] * B[0 * 3 + j] + E.m[1 * 3 + i] * B[1 * 3 + j] +
+                            E.m[2 * 3 + i] * B[2 * 3 + j];
+}
+template <class T>
+PZ_HD void full_rot(const R3<T>& E, T* H) {
+    T B[9];
+#pragma unroll
+    for (int i = 0; i < 3; i++)
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            B[i * 3 + j] =
+                H[i * 3 + 0] * E.m[0 * 3 + j] + H[i * 3 + 1] * E.m[1 * 3 + j] + H[i * 3 + 2] * E.m[2 * 3 + j];
+#pragma unroll
+    for (int i = 0; i < 3; i++)
+#pragma unroll
+        for (int j = 0; j < 3; j++)
+            H[i * 3 + j] =
+                E.m[0 * 3 + i] * B[0 * 3 + j] + E.m[1 * 3 + i] * B[1 * 3 + j] + E.m[2 * 3 + i] * B[2 * 3 + j];
+}
+template <class T>
+PZ_HD void ai_rot(const R3<T>& E, AI<T>& I) {
+    sym_rot(E, I.a);
+    full_rot(E, I.h);
+    sym_rot(E, I.m);
+}
+
+// Planar versions of the same congruence (rotation about axis K).
+template <int K, class T>
+PZ_HD void sym_prot(const T& c, const T& s, const T& cc, const T& ss, const T& cs, T* A) {
+    constexpr int I = (K + 1) % 3, J = (K + 2) % 3;
+    const T aii = A[sidx(I, I)], ajj = A[sidx(J, J)], aij = A[sidx(I, J)];
+    const T aik = A[sidx(I, K)], ajk = A[sidx(J, K)];
+    const T two_cs_aij = (cs + cs) * aij;
+    A[sidx(I, I)] = cc * aii + two_cs_aij + ss * ajj;
+    A[sidx(J, J)] = ss * aii - two_cs_aij + cc * ajj;
+    A[sidx(I, J)] = cs * (ajj - aii) + (cc - ss) * aij;
+    A[sidx(I, K)] = c * aik + s * ajk;
+    A[sidx(J, K)] = c * ajk - s * aik;
+}
+template <int K, class T>
+PZ_HD void full_prot(const T& c, const T& s, T* H) {
+    constexpr int I = (K + 1) % 3, J = (K + 2) % 3;
+    // columns: B = H E
+#pragma unroll
+    for (int r = 0; r < 3; r++) {
+        const T hi = H[r * 3 + I], hj = H[r * 3 + J];
+        H[r * 3 + I] = c * hi + s * hj;
+        H[r * 3 + J] = c * hj - s * hi;
+    }
+    // rows: H' = E^T B
+#pragma unroll
+    for (int q = 0; q < 3; q++) {
+        const T hi = H[I * 3 + q], hj = H[J * 3 + q];
+        H[I * 3 + q] = c * hi + s * hj;
+        H[J * 3 + q] = c * hj - s * hi;
+    }
+}
+template <int K, class T>
+PZ_HD void ai_prot(const T& c, const T& s, AI<T>& I) {
+    const T cc = c * c, ss = s * s, cs = c * s;
+    sym_prot<K>(c, s, cc, ss, cs, I.a);
+    full_prot<K>(c, s, I.h);
+    sym_prot<K>(c, s, cc, ss, cs, I.m);
+}
+
+// Inertia congruence by a translation r (X = [1 0; -r^x 1]):
+//   M' = M, H' = H + r^x M, Ia' = Ia - Z - Z^T - (r^x M) r^x with Z = H r^x.
+// Row i of (A r^x) is (row i of A) x r; column j of (r^x M) is r x M e_j.
+template <class T>
+PZ_HD void ai_trans(const V3<T>& r, AI<T>& I) {
+    // T1 = r^x M (full), columns r x M_col
+    T t1[9];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        V3<T> col = mk3<T>(I.m[sidx(0, j)], I.m[sidx(1, j)], I.m[sidx(2, j)]);
+        V3<T> rc = cross(r, col);
+        t1[0 * 3 + j] = rc.x;
+        t1[1 * 3 + j] = rc.y;
+        t1[2 * 3 + j] = rc.z;
+    }
+    // Z = H r^x (rows of H crossed with r)
+    T z[9];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        V3<T> row = mk3<T>(I.h[i * 3 + 0], I.h[i * 3 + 1], I.h[i * 3 + 2]);
+        V3<T> rr = cross(row, r);
+        z[i * 3 + 0] = rr.x;
+        z[i * 3 + 1] = rr.y;
+        z[i * 3 + 2] = rr.z;
+    }
+    // W = T1 r^x (symmetric): rows of T1 crossed with r
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        V3<T> row = mk3<T>(t1[i * 3 + 0], t1[i * 3 + 1], t1[i * 3 + 2]);
+        V3<T> w = cross(row, r);
+#pragma unroll
+        for (int j = i; j < 3; j++) {
+            const T wij = get(w, j);
+            I.a[sidx(i, j)] = I.a[sidx(i, j)] - z[i * 3 + j] - z[j * 3 + i] - wij;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + t1[k];
+}
+
+}  // namespace pz

@@ -1,0 +1,967 @@
+// One world's fused multi-step rollout: Featherstone's articulated-body
+// algorithm with penalty ground contact and the semi-implicit integrator,
+// written once for the device kernel and for the host flop counter.
+//
+// Semantics follow phyz's CPU referee (crates/phyz-rigid/src/aba.rs:147-420,
+// integrate.rs:41-91, actuation.rs:18-54, joint.rs:232-316) and the step
+// order of phyz-gpu's batched path (cuda/mod.rs:879-945: PD -> contact ->
+// ABA -> integrate; contact law phyz_kernels.cu:804-965). The formulation is
+// this kernel's own:
+//
+//   * a step is two sweeps over the bodies instead of the reference's four
+//     launches: a backward sweep (ABA pass 2) and a forward sweep that
+//     finishes the step (pass 3 + integration) and immediately starts the
+//     next one (pass 1 + FK + contact of the new state), so q, v and every
+//     per-body intermediate stay on chip for the whole rollout;
+//   * articulated inertias are 21-number block forms and transforms are
+//     rotate-then-translate (pz_types.cuh); the 1-DOF path is scalar; a hinge
+//     about a coordinate axis rotates with a planar formula;
+//   * a serial chain passes its recursion state in registers ("carry"); only
+//     bodies with a child that is not the next body ("branch" bodies) keep
+//     accumulators in scratch.
+//
+// Per-world scratch is accessed through `Scr`: S(slot) is this world's
+// element of a slot, S.prefetch(slot, src) an asynchronous copy of one
+// control input into a slot, S.wait() the fence before reading them.
+#pragma once
+
+#include "pz_model.cuh"
+#include "pz_types.cuh"
+
+namespace pz {
+
+// ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
+template <class T>
+struct Q4 {
+    T w, x, y, z;
+};
+template <class T>
+PZ_HD Q4<T> qexp(const V3<T>& om) {
+    const T ang = pz_sqrt(dot(om, om));
+    Q4<T> q;
+    if (ang < T(Eps<T>::quat)) {
+        q.w = T(1);
+        q.x = om.x * T(0.5);
+        q.y = om.y * T(0.5);
+        q.z = om.z * T(0.5);
+        return q;
+    }
+    T s, c;
+    pz_sincos(ang * T(0.5), &s, &c);
+    const T k = s / ang;
+    q.w = c;
+    q.x = om.x * k;
+    q.y = om.y * k;
+    q.z = om.z * k;
+    return q;
+}
+template <class T>
+PZ_HD V3<T> qlog(const Q4<T>& q) {
+    const V3<T> v = mk3<T>(q.x, q.y, q.z);
+    const T n = pz_sqrt(dot(v, v));
+    if (n < T(Eps<T>::quat)) return v * T(2);
+    const T ang = T(2) * pz_atan2(n, q.w);
+    return v * (ang / n);
+}
+template <class T>
+PZ_HD Q4<T> qmul(const Q4<T>& a, const Q4<T>& b) {
+    Q4<T> r;
+    r.w = a.w * b.w - a.x * b.x - a.y * b.y - a.z * b.z;
+    r.x = a.w * b.x + a.x * b.w + a.y * b.z - a.z * b.y;
+    r.y = a.w * b.y - a.x * b.z + a.y * b.w + a.z * b.x;
+    r.z = a.w * b.z + a.x * b.y - a.y * b.x + a.z * b.w;
+    return r;
+}
+template <class T>
+PZ_HD Q4<T> qnormalize(const Q4<T>& q) {
+    const T n = pz_sqrt(q.w * q.w + q.x * q.x + q.y * q.y + q.z * q.z);
+    Q4<T> r;
+    r.w = q.w / n;
+    r.x = q.x / n;
+    r.y = q.y / n;
+    r.z = q.z / n;
+    return r;
+}
+template <class T>
+PZ_HD V3<T> qrotate(const Q4<T>& q, const V3<T>& p) {
+    const V3<T> u = mk3<T>(q.x, q.y, q.z);
+    const V3<T> t = cross(u, p) * T(2);
+    return p + t * q.w + cross(u, t);
+}
+// Joint rotation of a ball / free joint: (to_matrix(exp(w)))^T, joint.rs:276-306.
+template <class T>
+PZ_HD R3<T> qjoint_rot(const Q4<T>& q) {
+    const T w = q.w, x = q.x, y = q.y, z = q.z;
+    R3<T> E;  // transpose of the rotation matrix of q
+    E.m[0] = T(1) - T(2) * (y * y + z * z);
+    E.m[3] = T(2) * (x * y - w * z);
+    E.m[6] = T(2) * (x * z + w * y);
+    E.m[1] = T(2) * (x * y + w * z);
+    E.m[4] = T(1) - T(2) * (x * x + z * z);
+    E.m[7] = T(2) * (y * z - w * x);
+    E.m[2] = T(2) * (x * z - w * y);
+    E.m[5] = T(2) * (y * z + w * x);
+    E.m[8] = T(1) - T(2) * (x * x + y * y);
+    return E;
+}
+
+// Hinge rotation about a general axis a: I + s K + (1 - c) K^2, K = a^x
+// (joint.rs:259-266; equal to phyz_kernels.cu:245-256 for a unit axis).
+template <class T>
+PZ_HD R3<T> hinge_matrix(const V3<T>& a, const T& c, const T& s) {
+    const T t = T(1) - c;
+    const T aa = dot(a, a);
+    R3<T> E;
+    E.m[0] = T(1) + t * (a.x * a.x - aa);
+    E.m[1] = t * (a.x * a.y) - s * a.z;
+    E.m[2] = t * (a.x * a.z) + s * a.y;
+    E.m[3] = t * (a.x * a.y) + s * a.z;
+    E.m[4] = T(1) + t * (a.y * a.y - aa);
+    E.m[5] = t * (a.y * a.z) - s * a.x;
+    E.m[6] = t * (a.x * a.z) - s * a.y;
+    E.m[7] = t * (a.y * a.z) + s * a.x;
+    E.m[8] = T(1) + t * (a.z * a.z - aa);
+    return E;
+}
+
+template <class T>
+PZ_HD V3<T> ld3(const T* p) {
+    return mk3<T>(p[0], p[1], p[2]);
+}
+template <class T>
+PZ_HD R3<T> ld9(const T* p) {
+    R3<T> E;
+#pragma unroll
+    for (int k = 0; k < 9; k++) E.m[k] = p[k];
+    return E;
+}
+
+// ── joint transform of one body, decoded from scratch ─────────────────────
+template <class T>
+struct JX {
+    T c, s;   // hinge: cos, sin of -q
+    R3<T> E;  // rotation (ball, free, general-axis hinge)
+    V3<T> r;  // translation (prismatic, free)
+};
+
+template <class T, class Scr>
+PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
+    JX<T> j;
+    switch (bi.jtype) {
+        case J_REVOLUTE:
+            j.c = S(bi.s_xj);
+            j.s = S(bi.s_xj + 1);
+            if (bi.axis_k < 0) j.E = hinge_matrix(ld3(bt.axis), j.c, j.s);
+            break;
+        case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
+        case J_BALL:
+#pragma unroll
+            for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
+            break;
+        case J_FREE:
+#pragma unroll
+            for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
+            j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
+            break;
+        default: break;
+    }
+    return j;
+}
+
+// Compute the joint transform data of body i from q and store it.
+template <class T, class Scr>
+PZ_HD JX<T> make_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
+    JX<T> j;
+    switch (bi.jtype) {
+        case J_REVOLUTE: {
+            T s, c;
+            pz_sincos(-S(bi.off), &s, &c);
+            j.c = c;
+            j.s = s;
+            S(bi.s_xj) = c;
+            S(bi.s_xj + 1) = s;
+            if (bi.axis_k < 0) j.E = hinge_matrix(ld3(bt.axis), c, s);
+            break;
+        }
+        case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
+        case J_BALL:
+        case J_FREE: {
+            const Q4<T> q = qexp(mk3<T>(S(bi.off), S(bi.off + 1), S(bi.off + 2)));
+            j.E = qjoint_rot(q);
+#pragma unroll
+            for (int k = 0; k < 9; k++) S(bi.s_xj + k) = j.E.m[k];
+            if (bi.jtype == J_FREE) j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
+            break;
+        }
+        default: break;
+    }
+    return j;
+}
+
+// Planar hinge rotation with a runtime axis index.
+template <class T>
+PZ_HD V3<T> hrot(int k, const T& c, const T& s, const V3<T>& x) {
+    return k == 0 ? prot<0>(c, s, x) : (k == 1 ? prot<1>(c, s, x) : prot<2>(c, s, x));
+}
+template <class T>
+PZ_HD V3<T> hrot_t(int k, const T& c, const T& s, const V3<T>& x) {
+    return k == 0 ? prot_t<0>(c, s, x) : (k == 1 ? prot_t<1>(c, s, x) : prot_t<2>(c, s, x));
+}
+
+// The rotation part of X_tree = X_J X_ptj applied to a 3-vector: R_J R_ptj x.
+template <class T>
+PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> x) {
+    if (bi.flags & F_PTJ_ROT) x = m3v(bt.ptj_rot, x);
+    switch (bi.jtype) {
+        case J_REVOLUTE: x = bi.axis_k >= 0 ? hrot(bi.axis_k, j.c, j.s, x) : rmul(j.E, x); break;
+        case J_BALL:
+        case J_FREE: x = rmul(j.E, x); break;
+        default: break;
+    }
+    return x;
+}
+// Origin of the body in its parent: p_ptj + R_ptj^T p_J (tang compose).
+template <class T>
+PZ_HD V3<T> tree_pos(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j) {
+    V3<T> p = ld3(bt.ptj_pos);
+    if (bi.jtype == J_PRISMATIC || bi.jtype == J_FREE)
+        p = p + ((bi.flags & F_PTJ_ROT) ? m3tv(bt.ptj_rot, j.r) : j.r);
+    return p;
+}
+
+// X_tree m for a motion vector (X_ptj first, then X_J).
+template <class T>
+PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
+    if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
+    if (bi.flags & F_PTJ_ROT) {
+        const R3<T> P = ld9(bt.ptj_rot);
+        m = xm_apply_rot(P, m);
+    }
+    switch (bi.jtype) {
+        case J_REVOLUTE:
+            if (bi.axis_k >= 0)
+                m = mksv<T>(hrot(bi.axis_k, j.c, j.s, m.w), hrot(bi.axis_k, j.c, j.s, m.l));
+            else
+                m = xm_apply_rot(j.E, m);
+            break;
+        case J_PRISMATIC: m = xm_apply_trans(j.r, m); break;
+        case J_BALL: m = xm_apply_rot(j.E, m); break;
+        case J_FREE: m = xm_apply_rot(j.E, xm_apply_trans(j.r, m)); break;
+        default: break;
+    }
+    return m;
+}
+
+// X_tree^T f for a force vector (phyz's inv_apply_force).
+template <class T>
+PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f) {
+    switch (bi.jtype) {
+        case J_REVOLUTE:
+            if (bi.axis_k >= 0)
+                f = mksv<T>(hrot_t(bi.axis_k, j.c, j.s, f.w), hrot_t(bi.axis_k, j.c, j.s, f.l));
+            else
+                f = xf_tapply_rot(j.E, f);
+            break;
+        case J_PRISMATIC: f = xf_tapply_trans(j.r, f); break;
+        case J_BALL: f = xf_tapply_rot(j.E, f); break;
+        case J_FREE: f = xf_tapply_trans(j.r, xf_tapply_rot(j.E, f)); break;
+        default: break;
+    }
+    if (bi.flags & F_PTJ_ROT) {
+        const R3<T> P = ld9(bt.ptj_rot);
+        f = xf_tapply_rot(P, f);
+    }
+    if (bi.flags & F_PTJ_POS) f = xf_tapply_trans(ld3(bt.ptj_pos), f);
+    return f;
+}
+
+// X_tree^T I X_tree in place (J part first, then ptj).
+template <class T>
+PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I) {
+    switch (bi.jtype) {
+        case J_REVOLUTE:
+            if (bi.axis_k == 0)
+                ai_prot<0>(j.c, j.s, I);
+            else if (bi.axis_k == 1)
+                ai_prot<1>(j.c, j.s, I);
+            else if (bi.axis_k == 2)
+                ai_prot<2>(j.c, j.s, I);
+            else
+                ai_rot(j.E, I);
+            break;
+        case J_PRISMATIC: ai_trans(j.r, I); break;
+        case J_BALL: ai_rot(j.E, I); break;
+        case J_FREE:
+            ai_rot(j.E, I);
+            ai_trans(j.r, I);
+            break;
+        default: break;
+    }
+    if (bi.flags & F_PTJ_ROT) {
+        const R3<T> P = ld9(bt.ptj_rot);
+        ai_rot(P, I);
+    }
+    if (bi.flags & F_PTJ_POS) ai_trans(ld3(bt.ptj_pos), I);
+}
+
+// S qd of body i (aba.rs:15-30).
+template <class T, class Scr>
+PZ_HD SV<T> joint_vel(const BodyI& bi, const BodyT<T>& bt, const Scr& S, int nv) {
+    const int o = nv + bi.off;
+    switch (bi.jtype) {
+        case J_REVOLUTE: return mksv<T>(ld3(bt.axis) * S(o), zero3<T>());
+        case J_PRISMATIC: return mksv<T>(zero3<T>(), ld3(bt.axis) * S(o));
+        case J_BALL: return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), zero3<T>());
+        case J_FREE: return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), mk3<T>(S(o + 3), S(o + 4), S(o + 5)));
+        default: return zerosv<T>();
+    }
+}
+
+template <class T, class Scr>
+PZ_HD SV<T> ld_sv(const Scr& S, int s) {
+    return mksv<T>(mk3<T>(S(s), S(s + 1), S(s + 2)), mk3<T>(S(s + 3), S(s + 4), S(s + 5)));
+}
+template <class T, class Scr>
+PZ_HD void st_sv(const Scr& S, int s, const SV<T>& v) {
+    S(s) = v.w.x;
+    S(s + 1) = v.w.y;
+    S(s + 2) = v.w.z;
+    S(s + 3) = v.l.x;
+    S(s + 4) = v.l.y;
+    S(s + 5) = v.l.z;
+}
+
+// Generalized input force on DOF d: the control (or the PD servo output,
+// phyz_kernels.cu:464-483) plus the passive terms of joint.rs:232-247.
+template <class T, class Scr>
+PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S, int k) {
+    const int d = bi.off + k;
+    const T qd = S(M.nv + d);
+    T in = S(bi.s_w0 + k);
+    const int pdi = M.pd_of_dof[d];
+    if (pdi >= 0) {
+        const PdT<T>& e = M.pd[pdi];
+        const T tau = e.kp * (in - S(e.qi)) - e.kd * S(M.nv + e.vi);
+        in = pz_min(pz_max(tau, -e.maxf), e.maxf);
+    }
+    T f = in - bt.damping * qd;
+    if (bi.ndof == 1) {
+        const T q = S(d);
+        if (bi.flags & F_SPRING) f = f - bt.stiffness * (q - bt.spring_ref);
+        if (bi.flags & F_LIMITS) {
+            T depth = T(0), sign = T(0);
+            if (q < bt.lim_lo) {
+                depth = bt.lim_lo - q;
+                sign = T(1);
+            } else if (q > bt.lim_hi) {
+                depth = q - bt.lim_hi;
+                sign = T(-1);
+            }
+            const T inward = pz_max(-sign * qd, T(0));
+            f = f + sign * (bt.lim_k * depth + bt.lim_d * inward);
+        }
+        if (bi.flags & F_FRICTION) f = f - bt.fric * pz_tanh(qd / T(1e-3));
+    }
+    return f;
+}
+
+// Dense element (r, c) of an articulated inertia.
+template <class T>
+PZ_HD T ai_el(const AI<T>& I, int r, int c) {
+    if (r < 3) return c < 3 ? I.a[sidx(r, c)] : I.h[r * 3 + (c - 3)];
+    return c < 3 ? I.h[c * 3 + (r - 3)] : I.m[sidx(r - 3, c - 3)];
+}
+template <class T>
+PZ_HD void ai_sub_el(AI<T>& I, int r, int c, const T& v) {  // only r <= c for symmetric blocks
+    if (r < 3) {
+        if (c < 3)
+            I.a[sidx(r, c)] = I.a[sidx(r, c)] - v;
+        else
+            I.h[r * 3 + (c - 3)] = I.h[r * 3 + (c - 3)] - v;
+    } else {
+        I.m[sidx(r - 3, c - 3)] = I.m[sidx(r - 3, c - 3)] - v;
+    }
+}
+
+// Multi-DOF joint (ball: S = [1;0], free: S = 1, both unit columns e_0..e_{ND-1}):
+// U = I S, D = S^T U + d_extra, W = U D^-1, w0 = D^-1 u, stored; when the
+// body has a parent, I <- I - W U^T and p <- p + I c + U w0. Returns false
+// when D is singular (aba.rs:291-294: the body is skipped).
+template <int ND, class T, class Scr>
+PZ_OUTLINE bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S,
+                     AI<T>& I, SV<T>& p, const SV<T>& c, bool has_parent) {
+    T U[6][ND];
+#pragma unroll
+    for (int r = 0; r < 6; r++)
+#pragma unroll
+        for (int k = 0; k < ND; k++) U[r][k] = ai_el(I, r, k);
+    // Cholesky of D = U[0..ND) + d_extra 1
+    T L[ND][ND];
+#pragma unroll
+    for (int a = 0; a < ND; a++)
+#pragma unroll
+        for (int b = 0; b < ND; b++) L[a][b] = T(0);
+    T u[ND];
+#pragma unroll
+    for (int k = 0; k < ND; k++) u[k] = dof_force(M, bi, bt, S, k) - svget(p, k);
+    bool ok = true;
+#pragma unroll
+    for (int a = 0; a < ND; a++) {
+        T d = U[a][a] + bt.d_extra;
+#pragma unroll
+        for (int k = 0; k < a; k++) d = d - L[a][k] * L[a][k];
+        if (!(d > T(0))) {
+            ok = false;
+            d = T(1);
+        }
+        const T ld = pz_sqrt(d);
+        L[a][a] = ld;
+        const T inv = T(1) / ld;
+#pragma unroll
+        for (int b = a + 1; b < ND; b++) {
+            T e = U[b][a];
+#pragma unroll
+            for (int k = 0; k < a; k++) e = e - L[b][k] * L[a][k];
+            L[b][a] = e * inv;
+        }
+    }
+    if (!ok) {
+#pragma unroll
+        for (int k = 0; k < 6 * ND; k++) S(bi.s_vw + k) = T(0);
+#pragma unroll
+        for (int k = 0; k < ND; k++) S(bi.s_w0 + k) = T(0);
+        return false;
+    }
+    // Solve D X = B for a right-hand side (forward, then backward substitution).
+    auto solve = [&](T* x) {
+#pragma unroll
+        for (int a = 0; a < ND; a++) {
+            T e = x[a];
+#pragma unroll
+            for (int k = 0; k < a; k++) e = e - L[a][k] * x[k];
+            x[a] = e / L[a][a];
+        }
+#pragma unroll
+        for (int a = ND - 1; a >= 0; a--) {
+            T e = x[a];
+#pragma unroll
+            for (int k = a + 1; k < ND; k++) e = e - L[k][a] * x[k];
+            x[a] = e / L[a][a];
+        }
+    };
+    // W row r = D^-1 U row r (D symmetric)
+    T W[6][ND];
+#pragma unroll
+    for (int r = 0; r < 6; r++) {
+        T x[ND];
+#pragma unroll
+        for (int k = 0; k < ND; k++) x[k] = U[r][k];
+        solve(x);
+#pragma unroll
+        for (int k = 0; k < ND; k++) W[r][k] = x[k];
+    }
+    solve(u);
+#pragma unroll
+    for (int k = 0; k < ND; k++) {
+#pragma unroll
+        for (int r = 0; r < 6; r++) S(bi.s_vw + k * 6 + r) = W[r][k];
+        S(bi.s_w0 + k) = u[k];
+    }
+    if (has_parent) {
+        // I <- I - W U^T over the upper triangle: covers Ia, H (r < 3 <= c) and M
+#pragma unroll
+        for (int r = 0; r < 6; r++)
+#pragma unroll
+            for (int cc = r; cc < 6; cc++) {
+                T s = T(0);
+#pragma unroll
+                for (int k = 0; k < ND; k++) s = s + W[r][k] * U[cc][k];
+                ai_sub_el(I, r, cc, s);
+            }
+        SV<T> uw;
+        T tmp[6];
+#pragma unroll
+        for (int r = 0; r < 6; r++) {
+            T s = T(0);
+#pragma unroll
+            for (int k = 0; k < ND; k++) s = s + U[r][k] * u[k];
+            tmp[r] = s;
+        }
+        uw = mksv<T>(mk3<T>(tmp[0], tmp[1], tmp[2]), mk3<T>(tmp[3], tmp[4], tmp[5]));
+        p = p + ai_mul(I, c) + uw;
+    }
+    return true;
+}
+
+// ── penalty ground contact of one body (phyz_kernels.cu:541-578, 691-725, 939-965)
+template <class T>
+PZ_HD T eff_mass(const BodyT<T>& bt, const V3<T>& r, const V3<T>& u) {
+    if (!(bt.mass > T(0))) return T(1e30);
+    const V3<T> a = cross(r - ld3(bt.com), u);
+    const T ang = pz_max(dot(a, symv(bt.Icinv, a)), T(0));
+    return T(1) / (T(1) / bt.mass + ang);
+}
+template <class T>
+PZ_HD T fsign(const T& x) {
+    return x > T(0) ? T(1) : (x < T(0) ? T(-1) : T(0));
+}
+template <class T>
+PZ_HD V3<T> support_pt(const BodyI& bi, const BodyT<T>& bt, const V3<T>& n_body, int corner) {
+    const R3<T> O = ld9(bt.grot);
+    V3<T> s = zero3<T>();
+    if (bi.gtype == 2) {  // box corner (phyz_kernels.cu:679-689)
+        s = mk3<T>(bt.geom[0] * ((corner & 1) ? T(1) : T(-1)), bt.geom[1] * ((corner & 2) ? T(1) : T(-1)),
+                   bt.geom[2] * ((corner & 4) ? T(1) : T(-1)));
+    } else {
+        const V3<T> n = rmul(O, n_body);
+        if (bi.gtype == 1) {
+            s = n * (-bt.geom[0]);
+        } else if (bi.gtype == 3) {
+            s = mk3<T>(T(0), T(0), -(bt.geom[1] * T(0.5)) * fsign(n.z)) - n * bt.geom[0];
+        } else if (bi.gtype == 4) {
+            const V3<T> radial = mk3<T>(-n.x, -n.y, T(0));
+            const T rl = pz_sqrt(dot(radial, radial));
+            V3<T> rim = zero3<T>();
+            if (rl > T(1e-6)) rim = radial * (bt.geom[0] / rl);
+            s = rim + mk3<T>(T(0), T(0), -(bt.geom[1] * T(0.5)) * fsign(n.z));
+        } else if (bi.gtype == 5) {
+            const V3<T> mn = ld3(bt.geom), mx = ld3(bt.geom + 3);
+            const V3<T> mc = (mn + mx) * T(0.5), mh = (mx - mn) * T(0.5);
+            s = mc - mk3<T>(mh.x * fsign(n.x), mh.y * fsign(n.y), mh.z * fsign(n.z));
+        }
+    }
+    return ld3(bt.gpos) + rtmul(O, s);
+}
+
+// World frame of a body: rows of the body->world rotation (row 2 is world
+// up seen in the body frame) and the origin. Normal sweeps track row 2 and
+// the height only; the sweep that writes contact state tracks all of it.
+template <class T>
+struct WF {
+    V3<T> r0, r1, up;
+    V3<T> pos;  // pos.z is the height of the origin
+};
+
+// A strided output: element k goes to base[k * stride] (null base: dropped).
+template <class T>
+struct Out {
+    T* base;
+    long long stride;
+    PZ_HD void put(int k, const T& v) const {
+        if (base) base[(long long)k * stride] = v;
+    }
+};
+
+// Contact wrench (body frame) of body i at body velocity v, and its state.
+// With `full`, the body's contact state [touching, depth, point(3),
+// force(3)] (layout.rs:68-80) goes to rows 8*i.. of `cs`.
+template <class T>
+PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const WF<T>& wf,
+                           const SV<T>& v, bool full, int i, const Out<T>& cs) {
+    SV<T> f = zerosv<T>();
+    V3<T> fw = zero3<T>();
+    T deepest = T(0), dx = T(0), dy = T(0);
+    bool any = false;
+    const T pt_scale = bi.gtype == 2 ? T(0.25) : T(1);
+    for (int c = 0; c < bi.npts; c++) {
+        const V3<T> sup = support_pt(bi, bt, wf.up, c);
+        const T z = wf.pos.z + dot(wf.up, sup);
+        const T pen = M.ground_h - z;
+        if (!(pen > T(0))) continue;
+        const V3<T>& n = wf.up;
+        const V3<T> vp = v.l + cross(v.w, sup);
+        const T vn = dot(vp, n);
+        const T mn = eff_mass(bt, sup, n);
+        const T kb = pz_min(pt_scale * bt.gk, M.kstiff_c * mn);
+        const T db = pz_min(pt_scale * bt.gd, M.inv_dt_c * mn);
+        const T fn = pz_max(kb * pen - db * vn, T(0));
+        const V3<T> vt3 = vp - n * vn;
+        const T vt = pz_sqrt(dot(vt3, vt3));
+        V3<T> fb = n * fn;
+        if (vt > T(1e-6)) {
+            const V3<T> td = vt3 * (T(1) / vt);
+            const T coul = (M.friction * fn) * pz_min(T(1), vt / T(1e-3));
+            const T ft = pz_min(coul, (M.inv_dt_c * eff_mass(bt, sup, td)) * vt);
+            fb = fb - td * ft;
+        }
+        f.w = f.w + cross(sup, fb);
+        f.l = f.l + fb;
+        any = true;
+        if (full) {
+            fw = fw + mk3<T>(dot(wf.r0, fb), dot(wf.r1, fb), dot(wf.up, fb));
+            if (pen > deepest) {
+                deepest = pen;
+                dx = wf.pos.x + dot(wf.r0, sup);
+                dy = wf.pos.y + dot(wf.r1, sup);
+            }
+        }
+    }
+    if (full) {
+        cs.put(8 * i + 0, any ? T(1) : T(0));
+        cs.put(8 * i + 1, any ? deepest : T(0));
+        cs.put(8 * i + 2, any ? dx : T(0));
+        cs.put(8 * i + 3, any ? dy : T(0));
+        cs.put(8 * i + 4, any ? M.ground_h : T(0));
+        cs.put(8 * i + 5, any ? fw.x : T(0));
+        cs.put(8 * i + 6, any ? fw.y : T(0));
+        cs.put(8 * i + 7, any ? fw.z : T(0));
+    }
+    return f;
+}
+
+// ── per-world I/O of a launch ──────────────────────────────────────────────
+template <class T>
+struct WorldIO {
+    const T* ctrl;          // [nv][nworld] held, or [step][nv][nworld] schedule
+    long long ctrl_stride;  // elements between steps (0: held)
+    const T* targets;       // PD targets [npd][nworld]
+    long long nworld;
+    long long w;
+};
+
+// Queue the control inputs of `step` for body i into its w0 slots.
+template <class T, class Scr>
+PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
+                             int step) {
+    for (int k = 0; k < bi.ndof; k++) {
+        const int d = bi.off + k;
+        const int pdi = M.pd_of_dof[d];
+        const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
+                                : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
+        S.prefetch(bi.s_w0 + k, src);
+    }
+}
+
+// ── pass 1 of body i for the state in scratch: joint transform, velocity,
+// world frame and contact wrench. `cv`/`cw` carry body i-1's values.
+template <class T, class Scr>
+PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<T>& cw, bool full,
+                      const Out<T>& cs) {
+    const BodyI bi = M.bi[i];
+    const BodyT<T>& bt = M.bt[i];
+    const int p = bi.parent;
+    const JX<T> j = make_jx(bi, bt, S);
+    SV<T> vpar;
+    if (p < 0)
+        vpar = zerosv<T>();
+    else if (p == i - 1)
+        vpar = cv;
+    else
+        vpar = ld_sv<T>(S, M.bi[p].s_vw);
+    const SV<T> v = mot_X(bi, bt, j, vpar) + joint_vel(bi, bt, S, M.nv);
+    st_sv(S, bi.s_vw, v);
+    cv = v;
+    if (M.contact) {
+        WF<T> wp;
+        if (p < 0) {
+            wp.r0 = mk3<T>(T(1), T(0), T(0));
+            wp.r1 = mk3<T>(T(0), T(1), T(0));
+            wp.up = mk3<T>(T(0), T(0), T(1));
+            wp.pos = zero3<T>();
+        } else if (p == i - 1) {
+            wp = cw;
+        } else {
+            const int s = M.bi[p].s_wx;
+            wp.up = mk3<T>(S(s), S(s + 1), S(s + 2));
+            wp.pos.z = S(s + 3);
+            if (full) {
+                wp.r0 = mk3<T>(S(s + 4), S(s + 5), S(s + 6));
+                wp.r1 = mk3<T>(S(s + 7), S(s + 8), S(s + 9));
+                wp.pos.x = S(s + 10);
+                wp.pos.y = S(s + 11);
+            }
+        }
+        const V3<T> tp = tree_pos(bi, bt, j);
+        WF<T> wf;
+        wf.up = tree_rot(bi, bt, j, wp.up);
+        wf.pos.z = wp.pos.z + dot(wp.up, tp);
+        if (full) {
+            wf.r0 = tree_rot(bi, bt, j, wp.r0);
+            wf.r1 = tree_rot(bi, bt, j, wp.r1);
+            wf.pos.x = wp.pos.x + dot(wp.r0, tp);
+            wf.pos.y = wp.pos.y + dot(wp.r1, tp);
+        }
+        cw = wf;
+        if (bi.flags & F_BRANCH) {
+            const int s = bi.s_wx;
+            S(s) = wf.up.x;
+            S(s + 1) = wf.up.y;
+            S(s + 2) = wf.up.z;
+            S(s + 3) = wf.pos.z;
+            if (full) {
+                S(s + 4) = wf.r0.x;
+                S(s + 5) = wf.r0.y;
+                S(s + 6) = wf.r0.z;
+                S(s + 7) = wf.r1.x;
+                S(s + 8) = wf.r1.y;
+                S(s + 9) = wf.r1.z;
+                S(s + 10) = wf.pos.x;
+                S(s + 11) = wf.pos.y;
+            }
+        }
+        if (bi.flags & F_CONTACT) {
+            const SV<T> f = contact_wrench(M, bi, bt, wf, v, full, i, cs);
+            st_sv(S, bi.s_f, f);
+        } else if (full) {
+            for (int k = 0; k < 8; k++) cs.put(8 * i + k, T(0));
+        }
+    }
+}
+
+// ── pass 2: backward sweep (aba.rs:215-320) ───────────────────────────────
+template <class T, class Scr>
+PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
+    // zero the stored accumulators of branch bodies
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        if (bi.flags & F_BRANCH)
+            for (int k = 0; k < 27; k++) S(bi.s_acc + k) = T(0);
+    }
+    AI<T> cI;
+    SV<T> cp = zerosv<T>();
+    ai_zero(cI);
+    for (int i = M.nb - 1; i >= 0; i--) {
+        const BodyI bi = M.bi[i];
+        const BodyT<T>& bt = M.bt[i];
+        const int p = bi.parent;
+        const SV<T> v = ld_sv<T>(S, bi.s_vw);
+        // rigid inertia about the origin and the bias force v x* (I v)
+        AI<T> I;
+#pragma unroll
+        for (int k = 0; k < 6; k++) I.a[k] = bt.Io[k];
+        I.h[0] = T(0);
+        I.h[1] = -bt.mcom[2];
+        I.h[2] = bt.mcom[1];
+        I.h[3] = bt.mcom[2];
+        I.h[4] = T(0);
+        I.h[5] = -bt.mcom[0];
+        I.h[6] = -bt.mcom[1];
+        I.h[7] = bt.mcom[0];
+        I.h[8] = T(0);
+        I.m[0] = I.m[1] = I.m[2] = bt.mass;
+        I.m[3] = I.m[4] = I.m[5] = T(0);
+        const V3<T> mc = ld3(bt.mcom);
+        const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
+        SV<T> pA = crf(v, hv);
+        if (bi.flags & F_CONTACT) pA = pA - ld_sv<T>(S, bi.s_f);
+        if (bi.flags & F_CHAIN) {
+            ai_add(I, cI);
+            pA = pA + cp;
+        }
+        if (bi.flags & F_BRANCH) {
+            const int s = bi.s_acc;
+#pragma unroll
+            for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + S(s + k);
+#pragma unroll
+            for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + S(s + 6 + k);
+#pragma unroll
+            for (int k = 0; k < 6; k++) I.m[k] = I.m[k] + S(s + 15 + k);
+            pA = pA + ld_sv<T>(S, s + 21);
+        }
+        const SV<T> vj = joint_vel(bi, bt, S, M.nv);
+        const SV<T> c = crm(v, vj);
+        bool live = true;
+        if (bi.ndof == 1) {
+            const V3<T> a = ld3(bt.axis);
+            V3<T> Uw, Ul;
+            const bool hinge = bi.jtype == J_REVOLUTE;
+            const int k = bi.axis_k;
+            if (hinge) {
+                if (k >= 0) {
+                    Uw = mk3<T>(I.a[sidx(0, k)], I.a[sidx(1, k)], I.a[sidx(2, k)]);
+                    Ul = mk3<T>(I.h[k * 3 + 0], I.h[k * 3 + 1], I.h[k * 3 + 2]);
+                } else {
+                    Uw = symv(I.a, a);
+                    Ul = m3tv(I.h, a);
+                }
+            } else {
+                if (k >= 0) {
+                    Uw = mk3<T>(I.h[0 * 3 + k], I.h[1 * 3 + k], I.h[2 * 3 + k]);
+                    Ul = mk3<T>(I.m[sidx(0, k)], I.m[sidx(1, k)], I.m[sidx(2, k)]);
+                } else {
+                    Uw = m3v(I.h, a);
+                    Ul = symv(I.m, a);
+                }
+            }
+            const T sU = hinge ? (k >= 0 ? get(Uw, k) : dot(a, Uw)) : (k >= 0 ? get(Ul, k) : dot(a, Ul));
+            const T D = sU + bt.d_extra;
+            const T sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
+            const T u = dof_force(M, bi, bt, S, 0) - sp;
+            if (pz_abs(D) < T(1e-20)) {  // aba.rs:240-242: skip the body
+                live = false;
+                for (int r = 0; r < 6; r++) S(bi.s_vw + r) = T(0);
+                S(bi.s_w0) = T(0);
+            } else {
+                const T invD = T(1) / D;
+                const V3<T> Ww = Uw * invD, Wl = Ul * invD;
+                const T w0 = u * invD;
+                st_sv(S, bi.s_vw, mksv<T>(Ww, Wl));
+                S(bi.s_w0) = w0;
+                if (p >= 0) {
+                    // I <- I - W U^T (rank-1, symmetric)
+#pragma unroll
+                    for (int r = 0; r < 3; r++)
+#pragma unroll
+                        for (int q = r; q < 3; q++) {
+                            I.a[sidx(r, q)] = I.a[sidx(r, q)] - get(Ww, r) * get(Uw, q);
+                            I.m[sidx(r, q)] = I.m[sidx(r, q)] - get(Wl, r) * get(Ul, q);
+                        }
+#pragma unroll
+                    for (int r = 0; r < 3; r++)
+#pragma unroll
+                        for (int q = 0; q < 3; q++) I.h[r * 3 + q] = I.h[r * 3 + q] - get(Ww, r) * get(Ul, q);
+                    pA = pA + ai_mul(I, c) + mksv<T>(Uw * w0, Ul * w0);
+                }
+            }
+        } else if (bi.ndof == 3) {
+            live = multi_dof<3>(M, bi, bt, S, I, pA, c, p >= 0);
+        } else if (bi.ndof == 6) {
+            live = multi_dof<6>(M, bi, bt, S, I, pA, c, p >= 0);
+        }
+        if (p < 0) continue;
+        if (!live) {  // a skipped body passes nothing to its parent
+            if (p == i - 1) {
+                ai_zero(cI);
+                cp = zerosv<T>();
+            }
+            continue;
+        }
+        const JX<T> j = load_jx(bi, bt, S);
+        ai_XtIX(bi, bt, j, I);
+        const SV<T> pc = frc_XT(bi, bt, j, pA);
+        if (p == i - 1) {
+            cI = I;
+            cp = pc;
+        } else {
+            const int s = M.bi[p].s_acc;
+#pragma unroll
+            for (int k = 0; k < 6; k++) S(s + k) = S(s + k) + I.a[k];
+#pragma unroll
+            for (int k = 0; k < 9; k++) S(s + 6 + k) = S(s + 6 + k) + I.h[k];
+#pragma unroll
+            for (int k = 0; k < 6; k++) S(s + 15 + k) = S(s + 15 + k) + I.m[k];
+            const SV<T> old = ld_sv<T>(S, s + 21);
+            st_sv(S, s + 21, old + pc);
+        }
+    }
+}
+
+// ── integrator of body i (integrate.rs:41-91), v first then q ─────────────
+template <class T, class Scr>
+PZ_HD void integrate_1dof(const ModelView<T>& M, const BodyI& bi, const Scr& S, const T& qdd) {
+    const int o = bi.off, ov = M.nv + bi.off;
+    const T vn = S(ov) + M.dt * qdd;
+    S(ov) = vn;
+    S(o) = S(o) + M.dt * vn;
+}
+
+// Multi-DOF accelerations qdd = w0 - W^T a, written into the w0 slots (the
+// integrator reads them back), and a += S qdd.
+template <class T, class Scr>
+PZ_OUTLINE void multi_qdd(const BodyI& bi, const Scr& S, SV<T>& a) {
+    const int nd = bi.ndof;
+    T q[6];
+#pragma unroll
+    for (int k = 0; k < 6; k++) q[k] = k < nd ? S(bi.s_w0 + k) - dot(ld_sv<T>(S, bi.s_vw + 6 * k), a) : T(0);
+#pragma unroll
+    for (int k = 0; k < 6; k++)
+        if (k < nd) S(bi.s_w0 + k) = q[k];
+    a.w = a.w + mk3<T>(q[0], q[1], q[2]);
+    if (nd == 6) a.l = a.l + mk3<T>(q[3], q[4], q[5]);
+}
+
+// Ball / free joint: exponential-map step of the rotation, body-frame linear
+// velocity rotated into the parent for the free joint's position.
+template <class T, class Scr>
+PZ_OUTLINE void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Scr& S, const Out<T>& qdd_out) {
+    const int o = bi.off, ov = M.nv + bi.off;
+    const T dt = M.dt;
+    for (int k = 0; k < bi.ndof; k++) {
+        const T qk = S(bi.s_w0 + k);
+        qdd_out.put(bi.off + k, qk);
+        S(ov + k) = S(ov + k) + dt * qk;
+    }
+    const V3<T> om = mk3<T>(S(ov), S(ov + 1), S(ov + 2));
+    const Q4<T> cur = qexp(mk3<T>(S(o), S(o + 1), S(o + 2)));
+    if (bi.jtype == J_FREE) {
+        const V3<T> wl = qrotate(cur, mk3<T>(S(ov + 3), S(ov + 4), S(ov + 5)));
+        S(o + 3) = S(o + 3) + dt * wl.x;
+        S(o + 4) = S(o + 4) + dt * wl.y;
+        S(o + 5) = S(o + 5) + dt * wl.z;
+    }
+    const Q4<T> nxt = qnormalize(qmul(cur, qexp(om * dt)));
+    const V3<T> lg = qlog(nxt);
+    S(o) = lg.x;
+    S(o + 1) = lg.y;
+    S(o + 2) = lg.z;
+}
+
+// ── pass 3 + integration of the current step, fused with pass 1 of the next
+// (aba.rs:322-400, then integrate.rs, then aba.rs:175-213 / contact).
+// `next_step` < 0 means this is the last step of the launch.
+template <class T, class Scr>
+PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int next_step, bool full,
+                      const Out<T>& qdd_out, const Out<T>& cs) {
+    SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
+    WF<T> cw;
+    const SV<T> a0 = mksv<T>(zero3<T>(), mk3<T>(-M.gx, -M.gy, -M.gz));
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        const BodyT<T>& bt = M.bt[i];
+        const int p = bi.parent;
+        const JX<T> j = load_jx(bi, bt, S);
+        SV<T> vpo, apar;
+        if (p < 0) {
+            vpo = zerosv<T>();
+            apar = a0;
+        } else if (p == i - 1) {
+            vpo = cvo;
+            apar = ca;
+        } else {
+            vpo = ld_sv<T>(S, M.bi[p].s_vold);
+            apar = ld_sv<T>(S, M.bi[p].s_acca);
+        }
+        const SV<T> vj = joint_vel(bi, bt, S, M.nv);
+        const SV<T> vo = mot_X(bi, bt, j, vpo) + vj;
+        const SV<T> c = crm(vo, vj);
+        SV<T> a = mot_X(bi, bt, j, apar) + c;
+        const int nd = bi.ndof;
+        T qdd0 = T(0);
+        if (nd == 1) {
+            qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
+            const V3<T> ax = ld3(bt.axis);
+            if (bi.jtype == J_REVOLUTE)
+                a.w = a.w + ax * qdd0;
+            else
+                a.l = a.l + ax * qdd0;
+        } else if (nd > 1) {
+            multi_qdd(bi, S, a);
+        }
+        if (bi.flags & F_BRANCH) {
+            st_sv(S, bi.s_vold, vo);
+            st_sv(S, bi.s_acca, a);
+        }
+        cvo = vo;
+        ca = a;
+        if (nd == 1) {
+            integrate_1dof(M, bi, S, qdd0);
+            qdd_out.put(bi.off, qdd0);
+        } else if (nd > 1) {
+            integrate_multi(M, bi, S, qdd_out);
+        }
+        if (next_step >= 0) {
+            prefetch_controls(M, bi, S, io, next_step);
+            pass1_body(M, S, i, cvn, cw, full, cs);
+        }
+    }
+}
+
+// The initial pass 1 over the state loaded at the start of a launch.
+template <class T, class Scr>
+PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S, bool full, const Out<T>& cs) {
+    SV<T> cv = zerosv<T>();
+    WF<T> cw;
+    for (int i = 0; i < M.nb; i++) pass1_body(M, S, i, cv, cw, full, cs);
+}
+
+}  // namespace pz
