@@ -1,0 +1,389 @@
+"""Benchmark of the B200 batched rigid-body stepper.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2_chain32] [--precision f32|f64] [--horizon H]
+
+One bench "step" is one rollout of the workload: every world of the config
+(BASELINE.json configs[1] by default: the 32-link chain, 65536 worlds)
+advanced `horizon` physics steps (the config's 1000) under per-step controls
+N(0, sigma), starting from the seeded initial state. Metric: world-steps/s
+of the whole job, device-timed with CUDA events on the launching stream,
+max over ranks. Multi-GPU runs are weak-scaled: each rank owns its own
+contiguous block of worlds (no per-step communication); one NCCL all-reduce
+of the per-world objective closes every rollout.
+
+`value` has the inputs (initial state, control schedule) resident in HBM.
+`e2e` is the same metric through the C ABI with host buffers: the initial
+state and every step's controls copied in from pinned host memory and the
+final state read back, inside the timed region. `roofline` is the fused
+kernel against the measured FP32/FP64 FMA pipe. `cpu_baseline` is the
+reference's own kernels compiled as host C++ (oracle/_ref), on this host's
+cores. `--impl reference` times only that reference CPU path.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+# DRAM bytes per world-step of the fused kernel measured by ncu
+# (profiles/rollout_kernel_c2_chain32.md: dram__bytes_read.sum +
+# dram__bytes_write.sum of one launch / (worlds x steps)); None until measured.
+NCU_DRAM_BYTES_PER_WORLD_STEP: dict = {}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c2_chain32")
+    ap.add_argument("--precision", default="f32", choices=["f32", "f64"])
+    ap.add_argument("--horizon", type=int, default=0, help="physics steps per bench step (0: the config's)")
+    ap.add_argument("--nworld", type=int, default=0, help="worlds per GPU (0: the config's)")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-horizon", type=int, default=100)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+# ── clocks during the timed region ─────────────────────────────────────────
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ── distributed plumbing ──────────────────────────────────────────────────
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ── the reference's CPU path (oracle/_ref) ────────────────────────────────
+def reference_cpu(cfg_name, model, nworld, horizon, seconds, world_offset=0):
+    """Time the reference's own kernels compiled as host C++ on every host
+    core, on a bounded sample of the workload: up to 16384 of its worlds for
+    as many of its steps as fit ~`seconds` (controls from a 64-step seeded
+    schedule reused cyclically). Returns (world-steps/s, threads, sample)."""
+    from oracle.oracle import RefHost, cpu_threads
+    from phyz_b200 import configs
+
+    ref = RefHost()
+    cfg = configs.CONFIGS[cfg_name]
+    threads = cpu_threads()
+    n = min(nworld, 16384)
+    worlds = np.arange(world_offset, world_offset + n)
+    q, v = configs.initial_state(cfg_name, model, worlds)
+    contact = None
+    if cfg.contact:
+        g, k, d, mu = cfg.contact
+        contact = (g, mu, k, d)
+    rng = np.random.default_rng(configs.CTRL_SEED)
+    period = 64
+    sched = (rng.standard_normal((period, n, model.nv)) * cfg.ctrl_sigma * configs.actuated(model)).astype(np.float32)
+    # calibrate on 4 steps, then run whole 64-step chunks for ~`seconds`
+    t0 = time.perf_counter()
+    ref.rollout(model, q, v, sched[:4], 4, schedule=True, contact=contact, nthreads=threads)
+    per_step = (time.perf_counter() - t0) / 4
+    chunks = int(max(1, min(-(-horizon // period), seconds / max(per_step * period, 1e-9))))
+    t0 = time.perf_counter()
+    for _ in range(chunks):
+        q, v, _, _ = ref.rollout(model, q, v, sched, period, schedule=True, contact=contact, nthreads=threads)
+    dt = time.perf_counter() - t0
+    steps = chunks * period
+    return n * steps / dt, threads, (f"{n} of {nworld} worlds x {steps} of {horizon} steps, f32, "
+                                     f"{threads} threads, {dt:.1f} s")
+
+
+def run_reference_impl(args, world, rank):
+    from phyz_b200 import configs
+
+    if rank != 0:
+        return
+    cfg = configs.CONFIGS[args.config]
+    model = cfg.builder()
+    nworld = args.nworld or cfg.nworld
+    horizon = args.horizon or cfg.steps
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, threads, sample = reference_cpu(args.config, model, nworld, horizon,
+                                           max(2.0, args.cpu_seconds / 3), 0)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": "world-steps/sec", "value": value, "unit": "world-steps/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": args.config, "nworld": nworld, "horizon": horizon, "precision": "f32"},
+        "cpu_baseline": {"value": value, "unit": "world-steps/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "world-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ── our arm ────────────────────────────────────────────────────────────────
+def main():
+    args = parse()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        run_reference_impl(args, world, rank)
+        finish(world)
+        return
+
+    import torch
+
+    from phyz_b200 import BatchSim, configs
+    from phyz_b200 import _lib as L
+
+    cfg = configs.CONFIGS[args.config]
+    model = cfg.builder()
+    nworld = args.nworld or cfg.nworld
+    horizon = args.horizon or cfg.steps
+    prec = args.precision
+    tdt = torch.float32 if prec == "f32" else torch.float64
+    esz = 4 if prec == "f32" else 8
+    nv = model.nv
+    offset = rank * nworld  # this rank's block of worlds
+
+    sim = BatchSim(model, nworld, device=local, precision=prec)
+    if cfg.contact:
+        sim.enable_ground_contact(*cfg.contact)
+    stream = torch.cuda.Stream()
+    sim.set_stream(stream.cuda_stream)
+
+    # inputs resident in HBM: initial state (SoA) and the per-step controls
+    q0, v0 = configs.initial_state(args.config, model, np.arange(offset, offset + nworld))
+    sim.load_states(q0, v0)
+    q0_dev = torch.tensor(q0.T.copy(), dtype=tdt, device="cuda")
+    v0_dev = torch.tensor(v0.T.copy(), dtype=tdt, device="cuda")
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(configs.CTRL_SEED + rank)
+    mask = torch.tensor(configs.actuated(model), dtype=tdt, device="cuda").view(1, nv, 1)
+    with torch.cuda.stream(stream):
+        sched = torch.randn(horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
+        objective = torch.zeros(1, dtype=tdt, device="cuda")
+    stream.synchronize()
+
+    def reset_state():
+        # every rollout starts from the same seeded state: same work each step
+        sim.load_states_device(q0_dev.data_ptr(), v0_dev.data_ptr())
+
+    def rollout(ev=None):
+        reset_state()
+        if ev is not None:
+            ev[0].record(stream)
+        sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
+        if ev is not None:
+            ev[1].record(stream)
+        with torch.cuda.stream(stream):
+            objective.zero_()
+        sim.objective_device(0, objective.data_ptr())
+        if world > 1:
+            import torch.distributed as dist
+
+            with torch.cuda.stream(stream):
+                dist.all_reduce(objective)
+
+    for _ in range(args.warmup):
+        rollout()
+    stream.synchronize()
+    sim.sync()
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for k in range(args.steps):
+            rollout(kev[k])
+        t1.record(stream)
+        stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    sim.sync()  # raises if any world went non-finite
+    ms = allreduce_max(t0.elapsed_time(t1), world)
+    kernel_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in kev) / args.steps, world)
+    world_steps = nworld * horizon * world
+    value = world_steps * args.steps / (ms * 1e-3)
+
+    # roofline of the fused kernel: algorithmic flops / launch time vs the
+    # measured FMA pipe of this precision
+    flops_ws, trans_ws = sim.flops_per_world_step()
+    pk = np.zeros(1)
+    L.check(L.load().phyzb_measure_fma_peak(L.F32 if prec == "f32" else L.F64, L.dptr(pk)))
+    achieved = flops_ws * nworld * horizon / (kernel_ms * 1e-3) / 1e12
+    traffic = None
+    if (args.config, prec) in NCU_DRAM_BYTES_PER_WORLD_STEP:
+        traffic = NCU_DRAM_BYTES_PER_WORLD_STEP[(args.config, prec)] * nworld * horizon
+    alg_bytes = (3 + 2) * nv * esz  # read q, v, ctrl; write q, v per world-step
+    roofline = {
+        "bound": "fma", "pipe": f"{'fp32' if prec == 'f32' else 'fp64'} FMA", "achieved": achieved,
+        "peak": float(pk[0]), "unit": "TFLOP/s", "frac": achieved / float(pk[0]),
+        "peak_source": "measured in this run (independent FMA chains over every SM, phyzb_measure_fma_peak)",
+        "traffic": traffic, "kernel": "rollout_kernel", "kernel_ms_per_launch": kernel_ms,
+        "flops_per_world_step": flops_ws, "transcendentals_per_world_step": trans_ws,
+        "algorithmic_bytes_per_world_step": alg_bytes,
+        "hbm_gbs_algorithmic": alg_bytes * nworld * horizon / (kernel_ms * 1e-3) / 1e9,
+    }
+
+    # e2e through the C ABI with host buffers
+    e2e = None
+    if not args.no_e2e:
+        eh = min(args.e2e_horizon, horizon)
+        host_ctrl = torch.empty((eh, nworld, nv), dtype=torch.float32 if prec == "f32" else torch.float64,
+                                pin_memory=True)
+        host_ctrl.copy_(sched[:eh].permute(0, 2, 1).cpu())
+        hq = np.zeros((nworld, nv))
+        hv = np.zeros((nworld, nv))
+        hdt = L.HOST_F32 if prec == "f32" else L.HOST_F64
+
+        def e2e_step():
+            sim.load_states(q0, v0)
+            sim.step_with_controls_ptr(host_ctrl.data_ptr(), hdt, eh)
+            L.check(L.load().phyzb_readback_states(sim._h, L.dptr(hq), L.dptr(hv)))
+
+        e2e_step()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        stream.synchronize()
+        barrier(world)
+        ems = allreduce_max(e0.elapsed_time(e1), world)
+        e2e = {"value": nworld * eh * world * args.e2e_steps / (ems * 1e-3), "unit": "world-steps/s",
+               "h2d_bytes_per_step": int(2 * nworld * nv * 8 + host_ctrl.numel() * host_ctrl.element_size()),
+               "d2h_bytes_per_step": int(2 * nworld * nv * 8), "horizon": eh,
+               "path": "phyzb_load_states + phyzb_step_with_controls (pinned) + phyzb_readback_states"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, threads, sample = reference_cpu(args.config, model, nworld, horizon, args.cpu_seconds)
+            cpu = {"value": v, "unit": "world-steps/s", "cores": threads, "kind": "reference", "sample": sample}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "world-steps/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+
+    info = sim.launch_info()
+    if rank == 0:
+        line = {
+            "metric": "world-steps/sec", "value": value, "unit": "world-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": prec, "data": "synthetic (seeded)",
+            "config": {"workload": args.config, "nworld_per_gpu": nworld, "horizon": horizon, "nbodies":
+                       model.nbodies, "nv": nv, "parallelism": f"worlds sharded over {world} GPU(s)",
+                       "l2": "inputs larger than L2: the per-step control schedule "
+                             f"({horizon * nv * nworld * esz / 1e9:.1f} GB) streams from HBM every rollout",
+                       "launch": info},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
+            "gpu_launches": args.steps * 2,  # per rollout: rollout_kernel + objective_kernel
+            "objective": float(objective.item()),
+        }
+        print(json.dumps(line), flush=True)
+    sim.close()
+    finish(world)
+
+
+def finish(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -243,6 +243,10 @@ int phyzb_readback_contacts(phyzb_sim* sim, double* contact_state);
 
 /* Device pointers and layout of the resident state (zero-copy). */
 int phyzb_device_view_get(phyzb_sim* sim, phyzb_device_view* out);
+/* Device-resident form of phyzb_load_states: q, v (and ctrl, NULL = keep)
+ * are device arrays in the simulator's precision and SoA layout
+ * ([nv][nworld]); copied on the simulator's stream, asynchronously. */
+int phyzb_load_states_device(phyzb_sim* sim, const void* q, const void* v, const void* ctrl);
 /* Launch on a caller-provided stream (a cudaStream_t; NULL = the
  * simulator's own stream). */
 int phyzb_set_stream(phyzb_sim* sim, void* stream);
@@ -264,6 +268,10 @@ int phyzb_objective_device(phyzb_sim* sim, int kind, void* out_device_scalar);
  * settings, as executed by the kernel's formulation (add/sub/mul = 1,
  * fma = 2, div = 1), with transcendental calls tallied separately. */
 int phyzb_flops_per_world_step(const phyzb_sim* sim, double* flops, double* transcendentals);
+/* FP32 (PHYZB_F32) or FP64 (PHYZB_F64) FMA-pipe throughput of the calling
+ * thread's current device in TFLOP/s, measured with independent FMA chains
+ * over every SM: the roofline denominator of the stepper's kernels. */
+int phyzb_measure_fma_peak(int precision, double* tflops);
 /* Launch configuration the fused kernel uses for this simulator. */
 int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
                       int32_t* smem_bytes, int32_t* scratch_per_world);

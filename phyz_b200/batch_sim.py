@@ -221,6 +221,11 @@ class BatchSim:
         check(self._lib.phyzb_device_view_get(self._h, C.byref(v)))
         return {k: getattr(v, k) for k, _ in _lib.PhyzbDeviceView._fields_}
 
+    def load_states_device(self, q_ptr: int, v_ptr: int, ctrl_ptr: int | None = None) -> None:
+        """Device SoA ([nv][nworld], sim precision) state upload, asynchronous."""
+        check(self._lib.phyzb_load_states_device(self._h, C.c_void_p(q_ptr), C.c_void_p(v_ptr),
+                                                 C.c_void_p(ctrl_ptr or 0)))
+
     def set_stream(self, stream_ptr: int | None) -> None:
         check(self._lib.phyzb_set_stream(self._h, C.c_void_p(stream_ptr or 0)))
 

@@ -16,7 +16,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libphyzb200.so"
-SOURCES = ["stepper.cu", "capi.cu", "flops.cpp"]
+SOURCES = ["stepper.cu", "capi.cu", "flops.cpp", "peaks.cu"]
 HEADERS = ["pz_types.cuh", "pz_model.cuh", "pz_world.cuh", "pz_launch.h", "pz_pack.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -11,7 +11,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .model import (FREE, GRAVITY, Geometry, Joint, ModelBuilder, SpatialInertia,
+from .model import (FREE, GRAVITY, REVOLUTE, Geometry, Joint, ModelBuilder, SpatialInertia,
                     Transform)
 from .rng import KernelRng
 
@@ -20,6 +20,19 @@ CTRL_SEED = 0xC7A1
 MODEL_SEED = 0x3D0C
 
 AXES = [np.array([1.0, 0.0, 0.0]), np.array([0.0, 1.0, 0.0]), np.array([0.0, 0.0, 1.0])]
+
+# Rotor inertia of every actuated hinge in configs 2-4: the value phyz's own
+# ant model gives its motors (models/ant.xml:18, armature="0.01"). Without it
+# a twist joint of a thin rod has ~1e-4 kg m^2 about its axis and N(0,1)
+# torques spin it up without bound within a few hundred steps.
+ARMATURE = 0.01
+
+
+def _with_armature(model):
+    for b in model.bodies:
+        if b.joint.kind == REVOLUTE:
+            b.joint.armature = ARMATURE
+    return model
 
 
 def rod(m: float, half_len: float, eps: float = 0.0) -> SpatialInertia:
@@ -49,7 +62,7 @@ def chain(n: int = 32, dt: float = 0.001, seed: int = MODEL_SEED):
     """m ~ U(0.5, 2), half-length ~ U(0.1, 0.3), axes cycling x, y, z; rods
     hang along -Y with COM (0, -h, 0), each child joint at its parent's tip
     (0, -2 h_parent, 0); the inertia about the rod's own axis is that of a
-    2 cm-radius solid rod (0.5 m r^2), so no joint's D is singular."""
+    2 cm-radius solid rod (0.5 m r^2); every hinge carries ARMATURE."""
     rng = KernelRng(seed, [0])
     b = ModelBuilder().gravity([0.0, -GRAVITY, 0.0]).dt(dt)
     prev_h = 0.0
@@ -59,7 +72,7 @@ def chain(n: int = 32, dt: float = 0.001, seed: int = MODEL_SEED):
         ptj = Transform.identity() if k == 0 else Transform.from_translation([0.0, -2.0 * prev_h, 0.0])
         b.add_revolute_body(f"link{k}", k - 1, ptj, rod(m, h, eps=0.5 * m * 0.02 ** 2), axis=AXES[k % 3])
         prev_h = h
-    return b.build()
+    return _with_armature(b.build())
 
 
 # ── C3: quadruped, Z-up ──────────────────────────────────────────────────
@@ -68,7 +81,7 @@ def quadruped(dt: float = 0.002):
     (hips at (+-0.15, +-0.15, -0.15)); thigh and shin capsules r 0.04,
     length 0.2, 0.5 kg, hanging along -Z; a foot sphere r 0.05 at the shin
     tip is the shin's collision shape. Ground z = 0, gravity -Z (the config's
-    plane y = 0 restated Z-up)."""
+    plane y = 0 restated Z-up). Hinges carry ARMATURE."""
     b = ModelBuilder().gravity([0.0, 0.0, -GRAVITY]).dt(dt)
     b.add_body("torso", -1, Joint.free(), SpatialInertia.sphere(5.0, 0.25))
     cap = SpatialInertia.new(0.5, [0.0, 0.0, -0.1], capsule_inertia(0.5, 0.04, 0.2))
@@ -79,7 +92,7 @@ def quadruped(dt: float = 0.002):
         foot = Geometry.sphere(0.05, Transform.from_translation([0.0, 0.0, -0.2]))
         b.add_revolute_body(f"shin{leg}", thigh, Transform.from_translation([0.0, 0.0, -0.2]), cap,
                             axis=AXES[1], geometry=foot)
-    return b.build()
+    return _with_armature(b.build())
 
 
 # ── C4: humanoid-like tree, Z-up ─────────────────────────────────────────
@@ -88,7 +101,7 @@ def humanoid(dt: float = 0.002, seed: int = MODEL_SEED):
     (neck x, y, z), two arms (shoulder x, y, elbow y) off the chest, two legs
     (hip x, z, y, knee y, ankle y) off the pelvis. Body masses ~ U(0.5, 8).
     Ten contact shapes: pelvis, head, forearms, thighs, shins (capsules /
-    spheres) and feet (spheres)."""
+    spheres) and feet (spheres). Hinges carry ARMATURE."""
     rng = KernelRng(seed + 1, [0])
 
     def mass():
@@ -147,7 +160,7 @@ def humanoid(dt: float = 0.002, seed: int = MODEL_SEED):
         mft = mass()
         b.add_revolute_body(f"foot_{side}", sh, T([0.0, 0.0, -0.4]), small(mft), axis=AXES[1],
                             geometry=Geometry.sphere(0.05, T([0.0, 0.0, 0.0])))
-    return b.build()
+    return _with_armature(b.build())
 
 
 @dataclass

@@ -601,6 +601,16 @@ int phyzb_device_view_get(phyzb_sim* s, phyzb_device_view* out) {
     return PHYZB_OK;
 }
 
+int phyzb_load_states_device(phyzb_sim* s, const void* q, const void* v, const void* ctrl) {
+    PZ_TRY(check_sim(s));
+    if (!q || !v) return fail(PHYZB_ERR_INVALID, "q and v must not be null");
+    DeviceGuard g(s->device);
+    PZ_CUDA(cudaMemcpyAsync(s->q, q, s->state_bytes(), cudaMemcpyDeviceToDevice, s->stream));
+    PZ_CUDA(cudaMemcpyAsync(s->v, v, s->state_bytes(), cudaMemcpyDeviceToDevice, s->stream));
+    if (ctrl) PZ_CUDA(cudaMemcpyAsync(s->ctrl, ctrl, s->state_bytes(), cudaMemcpyDeviceToDevice, s->stream));
+    return PHYZB_OK;
+}
+
 int phyzb_set_stream(phyzb_sim* s, void* stream) {
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
