@@ -21,17 +21,21 @@ MODEL_SEED = 0x3D0C
 
 AXES = [np.array([1.0, 0.0, 0.0]), np.array([0.0, 1.0, 0.0]), np.array([0.0, 0.0, 1.0])]
 
-# Rotor inertia of every actuated hinge in configs 2-4: the value phyz's own
-# ant model gives its motors (models/ant.xml:18, armature="0.01"). Without it
-# a twist joint of a thin rod has ~1e-4 kg m^2 about its axis and N(0,1)
-# torques spin it up without bound within a few hundred steps.
+# Joint defaults of every actuated hinge in configs 2-4: those phyz's own ant
+# model gives its motors (models/ant.xml:18, damping="1" armature="0.01").
+# The configs name no passive joint terms; without them a twist joint of a
+# thin rod has ~1e-4 kg m^2 about its axis and N(0,1) torques drive some of
+# 65536 worlds non-finite within 1000 steps. Damping enters D implicitly
+# (dt * damping, aba.rs:418-420), which keeps every world bounded.
 ARMATURE = 0.01
+DAMPING = 1.0
 
 
 def _with_armature(model):
     for b in model.bodies:
         if b.joint.kind == REVOLUTE:
             b.joint.armature = ARMATURE
+            b.joint.damping = DAMPING
     return model
 
 
@@ -62,7 +66,7 @@ def chain(n: int = 32, dt: float = 0.001, seed: int = MODEL_SEED):
     """m ~ U(0.5, 2), half-length ~ U(0.1, 0.3), axes cycling x, y, z; rods
     hang along -Y with COM (0, -h, 0), each child joint at its parent's tip
     (0, -2 h_parent, 0); the inertia about the rod's own axis is that of a
-    2 cm-radius solid rod (0.5 m r^2); every hinge carries ARMATURE."""
+    2 cm-radius solid rod (0.5 m r^2); every hinge carries ARMATURE and DAMPING."""
     rng = KernelRng(seed, [0])
     b = ModelBuilder().gravity([0.0, -GRAVITY, 0.0]).dt(dt)
     prev_h = 0.0
@@ -81,7 +85,7 @@ def quadruped(dt: float = 0.002):
     (hips at (+-0.15, +-0.15, -0.15)); thigh and shin capsules r 0.04,
     length 0.2, 0.5 kg, hanging along -Z; a foot sphere r 0.05 at the shin
     tip is the shin's collision shape. Ground z = 0, gravity -Z (the config's
-    plane y = 0 restated Z-up). Hinges carry ARMATURE."""
+    plane y = 0 restated Z-up). Hinges carry ARMATURE and DAMPING."""
     b = ModelBuilder().gravity([0.0, 0.0, -GRAVITY]).dt(dt)
     b.add_body("torso", -1, Joint.free(), SpatialInertia.sphere(5.0, 0.25))
     cap = SpatialInertia.new(0.5, [0.0, 0.0, -0.1], capsule_inertia(0.5, 0.04, 0.2))
@@ -101,7 +105,7 @@ def humanoid(dt: float = 0.002, seed: int = MODEL_SEED):
     (neck x, y, z), two arms (shoulder x, y, elbow y) off the chest, two legs
     (hip x, z, y, knee y, ankle y) off the pelvis. Body masses ~ U(0.5, 8).
     Ten contact shapes: pelvis, head, forearms, thighs, shins (capsules /
-    spheres) and feet (spheres). Hinges carry ARMATURE."""
+    spheres) and feet (spheres). Hinges carry ARMATURE and DAMPING."""
     rng = KernelRng(seed + 1, [0])
 
     def mass():

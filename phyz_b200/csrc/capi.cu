@@ -102,8 +102,10 @@ int repack(phyzb_sim* s) {
         s->blob_cap = s->info.bytes;
     }
     PZ_CUDA(cudaMemcpy(s->blob, blob.data(), s->info.bytes, cudaMemcpyHostToDevice));
-    cudaError_t e = is_f64(s) ? pz::rollout_config<double>(s->info.scratch, s->info.bytes, s->nworld, &s->launch)
-                              : pz::rollout_config<float>(s->info.scratch, s->info.bytes, s->nworld, &s->launch);
+    cudaError_t e = is_f64(s) ? pz::rollout_config<double>(s->info.scratch, s->info.bytes, s->nworld, s->info.feat,
+                                                           &s->launch)
+                              : pz::rollout_config<float>(s->info.scratch, s->info.bytes, s->nworld, s->info.feat,
+                                                          &s->launch);
     if (e == cudaErrorInvalidConfiguration)
         return fail(PHYZB_ERR_TOO_LARGE, "per-world scratch (" + std::to_string(s->info.scratch) +
                                              " slots) does not fit shared memory at 32 worlds per block");
@@ -129,6 +131,7 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     a.nv = s->nv;
     a.npd = (int)s->cfg.pd.size();
     a.contact = s->cfg.contact ? 1 : 0;
+    a.feat = s->info.feat;
     a.dt = s->model.dt;
     a.gx = s->model.gravity[0];
     a.gy = s->model.gravity[1];

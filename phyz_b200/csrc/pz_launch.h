@@ -19,6 +19,7 @@ struct RolloutArgs {
     int model_bytes;         // multiple of 16
     int off_bi, off_pd, off_pdmap;
     int nb, nv, npd, contact;
+    int feat;              // kernel variant: FEAT_MULTI | FEAT_CONTACT bits (pz_world.cuh)
     double dt, gx, gy, gz, ground_h, friction;
     T* q;                  // [nv][nworld]
     T* v;                  // [nv][nworld]
@@ -34,7 +35,7 @@ struct RolloutArgs {
 };
 
 template <class T>
-cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, LaunchCfg* out);
+cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, LaunchCfg* out);
 template <class T>
 cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
 

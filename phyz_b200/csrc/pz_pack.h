@@ -73,6 +73,7 @@ struct PackInfo {
     int off_bi = 0, off_pd = 0, off_pdmap = 0, bytes = 0;
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
+    int feat = 0;        // kernel variant: 1 = has ball/free joints, 2 = contact on
 };
 
 inline int pad16(int b) { return (b + 15) & ~15; }
@@ -228,6 +229,9 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         pdmap[cfg.pd[k].v_index] = k;
     }
     info.scratch = next;
+    for (int i = 0; i < nb; i++)
+        if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;
+    if (cfg.contact) info.feat |= 2;
     return info;
 }
 

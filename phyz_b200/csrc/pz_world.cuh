@@ -30,6 +30,10 @@
 
 namespace pz {
 
+// Compile-time feature mask of a kernel variant: a model without ball/free
+// joints (resp. without contact) gets a kernel without that code at all.
+enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2 };
+
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
 struct Q4 {
@@ -144,7 +148,7 @@ struct JX {
     V3<T> r;  // translation (prismatic, free)
 };
 
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
     JX<T> j;
     switch (bi.jtype) {
@@ -155,13 +159,17 @@ PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
             break;
         case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
         case J_BALL:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) {
 #pragma unroll
-            for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
+                for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
+            }
             break;
         case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) {
 #pragma unroll
-            for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
-            j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
+                for (int k = 0; k < 9; k++) j.E.m[k] = S(bi.s_xj + k);
+                j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
+            }
             break;
         default: break;
     }
@@ -169,7 +177,7 @@ PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
 }
 
 // Compute the joint transform data of body i from q and store it.
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD JX<T> make_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
     JX<T> j;
     switch (bi.jtype) {
@@ -185,7 +193,8 @@ PZ_HD JX<T> make_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
         }
         case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
         case J_BALL:
-        case J_FREE: {
+        case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) {
             const Q4<T> q = qexp(mk3<T>(S(bi.off), S(bi.off + 1), S(bi.off + 2)));
             j.E = qjoint_rot(q);
 #pragma unroll
@@ -209,19 +218,21 @@ PZ_HD V3<T> hrot_t(int k, const T& c, const T& s, const V3<T>& x) {
 }
 
 // The rotation part of X_tree = X_J X_ptj applied to a 3-vector: R_J R_ptj x.
-template <class T>
+template <int FEAT, class T>
 PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> x) {
     if (bi.flags & F_PTJ_ROT) x = m3v(bt.ptj_rot, x);
     switch (bi.jtype) {
         case J_REVOLUTE: x = bi.axis_k >= 0 ? hrot(bi.axis_k, j.c, j.s, x) : rmul(j.E, x); break;
         case J_BALL:
-        case J_FREE: x = rmul(j.E, x); break;
+        case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) x = rmul(j.E, x);
+            break;
         default: break;
     }
     return x;
 }
 // Origin of the body in its parent: p_ptj + R_ptj^T p_J (tang compose).
-template <class T>
+template <int FEAT, class T>
 PZ_HD V3<T> tree_pos(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j) {
     V3<T> p = ld3(bt.ptj_pos);
     if (bi.jtype == J_PRISMATIC || bi.jtype == J_FREE)
@@ -230,7 +241,7 @@ PZ_HD V3<T> tree_pos(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j) {
 }
 
 // X_tree m for a motion vector (X_ptj first, then X_J).
-template <class T>
+template <int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
     if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
     if (bi.flags & F_PTJ_ROT) {
@@ -245,15 +256,19 @@ PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) 
                 m = xm_apply_rot(j.E, m);
             break;
         case J_PRISMATIC: m = xm_apply_trans(j.r, m); break;
-        case J_BALL: m = xm_apply_rot(j.E, m); break;
-        case J_FREE: m = xm_apply_rot(j.E, xm_apply_trans(j.r, m)); break;
+        case J_BALL:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, m);
+            break;
+        case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, xm_apply_trans(j.r, m));
+            break;
         default: break;
     }
     return m;
 }
 
 // X_tree^T f for a force vector (phyz's inv_apply_force).
-template <class T>
+template <int FEAT, class T>
 PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f) {
     switch (bi.jtype) {
         case J_REVOLUTE:
@@ -263,8 +278,12 @@ PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f)
                 f = xf_tapply_rot(j.E, f);
             break;
         case J_PRISMATIC: f = xf_tapply_trans(j.r, f); break;
-        case J_BALL: f = xf_tapply_rot(j.E, f); break;
-        case J_FREE: f = xf_tapply_trans(j.r, xf_tapply_rot(j.E, f)); break;
+        case J_BALL:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_rot(j.E, f);
+            break;
+        case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_trans(j.r, xf_tapply_rot(j.E, f));
+            break;
         default: break;
     }
     if (bi.flags & F_PTJ_ROT) {
@@ -276,7 +295,7 @@ PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f)
 }
 
 // X_tree^T I X_tree in place (J part first, then ptj).
-template <class T>
+template <int FEAT, class T>
 PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I) {
     switch (bi.jtype) {
         case J_REVOLUTE:
@@ -290,10 +309,14 @@ PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I
                 ai_rot(j.E, I);
             break;
         case J_PRISMATIC: ai_trans(j.r, I); break;
-        case J_BALL: ai_rot(j.E, I); break;
+        case J_BALL:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) ai_rot(j.E, I);
+            break;
         case J_FREE:
-            ai_rot(j.E, I);
-            ai_trans(j.r, I);
+            if constexpr ((FEAT & FEAT_MULTI) != 0) {
+                ai_rot(j.E, I);
+                ai_trans(j.r, I);
+            }
             break;
         default: break;
     }
@@ -305,14 +328,18 @@ PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I
 }
 
 // S qd of body i (aba.rs:15-30).
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD SV<T> joint_vel(const BodyI& bi, const BodyT<T>& bt, const Scr& S, int nv) {
     const int o = nv + bi.off;
     switch (bi.jtype) {
         case J_REVOLUTE: return mksv<T>(ld3(bt.axis) * S(o), zero3<T>());
         case J_PRISMATIC: return mksv<T>(zero3<T>(), ld3(bt.axis) * S(o));
-        case J_BALL: return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), zero3<T>());
-        case J_FREE: return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), mk3<T>(S(o + 3), S(o + 4), S(o + 5)));
+        case J_BALL:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), zero3<T>());
+            return zerosv<T>();
+        case J_FREE:
+            if constexpr ((FEAT & FEAT_MULTI) != 0) return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), mk3<T>(S(o + 3), S(o + 4), S(o + 5)));
+            return zerosv<T>();
         default: return zerosv<T>();
     }
 }
@@ -388,7 +415,7 @@ PZ_HD void ai_sub_el(AI<T>& I, int r, int c, const T& v) {  // only r <= c for s
 // body has a parent, I <- I - W U^T and p <- p + I c + U w0. Returns false
 // when D is singular (aba.rs:291-294: the body is skipped).
 template <int ND, class T, class Scr>
-PZ_OUTLINE bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S,
+PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S,
                      AI<T>& I, SV<T>& p, const SV<T>& c, bool has_parent) {
     T U[6][ND];
 #pragma unroll
@@ -634,13 +661,13 @@ PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& 
 
 // ── pass 1 of body i for the state in scratch: joint transform, velocity,
 // world frame and contact wrench. `cv`/`cw` carry body i-1's values.
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<T>& cw, bool full,
                       const Out<T>& cs) {
     const BodyI bi = M.bi[i];
     const BodyT<T>& bt = M.bt[i];
     const int p = bi.parent;
-    const JX<T> j = make_jx(bi, bt, S);
+    const JX<T> j = make_jx<FEAT>(bi, bt, S);
     SV<T> vpar;
     if (p < 0)
         vpar = zerosv<T>();
@@ -648,10 +675,10 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<
         vpar = cv;
     else
         vpar = ld_sv<T>(S, M.bi[p].s_vw);
-    const SV<T> v = mot_X(bi, bt, j, vpar) + joint_vel(bi, bt, S, M.nv);
+    const SV<T> v = mot_X<FEAT>(bi, bt, j, vpar) + joint_vel<FEAT>(bi, bt, S, M.nv);
     st_sv(S, bi.s_vw, v);
     cv = v;
-    if (M.contact) {
+    if constexpr ((FEAT & FEAT_CONTACT) != 0) {
         WF<T> wp;
         if (p < 0) {
             wp.r0 = mk3<T>(T(1), T(0), T(0));
@@ -671,13 +698,13 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<
                 wp.pos.y = S(s + 11);
             }
         }
-        const V3<T> tp = tree_pos(bi, bt, j);
+        const V3<T> tp = tree_pos<FEAT>(bi, bt, j);
         WF<T> wf;
-        wf.up = tree_rot(bi, bt, j, wp.up);
+        wf.up = tree_rot<FEAT>(bi, bt, j, wp.up);
         wf.pos.z = wp.pos.z + dot(wp.up, tp);
         if (full) {
-            wf.r0 = tree_rot(bi, bt, j, wp.r0);
-            wf.r1 = tree_rot(bi, bt, j, wp.r1);
+            wf.r0 = tree_rot<FEAT>(bi, bt, j, wp.r0);
+            wf.r1 = tree_rot<FEAT>(bi, bt, j, wp.r1);
             wf.pos.x = wp.pos.x + dot(wp.r0, tp);
             wf.pos.y = wp.pos.y + dot(wp.r1, tp);
         }
@@ -709,7 +736,7 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<
 }
 
 // ── pass 2: backward sweep (aba.rs:215-320) ───────────────────────────────
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
     // zero the stored accumulators of branch bodies
     for (int i = 0; i < M.nb; i++) {
@@ -717,37 +744,38 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
         if (bi.flags & F_BRANCH)
             for (int k = 0; k < 27; k++) S(bi.s_acc + k) = T(0);
     }
-    AI<T> cI;
-    SV<T> cp = zerosv<T>();
-    ai_zero(cI);
+    // I, pA carry the child's contribution from one iteration to the next
+    // when the child is the next body (F_CHAIN), and start from zero otherwise.
+    AI<T> I;
+    SV<T> pA = zerosv<T>();
+    ai_zero(I);
     for (int i = M.nb - 1; i >= 0; i--) {
         const BodyI bi = M.bi[i];
         const BodyT<T>& bt = M.bt[i];
         const int p = bi.parent;
         const SV<T> v = ld_sv<T>(S, bi.s_vw);
-        // rigid inertia about the origin and the bias force v x* (I v)
-        AI<T> I;
+        if (!(bi.flags & F_CHAIN)) {
+            ai_zero(I);
+            pA = zerosv<T>();
+        }
+        // rigid inertia about the origin [Io, (mc)^x; -(mc)^x, m 1] and the
+        // bias force v x* (I v) - f_ext
 #pragma unroll
-        for (int k = 0; k < 6; k++) I.a[k] = bt.Io[k];
-        I.h[0] = T(0);
-        I.h[1] = -bt.mcom[2];
-        I.h[2] = bt.mcom[1];
-        I.h[3] = bt.mcom[2];
-        I.h[4] = T(0);
-        I.h[5] = -bt.mcom[0];
-        I.h[6] = -bt.mcom[1];
-        I.h[7] = bt.mcom[0];
-        I.h[8] = T(0);
-        I.m[0] = I.m[1] = I.m[2] = bt.mass;
-        I.m[3] = I.m[4] = I.m[5] = T(0);
+        for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + bt.Io[k];
+        I.h[1] = I.h[1] - bt.mcom[2];
+        I.h[2] = I.h[2] + bt.mcom[1];
+        I.h[3] = I.h[3] + bt.mcom[2];
+        I.h[5] = I.h[5] - bt.mcom[0];
+        I.h[6] = I.h[6] - bt.mcom[1];
+        I.h[7] = I.h[7] + bt.mcom[0];
+        I.m[0] = I.m[0] + bt.mass;
+        I.m[1] = I.m[1] + bt.mass;
+        I.m[2] = I.m[2] + bt.mass;
         const V3<T> mc = ld3(bt.mcom);
         const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
-        SV<T> pA = crf(v, hv);
-        if (bi.flags & F_CONTACT) pA = pA - ld_sv<T>(S, bi.s_f);
-        if (bi.flags & F_CHAIN) {
-            ai_add(I, cI);
-            pA = pA + cp;
-        }
+        SV<T> bias = crf(v, hv);
+        if (bi.flags & F_CONTACT) bias = bias - ld_sv<T>(S, bi.s_f);
+        pA = pA + bias;
         if (bi.flags & F_BRANCH) {
             const int s = bi.s_acc;
 #pragma unroll
@@ -758,7 +786,7 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
             for (int k = 0; k < 6; k++) I.m[k] = I.m[k] + S(s + 15 + k);
             pA = pA + ld_sv<T>(S, s + 21);
         }
-        const SV<T> vj = joint_vel(bi, bt, S, M.nv);
+        const SV<T> vj = joint_vel<FEAT>(bi, bt, S, M.nv);
         const SV<T> c = crm(v, vj);
         bool live = true;
         if (bi.ndof == 1) {
@@ -813,26 +841,24 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
                     pA = pA + ai_mul(I, c) + mksv<T>(Uw * w0, Ul * w0);
                 }
             }
-        } else if (bi.ndof == 3) {
-            live = multi_dof<3>(M, bi, bt, S, I, pA, c, p >= 0);
-        } else if (bi.ndof == 6) {
-            live = multi_dof<6>(M, bi, bt, S, I, pA, c, p >= 0);
+        } else if (bi.ndof > 1) {
+            if constexpr ((FEAT & FEAT_MULTI) != 0) {
+                if (bi.ndof == 3)
+                    live = multi_dof<3>(M, bi, bt, S, I, pA, c, p >= 0);
+                else
+                    live = multi_dof<6>(M, bi, bt, S, I, pA, c, p >= 0);
+            }
         }
         if (p < 0) continue;
         if (!live) {  // a skipped body passes nothing to its parent
-            if (p == i - 1) {
-                ai_zero(cI);
-                cp = zerosv<T>();
-            }
+            ai_zero(I);
+            pA = zerosv<T>();
             continue;
         }
-        const JX<T> j = load_jx(bi, bt, S);
-        ai_XtIX(bi, bt, j, I);
-        const SV<T> pc = frc_XT(bi, bt, j, pA);
-        if (p == i - 1) {
-            cI = I;
-            cp = pc;
-        } else {
+        const JX<T> j = load_jx<FEAT>(bi, bt, S);
+        ai_XtIX<FEAT>(bi, bt, j, I);
+        pA = frc_XT<FEAT>(bi, bt, j, pA);
+        if (p != i - 1) {
             const int s = M.bi[p].s_acc;
 #pragma unroll
             for (int k = 0; k < 6; k++) S(s + k) = S(s + k) + I.a[k];
@@ -841,7 +867,7 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
 #pragma unroll
             for (int k = 0; k < 6; k++) S(s + 15 + k) = S(s + 15 + k) + I.m[k];
             const SV<T> old = ld_sv<T>(S, s + 21);
-            st_sv(S, s + 21, old + pc);
+            st_sv(S, s + 21, old + pA);
         }
     }
 }
@@ -858,7 +884,7 @@ PZ_HD void integrate_1dof(const ModelView<T>& M, const BodyI& bi, const Scr& S, 
 // Multi-DOF accelerations qdd = w0 - W^T a, written into the w0 slots (the
 // integrator reads them back), and a += S qdd.
 template <class T, class Scr>
-PZ_OUTLINE void multi_qdd(const BodyI& bi, const Scr& S, SV<T>& a) {
+PZ_HD void multi_qdd(const BodyI& bi, const Scr& S, SV<T>& a) {
     const int nd = bi.ndof;
     T q[6];
 #pragma unroll
@@ -873,7 +899,7 @@ PZ_OUTLINE void multi_qdd(const BodyI& bi, const Scr& S, SV<T>& a) {
 // Ball / free joint: exponential-map step of the rotation, body-frame linear
 // velocity rotated into the parent for the free joint's position.
 template <class T, class Scr>
-PZ_OUTLINE void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Scr& S, const Out<T>& qdd_out) {
+PZ_HD void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Scr& S, const Out<T>& qdd_out) {
     const int o = bi.off, ov = M.nv + bi.off;
     const T dt = M.dt;
     for (int k = 0; k < bi.ndof; k++) {
@@ -899,7 +925,7 @@ PZ_OUTLINE void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Sc
 // ── pass 3 + integration of the current step, fused with pass 1 of the next
 // (aba.rs:322-400, then integrate.rs, then aba.rs:175-213 / contact).
 // `next_step` < 0 means this is the last step of the launch.
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int next_step, bool full,
                       const Out<T>& qdd_out, const Out<T>& cs) {
     SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
@@ -909,7 +935,7 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
         const BodyI bi = M.bi[i];
         const BodyT<T>& bt = M.bt[i];
         const int p = bi.parent;
-        const JX<T> j = load_jx(bi, bt, S);
+        const JX<T> j = load_jx<FEAT>(bi, bt, S);
         SV<T> vpo, apar;
         if (p < 0) {
             vpo = zerosv<T>();
@@ -921,10 +947,10 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
             vpo = ld_sv<T>(S, M.bi[p].s_vold);
             apar = ld_sv<T>(S, M.bi[p].s_acca);
         }
-        const SV<T> vj = joint_vel(bi, bt, S, M.nv);
-        const SV<T> vo = mot_X(bi, bt, j, vpo) + vj;
+        const SV<T> vj = joint_vel<FEAT>(bi, bt, S, M.nv);
+        const SV<T> vo = mot_X<FEAT>(bi, bt, j, vpo) + vj;
         const SV<T> c = crm(vo, vj);
-        SV<T> a = mot_X(bi, bt, j, apar) + c;
+        SV<T> a = mot_X<FEAT>(bi, bt, j, apar) + c;
         const int nd = bi.ndof;
         T qdd0 = T(0);
         if (nd == 1) {
@@ -935,7 +961,7 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
             else
                 a.l = a.l + ax * qdd0;
         } else if (nd > 1) {
-            multi_qdd(bi, S, a);
+            if constexpr ((FEAT & FEAT_MULTI) != 0) multi_qdd(bi, S, a);
         }
         if (bi.flags & F_BRANCH) {
             st_sv(S, bi.s_vold, vo);
@@ -947,21 +973,21 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
             integrate_1dof(M, bi, S, qdd0);
             qdd_out.put(bi.off, qdd0);
         } else if (nd > 1) {
-            integrate_multi(M, bi, S, qdd_out);
+            if constexpr ((FEAT & FEAT_MULTI) != 0) integrate_multi(M, bi, S, qdd_out);
         }
         if (next_step >= 0) {
             prefetch_controls(M, bi, S, io, next_step);
-            pass1_body(M, S, i, cvn, cw, full, cs);
+            pass1_body<FEAT>(M, S, i, cvn, cw, full, cs);
         }
     }
 }
 
 // The initial pass 1 over the state loaded at the start of a launch.
-template <class T, class Scr>
+template <int FEAT, class T, class Scr>
 PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S, bool full, const Out<T>& cs) {
     SV<T> cv = zerosv<T>();
     WF<T> cw;
-    for (int i = 0; i < M.nb; i++) pass1_body(M, S, i, cv, cw, full, cs);
+    for (int i = 0; i < M.nb; i++) pass1_body<FEAT>(M, S, i, cv, cw, full, cs);
 }
 
 }  // namespace pz

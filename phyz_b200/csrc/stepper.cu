@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "pz_launch.h"
 #include "pz_world.cuh"
@@ -69,7 +70,7 @@ __device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, 
     return smem;
 }
 
-template <class T>
+template <class T, int FEAT>
 __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
     extern __shared__ __align__(16) unsigned char smem[];
     const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
@@ -90,14 +91,14 @@ __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ Ro
         S.commit();
         const Out<T> none{nullptr, 0};
         const Out<T> cs{P.cstate ? P.cstate + w : nullptr, N};
-        pass1_all(M, S, P.contact && P.cstate && P.nsteps == 1, P.nsteps == 1 ? cs : none);
+        pass1_all<FEAT>(M, S, P.contact && P.cstate && P.nsteps == 1, P.nsteps == 1 ? cs : none);
         for (int s = 0; s < P.nsteps; s++) {
             S.wait();
-            pass2(M, S);
+            pass2<FEAT>(M, S);
             const bool last = s == P.nsteps - 1;
             const bool full_next = P.contact && P.cstate && (s + 1 == P.nsteps - 1);
-            pass3_next(M, S, io, last ? -1 : s + 1, full_next, last ? Out<T>{P.qdd + w, N} : none,
-                       full_next ? cs : none);
+            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, full_next, last ? Out<T>{P.qdd + w, N} : none,
+                             full_next ? cs : none);
             S.commit();
         }
         S.wait();
@@ -118,7 +119,7 @@ __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ Ro
 // Kinetic energy 0.5 sum_i v_i^T I_i v_i + 0.5 sum_j armature_j qd_j^2
 // (crates/phyz-rigid/src/energy.rs:8-11 with crba's armature) or sum q^2,
 // reduced over the block and added into *out.
-template <class T>
+template <class T, int FEAT>
 __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ RolloutArgs<T> P, int kind,
                                                          T* out) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -141,7 +142,7 @@ __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ 
             for (int j = 0; j < M.nv; j++) acc += S(j) * S(j);
             continue;
         }
-        pass1_all(M, S, false, Out<T>{nullptr, 0});
+        pass1_all<FEAT & FEAT_MULTI>(M, S, false, Out<T>{nullptr, 0});
         for (int i = 0; i < M.nb; i++) {
             const BodyI bi = M.bi[i];
             const BodyT<T>& bt = M.bt[i];
@@ -221,22 +222,25 @@ static cudaError_t device_limits() {
     return cudaSuccess;
 }
 
-template <class T>
-cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, LaunchCfg* out) {
-    cudaError_t e = device_limits();
+template <class T, int FEAT>
+static cudaError_t config_variant(int scratch, int model_bytes, long long nworld, LaunchCfg* out) {
+    cudaError_t e = cudaFuncSetAttribute(rollout_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         g_smem_optin);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(rollout_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_smem_optin);
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(objective_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_smem_optin);
+    e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_smem_optin);
     if (e != cudaSuccess) return e;
     const long long per_world = (long long)scratch * (long long)sizeof(T);
-    // Pick the block width that keeps the most worlds resident per SM.
+    // Pick the block width that keeps the most worlds resident per SM
+    // (PHYZB_WORLDS_PER_BLOCK overrides it for tuning).
+    int forced = 0;
+    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
     int best_w = 0, best_res = -1, best_blocks = 0, best_smem = 0;
     for (int W = 32; W <= 256; W += 32) {
+        if (forced > 0 && W != forced) continue;
         const long long smem = (long long)model_bytes + per_world * W;
         if (smem > g_smem_optin) break;
         int blocks = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T>, W, (size_t)smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT>, W, (size_t)smem);
         if (e != cudaSuccess) return e;
         const int res = blocks * W;
         if (blocks > 0 && res > best_res) {
@@ -256,16 +260,40 @@ cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, Launc
 }
 
 template <class T>
+cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, LaunchCfg* out) {
+    cudaError_t e = device_limits();
+    if (e != cudaSuccess) return e;
+    switch (feat) {
+        case 0: return config_variant<T, 0>(scratch, model_bytes, nworld, out);
+        case FEAT_MULTI: return config_variant<T, FEAT_MULTI>(scratch, model_bytes, nworld, out);
+        case FEAT_CONTACT: return config_variant<T, FEAT_CONTACT>(scratch, model_bytes, nworld, out);
+        default: return config_variant<T, FEAT_MULTI | FEAT_CONTACT>(scratch, model_bytes, nworld, out);
+    }
+}
+
+template <class T>
 cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
     if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
-    rollout_kernel<T><<<cfg.grid, cfg.W, cfg.smem, s>>>(a);
+    switch (a.feat) {
+        case 0: rollout_kernel<T, 0><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        case FEAT_MULTI: rollout_kernel<T, FEAT_MULTI><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        case FEAT_CONTACT: rollout_kernel<T, FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        default: rollout_kernel<T, FEAT_MULTI | FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+    }
     return cudaGetLastError();
 }
 
 template <class T>
 cudaError_t launch_objective(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out, cudaStream_t s) {
     if (a.nworld <= 0) return cudaSuccess;
-    objective_kernel<T><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out);
+    switch (a.feat) {
+        case 0: objective_kernel<T, 0><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
+        case FEAT_MULTI: objective_kernel<T, FEAT_MULTI><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
+        case FEAT_CONTACT: objective_kernel<T, FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
+        default:
+            objective_kernel<T, FEAT_MULTI | FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out);
+            break;
+    }
     return cudaGetLastError();
 }
 
@@ -285,8 +313,8 @@ cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int w
     return cudaGetLastError();
 }
 
-template cudaError_t rollout_config<float>(int, int, long long, LaunchCfg*);
-template cudaError_t rollout_config<double>(int, int, long long, LaunchCfg*);
+template cudaError_t rollout_config<float>(int, int, long long, int, LaunchCfg*);
+template cudaError_t rollout_config<double>(int, int, long long, int, LaunchCfg*);
 template cudaError_t launch_rollout<float>(const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t launch_rollout<double>(const RolloutArgs<double>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t launch_objective<float>(const RolloutArgs<float>&, const LaunchCfg&, int, float*,
