@@ -392,6 +392,20 @@ PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, co
     return f;
 }
 
+// U = I s for s = e_K in the angular (HINGE) or linear part, and s.U.
+template <int K, bool HINGE, class T>
+PZ_HD void unit_u(const AI<T>& I, V3<T>& Uw, V3<T>& Ul, T& sU) {
+    if (HINGE) {
+        Uw = mk3<T>(I.a[sidx(0, K)], I.a[sidx(1, K)], I.a[sidx(2, K)]);
+        Ul = mk3<T>(I.h[K * 3 + 0], I.h[K * 3 + 1], I.h[K * 3 + 2]);
+        sU = at<K>(Uw);
+    } else {
+        Uw = mk3<T>(I.h[0 * 3 + K], I.h[1 * 3 + K], I.h[2 * 3 + K]);
+        Ul = mk3<T>(I.m[sidx(0, K)], I.m[sidx(1, K)], I.m[sidx(2, K)]);
+        sU = at<K>(Ul);
+    }
+}
+
 // Dense element (r, c) of an articulated inertia.
 template <class T>
 PZ_HD T ai_el(const AI<T>& I, int r, int c) {
@@ -792,26 +806,29 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
         if (bi.ndof == 1) {
             const V3<T> a = ld3(bt.axis);
             V3<T> Uw, Ul;
+            T sU;
             const bool hinge = bi.jtype == J_REVOLUTE;
-            const int k = bi.axis_k;
-            if (hinge) {
-                if (k >= 0) {
-                    Uw = mk3<T>(I.a[sidx(0, k)], I.a[sidx(1, k)], I.a[sidx(2, k)]);
-                    Ul = mk3<T>(I.h[k * 3 + 0], I.h[k * 3 + 1], I.h[k * 3 + 2]);
-                } else {
-                    Uw = symv(I.a, a);
-                    Ul = m3tv(I.h, a);
-                }
-            } else {
-                if (k >= 0) {
-                    Uw = mk3<T>(I.h[0 * 3 + k], I.h[1 * 3 + k], I.h[2 * 3 + k]);
-                    Ul = mk3<T>(I.m[sidx(0, k)], I.m[sidx(1, k)], I.m[sidx(2, k)]);
-                } else {
-                    Uw = m3v(I.h, a);
-                    Ul = symv(I.m, a);
-                }
+            // U = I s: a column of the blocks for a coordinate axis (indices are
+            // compile-time in every branch, so I stays in registers)
+            switch (hinge ? bi.axis_k : bi.axis_k + 3) {
+                case 0: unit_u<0, true>(I, Uw, Ul, sU); break;
+                case 1: unit_u<1, true>(I, Uw, Ul, sU); break;
+                case 2: unit_u<2, true>(I, Uw, Ul, sU); break;
+                case 3: unit_u<0, false>(I, Uw, Ul, sU); break;
+                case 4: unit_u<1, false>(I, Uw, Ul, sU); break;
+                case 5: unit_u<2, false>(I, Uw, Ul, sU); break;
+                default:
+                    if (hinge) {
+                        Uw = symv(I.a, a);
+                        Ul = m3tv(I.h, a);
+                        sU = dot(a, Uw);
+                    } else {
+                        Uw = m3v(I.h, a);
+                        Ul = symv(I.m, a);
+                        sU = dot(a, Ul);
+                    }
+                    break;
             }
-            const T sU = hinge ? (k >= 0 ? get(Uw, k) : dot(a, Uw)) : (k >= 0 ? get(Ul, k) : dot(a, Ul));
             const T D = sU + bt.d_extra;
             const T sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
             const T u = dof_force(M, bi, bt, S, 0) - sp;

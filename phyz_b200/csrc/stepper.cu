@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cmath>
 #include <cstdlib>
 
 #include "pz_launch.h"
@@ -230,21 +231,27 @@ static cudaError_t config_variant(int scratch, int model_bytes, long long nworld
     e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_smem_optin);
     if (e != cudaSuccess) return e;
     const long long per_world = (long long)scratch * (long long)sizeof(T);
-    // Pick the block width that keeps the most worlds resident per SM
-    // (PHYZB_WORLDS_PER_BLOCK overrides it for tuning).
+    // Pick the block width (any even width up to the 256 of __launch_bounds__)
+    // that keeps the most worlds resident per SM, discounted by how full the
+    // last wave of tiles is. PHYZB_WORLDS_PER_BLOCK overrides it for tuning.
     int forced = 0;
     if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
-    int best_w = 0, best_res = -1, best_blocks = 0, best_smem = 0;
-    for (int W = 32; W <= 256; W += 32) {
+    int best_w = 0, best_blocks = 0, best_smem = 0;
+    double best_score = -1.0;
+    for (int W = 32; W <= 256; W += 2) {
         if (forced > 0 && W != forced) continue;
         const long long smem = (long long)model_bytes + per_world * W;
         if (smem > g_smem_optin) break;
         int blocks = 0;
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT>, W, (size_t)smem);
         if (e != cudaSuccess) return e;
-        const int res = blocks * W;
-        if (blocks > 0 && res > best_res) {
-            best_res = res;
+        if (blocks <= 0) continue;
+        const double resident = (double)blocks * W * g_sm_count;  // worlds in flight on the GPU
+        const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
+        const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
+        const double score = (double)blocks * W * used;
+        if (score > best_score * 1.0001) {
+            best_score = score;
             best_w = W;
             best_blocks = blocks;
             best_smem = (int)smem;
