@@ -139,11 +139,11 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
     const Out<Cnt> none{nullptr, 0};
     for (int i = 0; i < nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
     constexpr int ALL = FEAT_MULTI | FEAT_CONTACT;  // runtime flags select the paths taken
-    pass1_all<ALL>(M, S, false, none);
+    pass1_all<ALL>(M, S);
     // steady state: one backward sweep + one fused finish/start sweep
     g_tally = Tally{};
     pass2<ALL>(M, S);
-    pass3_next<ALL>(M, S, io, 1, false, none, none);
+    pass3_next<ALL>(M, S, io, 1, none);
     FlopCount fc;
     fc.flops = g_tally.flops;
     fc.transcendentals = g_tally.trans;

@@ -56,7 +56,7 @@ struct alignas(16) BodyI {
     int s_acc;        // branch: accumulated child inertia (21) + bias force (6)
     int s_vold;       // branch: velocity of the step being finished (6)
     int s_acca;       // branch: acceleration (6)
-    int s_wx;         // branch: world frame for contact (up 3, height 1 | full R 9 + p 3)
+    int s_wx;         // branch: world frame for contact (up 3, height 1)
     int gtype;        // geometry code (0 none)
     int npts;         // contact points (box 8, others 1)
 };

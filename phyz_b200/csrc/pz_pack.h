@@ -213,8 +213,8 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.s_acca = next;
             next += 6;
             if (cfg.contact) {
-                d.s_wx = next;
-                next += 12;
+                d.s_wx = next;  // world up (3) and origin height (1)
+                next += 4;
             }
         }
         d.flags = flags;

@@ -148,9 +148,30 @@ struct JX {
     V3<T> r;  // translation (prismatic, free)
 };
 
-template <int FEAT, class T, class Scr>
+// Body kinds. AX >= 0: a revolute joint about exactly +e_AX whose
+// parent->joint frame is unrotated -- every transform of it is a planar
+// rotation (plus the joint offset) known at compile time. AX = -1: any
+// joint, decoded at run time.
+PZ_HD int body_kind(const BodyI& bi) {
+    return (bi.jtype == J_REVOLUTE && bi.axis_k >= 0 && !(bi.flags & F_PTJ_ROT)) ? bi.axis_k : -1;
+}
+
+// a x (s e_K), with the structurally zero component exact
+template <int K, class T>
+PZ_HD V3<T> cross_axis(const V3<T>& a, const T& s) {
+    if (K == 0) return mk3<T>(T(0), a.z * s, -(a.y * s));
+    if (K == 1) return mk3<T>(-(a.z * s), T(0), a.x * s);
+    return mk3<T>(a.y * s, -(a.x * s), T(0));
+}
+
+template <int AX, int FEAT, class T, class Scr>
 PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
     JX<T> j;
+    if constexpr (AX >= 0) {
+        j.c = S(bi.s_xj);
+        j.s = S(bi.s_xj + 1);
+        return j;
+    }
     switch (bi.jtype) {
         case J_REVOLUTE:
             j.c = S(bi.s_xj);
@@ -177,37 +198,41 @@ PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
 }
 
 // Compute the joint transform data of body i from q and store it.
-template <int FEAT, class T, class Scr>
+template <int AX, int FEAT, class T, class Scr>
 PZ_HD JX<T> make_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
     JX<T> j;
-    switch (bi.jtype) {
-        case J_REVOLUTE: {
-            T s, c;
-            pz_sincos(-S(bi.off), &s, &c);
-            j.c = c;
-            j.s = s;
-            S(bi.s_xj) = c;
-            S(bi.s_xj + 1) = s;
+    if (AX >= 0 || bi.jtype == J_REVOLUTE) {
+        T s, c;
+        pz_sincos(-S(bi.off), &s, &c);
+        j.c = c;
+        j.s = s;
+        S(bi.s_xj) = c;
+        S(bi.s_xj + 1) = s;
+        if constexpr (AX < 0) {
             if (bi.axis_k < 0) j.E = hinge_matrix(ld3(bt.axis), c, s);
-            break;
         }
-        case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
-        case J_BALL:
-        case J_FREE:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) {
-            const Q4<T> q = qexp(mk3<T>(S(bi.off), S(bi.off + 1), S(bi.off + 2)));
-            j.E = qjoint_rot(q);
+        return j;
+    }
+    if constexpr (AX < 0) {
+        switch (bi.jtype) {
+            case J_PRISMATIC: j.r = ld3(bt.axis) * S(bi.off); break;
+            case J_BALL:
+            case J_FREE:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) {
+                    const Q4<T> q = qexp(mk3<T>(S(bi.off), S(bi.off + 1), S(bi.off + 2)));
+                    j.E = qjoint_rot(q);
 #pragma unroll
-            for (int k = 0; k < 9; k++) S(bi.s_xj + k) = j.E.m[k];
-            if (bi.jtype == J_FREE) j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
-            break;
+                    for (int k = 0; k < 9; k++) S(bi.s_xj + k) = j.E.m[k];
+                    if (bi.jtype == J_FREE) j.r = mk3<T>(S(bi.off + 3), S(bi.off + 4), S(bi.off + 5));
+                }
+                break;
+            default: break;
         }
-        default: break;
     }
     return j;
 }
 
-// Planar hinge rotation with a runtime axis index.
+// Planar hinge rotation with a runtime axis index (generic path only).
 template <class T>
 PZ_HD V3<T> hrot(int k, const T& c, const T& s, const V3<T>& x) {
     return k == 0 ? prot<0>(c, s, x) : (k == 1 ? prot<1>(c, s, x) : prot<2>(c, s, x));
@@ -218,8 +243,9 @@ PZ_HD V3<T> hrot_t(int k, const T& c, const T& s, const V3<T>& x) {
 }
 
 // The rotation part of X_tree = X_J X_ptj applied to a 3-vector: R_J R_ptj x.
-template <int FEAT, class T>
+template <int AX, int FEAT, class T>
 PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> x) {
+    if constexpr (AX >= 0) return prot<AX>(j.c, j.s, x);
     if (bi.flags & F_PTJ_ROT) x = m3v(bt.ptj_rot, x);
     switch (bi.jtype) {
         case J_REVOLUTE: x = bi.axis_k >= 0 ? hrot(bi.axis_k, j.c, j.s, x) : rmul(j.E, x); break;
@@ -232,105 +258,124 @@ PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> 
     return x;
 }
 // Origin of the body in its parent: p_ptj + R_ptj^T p_J (tang compose).
-template <int FEAT, class T>
+template <int AX, int FEAT, class T>
 PZ_HD V3<T> tree_pos(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j) {
     V3<T> p = ld3(bt.ptj_pos);
-    if (bi.jtype == J_PRISMATIC || bi.jtype == J_FREE)
-        p = p + ((bi.flags & F_PTJ_ROT) ? m3tv(bt.ptj_rot, j.r) : j.r);
+    if constexpr (AX < 0) {
+        if (bi.jtype == J_PRISMATIC || bi.jtype == J_FREE)
+            p = p + ((bi.flags & F_PTJ_ROT) ? m3tv(bt.ptj_rot, j.r) : j.r);
+    }
     return p;
 }
 
 // X_tree m for a motion vector (X_ptj first, then X_J).
-template <int FEAT, class T>
+template <int AX, int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
     if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
-    if (bi.flags & F_PTJ_ROT) {
-        const R3<T> P = ld9(bt.ptj_rot);
-        m = xm_apply_rot(P, m);
+    if constexpr (AX >= 0) {
+        return mksv<T>(prot<AX>(j.c, j.s, m.w), prot<AX>(j.c, j.s, m.l));
+    } else {
+        if (bi.flags & F_PTJ_ROT) {
+            const R3<T> P = ld9(bt.ptj_rot);
+            m = xm_apply_rot(P, m);
+        }
+        switch (bi.jtype) {
+            case J_REVOLUTE:
+                if (bi.axis_k >= 0)
+                    m = mksv<T>(hrot(bi.axis_k, j.c, j.s, m.w), hrot(bi.axis_k, j.c, j.s, m.l));
+                else
+                    m = xm_apply_rot(j.E, m);
+                break;
+            case J_PRISMATIC: m = xm_apply_trans(j.r, m); break;
+            case J_BALL:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, m);
+                break;
+            case J_FREE:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, xm_apply_trans(j.r, m));
+                break;
+            default: break;
+        }
+        return m;
     }
-    switch (bi.jtype) {
-        case J_REVOLUTE:
-            if (bi.axis_k >= 0)
-                m = mksv<T>(hrot(bi.axis_k, j.c, j.s, m.w), hrot(bi.axis_k, j.c, j.s, m.l));
-            else
-                m = xm_apply_rot(j.E, m);
-            break;
-        case J_PRISMATIC: m = xm_apply_trans(j.r, m); break;
-        case J_BALL:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, m);
-            break;
-        case J_FREE:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) m = xm_apply_rot(j.E, xm_apply_trans(j.r, m));
-            break;
-        default: break;
-    }
-    return m;
 }
 
 // X_tree^T f for a force vector (phyz's inv_apply_force).
-template <int FEAT, class T>
+template <int AX, int FEAT, class T>
 PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f) {
-    switch (bi.jtype) {
-        case J_REVOLUTE:
-            if (bi.axis_k >= 0)
-                f = mksv<T>(hrot_t(bi.axis_k, j.c, j.s, f.w), hrot_t(bi.axis_k, j.c, j.s, f.l));
-            else
-                f = xf_tapply_rot(j.E, f);
-            break;
-        case J_PRISMATIC: f = xf_tapply_trans(j.r, f); break;
-        case J_BALL:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_rot(j.E, f);
-            break;
-        case J_FREE:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_trans(j.r, xf_tapply_rot(j.E, f));
-            break;
-        default: break;
-    }
-    if (bi.flags & F_PTJ_ROT) {
-        const R3<T> P = ld9(bt.ptj_rot);
-        f = xf_tapply_rot(P, f);
+    if constexpr (AX >= 0) {
+        f = mksv<T>(prot_t<AX>(j.c, j.s, f.w), prot_t<AX>(j.c, j.s, f.l));
+    } else {
+        switch (bi.jtype) {
+            case J_REVOLUTE:
+                if (bi.axis_k >= 0)
+                    f = mksv<T>(hrot_t(bi.axis_k, j.c, j.s, f.w), hrot_t(bi.axis_k, j.c, j.s, f.l));
+                else
+                    f = xf_tapply_rot(j.E, f);
+                break;
+            case J_PRISMATIC: f = xf_tapply_trans(j.r, f); break;
+            case J_BALL:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_rot(j.E, f);
+                break;
+            case J_FREE:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) f = xf_tapply_trans(j.r, xf_tapply_rot(j.E, f));
+                break;
+            default: break;
+        }
+        if (bi.flags & F_PTJ_ROT) {
+            const R3<T> P = ld9(bt.ptj_rot);
+            f = xf_tapply_rot(P, f);
+        }
     }
     if (bi.flags & F_PTJ_POS) f = xf_tapply_trans(ld3(bt.ptj_pos), f);
     return f;
 }
 
 // X_tree^T I X_tree in place (J part first, then ptj).
-template <int FEAT, class T>
+template <int AX, int FEAT, class T>
 PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I) {
-    switch (bi.jtype) {
-        case J_REVOLUTE:
-            if (bi.axis_k == 0)
-                ai_prot<0>(j.c, j.s, I);
-            else if (bi.axis_k == 1)
-                ai_prot<1>(j.c, j.s, I);
-            else if (bi.axis_k == 2)
-                ai_prot<2>(j.c, j.s, I);
-            else
-                ai_rot(j.E, I);
-            break;
-        case J_PRISMATIC: ai_trans(j.r, I); break;
-        case J_BALL:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) ai_rot(j.E, I);
-            break;
-        case J_FREE:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) {
-                ai_rot(j.E, I);
-                ai_trans(j.r, I);
-            }
-            break;
-        default: break;
-    }
-    if (bi.flags & F_PTJ_ROT) {
-        const R3<T> P = ld9(bt.ptj_rot);
-        ai_rot(P, I);
+    if constexpr (AX >= 0) {
+        ai_prot<AX>(j.c, j.s, I);
+    } else {
+        switch (bi.jtype) {
+            case J_REVOLUTE:
+                if (bi.axis_k == 0)
+                    ai_prot<0>(j.c, j.s, I);
+                else if (bi.axis_k == 1)
+                    ai_prot<1>(j.c, j.s, I);
+                else if (bi.axis_k == 2)
+                    ai_prot<2>(j.c, j.s, I);
+                else
+                    ai_rot(j.E, I);
+                break;
+            case J_PRISMATIC: ai_trans(j.r, I); break;
+            case J_BALL:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) ai_rot(j.E, I);
+                break;
+            case J_FREE:
+                if constexpr ((FEAT & FEAT_MULTI) != 0) {
+                    ai_rot(j.E, I);
+                    ai_trans(j.r, I);
+                }
+                break;
+            default: break;
+        }
+        if (bi.flags & F_PTJ_ROT) {
+            const R3<T> P = ld9(bt.ptj_rot);
+            ai_rot(P, I);
+        }
     }
     if (bi.flags & F_PTJ_POS) ai_trans(ld3(bt.ptj_pos), I);
 }
 
 // S qd of body i (aba.rs:15-30).
-template <int FEAT, class T, class Scr>
+template <int AX, int FEAT, class T, class Scr>
 PZ_HD SV<T> joint_vel(const BodyI& bi, const BodyT<T>& bt, const Scr& S, int nv) {
     const int o = nv + bi.off;
+    if constexpr (AX >= 0) {
+        V3<T> w = zero3<T>();
+        at<AX>(w) = S(o);
+        return mksv<T>(w, zero3<T>());
+    }
     switch (bi.jtype) {
         case J_REVOLUTE: return mksv<T>(ld3(bt.axis) * S(o), zero3<T>());
         case J_PRISMATIC: return mksv<T>(zero3<T>(), ld3(bt.axis) * S(o));
@@ -338,7 +383,8 @@ PZ_HD SV<T> joint_vel(const BodyI& bi, const BodyT<T>& bt, const Scr& S, int nv)
             if constexpr ((FEAT & FEAT_MULTI) != 0) return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), zero3<T>());
             return zerosv<T>();
         case J_FREE:
-            if constexpr ((FEAT & FEAT_MULTI) != 0) return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), mk3<T>(S(o + 3), S(o + 4), S(o + 5)));
+            if constexpr ((FEAT & FEAT_MULTI) != 0)
+                return mksv<T>(mk3<T>(S(o), S(o + 1), S(o + 2)), mk3<T>(S(o + 3), S(o + 4), S(o + 5)));
             return zerosv<T>();
         default: return zerosv<T>();
     }
@@ -574,9 +620,10 @@ PZ_HD V3<T> support_pt(const BodyI& bi, const BodyT<T>& bt, const V3<T>& n_body,
     return ld3(bt.gpos) + rtmul(O, s);
 }
 
-// World frame of a body: rows of the body->world rotation (row 2 is world
-// up seen in the body frame) and the origin. Normal sweeps track row 2 and
-// the height only; the sweep that writes contact state tracks all of it.
+// World frame of a body for contact: world up seen in the body frame (row 2
+// of the body->world rotation) and the height of the body origin. The full
+// frame (rows r0, r1 and the origin's x, y) is only built for the contact
+// state output (contact_state_pass).
 template <class T>
 struct WF {
     V3<T> r0, r1, up;
@@ -650,6 +697,20 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
     return f;
 }
 
+// Out-of-line entry to contact_wrench: everything by value, so the caller's
+// sweep state stays in registers and the contact temporaries do not add to
+// the sweep's register pressure.
+template <class T>
+PZ_OUTLINE SV<T> contact_wrench_call(T ground_h, T friction, T inv_dt_c, T kstiff_c, BodyI bi, const BodyT<T>* bt,
+                                     WF<T> wf, SV<T> v, bool full, int i, Out<T> cs) {
+    ModelView<T> M;
+    M.ground_h = ground_h;
+    M.friction = friction;
+    M.inv_dt_c = inv_dt_c;
+    M.kstiff_c = kstiff_c;
+    return contact_wrench(M, bi, *bt, wf, v, full, i, cs);
+}
+
 // ── per-world I/O of a launch ──────────────────────────────────────────────
 template <class T>
 struct WorldIO {
@@ -673,15 +734,40 @@ PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& 
     }
 }
 
+// I c for a bias c whose K components are structurally zero (c = v x S qd
+// of a hinge about e_K): the products with those zeros are skipped.
+template <int K, class T>
+PZ_HD SV<T> ai_mul_zk(const AI<T>& I, const SV<T>& c) {
+    V3<T> w = zero3<T>(), l = zero3<T>();
+#pragma unroll
+    for (int r = 0; r < 3; r++) {
+        T sw = T(0), sl = T(0);
+        bool first_w = true, first_l = true;
+#pragma unroll
+        for (int k = 0; k < 3; k++) {
+            if (k == K) continue;
+            const T cw = get(c.w, k), cl = get(c.l, k);
+            // [Ia H; H^T M] [cw; cl]
+            const T a = I.a[sidx(r, k)] * cw, h = I.h[r * 3 + k] * cl;
+            const T ht = I.h[k * 3 + r] * cw, m = I.m[sidx(r, k)] * cl;
+            sw = first_w ? a + h : sw + a + h;
+            sl = first_l ? ht + m : sl + ht + m;
+            first_w = first_l = false;
+        }
+        if (r == 0) w.x = sw, l.x = sl;
+        if (r == 1) w.y = sw, l.y = sl;
+        if (r == 2) w.z = sw, l.z = sl;
+    }
+    return mksv<T>(w, l);
+}
+
 // ── pass 1 of body i for the state in scratch: joint transform, velocity,
 // world frame and contact wrench. `cv`/`cw` carry body i-1's values.
-template <int FEAT, class T, class Scr>
-PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<T>& cw, bool full,
-                      const Out<T>& cs) {
-    const BodyI bi = M.bi[i];
+template <int AX, int FEAT, class T, class Scr>
+PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& cv, WF<T>& cw) {
     const BodyT<T>& bt = M.bt[i];
     const int p = bi.parent;
-    const JX<T> j = make_jx<FEAT>(bi, bt, S);
+    const JX<T> j = make_jx<AX, FEAT>(bi, bt, S);
     SV<T> vpar;
     if (p < 0)
         vpar = zerosv<T>();
@@ -689,124 +775,161 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, SV<T>& cv, WF<
         vpar = cv;
     else
         vpar = ld_sv<T>(S, M.bi[p].s_vw);
-    const SV<T> v = mot_X<FEAT>(bi, bt, j, vpar) + joint_vel<FEAT>(bi, bt, S, M.nv);
+    SV<T> v = mot_X<AX, FEAT>(bi, bt, j, vpar);
+    if constexpr (AX >= 0)
+        at<AX>(v.w) = at<AX>(v.w) + S(M.nv + bi.off);
+    else
+        v = v + joint_vel<AX, FEAT>(bi, bt, S, M.nv);
     st_sv(S, bi.s_vw, v);
     cv = v;
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
-        WF<T> wp;
+        V3<T> up_p;
+        T h_p;
         if (p < 0) {
-            wp.r0 = mk3<T>(T(1), T(0), T(0));
-            wp.r1 = mk3<T>(T(0), T(1), T(0));
-            wp.up = mk3<T>(T(0), T(0), T(1));
-            wp.pos = zero3<T>();
+            up_p = mk3<T>(T(0), T(0), T(1));
+            h_p = T(0);
         } else if (p == i - 1) {
-            wp = cw;
+            up_p = cw.up;
+            h_p = cw.pos.z;
         } else {
             const int s = M.bi[p].s_wx;
-            wp.up = mk3<T>(S(s), S(s + 1), S(s + 2));
-            wp.pos.z = S(s + 3);
-            if (full) {
-                wp.r0 = mk3<T>(S(s + 4), S(s + 5), S(s + 6));
-                wp.r1 = mk3<T>(S(s + 7), S(s + 8), S(s + 9));
-                wp.pos.x = S(s + 10);
-                wp.pos.y = S(s + 11);
-            }
+            up_p = mk3<T>(S(s), S(s + 1), S(s + 2));
+            h_p = S(s + 3);
         }
-        const V3<T> tp = tree_pos<FEAT>(bi, bt, j);
         WF<T> wf;
-        wf.up = tree_rot<FEAT>(bi, bt, j, wp.up);
-        wf.pos.z = wp.pos.z + dot(wp.up, tp);
-        if (full) {
-            wf.r0 = tree_rot<FEAT>(bi, bt, j, wp.r0);
-            wf.r1 = tree_rot<FEAT>(bi, bt, j, wp.r1);
-            wf.pos.x = wp.pos.x + dot(wp.r0, tp);
-            wf.pos.y = wp.pos.y + dot(wp.r1, tp);
-        }
-        cw = wf;
+        wf.up = tree_rot<AX, FEAT>(bi, bt, j, up_p);
+        wf.pos.z = h_p + dot(up_p, tree_pos<AX, FEAT>(bi, bt, j));
+        cw.up = wf.up;
+        cw.pos.z = wf.pos.z;
         if (bi.flags & F_BRANCH) {
             const int s = bi.s_wx;
             S(s) = wf.up.x;
             S(s + 1) = wf.up.y;
             S(s + 2) = wf.up.z;
             S(s + 3) = wf.pos.z;
-            if (full) {
-                S(s + 4) = wf.r0.x;
-                S(s + 5) = wf.r0.y;
-                S(s + 6) = wf.r0.z;
-                S(s + 7) = wf.r1.x;
-                S(s + 8) = wf.r1.y;
-                S(s + 9) = wf.r1.z;
-                S(s + 10) = wf.pos.x;
-                S(s + 11) = wf.pos.y;
-            }
         }
         if (bi.flags & F_CONTACT) {
-            const SV<T> f = contact_wrench(M, bi, bt, wf, v, full, i, cs);
+            const SV<T> f = contact_wrench_call(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, bi, &bt, wf, v,
+                                                false, i, Out<T>{nullptr, 0});
             st_sv(S, bi.s_f, f);
-        } else if (full) {
-            for (int k = 0; k < 8; k++) cs.put(8 * i + k, T(0));
         }
     }
 }
 
-// ── pass 2: backward sweep (aba.rs:215-320) ───────────────────────────────
+// Contact state [touching, depth, point(3), force(3)] of every body for the
+// state in scratch (joint transforms and velocities of pass 1 in place),
+// written to rows 8*i.. of `cs` (layout.rs:68-80). Each collidable body's
+// full world frame is rebuilt by walking its ancestor chain: a body-frame
+// vector d maps into its parent as E_tree^T d (plus tree_pos for points).
 template <int FEAT, class T, class Scr>
-PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
-    // zero the stored accumulators of branch bodies
+PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>& cs) {
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
-        if (bi.flags & F_BRANCH)
-            for (int k = 0; k < 27; k++) S(bi.s_acc + k) = T(0);
+        if (!(bi.flags & F_CONTACT)) {
+            for (int k = 0; k < 8; k++) cs.put(8 * i + k, T(0));
+            continue;
+        }
+        // columns of the body->world rotation and the origin, built upwards
+        V3<T> cx = mk3<T>(T(1), T(0), T(0)), cy = mk3<T>(T(0), T(1), T(0)), cz = mk3<T>(T(0), T(0), T(1));
+        V3<T> o = zero3<T>();
+        for (int b = i; b >= 0; b = M.bi[b].parent) {
+            const BodyI bb = M.bi[b];
+            const BodyT<T>& tb = M.bt[b];
+            const JX<T> j = load_jx<-1, FEAT>(bb, tb, S);
+            // E_tree^T d = R_ptj^T R_J^T d
+            auto up_dir = [&](V3<T> d) {
+                switch (bb.jtype) {
+                    case J_REVOLUTE: d = bb.axis_k >= 0 ? hrot_t(bb.axis_k, j.c, j.s, d) : rtmul(j.E, d); break;
+                    case J_BALL:
+                    case J_FREE:
+                        if constexpr ((FEAT & FEAT_MULTI) != 0) d = rtmul(j.E, d);
+                        break;
+                    default: break;
+                }
+                if (bb.flags & F_PTJ_ROT) d = m3tv(tb.ptj_rot, d);
+                return d;
+            };
+            cx = up_dir(cx);
+            cy = up_dir(cy);
+            cz = up_dir(cz);
+            o = up_dir(o) + tree_pos<-1, FEAT>(bb, tb, j);
+        }
+        WF<T> wf;  // rows of the body->world rotation = components of the columns
+        wf.r0 = mk3<T>(cx.x, cy.x, cz.x);
+        wf.r1 = mk3<T>(cx.y, cy.y, cz.y);
+        wf.up = mk3<T>(cx.z, cy.z, cz.z);
+        wf.pos = o;
+        contact_wrench(M, bi, M.bt[i], wf, ld_sv<T>(S, bi.s_vw), true, i, cs);
     }
-    // I, pA carry the child's contribution from one iteration to the next
-    // when the child is the next body (F_CHAIN), and start from zero otherwise.
-    AI<T> I;
-    SV<T> pA = zerosv<T>();
-    ai_zero(I);
-    for (int i = M.nb - 1; i >= 0; i--) {
-        const BodyI bi = M.bi[i];
-        const BodyT<T>& bt = M.bt[i];
-        const int p = bi.parent;
-        const SV<T> v = ld_sv<T>(S, bi.s_vw);
-        if (!(bi.flags & F_CHAIN)) {
-            ai_zero(I);
-            pA = zerosv<T>();
-        }
-        // rigid inertia about the origin [Io, (mc)^x; -(mc)^x, m 1] and the
-        // bias force v x* (I v) - f_ext
+}
+
+// Run f<AX>() for the body's kind.
+#define PZ_BY_KIND(kind, CALL)      \
+    switch (kind) {                 \
+        case 0: CALL(0); break;     \
+        case 1: CALL(1); break;     \
+        case 2: CALL(2); break;     \
+        default: CALL(-1); break;   \
+    }
+
+// ── pass 2 of body i (aba.rs:215-320). I, pA carry the child's contribution
+// in from the next body (when it is this body's child) and this body's
+// contribution out to its parent.
+template <int AX, int FEAT, class T, class Scr>
+PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, AI<T>& I, SV<T>& pA) {
+    const BodyT<T>& bt = M.bt[i];
+    const int p = bi.parent;
+    const SV<T> v = ld_sv<T>(S, bi.s_vw);
+    if (!(bi.flags & F_CHAIN)) {
+        ai_zero(I);
+        pA = zerosv<T>();
+    }
+    // rigid inertia about the origin [Io, (mc)^x; -(mc)^x, m 1] and the
+    // bias force v x* (I v) - f_ext
 #pragma unroll
-        for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + bt.Io[k];
-        I.h[1] = I.h[1] - bt.mcom[2];
-        I.h[2] = I.h[2] + bt.mcom[1];
-        I.h[3] = I.h[3] + bt.mcom[2];
-        I.h[5] = I.h[5] - bt.mcom[0];
-        I.h[6] = I.h[6] - bt.mcom[1];
-        I.h[7] = I.h[7] + bt.mcom[0];
-        I.m[0] = I.m[0] + bt.mass;
-        I.m[1] = I.m[1] + bt.mass;
-        I.m[2] = I.m[2] + bt.mass;
-        const V3<T> mc = ld3(bt.mcom);
-        const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
-        SV<T> bias = crf(v, hv);
+    for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + bt.Io[k];
+    I.h[1] = I.h[1] - bt.mcom[2];
+    I.h[2] = I.h[2] + bt.mcom[1];
+    I.h[3] = I.h[3] + bt.mcom[2];
+    I.h[5] = I.h[5] - bt.mcom[0];
+    I.h[6] = I.h[6] - bt.mcom[1];
+    I.h[7] = I.h[7] + bt.mcom[0];
+    I.m[0] = I.m[0] + bt.mass;
+    I.m[1] = I.m[1] + bt.mass;
+    I.m[2] = I.m[2] + bt.mass;
+    const V3<T> mc = ld3(bt.mcom);
+    const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
+    SV<T> bias = crf(v, hv);
+    if constexpr ((FEAT & FEAT_CONTACT) != 0) {
         if (bi.flags & F_CONTACT) bias = bias - ld_sv<T>(S, bi.s_f);
-        pA = pA + bias;
-        if (bi.flags & F_BRANCH) {
-            const int s = bi.s_acc;
+    }
+    pA = pA + bias;
+    if (bi.flags & F_BRANCH) {
+        const int s = bi.s_acc;
 #pragma unroll
-            for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + S(s + k);
+        for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + S(s + k);
 #pragma unroll
-            for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + S(s + 6 + k);
+        for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + S(s + 6 + k);
 #pragma unroll
-            for (int k = 0; k < 6; k++) I.m[k] = I.m[k] + S(s + 15 + k);
-            pA = pA + ld_sv<T>(S, s + 21);
-        }
-        const SV<T> vj = joint_vel<FEAT>(bi, bt, S, M.nv);
-        const SV<T> c = crm(v, vj);
-        bool live = true;
-        if (bi.ndof == 1) {
+        for (int k = 0; k < 6; k++) I.m[k] = I.m[k] + S(s + 15 + k);
+        pA = pA + ld_sv<T>(S, s + 21);
+    }
+    SV<T> c;
+    if constexpr (AX >= 0) {
+        const T qd = S(M.nv + bi.off);
+        c = mksv<T>(cross_axis<AX>(v.w, qd), cross_axis<AX>(v.l, qd));
+    } else {
+        c = crm(v, joint_vel<AX, FEAT>(bi, bt, S, M.nv));
+    }
+    bool live = true;
+    if (AX >= 0 || bi.ndof == 1) {
+        V3<T> Uw, Ul;
+        T sU, sp;
+        if constexpr (AX >= 0) {
+            unit_u<AX, true>(I, Uw, Ul, sU);
+            sp = at<AX>(pA.w);
+        } else {
             const V3<T> a = ld3(bt.axis);
-            V3<T> Uw, Ul;
-            T sU;
             const bool hinge = bi.jtype == J_REVOLUTE;
             // U = I s: a column of the blocks for a coordinate axis (indices are
             // compile-time in every branch, so I stays in registers)
@@ -829,36 +952,43 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
                     }
                     break;
             }
-            const T D = sU + bt.d_extra;
-            const T sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
-            const T u = dof_force(M, bi, bt, S, 0) - sp;
-            if (pz_abs(D) < T(1e-20)) {  // aba.rs:240-242: skip the body
-                live = false;
-                for (int r = 0; r < 6; r++) S(bi.s_vw + r) = T(0);
-                S(bi.s_w0) = T(0);
-            } else {
-                const T invD = T(1) / D;
-                const V3<T> Ww = Uw * invD, Wl = Ul * invD;
-                const T w0 = u * invD;
-                st_sv(S, bi.s_vw, mksv<T>(Ww, Wl));
-                S(bi.s_w0) = w0;
-                if (p >= 0) {
-                    // I <- I - W U^T (rank-1, symmetric)
+            sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
+        }
+        const T D = sU + bt.d_extra;
+        const T u = dof_force(M, bi, bt, S, 0) - sp;
+        if (pz_abs(D) < T(1e-20)) {  // aba.rs:240-242: skip the body
+            live = false;
+            for (int r = 0; r < 6; r++) S(bi.s_vw + r) = T(0);
+            S(bi.s_w0) = T(0);
+        } else {
+            const T invD = T(1) / D;
+            const V3<T> Ww = Uw * invD, Wl = Ul * invD;
+            const T w0 = u * invD;
+            st_sv(S, bi.s_vw, mksv<T>(Ww, Wl));
+            S(bi.s_w0) = w0;
+            if (p >= 0) {
+                // I <- I - W U^T (rank-1, symmetric)
 #pragma unroll
-                    for (int r = 0; r < 3; r++)
+                for (int r = 0; r < 3; r++)
 #pragma unroll
-                        for (int q = r; q < 3; q++) {
-                            I.a[sidx(r, q)] = I.a[sidx(r, q)] - get(Ww, r) * get(Uw, q);
-                            I.m[sidx(r, q)] = I.m[sidx(r, q)] - get(Wl, r) * get(Ul, q);
-                        }
+                    for (int q = r; q < 3; q++) {
+                        I.a[sidx(r, q)] = I.a[sidx(r, q)] - get(Ww, r) * get(Uw, q);
+                        I.m[sidx(r, q)] = I.m[sidx(r, q)] - get(Wl, r) * get(Ul, q);
+                    }
 #pragma unroll
-                    for (int r = 0; r < 3; r++)
+                for (int r = 0; r < 3; r++)
 #pragma unroll
-                        for (int q = 0; q < 3; q++) I.h[r * 3 + q] = I.h[r * 3 + q] - get(Ww, r) * get(Ul, q);
-                    pA = pA + ai_mul(I, c) + mksv<T>(Uw * w0, Ul * w0);
-                }
+                    for (int q = 0; q < 3; q++) I.h[r * 3 + q] = I.h[r * 3 + q] - get(Ww, r) * get(Ul, q);
+                SV<T> Ic;
+                if constexpr (AX >= 0)
+                    Ic = ai_mul_zk<AX>(I, c);
+                else
+                    Ic = ai_mul(I, c);
+                pA = pA + Ic + mksv<T>(Uw * w0, Ul * w0);
             }
-        } else if (bi.ndof > 1) {
+        }
+    } else if constexpr (AX < 0) {
+        if (bi.ndof > 1) {
             if constexpr ((FEAT & FEAT_MULTI) != 0) {
                 if (bi.ndof == 3)
                     live = multi_dof<3>(M, bi, bt, S, I, pA, c, p >= 0);
@@ -866,26 +996,46 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
                     live = multi_dof<6>(M, bi, bt, S, I, pA, c, p >= 0);
             }
         }
-        if (p < 0) continue;
-        if (!live) {  // a skipped body passes nothing to its parent
-            ai_zero(I);
-            pA = zerosv<T>();
-            continue;
-        }
-        const JX<T> j = load_jx<FEAT>(bi, bt, S);
-        ai_XtIX<FEAT>(bi, bt, j, I);
-        pA = frc_XT<FEAT>(bi, bt, j, pA);
-        if (p != i - 1) {
-            const int s = M.bi[p].s_acc;
+    }
+    if (p < 0) return;
+    if (!live) {  // a skipped body passes nothing to its parent
+        ai_zero(I);
+        pA = zerosv<T>();
+        return;
+    }
+    const JX<T> j = load_jx<AX, FEAT>(bi, bt, S);
+    ai_XtIX<AX, FEAT>(bi, bt, j, I);
+    pA = frc_XT<AX, FEAT>(bi, bt, j, pA);
+    if (p != i - 1) {
+        const int s = M.bi[p].s_acc;
 #pragma unroll
-            for (int k = 0; k < 6; k++) S(s + k) = S(s + k) + I.a[k];
+        for (int k = 0; k < 6; k++) S(s + k) = S(s + k) + I.a[k];
 #pragma unroll
-            for (int k = 0; k < 9; k++) S(s + 6 + k) = S(s + 6 + k) + I.h[k];
+        for (int k = 0; k < 9; k++) S(s + 6 + k) = S(s + 6 + k) + I.h[k];
 #pragma unroll
-            for (int k = 0; k < 6; k++) S(s + 15 + k) = S(s + 15 + k) + I.m[k];
-            const SV<T> old = ld_sv<T>(S, s + 21);
-            st_sv(S, s + 21, old + pA);
-        }
+        for (int k = 0; k < 6; k++) S(s + 15 + k) = S(s + 15 + k) + I.m[k];
+        const SV<T> old = ld_sv<T>(S, s + 21);
+        st_sv(S, s + 21, old + pA);
+    }
+}
+
+// ── pass 2: backward sweep ─────────────────────────────────────────────────
+template <int FEAT, class T, class Scr>
+PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
+    // zero the stored accumulators of branch bodies
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        if (bi.flags & F_BRANCH)
+            for (int k = 0; k < 27; k++) S(bi.s_acc + k) = T(0);
+    }
+    AI<T> I;
+    SV<T> pA = zerosv<T>();
+    ai_zero(I);
+    for (int i = M.nb - 1; i >= 0; i--) {
+        const BodyI bi = M.bi[i];
+#define PZ_P2(AX) pass2_body<AX, FEAT>(M, S, i, bi, I, pA)
+        PZ_BY_KIND(body_kind(bi), PZ_P2)
+#undef PZ_P2
     }
 }
 
@@ -939,72 +1089,95 @@ PZ_HD void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Scr& S,
     S(o + 2) = lg.z;
 }
 
-// ── pass 3 + integration of the current step, fused with pass 1 of the next
-// (aba.rs:322-400, then integrate.rs, then aba.rs:175-213 / contact).
-// `next_step` < 0 means this is the last step of the launch.
-template <int FEAT, class T, class Scr>
-PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int next_step, bool full,
-                      const Out<T>& qdd_out, const Out<T>& cs) {
-    SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
-    WF<T> cw;
-    const SV<T> a0 = mksv<T>(zero3<T>(), mk3<T>(-M.gx, -M.gy, -M.gz));
-    for (int i = 0; i < M.nb; i++) {
-        const BodyI bi = M.bi[i];
-        const BodyT<T>& bt = M.bt[i];
-        const int p = bi.parent;
-        const JX<T> j = load_jx<FEAT>(bi, bt, S);
-        SV<T> vpo, apar;
-        if (p < 0) {
-            vpo = zerosv<T>();
-            apar = a0;
-        } else if (p == i - 1) {
-            vpo = cvo;
-            apar = ca;
+// ── pass 3 + integration of body i for the current step, fused with pass 1
+// of the next (aba.rs:322-400, then integrate.rs, then aba.rs:175-213 and
+// the contact pass). `next_step` < 0: the last step of the launch.
+template <int AX, int FEAT, class T, class Scr>
+PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int i, const BodyI& bi,
+                      int next_step, const Out<T>& qdd_out, SV<T>& cvo, SV<T>& ca, SV<T>& cvn, WF<T>& cw) {
+    const BodyT<T>& bt = M.bt[i];
+    const int p = bi.parent;
+    const JX<T> j = load_jx<AX, FEAT>(bi, bt, S);
+    SV<T> vpo, apar;
+    if (p < 0) {
+        vpo = zerosv<T>();
+        apar = mksv<T>(zero3<T>(), mk3<T>(-M.gx, -M.gy, -M.gz));
+    } else if (p == i - 1) {
+        vpo = cvo;
+        apar = ca;
+    } else {
+        vpo = ld_sv<T>(S, M.bi[p].s_vold);
+        apar = ld_sv<T>(S, M.bi[p].s_acca);
+    }
+    SV<T> vo, c;
+    if constexpr (AX >= 0) {
+        const T qd = S(M.nv + bi.off);
+        vo = mot_X<AX, FEAT>(bi, bt, j, vpo);
+        at<AX>(vo.w) = at<AX>(vo.w) + qd;
+        c = mksv<T>(cross_axis<AX>(vo.w, qd), cross_axis<AX>(vo.l, qd));
+    } else {
+        const SV<T> vj = joint_vel<AX, FEAT>(bi, bt, S, M.nv);
+        vo = mot_X<AX, FEAT>(bi, bt, j, vpo) + vj;
+        c = crm(vo, vj);
+    }
+    SV<T> a = mot_X<AX, FEAT>(bi, bt, j, apar) + c;
+    T qdd0 = T(0);
+    if (AX >= 0 || bi.ndof == 1) {
+        qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
+        if constexpr (AX >= 0) {
+            at<AX>(a.w) = at<AX>(a.w) + qdd0;
         } else {
-            vpo = ld_sv<T>(S, M.bi[p].s_vold);
-            apar = ld_sv<T>(S, M.bi[p].s_acca);
-        }
-        const SV<T> vj = joint_vel<FEAT>(bi, bt, S, M.nv);
-        const SV<T> vo = mot_X<FEAT>(bi, bt, j, vpo) + vj;
-        const SV<T> c = crm(vo, vj);
-        SV<T> a = mot_X<FEAT>(bi, bt, j, apar) + c;
-        const int nd = bi.ndof;
-        T qdd0 = T(0);
-        if (nd == 1) {
-            qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
             const V3<T> ax = ld3(bt.axis);
             if (bi.jtype == J_REVOLUTE)
                 a.w = a.w + ax * qdd0;
             else
                 a.l = a.l + ax * qdd0;
-        } else if (nd > 1) {
-            if constexpr ((FEAT & FEAT_MULTI) != 0) multi_qdd(bi, S, a);
         }
-        if (bi.flags & F_BRANCH) {
-            st_sv(S, bi.s_vold, vo);
-            st_sv(S, bi.s_acca, a);
-        }
-        cvo = vo;
-        ca = a;
-        if (nd == 1) {
-            integrate_1dof(M, bi, S, qdd0);
-            qdd_out.put(bi.off, qdd0);
-        } else if (nd > 1) {
-            if constexpr ((FEAT & FEAT_MULTI) != 0) integrate_multi(M, bi, S, qdd_out);
-        }
-        if (next_step >= 0) {
-            prefetch_controls(M, bi, S, io, next_step);
-            pass1_body<FEAT>(M, S, i, cvn, cw, full, cs);
-        }
+    } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
+        if (bi.ndof > 1) multi_qdd(bi, S, a);
+    }
+    if (bi.flags & F_BRANCH) {
+        st_sv(S, bi.s_vold, vo);
+        st_sv(S, bi.s_acca, a);
+    }
+    cvo = vo;
+    ca = a;
+    if (AX >= 0 || bi.ndof == 1) {
+        integrate_1dof(M, bi, S, qdd0);
+        qdd_out.put(bi.off, qdd0);
+    } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
+        if (bi.ndof > 1) integrate_multi(M, bi, S, qdd_out);
+    }
+    if (next_step >= 0) {
+        prefetch_controls(M, bi, S, io, next_step);
+        pass1_body<AX, FEAT>(M, S, i, bi, cvn, cw);
+    }
+}
+
+template <int FEAT, class T, class Scr>
+PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int next_step,
+                      const Out<T>& qdd_out) {
+    SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
+    WF<T> cw;
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+#define PZ_P3(AX) pass3_body<AX, FEAT>(M, S, io, i, bi, next_step, qdd_out, cvo, ca, cvn, cw)
+        PZ_BY_KIND(body_kind(bi), PZ_P3)
+#undef PZ_P3
     }
 }
 
 // The initial pass 1 over the state loaded at the start of a launch.
 template <int FEAT, class T, class Scr>
-PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S, bool full, const Out<T>& cs) {
+PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S) {
     SV<T> cv = zerosv<T>();
     WF<T> cw;
-    for (int i = 0; i < M.nb; i++) pass1_body<FEAT>(M, S, i, cv, cw, full, cs);
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+#define PZ_P1(AX) pass1_body<AX, FEAT>(M, S, i, bi, cv, cw)
+        PZ_BY_KIND(body_kind(bi), PZ_P1)
+#undef PZ_P1
+    }
 }
 
 }  // namespace pz

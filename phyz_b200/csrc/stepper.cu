@@ -91,15 +91,17 @@ __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ Ro
         for (int i = 0; i < M.nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
         S.commit();
         const Out<T> none{nullptr, 0};
-        const Out<T> cs{P.cstate ? P.cstate + w : nullptr, N};
-        pass1_all<FEAT>(M, S, P.contact && P.cstate && P.nsteps == 1, P.nsteps == 1 ? cs : none);
+        pass1_all<FEAT>(M, S);
         for (int s = 0; s < P.nsteps; s++) {
             S.wait();
-            pass2<FEAT>(M, S);
             const bool last = s == P.nsteps - 1;
-            const bool full_next = P.contact && P.cstate && (s + 1 == P.nsteps - 1);
-            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, full_next, last ? Out<T>{P.qdd + w, N} : none,
-                             full_next ? cs : none);
+            if constexpr ((FEAT & FEAT_CONTACT) != 0) {
+                // contact state of the last step, from the state it starts from
+                if (last && P.contact && P.cstate)
+                    contact_state_pass<FEAT>(M, S, Out<T>{P.cstate + w, N});
+            }
+            pass2<FEAT>(M, S);
+            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, last ? Out<T>{P.qdd + w, N} : none);
             S.commit();
         }
         S.wait();
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ 
             for (int j = 0; j < M.nv; j++) acc += S(j) * S(j);
             continue;
         }
-        pass1_all<FEAT & FEAT_MULTI>(M, S, false, Out<T>{nullptr, 0});
+        pass1_all<FEAT & FEAT_MULTI>(M, S);
         for (int i = 0; i < M.nb; i++) {
             const BodyI bi = M.bi[i];
             const BodyT<T>& bt = M.bt[i];
