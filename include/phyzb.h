@@ -272,9 +272,10 @@ int phyzb_flops_per_world_step(const phyzb_sim* sim, double* flops, double* tran
  * thread's current device in TFLOP/s, measured with independent FMA chains
  * over every SM: the roofline denominator of the stepper's kernels. */
 int phyzb_measure_fma_peak(int precision, double* tflops);
-/* Launch configuration the fused kernel uses for this simulator. */
+/* Launch configuration the fused kernel uses for this simulator; tmem_cols
+ * > 0 when its body records live in Tensor Memory (columns per world). */
 int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
-                      int32_t* smem_bytes, int32_t* scratch_per_world);
+                      int32_t* smem_bytes, int32_t* scratch_per_world, int32_t* tmem_cols);
 
 #ifdef __cplusplus
 }

@@ -127,7 +127,7 @@ SIGNATURES = {
     "phyzb_step_device_controls": (C.c_int, [_P, _P, C.c_int64, C.c_int32]),
     "phyzb_objective_device": (C.c_int, [_P, C.c_int, _P]),
     "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
-    "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P]),
+    "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
     "phyzb_measure_fma_peak": (C.c_int, [C.c_int, _D]),
 }
 

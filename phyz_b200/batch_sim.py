@@ -238,7 +238,7 @@ class BatchSim:
         return f.value, t.value
 
     def launch_info(self) -> dict:
-        vals = [C.c_int32() for _ in range(4)]
+        vals = [C.c_int32() for _ in range(5)]
         check(self._lib.phyzb_launch_info(self._h, *[C.byref(x) for x in vals]))
-        return dict(zip(("worlds_per_block", "blocks", "smem_bytes", "scratch_per_world"),
+        return dict(zip(("worlds_per_block", "blocks", "smem_bytes", "scratch_per_world", "tmem_cols"),
                         [x.value for x in vals]))

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstdint>
 #include <cstring>
 #include <string>
@@ -67,10 +68,16 @@ struct phyzb_sim {
     void *q = nullptr, *v = nullptr, *ctrl = nullptr, *qdd = nullptr;
     void *targets = nullptr, *cstate = nullptr;
     int* status = nullptr;
-    void* blob = nullptr;
-    size_t blob_cap = 0;
-    pz::PackInfo info;
-    pz::LaunchCfg launch{};
+    // lay[0]: every record in shared memory (the objective kernel's layout
+    // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the
+    // layout the rollout kernel runs with.
+    struct Layout {
+        pz::PackInfo info;
+        void* blob = nullptr;
+        size_t cap = 0;
+        pz::LaunchCfg launch{};
+    } lay[2];
+    int use = 0;
     void* staging = nullptr;  // device, AoS f64 rows for host copies
     size_t staging_bytes = 0;
     // bulk per-step control pipeline (phyzb_step_with_controls)
@@ -87,31 +94,59 @@ namespace {
 
 bool is_f64(const phyzb_sim* s) { return s->precision == PHYZB_F64; }
 
-int repack(phyzb_sim* s) {
-    std::vector<unsigned char> blob;
-    s->info = is_f64(s) ? pz::pack_model<double>(&s->model, s->nv, s->cfg, blob)
-                        : pz::pack_model<float>(&s->model, s->nv, s->cfg, blob);
-    s->collidable = s->info.collidable;
-    // kernels already queued may read the table: drain the stream first
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
-    if ((size_t)s->info.bytes > s->blob_cap) {
-        if (s->blob) cudaFree(s->blob);
-        s->blob = nullptr;
-        s->blob_cap = 0;
-        PZ_CUDA(cudaMalloc(&s->blob, s->info.bytes));
-        s->blob_cap = s->info.bytes;
+int upload_layout(phyzb_sim* s, phyzb_sim::Layout& L, const std::vector<unsigned char>& blob) {
+    if ((size_t)L.info.bytes > L.cap) {
+        if (L.blob) cudaFree(L.blob);
+        L.blob = nullptr;
+        L.cap = 0;
+        PZ_CUDA(cudaMalloc(&L.blob, L.info.bytes));
+        L.cap = L.info.bytes;
     }
-    PZ_CUDA(cudaMemcpy(s->blob, blob.data(), s->info.bytes, cudaMemcpyHostToDevice));
-    cudaError_t e = is_f64(s) ? pz::rollout_config<double>(s->info.scratch, s->info.bytes, s->nworld, s->info.feat,
-                                                           &s->launch)
-                              : pz::rollout_config<float>(s->info.scratch, s->info.bytes, s->nworld, s->info.feat,
-                                                          &s->launch);
-    if (e == cudaErrorInvalidConfiguration)
-        return fail(PHYZB_ERR_TOO_LARGE, "per-world scratch (" + std::to_string(s->info.scratch) +
-                                             " slots) does not fit shared memory at 32 worlds per block");
-    PZ_CUDA(e);
+    PZ_CUDA(cudaMemcpy(L.blob, blob.data(), L.info.bytes, cudaMemcpyHostToDevice));
     return PHYZB_OK;
 }
+
+template <class T>
+int repack_t(phyzb_sim* s) {
+    // kernels already queued may read the tables: drain the stream first
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    std::vector<unsigned char> blob;
+    phyzb_sim::Layout& L0 = s->lay[0];
+    L0.info = pz::pack_model<T>(&s->model, s->nv, s->cfg, blob, 0);
+    s->collidable = L0.info.collidable;
+    PZ_TRY(upload_layout(s, L0, blob));
+    cudaError_t e = pz::rollout_config<T>(L0.info.scratch, L0.info.bytes, s->nworld, L0.info.feat, 0, &L0.launch);
+    if (e == cudaErrorInvalidConfiguration)
+        return fail(PHYZB_ERR_TOO_LARGE, "per-world scratch (" + std::to_string(L0.info.scratch) +
+                                             " slots) does not fit shared memory at 32 worlds per block");
+    PZ_CUDA(e);
+    s->use = 0;
+    const char* env = getenv("PHYZB_TMEM");
+    if (env && env[0] == '0') return PHYZB_OK;
+    // Tensor-Memory layouts: records of up to 512 or 256 columns per world
+    // (one or two warps per TMEM lane quarter); keep the best if it beats
+    // the shared-memory layout clearly.
+    double best = L0.launch.score;
+    for (int budget : {512, 256}) {
+        std::vector<unsigned char> tb;
+        pz::PackInfo ti = pz::pack_model<T>(&s->model, s->nv, s->cfg, tb, budget);
+        if (ti.tmem_cols == 0) break;
+        pz::LaunchCfg tc{};
+        e = pz::rollout_config<T>(ti.scratch, ti.bytes, s->nworld, ti.feat, ti.tmem_cols, &tc);
+        if (e == cudaErrorInvalidConfiguration) continue;
+        PZ_CUDA(e);
+        if (tc.score > best * 1.05) {
+            best = tc.score;
+            s->lay[1].info = ti;
+            s->lay[1].launch = tc;
+            PZ_TRY(upload_layout(s, s->lay[1], tb));
+            s->use = 1;
+        }
+    }
+    return PHYZB_OK;
+}
+
+int repack(phyzb_sim* s) { return is_f64(s) ? repack_t<double>(s) : repack_t<float>(s); }
 
 void set_model_copy(phyzb_sim* s, const phyzb_model* m) {
     s->bodies.assign(m->bodies, m->bodies + m->nbodies);
@@ -120,18 +155,19 @@ void set_model_copy(phyzb_sim* s, const phyzb_model* m) {
 }
 
 template <class T>
-pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long stride, int nsteps, int layout) {
+    const phyzb_sim::Layout& L = s->lay[layout];
     pz::RolloutArgs<T> a;
-    a.model_blob = s->blob;
-    a.model_bytes = s->info.bytes;
-    a.off_bi = s->info.off_bi;
-    a.off_pd = s->info.off_pd;
-    a.off_pdmap = s->info.off_pdmap;
+    a.model_blob = L.blob;
+    a.model_bytes = L.info.bytes;
+    a.off_bi = L.info.off_bi;
+    a.off_pd = L.info.off_pd;
+    a.off_pdmap = L.info.off_pdmap;
     a.nb = s->nb;
     a.nv = s->nv;
     a.npd = (int)s->cfg.pd.size();
     a.contact = s->cfg.contact ? 1 : 0;
-    a.feat = s->info.feat;
+    a.feat = L.info.feat;
     a.dt = s->model.dt;
     a.gx = s->model.gravity[0];
     a.gy = s->model.gravity[1];
@@ -148,15 +184,16 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     a.status = s->status;
     a.nworld = s->nworld;
     a.nsteps = nsteps;
-    a.scratch = s->info.scratch;
+    a.scratch = L.info.scratch;
     return a;
 }
 
 int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
-    cudaError_t e = is_f64(s) ? pz::launch_rollout<double>(rollout_args<double>(s, ctrl, stride, nsteps), s->launch,
-                                                           s->stream)
-                              : pz::launch_rollout<float>(rollout_args<float>(s, ctrl, stride, nsteps), s->launch,
-                                                          s->stream);
+    const phyzb_sim::Layout& L = s->lay[s->use];
+    cudaError_t e = is_f64(s) ? pz::launch_rollout<double>(rollout_args<double>(s, ctrl, stride, nsteps, s->use),
+                                                           L.launch, s->stream)
+                              : pz::launch_rollout<float>(rollout_args<float>(s, ctrl, stride, nsteps, s->use),
+                                                          L.launch, s->stream);
     PZ_CUDA(e);
     return PHYZB_OK;
 }
@@ -277,7 +314,8 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(s->cstate);
     void* st = s->status;
     free_ptr(st);
-    free_ptr(s->blob);
+    free_ptr(s->lay[0].blob);
+    free_ptr(s->lay[1].blob);
     free_ptr(s->staging);
     for (int b = 0; b < 2; b++) {
         free_ptr(s->pipe_raw[b]);
@@ -627,10 +665,10 @@ int phyzb_objective_device(phyzb_sim* s, int kind, void* out) {
     if (kind != 0 && kind != 1) return fail(PHYZB_ERR_INVALID, "objective kind must be 0 or 1");
     if (!out) return fail(PHYZB_ERR_INVALID, "output is null");
     DeviceGuard g(s->device);
-    cudaError_t e = is_f64(s) ? pz::launch_objective<double>(rollout_args<double>(s, s->ctrl, 0, 1), s->launch, kind,
-                                                             (double*)out, s->stream)
-                              : pz::launch_objective<float>(rollout_args<float>(s, s->ctrl, 0, 1), s->launch, kind,
-                                                            (float*)out, s->stream);
+    cudaError_t e = is_f64(s) ? pz::launch_objective<double>(rollout_args<double>(s, s->ctrl, 0, 1, 0),
+                                                             s->lay[0].launch, kind, (double*)out, s->stream)
+                              : pz::launch_objective<float>(rollout_args<float>(s, s->ctrl, 0, 1, 0),
+                                                            s->lay[0].launch, kind, (float*)out, s->stream);
     PZ_CUDA(e);
     return PHYZB_OK;
 }
@@ -643,12 +681,15 @@ int phyzb_flops_per_world_step(const phyzb_sim* s, double* flops, double* transc
     return PHYZB_OK;
 }
 
-int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t* smem, int32_t* scratch) {
+int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t* smem, int32_t* scratch,
+                      int32_t* tmem_cols) {
     PZ_TRY(check_sim(s));
-    if (wpb) *wpb = s->launch.W;
-    if (blocks) *blocks = s->launch.grid;
-    if (smem) *smem = s->launch.smem;
-    if (scratch) *scratch = s->info.scratch;
+    const phyzb_sim::Layout& L = s->lay[s->use];
+    if (wpb) *wpb = L.launch.W;
+    if (blocks) *blocks = L.launch.grid;
+    if (smem) *smem = L.launch.smem;
+    if (scratch) *scratch = L.info.scratch;
+    if (tmem_cols) *tmem_cols = L.launch.tm ? L.info.tmem_cols : 0;
     return PHYZB_OK;
 }
 

@@ -85,6 +85,28 @@ struct HostScr {
     void prefetch(int s, const Cnt* g) const { base[s] = *g; }
     void commit() const {}
     void wait() const {}
+    void fence_st() const {}
+    Rec<Cnt> rec_get(const BodyI& bi) const {
+        Rec<Cnt> r;
+        r.c = base[bi.s_xj];
+        r.s = base[bi.s_xj + 1];
+        r.v = mksv<Cnt>(mk3<Cnt>(base[bi.s_vw], base[bi.s_vw + 1], base[bi.s_vw + 2]),
+                        mk3<Cnt>(base[bi.s_vw + 3], base[bi.s_vw + 4], base[bi.s_vw + 5]));
+        return r;
+    }
+    void rec_put(const BodyI& bi, const Rec<Cnt>& r) const {
+        base[bi.s_xj] = r.c;
+        base[bi.s_xj + 1] = r.s;
+        rec_put_vw(bi, r.v);
+    }
+    void rec_put_vw(const BodyI& bi, const SV<Cnt>& v) const {
+        base[bi.s_vw] = v.w.x;
+        base[bi.s_vw + 1] = v.w.y;
+        base[bi.s_vw + 2] = v.w.z;
+        base[bi.s_vw + 3] = v.l.x;
+        base[bi.s_vw + 4] = v.l.y;
+        base[bi.s_vw + 5] = v.l.z;
+    }
 };
 }  // namespace
 

@@ -7,9 +7,11 @@
 namespace pz {
 
 struct LaunchCfg {
-    int W;     // worlds (threads) per block
-    int grid;  // blocks
-    int smem;  // dynamic shared memory bytes per block
+    int W;         // worlds (threads) per block
+    int grid;      // blocks
+    int smem;      // dynamic shared memory bytes per block
+    int tm;        // 1: body records in Tensor Memory (one block per SM)
+    double score;  // worlds resident per SM x fill of the last wave
 };
 
 // One fused rollout launch: `nsteps` steps of every world.
@@ -34,8 +36,10 @@ struct RolloutArgs {
     int scratch;           // scratch slots per world
 };
 
+// tmem_cols > 0: configure the Tensor-Memory variant for a layout whose
+// body records need tmem_cols columns per world.
 template <class T>
-cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, LaunchCfg* out);
+cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols, LaunchCfg* out);
 template <class T>
 cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
 

@@ -58,7 +58,7 @@ struct alignas(16) BodyI {
     int s_acca;       // branch: acceleration (6)
     int s_wx;         // branch: world frame for contact (up 3, height 1)
     int gtype;        // geometry code (0 none)
-    int npts;         // contact points (box 8, others 1)
+    int t_rec;        // Tensor Memory column of the body's record [c, s, v|W] (-1: in s_xj/s_vw)
 };
 
 template <class T>

@@ -74,6 +74,7 @@ struct PackInfo {
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
     int feat = 0;        // kernel variant: 1 = has ball/free joints, 2 = contact on
+    int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
 };
 
 inline int pad16(int b) { return (b + 15) & ~15; }
@@ -85,8 +86,29 @@ struct PackCfg {
     std::vector<phyzb_pd_dof> pd;        // PD servos
 };
 
+// A body whose per-step record [cos, sin, velocity | W] can live in Tensor
+// Memory: a hinge about exactly +e_k with an unrotated parent->joint frame
+// (the kernel's compile-time body kinds).
+inline bool tmem_kind(const phyzb_body& b) {
+    if (b.joint_type != J_REVOLUTE) return false;
+    const double* R = b.ptj_rot;
+    if (!(R[0] == 1.0 && R[1] == 0.0 && R[2] == 0.0 && R[3] == 0.0 && R[4] == 1.0 && R[5] == 0.0 && R[6] == 0.0 &&
+          R[7] == 0.0 && R[8] == 1.0))
+        return false;
+    for (int k = 0; k < 3; k++) {
+        bool unit = true;
+        for (int q = 0; q < 3; q++) unit = unit && (b.axis[q] == (q == k ? 1.0 : 0.0));
+        if (unit) return true;
+    }
+    return false;
+}
+
+// `tmem_budget` > 0: place the records of tmem_kind bodies in Tensor Memory
+// columns (8 words per record in f32, 16 in f64) while they fit the budget;
+// their s_xj / s_vw slots are then not allocated in shared memory.
 template <class T>
-inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std::vector<unsigned char>& blob) {
+inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std::vector<unsigned char>& blob,
+                           int tmem_budget = 0) {
     const int nb = m->nbodies;
     const int npd = (int)cfg.pd.size();
     PackInfo info;
@@ -188,14 +210,21 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         for (int j = i + 2; j < nb; j++)
             if (m->bodies[j].parent == i) flags |= F_BRANCH;
         d.gtype = b.geom_type;
-        d.npts = b.geom_type == 2 ? 8 : 1;
         if (b.geom_type != 0) info.collidable++;
 
         // scratch layout of this body
-        d.s_xj = next;
-        next += b.joint_type == J_REVOLUTE ? 2 : ((b.joint_type == J_BALL || b.joint_type == J_FREE) ? 9 : 0);
-        d.s_vw = next;
-        next += nd > 1 ? 6 * nd : 6;
+        const int rec_cols = 8 * (int)(sizeof(T) / 4);
+        d.t_rec = -1;
+        if (tmem_budget > 0 && tmem_kind(b) && info.tmem_cols + rec_cols <= tmem_budget) {
+            d.t_rec = info.tmem_cols;
+            info.tmem_cols += rec_cols;
+            d.s_xj = d.s_vw = -1;
+        } else {
+            d.s_xj = next;
+            next += b.joint_type == J_REVOLUTE ? 2 : ((b.joint_type == J_BALL || b.joint_type == J_FREE) ? 9 : 0);
+            d.s_vw = next;
+            next += nd > 1 ? 6 * nd : 6;
+        }
         d.s_w0 = next;
         next += nd;
         d.s_f = -1;

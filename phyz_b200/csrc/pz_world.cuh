@@ -164,6 +164,16 @@ PZ_HD V3<T> cross_axis(const V3<T>& a, const T& s) {
     return mk3<T>(a.y * s, -(a.x * s), T(0));
 }
 
+// Per-step record of a hinge body: joint cos/sin and the body velocity
+// (pass 1 -> pass 2) or W = U/D (pass 2 -> pass 3). The scratch policy
+// decides where it lives (shared-memory slots s_xj/s_vw, or Tensor Memory
+// columns t_rec).
+template <class T>
+struct Rec {
+    T c, s;
+    SV<T> v;
+};
+
 template <int AX, int FEAT, class T, class Scr>
 PZ_HD JX<T> load_jx(const BodyI& bi, const BodyT<T>& bt, const Scr& S) {
     JX<T> j;
@@ -394,6 +404,13 @@ template <class T, class Scr>
 PZ_HD SV<T> ld_sv(const Scr& S, int s) {
     return mksv<T>(mk3<T>(S(s), S(s + 1), S(s + 2)), mk3<T>(S(s + 3), S(s + 4), S(s + 5)));
 }
+// Velocity (or W) of any body, wherever its record lives.
+template <class T, class Scr>
+PZ_HD SV<T> ld_vel(const Scr& S, const BodyI& bi) {
+    if (bi.t_rec >= 0) return S.rec_get(bi).v;
+    return ld_sv<T>(S, bi.s_vw);
+}
+
 template <class T, class Scr>
 PZ_HD void st_sv(const Scr& S, int s, const SV<T>& v) {
     S(s) = v.w.x;
@@ -651,7 +668,8 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
     T deepest = T(0), dx = T(0), dy = T(0);
     bool any = false;
     const T pt_scale = bi.gtype == 2 ? T(0.25) : T(1);
-    for (int c = 0; c < bi.npts; c++) {
+    const int npts = bi.gtype == 2 ? 8 : 1;
+    for (int c = 0; c < npts; c++) {
         const V3<T> sup = support_pt(bi, bt, wf.up, c);
         const T z = wf.pos.z + dot(wf.up, sup);
         const T pen = M.ground_h - z;
@@ -767,20 +785,34 @@ template <int AX, int FEAT, class T, class Scr>
 PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& cv, WF<T>& cw) {
     const BodyT<T>& bt = M.bt[i];
     const int p = bi.parent;
-    const JX<T> j = make_jx<AX, FEAT>(bi, bt, S);
     SV<T> vpar;
     if (p < 0)
         vpar = zerosv<T>();
     else if (p == i - 1)
         vpar = cv;
-    else
-        vpar = ld_sv<T>(S, M.bi[p].s_vw);
-    SV<T> v = mot_X<AX, FEAT>(bi, bt, j, vpar);
-    if constexpr (AX >= 0)
+    else {
+        S.fence_st();  // the parent's record was stored earlier in this sweep
+        vpar = ld_vel<T>(S, M.bi[p]);
+    }
+    JX<T> j;
+    SV<T> v;
+    if constexpr (AX >= 0) {
+        T sn, cs;
+        pz_sincos(-S(bi.off), &sn, &cs);
+        j.c = cs;
+        j.s = sn;
+        v = mot_X<AX, FEAT>(bi, bt, j, vpar);
         at<AX>(v.w) = at<AX>(v.w) + S(M.nv + bi.off);
-    else
-        v = v + joint_vel<AX, FEAT>(bi, bt, S, M.nv);
-    st_sv(S, bi.s_vw, v);
+        Rec<T> r;
+        r.c = cs;
+        r.s = sn;
+        r.v = v;
+        S.rec_put(bi, r);
+    } else {
+        j = make_jx<AX, FEAT>(bi, bt, S);
+        v = mot_X<AX, FEAT>(bi, bt, j, vpar) + joint_vel<AX, FEAT>(bi, bt, S, M.nv);
+        st_sv(S, bi.s_vw, v);
+    }
     cv = v;
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
         V3<T> up_p;
@@ -835,7 +867,14 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
         for (int b = i; b >= 0; b = M.bi[b].parent) {
             const BodyI bb = M.bi[b];
             const BodyT<T>& tb = M.bt[b];
-            const JX<T> j = load_jx<-1, FEAT>(bb, tb, S);
+            JX<T> j;
+            if (bb.t_rec >= 0) {
+                const Rec<T> r = S.rec_get(bb);
+                j.c = r.c;
+                j.s = r.s;
+            } else {
+                j = load_jx<-1, FEAT>(bb, tb, S);
+            }
             // E_tree^T d = R_ptj^T R_J^T d
             auto up_dir = [&](V3<T> d) {
                 switch (bb.jtype) {
@@ -859,7 +898,7 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
         wf.r1 = mk3<T>(cx.y, cy.y, cz.y);
         wf.up = mk3<T>(cx.z, cy.z, cz.z);
         wf.pos = o;
-        contact_wrench(M, bi, M.bt[i], wf, ld_sv<T>(S, bi.s_vw), true, i, cs);
+        contact_wrench(M, bi, M.bt[i], wf, ld_vel<T>(S, bi), true, i, cs);
     }
 }
 
@@ -879,7 +918,14 @@ template <int AX, int FEAT, class T, class Scr>
 PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, AI<T>& I, SV<T>& pA) {
     const BodyT<T>& bt = M.bt[i];
     const int p = bi.parent;
-    const SV<T> v = ld_sv<T>(S, bi.s_vw);
+    Rec<T> rec;
+    SV<T> v;
+    if constexpr (AX >= 0) {
+        rec = S.rec_get(bi);
+        v = rec.v;
+    } else {
+        v = ld_sv<T>(S, bi.s_vw);
+    }
     if (!(bi.flags & F_CHAIN)) {
         ai_zero(I);
         pA = zerosv<T>();
@@ -956,16 +1002,19 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         }
         const T D = sU + bt.d_extra;
         const T u = dof_force(M, bi, bt, S, 0) - sp;
-        if (pz_abs(D) < T(1e-20)) {  // aba.rs:240-242: skip the body
-            live = false;
-            for (int r = 0; r < 6; r++) S(bi.s_vw + r) = T(0);
-            S(bi.s_w0) = T(0);
-        } else {
-            const T invD = T(1) / D;
-            const V3<T> Ww = Uw * invD, Wl = Ul * invD;
-            const T w0 = u * invD;
+        // aba.rs:240-242: a singular D skips the body (W = 0, w0 = 0). The
+        // record store happens once, outside any per-world branch, because
+        // a Tensor-Memory store is warp-wide.
+        live = !(pz_abs(D) < T(1e-20));
+        const T invD = live ? T(1) / D : T(0);
+        const V3<T> Ww = Uw * invD, Wl = Ul * invD;
+        const T w0 = u * invD;
+        if constexpr (AX >= 0)
+            S.rec_put_vw(bi, mksv<T>(Ww, Wl));
+        else
             st_sv(S, bi.s_vw, mksv<T>(Ww, Wl));
-            S(bi.s_w0) = w0;
+        S(bi.s_w0) = w0;
+        if (live) {
             if (p >= 0) {
                 // I <- I - W U^T (rank-1, symmetric)
 #pragma unroll
@@ -1003,7 +1052,13 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         pA = zerosv<T>();
         return;
     }
-    const JX<T> j = load_jx<AX, FEAT>(bi, bt, S);
+    JX<T> j;
+    if constexpr (AX >= 0) {
+        j.c = rec.c;
+        j.s = rec.s;
+    } else {
+        j = load_jx<AX, FEAT>(bi, bt, S);
+    }
     ai_XtIX<AX, FEAT>(bi, bt, j, I);
     pA = frc_XT<AX, FEAT>(bi, bt, j, pA);
     if (p != i - 1) {
@@ -1037,6 +1092,7 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
         PZ_BY_KIND(body_kind(bi), PZ_P2)
 #undef PZ_P2
     }
+    S.fence_st();
 }
 
 // ── integrator of body i (integrate.rs:41-91), v first then q ─────────────
@@ -1097,7 +1153,16 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
                       int next_step, const Out<T>& qdd_out, SV<T>& cvo, SV<T>& ca, SV<T>& cvn, WF<T>& cw) {
     const BodyT<T>& bt = M.bt[i];
     const int p = bi.parent;
-    const JX<T> j = load_jx<AX, FEAT>(bi, bt, S);
+    JX<T> j;
+    SV<T> Wv;
+    if constexpr (AX >= 0) {
+        const Rec<T> rec = S.rec_get(bi);
+        j.c = rec.c;
+        j.s = rec.s;
+        Wv = rec.v;
+    } else {
+        j = load_jx<AX, FEAT>(bi, bt, S);
+    }
     SV<T> vpo, apar;
     if (p < 0) {
         vpo = zerosv<T>();
@@ -1123,7 +1188,10 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
     SV<T> a = mot_X<AX, FEAT>(bi, bt, j, apar) + c;
     T qdd0 = T(0);
     if (AX >= 0 || bi.ndof == 1) {
-        qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
+        if constexpr (AX >= 0)
+            qdd0 = S(bi.s_w0) - dot(Wv, a);
+        else
+            qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
         if constexpr (AX >= 0) {
             at<AX>(a.w) = at<AX>(a.w) + qdd0;
         } else {
@@ -1165,6 +1233,7 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
         PZ_BY_KIND(body_kind(bi), PZ_P3)
 #undef PZ_P3
     }
+    S.fence_st();
 }
 
 // The initial pass 1 over the state loaded at the start of a launch.
@@ -1178,6 +1247,7 @@ PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S) {
         PZ_BY_KIND(body_kind(bi), PZ_P1)
 #undef PZ_P1
     }
+    S.fence_st();
 }
 
 }  // namespace pz

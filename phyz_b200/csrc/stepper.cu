@@ -17,6 +17,8 @@
 #include <cstdint>
 #include <cmath>
 #include <cstdlib>
+#include <algorithm>
+#include <type_traits>
 
 #include "pz_launch.h"
 #include "pz_world.cuh"
@@ -36,6 +38,123 @@ struct SmemScr {
     }
     __device__ __forceinline__ void commit() const { asm volatile("cp.async.commit_group;\n" ::); }
     __device__ __forceinline__ void wait() const { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+    __device__ __forceinline__ void fence_st() const {}
+    __device__ __forceinline__ Rec<T> rec_get(const BodyI& bi) const {
+        Rec<T> r;
+        r.c = (*this)(bi.s_xj);
+        r.s = (*this)(bi.s_xj + 1);
+        r.v = ld_sv<T>(*this, bi.s_vw);
+        return r;
+    }
+    __device__ __forceinline__ void rec_put(const BodyI& bi, const Rec<T>& r) const {
+        (*this)(bi.s_xj) = r.c;
+        (*this)(bi.s_xj + 1) = r.s;
+        st_sv(*this, bi.s_vw, r.v);
+    }
+    __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const { st_sv(*this, bi.s_vw, v); }
+};
+
+// Tensor Memory scratch for body records: each thread owns the TMEM lane of
+// its position in its warp (the warp's lane quarter is warp % 4) and a range
+// of columns; a record [c, s, v0..v5] is 8 consecutive 32-bit columns (16 in
+// f64) moved with one tcgen05.ld / tcgen05.st of shape 32x32b. Bodies whose
+// t_rec < 0 keep their record in shared memory. All record accesses are
+// warp-uniform (every thread of a warp processes the same body).
+template <class T>
+struct TmemScr : SmemScr<T> {
+    unsigned tbase;  // (lane quarter << 16) | this warp's first column
+    __device__ __forceinline__ Rec<T> rec_get(const BodyI& bi) const {
+        if (bi.t_rec < 0) return SmemScr<T>::rec_get(bi);
+        const unsigned a = tbase + (unsigned)bi.t_rec;
+        Rec<T> r;
+        if constexpr (sizeof(T) == 4) {
+            unsigned x0, x1, x2, x3, x4, x5, x6, x7;
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+                         : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3), "=r"(x4), "=r"(x5), "=r"(x6), "=r"(x7)
+                         : "r"(a));
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                         : "+r"(x0), "+r"(x1), "+r"(x2), "+r"(x3), "+r"(x4), "+r"(x5), "+r"(x6), "+r"(x7)::"memory");
+            r.c = __uint_as_float(x0);
+            r.s = __uint_as_float(x1);
+            r.v = mksv<T>(mk3<T>(__uint_as_float(x2), __uint_as_float(x3), __uint_as_float(x4)),
+                          mk3<T>(__uint_as_float(x5), __uint_as_float(x6), __uint_as_float(x7)));
+        } else {
+            unsigned x[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                "%14, %15}, [%16];\n"
+                : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
+                  "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15])
+                : "r"(a));
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                         : "+r"(x[0]), "+r"(x[1]), "+r"(x[2]), "+r"(x[3]), "+r"(x[4]), "+r"(x[5]), "+r"(x[6]),
+                           "+r"(x[7]), "+r"(x[8]), "+r"(x[9]), "+r"(x[10]), "+r"(x[11]), "+r"(x[12]), "+r"(x[13]),
+                           "+r"(x[14]), "+r"(x[15])::"memory");
+            T d[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) d[k] = T(__hiloint2double((int)x[2 * k + 1], (int)x[2 * k]));
+            r.c = d[0];
+            r.s = d[1];
+            r.v = mksv<T>(mk3<T>(d[2], d[3], d[4]), mk3<T>(d[5], d[6], d[7]));
+        }
+        return r;
+    }
+    __device__ __forceinline__ void put_words(unsigned a, const T* d, int n) const {
+        // n = 8 (whole record) or 6 (columns 2..7: v / W only)
+        if constexpr (sizeof(T) == 4) {
+            unsigned x[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) x[k] = __float_as_uint(d[k]);
+            if (n == 8)
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(a),
+                             "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
+                             : "memory");
+            else {
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};\n" ::"r"(a + 2u), "r"(x[2]),
+                             "r"(x[3])
+                             : "memory");
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(a + 4u),
+                             "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
+                             : "memory");
+            }
+        } else {
+            unsigned x[16];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                x[2 * k] = (unsigned)__double2loint((double)d[k]);
+                x[2 * k + 1] = (unsigned)__double2hiint((double)d[k]);
+            }
+            if (n == 8)
+                asm volatile(
+                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                    "%13, %14, %15, %16};\n" ::"r"(a),
+                    "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7]), "r"(x[8]),
+                    "r"(x[9]), "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]), "r"(x[15])
+                    : "memory");
+            else {
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(a + 4u),
+                             "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
+                             : "memory");
+                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(
+                                 a + 8u),
+                             "r"(x[8]), "r"(x[9]), "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]),
+                             "r"(x[15])
+                             : "memory");
+            }
+        }
+    }
+    __device__ __forceinline__ void rec_put(const BodyI& bi, const Rec<T>& r) const {
+        if (bi.t_rec < 0) return SmemScr<T>::rec_put(bi, r);
+        const T d[8] = {r.c, r.s, r.v.w.x, r.v.w.y, r.v.w.z, r.v.l.x, r.v.l.y, r.v.l.z};
+        put_words(tbase + (unsigned)bi.t_rec, d, 8);
+    }
+    __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const {
+        if (bi.t_rec < 0) return SmemScr<T>::rec_put_vw(bi, v);
+        const T d[8] = {T(0), T(0), v.w.x, v.w.y, v.w.z, v.l.x, v.l.y, v.l.z};
+        put_words(tbase + (unsigned)bi.t_rec, d, 6);
+    }
+    // stores complete before later loads of the same columns
+    __device__ __forceinline__ void fence_st() const { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 };
 
 template <class T>
@@ -71,18 +190,46 @@ __device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, 
     return smem;
 }
 
-template <class T, int FEAT>
+// TMEM columns allocated per block by the Tensor-Memory variant: the whole
+// array (one block per SM).
+constexpr unsigned TMEM_COLS = 512;
+
+template <class T, int FEAT, bool TM>
 __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
     extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ unsigned tmem_slot;
     const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
     const ModelView<T> M = make_view<T>(P, blob);
     const int W = blockDim.x;
-    const SmemScr<T> S{reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x, W};
+    using Scr = typename std::conditional<TM, TmemScr<T>, SmemScr<T>>::type;
+    Scr S;
+    S.base = reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x;
+    S.W = W;
+    const int warp = threadIdx.x >> 5;
+    if constexpr (TM) {
+        if (warp == 0) {
+            const unsigned dst = (unsigned)__cvta_generic_to_shared(&tmem_slot);
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(dst),
+                         "r"(TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        // warps w, w+4, w+8, ... share lane quarter w % 4 and split its columns
+        const int nwarps = (W + 31) >> 5;
+        const unsigned per_quarter = (unsigned)((nwarps + 3) >> 2);
+        const unsigned cols = TMEM_COLS / per_quarter;
+        S.tbase = tmem_slot + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(warp >> 2) * cols;
+    }
     const long long ntiles = (P.nworld + W - 1) / W;
+    const long long N = P.nworld;
     for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long w = tile * W + threadIdx.x;
-        if (w >= P.nworld) continue;  // no block-wide synchronisation past this point
-        const long long N = P.nworld;
+        const long long wt = tile * W + threadIdx.x;
+        // lanes past the last world run world N-1 again and write nothing, so
+        // every warp stays converged for the warp-wide tcgen05 operations
+        const bool active = wt < N;
+        const long long w = active ? wt : N - 1;
         for (int j = 0; j < M.nv; j++) {
             S(j) = P.q[j * N + w];
             S(M.nv + j) = P.v[j * N + w];
@@ -97,25 +244,35 @@ __global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ Ro
             const bool last = s == P.nsteps - 1;
             if constexpr ((FEAT & FEAT_CONTACT) != 0) {
                 // contact state of the last step, from the state it starts from
+                // (every lane runs it, warp-wide record loads; only active lanes write)
                 if (last && P.contact && P.cstate)
-                    contact_state_pass<FEAT>(M, S, Out<T>{P.cstate + w, N});
+                    contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
             pass2<FEAT>(M, S);
-            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, last ? Out<T>{P.qdd + w, N} : none);
+            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, (last && active) ? Out<T>{P.qdd + w, N} : none);
             S.commit();
         }
         S.wait();
-        bool finite = true;
-        for (int j = 0; j < M.nv; j++) {
-            const T qj = S(j), vj = S(M.nv + j);
-            finite = finite && pz_finite(qj) && pz_finite(vj);
-            P.q[j * N + w] = qj;
-            P.v[j * N + w] = vj;
+        if (active) {
+            bool finite = true;
+            for (int j = 0; j < M.nv; j++) {
+                const T qj = S(j), vj = S(M.nv + j);
+                finite = finite && pz_finite(qj) && pz_finite(vj);
+                P.q[j * N + w] = qj;
+                P.v[j * N + w] = vj;
+            }
+            if (!finite) {
+                atomicOr(P.status, 1);
+                atomicMin(P.status + 1, (int)(w < 0x7fffffff ? w : 0x7fffffff));
+            }
         }
-        if (!finite) {
-            atomicOr(P.status, 1);
-            atomicMin(P.status + 1, (int)(w < 0x7fffffff ? w : 0x7fffffff));
-        }
+    }
+    if constexpr (TM) {
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncthreads();
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        if (warp == 0)
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_slot), "r"(TMEM_COLS));
     }
 }
 
@@ -225,29 +382,44 @@ static cudaError_t device_limits() {
     return cudaSuccess;
 }
 
-template <class T, int FEAT>
-static cudaError_t config_variant(int scratch, int model_bytes, long long nworld, LaunchCfg* out) {
-    cudaError_t e = cudaFuncSetAttribute(rollout_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <class T, int FEAT, bool TM>
+static cudaError_t config_variant(int scratch, int model_bytes, long long nworld, int tmem_cols, LaunchCfg* out) {
+    cudaError_t e = cudaFuncSetAttribute(rollout_kernel<T, FEAT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          g_smem_optin);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize, g_smem_optin);
-    if (e != cudaSuccess) return e;
+    if (!TM) {
+        e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 g_smem_optin);
+        if (e != cudaSuccess) return e;
+    }
     const long long per_world = (long long)scratch * (long long)sizeof(T);
-    // Pick the block width (any even width up to the 256 of __launch_bounds__)
-    // that keeps the most worlds resident per SM, discounted by how full the
-    // last wave of tiles is. PHYZB_WORLDS_PER_BLOCK overrides it for tuning.
+    // Pick the block width that keeps the most worlds resident per SM,
+    // discounted by how full the last wave of tiles is. Shared-memory layout:
+    // any even width up to the 256 of __launch_bounds__. Tensor-Memory layout:
+    // whole warps, one block per SM, and few enough warps per TMEM lane
+    // quarter that each thread's columns hold its records.
+    // PHYZB_WORLDS_PER_BLOCK overrides the width for tuning.
     int forced = 0;
     if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
     int best_w = 0, best_blocks = 0, best_smem = 0;
     double best_score = -1.0;
-    for (int W = 32; W <= 256; W += 2) {
+    const int step = TM ? 32 : 2;
+    for (int W = 32; W <= 256; W += step) {
         if (forced > 0 && W != forced) continue;
-        const long long smem = (long long)model_bytes + per_world * W;
+        if (TM) {
+            const int per_quarter = ((W + 31) / 32 + 3) / 4;
+            if (tmem_cols * per_quarter > (int)TMEM_COLS) break;
+        }
+        long long smem = (long long)model_bytes + per_world * W;
         if (smem > g_smem_optin) break;
+        // Tensor-Memory blocks ask for more than half an SM's shared memory so
+        // that no second block lands on the SM and waits on the allocation
+        if (TM) smem = std::max(smem, (long long)(g_smem_optin / 2 + 16) & ~15LL);
         int blocks = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT>, W, (size_t)smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT, TM>, W, (size_t)smem);
         if (e != cudaSuccess) return e;
         if (blocks <= 0) continue;
+        if (TM) blocks = 1;  // each block holds the whole Tensor Memory
         const double resident = (double)blocks * W * g_sm_count;  // worlds in flight on the GPU
         const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
         const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
@@ -265,30 +437,48 @@ static cudaError_t config_variant(int scratch, int model_bytes, long long nworld
     out->W = best_w;
     out->grid = (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
     out->smem = best_smem;
+    out->tm = TM ? 1 : 0;
+    out->score = best_score;
     return cudaSuccess;
 }
 
+template <class T, bool TM>
+static cudaError_t config_dispatch(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols,
+                                   LaunchCfg* out) {
+    switch (feat) {
+        case 0: return config_variant<T, 0, TM>(scratch, model_bytes, nworld, tmem_cols, out);
+        case FEAT_MULTI: return config_variant<T, FEAT_MULTI, TM>(scratch, model_bytes, nworld, tmem_cols, out);
+        case FEAT_CONTACT: return config_variant<T, FEAT_CONTACT, TM>(scratch, model_bytes, nworld, tmem_cols, out);
+        default:
+            return config_variant<T, FEAT_MULTI | FEAT_CONTACT, TM>(scratch, model_bytes, nworld, tmem_cols, out);
+    }
+}
+
 template <class T>
-cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, LaunchCfg* out) {
+cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols, LaunchCfg* out) {
     cudaError_t e = device_limits();
     if (e != cudaSuccess) return e;
-    switch (feat) {
-        case 0: return config_variant<T, 0>(scratch, model_bytes, nworld, out);
-        case FEAT_MULTI: return config_variant<T, FEAT_MULTI>(scratch, model_bytes, nworld, out);
-        case FEAT_CONTACT: return config_variant<T, FEAT_CONTACT>(scratch, model_bytes, nworld, out);
-        default: return config_variant<T, FEAT_MULTI | FEAT_CONTACT>(scratch, model_bytes, nworld, out);
+    if (tmem_cols > 0) return config_dispatch<T, true>(scratch, model_bytes, nworld, feat, tmem_cols, out);
+    return config_dispatch<T, false>(scratch, model_bytes, nworld, feat, 0, out);
+}
+
+template <class T, bool TM>
+static void launch_variant(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
+    switch (a.feat) {
+        case 0: rollout_kernel<T, 0, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        case FEAT_MULTI: rollout_kernel<T, FEAT_MULTI, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        case FEAT_CONTACT: rollout_kernel<T, FEAT_CONTACT, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
+        default: rollout_kernel<T, FEAT_MULTI | FEAT_CONTACT, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
     }
 }
 
 template <class T>
 cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
     if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
-    switch (a.feat) {
-        case 0: rollout_kernel<T, 0><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        case FEAT_MULTI: rollout_kernel<T, FEAT_MULTI><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        case FEAT_CONTACT: rollout_kernel<T, FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        default: rollout_kernel<T, FEAT_MULTI | FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-    }
+    if (cfg.tm)
+        launch_variant<T, true>(a, cfg, s);
+    else
+        launch_variant<T, false>(a, cfg, s);
     return cudaGetLastError();
 }
 
@@ -322,8 +512,8 @@ cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int w
     return cudaGetLastError();
 }
 
-template cudaError_t rollout_config<float>(int, int, long long, int, LaunchCfg*);
-template cudaError_t rollout_config<double>(int, int, long long, int, LaunchCfg*);
+template cudaError_t rollout_config<float>(int, int, long long, int, int, LaunchCfg*);
+template cudaError_t rollout_config<double>(int, int, long long, int, int, LaunchCfg*);
 template cudaError_t launch_rollout<float>(const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t launch_rollout<double>(const RolloutArgs<double>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t launch_objective<float>(const RolloutArgs<float>&, const LaunchCfg&, int, float*,
