@@ -36,10 +36,26 @@ sys.path.insert(0, str(ROOT))
 
 import numpy as np  # noqa: E402
 
-# DRAM bytes per world-step of the fused kernel measured by ncu
-# (profiles/rollout_kernel_c2_chain32.md: dram__bytes_read.sum +
-# dram__bytes_write.sum of one launch / (worlds x steps)); None until measured.
-NCU_DRAM_BYTES_PER_WORLD_STEP: dict = {}
+# DRAM traffic of one rollout_kernel launch measured by ncu on a smaller
+# case of the same workload (profiles/rollout_kernel_c2_chain32_f32.md:
+# dram__bytes_read.sum + dram__bytes_write.sum, 65536 worlds x 20 steps).
+# A launch reads/writes each world's state once and streams one control row
+# per step, so it is scaled to the bench's launch as
+#   state bytes (q, v in and out) + per-world-step bytes x worlds x steps,
+# with the per-world-step part taken from the capture after removing its
+# state bytes.
+NCU_DRAM_CAPTURES: dict = {
+    ("c2_chain32", "f32"): {"nworld": 65536, "horizon": 20, "bytes": 184.842240e6 + 12.996096e6},
+}
+
+
+def ncu_traffic(config, prec, nv, esz, nworld, horizon):
+    cap = NCU_DRAM_CAPTURES.get((config, prec))
+    if cap is None:
+        return None
+    state = lambda n: 4 * nv * esz * n  # q, v read and written once per launch
+    per_ws = (cap["bytes"] - state(cap["nworld"])) / (cap["nworld"] * cap["horizon"])
+    return state(nworld) + per_ws * nworld * horizon
 
 
 def parse():
@@ -303,9 +319,9 @@ def main():
     pk = np.zeros(1)
     L.check(L.load().phyzb_measure_fma_peak(L.F32 if prec == "f32" else L.F64, L.dptr(pk)))
     achieved = flops_ws * nworld * horizon / (kernel_ms * 1e-3) / 1e12
-    traffic = None
-    if (args.config, prec) in NCU_DRAM_BYTES_PER_WORLD_STEP:
-        traffic = NCU_DRAM_BYTES_PER_WORLD_STEP[(args.config, prec)] * nworld * horizon
+    traffic = ncu_traffic(args.config, prec, nv, esz, nworld, horizon)
+    hbm_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs") \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
     alg_bytes = (3 + 2) * nv * esz  # read q, v, ctrl; write q, v per world-step
     roofline = {
         "bound": "fma", "pipe": f"{'fp32' if prec == 'f32' else 'fp64'} FMA", "achieved": achieved,
@@ -315,6 +331,11 @@ def main():
         "flops_per_world_step": flops_ws, "transcendentals_per_world_step": trans_ws,
         "algorithmic_bytes_per_world_step": alg_bytes,
         "hbm_gbs_algorithmic": alg_bytes * nworld * horizon / (kernel_ms * 1e-3) / 1e9,
+        "hbm_gbs_measured_traffic": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9,
+        "hbm_peak_gbs": hbm_peak,
+        "hbm_frac": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9 / hbm_peak,
+        "traffic_note": "ncu DRAM bytes of a 20-step capture scaled to this launch (state once + "
+                        "control stream per step); None where no capture exists for this config",
     }
 
     # e2e through the C ABI with host buffers

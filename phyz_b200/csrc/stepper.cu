@@ -384,8 +384,12 @@ static cudaError_t device_limits() {
 
 template <class T, int FEAT, bool TM>
 static cudaError_t config_variant(int scratch, int model_bytes, long long nworld, int tmem_cols, LaunchCfg* out) {
-    cudaError_t e = cudaFuncSetAttribute(rollout_kernel<T, FEAT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         g_smem_optin);
+    // the opt-in limit covers static and dynamic shared memory together
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaFuncGetAttributes(&fa, rollout_kernel<T, FEAT, TM>);
+    if (e != cudaSuccess) return e;
+    const int dyn_cap = g_smem_optin - (int)fa.sharedSizeBytes;
+    e = cudaFuncSetAttribute(rollout_kernel<T, FEAT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_cap);
     if (e != cudaSuccess) return e;
     if (!TM) {
         e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -411,7 +415,7 @@ static cudaError_t config_variant(int scratch, int model_bytes, long long nworld
             if (tmem_cols * per_quarter > (int)TMEM_COLS) break;
         }
         long long smem = (long long)model_bytes + per_world * W;
-        if (smem > g_smem_optin) break;
+        if (smem > dyn_cap) break;
         // Tensor-Memory blocks ask for more than half an SM's shared memory so
         // that no second block lands on the SM and waits on the allocation
         if (TM) smem = std::max(smem, (long long)(g_smem_optin / 2 + 16) & ~15LL);

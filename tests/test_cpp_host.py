@@ -44,6 +44,7 @@ def test_cpp_host_rollout_matches_oracle(host_binary, oracle):
 
     n, steps = 8, 100
     out = run(host_binary, n, steps)
+    assert "error" not in out, out
     assert out["contacts_err"] == -4
     t = np.arange(n) / n
     q0 = np.stack([0.2 + 1.2 * t, -0.4 + 0.8 * t], 1)

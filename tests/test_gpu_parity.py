@@ -257,3 +257,36 @@ def test_device_schedule_matches_host_schedule():
     sim.sync()
     qd, vd = sim.readback_states()
     assert np.array_equal(qd, qh) and np.array_equal(vd, vh)
+
+
+@pytest.mark.parametrize("name", list(configs.CONFIGS))
+@pytest.mark.parametrize("precision", ["f64", "f32"])
+def test_tensor_memory_layout(oracle, monkeypatch, name, precision):
+    """The Tensor-Memory layout (hinge records in TMEM, one block per SM)
+    forced at a ragged world count (the last warp partly idle) agrees with
+    the oracle and with the shared-memory layout over a 30-step schedule."""
+    n, steps = 70, 30
+    model, q0, v0, sched, contact = config_inputs(name, n, steps)
+    out = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("PHYZB_TMEM", mode)
+        sim = BatchSim(model, n, precision=precision)
+        if contact is not None:
+            sim.enable_ground_contact(*contact)
+        info = sim.launch_info()
+        assert (info["tmem_cols"] > 0) == (mode == "1"), info
+        sim.load_states(q0, v0)
+        sim.step_with_controls(np.ascontiguousarray(sched))
+        sim.sync()
+        q, v = sim.readback_states()
+        out[mode] = (q, v, sim.readback_qdd(), sim.readback_contacts() if contact is not None else None)
+        sim.close()
+    oc = None if contact is None else (contact[0], contact[3], contact[1], contact[2])
+    qo, vo, qddo, cso = oracle.rollout(model, q0, v0, sched, steps, schedule=True, contact=oc)
+    tol = 1e-7 if precision == "f64" else F32_TOL
+    q, v, qdd, cs = out["1"]
+    assert rel_err(q, qo) <= tol and rel_err(v, vo) <= tol, (rel_err(q, qo), rel_err(v, vo))
+    same = 1e-12 if precision == "f64" else 1e-5
+    for a, b in zip(out["1"], out["0"]):
+        if a is not None:
+            assert rel_err(a, b) <= same, rel_err(a, b)
