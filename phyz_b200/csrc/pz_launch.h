@@ -21,7 +21,7 @@ struct RolloutArgs {
     int model_bytes;         // multiple of 16
     int off_bi, off_pd, off_pdmap;
     int nb, nv, npd, contact;
-    int feat;              // kernel variant: FEAT_MULTI | FEAT_CONTACT bits (pz_world.cuh)
+    int feat;              // kernel variant: FEAT_MULTI | FEAT_CONTACT | FEAT_PERM bits (pz_world.cuh)
     double dt, gx, gy, gz, ground_h, friction;
     T* q;                  // [nv][nworld]
     T* v;                  // [nv][nworld]

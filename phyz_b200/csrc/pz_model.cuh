@@ -10,6 +10,14 @@
 // formulation (inertia about the body origin, m*c, COM inverse inertia,
 // armature + dt*damping).
 //
+// Frames: a hinge about a coordinate axis e_k with an unrotated parent->joint
+// frame is stored in its body frame with the coordinates cyclically
+// relabelled so that its axis is z (a proper rotation P_k, applied to every
+// body-frame constant at pack time). Its parent->child transform is then
+// "translate, relabel (a cyclic permutation), rotate about z": one code path
+// for all three axes. Joint-space quantities and world-frame outputs do not
+// depend on the relabelling.
+//
 // The integer half names where each body's per-world scratch lives: the
 // per-world state is structure-of-arrays in shared memory, slot s of a
 // world at smem[s * worlds_per_block + thread].
@@ -28,6 +36,8 @@ enum BodyFlags {
     F_CONTACT = 1 << 5,   // collidable while contact is enabled (has an F slot)
     F_CHAIN = 1 << 6,     // body i+1 has this body as parent (backward carry)
     F_BRANCH = 1 << 7,    // parent of a child that is not i+1 (stored accumulators)
+    F_ZHINGE = 1 << 8,    // hinge about z of its (relabelled) frame; parent->joint rotation
+                          // is the cyclic relabelling `qshift` (the kernel's fast path)
 };
 
 template <class T>
@@ -59,6 +69,7 @@ struct alignas(16) BodyI {
     int s_wx;         // branch: world frame for contact (up 3, height 1)
     int gtype;        // geometry code (0 none)
     int t_rec;        // Tensor Memory column of the body's record [c, s, v|W] (-1: in s_xj/s_vw)
+    int qshift;       // F_ZHINGE: parent->child relabelling (Q v)_a = v_(a+qshift mod 3)
 };
 
 template <class T>

@@ -73,7 +73,7 @@ struct PackInfo {
     int off_bi = 0, off_pd = 0, off_pdmap = 0, bytes = 0;
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
-    int feat = 0;        // kernel variant: 1 = has ball/free joints, 2 = contact on
+    int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges
     int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
 };
 
@@ -103,6 +103,57 @@ inline bool tmem_kind(const phyzb_body& b) {
     return false;
 }
 
+// Coordinate relabelling of each body frame (pz_model.cuh): shift s with
+// (P_s v)_a = v_(a+s mod 3). A hinge about e_x gets s = 1, about e_y s = 2
+// (both map the axis to e_z); every other body keeps s = 0.
+inline int frame_shift(const phyzb_body& b) {
+    if (!tmem_kind(b)) return 0;
+    return b.axis[0] == 1.0 ? 1 : (b.axis[1] == 1.0 ? 2 : 0);
+}
+
+// The model with every body-frame constant expressed in the relabelled
+// frames: com, COM inertia, axis, geometry origin (P_i), the parent->joint
+// offset in the parent's frame (P_p), and the parent->joint rotation
+// P_i R P_p^T (for a relabelled hinge the cyclic permutation P_(s_i - s_p)).
+inline std::vector<phyzb_body> relabel_frames(const phyzb_model* m, std::vector<int>& shift) {
+    const int nb = m->nbodies;
+    std::vector<phyzb_body> out(m->bodies, m->bodies + nb);
+    shift.assign(nb, 0);
+    for (int i = 0; i < nb; i++) shift[i] = frame_shift(m->bodies[i]);
+    auto pv = [](const double* v, int s, double* o) {
+        double t[3];
+        for (int a = 0; a < 3; a++) t[a] = v[(a + s) % 3];
+        for (int a = 0; a < 3; a++) o[a] = t[a];
+    };
+    for (int i = 0; i < nb; i++) {
+        const phyzb_body& b = m->bodies[i];
+        phyzb_body& o = out[i];
+        const int si = shift[i], sp = b.parent >= 0 ? shift[b.parent] : 0;
+        pv(b.com, si, o.com);
+        pv(b.axis, si, o.axis);
+        pv(b.geom_origin_pos, si, o.geom_origin_pos);
+        pv(b.ptj_pos, sp, o.ptj_pos);
+        // COM inertia P I P^T: I'_rc = I_(r+s)(c+s)
+        const double* J = b.inertia;
+        const double full[9] = {J[0], J[3], J[4], J[3], J[1], J[5], J[4], J[5], J[2]};
+        auto f = [&](int r, int c) { return full[((r + si) % 3) * 3 + (c + si) % 3]; };
+        o.inertia[0] = f(0, 0);
+        o.inertia[1] = f(1, 1);
+        o.inertia[2] = f(2, 2);
+        o.inertia[3] = f(0, 1);
+        o.inertia[4] = f(0, 2);
+        o.inertia[5] = f(1, 2);
+        // parent->joint rotation P_i R P_p^T: R'_rc = R_(r+si)(c+sp)
+        for (int r = 0; r < 3; r++)
+            for (int c = 0; c < 3; c++) o.ptj_rot[r * 3 + c] = b.ptj_rot[((r + si) % 3) * 3 + (c + sp) % 3];
+        // geometry rotation (body -> geometry) O P_i^T: O'_rc = O_r(c+si)
+        for (int r = 0; r < 3; r++)
+            for (int c = 0; c < 3; c++)
+                o.geom_origin_rot[r * 3 + c] = b.geom_origin_rot[r * 3 + (c + si) % 3];
+    }
+    return out;
+}
+
 // `tmem_budget` > 0: place the records of tmem_kind bodies in Tensor Memory
 // columns (8 words per record in f32, 16 in f64) while they fit the budget;
 // their s_xj / s_vw slots are then not allocated in shared memory.
@@ -126,10 +177,12 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
     PdT<T>* pd = reinterpret_cast<PdT<T>*>(blob.data() + info.off_pd);
     int* pdmap = reinterpret_cast<int*>(blob.data() + info.off_pdmap);
 
+    std::vector<int> shift;
+    const std::vector<phyzb_body> rb = relabel_frames(m, shift);
     int next = 2 * nv;  // q, v
     int off = 0;
     for (int i = 0; i < nb; i++) {
-        const phyzb_body& b = m->bodies[i];
+        const phyzb_body& b = rb[i];
         BodyT<T>& t = bt[i];
         BodyI& d = bi[i];
         const int nd = ndof_of(b.joint_type);
@@ -206,6 +259,11 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
                 for (int q = 0; q < 3; q++) unit = unit && (b.axis[q] == (q == k ? 1.0 : 0.0));
                 if (unit) d.axis_k = k;
             }
+        d.qshift = 0;
+        if (tmem_kind(m->bodies[i])) {
+            flags |= F_ZHINGE;
+            d.qshift = (shift[i] - (b.parent >= 0 ? shift[b.parent] : 0) + 3) % 3;
+        }
         if (i + 1 < nb && m->bodies[i + 1].parent == i) flags |= F_CHAIN;
         for (int j = i + 2; j < nb; j++)
             if (m->bodies[j].parent == i) flags |= F_BRANCH;
@@ -215,7 +273,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         // scratch layout of this body
         const int rec_cols = 8 * (int)(sizeof(T) / 4);
         d.t_rec = -1;
-        if (tmem_budget > 0 && tmem_kind(b) && info.tmem_cols + rec_cols <= tmem_budget) {
+        if (tmem_budget > 0 && (flags & F_ZHINGE) && info.tmem_cols + rec_cols <= tmem_budget) {
             d.t_rec = info.tmem_cols;
             info.tmem_cols += rec_cols;
             d.s_xj = d.s_vw = -1;
@@ -261,6 +319,8 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
     for (int i = 0; i < nb; i++)
         if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;
     if (cfg.contact) info.feat |= 2;
+    for (int i = 0; i < nb; i++)
+        if ((bi[i].flags & F_ZHINGE) && bi[i].qshift != 0) info.feat |= 4;
     return info;
 }
 

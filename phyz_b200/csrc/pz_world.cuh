@@ -32,7 +32,9 @@ namespace pz {
 
 // Compile-time feature mask of a kernel variant: a model without ball/free
 // joints (resp. without contact) gets a kernel without that code at all.
-enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2 };
+// Kernel feature bits: ball/free joints present, ground contact on, some
+// hinge frame relabelled by a non-identity cyclic permutation.
+enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4 };
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
@@ -148,12 +150,67 @@ struct JX {
     V3<T> r;  // translation (prismatic, free)
 };
 
-// Body kinds. AX >= 0: a revolute joint about exactly +e_AX whose
-// parent->joint frame is unrotated -- every transform of it is a planar
-// rotation (plus the joint offset) known at compile time. AX = -1: any
-// joint, decoded at run time.
-PZ_HD int body_kind(const BodyI& bi) {
-    return (bi.jtype == J_REVOLUTE && bi.axis_k >= 0 && !(bi.flags & F_PTJ_ROT)) ? bi.axis_k : -1;
+// Body kinds. AX = 2: a hinge about z of its relabelled frame (F_ZHINGE):
+// its transform is the joint offset, the cyclic relabelling qshift and a
+// planar rotation about z, with the rotation known at compile time. AX = -1:
+// any joint, decoded at run time.
+PZ_HD int body_kind(const BodyI& bi) { return (bi.flags & F_ZHINGE) ? 2 : -1; }
+
+// Cyclic relabelling Q = P_q of the parent's coordinates into the child's:
+// (Q v)_a = v_(a+q mod 3), and Q^T = P_(3-q). q is the same for every world
+// (a model constant), so the branches below never diverge.
+template <int Q, class T>
+PZ_HD V3<T> cperm(const V3<T>& v) {
+    if constexpr (Q == 1)
+        return mk3<T>(v.y, v.z, v.x);
+    else if constexpr (Q == 2)
+        return mk3<T>(v.z, v.x, v.y);
+    else
+        return v;
+}
+template <int FEAT, class T>
+PZ_HD V3<T> cperm_v(int q, const V3<T>& v) {
+    if constexpr ((FEAT & FEAT_PERM) == 0) return v;
+    return q == 1 ? cperm<1>(v) : (q == 2 ? cperm<2>(v) : v);
+}
+template <int FEAT, class T>
+PZ_HD SV<T> cperm_sv(int q, const SV<T>& m) {  // Q m
+    if constexpr ((FEAT & FEAT_PERM) == 0) return m;
+    if (q == 1) return mksv<T>(cperm<1>(m.w), cperm<1>(m.l));
+    if (q == 2) return mksv<T>(cperm<2>(m.w), cperm<2>(m.l));
+    return m;
+}
+template <int FEAT, class T>
+PZ_HD SV<T> cperm_t_sv(int q, const SV<T>& f) {  // Q^T f
+    if constexpr ((FEAT & FEAT_PERM) == 0) return f;
+    if (q == 1) return mksv<T>(cperm<2>(f.w), cperm<2>(f.l));
+    if (q == 2) return mksv<T>(cperm<1>(f.w), cperm<1>(f.l));
+    return f;
+}
+// E^T B E with E = P_Q on each 3x3 block: B'_bd = B_(b-Q)(d-Q)
+template <int Q, class T>
+PZ_HD void ai_cperm_fixed(AI<T>& I) {
+    constexpr int m = (3 - Q) % 3;
+    AI<T> o;
+#pragma unroll
+    for (int b = 0; b < 3; b++)
+#pragma unroll
+        for (int d = 0; d < 3; d++) {
+            o.h[b * 3 + d] = I.h[((b + m) % 3) * 3 + (d + m) % 3];
+            if (b <= d) {
+                o.a[sidx(b, d)] = I.a[sidx((b + m) % 3, (d + m) % 3)];
+                o.m[sidx(b, d)] = I.m[sidx((b + m) % 3, (d + m) % 3)];
+            }
+        }
+    I = o;
+}
+template <int FEAT, class T>
+PZ_HD void ai_cperm_t(int q, AI<T>& I) {
+    if constexpr ((FEAT & FEAT_PERM) == 0) return;
+    if (q == 1)
+        ai_cperm_fixed<1>(I);
+    else if (q == 2)
+        ai_cperm_fixed<2>(I);
 }
 
 // a x (s e_K), with the structurally zero component exact
@@ -255,7 +312,7 @@ PZ_HD V3<T> hrot_t(int k, const T& c, const T& s, const V3<T>& x) {
 // The rotation part of X_tree = X_J X_ptj applied to a 3-vector: R_J R_ptj x.
 template <int AX, int FEAT, class T>
 PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> x) {
-    if constexpr (AX >= 0) return prot<AX>(j.c, j.s, x);
+    if constexpr (AX >= 0) return prot<AX>(j.c, j.s, cperm_v<FEAT>(bi.qshift, x));
     if (bi.flags & F_PTJ_ROT) x = m3v(bt.ptj_rot, x);
     switch (bi.jtype) {
         case J_REVOLUTE: x = bi.axis_k >= 0 ? hrot(bi.axis_k, j.c, j.s, x) : rmul(j.E, x); break;
@@ -283,6 +340,7 @@ template <int AX, int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
     if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
     if constexpr (AX >= 0) {
+        m = cperm_sv<FEAT>(bi.qshift, m);
         return mksv<T>(prot<AX>(j.c, j.s, m.w), prot<AX>(j.c, j.s, m.l));
     } else {
         if (bi.flags & F_PTJ_ROT) {
@@ -313,7 +371,7 @@ PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) 
 template <int AX, int FEAT, class T>
 PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f) {
     if constexpr (AX >= 0) {
-        f = mksv<T>(prot_t<AX>(j.c, j.s, f.w), prot_t<AX>(j.c, j.s, f.l));
+        f = cperm_t_sv<FEAT>(bi.qshift, mksv<T>(prot_t<AX>(j.c, j.s, f.w), prot_t<AX>(j.c, j.s, f.l)));
     } else {
         switch (bi.jtype) {
             case J_REVOLUTE:
@@ -345,6 +403,7 @@ template <int AX, int FEAT, class T>
 PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I) {
     if constexpr (AX >= 0) {
         ai_prot<AX>(j.c, j.s, I);
+        ai_cperm_t<FEAT>(bi.qshift, I);
     } else {
         switch (bi.jtype) {
             case J_REVOLUTE:
@@ -903,12 +962,11 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
 }
 
 // Run f<AX>() for the body's kind.
-#define PZ_BY_KIND(kind, CALL)      \
-    switch (kind) {                 \
-        case 0: CALL(0); break;     \
-        case 1: CALL(1); break;     \
-        case 2: CALL(2); break;     \
-        default: CALL(-1); break;   \
+#define PZ_BY_KIND(kind, CALL) \
+    if ((kind) == 2) {         \
+        CALL(2);               \
+    } else {                   \
+        CALL(-1);              \
     }
 
 // ── pass 2 of body i (aba.rs:215-320). I, pA carry the child's contribution

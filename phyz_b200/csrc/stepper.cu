@@ -1,325 +1,14 @@
-// Kernels of the B200 batched rigid-body stepper (sm_100a).
+// Host dispatch of the stepper's kernels and the layout-conversion kernels.
 //
-// rollout_kernel runs phyz-gpu's whole step sequence (cuda/mod.rs:879-945:
-// PD -> contact -> ABA -> integrate) for `nsteps` steps in ONE launch: one
-// thread per world, the model table staged once per block into shared
-// memory, and each world's q, v and every per-body intermediate of the
-// articulated-body algorithm held in shared memory (structure-of-arrays,
-// conflict-free) for the whole rollout. Global memory sees the initial state
-// read, one coalesced control row per step (prefetched a sweep ahead with
-// cp.async), and the final state / accelerations / contact state written.
-//
-// The reference runs the same physics as 3-4 launches per step with every
-// intermediate in thread-local arrays (phyz_kernels.cu:1175-1369: 255
-// registers and 9.6 KB of spilled stack per thread on sm_100a).
+// The rollout and objective kernels (stepper_kernels.cuh) are compiled per
+// (precision, feature set) in rollout_variants.cu; this file picks the
+// variant of a model at run time and owns the device limits the launch
+// configuration is sized by.
 #include <cuda_runtime.h>
 
-#include <cstdint>
-#include <cmath>
-#include <cstdlib>
-#include <algorithm>
-#include <type_traits>
-
-#include "pz_launch.h"
-#include "pz_world.cuh"
+#include "pz_variants.h"
 
 namespace pz {
-
-// Per-thread view of the shared-memory scratch: slot s of this world lives
-// at base[s * W] (consecutive threads -> consecutive banks).
-template <class T>
-struct SmemScr {
-    T* base;
-    int W;
-    __device__ __forceinline__ T& operator()(int s) const { return base[s * W]; }
-    __device__ __forceinline__ void prefetch(int s, const T* g) const {
-        const unsigned sa = (unsigned)__cvta_generic_to_shared(&base[s * W]);
-        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(sa), "l"(g), "n"(sizeof(T)));
-    }
-    __device__ __forceinline__ void commit() const { asm volatile("cp.async.commit_group;\n" ::); }
-    __device__ __forceinline__ void wait() const { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-    __device__ __forceinline__ void fence_st() const {}
-    __device__ __forceinline__ Rec<T> rec_get(const BodyI& bi) const {
-        Rec<T> r;
-        r.c = (*this)(bi.s_xj);
-        r.s = (*this)(bi.s_xj + 1);
-        r.v = ld_sv<T>(*this, bi.s_vw);
-        return r;
-    }
-    __device__ __forceinline__ void rec_put(const BodyI& bi, const Rec<T>& r) const {
-        (*this)(bi.s_xj) = r.c;
-        (*this)(bi.s_xj + 1) = r.s;
-        st_sv(*this, bi.s_vw, r.v);
-    }
-    __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const { st_sv(*this, bi.s_vw, v); }
-};
-
-// Tensor Memory scratch for body records: each thread owns the TMEM lane of
-// its position in its warp (the warp's lane quarter is warp % 4) and a range
-// of columns; a record [c, s, v0..v5] is 8 consecutive 32-bit columns (16 in
-// f64) moved with one tcgen05.ld / tcgen05.st of shape 32x32b. Bodies whose
-// t_rec < 0 keep their record in shared memory. All record accesses are
-// warp-uniform (every thread of a warp processes the same body).
-template <class T>
-struct TmemScr : SmemScr<T> {
-    unsigned tbase;  // (lane quarter << 16) | this warp's first column
-    __device__ __forceinline__ Rec<T> rec_get(const BodyI& bi) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_get(bi);
-        const unsigned a = tbase + (unsigned)bi.t_rec;
-        Rec<T> r;
-        if constexpr (sizeof(T) == 4) {
-            unsigned x0, x1, x2, x3, x4, x5, x6, x7;
-            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
-                         : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3), "=r"(x4), "=r"(x5), "=r"(x6), "=r"(x7)
-                         : "r"(a));
-            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
-                         : "+r"(x0), "+r"(x1), "+r"(x2), "+r"(x3), "+r"(x4), "+r"(x5), "+r"(x6), "+r"(x7)::"memory");
-            r.c = __uint_as_float(x0);
-            r.s = __uint_as_float(x1);
-            r.v = mksv<T>(mk3<T>(__uint_as_float(x2), __uint_as_float(x3), __uint_as_float(x4)),
-                          mk3<T>(__uint_as_float(x5), __uint_as_float(x6), __uint_as_float(x7)));
-        } else {
-            unsigned x[16];
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-                "%14, %15}, [%16];\n"
-                : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
-                  "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15])
-                : "r"(a));
-            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
-                         : "+r"(x[0]), "+r"(x[1]), "+r"(x[2]), "+r"(x[3]), "+r"(x[4]), "+r"(x[5]), "+r"(x[6]),
-                           "+r"(x[7]), "+r"(x[8]), "+r"(x[9]), "+r"(x[10]), "+r"(x[11]), "+r"(x[12]), "+r"(x[13]),
-                           "+r"(x[14]), "+r"(x[15])::"memory");
-            T d[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) d[k] = T(__hiloint2double((int)x[2 * k + 1], (int)x[2 * k]));
-            r.c = d[0];
-            r.s = d[1];
-            r.v = mksv<T>(mk3<T>(d[2], d[3], d[4]), mk3<T>(d[5], d[6], d[7]));
-        }
-        return r;
-    }
-    __device__ __forceinline__ void put_words(unsigned a, const T* d, int n) const {
-        // n = 8 (whole record) or 6 (columns 2..7: v / W only)
-        if constexpr (sizeof(T) == 4) {
-            unsigned x[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++) x[k] = __float_as_uint(d[k]);
-            if (n == 8)
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(a),
-                             "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
-                             : "memory");
-            else {
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};\n" ::"r"(a + 2u), "r"(x[2]),
-                             "r"(x[3])
-                             : "memory");
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(a + 4u),
-                             "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
-                             : "memory");
-            }
-        } else {
-            unsigned x[16];
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                x[2 * k] = (unsigned)__double2loint((double)d[k]);
-                x[2 * k + 1] = (unsigned)__double2hiint((double)d[k]);
-            }
-            if (n == 8)
-                asm volatile(
-                    "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
-                    "%13, %14, %15, %16};\n" ::"r"(a),
-                    "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7]), "r"(x[8]),
-                    "r"(x[9]), "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]), "r"(x[15])
-                    : "memory");
-            else {
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(a + 4u),
-                             "r"(x[4]), "r"(x[5]), "r"(x[6]), "r"(x[7])
-                             : "memory");
-                asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"r"(
-                                 a + 8u),
-                             "r"(x[8]), "r"(x[9]), "r"(x[10]), "r"(x[11]), "r"(x[12]), "r"(x[13]), "r"(x[14]),
-                             "r"(x[15])
-                             : "memory");
-            }
-        }
-    }
-    __device__ __forceinline__ void rec_put(const BodyI& bi, const Rec<T>& r) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_put(bi, r);
-        const T d[8] = {r.c, r.s, r.v.w.x, r.v.w.y, r.v.w.z, r.v.l.x, r.v.l.y, r.v.l.z};
-        put_words(tbase + (unsigned)bi.t_rec, d, 8);
-    }
-    __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_put_vw(bi, v);
-        const T d[8] = {T(0), T(0), v.w.x, v.w.y, v.w.z, v.l.x, v.l.y, v.l.z};
-        put_words(tbase + (unsigned)bi.t_rec, d, 6);
-    }
-    // stores complete before later loads of the same columns
-    __device__ __forceinline__ void fence_st() const { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
-};
-
-template <class T>
-__device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const unsigned char* blob) {
-    ModelView<T> M;
-    M.bt = reinterpret_cast<const BodyT<T>*>(blob);
-    M.bi = reinterpret_cast<const BodyI*>(blob + P.off_bi);
-    M.pd = reinterpret_cast<const PdT<T>*>(blob + P.off_pd);
-    M.pd_of_dof = reinterpret_cast<const int*>(blob + P.off_pdmap);
-    M.nb = P.nb;
-    M.nv = P.nv;
-    M.npd = P.npd;
-    M.contact = P.contact;
-    M.dt = T(P.dt);
-    M.gx = T(P.gx);
-    M.gy = T(P.gy);
-    M.gz = T(P.gz);
-    M.ground_h = T(P.ground_h);
-    M.friction = T(P.friction);
-    const double dtc = P.dt > 1e-9 ? P.dt : 1e-9;
-    M.inv_dt_c = T(1.0 / dtc);
-    M.kstiff_c = T(4.0 / (dtc * dtc));
-    return M;
-}
-
-// Copy the model table into shared memory (16-byte chunks) and return its
-// shared-memory address. All threads of the block take part.
-__device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, unsigned char* smem) {
-    const int4* src = reinterpret_cast<const int4*>(g);
-    int4* dst = reinterpret_cast<int4*>(smem);
-    for (int k = threadIdx.x; k < bytes / 16; k += blockDim.x) dst[k] = __ldg(src + k);
-    __syncthreads();
-    return smem;
-}
-
-// TMEM columns allocated per block by the Tensor-Memory variant: the whole
-// array (one block per SM).
-constexpr unsigned TMEM_COLS = 512;
-
-template <class T, int FEAT, bool TM>
-__global__ void __launch_bounds__(256) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ unsigned tmem_slot;
-    const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
-    const ModelView<T> M = make_view<T>(P, blob);
-    const int W = blockDim.x;
-    using Scr = typename std::conditional<TM, TmemScr<T>, SmemScr<T>>::type;
-    Scr S;
-    S.base = reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x;
-    S.W = W;
-    const int warp = threadIdx.x >> 5;
-    if constexpr (TM) {
-        if (warp == 0) {
-            const unsigned dst = (unsigned)__cvta_generic_to_shared(&tmem_slot);
-            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(dst),
-                         "r"(TMEM_COLS));
-            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
-        }
-        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-        __syncthreads();
-        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        // warps w, w+4, w+8, ... share lane quarter w % 4 and split its columns
-        const int nwarps = (W + 31) >> 5;
-        const unsigned per_quarter = (unsigned)((nwarps + 3) >> 2);
-        const unsigned cols = TMEM_COLS / per_quarter;
-        S.tbase = tmem_slot + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(warp >> 2) * cols;
-    }
-    const long long ntiles = (P.nworld + W - 1) / W;
-    const long long N = P.nworld;
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long wt = tile * W + threadIdx.x;
-        // lanes past the last world run world N-1 again and write nothing, so
-        // every warp stays converged for the warp-wide tcgen05 operations
-        const bool active = wt < N;
-        const long long w = active ? wt : N - 1;
-        for (int j = 0; j < M.nv; j++) {
-            S(j) = P.q[j * N + w];
-            S(M.nv + j) = P.v[j * N + w];
-        }
-        const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
-        for (int i = 0; i < M.nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
-        S.commit();
-        const Out<T> none{nullptr, 0};
-        pass1_all<FEAT>(M, S);
-        for (int s = 0; s < P.nsteps; s++) {
-            S.wait();
-            const bool last = s == P.nsteps - 1;
-            if constexpr ((FEAT & FEAT_CONTACT) != 0) {
-                // contact state of the last step, from the state it starts from
-                // (every lane runs it, warp-wide record loads; only active lanes write)
-                if (last && P.contact && P.cstate)
-                    contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
-            }
-            pass2<FEAT>(M, S);
-            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, (last && active) ? Out<T>{P.qdd + w, N} : none);
-            S.commit();
-        }
-        S.wait();
-        if (active) {
-            bool finite = true;
-            for (int j = 0; j < M.nv; j++) {
-                const T qj = S(j), vj = S(M.nv + j);
-                finite = finite && pz_finite(qj) && pz_finite(vj);
-                P.q[j * N + w] = qj;
-                P.v[j * N + w] = vj;
-            }
-            if (!finite) {
-                atomicOr(P.status, 1);
-                atomicMin(P.status + 1, (int)(w < 0x7fffffff ? w : 0x7fffffff));
-            }
-        }
-    }
-    if constexpr (TM) {
-        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-        __syncthreads();
-        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        if (warp == 0)
-            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_slot), "r"(TMEM_COLS));
-    }
-}
-
-// Kinetic energy 0.5 sum_i v_i^T I_i v_i + 0.5 sum_j armature_j qd_j^2
-// (crates/phyz-rigid/src/energy.rs:8-11 with crba's armature) or sum q^2,
-// reduced over the block and added into *out.
-template <class T, int FEAT>
-__global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ RolloutArgs<T> P, int kind,
-                                                         T* out) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
-    ModelView<T> M = make_view<T>(P, blob);
-    M.contact = 0;
-    const int W = blockDim.x;
-    const SmemScr<T> S{reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x, W};
-    const long long ntiles = (P.nworld + W - 1) / W;
-    T acc = T(0);
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long w = tile * W + threadIdx.x;
-        if (w >= P.nworld) continue;
-        const long long N = P.nworld;
-        for (int j = 0; j < M.nv; j++) {
-            S(j) = P.q[j * N + w];
-            S(M.nv + j) = P.v[j * N + w];
-        }
-        if (kind == 1) {
-            for (int j = 0; j < M.nv; j++) acc += S(j) * S(j);
-            continue;
-        }
-        pass1_all<FEAT & FEAT_MULTI>(M, S);
-        for (int i = 0; i < M.nb; i++) {
-            const BodyI bi = M.bi[i];
-            const BodyT<T>& bt = M.bt[i];
-            const SV<T> v = ld_sv<T>(S, bi.s_vw);
-            const V3<T> mc = ld3(bt.mcom);
-            const SV<T> h = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
-            acc += T(0.5) * dot(v, h);
-            for (int k = 0; k < bi.ndof; k++) {
-                const T qd = S(M.nv + bi.off + k);
-                acc += T(0.5) * bt.armature * qd * qd;
-            }
-        }
-    }
-    // warp reduction, one atomic per warp (blockDim.x is a multiple of 32)
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-    if ((threadIdx.x & 31) == 0) atomicAdd(out, acc);
-}
 
 // aos [nrep][nworld][width] (Tin) -> soa [nrep][width][nworld] (Tout), 32x32 tiles.
 template <class Tin, class Tout>
@@ -365,16 +54,17 @@ __global__ void soa_to_aos_kernel(const Tin* __restrict__ soa, Tout* __restrict_
 
 // ── launch helpers ───────────────────────────────────────────────────────
 
-static int g_sm_count = -1, g_smem_optin = -1, g_device = -1;
+static int g_device = -1;
+static DeviceLimits g_limits{0, 0};
 
 static cudaError_t device_limits() {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev != g_device) {
-        if ((e = cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+        if ((e = cudaDeviceGetAttribute(&g_limits.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
             return e;
-        if ((e = cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) !=
+        if ((e = cudaDeviceGetAttribute(&g_limits.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) !=
             cudaSuccess)
             return e;
         g_device = dev;
@@ -382,79 +72,40 @@ static cudaError_t device_limits() {
     return cudaSuccess;
 }
 
-template <class T, int FEAT, bool TM>
-static cudaError_t config_variant(int scratch, int model_bytes, long long nworld, int tmem_cols, LaunchCfg* out) {
-    // the opt-in limit covers static and dynamic shared memory together
-    cudaFuncAttributes fa{};
-    cudaError_t e = cudaFuncGetAttributes(&fa, rollout_kernel<T, FEAT, TM>);
-    if (e != cudaSuccess) return e;
-    const int dyn_cap = g_smem_optin - (int)fa.sharedSizeBytes;
-    e = cudaFuncSetAttribute(rollout_kernel<T, FEAT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_cap);
-    if (e != cudaSuccess) return e;
-    if (!TM) {
-        e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 g_smem_optin);
-        if (e != cudaSuccess) return e;
+// run-time feature set -> compiled variant
+template <class T, bool TM, int F = 0>
+static cudaError_t config_by_feat(int feat, int scratch, int model_bytes, long long nworld, int tmem_cols,
+                                  LaunchCfg* out) {
+    if constexpr (F < FEAT_COUNT) {
+        if (feat == F) return config_variant<T, F, TM>(g_limits, scratch, model_bytes, nworld, tmem_cols, out);
+        return config_by_feat<T, TM, F + 1>(feat, scratch, model_bytes, nworld, tmem_cols, out);
+    } else {
+        return cudaErrorInvalidValue;
     }
-    const long long per_world = (long long)scratch * (long long)sizeof(T);
-    // Pick the block width that keeps the most worlds resident per SM,
-    // discounted by how full the last wave of tiles is. Shared-memory layout:
-    // any even width up to the 256 of __launch_bounds__. Tensor-Memory layout:
-    // whole warps, one block per SM, and few enough warps per TMEM lane
-    // quarter that each thread's columns hold its records.
-    // PHYZB_WORLDS_PER_BLOCK overrides the width for tuning.
-    int forced = 0;
-    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
-    int best_w = 0, best_blocks = 0, best_smem = 0;
-    double best_score = -1.0;
-    const int step = TM ? 32 : 2;
-    for (int W = 32; W <= 256; W += step) {
-        if (forced > 0 && W != forced) continue;
-        if (TM) {
-            const int per_quarter = ((W + 31) / 32 + 3) / 4;
-            if (tmem_cols * per_quarter > (int)TMEM_COLS) break;
-        }
-        long long smem = (long long)model_bytes + per_world * W;
-        if (smem > dyn_cap) break;
-        // Tensor-Memory blocks ask for more than half an SM's shared memory so
-        // that no second block lands on the SM and waits on the allocation
-        if (TM) smem = std::max(smem, (long long)(g_smem_optin / 2 + 16) & ~15LL);
-        int blocks = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT, TM>, W, (size_t)smem);
-        if (e != cudaSuccess) return e;
-        if (blocks <= 0) continue;
-        if (TM) blocks = 1;  // each block holds the whole Tensor Memory
-        const double resident = (double)blocks * W * g_sm_count;  // worlds in flight on the GPU
-        const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
-        const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
-        const double score = (double)blocks * W * used;
-        if (score > best_score * 1.0001) {
-            best_score = score;
-            best_w = W;
-            best_blocks = blocks;
-            best_smem = (int)smem;
-        }
-    }
-    if (best_w == 0) return cudaErrorInvalidConfiguration;
-    const long long ntiles = (nworld + best_w - 1) / best_w;
-    const long long cap = (long long)g_sm_count * best_blocks;
-    out->W = best_w;
-    out->grid = (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
-    out->smem = best_smem;
-    out->tm = TM ? 1 : 0;
-    out->score = best_score;
-    return cudaSuccess;
 }
-
-template <class T, bool TM>
-static cudaError_t config_dispatch(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols,
-                                   LaunchCfg* out) {
-    switch (feat) {
-        case 0: return config_variant<T, 0, TM>(scratch, model_bytes, nworld, tmem_cols, out);
-        case FEAT_MULTI: return config_variant<T, FEAT_MULTI, TM>(scratch, model_bytes, nworld, tmem_cols, out);
-        case FEAT_CONTACT: return config_variant<T, FEAT_CONTACT, TM>(scratch, model_bytes, nworld, tmem_cols, out);
-        default:
-            return config_variant<T, FEAT_MULTI | FEAT_CONTACT, TM>(scratch, model_bytes, nworld, tmem_cols, out);
+template <class T, bool TM, int F = 0>
+static cudaError_t launch_by_feat(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
+    if constexpr (F < FEAT_COUNT) {
+        if (a.feat == F) {
+            launch_variant<T, F, TM>(a, cfg, s);
+            return cudaSuccess;
+        }
+        return launch_by_feat<T, TM, F + 1>(a, cfg, s);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+}
+template <class T, int F = 0>
+static cudaError_t objective_by_feat(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out,
+                                     cudaStream_t s) {
+    if constexpr (F < FEAT_COUNT) {
+        if (a.feat == F) {
+            launch_objective_variant<T, F>(a, cfg, kind, out, s);
+            return cudaSuccess;
+        }
+        return objective_by_feat<T, F + 1>(a, cfg, kind, out, s);
+    } else {
+        return cudaErrorInvalidValue;
     }
 }
 
@@ -462,41 +113,23 @@ template <class T>
 cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols, LaunchCfg* out) {
     cudaError_t e = device_limits();
     if (e != cudaSuccess) return e;
-    if (tmem_cols > 0) return config_dispatch<T, true>(scratch, model_bytes, nworld, feat, tmem_cols, out);
-    return config_dispatch<T, false>(scratch, model_bytes, nworld, feat, 0, out);
-}
-
-template <class T, bool TM>
-static void launch_variant(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
-    switch (a.feat) {
-        case 0: rollout_kernel<T, 0, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        case FEAT_MULTI: rollout_kernel<T, FEAT_MULTI, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        case FEAT_CONTACT: rollout_kernel<T, FEAT_CONTACT, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-        default: rollout_kernel<T, FEAT_MULTI | FEAT_CONTACT, TM><<<cfg.grid, cfg.W, cfg.smem, s>>>(a); break;
-    }
+    if (tmem_cols > 0) return config_by_feat<T, true>(feat, scratch, model_bytes, nworld, tmem_cols, out);
+    return config_by_feat<T, false>(feat, scratch, model_bytes, nworld, 0, out);
 }
 
 template <class T>
 cudaError_t launch_rollout(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
     if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
-    if (cfg.tm)
-        launch_variant<T, true>(a, cfg, s);
-    else
-        launch_variant<T, false>(a, cfg, s);
+    cudaError_t e = cfg.tm ? launch_by_feat<T, true>(a, cfg, s) : launch_by_feat<T, false>(a, cfg, s);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
 template <class T>
 cudaError_t launch_objective(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out, cudaStream_t s) {
     if (a.nworld <= 0) return cudaSuccess;
-    switch (a.feat) {
-        case 0: objective_kernel<T, 0><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
-        case FEAT_MULTI: objective_kernel<T, FEAT_MULTI><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
-        case FEAT_CONTACT: objective_kernel<T, FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out); break;
-        default:
-            objective_kernel<T, FEAT_MULTI | FEAT_CONTACT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out);
-            break;
-    }
+    cudaError_t e = objective_by_feat<T>(a, cfg, kind, out, s);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 
