@@ -154,9 +154,10 @@ inline std::vector<phyzb_body> relabel_frames(const phyzb_model* m, std::vector<
     return out;
 }
 
-// `tmem_budget` > 0: place the records of tmem_kind bodies in Tensor Memory
-// columns (8 words per record in f32, 16 in f64) while they fit the budget;
-// their s_xj / s_vw slots are then not allocated in shared memory.
+// `tmem_budget` > 0: place the records of all tmem_kind bodies in Tensor
+// Memory columns (8 words per record in f32, 16 in f64) if they all fit the
+// budget (else none: info.tmem_cols = 0); their s_xj / s_vw slots are then
+// not allocated in shared memory.
 template <class T>
 inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std::vector<unsigned char>& blob,
                            int tmem_budget = 0) {
@@ -179,6 +180,14 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
 
     std::vector<int> shift;
     const std::vector<phyzb_body> rb = relabel_frames(m, shift);
+    // a Tensor-Memory layout holds the records of every relabelled hinge
+    // (the kernel then accesses them without a per-body test) or none
+    {
+        int need = 0;
+        for (int i = 0; i < nb; i++)
+            if (tmem_kind(m->bodies[i])) need += 8 * (int)(sizeof(T) / 4);
+        if (need > tmem_budget) tmem_budget = 0;
+    }
     int next = 2 * nv;  // q, v
     int off = 0;
     for (int i = 0; i < nb; i++) {

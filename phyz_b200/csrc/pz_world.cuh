@@ -168,25 +168,6 @@ PZ_HD V3<T> cperm(const V3<T>& v) {
     else
         return v;
 }
-template <int FEAT, class T>
-PZ_HD V3<T> cperm_v(int q, const V3<T>& v) {
-    if constexpr ((FEAT & FEAT_PERM) == 0) return v;
-    return q == 1 ? cperm<1>(v) : (q == 2 ? cperm<2>(v) : v);
-}
-template <int FEAT, class T>
-PZ_HD SV<T> cperm_sv(int q, const SV<T>& m) {  // Q m
-    if constexpr ((FEAT & FEAT_PERM) == 0) return m;
-    if (q == 1) return mksv<T>(cperm<1>(m.w), cperm<1>(m.l));
-    if (q == 2) return mksv<T>(cperm<2>(m.w), cperm<2>(m.l));
-    return m;
-}
-template <int FEAT, class T>
-PZ_HD SV<T> cperm_t_sv(int q, const SV<T>& f) {  // Q^T f
-    if constexpr ((FEAT & FEAT_PERM) == 0) return f;
-    if (q == 1) return mksv<T>(cperm<2>(f.w), cperm<2>(f.l));
-    if (q == 2) return mksv<T>(cperm<1>(f.w), cperm<1>(f.l));
-    return f;
-}
 // E^T B E with E = P_Q on each 3x3 block: B'_bd = B_(b-Q)(d-Q)
 template <int Q, class T>
 PZ_HD void ai_cperm_fixed(AI<T>& I) {
@@ -204,13 +185,50 @@ PZ_HD void ai_cperm_fixed(AI<T>& I) {
         }
     I = o;
 }
-template <int FEAT, class T>
-PZ_HD void ai_cperm_t(int q, AI<T>& I) {
-    if constexpr ((FEAT & FEAT_PERM) == 0) return;
-    if (q == 1)
-        ai_cperm_fixed<1>(I);
-    else if (q == 2)
-        ai_cperm_fixed<2>(I);
+
+// The relabelling folded into the planar rotation about e_AX that follows
+// (motion: R Q m) or precedes (force: Q^T R^T f; inertia: Q^T R^T I R Q) it:
+// one branch per shift, so each branch writes the rotated values straight
+// into the permuted slots instead of moving registers after the fact.
+template <int AX, int FEAT, class T>
+PZ_HD V3<T> rot_fwd3(int q, const T& c, const T& s, const V3<T>& x) {
+    if constexpr ((FEAT & FEAT_PERM) != 0) {
+        if (q == 1) return prot<AX>(c, s, cperm<1>(x));
+        if (q == 2) return prot<AX>(c, s, cperm<2>(x));
+    }
+    return prot<AX>(c, s, x);
+}
+template <int AX, int FEAT, class T>
+PZ_HD SV<T> rot_fwd(int q, const T& c, const T& s, const SV<T>& m) {
+    if constexpr ((FEAT & FEAT_PERM) != 0) {
+        if (q == 1) return mksv<T>(prot<AX>(c, s, cperm<1>(m.w)), prot<AX>(c, s, cperm<1>(m.l)));
+        if (q == 2) return mksv<T>(prot<AX>(c, s, cperm<2>(m.w)), prot<AX>(c, s, cperm<2>(m.l)));
+    }
+    return mksv<T>(prot<AX>(c, s, m.w), prot<AX>(c, s, m.l));
+}
+template <int AX, int FEAT, class T>
+PZ_HD SV<T> rot_bwd(int q, const T& c, const T& s, const SV<T>& f) {
+    if constexpr ((FEAT & FEAT_PERM) != 0) {
+        if (q == 1) return mksv<T>(cperm<2>(prot_t<AX>(c, s, f.w)), cperm<2>(prot_t<AX>(c, s, f.l)));
+        if (q == 2) return mksv<T>(cperm<1>(prot_t<AX>(c, s, f.w)), cperm<1>(prot_t<AX>(c, s, f.l)));
+    }
+    return mksv<T>(prot_t<AX>(c, s, f.w), prot_t<AX>(c, s, f.l));
+}
+template <int AX, int FEAT, class T>
+PZ_HD void ai_rot_bwd(int q, const T& c, const T& s, AI<T>& I) {
+    if constexpr ((FEAT & FEAT_PERM) != 0) {
+        if (q == 1) {
+            ai_prot<AX>(c, s, I);
+            ai_cperm_fixed<1>(I);
+            return;
+        }
+        if (q == 2) {
+            ai_prot<AX>(c, s, I);
+            ai_cperm_fixed<2>(I);
+            return;
+        }
+    }
+    ai_prot<AX>(c, s, I);
 }
 
 // a x (s e_K), with the structurally zero component exact
@@ -312,7 +330,7 @@ PZ_HD V3<T> hrot_t(int k, const T& c, const T& s, const V3<T>& x) {
 // The rotation part of X_tree = X_J X_ptj applied to a 3-vector: R_J R_ptj x.
 template <int AX, int FEAT, class T>
 PZ_HD V3<T> tree_rot(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, V3<T> x) {
-    if constexpr (AX >= 0) return prot<AX>(j.c, j.s, cperm_v<FEAT>(bi.qshift, x));
+    if constexpr (AX >= 0) return rot_fwd3<AX, FEAT>(bi.qshift, j.c, j.s, x);
     if (bi.flags & F_PTJ_ROT) x = m3v(bt.ptj_rot, x);
     switch (bi.jtype) {
         case J_REVOLUTE: x = bi.axis_k >= 0 ? hrot(bi.axis_k, j.c, j.s, x) : rmul(j.E, x); break;
@@ -340,8 +358,7 @@ template <int AX, int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
     if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
     if constexpr (AX >= 0) {
-        m = cperm_sv<FEAT>(bi.qshift, m);
-        return mksv<T>(prot<AX>(j.c, j.s, m.w), prot<AX>(j.c, j.s, m.l));
+        return rot_fwd<AX, FEAT>(bi.qshift, j.c, j.s, m);
     } else {
         if (bi.flags & F_PTJ_ROT) {
             const R3<T> P = ld9(bt.ptj_rot);
@@ -371,7 +388,7 @@ PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) 
 template <int AX, int FEAT, class T>
 PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f) {
     if constexpr (AX >= 0) {
-        f = cperm_t_sv<FEAT>(bi.qshift, mksv<T>(prot_t<AX>(j.c, j.s, f.w), prot_t<AX>(j.c, j.s, f.l)));
+        f = rot_bwd<AX, FEAT>(bi.qshift, j.c, j.s, f);
     } else {
         switch (bi.jtype) {
             case J_REVOLUTE:
@@ -402,8 +419,7 @@ PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f)
 template <int AX, int FEAT, class T>
 PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I) {
     if constexpr (AX >= 0) {
-        ai_prot<AX>(j.c, j.s, I);
-        ai_cperm_t<FEAT>(bi.qshift, I);
+        ai_rot_bwd<AX, FEAT>(bi.qshift, j.c, j.s, I);
     } else {
         switch (bi.jtype) {
             case J_REVOLUTE:

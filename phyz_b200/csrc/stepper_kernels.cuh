@@ -65,14 +65,15 @@ struct SmemScr {
 // Tensor Memory scratch for body records: each thread owns the TMEM lane of
 // its position in its warp (the warp's lane quarter is warp % 4) and a range
 // of columns; a record [c, s, v0..v5] is 8 consecutive 32-bit columns (16 in
-// f64) moved with one tcgen05.ld / tcgen05.st of shape 32x32b. Bodies whose
-// t_rec < 0 keep their record in shared memory. All record accesses are
-// warp-uniform (every thread of a warp processes the same body).
+// f64) moved with one tcgen05.ld / tcgen05.st of shape 32x32b. In a
+// Tensor-Memory layout every relabelled hinge (the only bodies whose
+// records go through this interface) has its record here (t_rec >= 0). All
+// record accesses are warp-uniform (every thread of a warp processes the
+// same body).
 template <class T>
 struct TmemScr : SmemScr<T> {
     unsigned tbase;  // (lane quarter << 16) | this warp's first column
     __device__ __forceinline__ Rec<T> rec_get(const BodyI& bi) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_get(bi);
         const unsigned a = tbase + (unsigned)bi.t_rec;
         Rec<T> r;
         if constexpr (sizeof(T) == 4) {
@@ -152,12 +153,10 @@ struct TmemScr : SmemScr<T> {
         }
     }
     __device__ __forceinline__ void rec_put(const BodyI& bi, const Rec<T>& r) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_put(bi, r);
         const T d[8] = {r.c, r.s, r.v.w.x, r.v.w.y, r.v.w.z, r.v.l.x, r.v.l.y, r.v.l.z};
         put_words(tbase + (unsigned)bi.t_rec, d, 8);
     }
     __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const {
-        if (bi.t_rec < 0) return SmemScr<T>::rec_put_vw(bi, v);
         const T d[8] = {T(0), T(0), v.w.x, v.w.y, v.w.z, v.l.x, v.l.y, v.l.z};
         put_words(tbase + (unsigned)bi.t_rec, d, 6);
     }
