@@ -230,16 +230,17 @@ def run_reference_impl(args, world, rank):
 # ── our arm ────────────────────────────────────────────────────────────────
 def main():
     args = parse()
-    world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        run_reference_impl(args, world, rank)
-        finish(world)
+        # CPU only: no process group; rank 0 runs, the other ranks exit 0
+        run_reference_impl(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
+    world, rank, local = dist_setup(args)
 
     import torch
 
     from phyz_b200 import BatchSim, configs
     from phyz_b200 import _lib as L
+    from phyz_b200.parallel import Comm, share_bytes, weak_block
 
     cfg = configs.CONFIGS[args.config]
     model = cfg.builder()
@@ -249,7 +250,7 @@ def main():
     tdt = torch.float32 if prec == "f32" else torch.float64
     esz = 4 if prec == "f32" else 8
     nv = model.nv
-    offset = rank * nworld  # this rank's block of worlds
+    offset, _ = weak_block(nworld, rank)  # this rank's block of worlds
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
     if cfg.contact:
@@ -267,8 +268,12 @@ def main():
     mask = torch.tensor(configs.actuated(model), dtype=tdt, device="cuda").view(1, nv, 1)
     with torch.cuda.stream(stream):
         sched = torch.randn(horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
-        objective = torch.zeros(1, dtype=tdt, device="cuda")
     stream.synchronize()
+    # the end-of-rollout collective: sum of the per-world objective over all
+    # ranks (NCCL through the library; one rank at N=1)
+    comm = Comm(rank, world, local, timeout=120.0,
+                id_channel=(lambda p, r: share_bytes(p, r)) if world > 1 else (lambda p, r: p))
+    objective = [0.0]
 
     def reset_state():
         # every rollout starts from the same seeded state: same work each step
@@ -281,14 +286,7 @@ def main():
         sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
         if ev is not None:
             ev[1].record(stream)
-        with torch.cuda.stream(stream):
-            objective.zero_()
-        sim.objective_device(0, objective.data_ptr())
-        if world > 1:
-            import torch.distributed as dist
-
-            with torch.cuda.stream(stream):
-                dist.all_reduce(objective)
+        objective[0] = comm.reduce_objective(sim, 0)
 
     for _ in range(args.warmup):
         rollout()
@@ -392,9 +390,11 @@ def main():
                        "launch": info},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": args.steps * 2,  # per rollout: rollout_kernel + objective_kernel
-            "objective": float(objective.item()),
+            "objective": objective[0],
+            "objective_reduce": "phyzb_reduce_objective (NCCL all-reduce over all ranks, once per rollout)",
         }
         print(json.dumps(line), flush=True)
+    comm.close()
     sim.close()
     finish(world)
 

@@ -47,6 +47,7 @@ extern "C" {
 #define PHYZB_ERR_NONFINITE (-5)   /* a world's state went non-finite on device */
 #define PHYZB_ERR_TOO_LARGE (-6)   /* model does not fit the kernel's limits */
 #define PHYZB_ERR_UNSUPPORTED (-7) /* feature outside the implemented path */
+#define PHYZB_ERR_COMM (-8)        /* NCCL missing, collective failed or timed out */
 
 /* ── enums ────────────────────────────────────────────────────────────── */
 /* Joint codes: crates/phyz-gpu/src/layout.rs:23 ([1] joint_type). */
@@ -261,6 +262,29 @@ int phyzb_step_device_controls(phyzb_sim* sim, const void* ctrl_schedule, int64_
  * body-wise, kind 1 = sum of squared joint positions. The value a
  * multi-GPU job all-reduces at the end of a rollout. */
 int phyzb_objective_device(phyzb_sim* sim, int kind, void* out_device_scalar);
+
+/* ── multi-GPU: one process per GPU, worlds sharded contiguously ──────── */
+
+/* Worlds are independent, so ranks exchange nothing per step; the one
+ * collective is the sum of the per-world objective over every rank's shard
+ * at the end of a rollout (NCCL over NVLink; the reduction phyz-gpu's
+ * callers do on the host). NCCL is loaded at run time. */
+#define PHYZB_COMM_ID_BYTES 128
+typedef struct phyzb_comm phyzb_comm;
+/* Rank 0 creates the communicator id and hands the bytes to the other
+ * ranks (any host channel: a store, an MPI/torch broadcast). */
+int phyzb_comm_unique_id(uint8_t* id_out /* PHYZB_COMM_ID_BYTES */);
+/* Join the communicator on `device`. Returns PHYZB_ERR_COMM when not every
+ * rank joined within timeout_s seconds. */
+int phyzb_comm_init(const uint8_t* id, int32_t nranks, int32_t rank, int32_t device, double timeout_s,
+                    phyzb_comm** out);
+int phyzb_comm_destroy(phyzb_comm* comm);
+/* phyzb_objective_device of this rank's shard, summed over all ranks (NCCL
+ * all-reduce on the simulator's stream) and returned to the host on every
+ * rank. Every rank calls it in the same order. A rank that does not take
+ * part makes the others return PHYZB_ERR_COMM after timeout_s seconds; the
+ * communicator is then aborted and must be rebuilt. */
+int phyzb_reduce_objective(phyzb_sim* sim, phyzb_comm* comm, int kind, double timeout_s, double* out);
 
 /* ── measurement helpers (no reference counterpart) ───────────────────── */
 

@@ -19,6 +19,8 @@ ERR_STATE = -4
 ERR_NONFINITE = -5
 ERR_TOO_LARGE = -6
 ERR_UNSUPPORTED = -7
+ERR_COMM = -8
+COMM_ID_BYTES = 128
 
 F32 = 0
 F64 = 1
@@ -128,6 +130,11 @@ SIGNATURES = {
     "phyzb_objective_device": (C.c_int, [_P, C.c_int, _P]),
     "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
     "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
+    "phyzb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
+    "phyzb_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int32, C.c_double,
+                                  C.POINTER(_P)]),
+    "phyzb_comm_destroy": (C.c_int, [_P]),
+    "phyzb_reduce_objective": (C.c_int, [_P, _P, C.c_int, C.c_double, C.POINTER(C.c_double)]),
     "phyzb_measure_fma_peak": (C.c_int, [C.c_int, _D]),
 }
 

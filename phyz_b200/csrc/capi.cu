@@ -5,8 +5,12 @@
 // converted on the device between phyz's world-major f64 rows and the
 // simulator's structure-of-arrays state (f32 or f64).
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
+#include <thread>
 #include <cstdlib>
 #include <cstdint>
 #include <cstring>
@@ -85,6 +89,9 @@ struct phyzb_sim {
     void* pipe_soa[2] = {nullptr, nullptr};
     size_t pipe_raw_bytes = 0, pipe_soa_bytes = 0;
     cudaEvent_t ev_copied[2] = {nullptr, nullptr}, ev_converted[2] = {nullptr, nullptr};
+    void* obj = nullptr;       // device scalar of phyzb_reduce_objective
+    void* obj_host = nullptr;  // pinned: the read-back never blocks the host
+    cudaEvent_t ev_obj = nullptr;
 
     size_t esz() const { return precision == PHYZB_F64 ? 8 : 4; }
     size_t state_bytes() const { return (size_t)nworld * nv * esz(); }
@@ -328,6 +335,9 @@ void destroy_sim(phyzb_sim* s) {
         if (s->ev_copied[b]) cudaEventDestroy(s->ev_copied[b]);
         if (s->ev_converted[b]) cudaEventDestroy(s->ev_converted[b]);
     }
+    free_ptr(s->obj);
+    if (s->obj_host) cudaFreeHost(s->obj_host);
+    if (s->ev_obj) cudaEventDestroy(s->ev_obj);
     if (s->copy_stream) cudaStreamDestroy(s->copy_stream);
     if (s->own_stream) cudaStreamDestroy(s->own_stream);
     delete s;
@@ -695,6 +705,216 @@ int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t
     if (smem) *smem = L.launch.smem;
     if (scratch) *scratch = L.info.scratch;
     if (tmem_cols) *tmem_cols = L.launch.tm ? L.info.tmem_cols : 0;
+    return PHYZB_OK;
+}
+
+}  // extern "C"
+
+// ── multi-GPU: NCCL communicator and the all-reduced objective ────────────
+//
+// NCCL is loaded at run time (libnccl.so.2; in a process that already holds
+// one -- e.g. torch's -- that copy is reused), so the library itself keeps no
+// link-time dependency on it. Communicators are created non-blocking and
+// every wait on one is bounded: a rank that never joins or a collective that
+// never completes ends in PHYZB_ERR_COMM after the caller's timeout, with the
+// communicator aborted.
+
+namespace {
+
+struct NcclApi {
+    bool tried = false, ok = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    const char* (*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+NcclApi& nccl() {
+    static NcclApi api;
+    if (api.tried) return api;
+    api.tried = true;
+    void* h = nullptr;
+    for (const char* name : {"libnccl.so.2", "libnccl.so"})
+        if ((h = dlopen(name, RTLD_NOW | RTLD_GLOBAL)) != nullptr) break;
+    if (!h) {
+        api.why = std::string("NCCL not found (dlopen libnccl.so.2): ") + dlerror();
+        return api;
+    }
+    auto sym = [&](const char* n) { return dlsym(h, n); };
+    api.GetUniqueId = (decltype(api.GetUniqueId))sym("ncclGetUniqueId");
+    api.CommInitRankConfig = (decltype(api.CommInitRankConfig))sym("ncclCommInitRankConfig");
+    api.CommGetAsyncError = (decltype(api.CommGetAsyncError))sym("ncclCommGetAsyncError");
+    api.CommAbort = (decltype(api.CommAbort))sym("ncclCommAbort");
+    api.CommDestroy = (decltype(api.CommDestroy))sym("ncclCommDestroy");
+    api.AllReduce = (decltype(api.AllReduce))sym("ncclAllReduce");
+    api.GetErrorString = (decltype(api.GetErrorString))sym("ncclGetErrorString");
+    api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommGetAsyncError && api.CommAbort &&
+             api.CommDestroy && api.AllReduce && api.GetErrorString;
+    if (!api.ok) api.why = "NCCL library lacks a required entry point (needs NCCL >= 2.14)";
+    return api;
+}
+
+std::string nccl_msg(ncclResult_t r) {
+    NcclApi& n = nccl();
+    return n.GetErrorString ? n.GetErrorString(r) : ("NCCL error " + std::to_string((int)r));
+}
+
+double seconds_since(std::chrono::steady_clock::time_point t0) {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+}  // namespace
+
+struct phyzb_comm {
+    ncclComm_t comm = nullptr;
+    int nranks = 0, rank = 0, device = 0;
+    bool broken = false;
+};
+
+namespace {
+
+// Wait (bounded) until a non-blocking communicator has no operation in
+// progress. On error or timeout the communicator is aborted.
+int comm_settle(phyzb_comm* c, double timeout_s, const char* what) {
+    NcclApi& n = nccl();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = n.CommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess) st = r;
+        if (st == ncclSuccess) return PHYZB_OK;
+        if (st != ncclInProgress) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, std::string(what) + ": " + nccl_msg(st));
+        }
+        if (seconds_since(t0) > timeout_s) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, std::string(what) + ": timed out after " + std::to_string(timeout_s) +
+                                            " s (a rank did not take part)");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+int phyzb_comm_unique_id(uint8_t* id_out) {
+    if (!id_out) return fail(PHYZB_ERR_INVALID, "id buffer is null");
+    NcclApi& n = nccl();
+    if (!n.ok) return fail(PHYZB_ERR_COMM, n.why);
+    ncclUniqueId id;
+    const ncclResult_t r = n.GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(PHYZB_ERR_COMM, "ncclGetUniqueId: " + nccl_msg(r));
+    static_assert(sizeof(ncclUniqueId) == PHYZB_COMM_ID_BYTES, "NCCL unique id size");
+    std::memcpy(id_out, &id, sizeof(id));
+    return PHYZB_OK;
+}
+
+int phyzb_comm_init(const uint8_t* id, int32_t nranks, int32_t rank, int32_t device, double timeout_s,
+                    phyzb_comm** out) {
+    if (!id || !out) return fail(PHYZB_ERR_INVALID, "id or output is null");
+    *out = nullptr;
+    if (nranks < 1 || rank < 0 || rank >= nranks) return fail(PHYZB_ERR_INVALID, "rank must be in [0, nranks)");
+    if (!(timeout_s > 0.0)) return fail(PHYZB_ERR_INVALID, "timeout must be > 0");
+    NcclApi& n = nccl();
+    if (!n.ok) return fail(PHYZB_ERR_COMM, n.why);
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return fail(PHYZB_ERR_NO_DEVICE, "no CUDA device");
+    }
+    if (device < 0 || device >= ndev) return fail(PHYZB_ERR_INVALID, "device ordinal out of range");
+    DeviceGuard g(device);
+    phyzb_comm* c = new phyzb_comm;
+    c->nranks = nranks;
+    c->rank = rank;
+    c->device = device;
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    const ncclResult_t r = n.CommInitRankConfig(&c->comm, nranks, uid, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        delete c;
+        return fail(PHYZB_ERR_COMM, "ncclCommInitRankConfig: " + nccl_msg(r));
+    }
+    const int rc = comm_settle(c, timeout_s, "communicator init");
+    if (rc != PHYZB_OK) {
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return PHYZB_OK;
+}
+
+int phyzb_comm_destroy(phyzb_comm* c) {
+    if (!c) return PHYZB_OK;
+    NcclApi& n = nccl();
+    if (c->comm && n.ok) {
+        DeviceGuard g(c->device);
+        if (c->broken)
+            n.CommAbort(c->comm);
+        else
+            n.CommDestroy(c->comm);
+    }
+    delete c;
+    return PHYZB_OK;
+}
+
+int phyzb_reduce_objective(phyzb_sim* s, phyzb_comm* c, int kind, double timeout_s, double* out) {
+    PZ_TRY(check_sim(s));
+    if (!c || !out) return fail(PHYZB_ERR_INVALID, "communicator or output is null");
+    if (c->broken) return fail(PHYZB_ERR_COMM, "communicator was aborted by an earlier failure");
+    if (c->device != s->device) return fail(PHYZB_ERR_INVALID, "communicator and simulator are on different devices");
+    if (!(timeout_s > 0.0)) return fail(PHYZB_ERR_INVALID, "timeout must be > 0");
+    NcclApi& n = nccl();
+    DeviceGuard g(s->device);
+    if (!s->obj) PZ_CUDA(cudaMalloc(&s->obj, 16));
+    if (!s->obj_host) PZ_CUDA(cudaHostAlloc(&s->obj_host, 16, cudaHostAllocDefault));
+    if (!s->ev_obj) PZ_CUDA(cudaEventCreateWithFlags(&s->ev_obj, cudaEventDisableTiming));
+    PZ_CUDA(cudaMemsetAsync(s->obj, 0, s->esz(), s->stream));
+    PZ_TRY(phyzb_objective_device(s, kind, s->obj));
+    const ncclResult_t r = n.AllReduce(s->obj, s->obj, 1, is_f64(s) ? ncclFloat64 : ncclFloat32, ncclSum, c->comm,
+                                       s->stream);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        n.CommAbort(c->comm);
+        c->broken = true;
+        return fail(PHYZB_ERR_COMM, "ncclAllReduce: " + nccl_msg(r));
+    }
+    PZ_TRY(comm_settle(c, timeout_s, "objective all-reduce (enqueue)"));
+    PZ_CUDA(cudaMemcpyAsync(s->obj_host, s->obj, s->esz(), cudaMemcpyDeviceToHost, s->stream));
+    PZ_CUDA(cudaEventRecord(s->ev_obj, s->stream));
+    // bounded wait on the collective: poll the event and NCCL's error state
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(s->ev_obj);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) PZ_CUDA(q);
+        ncclResult_t st = ncclSuccess;
+        n.CommGetAsyncError(c->comm, &st);
+        if (st != ncclSuccess && st != ncclInProgress) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, "objective all-reduce: " + nccl_msg(st));
+        }
+        if (seconds_since(t0) > timeout_s) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, "objective all-reduce: timed out after " + std::to_string(timeout_s) +
+                                            " s (a rank did not take part)");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    *out = is_f64(s) ? *static_cast<const double*>(s->obj_host) : (double)*static_cast<const float*>(s->obj_host);
     return PHYZB_OK;
 }
 
