@@ -71,6 +71,10 @@ template <>
 struct Eps<Cnt> {
     static constexpr double quat = 2.220446049250313e-16;
 };
+template <>
+struct Counting<Cnt> {
+    static constexpr bool value = true;
+};
 
 }  // namespace pz
 

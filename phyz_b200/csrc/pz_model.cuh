@@ -38,6 +38,7 @@ enum BodyFlags {
     F_BRANCH = 1 << 7,    // parent of a child that is not i+1 (stored accumulators)
     F_ZHINGE = 1 << 8,    // hinge about z of its (relabelled) frame; parent->joint rotation
                           // is the cyclic relabelling `qshift` (the kernel's fast path)
+    F_PD = 1 << 9,        // a DOF of this body is driven by a PD servo
 };
 
 template <class T>

@@ -324,6 +324,9 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         pd[k].vi = cfg.pd[k].v_index;
         pdmap[cfg.pd[k].v_index] = k;
     }
+    for (int i = 0; i < nb; i++)
+        for (int k = 0; k < bi[i].ndof; k++)
+            if (pdmap[bi[i].off + k] >= 0) bi[i].flags |= F_PD;
     info.scratch = next;
     for (int i = 0; i < nb; i++)
         if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;

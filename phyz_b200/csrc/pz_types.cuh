@@ -53,6 +53,12 @@ __device__ __forceinline__ bool pz_finite(double x) { return isfinite(x); }
 // Small-angle threshold of the exp/log maps: f64 uses f64::EPSILON like
 // crates/phyz-math/src/lib.rs:48,67; f32 uses the 1e-6 of the reference's
 // f32 kernels (phyz_kernels.cu:262,292).
+// Counting(T): T is the host op-counting scalar (flops.cpp), which tallies
+// only algorithmic work. The kernel does some structurally zero work
+// unconditionally (a zero offset, a zero spring) because it is cheaper than
+// a branch; under counting those terms are skipped.
+template <class T> struct Counting { static constexpr bool value = false; };
+
 template <class T> struct Eps;
 template <> struct Eps<float> { static constexpr double quat = 1e-6; };
 template <> struct Eps<double> { static constexpr double quat = 2.220446049250313e-16; };

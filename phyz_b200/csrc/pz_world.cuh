@@ -356,7 +356,9 @@ PZ_HD V3<T> tree_pos(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j) {
 // X_tree m for a motion vector (X_ptj first, then X_J).
 template <int AX, int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
-    if (bi.flags & F_PTJ_POS) m = xm_apply_trans(ld3(bt.ptj_pos), m);
+    // (relabelled hinges translate unconditionally: a zero offset is exact and
+    // cheaper than the branch)
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) m = xm_apply_trans(ld3(bt.ptj_pos), m);
     if constexpr (AX >= 0) {
         return rot_fwd<AX, FEAT>(bi.qshift, j.c, j.s, m);
     } else {
@@ -411,7 +413,7 @@ PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f)
             f = xf_tapply_rot(P, f);
         }
     }
-    if (bi.flags & F_PTJ_POS) f = xf_tapply_trans(ld3(bt.ptj_pos), f);
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) f = xf_tapply_trans(ld3(bt.ptj_pos), f);
     return f;
 }
 
@@ -449,7 +451,7 @@ PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I
             ai_rot(P, I);
         }
     }
-    if (bi.flags & F_PTJ_POS) ai_trans(ld3(bt.ptj_pos), I);
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) ai_trans(ld3(bt.ptj_pos), I);
 }
 
 // S qd of body i (aba.rs:15-30).
@@ -503,16 +505,19 @@ PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, co
     const int d = bi.off + k;
     const T qd = S(M.nv + d);
     T in = S(bi.s_w0 + k);
-    const int pdi = M.pd_of_dof[d];
-    if (pdi >= 0) {
-        const PdT<T>& e = M.pd[pdi];
-        const T tau = e.kp * (in - S(e.qi)) - e.kd * S(M.nv + e.vi);
-        in = pz_min(pz_max(tau, -e.maxf), e.maxf);
+    if (bi.flags & F_PD) {
+        const int pdi = M.pd_of_dof[d];
+        if (pdi >= 0) {
+            const PdT<T>& e = M.pd[pdi];
+            const T tau = e.kp * (in - S(e.qi)) - e.kd * S(M.nv + e.vi);
+            in = pz_min(pz_max(tau, -e.maxf), e.maxf);
+        }
     }
     T f = in - bt.damping * qd;
     if (bi.ndof == 1) {
         const T q = S(d);
-        if (bi.flags & F_SPRING) f = f - bt.stiffness * (q - bt.spring_ref);
+        // the spring term is exact with stiffness 0, and cheaper than a branch
+        if (!Counting<T>::value || (bi.flags & F_SPRING)) f = f - bt.stiffness * (q - bt.spring_ref);
         if (bi.flags & F_LIMITS) {
             T depth = T(0), sign = T(0);
             if (q < bt.lim_lo) {
@@ -818,13 +823,24 @@ struct WorldIO {
 template <class T, class Scr>
 PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
                              int step) {
-    for (int k = 0; k < bi.ndof; k++) {
+    const int nd = bi.ndof;
+    for (int k = 0; k < nd; k++) {
         const int d = bi.off + k;
-        const int pdi = M.pd_of_dof[d];
+        const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
         const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
                                 : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
         S.prefetch(bi.s_w0 + k, src);
     }
+}
+// One-DOF form for the relabelled-hinge path.
+template <class T, class Scr>
+PZ_HD void prefetch_control1(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
+                             int step) {
+    const int d = bi.off;
+    const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
+    const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
+                            : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
+    S.prefetch(bi.s_w0, src);
 }
 
 // I c for a bias c whose K components are structurally zero (c = v x S qd
@@ -1088,7 +1104,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         else
             st_sv(S, bi.s_vw, mksv<T>(Ww, Wl));
         S(bi.s_w0) = w0;
-        if (live) {
+        {  // (a skipped body's contribution is dropped below; W = 0 keeps this exact)
             if (p >= 0) {
                 // I <- I - W U^T (rank-1, symmetric)
 #pragma unroll
@@ -1291,7 +1307,10 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
         if (bi.ndof > 1) integrate_multi(M, bi, S, qdd_out);
     }
     if (next_step >= 0) {
-        prefetch_controls(M, bi, S, io, next_step);
+        if constexpr (AX >= 0)
+            prefetch_control1(M, bi, S, io, next_step);
+        else
+            prefetch_controls(M, bi, S, io, next_step);
         pass1_body<AX, FEAT>(M, S, i, bi, cvn, cw);
     }
 }
