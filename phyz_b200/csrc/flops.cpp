@@ -169,7 +169,7 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
     // steady state: one backward sweep + one fused finish/start sweep
     g_tally = Tally{};
     pass2<ALL>(M, S);
-    pass3_next<ALL>(M, S, io, 1, none);
+    pass3_next<ALL, false>(M, S, io, 1, none);
     FlopCount fc;
     fc.flops = g_tally.flops;
     fc.transcendentals = g_tally.trans;

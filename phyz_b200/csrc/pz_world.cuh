@@ -518,19 +518,21 @@ PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, co
         const T q = S(d);
         // the spring term is exact with stiffness 0, and cheaper than a branch
         if (!Counting<T>::value || (bi.flags & F_SPRING)) f = f - bt.stiffness * (q - bt.spring_ref);
-        if (bi.flags & F_LIMITS) {
-            T depth = T(0), sign = T(0);
-            if (q < bt.lim_lo) {
-                depth = bt.lim_lo - q;
-                sign = T(1);
-            } else if (q > bt.lim_hi) {
-                depth = q - bt.lim_hi;
-                sign = T(-1);
+        if (bi.flags & (F_LIMITS | F_FRICTION)) {
+            if (bi.flags & F_LIMITS) {
+                T depth = T(0), sign = T(0);
+                if (q < bt.lim_lo) {
+                    depth = bt.lim_lo - q;
+                    sign = T(1);
+                } else if (q > bt.lim_hi) {
+                    depth = q - bt.lim_hi;
+                    sign = T(-1);
+                }
+                const T inward = pz_max(-sign * qd, T(0));
+                f = f + sign * (bt.lim_k * depth + bt.lim_d * inward);
             }
-            const T inward = pz_max(-sign * qd, T(0));
-            f = f + sign * (bt.lim_k * depth + bt.lim_d * inward);
+            if (bi.flags & F_FRICTION) f = f - bt.fric * pz_tanh(qd / T(1e-3));
         }
-        if (bi.flags & F_FRICTION) f = f - bt.fric * pz_tanh(qd / T(1e-3));
     }
     return f;
 }
@@ -1238,7 +1240,7 @@ PZ_HD void integrate_multi(const ModelView<T>& M, const BodyI& bi, const Scr& S,
 // ── pass 3 + integration of body i for the current step, fused with pass 1
 // of the next (aba.rs:322-400, then integrate.rs, then aba.rs:175-213 and
 // the contact pass). `next_step` < 0: the last step of the launch.
-template <int AX, int FEAT, class T, class Scr>
+template <int AX, int FEAT, bool LAST, class T, class Scr>
 PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int i, const BodyI& bi,
                       int next_step, const Out<T>& qdd_out, SV<T>& cvo, SV<T>& ca, SV<T>& cvn, WF<T>& cw) {
     const BodyT<T>& bt = M.bt[i];
@@ -1302,11 +1304,11 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
     ca = a;
     if (AX >= 0 || bi.ndof == 1) {
         integrate_1dof(M, bi, S, qdd0);
-        qdd_out.put(bi.off, qdd0);
+        if constexpr (LAST) qdd_out.put(bi.off, qdd0);
     } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
         if (bi.ndof > 1) integrate_multi(M, bi, S, qdd_out);
     }
-    if (next_step >= 0) {
+    if constexpr (!LAST) {
         if constexpr (AX >= 0)
             prefetch_control1(M, bi, S, io, next_step);
         else
@@ -1315,14 +1317,16 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
     }
 }
 
-template <int FEAT, class T, class Scr>
+// LAST: the launch's final step (qdd written out, no next step); otherwise
+// `next_step` is the step whose controls are prefetched and whose pass 1 runs.
+template <int FEAT, bool LAST, class T, class Scr>
 PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io, int next_step,
                       const Out<T>& qdd_out) {
     SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
     WF<T> cw;
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
-#define PZ_P3(AX) pass3_body<AX, FEAT>(M, S, io, i, bi, next_step, qdd_out, cvo, ca, cvn, cw)
+#define PZ_P3(AX) pass3_body<AX, FEAT, LAST>(M, S, io, i, bi, next_step, qdd_out, cvo, ca, cvn, cw)
         PZ_BY_KIND(body_kind(bi), PZ_P3)
 #undef PZ_P3
     }

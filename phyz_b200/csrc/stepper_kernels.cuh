@@ -256,7 +256,10 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
                     contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
             pass2<FEAT>(M, S);
-            pass3_next<FEAT>(M, S, io, last ? -1 : s + 1, (last && active) ? Out<T>{P.qdd + w, N} : none);
+            if (last)
+                pass3_next<FEAT, true>(M, S, io, -1, active ? Out<T>{P.qdd + w, N} : none);
+            else
+                pass3_next<FEAT, false>(M, S, io, s + 1, none);
             S.commit();
         }
         S.wait();
