@@ -61,7 +61,7 @@ def ncu_traffic(config, prec, nv, esz, nworld, horizon):
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=7)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c2_chain32")
@@ -307,7 +307,10 @@ def main():
     torch.cuda.synchronize()
     sim.sync()  # raises if any world went non-finite
     ms = allreduce_max(t0.elapsed_time(t1), world)
-    kernel_ms = allreduce_max(sum(a.elapsed_time(b) for a, b in kev) / args.steps, world)
+    per_launch = sorted(a.elapsed_time(b) for a, b in kev)
+    kernel_ms = allreduce_max(sum(per_launch) / args.steps, world)
+    kernel_ms_min = allreduce_max(per_launch[0], world)
+    kernel_ms_median = allreduce_max(statistics.median(per_launch), world)
     world_steps = nworld * horizon * world
     value = world_steps * args.steps / (ms * 1e-3)
 
@@ -326,6 +329,7 @@ def main():
         "peak": float(pk[0]), "unit": "TFLOP/s", "frac": achieved / float(pk[0]),
         "peak_source": "measured in this run (independent FMA chains over every SM, phyzb_measure_fma_peak)",
         "traffic": traffic, "kernel": "rollout_kernel", "kernel_ms_per_launch": kernel_ms,
+        "kernel_ms_min": kernel_ms_min, "kernel_ms_median": kernel_ms_median,
         "flops_per_world_step": flops_ws, "transcendentals_per_world_step": trans_ws,
         "algorithmic_bytes_per_world_step": alg_bytes,
         "hbm_gbs_algorithmic": alg_bytes * nworld * horizon / (kernel_ms * 1e-3) / 1e9,
