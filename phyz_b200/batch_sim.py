@@ -49,7 +49,12 @@ class BodyContactGains:
 
 
 def _rows(a, nworld: int, width: int) -> np.ndarray:
-    """pack_rows semantics (layout.rs:327-337): zero-pad / truncate rows."""
+    """pack_rows semantics (layout.rs:327-337): zero-pad / truncate rows.
+    An array already of exactly that shape, C-contiguous f64, is used in
+    place (no copy: pinned host memory stays pinned)."""
+    if (isinstance(a, np.ndarray) and a.dtype == np.float64 and a.shape == (nworld, width)
+            and a.flags.c_contiguous):
+        return a
     out = np.zeros((nworld, width), np.float64)
     if a is None:
         return out
@@ -198,9 +203,17 @@ class BatchSim:
         check(self._lib.phyzb_clear_status(self._h))
 
     # ── readback (cuda/mod.rs:978-996) ─────────────────────────────────────
-    def readback_states(self):
-        q = np.zeros((self.nworld, self.nv))
-        v = np.zeros((self.nworld, self.nv))
+    def readback_states(self, out=None):
+        """(q, v) rows; `out` = a caller's (q, v) pair of (nworld, nv) C-contiguous
+        f64 arrays (e.g. pinned) to fill instead of new ones."""
+        if out is not None:
+            q, v = out
+            if not all(isinstance(a, np.ndarray) and a.dtype == np.float64 and a.shape == (self.nworld, self.nv)
+                       and a.flags.c_contiguous for a in (q, v)):
+                raise ValueError("out must be two C-contiguous float64 arrays of shape (nworld, nv)")
+        else:
+            q = np.zeros((self.nworld, self.nv))
+            v = np.zeros((self.nworld, self.nv))
         check(self._lib.phyzb_readback_states(self._h, dptr(q), dptr(v)))
         return q, v
 
