@@ -263,6 +263,66 @@ int phyzb_step_device_controls(phyzb_sim* sim, const void* ctrl_schedule, int64_
  * multi-GPU job all-reduces at the end of a rollout. */
 int phyzb_objective_device(phyzb_sim* sim, int kind, void* out_device_scalar);
 
+/* ── on-device control loop (crates/phyz-gpu/src/policy_pipeline.rs,
+ *    cuda/mod.rs:1081-1271, phyz_kernels.cu:1436-1715) ──────────────────── */
+
+/* Observation op kinds, one table row of 4 floats (kind, a, b, c) each, as
+ * ObsOp::pack lays them out (policy_pipeline.rs:113-128). */
+#define PHYZB_OBS_CONST 0          /* c */
+#define PHYZB_OBS_Q_MINUS 1        /* q[a] - c */
+#define PHYZB_OBS_V 2              /* v[a] */
+#define PHYZB_OBS_BODY_PITCH 3     /* atan2(-r02, r22) of body a */
+#define PHYZB_OBS_BODY_ROLL 4      /* atan2(r12, r22) */
+#define PHYZB_OBS_BODY_YAW_ERROR 5 /* wrap(c - atan2(r01, r00)) */
+#define PHYZB_OBS_BODY_POS_Z 6     /* body a origin, world z */
+#define PHYZB_OBS_BODY_POS 7       /* body a origin, world axis b */
+#define PHYZB_OBS_COM_OVER_SUPPORT 8 /* aux window (offset a, n_support b), axis c */
+#define PHYZB_KINEMATICS_STRIDE 18 /* world->body rot (9), origin (3), body-frame w (3), v (3) */
+
+/* PolicySpec (policy_pipeline.rs:285-320) in flat form. */
+typedef struct {
+    int32_t n_obs;                 /* observation width = MLP input, 1..128 */
+    const float* obs_ops;          /* n_obs x 4 floats */
+    int32_t n_aux;                 /* floats in obs_aux */
+    const float* obs_aux;          /* ComOverSupport payloads (pack_obs_ops) */
+    int32_t hidden;                /* hidden width of both layers, 1..128 */
+    int32_t n_act;                 /* actions = MLP output, 1..32 */
+    const int32_t* act_slots;      /* PD servo slot (registration order) of each action */
+    double act_clamp;              /* applied-action clamp, every slot */
+    const double* act_clamp_slots; /* per-action clamp (n_act), or NULL */
+    double noise_rho;              /* AR(1) coefficient of the exploration noise */
+    const double* input_noise;     /* n_obs input-noise scales (0 = no draw) */
+    int32_t history_steps;         /* control steps of obs/action history kept */
+} phyzb_policy_spec;
+
+/* enable_policy (mod.rs:1081-1148): needs PD control (the actions are PD
+ * targets). PHYZB_ERR_UNSUPPORTED for a hidden width above 128. */
+int phyzb_enable_policy(phyzb_sim* sim, const phyzb_policy_spec* spec);
+/* set_policy_weights (mod.rs:1151-1162): W1[h][n_obs] b1[h] W2[h][h] b2[h]
+ * W3[n_act][h] b3[n_act], row-major, n = their total. */
+int phyzb_set_policy_weights(phyzb_sim* sim, const double* weights, int64_t n);
+/* set_policy_std (mod.rs:1165-1176): per-action Gaussian standard deviation. */
+int phyzb_set_policy_std(phyzb_sim* sim, const double* std_dev, int32_t n);
+/* set_policy_base_targets (mod.rs:1180-1186): rows [nworld][n_pd]. */
+int phyzb_set_policy_base_targets(phyzb_sim* sim, const double* rows);
+/* seed_policy (mod.rs:1191-1205): every world's xorshift64 stream from
+ * world_seed(seed, w) (policy_pipeline.rs:420-428); AR(1) state zeroed. */
+int phyzb_seed_policy(phyzb_sim* sim, uint64_t seed);
+/* run_policy (mod.rs:1209-1271): kinematics, observation row `step`,
+ * policy forward + sample into action row `step` and the PD targets. */
+int phyzb_run_policy(phyzb_sim* sim, int32_t step);
+/* n_control x (phyzb_run_policy(step0 + c); phyzb_step(substeps)) on the
+ * device, asynchronously (no host round trip between control steps). */
+int phyzb_policy_rollout(phyzb_sim* sim, int32_t step0, int32_t n_control, int32_t substeps);
+/* readback_policy_history (mod.rs:1277-1306): obs [n][nworld][n_obs] and
+ * out [n][nworld][n_act + 1] (actions, then log-prob), f32. */
+int phyzb_readback_policy_history(phyzb_sim* sim, int32_t step0, int32_t n, float* obs, float* out);
+/* readback_targets (mod.rs:1309-1313): PD targets, rows [nworld][n_pd]. */
+int phyzb_readback_targets(phyzb_sim* sim, double* rows);
+/* compute_kinematics + readback (phyz_fk, phyz_kernels.cu:1436-1454):
+ * rows [nworld][nbodies][PHYZB_KINEMATICS_STRIDE]. */
+int phyzb_readback_kinematics(phyzb_sim* sim, double* xforms);
+
 /* ── multi-GPU: one process per GPU, worlds sharded contiguously ──────── */
 
 /* Worlds are independent, so ranks exchange nothing per step; the one

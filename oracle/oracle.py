@@ -166,6 +166,60 @@ class RefHost:
         L.phyzref_rollout.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
                                       C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, C.c_uint32, _F, _F,
                                       _F, _F, _F, C.c_int64, C.c_int32, _F, _F]
+        u = C.c_uint32
+        L.phyz_host_fk.argtypes = [u, u, u, u, _F, _F, _F, _F]
+        L.phyz_host_obs.argtypes = [u, u, u, u, u, u, u, _F, _F, _F, _F, _F, _F, _F]
+        L.phyz_host_policy.argtypes = [u, u, u, u, u, u, C.c_float, u, C.c_float, u, u, _F, _F, _F, _F, _F, _F,
+                                       _F, _F, _F, _F, _F]
+
+    def _bodies(self, model):
+        cm, keep = model.to_c()
+        bodies = np.zeros(model.nbodies * self.BODY_STRIDE, np.float32)
+        self.lib.phyzref_pack_bodies(C.addressof(cm), _f(bodies))
+        return bodies
+
+    def kinematics(self, model, q, v):
+        """phyz_host_fk: [nworld][nb][18] f32 (world->body rot, origin, w, v)."""
+        n, nb = q.shape[0], model.nbodies
+        xf = np.zeros((n, nb, 18), np.float32)
+        self.lib.phyz_host_fk(n, n, model.nv, nb, _f(self._bodies(model)), _f(np.ascontiguousarray(q, np.float32)),
+                              _f(np.ascontiguousarray(v, np.float32)), _f(xf))
+        return xf
+
+    def observe(self, model, q, v, table, aux):
+        """phyz_host_fk then phyz_host_obs: [nworld][n_in] f32."""
+        n, nb, nv = q.shape[0], model.nbodies, model.nv
+        qf, vf = np.ascontiguousarray(q, np.float32), np.ascontiguousarray(v, np.float32)
+        xf = self.kinematics(model, q, v)
+        com = np.array([[b.inertia.mass, *b.inertia.com] for b in model.bodies], np.float32).reshape(-1)
+        n_in = table.size // 4
+        obs = np.zeros((n, n_in), np.float32)
+        aux = np.ascontiguousarray(aux if np.size(aux) else np.zeros(1), np.float32)
+        self.lib.phyz_host_obs(n, n, nv, nv, nb, n_in, 0, _f(np.ascontiguousarray(table, np.float32)), _f(aux),
+                               _f(com), _f(qf), _f(vf), _f(xf), _f(obs))
+        return obs
+
+    def policy(self, spec, weights, std, obs, rng_state, z, base_targets):
+        """phyz_host_policy on rows: obs [n][n_in] (noised in place), rng_state
+        [n] u64, z [n][n_out], base_targets [n][n_pd]. Returns (targets,
+        out [n][n_out + 1], obs, rng_state, z) after one call."""
+        n = obs.shape[0]
+        npd = base_targets.shape[1]
+        obs = np.ascontiguousarray(obs, np.float32).copy()
+        words = np.ascontiguousarray(rng_state, np.uint64).view(np.uint32).copy()  # lo, hi per world
+        zf = np.ascontiguousarray(z, np.float32).copy()
+        clamp = spec.clamp_row().astype(np.float32)
+        targets = np.zeros((n, npd), np.float32)
+        out = np.zeros((n, spec.n_out + 1), np.float32)
+        self.lib.phyz_host_policy(n, n, spec.n_in, spec.hidden, spec.n_out, npd, float(spec.act_clamp),
+                                  int(spec.act_clamp_slots is not None), float(spec.noise_rho), 0, 0,
+                                  _f(np.ascontiguousarray(weights, np.float32)), _f(np.asarray(std, np.float32)),
+                                  _f(np.asarray(spec.input_noise if spec.input_noise is not None
+                                                else np.zeros(spec.n_in), np.float32)),
+                                  _f(obs), _f(words.view(np.float32)), _f(zf),
+                                  _f(np.asarray(spec.act_slots, np.float32)), _f(clamp),
+                                  _f(np.ascontiguousarray(base_targets, np.float32)), _f(targets), _f(out))
+        return targets, out, obs, words.view(np.uint64).copy(), zf
 
     def rollout(self, model, q, v, ctrl, nsteps=1, schedule=False, contact=None, pd=None, targets=None,
                 nthreads=1):

@@ -2,7 +2,8 @@
 batched-simulation API (BatchSim) over the C ABI of libphyzb200.so."""
 from ._lib import PhyzbError
 from .batch_sim import BatchSim, BodyContactGains, PdDof
+from .policy import ObsOp, PolicySpec
 from .model import Geometry, Joint, Model, ModelBuilder, SpatialInertia, Transform
 
-__all__ = ["BatchSim", "BodyContactGains", "PdDof", "PhyzbError", "Geometry", "Joint", "Model",
+__all__ = ["BatchSim", "BodyContactGains", "PdDof", "PhyzbError", "ObsOp", "PolicySpec", "Geometry", "Joint", "Model",
            "ModelBuilder", "SpatialInertia", "Transform"]

@@ -95,9 +95,29 @@ class PhyzbDeviceView(C.Structure):
     ]
 
 
+class PhyzbPolicySpec(C.Structure):
+    _fields_ = [
+        ("n_obs", C.c_int32),
+        ("obs_ops", C.POINTER(C.c_float)),
+        ("n_aux", C.c_int32),
+        ("obs_aux", C.POINTER(C.c_float)),
+        ("hidden", C.c_int32),
+        ("n_act", C.c_int32),
+        ("act_slots", C.POINTER(C.c_int32)),
+        ("act_clamp", C.c_double),
+        ("act_clamp_slots", C.POINTER(C.c_double)),
+        ("noise_rho", C.c_double),
+        ("input_noise", C.POINTER(C.c_double)),
+        ("history_steps", C.c_int32),
+    ]
+
+
+KINEMATICS_STRIDE = 18
+
 _P = C.c_void_p
 _D = C.POINTER(C.c_double)
 _I32P = C.POINTER(C.c_int32)
+_FP = C.POINTER(C.c_float)
 
 # name -> (restype, argtypes)
 SIGNATURES = {
@@ -130,6 +150,16 @@ SIGNATURES = {
     "phyzb_objective_device": (C.c_int, [_P, C.c_int, _P]),
     "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
     "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
+    "phyzb_enable_policy": (C.c_int, [_P, C.POINTER(PhyzbPolicySpec)]),
+    "phyzb_set_policy_weights": (C.c_int, [_P, _D, C.c_int64]),
+    "phyzb_set_policy_std": (C.c_int, [_P, _D, C.c_int32]),
+    "phyzb_set_policy_base_targets": (C.c_int, [_P, _D]),
+    "phyzb_seed_policy": (C.c_int, [_P, C.c_uint64]),
+    "phyzb_run_policy": (C.c_int, [_P, C.c_int32]),
+    "phyzb_policy_rollout": (C.c_int, [_P, C.c_int32, C.c_int32, C.c_int32]),
+    "phyzb_readback_policy_history": (C.c_int, [_P, C.c_int32, C.c_int32, _FP, _FP]),
+    "phyzb_readback_targets": (C.c_int, [_P, _D]),
+    "phyzb_readback_kinematics": (C.c_int, [_P, _D]),
     "phyzb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "phyzb_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                   C.POINTER(_P)]),

@@ -245,6 +245,53 @@ class BatchSim:
     def objective_device(self, kind: int, out_ptr: int) -> None:
         check(self._lib.phyzb_objective_device(self._h, int(kind), C.c_void_p(out_ptr)))
 
+    # ── on-device control loop (cuda/mod.rs:1081-1313) ─────────────────────
+    def enable_policy(self, spec) -> None:
+        cs, keep = spec.to_c()
+        check(self._lib.phyzb_enable_policy(self._h, C.byref(cs)))
+        self._policy = spec
+
+    def set_policy_weights(self, weights) -> None:
+        w = np.ascontiguousarray(weights, np.float64)
+        check(self._lib.phyzb_set_policy_weights(self._h, dptr(w), int(w.size)))
+
+    def set_policy_std(self, std) -> None:
+        s = np.ascontiguousarray(std, np.float64)
+        check(self._lib.phyzb_set_policy_std(self._h, dptr(s), int(s.size)))
+
+    def set_policy_base_targets(self, rows) -> None:
+        r = _rows(rows, self.nworld, getattr(self, "_npd", 0))
+        check(self._lib.phyzb_set_policy_base_targets(self._h, dptr(r)))
+
+    def seed_policy(self, seed: int) -> None:
+        check(self._lib.phyzb_seed_policy(self._h, C.c_uint64(int(seed) & 0xFFFFFFFFFFFFFFFF)))
+
+    def run_policy(self, step: int) -> None:
+        check(self._lib.phyzb_run_policy(self._h, int(step)))
+
+    def policy_rollout(self, step0: int, n_control: int, substeps: int) -> None:
+        check(self._lib.phyzb_policy_rollout(self._h, int(step0), int(n_control), int(substeps)))
+
+    def readback_policy_history(self, step0: int, n: int):
+        """(obs [n][nworld][n_in], out [n][nworld][n_out + 1]) float32."""
+        sp = self._policy
+        obs = np.zeros((n, self.nworld, sp.n_in), np.float32)
+        out = np.zeros((n, self.nworld, sp.n_out + 1), np.float32)
+        fp = lambda a: a.ctypes.data_as(C.POINTER(C.c_float))
+        check(self._lib.phyzb_readback_policy_history(self._h, int(step0), int(n), fp(obs), fp(out)))
+        return obs, out
+
+    def readback_targets(self) -> np.ndarray:
+        t = np.zeros((self.nworld, getattr(self, "_npd", 0)))
+        check(self._lib.phyzb_readback_targets(self._h, dptr(t)))
+        return t
+
+    def readback_kinematics(self) -> np.ndarray:
+        """[nworld][nbodies][18]: world->body rot, origin, body-frame w, v."""
+        xf = np.zeros((self.nworld, self.nb, _lib.KINEMATICS_STRIDE))
+        check(self._lib.phyzb_readback_kinematics(self._h, dptr(xf)))
+        return xf
+
     def flops_per_world_step(self):
         f, t = C.c_double(), C.c_double()
         check(self._lib.phyzb_flops_per_world_step(self._h, C.byref(f), C.byref(t)))

@@ -243,3 +243,41 @@ def controls(name: str, model, worlds, step: int, seed: int = CTRL_SEED) -> np.n
 
 def control_schedule(name: str, model, worlds, steps: int, seed: int = CTRL_SEED) -> np.ndarray:
     return np.stack([controls(name, model, worlds, t, seed) for t in range(steps)])
+
+
+# ── C5: the quadruped under an on-device policy ───────────────────────────
+C5_HIDDEN = 64
+C5_STEPS = 64
+C5_SUBSTEPS = 1
+C5_PD = (20.0, 1.0, 20.0)  # kp, kd, max force of each hinge servo
+C5_SEED = 0xC5C5
+C5_STD = 0.3
+
+
+def c5_pd_dofs(model):
+    """A PD servo on every hinge DOF of the quadruped (registration order =
+    DOF order), the actions' slots."""
+    from .batch_sim import PdDof
+
+    kp, kd, mf = C5_PD
+    return [PdDof(j, j, kp, kd, mf) for j in np.flatnonzero(actuated(model))]
+
+
+def c5_policy_spec(model):
+    """Observation 30 -> 64 -> 64 tanh -> 8 actions:
+    the 8 hinge angles, the 14 velocities, torso pitch / roll / height / yaw
+    error, the centre of mass over the four feet (heading frame, 3 axes) and
+    a constant. Actions are PD target offsets of the 8 hinges."""
+    from .policy import ObsOp, PolicySpec
+
+    hinges = list(np.flatnonzero(actuated(model)))
+    shins = [i for i, b in enumerate(model.bodies) if b.name.startswith("shin")]
+    feet = [(b, (0.0, 0.0, -0.2)) for b in shins]
+    obs = [ObsOp.q_minus(int(j), 0.0) for j in hinges]
+    obs += [ObsOp.v(j) for j in range(model.nv)]
+    obs += [ObsOp.body_pitch(0), ObsOp.body_roll(0), ObsOp.body_pos_z(0), ObsOp.body_yaw_error(0, 0.0)]
+    obs += [ObsOp.com_over_support(feet, axis, heading_body=0) for axis in range(3)]
+    obs += [ObsOp.const(1.0)]
+    assert len(obs) == 30
+    return PolicySpec(obs=obs, hidden=C5_HIDDEN, act_slots=list(range(len(hinges))), act_clamp=0.5,
+                      noise_rho=0.0, input_noise=[0.0] * len(obs), history_steps=C5_STEPS)

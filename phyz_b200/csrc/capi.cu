@@ -18,10 +18,11 @@
 #include <vector>
 
 #include "../../include/phyzb.h"
+#include "capi_internal.h"
 #include "pz_launch.h"
 #include "pz_pack.h"
 
-namespace {
+namespace pzc {
 
 thread_local std::string g_err;
 
@@ -29,75 +30,13 @@ int fail(int code, const std::string& msg) {
     g_err = msg;
     return code;
 }
+const char* last_error() { return g_err.c_str(); }
 
-#define PZ_CUDA(expr)                                                                           \
-    do {                                                                                        \
-        cudaError_t e_ = (expr);                                                                \
-        if (e_ != cudaSuccess)                                                                  \
-            return fail(PHYZB_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));    \
-    } while (0)
+}  // namespace pzc
 
-#define PZ_TRY(expr)                \
-    do {                            \
-        int r_ = (expr);            \
-        if (r_ != PHYZB_OK) return r_; \
-    } while (0)
+using namespace pzc;
 
-// Restores the caller's current device on scope exit.
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
-    }
-};
-
-}  // namespace
-
-struct phyzb_sim {
-    int device = 0, precision = PHYZB_F64;
-    long long nworld = 0;
-    int nb = 0, nv = 0;
-    std::vector<phyzb_body> bodies;
-    phyzb_model model{};  // points into `bodies`
-    pz::PackCfg cfg;
-    double ground_h = 0.0, friction = 0.0;
-    int collidable = 0;
-
-    cudaStream_t own_stream = nullptr, stream = nullptr, copy_stream = nullptr;
-    void *q = nullptr, *v = nullptr, *ctrl = nullptr, *qdd = nullptr;
-    void *targets = nullptr, *cstate = nullptr;
-    int* status = nullptr;
-    // lay[0]: every record in shared memory (the objective kernel's layout
-    // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the
-    // layout the rollout kernel runs with.
-    struct Layout {
-        pz::PackInfo info;
-        void* blob = nullptr;
-        size_t cap = 0;
-        pz::LaunchCfg launch{};
-    } lay[2];
-    int use = 0;
-    void* staging = nullptr;  // device, AoS f64 rows for host copies
-    size_t staging_bytes = 0;
-    // bulk per-step control pipeline (phyzb_step_with_controls)
-    void* pipe_raw[2] = {nullptr, nullptr};
-    void* pipe_soa[2] = {nullptr, nullptr};
-    size_t pipe_raw_bytes = 0, pipe_soa_bytes = 0;
-    cudaEvent_t ev_copied[2] = {nullptr, nullptr}, ev_converted[2] = {nullptr, nullptr};
-    void* obj = nullptr;       // device scalar of phyzb_reduce_objective
-    void* obj_host = nullptr;  // pinned: the read-back never blocks the host
-    cudaEvent_t ev_obj = nullptr;
-
-    size_t esz() const { return precision == PHYZB_F64 ? 8 : 4; }
-    size_t state_bytes() const { return (size_t)nworld * nv * esz(); }
-};
-
-namespace {
+namespace pzc {
 
 bool is_f64(const phyzb_sim* s) { return s->precision == PHYZB_F64; }
 
@@ -316,6 +255,7 @@ int ensure_pipeline(phyzb_sim* s, size_t raw_bytes, size_t soa_bytes) {
 void destroy_sim(phyzb_sim* s) {
     if (!s) return;
     DeviceGuard g(s->device);
+    destroy_policy(s);
     if (s->stream) cudaStreamSynchronize(s->stream);
     if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
     free_ptr(s->q);
@@ -343,11 +283,11 @@ void destroy_sim(phyzb_sim* s) {
     delete s;
 }
 
-}  // namespace
+}  // namespace pzc
 
 extern "C" {
 
-const char* phyzb_last_error(void) { return g_err.c_str(); }
+const char* phyzb_last_error(void) { return pzc::last_error(); }
 
 int phyzb_abi_version(void) { return PHYZB_ABI_VERSION; }
 
@@ -411,7 +351,7 @@ int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int preci
         return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc staging"));
     int r = repack(s);
     if (r != PHYZB_OK) {
-        std::string msg = g_err;
+        std::string msg = pzc::last_error();
         destroy_sim(s);
         return fail(r, msg);
     }

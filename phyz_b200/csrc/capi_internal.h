@@ -1,0 +1,107 @@
+// Internals shared by the C ABI's translation units (capi.cu, capi_policy.cu):
+// the simulator handle, error reporting and the host-row transfer helpers.
+// Not part of the public interface (include/phyzb.h).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/phyzb.h"
+#include "pz_launch.h"
+#include "pz_pack.h"
+
+namespace pzc {
+
+// Record `msg` as the calling thread's last error and return `code`.
+int fail(int code, const std::string& msg);
+const char* last_error();
+
+#define PZ_CUDA(expr)                                                                           \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess)                                                                  \
+            return fail(PHYZB_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_));    \
+    } while (0)
+
+#define PZ_TRY(expr)                \
+    do {                            \
+        int r_ = (expr);            \
+        if (r_ != PHYZB_OK) return r_; \
+    } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace pzc
+
+struct PolicyDev;  // the on-device control loop's buffers (capi_policy.cu)
+
+struct phyzb_sim {
+    int device = 0, precision = PHYZB_F64;
+    long long nworld = 0;
+    int nb = 0, nv = 0;
+    std::vector<phyzb_body> bodies;
+    phyzb_model model{};  // points into `bodies`
+    pz::PackCfg cfg;
+    double ground_h = 0.0, friction = 0.0;
+    int collidable = 0;
+
+    cudaStream_t own_stream = nullptr, stream = nullptr, copy_stream = nullptr;
+    void *q = nullptr, *v = nullptr, *ctrl = nullptr, *qdd = nullptr;
+    void *targets = nullptr, *cstate = nullptr;
+    int* status = nullptr;
+    // lay[0]: every record in shared memory (the objective kernel's layout
+    // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the
+    // layout the rollout kernel runs with.
+    struct Layout {
+        pz::PackInfo info;
+        void* blob = nullptr;
+        size_t cap = 0;
+        pz::LaunchCfg launch{};
+    } lay[2];
+    int use = 0;
+    void* staging = nullptr;  // device, AoS f64 rows for host copies
+    size_t staging_bytes = 0;
+    // bulk per-step control pipeline (phyzb_step_with_controls)
+    void* pipe_raw[2] = {nullptr, nullptr};
+    void* pipe_soa[2] = {nullptr, nullptr};
+    size_t pipe_raw_bytes = 0, pipe_soa_bytes = 0;
+    cudaEvent_t ev_copied[2] = {nullptr, nullptr}, ev_converted[2] = {nullptr, nullptr};
+    PolicyDev* policy = nullptr;  // phyzb_enable_policy
+    void* obj = nullptr;       // device scalar of phyzb_reduce_objective
+    void* obj_host = nullptr;  // pinned: the read-back never blocks the host
+    cudaEvent_t ev_obj = nullptr;
+
+    size_t esz() const { return precision == PHYZB_F64 ? 8 : 4; }
+    size_t state_bytes() const { return (size_t)nworld * nv * esz(); }
+};
+
+namespace pzc {
+
+bool is_f64(const phyzb_sim* s);
+int check_sim(const phyzb_sim* s);
+void free_ptr(void*& p);
+// one fused rollout launch of nsteps under `ctrl` (schedule stride or 0)
+int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps);
+// host rows [nworld][width] f64 <-> device SoA [width][nworld] (sim precision)
+int upload_rows(phyzb_sim* s, const double* host, int width, void* dst);
+int download_rows(phyzb_sim* s, const void* src, int width, double* host);
+void destroy_policy(phyzb_sim* s);  // capi_policy.cu
+
+}  // namespace pzc

@@ -163,5 +163,6 @@ template cudaError_t launch_aos_to_soa<float, float>(const float*, float*, long 
 template cudaError_t launch_aos_to_soa<float, double>(const float*, double*, long long, int, int, cudaStream_t);
 template cudaError_t launch_soa_to_aos<float, double>(const float*, double*, long long, int, cudaStream_t);
 template cudaError_t launch_soa_to_aos<double, double>(const double*, double*, long long, int, cudaStream_t);
+template cudaError_t launch_soa_to_aos<float, float>(const float*, float*, long long, int, cudaStream_t);
 
 }  // namespace pz
