@@ -323,6 +323,50 @@ int phyzb_readback_targets(phyzb_sim* sim, double* rows);
  * rows [nworld][nbodies][PHYZB_KINEMATICS_STRIDE]. */
 int phyzb_readback_kinematics(phyzb_sim* sim, double* xforms);
 
+/* ── PPO update (crates/phyz-gpu/cuda/phyz_train.cu, src/cuda/train.rs) ─ */
+
+/* TrainPipeline (train.rs:474-810): a clipped-surrogate PPO update of a
+ * three-layer tanh MLP actor (with a trailing log_std block) and critic,
+ * Adam with f64 master parameters and moments, on the device. */
+typedef struct phyzb_trainer phyzb_trainer;
+typedef struct {
+    int32_t n_in, n_h, n_out; /* n_h <= 128, n_out <= 32 */
+} phyzb_net_dims;
+typedef struct {
+    double lr, beta1, beta2, eps, weight_decay; /* tang's ModuleAdam */
+} phyzb_adam_cfg;
+#define PHYZB_KL_CUMULATIVE 0 /* mean of logp_old - logp over every row so far */
+#define PHYZB_KL_MINIBATCH 1  /* Schulman's k3 over the current minibatch */
+typedef struct {
+    double clip, entropy_coef, vdelta; /* surrogate clip, entropy bonus, value-gradient Huber delta */
+    int32_t minibatch, epochs;
+    double target_kl, kl_scale; /* the KL brake: stop after the first minibatch above target */
+    int32_t kl_mode;
+} phyzb_ppo_cfg;
+typedef struct {
+    double policy_loss, value_loss, kl;
+    int32_t grad_steps, stopped_early;
+} phyzb_update_stats;
+
+/* TrainPipeline::new (train.rs:523-580): at most `capacity` samples per
+ * update and `max_minibatch` per minibatch; the critic has one output. */
+int phyzb_trainer_create(int32_t device, phyzb_net_dims actor, phyzb_net_dims critic, int64_t capacity,
+                         int32_t max_minibatch, phyzb_trainer** out);
+int phyzb_trainer_destroy(phyzb_trainer* tr);
+/* set_adam (train.rs:800-806); defaults lr 3e-4, betas 0.9 / 0.999, eps 1e-8. */
+int phyzb_trainer_set_adam(phyzb_trainer* tr, const phyzb_adam_cfg* actor, const phyzb_adam_cfg* critic);
+/* set_actor_params / set_critic_params (which = 0 / 1): tang's flat order
+ * W1 b1 W2 b2 W3 b3 (+ log_std for the actor); params reads them back. */
+int phyzb_trainer_set_params(phyzb_trainer* tr, int32_t which, const double* flat, int64_t n);
+int phyzb_trainer_params(phyzb_trainer* tr, int32_t which, double* flat, int64_t n);
+/* upload_batch (train.rs:602-645): row-major host columns of n_rows rows. */
+int phyzb_trainer_upload_batch(phyzb_trainer* tr, int64_t n_rows, const float* obs_a, const float* obs_c,
+                               const float* act, const float* logp_old, const float* adv, const float* ret);
+/* update (train.rs:655-795): epochs over the uploaded batch in the order
+ * given (n_orders permutations of 0..n_rows, one per epoch). */
+int phyzb_trainer_update(phyzb_trainer* tr, const uint32_t* order, int32_t n_orders, const phyzb_ppo_cfg* cfg,
+                         phyzb_update_stats* out);
+
 /* ── multi-GPU: one process per GPU, worlds sharded contiguously ──────── */
 
 /* Worlds are independent, so ranks exchange nothing per step; the one

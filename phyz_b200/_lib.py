@@ -112,6 +112,26 @@ class PhyzbPolicySpec(C.Structure):
     ]
 
 
+class PhyzbNetDims(C.Structure):
+    _fields_ = [("n_in", C.c_int32), ("n_h", C.c_int32), ("n_out", C.c_int32)]
+
+
+class PhyzbAdamCfg(C.Structure):
+    _fields_ = [("lr", C.c_double), ("beta1", C.c_double), ("beta2", C.c_double), ("eps", C.c_double),
+                ("weight_decay", C.c_double)]
+
+
+class PhyzbPpoCfg(C.Structure):
+    _fields_ = [("clip", C.c_double), ("entropy_coef", C.c_double), ("vdelta", C.c_double),
+                ("minibatch", C.c_int32), ("epochs", C.c_int32), ("target_kl", C.c_double),
+                ("kl_scale", C.c_double), ("kl_mode", C.c_int32)]
+
+
+class PhyzbUpdateStats(C.Structure):
+    _fields_ = [("policy_loss", C.c_double), ("value_loss", C.c_double), ("kl", C.c_double),
+                ("grad_steps", C.c_int32), ("stopped_early", C.c_int32)]
+
+
 KINEMATICS_STRIDE = 18
 
 _P = C.c_void_p
@@ -160,6 +180,15 @@ SIGNATURES = {
     "phyzb_readback_policy_history": (C.c_int, [_P, C.c_int32, C.c_int32, _FP, _FP]),
     "phyzb_readback_targets": (C.c_int, [_P, _D]),
     "phyzb_readback_kinematics": (C.c_int, [_P, _D]),
+    "phyzb_trainer_create": (C.c_int, [C.c_int32, PhyzbNetDims, PhyzbNetDims, C.c_int64, C.c_int32,
+                                       C.POINTER(_P)]),
+    "phyzb_trainer_destroy": (C.c_int, [_P]),
+    "phyzb_trainer_set_adam": (C.c_int, [_P, C.POINTER(PhyzbAdamCfg), C.POINTER(PhyzbAdamCfg)]),
+    "phyzb_trainer_set_params": (C.c_int, [_P, C.c_int32, _D, C.c_int64]),
+    "phyzb_trainer_params": (C.c_int, [_P, C.c_int32, _D, C.c_int64]),
+    "phyzb_trainer_upload_batch": (C.c_int, [_P, C.c_int64, _FP, _FP, _FP, _FP, _FP, _FP]),
+    "phyzb_trainer_update": (C.c_int, [_P, C.POINTER(C.c_uint32), C.c_int32, C.POINTER(PhyzbPpoCfg),
+                                       C.POINTER(PhyzbUpdateStats)]),
     "phyzb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "phyzb_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                   C.POINTER(_P)]),

@@ -22,12 +22,13 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libphyzb200.so"
 OBJ = PKG / "_build"
-SOURCES = ["stepper.cu", "capi.cu", "capi_policy.cu", "policy.cu", "flops.cpp", "peaks.cu"]
+SOURCES = ["stepper.cu", "capi.cu", "capi_policy.cu", "capi_train.cu", "policy.cu", "train.cu", "flops.cpp",
+           "peaks.cu"]
 VARIANT_SOURCE = "rollout_variants.cu"
 FEAT_COUNT = 8  # pz_variants.h
 VARIANTS = [(t, f) for t in ("float", "double") for f in range(FEAT_COUNT)]
 HEADERS = ["pz_types.cuh", "pz_model.cuh", "pz_world.cuh", "pz_launch.h", "pz_pack.h", "pz_variants.h",
-           "stepper_kernels.cuh", "pz_policy.h", "capi_internal.h"]
+           "stepper_kernels.cuh", "pz_policy.h", "capi_internal.h", "pz_mlp.cuh", "pz_train.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wno-unknown-pragmas"]
 

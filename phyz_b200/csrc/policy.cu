@@ -15,6 +15,7 @@
 
 #include <cstdint>
 
+#include "pz_mlp.cuh"
 #include "pz_policy.h"
 #include "pz_world.cuh"
 
@@ -250,33 +251,6 @@ __device__ __forceinline__ double rng_normal(unsigned long long& x) {
     return sqrt(-2.0 * log(u1)) * cos(6.283185307179586476925286766559 * u2);
 }
 
-// One dense layer out of shared memory: y[j] = act(b[j] + sum_i Wt[i][j] x[i])
-// for j in [0, out_pad), 32 outputs per register tile. x and y are this
-// world's SoA rows (stride W); Wt is [in_pad][out_pad], zero-padded.
-template <bool TANH>
-__device__ __forceinline__ void dense(const float* Wt, const float* bias, int in_pad, int out_pad, const float* x,
-                                      float* y, int W) {
-    for (int jc = 0; jc < out_pad; jc += POLICY_TILE) {
-        float acc[POLICY_TILE];
-#pragma unroll
-        for (int j = 0; j < POLICY_TILE; j++) acc[j] = bias[jc + j];
-        for (int i = 0; i < in_pad; i++) {
-            const float xi = x[i * W];
-            const float4* wr = reinterpret_cast<const float4*>(Wt + i * out_pad + jc);
-#pragma unroll
-            for (int j4 = 0; j4 < POLICY_TILE / 4; j4++) {
-                const float4 wv = wr[j4];
-                acc[4 * j4 + 0] = fmaf(wv.x, xi, acc[4 * j4 + 0]);
-                acc[4 * j4 + 1] = fmaf(wv.y, xi, acc[4 * j4 + 1]);
-                acc[4 * j4 + 2] = fmaf(wv.z, xi, acc[4 * j4 + 2]);
-                acc[4 * j4 + 3] = fmaf(wv.w, xi, acc[4 * j4 + 3]);
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < POLICY_TILE; j++) y[(jc + j) * W] = TANH ? tanhf(acc[j]) : acc[j];
-    }
-}
-
 template <class T>
 __global__ void __launch_bounds__(POLICY_BLOCK) policy_kernel(const __grid_constant__ PolicyArgs<T> P) {
     extern __shared__ __align__(16) float sm[];
@@ -312,9 +286,9 @@ __global__ void __launch_bounds__(POLICY_BLOCK) policy_kernel(const __grid_const
         }
         X[k * W] = xk;
     }
-    dense<true>(W1, b1, P.in_pad, P.h_pad, X, H1, W);
-    dense<true>(W2, b2, P.h_pad, P.h_pad, H1, H2, W);
-    dense<false>(W3, b3, P.h_pad, P.out_pad, H2, Y, W);
+    dense_rows<1>(W1, b1, P.in_pad, P.h_pad, X, H1, W);
+    dense_rows<1>(W2, b2, P.h_pad, P.h_pad, H1, H2, W);
+    dense_rows<0>(W3, b3, P.h_pad, P.out_pad, H2, Y, W);
 
     // every servo tracks its base target; actions add onto their slots
     for (int j = 0; j < P.npd; j++) P.targets[(long long)j * N + w] = P.base[(long long)j * N + w];

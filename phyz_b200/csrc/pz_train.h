@@ -1,0 +1,78 @@
+// PPO update of an actor and a critic MLP on the device (train.cu): the
+// update half of phyz-gpu's training pipeline (crates/phyz-gpu/cuda/
+// phyz_train.cu, src/cuda/train.rs) re-designed around per-row fused
+// kernels, split-K gradient reductions and an f64-master Adam step.
+// Host-side launch interface, used by capi_train.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace pz {
+
+// A column block of per-sample data, rows r = t * N + w: feature k of row r
+// lives at base[(r / N) * F * N + k * N + r % N] ("blocked SoA": the policy
+// history [step][feature][world] with T = steps, and host batches uploaded
+// as one block of N = n_rows).
+struct BatchCol {
+    const float* base;
+    long long N;
+    int F;
+};
+
+// One network's device state.
+struct NetDev {
+    int n_in, n_h, n_out;
+    int in_pad, h_pad, out_pad;
+    int n_param;           // flat parameters (+ the actor's log_std)
+    int n_wf, n_wb;        // floats in the forward / backward packed weights
+    double* p;             // f64 master parameters, flat reference order
+    double* m;             // Adam moments
+    double* v;
+    float* g;              // gradient, flat order
+    float* wflat;          // f32 mirror, flat order
+    float* wf;             // forward pack: W1^T b1 W2^T b2 W3^T b3 (padded)
+    float* wb;             // backward pack: W3 [out_pad][h_pad], W2 [h_pad][h_pad]
+    const int* posf;       // flat index -> wf index (-1: none)
+    const int* posb;       // flat index -> wb index (-1: none)
+    float* h1;             // [h_pad][max_b]
+    float* h2;             // [h_pad][max_b]
+    float* out;            // [out_pad][max_b]
+    float* dout;           // [out_pad][max_b]
+    float* dh2;            // [h_pad][max_b]
+    float* dh1;            // [h_pad][max_b]
+    int max_b;
+};
+
+struct PpoArgs {
+    float clip, entropy_coef, vdelta;
+    int logstd_off;  // flat offset of the actor's log_std
+};
+
+// forward of `b` rows idx[0..b) of x through `net`, activations into its buffers
+cudaError_t train_forward(const NetDev& net, BatchCol x, const uint32_t* idx, int b, cudaStream_t s);
+// actor: dL/dmean into net.dout, per-row dL/dlogstd, stats cols 0-2
+cudaError_t train_ppo_grad(const NetDev& actor, const PpoArgs& a, BatchCol act, BatchCol logp_old, BatchCol adv,
+                           const uint32_t* idx, int b, float* dlogstd, float* stats, cudaStream_t s);
+// critic: dL/dvalue into net.dout, stats col 3
+cudaError_t train_value_grad(const NetDev& critic, const PpoArgs& a, BatchCol ret, const uint32_t* idx, int b,
+                             float* stats, cudaStream_t s);
+// backprop net.dout through both hidden layers (net.dh2, net.dh1), then the
+// gradient of every parameter into net.g (split-K, f64 accumulation), using
+// `work` (train_work_bytes) as scratch
+cudaError_t train_backward(const NetDev& net, BatchCol x, const uint32_t* idx, int b, double* work,
+                           cudaStream_t s);
+// sum of per-row values [rows][b] into g[off + row] (the log_std gradient)
+cudaError_t train_row_sums(const float* rows, int nrows, int ld, int b, float* g, int off, double* work,
+                           cudaStream_t s);
+// Adam (tang's ModuleAdam, bias corrections bc1, bc2) on every parameter,
+// refreshing the three f32 mirrors
+cudaError_t train_adam(const NetDev& net, double lr, double beta1, double beta2, double eps, double wd,
+                       double bc1, double bc2, cudaStream_t s);
+// column sums of stats [4][b] (f64 accumulation, fixed order) into out[4]
+cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s);
+// scratch bytes train_backward needs for minibatches of up to max_b rows
+size_t train_work_bytes(int max_b, int max_rows, int max_cols);
+
+}  // namespace pz

@@ -1,0 +1,354 @@
+// Kernels of the device-resident PPO update (pz_train.h).
+//
+// The reference walks the update as one thread per weight looping over the
+// whole minibatch (phyz_train.cu:195-246); here the per-row work is fused
+// (one thread per sample runs a network's forward, or its whole two-layer
+// backward, out of shared memory), and every parameter gradient is one
+// split-K reduction: blocks of 256 samples accumulate 32 x 32 tiles of
+// sum_r dsrc[m][r] * x[r][n] (plus the bias column, x = 1) in f64 -- the
+// reference's accumulator precision -- and a second pass adds the splits in a
+// fixed order, so results are deterministic run to run.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "pz_mlp.cuh"
+#include "pz_train.h"
+
+namespace pz {
+
+namespace {
+
+constexpr int ROW_BLOCK = 128;  // samples per block of the per-row kernels
+constexpr int GT = 32;          // gradient tile (outputs m x n)
+constexpr int GK = 32;          // rows per shared-memory stage
+constexpr int GKC = 256;        // rows per split
+
+__device__ __forceinline__ float col(const BatchCol& c, long long r, int k) {
+    return c.base[(r / c.N) * (long long)c.F * c.N + (long long)k * c.N + r % c.N];
+}
+
+__device__ __forceinline__ void stage(const float* g, int n, float* sm) {
+    for (int k = threadIdx.x; k < n / 4; k += blockDim.x)
+        reinterpret_cast<float4*>(sm)[k] = __ldg(reinterpret_cast<const float4*>(g) + k);
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(ROW_BLOCK) fwd_kernel(const NetDev n, const BatchCol x, const uint32_t* idx,
+                                                        int b) {
+    extern __shared__ __align__(16) float sm[];
+    const int W = blockDim.x;
+    stage(n.wf, n.n_wf, sm);
+    const float* W1 = sm;
+    const float* b1 = W1 + n.in_pad * n.h_pad;
+    const float* W2 = b1 + n.h_pad;
+    const float* b2 = W2 + n.h_pad * n.h_pad;
+    const float* W3 = b2 + n.h_pad;
+    const float* b3 = W3 + n.h_pad * n.out_pad;
+    float* X = sm + n.n_wf + threadIdx.x;
+    float* H1 = X + n.in_pad * W;
+    float* H2 = H1 + n.h_pad * W;
+    const int r = blockIdx.x * W + threadIdx.x;
+    if (r >= b) return;
+    const long long s = idx[r];
+    for (int k = 0; k < n.in_pad; k++) X[k * W] = k < n.n_in ? col(x, s, k) : 0.0f;
+    const long long L = n.max_b;
+    dense_rows<1>(W1, b1, n.in_pad, n.h_pad, X, H1, W);
+    for (int j = 0; j < n.h_pad; j++) n.h1[j * L + r] = H1[j * W];
+    dense_rows<1>(W2, b2, n.h_pad, n.h_pad, H1, H2, W);
+    for (int j = 0; j < n.h_pad; j++) n.h2[j * L + r] = H2[j * W];
+    dense_rows<0>(W3, b3, n.h_pad, n.out_pad, H2, X, W);
+    for (int k = 0; k < n.out_pad; k++) n.out[k * L + r] = X[k * W];
+}
+
+// phyz_train.cu:136-186, per row; the padding rows of dout are zeroed.
+__global__ void ppo_grad_kernel(const NetDev n, const PpoArgs a, const BatchCol act, const BatchCol logp_old,
+                                const BatchCol adv, const uint32_t* idx, int b, float* dlogstd, float* stats) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= b) return;
+    const long long L = n.max_b;
+    const long long s = idx[r];
+    const float LN_2PI = 1.8378770664093453f;
+    const float* logstd = n.wflat + a.logstd_off;
+    float logp = 0.0f;
+    for (int d = 0; d < n.n_out; d++) {
+        const float sd = expf(logstd[d]);
+        const float z = (col(act, s, d) - n.out[d * L + r]) / sd;
+        logp += -0.5f * z * z - logf(sd) - 0.5f * LN_2PI;
+    }
+    const float av = col(adv, s, 0);
+    const float lpo = col(logp_old, s, 0);
+    const float log_ratio = logp - lpo;
+    const float ratio = expf(log_ratio);
+    const float clipped = fminf(fmaxf(ratio, 1.0f - a.clip), 1.0f + a.clip);
+    const float unclipped_obj = ratio * av;
+    const float clipped_obj = clipped * av;
+    stats[0 * L + r] = -(unclipped_obj < clipped_obj ? unclipped_obj : clipped_obj);
+    stats[1 * L + r] = lpo - logp;
+    stats[2 * L + r] = ratio - 1.0f - log_ratio;
+    const bool active = unclipped_obj <= clipped_obj + 1e-12f;
+    const float ent = a.entropy_coef / (float)b;
+    for (int d = 0; d < n.out_pad; d++) {
+        if (d >= n.n_out) {
+            n.dout[d * L + r] = 0.0f;
+            continue;
+        }
+        if (!active) {
+            n.dout[d * L + r] = 0.0f;
+            dlogstd[d * L + r] = -ent;
+            continue;
+        }
+        const float coef = -av * ratio / (float)b;
+        const float sd = expf(logstd[d]);
+        const float z = (col(act, s, d) - n.out[d * L + r]) / sd;
+        n.dout[d * L + r] = coef * (z / sd);
+        dlogstd[d * L + r] = coef * (z * z - 1.0f) - ent;
+    }
+}
+
+// phyz_train.cu:193-203, per row.
+__global__ void value_grad_kernel(const NetDev n, const PpoArgs a, const BatchCol ret, const uint32_t* idx, int b,
+                                  float* stats) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= b) return;
+    const long long L = n.max_b;
+    const float err = n.out[r] - col(ret, idx[r], 0);
+    stats[3 * L + r] = err * err;
+    const float d = fminf(fmaxf(err, -a.vdelta), a.vdelta);
+    n.dout[r] = 2.0f * d / (float)b;
+    for (int k = 1; k < n.out_pad; k++) n.dout[k * L + r] = 0.0f;
+}
+
+// Both hidden layers of the backward pass for one row (phyz_train.cu:213-224
+// twice): dh2 = (W3^T dout) (1 - h2^2), dh1 = (W2^T dh2) (1 - h1^2).
+__global__ void __launch_bounds__(ROW_BLOCK) bwd_kernel(const NetDev n, int b) {
+    extern __shared__ __align__(16) float sm[];
+    const int W = blockDim.x;
+    stage(n.wb, n.n_wb, sm);
+    const float* W3 = sm;                        // [out_pad][h_pad]
+    const float* W2 = W3 + n.out_pad * n.h_pad;  // [h_pad][h_pad]
+    float* D = sm + n.n_wb + threadIdx.x;
+    float* G2 = D + n.out_pad * W;
+    float* G1 = G2 + n.h_pad * W;
+    const int r = blockIdx.x * W + threadIdx.x;
+    if (r >= b) return;
+    const long long L = n.max_b;
+    for (int k = 0; k < n.out_pad; k++) D[k * W] = n.dout[k * L + r];
+    dense_rows<0>(W3, nullptr, n.out_pad, n.h_pad, D, G2, W);
+    for (int j = 0; j < n.h_pad; j++) {
+        const float h = n.h2[j * L + r];
+        const float g = G2[j * W] * (1.0f - h * h);
+        G2[j * W] = g;
+        n.dh2[j * L + r] = g;
+    }
+    dense_rows<0>(W2, nullptr, n.h_pad, n.h_pad, G2, G1, W);
+    for (int j = 0; j < n.h_pad; j++) {
+        const float h = n.h1[j * L + r];
+        n.dh1[j * L + r] = G1[j * W] * (1.0f - h * h);
+    }
+}
+
+// Split-K partial sums part[split][m][n] = sum over the split's rows of
+// A[m][r] * Bv(r, n), n < N; column N is the bias (Bv = 1). A is SoA
+// [M][lda]; Bv is SoA activations [N][ldb] or, with gather, batch column x
+// at sample idx[r].
+__global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int M, const float* Bact, int ldb,
+                                                   BatchCol x, const uint32_t* idx, int gather, int N, int b,
+                                                   double* part) {
+    __shared__ float As[GK][GT + 1];
+    __shared__ float Bs[GK][GT + 1];
+    const int m0 = blockIdx.x * GT, n0 = blockIdx.y * GT, split = blockIdx.z;
+    const int r0 = split * GKC;
+    const int r1 = min(b, r0 + GKC);
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    double acc00 = 0.0, acc01 = 0.0, acc10 = 0.0, acc11 = 0.0;
+    for (int rs = r0; rs < r1; rs += GK) {
+        for (int e = threadIdx.x; e < GT * GK; e += blockDim.x) {
+            const int mm = e / GK, kk = e % GK, r = rs + kk;
+            const int m = m0 + mm;
+            As[kk][mm] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
+            const int nn = mm, n = n0 + nn;
+            float bv = 0.0f;
+            if (r < r1) {
+                if (n < N)
+                    bv = gather ? col(x, idx[r], n) : Bact[(long long)n * ldb + r];
+                else if (n == N)
+                    bv = 1.0f;
+            }
+            Bs[kk][nn] = bv;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < GK; kk++) {
+            const double a0 = As[kk][2 * ty], a1 = As[kk][2 * ty + 1];
+            const double b0 = Bs[kk][2 * tx], b1 = Bs[kk][2 * tx + 1];
+            acc00 = fma(a0, b0, acc00);
+            acc01 = fma(a0, b1, acc01);
+            acc10 = fma(a1, b0, acc10);
+            acc11 = fma(a1, b1, acc11);
+        }
+        __syncthreads();
+    }
+    const int N1 = N + 1;
+    const double acc[2][2] = {{acc00, acc01}, {acc10, acc11}};
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const int m = m0 + 2 * ty + i, n = n0 + 2 * tx + j;
+            if (m < M && n <= N) part[((long long)split * M + m) * N1 + n] = acc[i][j];
+        }
+}
+
+// g[off_w + m * N + n] (n < N) and g[off_b + m] (bias) from the splits, in
+// split order.
+__global__ void grad_reduce_kernel(const double* part, int nsplit, int M, int N, float* g, int off_w, int off_b) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const int N1 = N + 1;
+    if (t >= M * N1) return;
+    const int m = t / N1, n = t % N1;
+    double s = 0.0;
+    for (int k = 0; k < nsplit; k++) s += part[((long long)k * M + m) * N1 + n];
+    if (n < N)
+        g[off_w + m * N + n] = (float)s;
+    else
+        g[off_b + m] = (float)s;
+}
+
+// tang's ModuleAdam step (phyz_train.cu:260-276) on the f64 master, then the
+// f32 mirrors the forward, backward and log_std readers use.
+__global__ void adam_kernel(const NetDev n, double lr, double beta1, double beta2, double eps, double wd,
+                            double bc1, double bc2) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n.n_param) return;
+    double x = n.p[t];
+    if (wd > 0.0) x = x * (1.0 - lr * wd);
+    const double gr = (double)n.g[t];
+    const double mt = beta1 * n.m[t] + (1.0 - beta1) * gr;
+    const double vt = beta2 * n.v[t] + (1.0 - beta2) * gr * gr;
+    n.m[t] = mt;
+    n.v[t] = vt;
+    const double m_hat = mt / bc1;
+    const double v_hat = vt / bc2;
+    x -= lr * m_hat / (sqrt(v_hat) + eps);
+    n.p[t] = x;
+    const float xf = (float)x;
+    n.wflat[t] = xf;
+    if (n.posf[t] >= 0) n.wf[n.posf[t]] = xf;
+    if (n.posb[t] >= 0) n.wb[n.posb[t]] = xf;
+}
+
+// out[c] = sum_r stats[c][r], f64, one block per column, fixed tree order.
+__global__ void stats_kernel(const float* stats, int ld, int b, float* out) {
+    __shared__ double red[256];
+    const int c = blockIdx.x;
+    double s = 0.0;
+    for (int r = threadIdx.x; r < b; r += blockDim.x) s += (double)stats[(long long)c * ld + r];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[c] = (float)red[0];
+}
+
+int row_smem(int packed, int per_row, int W) { return (packed + per_row * W) * (int)sizeof(float); }
+
+// Samples per block of a per-row kernel: the largest of 128 / 64 / 32 whose
+// staged weights and per-row vectors fit the opt-in shared memory.
+cudaError_t row_block(int packed, int per_row, int* W_out, int* smem_out) {
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
+    for (int W = ROW_BLOCK; W >= 32; W /= 2)
+        if (row_smem(packed, per_row, W) <= optin) {
+            *W_out = W;
+            *smem_out = row_smem(packed, per_row, W);
+            return cudaSuccess;
+        }
+    return cudaErrorInvalidConfiguration;
+}
+
+cudaError_t grad(const float* A, int lda, int M, const float* Bact, int ldb, BatchCol x, const uint32_t* idx,
+                 int gather, int N, int b, float* g, int off_w, int off_b, double* work, cudaStream_t s) {
+    const int nsplit = (b + GKC - 1) / GKC;
+    dim3 grid((unsigned)((M + GT - 1) / GT), (unsigned)((N + 1 + GT - 1) / GT), (unsigned)nsplit);
+    grad_kernel<<<grid, 256, 0, s>>>(A, lda, M, Bact, ldb, x, idx, gather, N, b, work);
+    const int tot = M * (N + 1);
+    grad_reduce_kernel<<<(tot + 255) / 256, 256, 0, s>>>(work, nsplit, M, N, g, off_w, off_b);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t train_work_bytes(int max_b, int max_rows, int max_cols) {
+    const size_t nsplit = (size_t)(max_b + GKC - 1) / GKC;
+    return nsplit * (size_t)max_rows * (size_t)(max_cols + 1) * sizeof(double);
+}
+
+cudaError_t train_forward(const NetDev& n, BatchCol x, const uint32_t* idx, int b, cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    int W = 0, smem = 0;
+    cudaError_t e = row_block(n.n_wf, n.in_pad + 2 * n.h_pad, &W, &smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    fwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, x, idx, b);
+    return cudaGetLastError();
+}
+
+cudaError_t train_ppo_grad(const NetDev& actor, const PpoArgs& a, BatchCol act, BatchCol logp_old, BatchCol adv,
+                           const uint32_t* idx, int b, float* dlogstd, float* stats, cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    ppo_grad_kernel<<<(b + 127) / 128, 128, 0, s>>>(actor, a, act, logp_old, adv, idx, b, dlogstd, stats);
+    return cudaGetLastError();
+}
+
+cudaError_t train_value_grad(const NetDev& critic, const PpoArgs& a, BatchCol ret, const uint32_t* idx, int b,
+                             float* stats, cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    value_grad_kernel<<<(b + 127) / 128, 128, 0, s>>>(critic, a, ret, idx, b, stats);
+    return cudaGetLastError();
+}
+
+cudaError_t train_backward(const NetDev& n, BatchCol x, const uint32_t* idx, int b, double* work, cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    const long long L = n.max_b;
+    // flat offsets (tang's Mlp::to_flat): W1 b1 W2 b2 W3 b3
+    const int oW1 = 0, ob1 = n.n_h * n.n_in, oW2 = ob1 + n.n_h, ob2 = oW2 + n.n_h * n.n_h, oW3 = ob2 + n.n_h,
+              ob3 = oW3 + n.n_out * n.n_h;
+    // layer 3: input h2
+    cudaError_t e = grad(n.dout, (int)L, n.n_out, n.h2, (int)L, x, idx, 0, n.n_h, b, n.g, oW3, ob3, work, s);
+    if (e != cudaSuccess) return e;
+    int W = 0, smem = 0;
+    if ((e = row_block(n.n_wb, n.out_pad + 2 * n.h_pad, &W, &smem)) != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    bwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, b);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // layer 2: input h1; layer 1: input the batch rows
+    e = grad(n.dh2, (int)L, n.n_h, n.h1, (int)L, x, idx, 0, n.n_h, b, n.g, oW2, ob2, work, s);
+    if (e != cudaSuccess) return e;
+    return grad(n.dh1, (int)L, n.n_h, nullptr, 0, x, idx, 1, n.n_in, b, n.g, oW1, ob1, work, s);
+}
+
+cudaError_t train_row_sums(const float* rows, int nrows, int ld, int b, float* g, int off, double* work,
+                           cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    return grad(rows, ld, nrows, nullptr, 0, BatchCol{nullptr, 1, 1}, nullptr, 0, 0, b, g, 0, off, work, s);
+}
+
+cudaError_t train_adam(const NetDev& n, double lr, double beta1, double beta2, double eps, double wd, double bc1,
+                       double bc2, cudaStream_t s) {
+    adam_kernel<<<(n.n_param + 255) / 256, 256, 0, s>>>(n, lr, beta1, beta2, eps, wd, bc1, bc2);
+    return cudaGetLastError();
+}
+
+cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s) {
+    stats_kernel<<<4, 256, 0, s>>>(stats, ld, b, out);
+    return cudaGetLastError();
+}
+
+}  // namespace pz
