@@ -329,6 +329,7 @@ int phyzb_readback_kinematics(phyzb_sim* sim, double* xforms);
  * three-layer tanh MLP actor (with a trailing log_std block) and critic,
  * Adam with f64 master parameters and moments, on the device. */
 typedef struct phyzb_trainer phyzb_trainer;
+typedef struct phyzb_comm phyzb_comm;
 typedef struct {
     int32_t n_in, n_h, n_out; /* n_h <= 128, n_out <= 32 */
 } phyzb_net_dims;
@@ -367,6 +368,56 @@ int phyzb_trainer_upload_batch(phyzb_trainer* tr, int64_t n_rows, const float* o
 int phyzb_trainer_update(phyzb_trainer* tr, const uint32_t* order, int32_t n_orders, const phyzb_ppo_cfg* cfg,
                          phyzb_update_stats* out);
 
+/* A column block of per-sample device data: rows r = t * block + w, feature
+ * k of row r at base[(r / block) * features * block + k * block + r % block]
+ * (the policy history's [step][feature][world]: block = nworld). */
+typedef struct {
+    const float* base;
+    int64_t block;
+    int32_t features;
+} phyzb_batch_col;
+/* The update's batch from device memory instead of upload_batch: columns
+ * obs_a, obs_c, act, logp_old, adv, ret, n_rows rows each (not copied). */
+int phyzb_trainer_set_batch_device(phyzb_trainer* tr, int64_t n_rows, const phyzb_batch_col* cols /* 6 */);
+/* update with one device-generated permutation per epoch (an affine map
+ * (a k + c) mod n_rows, a coprime with n_rows, from `seed`). */
+int phyzb_trainer_update_shuffled(phyzb_trainer* tr, const phyzb_ppo_cfg* cfg, uint64_t seed,
+                                  phyzb_update_stats* out);
+/* Network `which` (0 actor, 1 critic) on n_rows rows of x; outputs to the
+ * device array out [n_out][n_rows]. */
+int phyzb_trainer_evaluate(phyzb_trainer* tr, int32_t which, phyzb_batch_col x, int64_t n_rows, float* out);
+/* Data-parallel updates: every gradient and minibatch statistic is summed
+ * over the communicator's ranks (NCCL) before Adam and the KL brake, so the
+ * ranks' networks stay identical. NULL = one rank. */
+int phyzb_trainer_set_comm(phyzb_trainer* tr, struct phyzb_comm* comm);
+
+/* Device pointers of a simulator's policy history: obs [steps][n_obs][nworld],
+ * out [steps][n_act + 1][nworld] (actions, then log-prob). */
+typedef struct {
+    float* obs;
+    float* out;
+    int32_t n_obs, n_act;
+    int64_t nworld;
+    int32_t steps;
+} phyzb_policy_history;
+int phyzb_policy_history_view(phyzb_sim* sim, phyzb_policy_history* out);
+/* Returns of a rollout of `steps` control steps (history rows 0..steps):
+ * reward r_t = reward_coef . obs_{t+1} - action_penalty |a_t|^2, critic
+ * values of rows 0..steps, GAE(gamma, lambda), advantages normalized over
+ * every rank when `normalize` (the sums go through `comm`, NULL = one rank).
+ * adv, ret: device arrays [steps][nworld]. stats (optional, 3): mean return
+ * per world over all ranks, advantage mean and std before normalization. */
+typedef struct {
+    const double* reward_coef; /* n_obs */
+    double action_penalty, gamma, lambda;
+    int32_t steps, normalize;
+} phyzb_return_cfg;
+int phyzb_policy_advantages(phyzb_sim* sim, phyzb_trainer* tr, struct phyzb_comm* comm, const phyzb_return_cfg* cfg,
+                            float* adv, float* ret, double* stats);
+/* The trainer's actor (weights, std = exp(log_std)) into the simulator's
+ * policy, device to device. */
+int phyzb_policy_sync_from_trainer(phyzb_sim* sim, phyzb_trainer* tr);
+
 /* ── multi-GPU: one process per GPU, worlds sharded contiguously ──────── */
 
 /* Worlds are independent, so ranks exchange nothing per step; the one
@@ -374,7 +425,6 @@ int phyzb_trainer_update(phyzb_trainer* tr, const uint32_t* order, int32_t n_ord
  * at the end of a rollout (NCCL over NVLink; the reduction phyz-gpu's
  * callers do on the host). NCCL is loaded at run time. */
 #define PHYZB_COMM_ID_BYTES 128
-typedef struct phyzb_comm phyzb_comm;
 /* Rank 0 creates the communicator id and hands the bytes to the other
  * ranks (any host channel: a store, an MPI/torch broadcast). */
 int phyzb_comm_unique_id(uint8_t* id_out /* PHYZB_COMM_ID_BYTES */);

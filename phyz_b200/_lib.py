@@ -132,6 +132,20 @@ class PhyzbUpdateStats(C.Structure):
                 ("grad_steps", C.c_int32), ("stopped_early", C.c_int32)]
 
 
+class PhyzbBatchCol(C.Structure):
+    _fields_ = [("base", C.c_void_p), ("block", C.c_int64), ("features", C.c_int32)]
+
+
+class PhyzbPolicyHistory(C.Structure):
+    _fields_ = [("obs", C.c_void_p), ("out", C.c_void_p), ("n_obs", C.c_int32), ("n_act", C.c_int32),
+                ("nworld", C.c_int64), ("steps", C.c_int32)]
+
+
+class PhyzbReturnCfg(C.Structure):
+    _fields_ = [("reward_coef", C.POINTER(C.c_double)), ("action_penalty", C.c_double), ("gamma", C.c_double),
+                ("lambda_", C.c_double), ("steps", C.c_int32), ("normalize", C.c_int32)]
+
+
 KINEMATICS_STRIDE = 18
 
 _P = C.c_void_p
@@ -189,6 +203,14 @@ SIGNATURES = {
     "phyzb_trainer_upload_batch": (C.c_int, [_P, C.c_int64, _FP, _FP, _FP, _FP, _FP, _FP]),
     "phyzb_trainer_update": (C.c_int, [_P, C.POINTER(C.c_uint32), C.c_int32, C.POINTER(PhyzbPpoCfg),
                                        C.POINTER(PhyzbUpdateStats)]),
+    "phyzb_trainer_set_batch_device": (C.c_int, [_P, C.c_int64, C.POINTER(PhyzbBatchCol)]),
+    "phyzb_trainer_update_shuffled": (C.c_int, [_P, C.POINTER(PhyzbPpoCfg), C.c_uint64,
+                                                C.POINTER(PhyzbUpdateStats)]),
+    "phyzb_trainer_evaluate": (C.c_int, [_P, C.c_int32, PhyzbBatchCol, C.c_int64, C.c_void_p]),
+    "phyzb_trainer_set_comm": (C.c_int, [_P, _P]),
+    "phyzb_policy_history_view": (C.c_int, [_P, C.POINTER(PhyzbPolicyHistory)]),
+    "phyzb_policy_advantages": (C.c_int, [_P, _P, _P, C.POINTER(PhyzbReturnCfg), C.c_void_p, C.c_void_p, _D]),
+    "phyzb_policy_sync_from_trainer": (C.c_int, [_P, _P]),
     "phyzb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "phyzb_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                   C.POINTER(_P)]),

@@ -292,6 +292,29 @@ class BatchSim:
         check(self._lib.phyzb_readback_kinematics(self._h, dptr(xf)))
         return xf
 
+    def policy_history_view(self) -> dict:
+        h = _lib.PhyzbPolicyHistory()
+        check(self._lib.phyzb_policy_history_view(self._h, C.byref(h)))
+        return {"obs": h.obs, "out": h.out, "n_obs": h.n_obs, "n_act": h.n_act, "nworld": h.nworld,
+                "steps": h.steps}
+
+    def policy_advantages(self, trainer, comm, reward_coef, action_penalty: float, gamma: float, lam: float,
+                          steps: int, adv_ptr: int, ret_ptr: int, normalize: bool = True):
+        """Rewards, critic values, GAE and (global) advantage normalization of
+        the last `steps` control steps, on the device. Returns (mean return
+        per world, advantage mean, advantage std) over every rank."""
+        coef = np.ascontiguousarray(reward_coef, np.float64)
+        cfg = _lib.PhyzbReturnCfg(dptr(coef), float(action_penalty), float(gamma), float(lam), int(steps),
+                                  int(bool(normalize)))
+        st = np.zeros(3)
+        check(self._lib.phyzb_policy_advantages(self._h, trainer._h, comm._h if comm is not None else None,
+                                                C.byref(cfg), C.c_void_p(int(adv_ptr)), C.c_void_p(int(ret_ptr)),
+                                                dptr(st)))
+        return tuple(st)
+
+    def policy_sync_from_trainer(self, trainer) -> None:
+        check(self._lib.phyzb_policy_sync_from_trainer(self._h, trainer._h))
+
     def flops_per_world_step(self):
         f, t = C.c_double(), C.c_double()
         check(self._lib.phyzb_flops_per_world_step(self._h, C.byref(f), C.byref(t)))

@@ -714,6 +714,7 @@ struct phyzb_comm {
     ncclComm_t comm = nullptr;
     int nranks = 0, rank = 0, device = 0;
     bool broken = false;
+    cudaEvent_t ev = nullptr;  // comm_wait
 };
 
 namespace {
@@ -743,6 +744,59 @@ int comm_settle(phyzb_comm* c, double timeout_s, const char* what) {
     }
 }
 
+
+}  // namespace
+
+namespace pzc {
+
+int comm_nranks(const phyzb_comm* c) { return c ? c->nranks : 1; }
+
+int comm_allreduce_sum(phyzb_comm* c, void* buf, size_t count, bool f64, cudaStream_t stream) {
+    if (!c) return PHYZB_OK;
+    if (c->broken) return fail(PHYZB_ERR_COMM, "communicator was aborted by an earlier failure");
+    NcclApi& n = nccl();
+    const ncclResult_t r = n.AllReduce(buf, buf, count, f64 ? ncclFloat64 : ncclFloat32, ncclSum, c->comm, stream);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        n.CommAbort(c->comm);
+        c->broken = true;
+        return fail(PHYZB_ERR_COMM, "ncclAllReduce: " + nccl_msg(r));
+    }
+    return comm_settle(c, 60.0, "all-reduce (enqueue)");
+}
+
+int comm_wait(phyzb_comm* c, cudaStream_t stream, double timeout_s) {
+    if (!c) {
+        PZ_CUDA(cudaStreamSynchronize(stream));
+        return PHYZB_OK;
+    }
+    NcclApi& n = nccl();
+    if (!c->ev) PZ_CUDA(cudaEventCreateWithFlags(&c->ev, cudaEventDisableTiming));
+    PZ_CUDA(cudaEventRecord(c->ev, stream));
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaEventQuery(c->ev);
+        if (q == cudaSuccess) return PHYZB_OK;
+        if (q != cudaErrorNotReady) PZ_CUDA(q);
+        ncclResult_t st = ncclSuccess;
+        n.CommGetAsyncError(c->comm, &st);
+        if (st != ncclSuccess && st != ncclInProgress) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, "collective failed: " + nccl_msg(st));
+        }
+        if (seconds_since(t0) > timeout_s) {
+            n.CommAbort(c->comm);
+            c->broken = true;
+            return fail(PHYZB_ERR_COMM, "collective timed out after " + std::to_string(timeout_s) +
+                                            " s (a rank did not take part)");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+}  // namespace pzc
+
+namespace {
 }  // namespace
 
 extern "C" {
@@ -806,6 +860,7 @@ int phyzb_comm_destroy(phyzb_comm* c) {
         else
             n.CommDestroy(c->comm);
     }
+    if (c->ev) cudaEventDestroy(c->ev);
     delete c;
     return PHYZB_OK;
 }

@@ -50,7 +50,36 @@ struct DeviceGuard {
 
 }  // namespace pzc
 
-struct PolicyDev;  // the on-device control loop's buffers (capi_policy.cu)
+// The on-device control loop's buffers (capi_policy.cu).
+struct PolicyDev {
+    // spec
+    int n_in = 0, n_h = 0, n_out = 0, history = 0;
+    int in_pad = 0, h_pad = 0, out_pad = 0, n_wf = 0;
+    float rho = 0.0f;
+    // device buffers
+    void* fk = nullptr;     // FkBody<T>[nb]
+    float* d_ops = nullptr;
+    float* d_aux = nullptr;
+    float* d_com = nullptr;  // [nb][4]
+    float* d_w = nullptr;    // packed weights
+    float* d_std = nullptr;
+    float* d_noise = nullptr;
+    int* d_slots = nullptr;
+    float* d_clamp = nullptr;
+    unsigned long long* d_rng = nullptr;
+    float* d_z = nullptr;      // [n_out][nworld]
+    void* d_base = nullptr;    // T [npd][nworld]
+    void* d_xf = nullptr;      // T [nb * 18][nworld]
+    float* d_obs = nullptr;    // [history][n_in][nworld]
+    float* d_out = nullptr;    // [history][n_out + 1][nworld]
+    void* d_rows = nullptr;    // readback transpose buffer
+    size_t rows_bytes = 0;
+    void* d_ret_scratch = nullptr;  // phyzb_policy_advantages: sums, rewards, values, coefficients
+    size_t ret_bytes = 0;
+    bool has_weights = false, has_std = false;
+};
+
+struct phyzb_comm;  // NCCL communicator (capi.cu)
 
 struct phyzb_sim {
     int device = 0, precision = PHYZB_F64;
@@ -103,5 +132,11 @@ int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps);
 int upload_rows(phyzb_sim* s, const double* host, int width, void* dst);
 int download_rows(phyzb_sim* s, const void* src, int width, double* host);
 void destroy_policy(phyzb_sim* s);  // capi_policy.cu
+// NCCL (capi.cu): sum all-reduce of `count` f32 / f64 values in place, enqueued
+// on `stream`; and a bounded wait for everything enqueued on `stream` so far
+// (the communicator is aborted on failure or timeout).
+int comm_allreduce_sum(phyzb_comm* c, void* buf, size_t count, bool f64, cudaStream_t stream);
+int comm_wait(phyzb_comm* c, cudaStream_t stream, double timeout_s);
+int comm_nranks(const phyzb_comm* c);
 
 }  // namespace pzc

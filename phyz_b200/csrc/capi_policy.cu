@@ -14,40 +14,15 @@
 
 using namespace pzc;
 
-struct PolicyDev {
-    // spec
-    int n_in = 0, n_h = 0, n_out = 0, history = 0;
-    int in_pad = 0, h_pad = 0, out_pad = 0, n_wf = 0;
-    float rho = 0.0f;
-    std::vector<float> ops, aux;
-    // device buffers
-    void* fk = nullptr;     // FkBody<T>[nb]
-    float* d_ops = nullptr;
-    float* d_aux = nullptr;
-    float* d_com = nullptr;  // [nb][4]
-    float* d_w = nullptr;    // packed weights
-    float* d_std = nullptr;
-    float* d_noise = nullptr;
-    int* d_slots = nullptr;
-    float* d_clamp = nullptr;
-    unsigned long long* d_rng = nullptr;
-    float* d_z = nullptr;      // [n_out][nworld]
-    void* d_base = nullptr;    // T [npd][nworld]
-    void* d_xf = nullptr;      // T [nb * 18][nworld]
-    float* d_obs = nullptr;    // [history][n_in][nworld]
-    float* d_out = nullptr;    // [history][n_out + 1][nworld]
-    void* d_rows = nullptr;    // readback transpose buffer
-    size_t rows_bytes = 0;
-    bool has_weights = false, has_std = false;
-};
 
 namespace pzc {
 
 void destroy_policy(phyzb_sim* s) {
     PolicyDev* p = s->policy;
     if (!p) return;
-    void* bufs[] = {p->fk,      p->d_ops, p->d_aux, p->d_com, p->d_w,    p->d_std, p->d_noise, p->d_slots,
-                    p->d_clamp, p->d_rng, p->d_z,   p->d_base, p->d_xf, p->d_obs, p->d_out,  p->d_rows};
+    void* bufs[] = {p->fk,    p->d_ops,  p->d_aux, p->d_com, p->d_w,   p->d_std,  p->d_noise,
+                    p->d_slots, p->d_clamp, p->d_rng, p->d_z, p->d_base, p->d_xf, p->d_obs,
+                    p->d_out, p->d_rows, p->d_ret_scratch};
     for (void* b : bufs)
         if (b) cudaFree(b);
     delete p;

@@ -146,6 +146,11 @@ struct phyzb_trainer {
     float* reduced = nullptr;  // [4]
     float* reduced_host = nullptr;
     double* work = nullptr;
+    // the batch the update reads: the uploaded columns, or device arrays
+    // (phyzb_trainer_set_batch_device)
+    pz::BatchCol c_obs_a{}, c_obs_c{}, c_act{}, c_logp{}, c_adv{}, c_ret{};
+    phyzb_comm* comm = nullptr;  // data-parallel: gradients and statistics summed over ranks
+    unsigned long long* ac = nullptr;  // device order parameters
 };
 
 namespace {
@@ -156,8 +161,8 @@ void destroy_trainer(phyzb_trainer* t) {
     if (t->stream) cudaStreamSynchronize(t->stream);
     free_net(t->actor);
     free_net(t->critic);
-    void* bufs[] = {t->obs_a, t->obs_c, t->act,     t->logp,    t->adv, t->ret,
-                    t->upload_raw, t->order, t->dlogstd, t->stats, t->reduced, t->work};
+    void* bufs[] = {t->obs_a, t->obs_c,   t->act,   t->logp,    t->adv,  t->ret,  t->upload_raw,
+                    t->order, t->dlogstd, t->stats, t->reduced, t->work, t->ac};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (t->reduced_host) cudaFreeHost(t->reduced_host);
@@ -180,12 +185,91 @@ int upload_col(phyzb_trainer* t, const float* host, int F, long long n, float* d
     return PHYZB_OK;
 }
 
+// One Adam step of `n`; data-parallel: the gradient is first summed over the
+// ranks and averaged inside the step.
 int adam_step(phyzb_trainer* t, Net& n) {
+    PZ_TRY(comm_allreduce_sum(t->comm, n.d.g, (size_t)n.d.n_param, false, t->stream));
     n.t += 1;
     const phyzb_adam_cfg& a = n.adam;
     const double bc1 = 1.0 - std::pow(a.beta1, (double)n.t);
     const double bc2 = 1.0 - std::pow(a.beta2, (double)n.t);
-    PZ_CUDA(pz::train_adam(n.d, a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, bc1, bc2, t->stream));
+    const double gscale = 1.0 / comm_nranks(t->comm);
+    PZ_CUDA(pz::train_adam(n.d, a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, bc1, bc2, gscale, t->stream));
+    return PHYZB_OK;
+}
+
+// The update loop of train.rs:655-795 over `t->order` (epochs x n_rows,
+// already on the device).
+int run_update(phyzb_trainer* t, const phyzb_ppo_cfg* cfg, phyzb_update_stats* out) {
+    const long long N = t->n_rows;
+    pz::PpoArgs pa{(float)cfg->clip, (float)cfg->entropy_coef, (float)cfg->vdelta, t->actor.mlp_params};
+    double policy_acc = 0, value_acc = 0, brake_acc = 0, kl_acc = 0;
+    long long kl_rows = 0;
+    int batches = 0;
+    bool stopped = false;
+    cudaStream_t s = t->stream;
+    const int L = t->max_b;
+    const int R = comm_nranks(t->comm);
+    for (int ep = 0; ep < cfg->epochs && !stopped; ep++) {
+        for (long long start = 0; start < N; start += cfg->minibatch) {
+            const int b = (int)std::min<long long>(cfg->minibatch, N - start);
+            const uint32_t* idx = t->order + (size_t)ep * N + start;
+            // actor
+            PZ_CUDA(pz::train_forward(t->actor.d, t->c_obs_a, idx, b, s));
+            PZ_CUDA(pz::train_ppo_grad(t->actor.d, pa, t->c_act, t->c_logp, t->c_adv, idx, b, t->dlogstd, t->stats,
+                                       s));
+            PZ_CUDA(pz::train_row_sums(t->dlogstd, t->actor.d.n_out, L, b, t->actor.d.g, pa.logstd_off, t->work, s));
+            PZ_CUDA(pz::train_backward(t->actor.d, t->c_obs_a, idx, b, t->work, s));
+            PZ_TRY(adam_step(t, t->actor));
+            // critic
+            PZ_CUDA(pz::train_forward(t->critic.d, t->c_obs_c, idx, b, s));
+            PZ_CUDA(pz::train_value_grad(t->critic.d, pa, t->c_ret, idx, b, t->stats, s));
+            PZ_CUDA(pz::train_backward(t->critic.d, t->c_obs_c, idx, b, t->work, s));
+            PZ_TRY(adam_step(t, t->critic));
+            // the brake: the minibatch's statistics (summed over ranks) to the host
+            PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, s));
+            PZ_TRY(comm_allreduce_sum(t->comm, t->reduced, 4, false, s));
+            PZ_CUDA(cudaMemcpyAsync(t->reduced_host, t->reduced, 16, cudaMemcpyDeviceToHost, s));
+            PZ_TRY(comm_wait(t->comm, s, 120.0));
+            const float* r = t->reduced_host;
+            const double rows = (double)b * R;
+            const double ploss = r[0], kl_sum = r[1], k3_sum = r[2], vloss = r[3];
+            policy_acc += ploss / rows;
+            value_acc += vloss / rows;
+            kl_acc += kl_sum;
+            kl_rows += (long long)b * R;
+            const double brake =
+                (cfg->kl_mode == PHYZB_KL_CUMULATIVE ? std::fabs(kl_acc / (double)std::max<long long>(kl_rows, 1))
+                                                     : k3_sum / rows) /
+                cfg->kl_scale;
+            brake_acc += brake;
+            batches++;
+            if (brake > cfg->target_kl) {
+                stopped = true;
+                break;
+            }
+        }
+    }
+    const double nb = std::max(batches, 1);
+    *out = phyzb_update_stats{policy_acc / nb, value_acc / nb, brake_acc / nb, batches, stopped ? 1 : 0};
+    return PHYZB_OK;
+}
+
+int ensure_order(phyzb_trainer* t, size_t bytes) {
+    if (bytes <= t->order_cap) return PHYZB_OK;
+    if (t->order) cudaFree(t->order);
+    t->order = nullptr;
+    t->order_cap = 0;
+    PZ_CUDA(cudaMalloc((void**)&t->order, bytes));
+    t->order_cap = bytes;
+    return PHYZB_OK;
+}
+
+int check_update(phyzb_trainer* t, const phyzb_ppo_cfg* cfg) {
+    if (cfg->minibatch < 1 || cfg->minibatch > t->max_b)
+        return fail(PHYZB_ERR_INVALID, "minibatch " + std::to_string(cfg->minibatch) + " exceeds the pipeline's " +
+                                           std::to_string(t->max_b));
+    if (cfg->epochs < 0) return fail(PHYZB_ERR_INVALID, "epochs must be >= 0");
     return PHYZB_OK;
 }
 
@@ -296,6 +380,12 @@ int phyzb_trainer_upload_batch(phyzb_trainer* t, int64_t n, const float* obs_a, 
     PZ_TRY(upload_col(t, ret, 1, n, t->ret));
     PZ_CUDA(cudaStreamSynchronize(t->stream));
     t->n_rows = n;
+    t->c_obs_a = pz::BatchCol{t->obs_a, std::max<long long>(n, 1), t->actor.d.n_in};
+    t->c_obs_c = pz::BatchCol{t->obs_c, std::max<long long>(n, 1), t->critic.d.n_in};
+    t->c_act = pz::BatchCol{t->act, std::max<long long>(n, 1), t->actor.d.n_out};
+    t->c_logp = pz::BatchCol{t->logp, std::max<long long>(n, 1), 1};
+    t->c_adv = pz::BatchCol{t->adv, std::max<long long>(n, 1), 1};
+    t->c_ret = pz::BatchCol{t->ret, std::max<long long>(n, 1), 1};
     return PHYZB_OK;
 }
 
@@ -305,9 +395,7 @@ int phyzb_trainer_update(phyzb_trainer* t, const uint32_t* order, int32_t n_orde
     *out = phyzb_update_stats{0.0, 0.0, 0.0, 0, 0};
     const long long N = t->n_rows;
     if (N == 0) return PHYZB_OK;
-    if (cfg->minibatch < 1 || cfg->minibatch > t->max_b)
-        return fail(PHYZB_ERR_INVALID, "minibatch " + std::to_string(cfg->minibatch) + " exceeds the pipeline's " +
-                                           std::to_string(t->max_b));
+    PZ_TRY(check_update(t, cfg));
     if (n_orders < cfg->epochs || !order)
         return fail(PHYZB_ERR_INVALID, std::to_string(n_orders) + " shuffles for " + std::to_string(cfg->epochs) +
                                            " epochs");
@@ -315,62 +403,198 @@ int phyzb_trainer_update(phyzb_trainer* t, const uint32_t* order, int32_t n_orde
         if (order[k] >= N) return fail(PHYZB_ERR_INVALID, "shuffle index out of range");
     DeviceGuard g(t->device);
     const size_t obytes = (size_t)cfg->epochs * N * 4;
-    if (obytes > t->order_cap) {
-        if (t->order) cudaFree(t->order);
-        t->order = nullptr;
-        t->order_cap = 0;
-        PZ_CUDA(cudaMalloc((void**)&t->order, obytes));
-        t->order_cap = obytes;
-    }
+    PZ_TRY(ensure_order(t, obytes));
     PZ_CUDA(cudaMemcpyAsync(t->order, order, obytes, cudaMemcpyHostToDevice, t->stream));
-    const pz::BatchCol obs_a{t->obs_a, N, t->actor.d.n_in}, obs_c{t->obs_c, N, t->critic.d.n_in},
-        act{t->act, N, t->actor.d.n_out}, logp{t->logp, N, 1}, adv{t->adv, N, 1}, ret{t->ret, N, 1};
-    pz::PpoArgs pa{(float)cfg->clip, (float)cfg->entropy_coef, (float)cfg->vdelta, t->actor.mlp_params};
-    double policy_acc = 0, value_acc = 0, brake_acc = 0, kl_acc = 0;
-    long long kl_rows = 0;
-    int batches = 0;
-    bool stopped = false;
-    cudaStream_t s = t->stream;
-    const int L = t->max_b;
-    for (int ep = 0; ep < cfg->epochs && !stopped; ep++) {
-        for (long long start = 0; start < N; start += cfg->minibatch) {
-            const int b = (int)std::min<long long>(cfg->minibatch, N - start);
-            const uint32_t* idx = t->order + (size_t)ep * N + start;
-            // actor
-            PZ_CUDA(pz::train_forward(t->actor.d, obs_a, idx, b, s));
-            PZ_CUDA(pz::train_ppo_grad(t->actor.d, pa, act, logp, adv, idx, b, t->dlogstd, t->stats, s));
-            PZ_CUDA(pz::train_row_sums(t->dlogstd, t->actor.d.n_out, L, b, t->actor.d.g, pa.logstd_off, t->work, s));
-            PZ_CUDA(pz::train_backward(t->actor.d, obs_a, idx, b, t->work, s));
-            PZ_TRY(adam_step(t, t->actor));
-            // critic
-            PZ_CUDA(pz::train_forward(t->critic.d, obs_c, idx, b, s));
-            PZ_CUDA(pz::train_value_grad(t->critic.d, pa, ret, idx, b, t->stats, s));
-            PZ_CUDA(pz::train_backward(t->critic.d, obs_c, idx, b, t->work, s));
-            PZ_TRY(adam_step(t, t->critic));
-            // the brake: the minibatch's statistics back to the host
-            PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, s));
-            PZ_CUDA(cudaMemcpyAsync(t->reduced_host, t->reduced, 16, cudaMemcpyDeviceToHost, s));
-            PZ_CUDA(cudaStreamSynchronize(s));
-            const float* r = t->reduced_host;
-            const double ploss = r[0], kl_sum = r[1], k3_sum = r[2], vloss = r[3];
-            policy_acc += ploss / b;
-            value_acc += vloss / b;
-            kl_acc += kl_sum;
-            kl_rows += b;
-            const double brake =
-                (cfg->kl_mode == PHYZB_KL_CUMULATIVE ? std::fabs(kl_acc / (double)std::max<long long>(kl_rows, 1))
-                                                     : k3_sum / b) /
-                cfg->kl_scale;
-            brake_acc += brake;
-            batches++;
-            if (brake > cfg->target_kl) {
-                stopped = true;
-                break;
-            }
+    return run_update(t, cfg, out);
+}
+
+int phyzb_trainer_update_shuffled(phyzb_trainer* t, const phyzb_ppo_cfg* cfg, uint64_t seed,
+                                  phyzb_update_stats* out) {
+    if (!t || !cfg || !out) return fail(PHYZB_ERR_INVALID, "null argument");
+    *out = phyzb_update_stats{0.0, 0.0, 0.0, 0, 0};
+    const long long N = t->n_rows;
+    if (N == 0) return PHYZB_OK;
+    PZ_TRY(check_update(t, cfg));
+    DeviceGuard g(t->device);
+    // one affine permutation (a k + c) mod N per epoch, a coprime with N,
+    // drawn from a SplitMix64 stream of `seed`
+    std::vector<unsigned long long> ac(2 * (size_t)std::max(cfg->epochs, 1));
+    uint64_t z = seed;
+    auto next = [&]() {
+        z += 0x9E3779B97F4A7C15ull;
+        uint64_t x = z;
+        x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+        x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+        return x ^ (x >> 31);
+    };
+    auto gcd = [](unsigned long long a, unsigned long long b) {
+        while (b) {
+            const unsigned long long r = a % b;
+            a = b;
+            b = r;
         }
+        return a;
+    };
+    for (int e = 0; e < cfg->epochs; e++) {
+        unsigned long long a = 1;
+        if (N > 2)
+            do a = 1 + next() % (unsigned long long)(N - 1);
+            while (gcd(a, (unsigned long long)N) != 1);
+        ac[2 * e] = a;
+        ac[2 * e + 1] = next() % (unsigned long long)N;
     }
-    const double nb = std::max(batches, 1);
-    *out = phyzb_update_stats{policy_acc / nb, value_acc / nb, brake_acc / nb, batches, stopped ? 1 : 0};
+    if (!t->ac) PZ_CUDA(cudaMalloc((void**)&t->ac, 2 * 64 * sizeof(unsigned long long)));
+    if (cfg->epochs > 64) return fail(PHYZB_ERR_INVALID, "at most 64 epochs per update");
+    PZ_CUDA(cudaMemcpyAsync(t->ac, ac.data(), ac.size() * 8, cudaMemcpyHostToDevice, t->stream));
+    PZ_TRY(ensure_order(t, (size_t)cfg->epochs * N * 4));
+    PZ_CUDA(pz::train_orders(t->order, N, cfg->epochs, t->ac, t->stream));
+    return run_update(t, cfg, out);
+}
+
+int phyzb_trainer_set_batch_device(phyzb_trainer* t, int64_t n_rows, const phyzb_batch_col* cols) {
+    if (!t || !cols) return fail(PHYZB_ERR_INVALID, "null argument");
+    if (n_rows < 0) return fail(PHYZB_ERR_INVALID, "n_rows must be >= 0");
+    const int want[6] = {t->actor.d.n_in, t->critic.d.n_in, t->actor.d.n_out, 1, 1, 1};
+    for (int k = 0; k < 6; k++) {
+        if (n_rows > 0 && (!cols[k].base || cols[k].block < 1 || n_rows % cols[k].block != 0))
+            return fail(PHYZB_ERR_INVALID, "batch column " + std::to_string(k) +
+                                               ": null, or n_rows not a multiple of its block");
+        if (cols[k].features < want[k])
+            return fail(PHYZB_ERR_INVALID, "batch column " + std::to_string(k) + " has " +
+                                               std::to_string(cols[k].features) + " features, needs " +
+                                               std::to_string(want[k]));
+    }
+    if (n_rows > 0xFFFFFFFFLL) return fail(PHYZB_ERR_INVALID, "at most 2^32 - 1 rows (32-bit shuffle indices)");
+    auto bc = [](const phyzb_batch_col& c) { return pz::BatchCol{c.base, c.block, c.features}; };
+    t->c_obs_a = bc(cols[0]);
+    t->c_obs_c = bc(cols[1]);
+    t->c_act = bc(cols[2]);
+    t->c_logp = bc(cols[3]);
+    t->c_adv = bc(cols[4]);
+    t->c_ret = bc(cols[5]);
+    t->n_rows = n_rows;
+    return PHYZB_OK;
+}
+
+int phyzb_trainer_evaluate(phyzb_trainer* t, int32_t which, phyzb_batch_col x, int64_t n_rows, float* out) {
+    if (!t || !out) return fail(PHYZB_ERR_INVALID, "null argument");
+    Net* net = net_of(t, which);
+    if (!net) return fail(PHYZB_ERR_INVALID, "which must be 0 (actor) or 1 (critic)");
+    if (!x.base || x.block < 1 || x.features < net->d.n_in) return fail(PHYZB_ERR_INVALID, "bad input column");
+    DeviceGuard g(t->device);
+    const pz::BatchCol c{x.base, x.block, x.features};
+    for (long long r0 = 0; r0 < n_rows; r0 += t->max_b) {
+        const int b = (int)std::min<long long>(t->max_b, n_rows - r0);
+        PZ_CUDA(pz::train_forward(net->d, c, nullptr, b, t->stream, r0));
+        for (int k = 0; k < net->d.n_out; k++)
+            PZ_CUDA(cudaMemcpyAsync(out + (size_t)k * n_rows + r0, net->d.out + (size_t)k * t->max_b,
+                                    (size_t)b * 4, cudaMemcpyDeviceToDevice, t->stream));
+    }
+    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    return PHYZB_OK;
+}
+
+int phyzb_trainer_set_comm(phyzb_trainer* t, phyzb_comm* comm) {
+    if (!t) return fail(PHYZB_ERR_INVALID, "trainer is null");
+    t->comm = comm;
+    return PHYZB_OK;
+}
+
+// ── the collector side: a sim's policy history as the update's batch ────
+
+int phyzb_policy_history_view(phyzb_sim* s, phyzb_policy_history* out) {
+    PZ_TRY(check_sim(s));
+    if (!out) return fail(PHYZB_ERR_INVALID, "output is null");
+    if (!s->policy) return fail(PHYZB_ERR_STATE, "policy pass not enabled — call enable_policy first");
+    PolicyDev* p = s->policy;
+    out->obs = p->d_obs;
+    out->out = p->d_out;
+    out->n_obs = p->n_in;
+    out->n_act = p->n_out;
+    out->nworld = s->nworld;
+    out->steps = p->history;
+    return PHYZB_OK;
+}
+
+int phyzb_policy_advantages(phyzb_sim* s, phyzb_trainer* t, phyzb_comm* comm, const phyzb_return_cfg* cfg,
+                            float* adv, float* ret, double* stats) {
+    PZ_TRY(check_sim(s));
+    if (!t || !cfg || !adv || !ret) return fail(PHYZB_ERR_INVALID, "null argument");
+    if (!s->policy) return fail(PHYZB_ERR_STATE, "policy pass not enabled — call enable_policy first");
+    PolicyDev* p = s->policy;
+    const int T = cfg->steps;
+    if (T < 1 || T + 1 > p->history)
+        return fail(PHYZB_ERR_INVALID, "returns over " + std::to_string(T) + " steps need " + std::to_string(T + 1) +
+                                           " history rows (have " + std::to_string(p->history) + ")");
+    if (t->critic.d.n_in != p->n_in)
+        return fail(PHYZB_ERR_INVALID, "critic input width " + std::to_string(t->critic.d.n_in) +
+                                           " differs from the observation width " + std::to_string(p->n_in));
+    if (!cfg->reward_coef) return fail(PHYZB_ERR_INVALID, "reward_coef is null");
+    DeviceGuard g(s->device);
+    const long long N = s->nworld;
+    // scratch (kept on the policy state)
+    const size_t need_r = (size_t)T * N * 4, need_v = (size_t)(T + 1) * N * 4,
+                 need_p = (size_t)pz::gae_blocks(N) * 3 * 8 + 4 * 8;
+    if (need_r + need_v + need_p + (size_t)p->n_in * 4 > p->ret_bytes) {
+        if (p->d_ret_scratch) cudaFree(p->d_ret_scratch);
+        p->d_ret_scratch = nullptr;
+        p->ret_bytes = 0;
+        const size_t bytes = need_r + need_v + need_p + (size_t)pz::POLICY_MAX_IN * 4 + 256;
+        PZ_CUDA(cudaMalloc(&p->d_ret_scratch, bytes));
+        p->ret_bytes = bytes;
+    }
+    char* base = (char*)p->d_ret_scratch;
+    double* sums = (double*)base;  // 4 doubles
+    double* part = sums + 4;
+    float* rew = (float*)(base + need_p);
+    float* val = rew + (size_t)T * N;
+    float* coef = val + (size_t)(T + 1) * N;
+    std::vector<float> cf(p->n_in);
+    for (int j = 0; j < p->n_in; j++) cf[j] = (float)cfg->reward_coef[j];
+    PZ_CUDA(cudaMemcpyAsync(coef, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    PZ_CUDA(pz::rollout_rewards(p->d_obs, p->d_out, p->n_in, p->n_out, N, T, coef, (float)cfg->action_penalty, rew,
+                                s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    // critic values of rows 0 .. T
+    const phyzb_batch_col oc{p->d_obs, N, p->n_in};
+    PZ_TRY(phyzb_trainer_evaluate(t, 1, oc, (int64_t)(T + 1) * N, val));
+    PZ_CUDA(pz::rollout_gae(rew, val, N, T, (float)cfg->gamma, (float)cfg->lambda, adv, ret, part, sums, s->stream));
+    PZ_TRY(comm_allreduce_sum(comm, sums, 3, true, s->stream));
+    const double count = (double)T * N * comm_nranks(comm);
+    if (cfg->normalize) PZ_CUDA(pz::normalize_advantages(adv, (long long)T * N, sums, count, s->stream));
+    // bounded wait on the collective first: the read-back below then finds
+    // the stream idle
+    PZ_TRY(comm_wait(comm, s->stream, 120.0));
+    double hs[3] = {0, 0, 0};
+    PZ_CUDA(cudaMemcpyAsync(hs, sums, sizeof(hs), cudaMemcpyDeviceToHost, s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    if (stats) {
+        const double mean = hs[0] / count;
+        stats[0] = hs[2] / ((double)N * comm_nranks(comm));  // mean return per world
+        stats[1] = mean;
+        stats[2] = std::sqrt(std::max(hs[1] / count - mean * mean, 0.0));
+    }
+    return PHYZB_OK;
+}
+
+int phyzb_policy_sync_from_trainer(phyzb_sim* s, phyzb_trainer* t) {
+    PZ_TRY(check_sim(s));
+    if (!t) return fail(PHYZB_ERR_INVALID, "trainer is null");
+    if (!s->policy) return fail(PHYZB_ERR_STATE, "policy pass not enabled — call enable_policy first");
+    PolicyDev* p = s->policy;
+    const pz::NetDev& a = t->actor.d;
+    if (a.n_in != p->n_in || a.n_h != p->n_h || a.n_out != p->n_out || a.n_wf != p->n_wf)
+        return fail(PHYZB_ERR_INVALID, "actor shape differs from the policy's");
+    DeviceGuard g(s->device);
+    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    PZ_CUDA(cudaMemcpyAsync(p->d_w, a.wf, (size_t)a.n_wf * 4, cudaMemcpyDeviceToDevice, s->stream));
+    std::vector<double> logstd(a.n_out);
+    PZ_CUDA(cudaMemcpy(logstd.data(), a.p + t->actor.mlp_params, (size_t)a.n_out * 8, cudaMemcpyDeviceToHost));
+    std::vector<float> sd(a.n_out);
+    for (int k = 0; k < a.n_out; k++) sd[k] = (float)std::exp(logstd[k]);
+    PZ_CUDA(cudaMemcpyAsync(p->d_std, sd.data(), sd.size() * 4, cudaMemcpyHostToDevice, s->stream));
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    p->has_weights = p->has_std = true;
     return PHYZB_OK;
 }
 

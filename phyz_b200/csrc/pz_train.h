@@ -50,8 +50,10 @@ struct PpoArgs {
     int logstd_off;  // flat offset of the actor's log_std
 };
 
-// forward of `b` rows idx[0..b) of x through `net`, activations into its buffers
-cudaError_t train_forward(const NetDev& net, BatchCol x, const uint32_t* idx, int b, cudaStream_t s);
+// forward of `b` rows idx[0..b) of x (idx null: rows r0 .. r0 + b) through
+// `net`, activations into its buffers
+cudaError_t train_forward(const NetDev& net, BatchCol x, const uint32_t* idx, int b, cudaStream_t s,
+                          long long r0 = 0);
 // actor: dL/dmean into net.dout, per-row dL/dlogstd, stats cols 0-2
 cudaError_t train_ppo_grad(const NetDev& actor, const PpoArgs& a, BatchCol act, BatchCol logp_old, BatchCol adv,
                            const uint32_t* idx, int b, float* dlogstd, float* stats, cudaStream_t s);
@@ -69,10 +71,25 @@ cudaError_t train_row_sums(const float* rows, int nrows, int ld, int b, float* g
 // Adam (tang's ModuleAdam, bias corrections bc1, bc2) on every parameter,
 // refreshing the three f32 mirrors
 cudaError_t train_adam(const NetDev& net, double lr, double beta1, double beta2, double eps, double wd,
-                       double bc1, double bc2, cudaStream_t s);
+                       double bc1, double bc2, double gscale, cudaStream_t s);
 // column sums of stats [4][b] (f64 accumulation, fixed order) into out[4]
 cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s);
 // scratch bytes train_backward needs for minibatches of up to max_b rows
 size_t train_work_bytes(int max_b, int max_rows, int max_cols);
+
+// epochs x n indices: order[e][k] = (a_e k + c_e) mod n, ac = [a_0, c_0, ...]
+// on the device (a_e coprime with n: a permutation per epoch)
+cudaError_t train_orders(uint32_t* order, long long n, int epochs, const unsigned long long* ac_dev, cudaStream_t s);
+// rewards [T][N] of a policy history (obs [T+1][n_in][N], out [T][n_out+1][N]):
+// r = coef . obs[t+1] - pen |act[t]|^2
+cudaError_t rollout_rewards(const float* obs, const float* out, int n_in, int n_out, long long N, int T,
+                            const float* coef, float pen, float* r, cudaStream_t s);
+// GAE(gamma, lam) per world over values V [T+1][N]: adv, ret [T][N]; sums =
+// [sum adv, sum adv^2, sum r] over the worlds (part: gae_blocks(N) x 3 scratch)
+int gae_blocks(long long N);
+cudaError_t rollout_gae(const float* r, const float* V, long long N, int T, float gamma, float lam, float* adv,
+                        float* ret, double* part, double* sums, cudaStream_t s);
+// adv <- (adv - mean) / (std + 1e-8), moments from sums over `count` rows
+cudaError_t normalize_advantages(float* adv, long long n, const double* sums, double count, cudaStream_t s);
 
 }  // namespace pz

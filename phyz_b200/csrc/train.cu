@@ -35,7 +35,7 @@ __device__ __forceinline__ void stage(const float* g, int n, float* sm) {
 }
 
 __global__ void __launch_bounds__(ROW_BLOCK) fwd_kernel(const NetDev n, const BatchCol x, const uint32_t* idx,
-                                                        int b) {
+                                                        long long r0, int b) {
     extern __shared__ __align__(16) float sm[];
     const int W = blockDim.x;
     stage(n.wf, n.n_wf, sm);
@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(ROW_BLOCK) fwd_kernel(const NetDev n, const Ba
     float* H2 = H1 + n.h_pad * W;
     const int r = blockIdx.x * W + threadIdx.x;
     if (r >= b) return;
-    const long long s = idx[r];
+    const long long s = idx ? (long long)idx[r] : r0 + r;
     for (int k = 0; k < n.in_pad; k++) X[k * W] = k < n.n_in ? col(x, s, k) : 0.0f;
     const long long L = n.max_b;
     dense_rows<1>(W1, b1, n.in_pad, n.h_pad, X, H1, W);
@@ -218,12 +218,12 @@ __global__ void grad_reduce_kernel(const double* part, int nsplit, int M, int N,
 // tang's ModuleAdam step (phyz_train.cu:260-276) on the f64 master, then the
 // f32 mirrors the forward, backward and log_std readers use.
 __global__ void adam_kernel(const NetDev n, double lr, double beta1, double beta2, double eps, double wd,
-                            double bc1, double bc2) {
+                            double bc1, double bc2, double gscale) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= n.n_param) return;
     double x = n.p[t];
     if (wd > 0.0) x = x * (1.0 - lr * wd);
-    const double gr = (double)n.g[t];
+    const double gr = gscale == 1.0 ? (double)n.g[t] : (double)n.g[t] * gscale;
     const double mt = beta1 * n.m[t] + (1.0 - beta1) * gr;
     const double vt = beta2 * n.v[t] + (1.0 - beta2) * gr * gr;
     n.m[t] = mt;
@@ -288,14 +288,14 @@ size_t train_work_bytes(int max_b, int max_rows, int max_cols) {
     return nsplit * (size_t)max_rows * (size_t)(max_cols + 1) * sizeof(double);
 }
 
-cudaError_t train_forward(const NetDev& n, BatchCol x, const uint32_t* idx, int b, cudaStream_t s) {
+cudaError_t train_forward(const NetDev& n, BatchCol x, const uint32_t* idx, int b, cudaStream_t s, long long r0) {
     if (b <= 0) return cudaSuccess;
     int W = 0, smem = 0;
     cudaError_t e = row_block(n.n_wf, n.in_pad + 2 * n.h_pad, &W, &smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    fwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, x, idx, b);
+    fwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, x, idx, r0, b);
     return cudaGetLastError();
 }
 
@@ -341,13 +341,126 @@ cudaError_t train_row_sums(const float* rows, int nrows, int ld, int b, float* g
 }
 
 cudaError_t train_adam(const NetDev& n, double lr, double beta1, double beta2, double eps, double wd, double bc1,
-                       double bc2, cudaStream_t s) {
-    adam_kernel<<<(n.n_param + 255) / 256, 256, 0, s>>>(n, lr, beta1, beta2, eps, wd, bc1, bc2);
+                       double bc2, double gscale, cudaStream_t s) {
+    adam_kernel<<<(n.n_param + 255) / 256, 256, 0, s>>>(n, lr, beta1, beta2, eps, wd, bc1, bc2, gscale);
     return cudaGetLastError();
 }
 
 cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s) {
     stats_kernel<<<4, 256, 0, s>>>(stats, ld, b, out);
+    return cudaGetLastError();
+}
+
+// ── the collector side of an update: rewards, GAE, normalization ────────
+
+namespace {
+
+// order[e][k] = (a_e k + c_e) mod n: one affine permutation per epoch
+__global__ void order_kernel(uint32_t* order, long long n, int epochs, const unsigned long long* ac) {
+    const long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    for (int e = 0; e < epochs; e++) {
+        const unsigned long long a = ac[2 * e], c = ac[2 * e + 1];
+        // a, k < n <= 2^32: the product fits 64 bits
+        order[(long long)e * n + k] = (uint32_t)((a * (unsigned long long)k % (unsigned long long)n + c) %
+                                                 (unsigned long long)n);
+    }
+}
+
+// r[t][w] = sum_j coef[j] obs[t+1][j][w] - pen sum_k act[t][k][w]^2
+__global__ void reward_kernel(const float* obs, const float* out, int n_in, int n_out, long long N, int T,
+                              const float* coef, float pen, float* r) {
+    const long long w = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (w >= N) return;
+    for (int t = 0; t < T; t++) {
+        const float* o = obs + (long long)(t + 1) * n_in * N + w;
+        float acc = 0.0f;
+        for (int j = 0; j < n_in; j++)
+            if (coef[j] != 0.0f) acc += coef[j] * o[(long long)j * N];
+        const float* a = out + (long long)t * (n_out + 1) * N + w;
+        float e = 0.0f;
+        for (int k = 0; k < n_out; k++) e += a[(long long)k * N] * a[(long long)k * N];
+        r[(long long)t * N + w] = acc - pen * e;
+    }
+}
+
+// GAE per world (backward over t), with per-block sums of adv, adv^2 and the
+// world's return into part[block][3] (fixed tree order).
+__global__ void gae_kernel(const float* r, const float* V, long long N, int T, float gamma, float lam, float* adv,
+                           float* ret, double* part) {
+    __shared__ double red[3][256];
+    const long long w = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    double sa = 0.0, sa2 = 0.0, sr = 0.0;
+    if (w < N) {
+        float A = 0.0f;
+        for (int t = T - 1; t >= 0; t--) {
+            const float v = V[(long long)t * N + w];
+            const float rt = r[(long long)t * N + w];
+            const float delta = rt + gamma * V[(long long)(t + 1) * N + w] - v;
+            A = delta + gamma * lam * A;
+            adv[(long long)t * N + w] = A;
+            ret[(long long)t * N + w] = A + v;
+            sa += A;
+            sa2 += (double)A * A;
+            sr += rt;
+        }
+    }
+    red[0][threadIdx.x] = sa;
+    red[1][threadIdx.x] = sa2;
+    red[2][threadIdx.x] = sr;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s)
+            for (int c = 0; c < 3; c++) red[c][threadIdx.x] += red[c][threadIdx.x + s];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0)
+        for (int c = 0; c < 3; c++) part[(long long)blockIdx.x * 3 + c] = red[c][0];
+}
+
+__global__ void sum_parts_kernel(const double* part, int nblocks, double* sums) {
+    const int c = threadIdx.x;
+    if (c >= 3) return;
+    double s = 0.0;
+    for (int b = 0; b < nblocks; b++) s += part[(long long)b * 3 + c];
+    sums[c] = s;
+}
+
+// adv <- (adv - mean) / (std + 1e-8) from sums = [sum adv, sum adv^2, .],
+// count = rows over every rank
+__global__ void normalize_kernel(float* adv, long long n, const double* sums, double count) {
+    const long long k = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    const double mean = sums[0] / count;
+    const double var = fmax(sums[1] / count - mean * mean, 0.0);
+    adv[k] = (float)(((double)adv[k] - mean) / (sqrt(var) + 1e-8));
+}
+
+}  // namespace
+
+cudaError_t train_orders(uint32_t* order, long long n, int epochs, const unsigned long long* ac_dev, cudaStream_t s) {
+    order_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(order, n, epochs, ac_dev);
+    return cudaGetLastError();
+}
+
+cudaError_t rollout_rewards(const float* obs, const float* out, int n_in, int n_out, long long N, int T,
+                            const float* coef, float pen, float* r, cudaStream_t s) {
+    reward_kernel<<<(unsigned)((N + 127) / 128), 128, 0, s>>>(obs, out, n_in, n_out, N, T, coef, pen, r);
+    return cudaGetLastError();
+}
+
+int gae_blocks(long long N) { return (int)((N + 255) / 256); }
+
+cudaError_t rollout_gae(const float* r, const float* V, long long N, int T, float gamma, float lam, float* adv,
+                        float* ret, double* part, double* sums, cudaStream_t s) {
+    const int nb = gae_blocks(N);
+    gae_kernel<<<nb, 256, 0, s>>>(r, V, N, T, gamma, lam, adv, ret, part);
+    sum_parts_kernel<<<1, 32, 0, s>>>(part, nb, sums);
+    return cudaGetLastError();
+}
+
+cudaError_t normalize_advantages(float* adv, long long n, const double* sums, double count, cudaStream_t s) {
+    normalize_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(adv, n, sums, count);
     return cudaGetLastError();
 }
 

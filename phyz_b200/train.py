@@ -90,6 +90,30 @@ class Trainer:
         return {"policy_loss": st.policy_loss, "value_loss": st.value_loss, "kl": st.kl,
                 "grad_steps": st.grad_steps, "stopped_early": bool(st.stopped_early)}
 
+    # ── device-resident batches (the collector feeding the update) ─────────
+    def set_batch_device(self, n_rows: int, cols) -> None:
+        """cols: 6 (device_ptr, block, features) triples: obs_a, obs_c, act,
+        logp_old, adv, ret in blocked SoA (pz BatchCol)."""
+        arr = (_lib.PhyzbBatchCol * 6)(*[_lib.PhyzbBatchCol(int(p), int(b), int(f)) for p, b, f in cols])
+        check(self._lib.phyzb_trainer_set_batch_device(self._h, int(n_rows), arr))
+
+    def update_shuffled(self, cfg: PpoCfg, seed: int) -> dict:
+        c = _lib.PhyzbPpoCfg(cfg.clip, cfg.entropy_coef, cfg.vdelta, int(cfg.minibatch), int(cfg.epochs),
+                             cfg.target_kl, cfg.kl_scale, int(cfg.kl_mode))
+        st = _lib.PhyzbUpdateStats()
+        check(self._lib.phyzb_trainer_update_shuffled(self._h, C.byref(c), C.c_uint64(seed & (2 ** 64 - 1)),
+                                                      C.byref(st)))
+        return {"policy_loss": st.policy_loss, "value_loss": st.value_loss, "kl": st.kl,
+                "grad_steps": st.grad_steps, "stopped_early": bool(st.stopped_early)}
+
+    def evaluate(self, which: int, x_col, n_rows: int, out_ptr: int) -> None:
+        p, b, f = x_col
+        check(self._lib.phyzb_trainer_evaluate(self._h, int(which), _lib.PhyzbBatchCol(int(p), int(b), int(f)),
+                                               int(n_rows), C.c_void_p(int(out_ptr))))
+
+    def set_comm(self, comm) -> None:
+        check(self._lib.phyzb_trainer_set_comm(self._h, comm._h if comm is not None else None))
+
     def close(self) -> None:
         if getattr(self, "_h", None) is not None and self._h.value:
             self._lib.phyzb_trainer_destroy(self._h)
