@@ -235,6 +235,10 @@ def main():
         run_reference_impl(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
     world, rank, local = dist_setup(args)
+    if args.config == "c5_quadruped_ppo":
+        run_c5(args, world, rank, local)
+        finish(world)
+        return
 
     import torch
 
@@ -405,6 +409,87 @@ def main():
     comm.close()
     sim.close()
     finish(world)
+
+
+# ── C5: the quadruped batch under an on-device policy, with PPO updates ──
+def run_c5(args, world, rank, local):
+    """One bench step = one PPO iteration of BASELINE.json configs[4]: reset,
+    64 control steps of the on-device policy driving the quadruped's PD
+    servos (262144 worlds per GPU), returns on the device with the NCCL
+    reduction of the advantage moments, and one PPO epoch (minibatches of
+    65536, gradients all-reduced over ranks). Metric: simulated world-steps/s
+    of the whole job, the update included."""
+    import torch
+
+    from phyz_b200.parallel import Comm, share_bytes
+    from phyz_b200.rl import C5Cfg, OnDevicePpo
+
+    cfg = C5Cfg(nworld=args.nworld or 262144, steps=args.horizon or 64, precision=args.precision)
+    comm = Comm(rank, world, local, timeout=120.0,
+                id_channel=(lambda p, r: share_bytes(p, r))) if world > 1 else None
+    ppo = OnDevicePpo(cfg, device=local, rank=rank, comm=comm)
+    stream = torch.cuda.Stream()
+    ppo.sim.set_stream(stream.cuda_stream)
+    for _ in range(args.warmup):
+        ppo.iteration()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rollout_ms = 0.0
+    stats = []
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for _ in range(args.steps):
+            r0.record(stream)
+            ppo.rollout()
+            r1.record(stream)
+            stats.append(ppo.update())
+            r1.synchronize()
+            rollout_ms += r0.elapsed_time(r1)
+        t1.record(stream)
+        stream.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ppo.sim.sync()
+    ms = allreduce_max(t0.elapsed_time(t1), world)
+    rollout_ms = allreduce_max(rollout_ms / args.steps, world)
+    world_steps = cfg.nworld * cfg.steps * cfg.substeps * world
+    value = world_steps * args.steps / (ms * 1e-3)
+    flops_phys, _ = ppo.sim.flops_per_world_step()
+    i, h, o = ppo.spec.n_in, ppo.spec.hidden, ppo.spec.n_out
+    mlp = lambda out: 2 * (i * h + h * h + h * out)
+    # per control step and world: policy forward, critic value, and one
+    # epoch of update (forward + backward ~ 3x forward, actor and critic)
+    flops_ctrl = mlp(o) + mlp(1) + 3 * (mlp(o) + mlp(1)) * cfg.epochs
+    flops_ws = flops_phys + flops_ctrl / cfg.substeps
+    pk = np.zeros(1)
+    from phyz_b200 import _lib as L
+    L.check(L.load().phyzb_measure_fma_peak(L.F32, L.dptr(pk)))
+    achieved = flops_ws * world_steps / world * args.steps / (ms * 1e-3) / 1e12
+    if rank == 0:
+        ret_mean, adv_mean, adv_std = stats[-1][0]
+        upd = stats[-1][1]
+        line = {
+            "metric": "world-steps/sec", "value": value, "unit": "world-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": cfg.precision, "data": "synthetic (seeded)",
+            "config": {"workload": "c5_quadruped_ppo", "nworld_per_gpu": cfg.nworld, "control_steps": cfg.steps,
+                       "substeps": cfg.substeps, "policy": f"{i}->{h}->{h} tanh->{o}", "minibatch": cfg.minibatch,
+                       "epochs": cfg.epochs, "parallelism": f"worlds sharded over {world} GPU(s), "
+                                                            "gradients all-reduced per minibatch"},
+            "phases_ms": {"rollout": rollout_ms, "returns_and_update": ms / args.steps - rollout_ms},
+            "roofline": {"bound": "fma", "pipe": "fp32 FMA", "achieved": achieved, "peak": float(pk[0]),
+                         "unit": "TFLOP/s", "frac": achieved / float(pk[0]),
+                         "flops_per_world_step": flops_ws, "peak_source": "measured in this run"},
+            "clocks": clk.summary(), "gpu_launches": None,
+            "last_iteration": {"mean_return": ret_mean, "adv_std": adv_std, **upd},
+        }
+        print(json.dumps(line), flush=True)
+    ppo.close()
+    if comm is not None:
+        comm.close()
 
 
 def finish(world):

@@ -70,6 +70,7 @@ struct PolicyDev {
     float* d_z = nullptr;      // [n_out][nworld]
     void* d_base = nullptr;    // T [npd][nworld]
     void* d_xf = nullptr;      // T [nb * 18][nworld]
+    float* d_h = nullptr;      // [2][h_pad][nworld] hidden-layer scratch
     float* d_obs = nullptr;    // [history][n_in][nworld]
     float* d_out = nullptr;    // [history][n_out + 1][nworld]
     void* d_rows = nullptr;    // readback transpose buffer

@@ -22,7 +22,7 @@ void destroy_policy(phyzb_sim* s) {
     if (!p) return;
     void* bufs[] = {p->fk,    p->d_ops,  p->d_aux, p->d_com, p->d_w,   p->d_std,  p->d_noise,
                     p->d_slots, p->d_clamp, p->d_rng, p->d_z, p->d_base, p->d_xf, p->d_obs,
-                    p->d_out, p->d_rows, p->d_ret_scratch};
+                    p->d_out, p->d_rows, p->d_ret_scratch, p->d_h};
     for (void* b : bufs)
         if (b) cudaFree(b);
     delete p;
@@ -67,6 +67,7 @@ pz::PolicyArgs<T> policy_args(phyzb_sim* s, int step) {
     a.base = (const T*)p->d_base;
     a.targets = (T*)s->targets;
     a.npd = (int)s->cfg.pd.size();
+    a.h = p->d_h;
     a.obs = p->d_obs ? p->d_obs + (size_t)step * p->n_in * N : nullptr;
     a.out = p->d_out ? p->d_out + (size_t)step * (p->n_out + 1) * N : nullptr;
     return a;
@@ -251,6 +252,7 @@ int phyzb_enable_policy(phyzb_sim* s, const phyzb_policy_spec* sp) {
     PZ_CUDA(cudaMalloc(&p->d_base, (size_t)npd * N * esz));
     PZ_CUDA(cudaMemsetAsync(p->d_base, 0, (size_t)npd * N * esz, s->stream));
     PZ_CUDA(cudaMalloc(&p->d_xf, (size_t)s->nb * pz::XF_STRIDE * N * esz));
+    PZ_CUDA(cudaMalloc((void**)&p->d_h, (size_t)2 * p->h_pad * N * sizeof(float)));
     PZ_CUDA(cudaMalloc((void**)&p->d_obs, (size_t)p->history * p->n_in * N * sizeof(float)));
     PZ_CUDA(cudaMalloc((void**)&p->d_out, (size_t)p->history * (p->n_out + 1) * N * sizeof(float)));
     PZ_CUDA(cudaStreamSynchronize(s->stream));

@@ -227,7 +227,7 @@ int run_update(phyzb_trainer* t, const phyzb_ppo_cfg* cfg, phyzb_update_stats* o
             PZ_CUDA(pz::train_backward(t->critic.d, t->c_obs_c, idx, b, t->work, s));
             PZ_TRY(adam_step(t, t->critic));
             // the brake: the minibatch's statistics (summed over ranks) to the host
-            PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, s));
+            PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, t->work, s));
             PZ_TRY(comm_allreduce_sum(t->comm, t->reduced, 4, false, s));
             PZ_CUDA(cudaMemcpyAsync(t->reduced_host, t->reduced, 16, cudaMemcpyDeviceToHost, s));
             PZ_TRY(comm_wait(t->comm, s, 120.0));

@@ -254,49 +254,60 @@ __device__ __forceinline__ double rng_normal(unsigned long long& x) {
 template <class T>
 __global__ void __launch_bounds__(POLICY_BLOCK) policy_kernel(const __grid_constant__ PolicyArgs<T> P) {
     extern __shared__ __align__(16) float sm[];
-    const int W = blockDim.x;
-    // stage the packed weights (16-byte chunks)
-    for (int k = threadIdx.x; k < P.n_wf / 4; k += W)
-        reinterpret_cast<float4*>(sm)[k] = __ldg(reinterpret_cast<const float4*>(P.w) + k);
-    __syncthreads();
+    stage_weights(P.w, P.n_wf, sm);
     const float* W1 = sm;
     const float* b1 = W1 + P.in_pad * P.h_pad;
     const float* W2 = b1 + P.h_pad;
     const float* b2 = W2 + P.h_pad * P.h_pad;
     const float* W3 = b2 + P.h_pad;
     const float* b3 = W3 + P.h_pad * P.out_pad;
-    float* X = sm + P.n_wf + threadIdx.x;  // SoA rows of this world
-    float* H1 = X + P.in_pad * W;
-    float* H2 = H1 + P.h_pad * W;
-    float* Y = X;  // the output row reuses the input row
 
-    const long long w = (long long)blockIdx.x * W + threadIdx.x;
+    const long long w = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (w >= P.nworld) return;
     const long long N = P.nworld;
 
     kinematics_world(P, w);
     unsigned long long r = P.rng[w];
-    for (int k = 0; k < P.in_pad; k++) {
-        float xk = 0.0f;
-        if (k < P.n_in) {
-            xk = obs_feature(P, w, k);
-            const float sc = P.in_noise[k];
-            if (sc != 0.0f) xk += sc * (float)rng_normal(r);
-            P.obs[(long long)k * N + w] = xk;
-        }
-        X[k * W] = xk;
+    float* xo = P.obs + w;  // the observation row, as recorded (noise included)
+    for (int k = 0; k < P.n_in; k++) {
+        float xk = obs_feature(P, w, k);
+        const float sc = P.in_noise[k];
+        if (sc != 0.0f) xk += sc * (float)rng_normal(r);
+        xo[(long long)k * N] = xk;
     }
-    dense_rows<1>(W1, b1, P.in_pad, P.h_pad, X, H1, W);
-    dense_rows<1>(W2, b2, P.h_pad, P.h_pad, H1, H2, W);
-    dense_rows<0>(W3, b3, P.h_pad, P.out_pad, H2, Y, W);
+    const int n_in = P.n_in;
+    float* h1 = P.h + w;
+    float* h2 = P.h + (long long)P.h_pad * N + w;
+    dense_tiles(W1, b1, P.in_pad, P.h_pad, [&](int i) { return i < n_in ? xo[(long long)i * N] : 0.0f; },
+                [&](int j, float a) { h1[(long long)j * N] = tanhf(a); });
+    dense_tiles(W2, b2, P.h_pad, P.h_pad, [&](int i) { return h1[(long long)i * N]; },
+                [&](int j, float a) { h2[(long long)j * N] = tanhf(a); });
+    // the action means stay in registers (out_pad is one tile)
+    float mean[POLICY_TILE];
+#pragma unroll
+    for (int k = 0; k < POLICY_TILE; k++) mean[k] = b3[k];
+    for (int i = 0; i < P.h_pad; i++) {
+        const float xi = h2[(long long)i * N];
+        const float4* wr = reinterpret_cast<const float4*>(W3 + i * P.out_pad);
+#pragma unroll
+        for (int k4 = 0; k4 < POLICY_TILE / 4; k4++) {
+            const float4 wv = wr[k4];
+            mean[4 * k4 + 0] = fmaf(wv.x, xi, mean[4 * k4 + 0]);
+            mean[4 * k4 + 1] = fmaf(wv.y, xi, mean[4 * k4 + 1]);
+            mean[4 * k4 + 2] = fmaf(wv.z, xi, mean[4 * k4 + 2]);
+            mean[4 * k4 + 3] = fmaf(wv.w, xi, mean[4 * k4 + 3]);
+        }
+    }
 
     // every servo tracks its base target; actions add onto their slots
     for (int j = 0; j < P.npd; j++) P.targets[(long long)j * N + w] = P.base[(long long)j * N + w];
     const float keep = sqrtf(fmaxf(0.0f, 1.0f - P.rho * P.rho));
     const float LN_2PI = 1.8378770664093453f;
     float logp = 0.0f;
-    for (int k = 0; k < P.n_out; k++) {
-        const float m = Y[k * W];
+#pragma unroll
+    for (int k = 0; k < POLICY_TILE; k++) {
+        if (k >= P.n_out) break;
+        const float m = mean[k];
         const float zk = P.rho * P.z[(long long)k * N + w] + keep * (float)rng_normal(r);
         P.z[(long long)k * N + w] = zk;
         const float sd = P.stdv[k];
@@ -315,16 +326,6 @@ __global__ void __launch_bounds__(POLICY_BLOCK) policy_kernel(const __grid_const
 
 }  // namespace
 
-static int policy_smem(int n_wf, int in_pad, int h_pad, int W) {
-    return (n_wf + (in_pad + 2 * h_pad) * W) * (int)sizeof(float);
-}
-
-int policy_worlds_per_block(int n_wf, int in_pad, int h_pad, int smem_optin) {
-    for (int W = POLICY_BLOCK; W >= 32; W /= 2)
-        if (policy_smem(n_wf, in_pad, h_pad, W) <= smem_optin) return W;
-    return 0;
-}
-
 template <class T>
 cudaError_t launch_kinematics(const PolicyArgs<T>& a, cudaStream_t s) {
     if (a.nworld <= 0) return cudaSuccess;
@@ -336,17 +337,11 @@ cudaError_t launch_kinematics(const PolicyArgs<T>& a, cudaStream_t s) {
 template <class T>
 cudaError_t launch_policy(const PolicyArgs<T>& a, cudaStream_t s) {
     if (a.nworld <= 0) return cudaSuccess;
-    int dev = 0, optin = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    const int smem = a.n_wf * (int)sizeof(float);  // the weights; a world's rows live in HBM
+    cudaError_t e = cudaFuncSetAttribute(policy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
-    const int W = policy_worlds_per_block(a.n_wf, a.in_pad, a.h_pad, optin);
-    if (W == 0) return cudaErrorInvalidConfiguration;
-    const int smem = policy_smem(a.n_wf, a.in_pad, a.h_pad, W);
-    e = cudaFuncSetAttribute(policy_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    const unsigned grid = (unsigned)((a.nworld + W - 1) / W);
-    policy_kernel<T><<<grid, W, smem, s>>>(a);
+    const unsigned grid = (unsigned)((a.nworld + POLICY_BLOCK - 1) / POLICY_BLOCK);
+    policy_kernel<T><<<grid, POLICY_BLOCK, smem, s>>>(a);
     return cudaGetLastError();
 }
 

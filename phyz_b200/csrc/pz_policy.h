@@ -59,6 +59,7 @@ struct PolicyArgs {
     const T* base;            // [npd][nworld] base PD targets
     T* targets;               // [npd][nworld] PD targets (written)
     int npd;
+    float* h;    // hidden-layer scratch, SoA [2][h_pad][nworld]
     float* obs;  // this step's observation rows, SoA [n_in][nworld]
     float* out;  // this step's actions + log-prob, SoA [n_out + 1][nworld]
 };
@@ -69,8 +70,6 @@ cudaError_t launch_kinematics(const PolicyArgs<T>& a, cudaStream_t s);
 // One control step: kinematics, observation, MLP, sample, PD targets.
 template <class T>
 cudaError_t launch_policy(const PolicyArgs<T>& a, cudaStream_t s);
-// Worlds per block launch_policy uses (its weights and per-world rows must
-// fit shared memory), or 0 if even 32 worlds do not fit.
-int policy_worlds_per_block(int n_wf, int in_pad, int h_pad, int smem_optin);
+
 
 }  // namespace pz

@@ -73,7 +73,7 @@ cudaError_t train_row_sums(const float* rows, int nrows, int ld, int b, float* g
 cudaError_t train_adam(const NetDev& net, double lr, double beta1, double beta2, double eps, double wd,
                        double bc1, double bc2, double gscale, cudaStream_t s);
 // column sums of stats [4][b] (f64 accumulation, fixed order) into out[4]
-cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s);
+cudaError_t train_stats(const float* stats, int ld, int b, float* out, double* work, cudaStream_t s);
 // scratch bytes train_backward needs for minibatches of up to max_b rows
 size_t train_work_bytes(int max_b, int max_rows, int max_cols);
 

@@ -20,45 +20,38 @@ namespace pz {
 namespace {
 
 constexpr int ROW_BLOCK = 128;  // samples per block of the per-row kernels
-constexpr int GT = 32;          // gradient tile (outputs m x n)
-constexpr int GK = 32;          // rows per shared-memory stage
-constexpr int GKC = 256;        // rows per split
+constexpr int GKC_MIN = 256;    // rows per split, at least
 
 __device__ __forceinline__ float col(const BatchCol& c, long long r, int k) {
     return c.base[(r / c.N) * (long long)c.F * c.N + (long long)k * c.N + r % c.N];
 }
 
-__device__ __forceinline__ void stage(const float* g, int n, float* sm) {
-    for (int k = threadIdx.x; k < n / 4; k += blockDim.x)
-        reinterpret_cast<float4*>(sm)[k] = __ldg(reinterpret_cast<const float4*>(g) + k);
-    __syncthreads();
-}
 
 __global__ void __launch_bounds__(ROW_BLOCK) fwd_kernel(const NetDev n, const BatchCol x, const uint32_t* idx,
                                                         long long r0, int b) {
     extern __shared__ __align__(16) float sm[];
-    const int W = blockDim.x;
-    stage(n.wf, n.n_wf, sm);
+    stage_weights(n.wf, n.n_wf, sm);
     const float* W1 = sm;
     const float* b1 = W1 + n.in_pad * n.h_pad;
     const float* W2 = b1 + n.h_pad;
     const float* b2 = W2 + n.h_pad * n.h_pad;
     const float* W3 = b2 + n.h_pad;
     const float* b3 = W3 + n.h_pad * n.out_pad;
-    float* X = sm + n.n_wf + threadIdx.x;
-    float* H1 = X + n.in_pad * W;
-    float* H2 = H1 + n.h_pad * W;
-    const int r = blockIdx.x * W + threadIdx.x;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= b) return;
     const long long s = idx ? (long long)idx[r] : r0 + r;
-    for (int k = 0; k < n.in_pad; k++) X[k * W] = k < n.n_in ? col(x, s, k) : 0.0f;
+    const float* xr = x.base + (s / x.N) * (long long)x.F * x.N + s % x.N;  // feature k at xr[k * N]
     const long long L = n.max_b;
-    dense_rows<1>(W1, b1, n.in_pad, n.h_pad, X, H1, W);
-    for (int j = 0; j < n.h_pad; j++) n.h1[j * L + r] = H1[j * W];
-    dense_rows<1>(W2, b2, n.h_pad, n.h_pad, H1, H2, W);
-    for (int j = 0; j < n.h_pad; j++) n.h2[j * L + r] = H2[j * W];
-    dense_rows<0>(W3, b3, n.h_pad, n.out_pad, H2, X, W);
-    for (int k = 0; k < n.out_pad; k++) n.out[k * L + r] = X[k * W];
+    const int n_in = n.n_in;
+    float* h1 = n.h1 + r;
+    float* h2 = n.h2 + r;
+    float* out = n.out + r;
+    dense_tiles(W1, b1, n.in_pad, n.h_pad, [&](int i) { return i < n_in ? xr[(long long)i * x.N] : 0.0f; },
+                [&](int j, float a) { h1[j * L] = tanhf(a); });
+    dense_tiles(W2, b2, n.h_pad, n.h_pad, [&](int i) { return h1[i * L]; },
+                [&](int j, float a) { h2[j * L] = tanhf(a); });
+    dense_tiles(W3, b3, n.h_pad, n.out_pad, [&](int i) { return h2[i * L]; },
+                [&](int k, float a) { out[k * L] = a; });
 }
 
 // phyz_train.cu:136-186, per row; the padding rows of dout are zeroed.
@@ -123,96 +116,119 @@ __global__ void value_grad_kernel(const NetDev n, const PpoArgs a, const BatchCo
 // twice): dh2 = (W3^T dout) (1 - h2^2), dh1 = (W2^T dh2) (1 - h1^2).
 __global__ void __launch_bounds__(ROW_BLOCK) bwd_kernel(const NetDev n, int b) {
     extern __shared__ __align__(16) float sm[];
-    const int W = blockDim.x;
-    stage(n.wb, n.n_wb, sm);
+    stage_weights(n.wb, n.n_wb, sm);
     const float* W3 = sm;                        // [out_pad][h_pad]
     const float* W2 = W3 + n.out_pad * n.h_pad;  // [h_pad][h_pad]
-    float* D = sm + n.n_wb + threadIdx.x;
-    float* G2 = D + n.out_pad * W;
-    float* G1 = G2 + n.h_pad * W;
-    const int r = blockIdx.x * W + threadIdx.x;
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= b) return;
     const long long L = n.max_b;
-    for (int k = 0; k < n.out_pad; k++) D[k * W] = n.dout[k * L + r];
-    dense_rows<0>(W3, nullptr, n.out_pad, n.h_pad, D, G2, W);
-    for (int j = 0; j < n.h_pad; j++) {
-        const float h = n.h2[j * L + r];
-        const float g = G2[j * W] * (1.0f - h * h);
-        G2[j * W] = g;
-        n.dh2[j * L + r] = g;
-    }
-    dense_rows<0>(W2, nullptr, n.h_pad, n.h_pad, G2, G1, W);
-    for (int j = 0; j < n.h_pad; j++) {
-        const float h = n.h1[j * L + r];
-        n.dh1[j * L + r] = G1[j * W] * (1.0f - h * h);
-    }
+    const float* dout = n.dout + r;
+    const float* h2 = n.h2 + r;
+    const float* h1 = n.h1 + r;
+    float* dh2 = n.dh2 + r;
+    float* dh1 = n.dh1 + r;
+    dense_tiles(W3, nullptr, n.out_pad, n.h_pad, [&](int k) { return dout[k * L]; },
+                [&](int j, float a) {
+                    const float h = h2[j * L];
+                    dh2[j * L] = a * (1.0f - h * h);
+                });
+    dense_tiles(W2, nullptr, n.h_pad, n.h_pad, [&](int k) { return dh2[k * L]; },
+                [&](int j, float a) {
+                    const float h = h1[j * L];
+                    dh1[j * L] = a * (1.0f - h * h);
+                });
 }
 
 // Split-K partial sums part[split][m][n] = sum over the split's rows of
-// A[m][r] * Bv(r, n), n < N; column N is the bias (Bv = 1). A is SoA
-// [M][lda]; Bv is SoA activations [N][ldb] or, with gather, batch column x
-// at sample idx[r].
+// A[m][r] * Bv(r, n) for n < N, and part[split][m][N] = sum A[m][r] (the
+// bias column). A is SoA [M][lda]; Bv is SoA activations [N][ldb] or, with
+// gather, batch column x at sample idx[r]. 64 x 64 output tile per block,
+// 4 x 4 per thread; each 32-row stage accumulates in f32 registers and is
+// added into f64 accumulators (the reference accumulates in f64).
+constexpr int TM = 64, TN = 64, KS = 32;
+
 __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int M, const float* Bact, int ldb,
                                                    BatchCol x, const uint32_t* idx, int gather, int N, int b,
-                                                   double* part) {
-    __shared__ float As[GK][GT + 1];
-    __shared__ float Bs[GK][GT + 1];
-    const int m0 = blockIdx.x * GT, n0 = blockIdx.y * GT, split = blockIdx.z;
-    const int r0 = split * GKC;
-    const int r1 = min(b, r0 + GKC);
+                                                   int kc, double* part) {
+    __shared__ __align__(16) float As[KS][TM + 4];
+    __shared__ __align__(16) float Bs[KS][TN + 4];
+    const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN, split = blockIdx.z;
+    const int r0 = split * kc;
+    const int r1 = min(b, r0 + kc);
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    double acc00 = 0.0, acc01 = 0.0, acc10 = 0.0, acc11 = 0.0;
-    for (int rs = r0; rs < r1; rs += GK) {
-        for (int e = threadIdx.x; e < GT * GK; e += blockDim.x) {
-            const int mm = e / GK, kk = e % GK, r = rs + kk;
-            const int m = m0 + mm;
+    const bool bias_col = blockIdx.y == 0 && tx == 0;
+    double acc[4][4], rs[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        rs[i] = 0.0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
+    }
+    for (int rst = r0; rst < r1; rst += KS) {
+        for (int e = threadIdx.x; e < TM * KS; e += blockDim.x) {
+            const int mm = e / KS, kk = e % KS, r = rst + kk;
+            const int m = m0 + mm, n = n0 + mm;
             As[kk][mm] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
-            const int nn = mm, n = n0 + nn;
             float bv = 0.0f;
-            if (r < r1) {
-                if (n < N)
-                    bv = gather ? col(x, idx[r], n) : Bact[(long long)n * ldb + r];
-                else if (n == N)
-                    bv = 1.0f;
-            }
-            Bs[kk][nn] = bv;
+            if (r < r1 && n < N) bv = gather ? col(x, idx[r], n) : Bact[(long long)n * ldb + r];
+            Bs[kk][mm] = bv;
         }
         __syncthreads();
+        float fa[4][4] = {}, fr[4] = {};
 #pragma unroll 8
-        for (int kk = 0; kk < GK; kk++) {
-            const double a0 = As[kk][2 * ty], a1 = As[kk][2 * ty + 1];
-            const double b0 = Bs[kk][2 * tx], b1 = Bs[kk][2 * tx + 1];
-            acc00 = fma(a0, b0, acc00);
-            acc01 = fma(a0, b1, acc01);
-            acc10 = fma(a1, b0, acc10);
-            acc11 = fma(a1, b1, acc11);
+        for (int kk = 0; kk < KS; kk++) {
+            const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
+            const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][4 * tx]);
+            const float av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) fa[i][j] = fmaf(av[i], bv[j], fa[i][j]);
+                fr[i] += av[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            rs[i] += (double)fr[i];
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[i][j] += (double)fa[i][j];
         }
         __syncthreads();
     }
     const int N1 = N + 1;
-    const double acc[2][2] = {{acc00, acc01}, {acc10, acc11}};
 #pragma unroll
-    for (int i = 0; i < 2; i++)
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + 4 * ty + i;
+        if (m >= M) continue;
+        double* row = part + ((long long)split * M + m) * N1;
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const int m = m0 + 2 * ty + i, n = n0 + 2 * tx + j;
-            if (m < M && n <= N) part[((long long)split * M + m) * N1 + n] = acc[i][j];
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + 4 * tx + j;
+            if (n < N) row[n] = acc[i][j];
         }
+        if (bias_col) row[N] = rs[i];
+    }
 }
 
-// g[off_w + m * N + n] (n < N) and g[off_b + m] (bias) from the splits, in
-// split order.
+// g[off_w + m * N + n] (n < N) and g[off_b + m] (bias) from the splits: 8
+// lanes per output, each summing every 8th split, combined in a fixed
+// shuffle order (deterministic).
 __global__ void grad_reduce_kernel(const double* part, int nsplit, int M, int N, float* g, int off_w, int off_b) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    const long long t = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 3;
+    const int lane = threadIdx.x & 7;
     const int N1 = N + 1;
-    if (t >= M * N1) return;
-    const int m = t / N1, n = t % N1;
+    const bool valid = t < (long long)M * N1;
     double s = 0.0;
-    for (int k = 0; k < nsplit; k++) s += part[((long long)k * M + m) * N1 + n];
-    if (n < N)
-        g[off_w + m * N + n] = (float)s;
-    else
-        g[off_b + m] = (float)s;
+    if (valid)
+        for (int k = lane; k < nsplit; k += 8) s += part[(long long)k * M * N1 + t];
+    for (int o = 4; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o, 8);
+    if (valid && lane == 0) {
+        const int m = (int)(t / N1), n = (int)(t % N1);
+        if (n < N)
+            g[off_w + m * N + n] = (float)s;
+        else
+            g[off_b + m] = (float)s;
+    }
 }
 
 // tang's ModuleAdam step (phyz_train.cu:260-276) on the f64 master, then the
@@ -238,21 +254,6 @@ __global__ void adam_kernel(const NetDev n, double lr, double beta1, double beta
     if (n.posb[t] >= 0) n.wb[n.posb[t]] = xf;
 }
 
-// out[c] = sum_r stats[c][r], f64, one block per column, fixed tree order.
-__global__ void stats_kernel(const float* stats, int ld, int b, float* out) {
-    __shared__ double red[256];
-    const int c = blockIdx.x;
-    double s = 0.0;
-    for (int r = threadIdx.x; r < b; r += blockDim.x) s += (double)stats[(long long)c * ld + r];
-    red[threadIdx.x] = s;
-    __syncthreads();
-    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
-        if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
-        __syncthreads();
-    }
-    if (threadIdx.x == 0) out[c] = (float)red[0];
-}
-
 int row_smem(int packed, int per_row, int W) { return (packed + per_row * W) * (int)sizeof(float); }
 
 // Samples per block of a per-row kernel: the largest of 128 / 64 / 32 whose
@@ -271,27 +272,38 @@ cudaError_t row_block(int packed, int per_row, int* W_out, int* smem_out) {
     return cudaErrorInvalidConfiguration;
 }
 
+// Rows per split: enough splits for about two blocks per SM over the
+// output tiles, no split shorter than GKC_MIN rows (a multiple of KS).
+int split_rows(int M, int N, int b) {
+    const int tiles = ((M + TM - 1) / TM) * (N > 0 ? (N + TN - 1) / TN : 1);
+    const int want = (2 * 148 + tiles - 1) / tiles;
+    int rows = (b + want - 1) / want;
+    rows = (rows + KS - 1) / KS * KS;
+    return rows < GKC_MIN ? GKC_MIN : rows;
+}
+
 cudaError_t grad(const float* A, int lda, int M, const float* Bact, int ldb, BatchCol x, const uint32_t* idx,
                  int gather, int N, int b, float* g, int off_w, int off_b, double* work, cudaStream_t s) {
-    const int nsplit = (b + GKC - 1) / GKC;
-    dim3 grid((unsigned)((M + GT - 1) / GT), (unsigned)((N + 1 + GT - 1) / GT), (unsigned)nsplit);
-    grad_kernel<<<grid, 256, 0, s>>>(A, lda, M, Bact, ldb, x, idx, gather, N, b, work);
-    const int tot = M * (N + 1);
-    grad_reduce_kernel<<<(tot + 255) / 256, 256, 0, s>>>(work, nsplit, M, N, g, off_w, off_b);
+    const int kc = split_rows(M, N, b);
+    const int nsplit = (b + kc - 1) / kc;
+    dim3 grid((unsigned)((M + TM - 1) / TM), (unsigned)(N > 0 ? (N + TN - 1) / TN : 1), (unsigned)nsplit);
+    grad_kernel<<<grid, 256, 0, s>>>(A, lda, M, Bact, ldb, x, idx, gather, N, b, kc, work);
+    const long long lanes = (long long)M * (N + 1) * 8;
+    grad_reduce_kernel<<<(unsigned)((lanes + 255) / 256), 256, 0, s>>>(work, nsplit, M, N, g, off_w, off_b);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 size_t train_work_bytes(int max_b, int max_rows, int max_cols) {
-    const size_t nsplit = (size_t)(max_b + GKC - 1) / GKC;
+    const size_t nsplit = (size_t)(max_b + GKC_MIN - 1) / GKC_MIN;
     return nsplit * (size_t)max_rows * (size_t)(max_cols + 1) * sizeof(double);
 }
 
 cudaError_t train_forward(const NetDev& n, BatchCol x, const uint32_t* idx, int b, cudaStream_t s, long long r0) {
     if (b <= 0) return cudaSuccess;
     int W = 0, smem = 0;
-    cudaError_t e = row_block(n.n_wf, n.in_pad + 2 * n.h_pad, &W, &smem);
+    cudaError_t e = row_block(n.n_wf, 0, &W, &smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -323,7 +335,7 @@ cudaError_t train_backward(const NetDev& n, BatchCol x, const uint32_t* idx, int
     cudaError_t e = grad(n.dout, (int)L, n.n_out, n.h2, (int)L, x, idx, 0, n.n_h, b, n.g, oW3, ob3, work, s);
     if (e != cudaSuccess) return e;
     int W = 0, smem = 0;
-    if ((e = row_block(n.n_wb, n.out_pad + 2 * n.h_pad, &W, &smem)) != cudaSuccess) return e;
+    if ((e = row_block(n.n_wb, 0, &W, &smem)) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     bwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, b);
@@ -346,9 +358,9 @@ cudaError_t train_adam(const NetDev& n, double lr, double beta1, double beta2, d
     return cudaGetLastError();
 }
 
-cudaError_t train_stats(const float* stats, int ld, int b, float* out, cudaStream_t s) {
-    stats_kernel<<<4, 256, 0, s>>>(stats, ld, b, out);
-    return cudaGetLastError();
+cudaError_t train_stats(const float* stats, int ld, int b, float* out, double* work, cudaStream_t s) {
+    // four row sums: the bias column of the split-K reduction
+    return grad(stats, ld, 4, nullptr, 0, BatchCol{nullptr, 1, 1}, nullptr, 0, 0, b, out, 0, 0, work, s);
 }
 
 // ── the collector side of an update: rewards, GAE, normalization ────────

@@ -69,7 +69,7 @@ def test_shuffled_update_equals_host_ordered_update():
         out.append((t.params(0), t.params(1)))
         t.close()
     for a, b in zip(out[0], out[1]):
-        assert np.max(np.abs(a - b)) <= 1e-9
+        assert np.max(np.abs(a - b)) <= 1e-7  # the row order changes only the f32 stage rounding
 
 
 def test_c5_iterations_run_and_learn_nothing_nonfinite():
