@@ -146,6 +146,8 @@ struct phyzb_trainer {
     float* reduced = nullptr;  // [4]
     float* reduced_host = nullptr;
     double* work = nullptr;
+    float* xa = nullptr;  // a minibatch's actor / critic inputs, gathered [n_in][max_b]
+    float* xc = nullptr;
     // the batch the update reads: the uploaded columns, or device arrays
     // (phyzb_trainer_set_batch_device)
     pz::BatchCol c_obs_a{}, c_obs_c{}, c_act{}, c_logp{}, c_adv{}, c_ret{};
@@ -162,7 +164,7 @@ void destroy_trainer(phyzb_trainer* t) {
     free_net(t->actor);
     free_net(t->critic);
     void* bufs[] = {t->obs_a, t->obs_c,   t->act,   t->logp,    t->adv,  t->ret,  t->upload_raw,
-                    t->order, t->dlogstd, t->stats, t->reduced, t->work, t->ac};
+                    t->order, t->dlogstd, t->stats, t->reduced, t->work, t->ac, t->xa, t->xc};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (t->reduced_host) cudaFreeHost(t->reduced_host);
@@ -214,17 +216,25 @@ int run_update(phyzb_trainer* t, const phyzb_ppo_cfg* cfg, phyzb_update_stats* o
         for (long long start = 0; start < N; start += cfg->minibatch) {
             const int b = (int)std::min<long long>(cfg->minibatch, N - start);
             const uint32_t* idx = t->order + (size_t)ep * N + start;
+            // the minibatch's inputs, gathered once (one copy when actor and
+            // critic read the same column)
+            PZ_CUDA(pz::train_gather(t->c_obs_a, idx, b, t->actor.d.n_in, t->xa, L, s));
+            const bool same = t->c_obs_c.base == t->c_obs_a.base && t->c_obs_c.N == t->c_obs_a.N &&
+                              t->c_obs_c.F == t->c_obs_a.F && t->critic.d.n_in == t->actor.d.n_in;
+            if (!same) PZ_CUDA(pz::train_gather(t->c_obs_c, idx, b, t->critic.d.n_in, t->xc, L, s));
+            const pz::BatchCol xa{t->xa, L, t->actor.d.n_in};
+            const pz::BatchCol xc{same ? t->xa : t->xc, L, t->critic.d.n_in};
             // actor
-            PZ_CUDA(pz::train_forward(t->actor.d, t->c_obs_a, idx, b, s));
+            PZ_CUDA(pz::train_forward(t->actor.d, xa, nullptr, b, s));
             PZ_CUDA(pz::train_ppo_grad(t->actor.d, pa, t->c_act, t->c_logp, t->c_adv, idx, b, t->dlogstd, t->stats,
                                        s));
             PZ_CUDA(pz::train_row_sums(t->dlogstd, t->actor.d.n_out, L, b, t->actor.d.g, pa.logstd_off, t->work, s));
-            PZ_CUDA(pz::train_backward(t->actor.d, t->c_obs_a, idx, b, t->work, s));
+            PZ_CUDA(pz::train_backward(t->actor.d, xa, nullptr, b, t->work, s));
             PZ_TRY(adam_step(t, t->actor));
             // critic
-            PZ_CUDA(pz::train_forward(t->critic.d, t->c_obs_c, idx, b, s));
+            PZ_CUDA(pz::train_forward(t->critic.d, xc, nullptr, b, s));
             PZ_CUDA(pz::train_value_grad(t->critic.d, pa, t->c_ret, idx, b, t->stats, s));
-            PZ_CUDA(pz::train_backward(t->critic.d, t->c_obs_c, idx, b, t->work, s));
+            PZ_CUDA(pz::train_backward(t->critic.d, xc, nullptr, b, t->work, s));
             PZ_TRY(adam_step(t, t->critic));
             // the brake: the minibatch's statistics (summed over ranks) to the host
             PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, t->work, s));
@@ -314,7 +324,8 @@ int phyzb_trainer_create(int32_t device, phyzb_net_dims actor, phyzb_net_dims cr
     } cols[] = {{&t->obs_a, C * actor.n_in}, {&t->obs_c, C * critic.n_in}, {&t->act, C * actor.n_out},
                 {&t->logp, C},              {&t->adv, C},                 {&t->ret, C},
                 {&t->upload_raw, C * widest}, {&t->dlogstd, (size_t)pad32(actor.n_out) * max_b},
-                {&t->stats, (size_t)4 * max_b}, {&t->reduced, 4}};
+                {&t->stats, (size_t)4 * max_b}, {&t->reduced, 4},
+                {&t->xa, (size_t)actor.n_in * max_b}, {&t->xc, (size_t)critic.n_in * max_b}};
     for (auto& c : cols)
         if (cudaMalloc((void**)c.p, c.n * 4) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc batch"));
     if (cudaHostAlloc((void**)&t->reduced_host, 16, cudaHostAllocDefault) != cudaSuccess)

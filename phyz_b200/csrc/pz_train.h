@@ -54,6 +54,8 @@ struct PpoArgs {
 // `net`, activations into its buffers
 cudaError_t train_forward(const NetDev& net, BatchCol x, const uint32_t* idx, int b, cudaStream_t s,
                           long long r0 = 0);
+// dst[k][r] = x(idx[r], k) for k < F, r < b (ld = row stride of dst)
+cudaError_t train_gather(BatchCol x, const uint32_t* idx, int b, int F, float* dst, int ld, cudaStream_t s);
 // actor: dL/dmean into net.dout, per-row dL/dlogstd, stats cols 0-2
 cudaError_t train_ppo_grad(const NetDev& actor, const PpoArgs& a, BatchCol act, BatchCol logp_old, BatchCol adv,
                            const uint32_t* idx, int b, float* dlogstd, float* stats, cudaStream_t s);

@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
             const int m = m0 + mm, n = n0 + mm;
             As[kk][mm] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
             float bv = 0.0f;
-            if (r < r1 && n < N) bv = gather ? col(x, idx[r], n) : Bact[(long long)n * ldb + r];
+            if (r < r1 && n < N) bv = gather ? col(x, idx ? (long long)idx[r] : r, n) : Bact[(long long)n * ldb + r];
             Bs[kk][mm] = bv;
         }
         __syncthreads();
@@ -208,6 +208,16 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
         }
         if (bias_col) row[N] = rs[i];
     }
+}
+
+// dst[k][r] = x(idx[r], k): a minibatch's rows of a batch column made
+// contiguous once (random reads), read coalesced by every later pass.
+__global__ void gather_kernel(const BatchCol x, const uint32_t* idx, int b, int F, float* dst, int ld) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= b) return;
+    const long long s = idx[r];
+    const float* xr = x.base + (s / x.N) * (long long)x.F * x.N + s % x.N;
+    for (int k = 0; k < F; k++) dst[(long long)k * ld + r] = xr[(long long)k * x.N];
 }
 
 // g[off_w + m * N + n] (n < N) and g[off_b + m] (bias) from the splits: 8
@@ -308,6 +318,12 @@ cudaError_t train_forward(const NetDev& n, BatchCol x, const uint32_t* idx, int 
     e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     fwd_kernel<<<(b + W - 1) / W, W, smem, s>>>(n, x, idx, r0, b);
+    return cudaGetLastError();
+}
+
+cudaError_t train_gather(BatchCol x, const uint32_t* idx, int b, int F, float* dst, int ld, cudaStream_t s) {
+    if (b <= 0) return cudaSuccess;
+    gather_kernel<<<(b + 255) / 256, 256, 0, s>>>(x, idx, b, F, dst, ld);
     return cudaGetLastError();
 }
 
