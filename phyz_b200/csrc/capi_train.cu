@@ -32,8 +32,9 @@ struct Net {
 };
 
 void free_net(Net& n) {
-    void* bufs[] = {n.d.p,  n.d.m,   n.d.v,   n.d.g,   n.d.wflat, n.d.wf,  n.d.wb,  n.d.h1,
-                    n.d.h2, n.d.out, n.d.dout, n.d.dh2, n.d.dh1,  n.d_posf, n.d_posb};
+    // (n.d.g points into the trainer's gradient block)
+    void* bufs[] = {n.d.p,  n.d.m,    n.d.v,   n.d.wflat, n.d.wf,  n.d.wb,   n.d.h1,
+                    n.d.h2, n.d.out,  n.d.dout, n.d.dh2,  n.d.dh1, n.d_posf, n.d_posb};
     for (void* b : bufs)
         if (b) cudaFree(b);
     n = Net{};
@@ -84,7 +85,6 @@ int alloc_net(Net& n, phyzb_net_dims dims, int extra, int max_b) {
     PZ_CUDA(cudaMalloc((void**)&d.p, P * 8));
     PZ_CUDA(cudaMalloc((void**)&d.m, P * 8));
     PZ_CUDA(cudaMalloc((void**)&d.v, P * 8));
-    PZ_CUDA(cudaMalloc((void**)&d.g, P * 4));
     PZ_CUDA(cudaMalloc((void**)&d.wflat, P * 4));
     PZ_CUDA(cudaMalloc((void**)&d.wf, (size_t)d.n_wf * 4));
     PZ_CUDA(cudaMalloc((void**)&d.wb, (size_t)d.n_wb * 4));
@@ -104,7 +104,6 @@ int alloc_net(Net& n, phyzb_net_dims dims, int extra, int max_b) {
     PZ_CUDA(cudaMemset(d.p, 0, P * 8));
     PZ_CUDA(cudaMemset(d.m, 0, P * 8));
     PZ_CUDA(cudaMemset(d.v, 0, P * 8));
-    PZ_CUDA(cudaMemset(d.g, 0, P * 4));
     PZ_CUDA(cudaMemset(d.wflat, 0, P * 4));
     PZ_CUDA(cudaMemset(d.wf, 0, (size_t)d.n_wf * 4));
     PZ_CUDA(cudaMemset(d.wb, 0, (size_t)d.n_wb * 4));
@@ -143,7 +142,8 @@ struct phyzb_trainer {
     size_t order_cap = 0;
     float* dlogstd = nullptr;  // [out_pad][max_b]
     float* stats = nullptr;    // [4][max_b]
-    float* reduced = nullptr;  // [4]
+    float* reduced = nullptr;  // [4], inside gblock
+    float* gblock = nullptr;   // actor g | critic g | minibatch statistics: one all-reduce
     float* reduced_host = nullptr;
     double* work = nullptr;
     float* xa = nullptr;  // a minibatch's actor / critic inputs, gathered [n_in][max_b]
@@ -164,7 +164,7 @@ void destroy_trainer(phyzb_trainer* t) {
     free_net(t->actor);
     free_net(t->critic);
     void* bufs[] = {t->obs_a, t->obs_c,   t->act,   t->logp,    t->adv,  t->ret,  t->upload_raw,
-                    t->order, t->dlogstd, t->stats, t->reduced, t->work, t->ac, t->xa, t->xc};
+                    t->order, t->dlogstd, t->stats, t->gblock, t->work, t->ac, t->xa, t->xc};
     for (void* b : bufs)
         if (b) cudaFree(b);
     if (t->reduced_host) cudaFreeHost(t->reduced_host);
@@ -187,10 +187,9 @@ int upload_col(phyzb_trainer* t, const float* host, int F, long long n, float* d
     return PHYZB_OK;
 }
 
-// One Adam step of `n`; data-parallel: the gradient is first summed over the
-// ranks and averaged inside the step.
+// One Adam step of `n` (data-parallel: its gradient is already summed over
+// the ranks; the step averages it).
 int adam_step(phyzb_trainer* t, Net& n) {
-    PZ_TRY(comm_allreduce_sum(t->comm, n.d.g, (size_t)n.d.n_param, false, t->stream));
     n.t += 1;
     const phyzb_adam_cfg& a = n.adam;
     const double bc1 = 1.0 - std::pow(a.beta1, (double)n.t);
@@ -230,15 +229,19 @@ int run_update(phyzb_trainer* t, const phyzb_ppo_cfg* cfg, phyzb_update_stats* o
                                        s));
             PZ_CUDA(pz::train_row_sums(t->dlogstd, t->actor.d.n_out, L, b, t->actor.d.g, pa.logstd_off, t->work, s));
             PZ_CUDA(pz::train_backward(t->actor.d, xa, nullptr, b, t->work, s));
-            PZ_TRY(adam_step(t, t->actor));
             // critic
             PZ_CUDA(pz::train_forward(t->critic.d, xc, nullptr, b, s));
             PZ_CUDA(pz::train_value_grad(t->critic.d, pa, t->c_ret, idx, b, t->stats, s));
             PZ_CUDA(pz::train_backward(t->critic.d, xc, nullptr, b, t->work, s));
-            PZ_TRY(adam_step(t, t->critic));
-            // the brake: the minibatch's statistics (summed over ranks) to the host
+            // the minibatch's statistics next to the gradients; data-parallel:
+            // all of it summed over the ranks in one all-reduce
             PZ_CUDA(pz::train_stats(t->stats, L, b, t->reduced, t->work, s));
-            PZ_TRY(comm_allreduce_sum(t->comm, t->reduced, 4, false, s));
+            PZ_TRY(comm_allreduce_sum(t->comm, t->gblock,
+                                      (size_t)t->actor.d.n_param + t->critic.d.n_param + 4, false, s));
+            // actor and critic are independent: both steps after both backward passes
+            PZ_TRY(adam_step(t, t->actor));
+            PZ_TRY(adam_step(t, t->critic));
+            // the brake: the statistics to the host
             PZ_CUDA(cudaMemcpyAsync(t->reduced_host, t->reduced, 16, cudaMemcpyDeviceToHost, s));
             PZ_TRY(comm_wait(t->comm, s, 120.0));
             const float* r = t->reduced_host;
@@ -324,10 +327,16 @@ int phyzb_trainer_create(int32_t device, phyzb_net_dims actor, phyzb_net_dims cr
     } cols[] = {{&t->obs_a, C * actor.n_in}, {&t->obs_c, C * critic.n_in}, {&t->act, C * actor.n_out},
                 {&t->logp, C},              {&t->adv, C},                 {&t->ret, C},
                 {&t->upload_raw, C * widest}, {&t->dlogstd, (size_t)pad32(actor.n_out) * max_b},
-                {&t->stats, (size_t)4 * max_b}, {&t->reduced, 4},
+                {&t->stats, (size_t)4 * max_b},
                 {&t->xa, (size_t)actor.n_in * max_b}, {&t->xc, (size_t)critic.n_in * max_b}};
     for (auto& c : cols)
         if (cudaMalloc((void**)c.p, c.n * 4) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc batch"));
+    const size_t ng = (size_t)t->actor.d.n_param + t->critic.d.n_param + 4;
+    if (cudaMalloc((void**)&t->gblock, ng * 4) != cudaSuccess || cudaMemset(t->gblock, 0, ng * 4) != cudaSuccess)
+        return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc gradients"));
+    t->actor.d.g = t->gblock;
+    t->critic.d.g = t->gblock + t->actor.d.n_param;
+    t->reduced = t->critic.d.g + t->critic.d.n_param;
     if (cudaHostAlloc((void**)&t->reduced_host, 16, cudaHostAllocDefault) != cudaSuccess)
         return bail(fail(PHYZB_ERR_CUDA, "cudaHostAlloc"));
     const int rows = std::max(std::max(actor.n_h, critic.n_h), actor.n_out);
