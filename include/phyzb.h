@@ -240,6 +240,14 @@ int phyzb_readback_qdd(phyzb_sim* sim, double* qdd);
  * PHYZB_CONTACT_STRIDE of the last step. PHYZB_ERR_STATE if contact off. */
 int phyzb_readback_contacts(phyzb_sim* sim, double* contact_state);
 
+/* State history (mod.rs:1316-1376): `slots` snapshots of q / v kept on the
+ * device; record_state copies the current state into a slot after every
+ * launch so far (the host does not wait); readback returns rows
+ * [n][nworld][nv]. Re-enabling with the same slot count keeps the buffers. */
+int phyzb_enable_state_history(phyzb_sim* sim, int32_t slots);
+int phyzb_record_state(phyzb_sim* sim, int32_t slot);
+int phyzb_readback_state_history(phyzb_sim* sim, int32_t slot0, int32_t n, double* q, double* v);
+
 /* ── device-resident path ─────────────────────────────────────────────── */
 
 /* Device pointers and layout of the resident state (zero-copy). */

@@ -257,6 +257,56 @@ class RefHost:
         return qf, vf, qdd, cs
 
 
+REF_CUDA_SO = HERE / "_ref" / "libphyz_ref_cuda.so"
+
+
+class RefCuda:
+    """The reference's own CUDA kernels on this GPU (ref_cuda_driver.cu):
+    contact -> aba -> integrate per step, 64-thread blocks, one captured
+    graph per rollout. AoS f32 rows, as the reference holds them."""
+
+    def __init__(self, refhost):
+        if not REF_CUDA_SO.exists():
+            build()
+        if not REF_CUDA_SO.exists():
+            raise RuntimeError(f"{REF_CUDA_SO} missing and the reference tree is not available to build it")
+        self.host = refhost
+        self.lib = C.CDLL(str(REF_CUDA_SO))
+        u = C.c_uint32
+        self.lib.phyzref_cuda_rollout.argtypes = [u, u, u, C.c_float, C.c_float, C.c_float, C.c_float, _F, _F, _F,
+                                                  _F, _F, _F, C.c_int64, C.c_int32, C.c_int32, _F, _F, _F]
+        refhost.lib.phyzref_pack_cparams.argtypes = [u, u, u, C.c_float, C.c_float, C.c_float, _F]
+
+    def rollout(self, model, q, v, ctrl, nsteps, schedule=False, contact=None, reps=0):
+        """Returns (q, v, qdd, contact_state [n][nb][56], best ms of `reps` replays)."""
+        cm, keep = model.to_c()
+        nb, nv, n = model.nbodies, model.nv, q.shape[0]
+        bodies = np.zeros(nb * RefHost.BODY_STRIDE, np.float32)
+        self.host.lib.phyzref_pack_bodies(C.addressof(cm), _f(bodies))
+        geom = cp = None
+        if contact is not None:
+            ground, fr, k, d = contact
+            k = np.ascontiguousarray(np.broadcast_to(k, (nb,)), np.float64)
+            d = np.ascontiguousarray(np.broadcast_to(d, (nb,)), np.float64)
+            geom = np.zeros(nb * RefHost.GEOM_STRIDE, np.float32)
+            self.host.lib.phyzref_pack_geometries(C.addressof(cm), _d(k), _d(d), _f(geom))
+            cp = np.zeros(32, np.float32)
+            self.host.lib.phyzref_pack_cparams(n, nb, nv, float(ground), float(model.dt), float(fr), _f(cp))
+        qf = np.ascontiguousarray(q, np.float32).copy()
+        vf = np.ascontiguousarray(v, np.float32).copy()
+        cf = np.ascontiguousarray(ctrl, np.float32)
+        qdd = np.zeros((n, nv), np.float32)
+        cs = np.zeros((n, nb, 56), np.float32)
+        ms = np.zeros(1, np.float32)
+        gx, gy, gz = (float(x) for x in model.gravity)
+        rc = self.lib.phyzref_cuda_rollout(n, nv, nb, float(model.dt), gx, gy, gz, _f(bodies), _f(geom), _f(cp),
+                                           _f(qf), _f(vf), _f(cf), n * nv if schedule else 0, nsteps, reps,
+                                           _f(qdd), _f(cs), _f(ms))
+        if rc != 0:
+            raise RuntimeError(f"reference CUDA rollout failed: cudaError {-rc}")
+        return qf, vf, qdd, cs, float(ms[0])
+
+
 def cpu_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))

@@ -211,6 +211,9 @@ SIGNATURES = {
     "phyzb_policy_history_view": (C.c_int, [_P, C.POINTER(PhyzbPolicyHistory)]),
     "phyzb_policy_advantages": (C.c_int, [_P, _P, _P, C.POINTER(PhyzbReturnCfg), C.c_void_p, C.c_void_p, _D]),
     "phyzb_policy_sync_from_trainer": (C.c_int, [_P, _P]),
+    "phyzb_enable_state_history": (C.c_int, [_P, C.c_int32]),
+    "phyzb_record_state": (C.c_int, [_P, C.c_int32]),
+    "phyzb_readback_state_history": (C.c_int, [_P, C.c_int32, C.c_int32, _D, _D]),
     "phyzb_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
     "phyzb_comm_init": (C.c_int, [C.POINTER(C.c_uint8), C.c_int32, C.c_int32, C.c_int32, C.c_double,
                                   C.POINTER(_P)]),

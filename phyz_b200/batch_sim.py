@@ -245,6 +245,21 @@ class BatchSim:
     def objective_device(self, kind: int, out_ptr: int) -> None:
         check(self._lib.phyzb_objective_device(self._h, int(kind), C.c_void_p(out_ptr)))
 
+    # ── state history (cuda/mod.rs:1316-1376) ───────────────────────────────
+    def enable_state_history(self, slots: int) -> None:
+        check(self._lib.phyzb_enable_state_history(self._h, int(slots)))
+        self._hist = int(slots)
+
+    def record_state(self, slot: int) -> None:
+        check(self._lib.phyzb_record_state(self._h, int(slot)))
+
+    def readback_state_history(self, slot0: int, n: int):
+        """(q, v) rows [n][nworld][nv]."""
+        q = np.zeros((n, self.nworld, self.nv))
+        v = np.zeros((n, self.nworld, self.nv))
+        check(self._lib.phyzb_readback_state_history(self._h, int(slot0), int(n), dptr(q), dptr(v)))
+        return q, v
+
     # ── on-device control loop (cuda/mod.rs:1081-1313) ─────────────────────
     def enable_policy(self, spec) -> None:
         cs, keep = spec.to_c()

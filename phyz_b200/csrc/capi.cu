@@ -269,6 +269,8 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(s->lay[0].blob);
     free_ptr(s->lay[1].blob);
     free_ptr(s->staging);
+    free_ptr(s->hist_q);
+    free_ptr(s->hist_v);
     for (int b = 0; b < 2; b++) {
         free_ptr(s->pipe_raw[b]);
         free_ptr(s->pipe_soa[b]);
@@ -562,6 +564,47 @@ int phyzb_readback_states(phyzb_sim* s, double* q, double* v) {
     DeviceGuard g(s->device);
     if (q) PZ_TRY(download_rows(s, s->q, s->nv, q));
     if (v) PZ_TRY(download_rows(s, s->v, s->nv, v));
+    return PHYZB_OK;
+}
+
+int phyzb_enable_state_history(phyzb_sim* s, int32_t slots) {
+    PZ_TRY(check_sim(s));
+    if (slots < 1) return fail(PHYZB_ERR_INVALID, "state history needs at least one slot");
+    if (s->hist_slots == slots) return PHYZB_OK;  // re-enabling keeps the buffers (mod.rs:1324-1326)
+    DeviceGuard g(s->device);
+    free_ptr(s->hist_q);
+    free_ptr(s->hist_v);
+    s->hist_slots = 0;
+    PZ_CUDA(cudaMalloc(&s->hist_q, (size_t)slots * s->state_bytes()));
+    PZ_CUDA(cudaMalloc(&s->hist_v, (size_t)slots * s->state_bytes()));
+    s->hist_slots = slots;
+    return PHYZB_OK;
+}
+
+int phyzb_record_state(phyzb_sim* s, int32_t slot) {
+    PZ_TRY(check_sim(s));
+    if (!s->hist_slots) return fail(PHYZB_ERR_STATE, "state history not enabled — call enable_state_history first");
+    if (slot < 0 || slot >= s->hist_slots)
+        return fail(PHYZB_ERR_INVALID, "history slot " + std::to_string(slot) + " exceeds " +
+                                           std::to_string(s->hist_slots) + " slots");
+    DeviceGuard g(s->device);
+    const size_t b = s->state_bytes();
+    PZ_CUDA(cudaMemcpyAsync((char*)s->hist_q + (size_t)slot * b, s->q, b, cudaMemcpyDeviceToDevice, s->stream));
+    PZ_CUDA(cudaMemcpyAsync((char*)s->hist_v + (size_t)slot * b, s->v, b, cudaMemcpyDeviceToDevice, s->stream));
+    return PHYZB_OK;
+}
+
+int phyzb_readback_state_history(phyzb_sim* s, int32_t slot0, int32_t n, double* q, double* v) {
+    PZ_TRY(check_sim(s));
+    if (!s->hist_slots) return fail(PHYZB_ERR_STATE, "state history not enabled");
+    if (slot0 < 0 || n < 0 || (int64_t)slot0 + n > s->hist_slots)
+        return fail(PHYZB_ERR_INVALID, "history range outside 0.." + std::to_string(s->hist_slots));
+    DeviceGuard g(s->device);
+    const size_t b = s->state_bytes(), rows = (size_t)s->nworld * s->nv;
+    for (int k = 0; k < n; k++) {
+        if (q) PZ_TRY(download_rows(s, (char*)s->hist_q + (size_t)(slot0 + k) * b, s->nv, q + k * rows));
+        if (v) PZ_TRY(download_rows(s, (char*)s->hist_v + (size_t)(slot0 + k) * b, s->nv, v + k * rows));
+    }
     return PHYZB_OK;
 }
 

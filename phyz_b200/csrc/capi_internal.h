@@ -107,6 +107,9 @@ struct phyzb_sim {
     } lay[2];
     int use = 0;
     void* staging = nullptr;  // device, AoS f64 rows for host copies
+    void* hist_q = nullptr;   // state history [slot][nv][nworld] (enable_state_history)
+    void* hist_v = nullptr;
+    int hist_slots = 0;
     size_t staging_bytes = 0;
     // bulk per-step control pipeline (phyzb_step_with_controls)
     void* pipe_raw[2] = {nullptr, nullptr};

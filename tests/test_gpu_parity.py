@@ -290,3 +290,28 @@ def test_tensor_memory_layout(oracle, monkeypatch, name, precision):
     for a, b in zip(out["1"], out["0"]):
         if a is not None:
             assert rel_err(a, b) <= same, rel_err(a, b)
+
+
+def test_state_history():
+    """mod.rs:1316-1376: snapshots recorded between launches read back as the
+    states at those times; re-enabling with the same slot count keeps them."""
+    name = "c3_quadruped"
+    model, q0, v0, sched, contact = config_inputs(name, 40, 6)
+    sim = BatchSim(model, 40, precision="f32")
+    sim.enable_ground_contact(*contact)
+    sim.load_states(q0, v0, sched[0])
+    sim.enable_state_history(3)
+    want = []
+    for slot in range(3):
+        sim.step_many(2)
+        sim.record_state(slot)
+        want.append(sim.readback_states())
+    sim.enable_state_history(3)
+    q, v = sim.readback_state_history(0, 3)
+    for k in range(3):
+        assert np.array_equal(q[k], want[k][0]) and np.array_equal(v[k], want[k][1])
+    with pytest.raises(PhyzbError):
+        sim.record_state(3)
+    with pytest.raises(PhyzbError):
+        sim.readback_state_history(2, 2)
+    sim.close()
