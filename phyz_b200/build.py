@@ -25,8 +25,8 @@ OBJ = PKG / "_build"
 SOURCES = ["stepper.cu", "capi.cu", "capi_policy.cu", "capi_train.cu", "policy.cu", "train.cu", "flops.cpp",
            "peaks.cu"]
 VARIANT_SOURCE = "rollout_variants.cu"
-FEAT_COUNT = 8  # pz_variants.h
-VARIANTS = [(t, f) for t in ("float", "double") for f in range(FEAT_COUNT)]
+FEAT_COUNT = 16  # pz_variants.h; bit 8 only with bit 4 (feat_valid)
+VARIANTS = [(t, f) for t in ("float", "double") for f in range(FEAT_COUNT) if not (f & 8 and not f & 4)]
 HEADERS = ["pz_types.cuh", "pz_model.cuh", "pz_world.cuh", "pz_launch.h", "pz_pack.h", "pz_variants.h",
            "stepper_kernels.cuh", "pz_policy.h", "capi_internal.h", "pz_mlp.cuh", "pz_train.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -73,7 +73,8 @@ struct PackInfo {
     int off_bi = 0, off_pd = 0, off_pdmap = 0, bytes = 0;
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
-    int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges
+    int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges,
+                         // 8 = (with 4) every relabel is the shift-1 cycle
     int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
 };
 
@@ -331,8 +332,13 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
     for (int i = 0; i < nb; i++)
         if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;
     if (cfg.contact) info.feat |= 2;
+    bool all_one = true;
     for (int i = 0; i < nb; i++)
-        if ((bi[i].flags & F_ZHINGE) && bi[i].qshift != 0) info.feat |= 4;
+        if (bi[i].flags & F_ZHINGE) {
+            if (bi[i].qshift != 0) info.feat |= 4;
+            all_one = all_one && bi[i].qshift == 1;
+        }
+    if ((info.feat & 4) && all_one) info.feat |= 8;  // every relabel is the shift-1 cycle
     return info;
 }
 

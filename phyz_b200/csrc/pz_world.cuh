@@ -33,8 +33,11 @@ namespace pz {
 // Compile-time feature mask of a kernel variant: a model without ball/free
 // joints (resp. without contact) gets a kernel without that code at all.
 // Kernel feature bits: ball/free joints present, ground contact on, some
-// hinge frame relabelled by a non-identity cyclic permutation.
-enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4 };
+// hinge frame relabelled by a non-identity cyclic permutation, and (with
+// FEAT_PERM) every relabelled hinge relabelled by the same shift 1 -- a chain
+// whose axes cycle x, y, z -- so the relabel is a compile-time register
+// renaming instead of a run-time branch.
+enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8 };
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
@@ -192,6 +195,7 @@ PZ_HD void ai_cperm_fixed(AI<T>& I) {
 // into the permuted slots instead of moving registers after the fact.
 template <int AX, int FEAT, class T>
 PZ_HD V3<T> rot_fwd3(int q, const T& c, const T& s, const V3<T>& x) {
+    if constexpr ((FEAT & FEAT_PERM1) != 0) return prot<AX>(c, s, cperm<1>(x));
     if constexpr ((FEAT & FEAT_PERM) != 0) {
         if (q == 1) return prot<AX>(c, s, cperm<1>(x));
         if (q == 2) return prot<AX>(c, s, cperm<2>(x));
@@ -200,6 +204,8 @@ PZ_HD V3<T> rot_fwd3(int q, const T& c, const T& s, const V3<T>& x) {
 }
 template <int AX, int FEAT, class T>
 PZ_HD SV<T> rot_fwd(int q, const T& c, const T& s, const SV<T>& m) {
+    if constexpr ((FEAT & FEAT_PERM1) != 0)
+        return mksv<T>(prot<AX>(c, s, cperm<1>(m.w)), prot<AX>(c, s, cperm<1>(m.l)));
     if constexpr ((FEAT & FEAT_PERM) != 0) {
         if (q == 1) return mksv<T>(prot<AX>(c, s, cperm<1>(m.w)), prot<AX>(c, s, cperm<1>(m.l)));
         if (q == 2) return mksv<T>(prot<AX>(c, s, cperm<2>(m.w)), prot<AX>(c, s, cperm<2>(m.l)));
@@ -208,6 +214,8 @@ PZ_HD SV<T> rot_fwd(int q, const T& c, const T& s, const SV<T>& m) {
 }
 template <int AX, int FEAT, class T>
 PZ_HD SV<T> rot_bwd(int q, const T& c, const T& s, const SV<T>& f) {
+    if constexpr ((FEAT & FEAT_PERM1) != 0)
+        return mksv<T>(cperm<2>(prot_t<AX>(c, s, f.w)), cperm<2>(prot_t<AX>(c, s, f.l)));
     if constexpr ((FEAT & FEAT_PERM) != 0) {
         if (q == 1) return mksv<T>(cperm<2>(prot_t<AX>(c, s, f.w)), cperm<2>(prot_t<AX>(c, s, f.l)));
         if (q == 2) return mksv<T>(cperm<1>(prot_t<AX>(c, s, f.w)), cperm<1>(prot_t<AX>(c, s, f.l)));
@@ -216,6 +224,11 @@ PZ_HD SV<T> rot_bwd(int q, const T& c, const T& s, const SV<T>& f) {
 }
 template <int AX, int FEAT, class T>
 PZ_HD void ai_rot_bwd(int q, const T& c, const T& s, AI<T>& I) {
+    if constexpr ((FEAT & FEAT_PERM1) != 0) {
+        ai_prot<AX>(c, s, I);
+        ai_cperm_fixed<1>(I);
+        return;
+    }
     if constexpr ((FEAT & FEAT_PERM) != 0) {
         if (q == 1) {
             ai_prot<AX>(c, s, I);
@@ -501,7 +514,7 @@ PZ_HD void st_sv(const Scr& S, int s, const SV<T>& v) {
 // Generalized input force on DOF d: the control (or the PD servo output,
 // phyz_kernels.cu:464-483) plus the passive terms of joint.rs:232-247.
 template <class T, class Scr>
-PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S, int k) {
+PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S, int k, bool one_dof) {
     const int d = bi.off + k;
     const T qd = S(M.nv + d);
     T in = S(bi.s_w0 + k);
@@ -514,7 +527,7 @@ PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, co
         }
     }
     T f = in - bt.damping * qd;
-    if (bi.ndof == 1) {
+    if (one_dof) {
         const T q = S(d);
         // the spring term is exact with stiffness 0, and cheaper than a branch
         if (!Counting<T>::value || (bi.flags & F_SPRING)) f = f - bt.stiffness * (q - bt.spring_ref);
@@ -589,7 +602,7 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
         for (int b = 0; b < ND; b++) L[a][b] = T(0);
     T u[ND];
 #pragma unroll
-    for (int k = 0; k < ND; k++) u[k] = dof_force(M, bi, bt, S, k) - svget(p, k);
+    for (int k = 0; k < ND; k++) u[k] = dof_force(M, bi, bt, S, k, false) - svget(p, k);
     bool ok = true;
 #pragma unroll
     for (int a = 0; a < ND; a++) {
@@ -1093,7 +1106,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
             sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
         }
         const T D = sU + bt.d_extra;
-        const T u = dof_force(M, bi, bt, S, 0) - sp;
+        const T u = dof_force(M, bi, bt, S, 0, AX >= 0 || bi.ndof == 1) - sp;
         // aba.rs:240-242: a singular D skips the body (W = 0, w0 = 0). The
         // record store happens once, outside any per-world branch, because
         // a Tensor-Memory store is warp-wide.

@@ -77,7 +77,8 @@ template <class T, bool TM, int F = 0>
 static cudaError_t config_by_feat(int feat, int scratch, int model_bytes, long long nworld, int tmem_cols,
                                   LaunchCfg* out) {
     if constexpr (F < FEAT_COUNT) {
-        if (feat == F) return config_variant<T, F, TM>(g_limits, scratch, model_bytes, nworld, tmem_cols, out);
+        if constexpr (feat_valid(F))
+            if (feat == F) return config_variant<T, F, TM>(g_limits, scratch, model_bytes, nworld, tmem_cols, out);
         return config_by_feat<T, TM, F + 1>(feat, scratch, model_bytes, nworld, tmem_cols, out);
     } else {
         return cudaErrorInvalidValue;
@@ -86,10 +87,11 @@ static cudaError_t config_by_feat(int feat, int scratch, int model_bytes, long l
 template <class T, bool TM, int F = 0>
 static cudaError_t launch_by_feat(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
     if constexpr (F < FEAT_COUNT) {
-        if (a.feat == F) {
-            launch_variant<T, F, TM>(a, cfg, s);
-            return cudaSuccess;
-        }
+        if constexpr (feat_valid(F))
+            if (a.feat == F) {
+                launch_variant<T, F, TM>(a, cfg, s);
+                return cudaSuccess;
+            }
         return launch_by_feat<T, TM, F + 1>(a, cfg, s);
     } else {
         return cudaErrorInvalidValue;
@@ -99,10 +101,11 @@ template <class T, int F = 0>
 static cudaError_t objective_by_feat(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out,
                                      cudaStream_t s) {
     if constexpr (F < FEAT_COUNT) {
-        if (a.feat == F) {
-            launch_objective_variant<T, F>(a, cfg, kind, out, s);
-            return cudaSuccess;
-        }
+        if constexpr (feat_valid(F))
+            if (a.feat == F) {
+                launch_objective_variant<T, F>(a, cfg, kind, out, s);
+                return cudaSuccess;
+            }
         return objective_by_feat<T, F + 1>(a, cfg, kind, out, s);
     } else {
         return cudaErrorInvalidValue;

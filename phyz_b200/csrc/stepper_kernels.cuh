@@ -312,7 +312,7 @@ __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ 
             for (int j = 0; j < M.nv; j++) acc += S(j) * S(j);
             continue;
         }
-        pass1_all<FEAT & (FEAT_MULTI | FEAT_PERM)>(M, S);
+        pass1_all<FEAT & (FEAT_MULTI | FEAT_PERM | FEAT_PERM1)>(M, S);
         for (int i = 0; i < M.nb; i++) {
             const BodyI bi = M.bi[i];
             const BodyT<T>& bt = M.bt[i];
