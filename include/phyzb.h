@@ -422,6 +422,30 @@ typedef struct {
 } phyzb_return_cfg;
 int phyzb_policy_advantages(phyzb_sim* sim, phyzb_trainer* tr, struct phyzb_comm* comm, const phyzb_return_cfg* cfg,
                             float* adv, float* ret, double* stats);
+/* GAE(gamma, lambda) and the advantage normalization of
+ * phyzb_policy_advantages (one rank) over caller-owned device buffers --
+ * rewards [steps][nworld], values [steps + 1][nworld], adv and ret
+ * [steps][nworld], all float on `device` -- that allocates no device memory.
+ * It has no counterpart in the reference. It is meant for callers that must
+ * not let a library allocate: a host framework that has reserved the GPU's
+ * memory for its own allocator or holds the process to a fixed budget, or a
+ * latency-bound training loop, where cudaMalloc can fail or stall and
+ * cudaFree synchronizes the device. Its only scratch, the GAE kernel's
+ * per-block partial sums, lives in a static device array sized for
+ * PHYZB_GAE_NOALLOC_MAX_WORLDS worlds (1.5 MiB, held by every device that
+ * loads the library until exit); a larger nworld returns
+ * PHYZB_ERR_TOO_LARGE. The first call on a device looks that array's address
+ * up (cudaGetSymbolAddress), so make the first call on each device before
+ * any stream capture. All calls on a device share the array: calls whose
+ * kernels overlap on the device race, so order them on one stream or with
+ * events. Runs on `stream` (a cudaStream_t, NULL = the default stream);
+ * asynchronous unless `stats` (optional, host, 3 doubles: mean return per
+ * world, advantage mean and std before normalization) is given, in which case
+ * it waits for the stream. */
+#define PHYZB_GAE_NOALLOC_MAX_WORLDS (1 << 24)
+int phyzb_gae_noalloc(const float* rewards, const float* values, int64_t nworld, int32_t steps, double gamma,
+                      double lambda, int32_t normalize, int32_t device, void* stream, float* adv, float* ret,
+                      double* stats);
 /* The trainer's actor (weights, std = exp(log_std)) into the simulator's
  * policy, device to device. */
 int phyzb_policy_sync_from_trainer(phyzb_sim* sim, phyzb_trainer* tr);

@@ -21,6 +21,7 @@ ERR_TOO_LARGE = -6
 ERR_UNSUPPORTED = -7
 ERR_COMM = -8
 COMM_ID_BYTES = 128
+GAE_NOALLOC_MAX_WORLDS = 1 << 24
 
 F32 = 0
 F64 = 1
@@ -211,6 +212,8 @@ SIGNATURES = {
     "phyzb_policy_history_view": (C.c_int, [_P, C.POINTER(PhyzbPolicyHistory)]),
     "phyzb_policy_advantages": (C.c_int, [_P, _P, _P, C.POINTER(PhyzbReturnCfg), C.c_void_p, C.c_void_p, _D]),
     "phyzb_policy_sync_from_trainer": (C.c_int, [_P, _P]),
+    "phyzb_gae_noalloc": (C.c_int, [_P, _P, C.c_int64, C.c_int32, C.c_double, C.c_double, C.c_int32, C.c_int32, _P,
+                                    _P, _P, _D]),
     "phyzb_enable_state_history": (C.c_int, [_P, C.c_int32]),
     "phyzb_record_state": (C.c_int, [_P, C.c_int32]),
     "phyzb_readback_state_history": (C.c_int, [_P, C.c_int32, C.c_int32, _D, _D]),

@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libphyzb200.so"
 OBJ = PKG / "_build"
 SOURCES = ["stepper.cu", "capi.cu", "capi_policy.cu", "capi_train.cu", "policy.cu", "train.cu", "flops.cpp",
-           "peaks.cu"]
+           "peaks.cu", "capi_noalloc.cu"]
 VARIANT_SOURCE = "rollout_variants.cu"
 FEAT_COUNT = 16  # pz_variants.h; bit 8 only with bit 4 (feat_valid)
 VARIANTS = [(t, f) for t in ("float", "double") for f in range(FEAT_COUNT) if not (f & 8 and not f & 4)]

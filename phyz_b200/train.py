@@ -124,3 +124,22 @@ class Trainer:
             self.close()
         except Exception:
             pass
+
+
+def gae_noalloc(rewards_ptr: int, values_ptr: int, nworld: int, steps: int, gamma: float, lam: float, adv_ptr: int,
+                ret_ptr: int, normalize: bool = True, device: int = 0, stream: int = 0) -> tuple:
+    """GAE and advantage normalization over caller-owned device float
+    buffers (rewards [steps][nworld], values [steps + 1][nworld], adv and ret
+    [steps][nworld]) without any device allocation by the library: for
+    callers whose framework owns the GPU's memory or whose loop must not stall
+    on cudaMalloc/cudaFree. Scratch is a fixed static device array, so nworld
+    is capped at _lib.GAE_NOALLOC_MAX_WORLDS, and calls that overlap on one
+    device race on it. Returns (mean return per world, advantage mean,
+    advantage std before normalization)."""
+    lib = _lib.load()
+    st = np.zeros(3)
+    check(lib.phyzb_gae_noalloc(C.c_void_p(int(rewards_ptr)), C.c_void_p(int(values_ptr)), int(nworld), int(steps),
+                                float(gamma), float(lam), int(bool(normalize)), int(device),
+                                C.c_void_p(int(stream)) if stream else None, C.c_void_p(int(adv_ptr)),
+                                C.c_void_p(int(ret_ptr)), _lib.dptr(st)))
+    return tuple(st)
