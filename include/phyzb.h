@@ -187,6 +187,25 @@ int phyzb_enable_ground_contact(phyzb_sim* sim, double ground_height, double sti
 int phyzb_enable_ground_contact_per_body(phyzb_sim* sim, double ground_height,
                                          double friction, const double* stiffness,
                                          const double* damping, int32_t* collidable_out);
+/* BatchSim::enable_contact_impulse (cuda/mod.rs:680-701): contact as the
+ * velocity-level convex impulse solve -- per step, the backward sweep with
+ * the previous step's contact wrenches, then `sweeps` x [one staged Coulomb
+ * update per contact point at the free velocity v + dt qdd, backward sweep]
+ * (cuda/mod.rs:902-927; phyz_kernels.cu:856-918), warm-started from the
+ * previous step's impulses. Material: GroundContactParams::default with
+ * solref_erp_from(0.02, 1.0, dt) (contact_pipeline.rs:199-237). The
+ * per-body gains (nullable; penalty-only) are kept but do not enter the
+ * impulse law. Enabling resets the warm start to zero. */
+int phyzb_enable_contact_impulse(phyzb_sim* sim, double ground_height, double friction,
+                                 const double* stiffness, const double* damping,
+                                 int32_t* collidable_out);
+/* BatchSim::contact_sweeps (cuda/mod.rs:449-451, default 16): contact sweeps
+ * per step in impulse mode, 1 .. PHYZB_MAX_CONTACT_SWEEPS. (The reference
+ * also accepts 0, which runs one contact pass against the previous step's
+ * qdd; that form is not offered.) */
+#define PHYZB_DEFAULT_CONTACT_SWEEPS 16
+#define PHYZB_MAX_CONTACT_SWEEPS 1024
+int phyzb_set_contact_sweeps(phyzb_sim* sim, int32_t sweeps);
 /* Turn contact off again (ext forces zero). */
 int phyzb_disable_contact(phyzb_sim* sim);
 /* BatchSim::collidable_bodies (cuda/mod.rs:999-1001): 0 when disabled. */

@@ -56,8 +56,10 @@ class Oracle:
         L.oracle_penalty_contact.argtypes = [MP, C.c_int64, _D, _D, C.c_double, C.c_double, _D, _D, _D, _D]
         L.oracle_rollout.argtypes = [MP, C.c_int64, _D, _D, _D, C.c_int64, C.c_int32, C.c_int32, C.c_double,
                                      C.c_double, _D, _D, C.c_int32, _I, _D, _D, _D, _D, C.c_int32]
+        L.oracle_rollout_impulse.argtypes = [MP, C.c_int64, _D, _D, _D, C.c_int64, C.c_int32, _D, C.c_int32,
+                                             C.c_int32, _I, _D, _D, _D, _D, _D, C.c_int32]
         for f in ("oracle_aba", "oracle_rnea", "oracle_integrate_configuration", "oracle_forward_kinematics",
-                  "oracle_energy", "oracle_penalty_contact", "oracle_rollout"):
+                  "oracle_energy", "oracle_penalty_contact", "oracle_rollout", "oracle_rollout_impulse"):
             getattr(L, f).restype = C.c_int
 
     @staticmethod
@@ -149,6 +151,61 @@ class Oracle:
         return q, v, qdd, cs
 
 
+def solref_erp_from(timeconst, dampratio, dt):
+    """contact_pipeline.rs:229-237."""
+    if dt <= 0.0:
+        return 0.0
+    tau, zeta = max(timeconst, 0.0), max(dampratio, 1e-6)
+    denom = 2.0 * tau * zeta * zeta + dt
+    return 1.0 if denom <= 0.0 else dt / denom
+
+
+def impulse_material(dt):
+    """enable_contact_impulse's material (cuda/mod.rs:680-701) over
+    GroundContactParams::default (contact_pipeline.rs:199-218): erp, margin,
+    restitution, restitution_threshold, solimp dmin, dmax, width, mid, power."""
+    return [solref_erp_from(0.02, 1.0, dt), 0.001, 0.0, 0.05, 0.9, 0.95, 0.001, 0.5, 2.0]
+
+
+IMPULSE_PTS = 8
+
+
+def _rollout_impulse(self, model, q, v, ctrl=None, nsteps=1, schedule=False, contact=(0.0, 0.0), sweeps=16,
+                     pd=None, targets=None, state=None, nthreads=1):
+    """nsteps impulse-mode steps (step_world_impulse). contact: (ground,
+    friction). state: per world nb*6 wrenches + nb*8*3 impulses (None: zeros);
+    returns (q, v, qdd, contact_state [n][nb][8], state)."""
+    cm, keep = self._m(model)
+    q = np.array(q, np.float64, copy=True, order="C")
+    v = np.array(v, np.float64, copy=True, order="C")
+    n, nv, nb = q.shape[0], model.nv, model.nbodies
+    stride = 0
+    if ctrl is not None:
+        ctrl = np.ascontiguousarray(ctrl, np.float64)
+        stride = n * nv if schedule else 0
+    per = nb * 6 + nb * IMPULSE_PTS * 3
+    st = np.zeros((n, per)) if state is None else np.array(state, np.float64, copy=True, order="C")
+    ground, fr = contact
+    m = impulse_material(model.dt)
+    params = np.array([ground, fr, m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], m[8]], np.float64)
+    npd = 0
+    pidx = pg = tg = None
+    if pd:
+        npd = len(pd)
+        pidx = np.ascontiguousarray([[p.q_index, p.v_index] for p in pd], np.int32)
+        pg = np.ascontiguousarray([[p.kp, p.kd, p.max_force] for p in pd], np.float64)
+        tg = np.ascontiguousarray(targets, np.float64)
+    qdd = np.zeros((n, nv))
+    cs = np.zeros((n, nb, 8))
+    self.lib.oracle_rollout_impulse(C.addressof(cm), n, _d(q), _d(v), _d(ctrl), stride, nsteps, _d(params),
+                                    int(sweeps), npd, None if pidx is None else pidx.ctypes.data_as(_I), _d(pg),
+                                    _d(tg), _d(st), _d(qdd), _d(cs), nthreads)
+    return q, v, qdd, cs, st
+
+
+Oracle.rollout_impulse = _rollout_impulse
+
+
 class RefHost:
     """The reference's f32 kernels compiled as host C++ (phyz_host_*)."""
 
@@ -166,6 +223,9 @@ class RefHost:
         L.phyzref_rollout.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
                                       C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, C.c_uint32, _F, _F,
                                       _F, _F, _F, C.c_int64, C.c_int32, _F, _F]
+        L.phyzref_rollout_impulse.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
+                                              C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, _F, C.c_int32,
+                                              C.c_uint32, _F, _F, _F, _F, _F, C.c_int64, C.c_int32, _F, _F, _F]
         u = C.c_uint32
         L.phyz_host_fk.argtypes = [u, u, u, u, _F, _F, _F, _F]
         L.phyz_host_obs.argtypes = [u, u, u, u, u, u, u, _F, _F, _F, _F, _F, _F, _F]
@@ -256,6 +316,44 @@ class RefHost:
                                  nsteps, _f(qdd), _f(cs))
         return qf, vf, qdd, cs
 
+    def rollout_impulse(self, model, q, v, ctrl, nsteps=1, schedule=False, contact=(0.0, 0.0), sweeps=16,
+                        pd=None, targets=None, state=None, nthreads=1):
+        """Impulse mode (phyzref_rollout_impulse). state: (ext [n][nb][6],
+        cs [n][nb][56]) f32 carried between calls (None: zeros). Returns
+        (q, v, qdd, contact_state [n][nb][8], state)."""
+        cm, keep = model.to_c()
+        nb, nv = model.nbodies, model.nv
+        bodies = np.zeros(nb * self.BODY_STRIDE, np.float32)
+        self.lib.phyzref_pack_bodies(C.addressof(cm), _f(bodies))
+        zeros = np.zeros(nb)
+        geom = np.zeros(nb * self.GEOM_STRIDE, np.float32)
+        self.lib.phyzref_pack_geometries(C.addressof(cm), _d(zeros), _d(zeros), _f(geom))
+        n = q.shape[0]
+        qf = np.ascontiguousarray(q, np.float32).copy()
+        vf = np.ascontiguousarray(v, np.float32).copy()
+        cf = np.ascontiguousarray(ctrl, np.float32)
+        stride = n * nv if schedule else 0
+        if state is None:
+            ext, cs = np.zeros((n, nb, 6), np.float32), np.zeros((n, nb, 56), np.float32)
+        else:
+            ext, cs = (np.array(a, np.float32, copy=True, order="C") for a in state)
+        npd = 0
+        tbl = tg = None
+        if pd:
+            npd = len(pd)
+            tbl = np.zeros(npd * self.PD_STRIDE, np.float32)
+            for i, p in enumerate(pd):
+                tbl[i * self.PD_STRIDE: i * self.PD_STRIDE + 5] = [p.q_index, p.v_index, p.kp, p.kd, p.max_force]
+            tg = np.ascontiguousarray(targets, np.float32)
+        imp = np.asarray(impulse_material(model.dt), np.float32)
+        qdd = np.zeros((n, nv), np.float32)
+        gx, gy, gz = (float(x) for x in model.gravity)
+        ground, fr = contact
+        self.lib.phyzref_rollout_impulse(nthreads, n, nv, nb, float(model.dt), gx, gy, gz, _f(bodies), _f(geom),
+                                         float(ground), float(fr), _f(imp), int(sweeps), npd, _f(tbl), _f(tg),
+                                         _f(qf), _f(vf), _f(cf), stride, nsteps, _f(ext), _f(cs), _f(qdd))
+        return qf, vf, qdd, cs[:, :, :8].copy(), (ext, cs)
+
 
 REF_CUDA_SO = HERE / "_ref" / "libphyz_ref_cuda.so"
 
@@ -275,16 +373,32 @@ class RefCuda:
         u = C.c_uint32
         self.lib.phyzref_cuda_rollout.argtypes = [u, u, u, C.c_float, C.c_float, C.c_float, C.c_float, _F, _F, _F,
                                                   _F, _F, _F, C.c_int64, C.c_int32, C.c_int32, _F, _F, _F]
+        self.lib.phyzref_cuda_rollout_sweeps.argtypes = [u, u, u, C.c_float, C.c_float, C.c_float, C.c_float, _F,
+                                                         _F, _F, _F, _F, _F, C.c_int64, C.c_int32, C.c_int32,
+                                                         C.c_int32, _F, _F, _F]
         refhost.lib.phyzref_pack_cparams.argtypes = [u, u, u, C.c_float, C.c_float, C.c_float, _F]
 
-    def rollout(self, model, q, v, ctrl, nsteps, schedule=False, contact=None, reps=0):
-        """Returns (q, v, qdd, contact_state [n][nb][56], best ms of `reps` replays)."""
+    def rollout(self, model, q, v, ctrl, nsteps, schedule=False, contact=None, reps=0, sweeps=0):
+        """Returns (q, v, qdd, contact_state [n][nb][56], best ms of `reps` replays).
+        sweeps > 0: impulse mode with `contact` = (ground, friction) and
+        enable_contact_impulse's material."""
         cm, keep = model.to_c()
         nb, nv, n = model.nbodies, model.nv, q.shape[0]
         bodies = np.zeros(nb * RefHost.BODY_STRIDE, np.float32)
         self.host.lib.phyzref_pack_bodies(C.addressof(cm), _f(bodies))
         geom = cp = None
-        if contact is not None:
+        if contact is not None and sweeps > 0:
+            ground, fr = contact
+            zeros = np.zeros(nb)
+            geom = np.zeros(nb * RefHost.GEOM_STRIDE, np.float32)
+            self.host.lib.phyzref_pack_geometries(C.addressof(cm), _d(zeros), _d(zeros), _f(geom))
+            cp = np.zeros(32, np.float32)
+            self.host.lib.phyzref_pack_cparams(n, nb, nv, float(ground), float(model.dt), float(fr), _f(cp))
+            imp = impulse_material(model.dt)
+            cp[17] = np.array([1], np.uint32).view(np.float32)[0]  # solve_mode: impulse
+            cp[19], cp[20], cp[21], cp[22] = imp[2], imp[3], imp[0], imp[1]
+            cp[23:28] = imp[4:9]
+        elif contact is not None:
             ground, fr, k, d = contact
             k = np.ascontiguousarray(np.broadcast_to(k, (nb,)), np.float64)
             d = np.ascontiguousarray(np.broadcast_to(d, (nb,)), np.float64)
@@ -299,9 +413,9 @@ class RefCuda:
         cs = np.zeros((n, nb, 56), np.float32)
         ms = np.zeros(1, np.float32)
         gx, gy, gz = (float(x) for x in model.gravity)
-        rc = self.lib.phyzref_cuda_rollout(n, nv, nb, float(model.dt), gx, gy, gz, _f(bodies), _f(geom), _f(cp),
-                                           _f(qf), _f(vf), _f(cf), n * nv if schedule else 0, nsteps, reps,
-                                           _f(qdd), _f(cs), _f(ms))
+        rc = self.lib.phyzref_cuda_rollout_sweeps(n, nv, nb, float(model.dt), gx, gy, gz, _f(bodies), _f(geom),
+                                                  _f(cp), _f(qf), _f(vf), _f(cf), n * nv if schedule else 0, nsteps,
+                                                  int(sweeps), reps, _f(qdd), _f(cs), _f(ms))
         if rc != 0:
             raise RuntimeError(f"reference CUDA rollout failed: cudaError {-rc}")
         return qf, vf, qdd, cs, float(ms[0])

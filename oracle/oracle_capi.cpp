@@ -190,4 +190,69 @@ int oracle_rollout(const phyzb_model* fm, int64_t nworld, double* q, double* v,
     return 0;
 }
 
+// Impulse-mode rollout (step_world_impulse), nsteps times. `state` carries
+// the per-world impulse state across calls: per world, nb x 6 wrenches then
+// nb x 8 x 3 staged impulses (in/out; zeros to start).
+int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, double* v,
+                           const double* ctrl, int64_t ctrl_step_stride, int32_t nsteps,
+                           const double* params /* ground, friction, erp, margin, restitution,
+                                                    restitution_threshold, dmin, dmax, width, mid,
+                                                    power */,
+                           int32_t sweeps, int32_t npd, const int32_t* pd_idx, const double* pd_gains,
+                           const double* targets, double* state, double* qdd_out, double* cstate_out,
+                           int32_t nthreads) {
+    Model m = from_flat(fm);
+    int nb = m.nb(), nv = m.nv;
+    ImpulseParams cp;
+    cp.ground_height = params[0];
+    cp.friction = params[1];
+    cp.erp = params[2];
+    cp.margin = params[3];
+    cp.restitution = params[4];
+    cp.restitution_threshold = params[5];
+    cp.dmin = params[6];
+    cp.dmax = params[7];
+    cp.width = params[8];
+    cp.mid = params[9];
+    cp.power = params[10];
+    cp.sweeps = sweeps;
+    std::vector<PdEntry> pd;
+    for (int i = 0; i < npd; i++)
+        pd.push_back(PdEntry{pd_idx[2 * i], pd_idx[2 * i + 1], pd_gains[3 * i], pd_gains[3 * i + 1],
+                             pd_gains[3 * i + 2]});
+    const int64_t per = (int64_t)nb * 6 + (int64_t)nb * IMPULSE_PTS * 3;
+    parallel_worlds(nworld, nthreads, [&](int64_t a, int64_t b) {
+        std::vector<double> c(nv), qdd(nv);
+        ImpulseState st;
+        for (int64_t w = a; w < b; w++) {
+            double* qw = q + w * nv;
+            double* vw = v + w * nv;
+            double* sw = state + w * per;
+            st.reset(nb);
+            for (int i = 0; i < nb; i++) {
+                st.ext[i].ang = v3(sw[6 * i], sw[6 * i + 1], sw[6 * i + 2]);
+                st.ext[i].lin = v3(sw[6 * i + 3], sw[6 * i + 4], sw[6 * i + 5]);
+            }
+            for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) st.imp[k] = sw[nb * 6 + k];
+            for (int s = 0; s < nsteps; s++) {
+                const double* src = ctrl ? ctrl + s * ctrl_step_stride + w * nv : nullptr;
+                for (int j = 0; j < nv; j++) c[j] = src ? src[j] : 0.0;
+                double* cs = (cstate_out && s == nsteps - 1) ? cstate_out + w * nb * PHYZB_CONTACT_STRIDE
+                                                             : nullptr;
+                step_world_impulse(m, cp, npd > 0 ? &pd : nullptr, targets ? targets + w * npd : nullptr, qw, vw,
+                                   c.data(), qdd.data(), cs, st);
+            }
+            for (int i = 0; i < nb; i++) {
+                const SVec& e = st.ext[i];
+                const double vals[6] = {e.ang.x, e.ang.y, e.ang.z, e.lin.x, e.lin.y, e.lin.z};
+                for (int k = 0; k < 6; k++) sw[6 * i + k] = vals[k];
+            }
+            for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) sw[nb * 6 + k] = st.imp[k];
+            if (qdd_out)
+                for (int j = 0; j < nv; j++) qdd_out[w * nv + j] = qdd[j];
+        }
+    });
+    return 0;
+}
+
 }  // extern "C"

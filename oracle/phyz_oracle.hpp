@@ -24,7 +24,15 @@
 //     law its GPU kernels run, so the GPU law itself is restated in f64
 //     from phyz_kernels.cu:541-578 (coulomb, eff. mass, gain bounds),
 //     :641-643 (flat Z-up terrain), :691-725 (support points), :748-802
-//     (FK), :939-965 (penalty branch), :1050-1060 (contact state).
+//     (FK), :939-965 (penalty branch), :1050-1060 (contact state);
+//   * impulse-mode ground contact (enable_contact_impulse, cuda/mod.rs:
+//     680-701, 902-927): likewise the GPU's velocity-level staged Coulomb
+//     update restated in f64 from phyz_kernels.cu:581-622 (tangents, SolImp
+//     impedance, restitution ramp) and :856-918 (the impulse branch), with
+//     the sweep sequence of cuda/mod.rs:916-927. The reference's CPU convex
+//     solver it is compared with (phyz-contact) needs the unvendored tang
+//     crate, so this restatement is pinned against the reference's own
+//     contact kernel compiled for the host (oracle/_ref) instead.
 //
 // Nothing in the product links this file; tests, smoke() and the bench's
 // CPU-baseline leg use it through oracle/oracle_capi.cpp.
@@ -976,6 +984,195 @@ inline void penalty_contact(const Model& m, const ContactParams& cp, const doubl
     }
 }
 
+// ── impulse-mode ground contact: the velocity-level staged Coulomb update
+// of phyz_kernels.cu:804-937 (solve_mode 1, flat ground), in f64 ─────────
+
+// Contact material of the impulse solve: enable_contact_impulse's settings
+// (cuda/mod.rs:680-701) over GroundContactParams::default
+// (contact_pipeline.rs:199-218).
+struct ImpulseParams {
+    double ground_height = 0, friction = 0;
+    double restitution = 0, restitution_threshold = 0.05;
+    double erp = 0;  // solref_erp_from(0.02, 1.0, dt)
+    double margin = 0.001;
+    double dmin = 0.9, dmax = 0.95, width = 0.001, mid = 0.5, power = 2.0;
+    int sweeps = 16;  // DEFAULT_CONTACT_SWEEPS (gpu_batch_simulator.rs:31)
+};
+
+// contact_pipeline.rs:229-237
+inline double solref_erp_from(double timeconst, double dampratio, double dt) {
+    if (dt <= 0.0) return 0.0;
+    double tau = std::fmax(timeconst, 0.0), zeta = std::fmax(dampratio, 1e-6);
+    double denom = 2.0 * tau * zeta * zeta + dt;
+    return denom <= 0.0 ? 1.0 : dt / denom;
+}
+inline double clampd(double x, double lo, double hi) { return std::fmin(std::fmax(x, lo), hi); }
+// phyz_kernels.cu:589-601 (SolImp impedance)
+inline double solimp_impedance(const ImpulseParams& c, double r) {
+    double dmin = clampd(c.dmin, 1e-4, 1.0 - 1e-9), dmax = clampd(c.dmax, 1e-4, 1.0 - 1e-9);
+    if (c.width <= 0.0) return dmax;
+    double x = clampd(std::fabs(r) / c.width, 0.0, 1.0);
+    double mid = clampd(c.mid, 1e-6, 1.0 - 1e-6);
+    double pw = std::fmax(c.power, 1.0);
+    double y = x <= mid ? std::pow(x, pw) / std::pow(mid, pw - 1.0)
+                        : 1.0 - std::pow(1.0 - x, pw) / std::pow(1.0 - mid, pw - 1.0);
+    return dmin + y * (dmax - dmin);
+}
+// phyz_kernels.cu:604-611
+inline double impedance_at(const ImpulseParams& c, double depth) {
+    if (depth >= 0.0) return solimp_impedance(c, depth);
+    double gap = -depth;
+    if (c.margin <= 0.0 || gap >= c.margin) return 0.0;
+    double sc = 1.0 - gap / c.margin;
+    return sc * sc * (3.0 - 2.0 * sc) * solimp_impedance(c, 0.0);
+}
+// phyz_kernels.cu:613-622
+inline double effective_restitution(const ImpulseParams& c, double e, double approach) {
+    double vr = c.restitution_threshold;
+    if (vr <= 0.0) return e;
+    double sp = std::fabs(approach);
+    if (sp <= vr) return 0.0;
+    if (sp >= 2.0 * vr) return e;
+    double t = (sp - vr) / vr;
+    return e * t * t * (3.0 - 2.0 * t);
+}
+// phyz_kernels.cu:581-586 (tangents around a unit normal)
+inline void contact_tangents(Vec3 n, Vec3& u, Vec3& w) {
+    Vec3 a = std::fabs(n.x) > 0.9 ? v3(0, 1, 0) : v3(1, 0, 0);
+    Vec3 c = cross(n, a);
+    double l = norm(c);
+    u = l > 0.0 ? c * (1.0 / l) : c;
+    w = cross(n, u);
+}
+
+// Per-world state the impulse solve carries across sweeps and steps: the
+// contact wrench of every body (body frame, the ext_forces buffer) and the
+// staged impulse [normal, tangent u, tangent w] of each (body, point) slot
+// (contact_state at CS_IMPULSE_OFF).
+constexpr int IMPULSE_PTS = 8;
+struct ImpulseState {
+    std::vector<SVec> ext;
+    std::vector<double> imp;  // [nb][IMPULSE_PTS][3]
+    void reset(int nb) {
+        ext.assign(nb, SVec{});
+        imp.assign((size_t)nb * IMPULSE_PTS * 3, 0.0);
+    }
+};
+
+// One contact sweep of one world: FK with the free velocity v + dt qdd, one
+// staged Coulomb update per contact point, the new wrenches into st.ext and
+// the contact state [touching, depth, point(3), force(3)] into cstate.
+inline void impulse_contact(const Model& m, const ImpulseParams& cp, const double* q, const double* v,
+                            const double* qdd, ImpulseState& st, double* cstate) {
+    int nb = m.nb();
+    const double dt = m.dt, idt = 1.0 / std::fmax(dt, 1e-9);
+    std::vector<double> vf(m.nv);
+    for (int k = 0; k < m.nv; k++) vf[k] = v[k] + dt * qdd[k];
+    std::vector<Mat3> wrot(nb);
+    std::vector<Vec3> wpos(nb);
+    std::vector<SVec> vel(nb);
+    for (int i = 0; i < nb; i++) {
+        const Joint& jt = m.joints[i];
+        SXform xj = jt.ndof() == 0 ? SXform{} : jt.joint_transform(q + m.q_off[i]);
+        SXform xt = xj.compose(jt.parent_to_joint);
+        SVec vj = jt.joint_velocity(vf.data() + m.v_off[i]);
+        Mat3 tree_rt = transpose(xt.rot);
+        int p = m.bodies[i].parent;
+        if (p < 0) {
+            wrot[i] = tree_rt;
+            wpos[i] = xt.pos;
+            vel[i] = vj;
+        } else {
+            wrot[i] = mul(wrot[p], tree_rt);
+            wpos[i] = wpos[p] + mul(wrot[p], xt.pos);
+            vel[i] = xt.apply_motion(vel[p]) + vj;
+        }
+    }
+    st.ext.assign(nb, SVec{});
+    for (int i = 0; i < nb; i++) {
+        const Body& b = m.bodies[i];
+        double* cs = cstate ? cstate + i * PHYZB_CONTACT_STRIDE : nullptr;
+        if (cs)
+            for (int k = 0; k < PHYZB_CONTACT_STRIDE; k++) cs[k] = 0.0;
+        double* slots = st.imp.data() + (size_t)i * IMPULSE_PTS * 3;
+        if (b.geom.type == 0) {
+            for (int k = 0; k < IMPULSE_PTS * 3; k++) slots[k] = 0.0;
+            continue;
+        }
+        Vec3 z_body = tmul(wrot[i], v3(0, 0, 1));
+        int npts = b.geom.type == 2 ? 8 : 1;
+        auto point = [&](int c) { return b.geom.type == 2 ? box_corner(b.geom, c) : support_point(b.geom, z_body); };
+        // within-body load sharing: points inside the margin
+        int n_active = 0;
+        for (int c = 0; c < npts; c++) {
+            Vec3 sw = wpos[i] + mul(wrot[i], point(c));
+            if (cp.ground_height - sw.z > -cp.margin) n_active++;
+        }
+        if (n_active < 1) n_active = 1;
+        Vec3 f_w_total{};
+        double deepest = 0;
+        Vec3 deepest_w{};
+        bool any = false;
+        for (int c = 0; c < npts; c++) {
+            double* f_c = slots + 3 * c;
+            Vec3 sup = point(c);
+            Vec3 sup_w = wpos[i] + mul(wrot[i], sup);
+            double pen = cp.ground_height - sup_w.z;
+            if (!(pen > -cp.margin)) {
+                f_c[0] = f_c[1] = f_c[2] = 0.0;
+                continue;
+            }
+            Vec3 n_body = z_body;
+            Vec3 v_point = vel[i].lin + cross(vel[i].ang, sup);
+            Vec3 t_u, t_w;
+            contact_tangents(n_body, t_u, t_w);
+            double b_n = dot(v_point, n_body), b_u = dot(v_point, t_u), b_w = dot(v_point, t_w);
+            double m_n = contact_eff_mass(b, sup, n_body) / n_active;
+            double a_nn = 1.0 / std::fmax(m_n, 1e-9);
+            double bias = impedance_at(cp, pen) * cp.erp * std::fmax(pen, 0.0) / std::fmax(dt, 1e-9);
+            double e = effective_restitution(cp, cp.restitution, std::fmin(b_n, 0.0));
+            double r_n = b_n * (1.0 + e) - a_nn * f_c[0];
+            double fn = std::fmax((bias - r_n) / a_nn, 0.0);
+            double a_uu = n_active / std::fmax(contact_eff_mass(b, sup, t_u), 1e-9);
+            double a_ww = n_active / std::fmax(contact_eff_mass(b, sup, t_w), 1e-9);
+            double tu = -(b_u - a_uu * f_c[1]) / a_uu;
+            double tw = -(b_w - a_ww * f_c[2]) / a_ww;
+            double limit = cp.friction * fn;
+            double tn = std::sqrt(tu * tu + tw * tw);
+            if (tn > limit) {
+                double sc = tn > 0.0 ? limit / tn : 0.0;
+                tu *= sc;
+                tw *= sc;
+            }
+            f_c[0] = fn;
+            f_c[1] = tu;
+            f_c[2] = tw;
+            Vec3 f_body = (n_body * fn + t_u * tu + t_w * tw) * idt;
+            st.ext[i].ang = st.ext[i].ang + cross(sup, f_body);
+            st.ext[i].lin = st.ext[i].lin + f_body;
+            f_w_total = f_w_total + mul(wrot[i], f_body);
+            any = true;
+            if (pen > deepest) {
+                deepest = pen;
+                deepest_w = sup_w;
+            }
+        }
+        if (!any) {
+            for (int k = 0; k < IMPULSE_PTS * 3; k++) slots[k] = 0.0;
+            continue;
+        }
+        if (!cs) continue;
+        cs[0] = 1.0;
+        cs[1] = deepest;
+        cs[2] = deepest_w.x;
+        cs[3] = deepest_w.y;
+        cs[4] = deepest_w.z;
+        cs[5] = f_w_total.x;
+        cs[6] = f_w_total.y;
+        cs[7] = f_w_total.z;
+    }
+}
+
 // One step of the batched path for one world: [PD ->] [contact ->] ABA ->
 // semi-implicit Euler (cuda/mod.rs:879-945 order), qdd written out.
 struct PdEntry {
@@ -1000,4 +1197,27 @@ inline void step_world(const Model& m, const ContactParams* cp, const std::vecto
         for (int i = 0; i < m.nv; i++) qdd_out[i] = qdd[i];
 }
 
+
+// One impulse-mode step of one world (cuda/mod.rs:879-945): [PD ->] ABA
+// with the wrenches of the previous step's last sweep, `sweeps` x [contact
+// at the free velocity v + dt qdd -> ABA], then semi-implicit Euler.
+inline void step_world_impulse(const Model& m, const ImpulseParams& cp, const std::vector<PdEntry>* pd,
+                               const double* targets, double* q, double* v, double* ctrl, double* qdd_out,
+                               double* cstate, ImpulseState& st) {
+    if (pd) {
+        for (size_t d = 0; d < pd->size(); d++) {
+            const PdEntry& e = (*pd)[d];
+            double tau = e.kp * (targets[d] - q[e.qi]) - e.kd * v[e.vi];
+            ctrl[e.vi] = std::fmin(std::fmax(tau, -e.maxf), e.maxf);
+        }
+    }
+    std::vector<double> qdd = aba(m, q, v, ctrl, st.ext.data());
+    for (int s = 0; s < cp.sweeps; s++) {
+        impulse_contact(m, cp, q, v, qdd.data(), st, cstate);
+        qdd = aba(m, q, v, ctrl, st.ext.data());
+    }
+    semi_implicit_euler(m, q, v, qdd.data(), m.dt);
+    if (qdd_out)
+        for (int i = 0; i < m.nv; i++) qdd_out[i] = qdd[i];
+}
 }  // namespace phyz_oracle

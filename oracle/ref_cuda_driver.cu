@@ -4,8 +4,9 @@
 // reference tree with nvcc for sm_100a (IEEE division and square root, no
 // fast math: the reference's NVRTC options, cuda/nvrtc.rs:83-90) and links
 // it with this driver into oracle/_ref/libphyz_ref_cuda.so. The driver
-// replays the reference's penalty-mode step sequence (cuda/mod.rs:879-945:
-// contact -> aba -> integrate, 64-thread blocks, nvrtc.rs:120-126) as one
+// replays the reference's step sequence (cuda/mod.rs:879-945: penalty
+// contact -> aba -> integrate, or impulse mode's aba, sweeps x [contact ->
+// aba], integrate; 64-thread blocks, nvrtc.rs:120-126) as one
 // captured CUDA graph per rollout, the way BatchSim::step_many replays its
 // graph cache (mod.rs:843-875). Used by the GPU tests for parity of the B200
 // stepper with the reference's GPU path and for its throughput on the same
@@ -44,13 +45,25 @@ struct Bufs {
     }
 };
 
+// sweeps == 0: the penalty sequence contact -> aba -> integrate; sweeps > 0
+// (impulse mode, cparams solve_mode 1): aba, sweeps x [contact -> aba],
+// integrate (cuda/mod.rs:916-927).
 int enqueue(cudaStream_t s, const Bufs& b, u32 n, u32 nv, u32 nb, float dt, float gx, float gy, float gz,
-            int64_t stride, int nsteps) {
+            int64_t stride, int nsteps, int sweeps) {
     const unsigned gw = (n + BLOCK - 1) / BLOCK, gi = (n * nb + BLOCK - 1) / BLOCK;
     for (int k = 0; k < nsteps; k++) {
         const float* c = b.ctrl + (size_t)k * stride;
-        if (b.geom) phyz_contact<<<gw, BLOCK, 0, s>>>(b.cp, b.bodies, b.geom, b.q, b.v, b.ext, b.cs, b.hf, b.qdd);
-        phyz_aba<<<gw, BLOCK, 0, s>>>(n, nv, dt, nb, gx, gy, gz, b.bodies, b.q, b.v, c, b.qdd, b.ext);
+        if (sweeps > 0) {
+            phyz_aba<<<gw, BLOCK, 0, s>>>(n, nv, dt, nb, gx, gy, gz, b.bodies, b.q, b.v, c, b.qdd, b.ext);
+            for (int w = 0; w < sweeps; w++) {
+                phyz_contact<<<gw, BLOCK, 0, s>>>(b.cp, b.bodies, b.geom, b.q, b.v, b.ext, b.cs, b.hf, b.qdd);
+                phyz_aba<<<gw, BLOCK, 0, s>>>(n, nv, dt, nb, gx, gy, gz, b.bodies, b.q, b.v, c, b.qdd, b.ext);
+            }
+        } else {
+            if (b.geom)
+                phyz_contact<<<gw, BLOCK, 0, s>>>(b.cp, b.bodies, b.geom, b.q, b.v, b.ext, b.cs, b.hf, b.qdd);
+            phyz_aba<<<gw, BLOCK, 0, s>>>(n, nv, dt, nb, gx, gy, gz, b.bodies, b.q, b.v, c, b.qdd, b.ext);
+        }
         phyz_integrate<<<gi, BLOCK, 0, s>>>(n, nv, dt, nb, b.q, b.v, b.qdd, b.bodies);
     }
     return (int)cudaGetLastError();
@@ -66,10 +79,13 @@ extern "C" {
 // = nworld * nv, or one held row set when 0. With reps > 0 the same rollout
 // is then replayed reps times from the same initial state and *ms_min gets
 // the fastest replay (CUDA events around one graph launch).
-int phyzref_cuda_rollout(u32 nworld, u32 nv, u32 nb, float dt, float gx, float gy, float gz, const float* bodies,
-                         const float* geometry, const float* cparams, float* q, float* v, const float* ctrl,
-                         int64_t ctrl_step_stride, int32_t nsteps, int32_t reps, float* qdd_out, float* cs_out,
-                         float* ms_min) {
+// `sweeps` > 0 runs the impulse-mode sequence (cparams must say solve_mode
+// 1); the wrench and impulse buffers start from zero on every call.
+int phyzref_cuda_rollout_sweeps(u32 nworld, u32 nv, u32 nb, float dt, float gx, float gy, float gz,
+                                const float* bodies, const float* geometry, const float* cparams, float* q, float* v,
+                                const float* ctrl, int64_t ctrl_step_stride, int32_t nsteps, int32_t sweeps,
+                                int32_t reps, float* qdd_out, float* cs_out, float* ms_min) {
+    if (sweeps > 0 && !geometry) return -1;
     Bufs b;
     const size_t n = nworld, S = (size_t)n * nv * 4;
     const size_t ctrl_bytes = ctrl_step_stride ? (size_t)nsteps * ctrl_step_stride * 4 : S;
@@ -106,7 +122,7 @@ int phyzref_cuda_rollout(u32 nworld, u32 nv, u32 nb, float dt, float gx, float g
     do {
         if ((rc = load())) break;
         if ((rc = -(int)cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal))) break;
-        const int er = enqueue(s, b, nworld, nv, nb, dt, gx, gy, gz, ctrl_step_stride, nsteps);
+        const int er = enqueue(s, b, nworld, nv, nb, dt, gx, gy, gz, ctrl_step_stride, nsteps, sweeps);
         const cudaError_t ec = cudaStreamEndCapture(s, &graph);
         if (er || ec != cudaSuccess) {
             rc = er ? -er : -(int)ec;
@@ -148,6 +164,14 @@ int phyzref_cuda_rollout(u32 nworld, u32 nv, u32 nb, float dt, float gx, float g
     cudaStreamSynchronize(s);
     cudaStreamDestroy(s);
     return rc;
+}
+
+int phyzref_cuda_rollout(u32 nworld, u32 nv, u32 nb, float dt, float gx, float gy, float gz, const float* bodies,
+                         const float* geometry, const float* cparams, float* q, float* v, const float* ctrl,
+                         int64_t ctrl_step_stride, int32_t nsteps, int32_t reps, float* qdd_out, float* cs_out,
+                         float* ms_min) {
+    return phyzref_cuda_rollout_sweeps(nworld, nv, nb, dt, gx, gy, gz, bodies, geometry, cparams, q, v, ctrl,
+                                       ctrl_step_stride, nsteps, 0, reps, qdd_out, cs_out, ms_min);
 }
 
 }  // extern "C"

@@ -170,4 +170,63 @@ int phyzref_rollout(int nthreads, uint32_t nworld, uint32_t nv, uint32_t nb, flo
     return 0;
 }
 
+// Impulse mode (cuda/mod.rs:902-927): cparams with solve_mode 1 and the
+// impulse material (contact_pipeline.rs:85-95), then per step [PD ->] ABA,
+// `sweeps` x [contact -> ABA], integrate. ext (nworld x nb x 6) and cs
+// (nworld x nb x CS_STRIDE, the warm-start impulses at CS_IMPULSE_OFF) carry
+// over between calls, as the reference's device buffers do between steps.
+//   imp: erp, margin, restitution, restitution_threshold, dmin, dmax, width, mid, power
+int phyzref_rollout_impulse(int nthreads, uint32_t nworld, uint32_t nv, uint32_t nb, float dt, float gx,
+                            float gy, float gz, const float* bodies, const float* geometry, float ground,
+                            float friction, const float* imp, int32_t sweeps, uint32_t npd,
+                            const float* pd_table, const float* targets, float* q, float* v, const float* ctrl,
+                            int64_t ctrl_step_stride, int32_t nsteps, float* ext_io, float* cs_io,
+                            float* qdd_out) {
+    if (nthreads < 1) nthreads = 1;
+    if ((uint32_t)nthreads > nworld) nthreads = (int)(nworld ? nworld : 1);
+    uint32_t chunk = (nworld + nthreads - 1) / nthreads;
+    auto work = [&](uint32_t a, uint32_t b) {
+        uint32_t n = b - a;
+        float* ext = ext_io + (size_t)a * nb * 6;
+        float* cs = cs_io + (size_t)a * nb * CS_STRIDE;
+        std::vector<float> qdd((size_t)n * nv, 0.0f), c((size_t)n * nv, 0.0f);
+        float cp[CP_STRIDE];
+        phyzref_pack_cparams(n, nb, nv, ground, dt, friction, cp);
+        cp[17] = bits_u(1u);  // solve_mode: impulse
+        cp[19] = imp[2];      // restitution
+        cp[20] = imp[3];      // restitution_threshold
+        cp[21] = imp[0];      // solref_erp
+        cp[22] = imp[1];      // margin
+        for (int k = 0; k < 5; k++) cp[23 + k] = imp[4 + k];  // solimp dmin, dmax, width, mid, power
+        float hf = 0.0f;
+        float* qa = q + (size_t)a * nv;
+        float* va = v + (size_t)a * nv;
+        for (int s = 0; s < nsteps; s++) {
+            const float* src = ctrl + (size_t)s * ctrl_step_stride + (size_t)a * nv;
+            std::memcpy(c.data(), src, sizeof(float) * n * nv);
+            if (npd)
+                phyz_host_pd(n * npd, n, nv, nv, npd, pd_table, qa, va, targets + (size_t)a * npd,
+                             c.data());
+            phyz_host_aba(n, n, nv, dt, nb, gx, gy, gz, bodies, qa, va, c.data(), qdd.data(), ext);
+            for (int k = 0; k < sweeps; k++) {
+                phyz_host_contact(n, cp, bodies, geometry, qa, va, ext, cs, &hf, qdd.data());
+                phyz_host_aba(n, n, nv, dt, nb, gx, gy, gz, bodies, qa, va, c.data(), qdd.data(), ext);
+            }
+            phyz_host_integrate(n * nb, n, nv, dt, nb, qa, va, qdd.data(), bodies);
+        }
+        if (qdd_out) std::memcpy(qdd_out + (size_t)a * nv, qdd.data(), sizeof(float) * n * nv);
+    };
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nthreads; t++) {
+        uint32_t a = t * chunk, b = a + chunk < nworld ? a + chunk : nworld;
+        if (a >= b) break;
+        if (nthreads == 1)
+            work(a, b);
+        else
+            pool.emplace_back(work, a, b);
+    }
+    for (auto& th : pool) th.join();
+    return 0;
+}
+
 }  // extern "C"

@@ -22,6 +22,8 @@ ERR_UNSUPPORTED = -7
 ERR_COMM = -8
 COMM_ID_BYTES = 128
 GAE_NOALLOC_MAX_WORLDS = 1 << 24
+DEFAULT_CONTACT_SWEEPS = 16
+MAX_CONTACT_SWEEPS = 1024
 
 F32 = 0
 F64 = 1
@@ -164,6 +166,8 @@ SIGNATURES = {
     "phyzb_set_model": (C.c_int, [_P, C.POINTER(PhyzbModel)]),
     "phyzb_enable_ground_contact": (C.c_int, [_P, C.c_double, C.c_double, C.c_double, C.c_double, _I32P]),
     "phyzb_enable_ground_contact_per_body": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _I32P]),
+    "phyzb_enable_contact_impulse": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _I32P]),
+    "phyzb_set_contact_sweeps": (C.c_int, [_P, C.c_int32]),
     "phyzb_disable_contact": (C.c_int, [_P]),
     "phyzb_collidable_bodies": (C.c_int, [_P]),
     "phyzb_enable_pd": (C.c_int, [_P, C.POINTER(PhyzbPdDof), C.c_int32]),

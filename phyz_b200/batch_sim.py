@@ -134,6 +134,34 @@ class BatchSim:
                                                              C.byref(n)))
         return n.value
 
+    def enable_contact_impulse(self, ground_height: float, friction: float, gains=None) -> int:
+        """Contact as the velocity-level impulse solve (cuda/mod.rs:680-701):
+        `contact_sweeps` staged Coulomb updates per step, warm-started from
+        the previous step. `gains` (BodyContactGains per body) only matter to
+        a later penalty enable."""
+        k = d = None
+        if gains is not None:
+            k = np.ascontiguousarray([g.stiffness for g in gains], np.float64)
+            d = np.ascontiguousarray([g.damping for g in gains], np.float64)
+            if k.size != self.nb:
+                raise PhyzbError(_lib.ERR_INVALID, f"need {self.nb} body gains, got {k.size}")
+        n = C.c_int32()
+        check(self._lib.phyzb_enable_contact_impulse(self._h, ground_height, friction,
+                                                     dptr(k) if k is not None else None,
+                                                     dptr(d) if d is not None else None, C.byref(n)))
+        return n.value
+
+    @property
+    def contact_sweeps(self) -> int:
+        """Contact sweeps per step in impulse mode (the reference's public
+        `contact_sweeps` field, default 16)."""
+        return getattr(self, "_sweeps", _lib.DEFAULT_CONTACT_SWEEPS)
+
+    @contact_sweeps.setter
+    def contact_sweeps(self, n: int) -> None:
+        check(self._lib.phyzb_set_contact_sweeps(self._h, int(n)))
+        self._sweeps = int(n)
+
     def disable_contact(self) -> None:
         check(self._lib.phyzb_disable_contact(self._h))
 

@@ -136,6 +136,20 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     a.nworld = s->nworld;
     a.nsteps = nsteps;
     a.scratch = L.info.scratch;
+    // impulse material: enable_contact_impulse over GroundContactParams::default
+    // (cuda/mod.rs:680-701, contact_pipeline.rs:199-218)
+    a.imp = (T*)s->imp;
+    a.imp_slots = L.info.imp_slots;
+    a.sweeps = s->sweeps;
+    a.erp = s->erp;
+    a.margin = 0.001;
+    a.restitution = 0.0;
+    a.rest_thr = 0.05;
+    a.si_dmin = 0.9;
+    a.si_dmax = 0.95;
+    a.si_width = 0.001;
+    a.si_mid = 0.5;
+    a.si_power = 2.0;
     return a;
 }
 
@@ -198,7 +212,28 @@ int read_status(phyzb_sim* s) {
     return PHYZB_OK;
 }
 
-int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d) {
+// contact_pipeline.rs:229-237 (SolRef error reduction at dt)
+double solref_erp_from(double timeconst, double dampratio, double dt) {
+    if (dt <= 0.0) return 0.0;
+    const double tau = std::max(timeconst, 0.0), zeta = std::max(dampratio, 1e-6);
+    const double denom = 2.0 * tau * zeta * zeta + dt;
+    return denom <= 0.0 ? 1.0 : dt / denom;
+}
+
+// The impulse buffer sized for the current layout, zeroed (a fresh warm start).
+int reset_impulse_state(phyzb_sim* s) {
+    const size_t bytes = (size_t)s->lay[0].info.imp_slots * s->nworld * s->esz();
+    if (bytes > s->imp_bytes) {
+        free_ptr(s->imp);
+        s->imp_bytes = 0;
+        PZ_CUDA(cudaMalloc(&s->imp, bytes));
+        s->imp_bytes = bytes;
+    }
+    if (bytes) PZ_CUDA(cudaMemsetAsync(s->imp, 0, bytes, s->stream));
+    return PHYZB_OK;
+}
+
+int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d, bool impulse) {
     int collidable = 0;
     for (int i = 0; i < s->nb; i++)
         if (s->bodies[i].geom_type != PHYZB_GEOM_NONE) collidable++;
@@ -221,11 +256,14 @@ int set_contact(phyzb_sim* s, double ground, double friction, const double* k, c
         PZ_CUDA(cudaMemsetAsync(s->cstate, 0, bytes, s->stream));
     }
     s->cfg.contact = true;
+    s->cfg.impulse = impulse;
     s->cfg.gk.assign(k, k + s->nb);
     s->cfg.gd.assign(d, d + s->nb);
     s->ground_h = ground;
     s->friction = friction;
+    s->erp = solref_erp_from(0.02, 1.0, s->model.dt);
     PZ_TRY(repack(s));
+    if (impulse) PZ_TRY(reset_impulse_state(s));
     return PHYZB_OK;
 }
 
@@ -264,6 +302,7 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(s->qdd);
     free_ptr(s->targets);
     free_ptr(s->cstate);
+    free_ptr(s->imp);
     void* st = s->status;
     free_ptr(st);
     free_ptr(s->lay[0].blob);
@@ -381,7 +420,12 @@ int phyzb_set_model(phyzb_sim* s, const phyzb_model* model) {
             return fail(PHYZB_ERR_INVALID, "set_model: topology or joint types changed; build a new simulator");
     DeviceGuard g(s->device);
     set_model_copy(s, model);
-    return repack(s);
+    PZ_TRY(repack(s));
+    // a geometry change can add impulse slots: those start from zero
+    if (s->cfg.contact && s->cfg.impulse &&
+        (size_t)s->lay[0].info.imp_slots * s->nworld * s->esz() > s->imp_bytes)
+        PZ_TRY(reset_impulse_state(s));
+    return PHYZB_OK;
 }
 
 int phyzb_enable_ground_contact(phyzb_sim* s, double ground_height, double stiffness, double damping, double friction,
@@ -389,7 +433,7 @@ int phyzb_enable_ground_contact(phyzb_sim* s, double ground_height, double stiff
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
     std::vector<double> k(s->nb, stiffness), d(s->nb, damping);
-    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data()));
+    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data(), false));
     if (collidable_out) *collidable_out = s->collidable;
     return PHYZB_OK;
 }
@@ -399,8 +443,31 @@ int phyzb_enable_ground_contact_per_body(phyzb_sim* s, double ground_height, dou
     PZ_TRY(check_sim(s));
     if (!stiffness || !damping) return fail(PHYZB_ERR_INVALID, "per-body gains are null");
     DeviceGuard g(s->device);
-    PZ_TRY(set_contact(s, ground_height, friction, stiffness, damping));
+    PZ_TRY(set_contact(s, ground_height, friction, stiffness, damping, false));
     if (collidable_out) *collidable_out = s->collidable;
+    return PHYZB_OK;
+}
+
+int phyzb_enable_contact_impulse(phyzb_sim* s, double ground_height, double friction, const double* stiffness,
+                                 const double* damping, int32_t* collidable_out) {
+    PZ_TRY(check_sim(s));
+    DeviceGuard g(s->device);
+    // the per-body gains only enter the penalty law; they are kept (and
+    // checked) so a later penalty enable sees the same table
+    std::vector<double> k(s->nb, 0.0), d(s->nb, 0.0);
+    if (stiffness) k.assign(stiffness, stiffness + s->nb);
+    if (damping) d.assign(damping, damping + s->nb);
+    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data(), true));
+    if (collidable_out) *collidable_out = s->collidable;
+    return PHYZB_OK;
+}
+
+int phyzb_set_contact_sweeps(phyzb_sim* s, int32_t sweeps) {
+    PZ_TRY(check_sim(s));
+    if (sweeps < 1 || sweeps > PHYZB_MAX_CONTACT_SWEEPS)
+        return fail(PHYZB_ERR_INVALID, "contact sweeps must be in [1, " + std::to_string(PHYZB_MAX_CONTACT_SWEEPS) +
+                                           "], got " + std::to_string(sweeps));
+    s->sweeps = sweeps;
     return PHYZB_OK;
 }
 
@@ -408,6 +475,7 @@ int phyzb_disable_contact(phyzb_sim* s) {
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
     s->cfg.contact = false;
+    s->cfg.impulse = false;
     return repack(s);
 }
 
@@ -673,7 +741,7 @@ int phyzb_objective_device(phyzb_sim* s, int kind, void* out) {
 
 int phyzb_flops_per_world_step(const phyzb_sim* s, double* flops, double* transcendentals) {
     PZ_TRY(check_sim(s));
-    const pz::FlopCount fc = pz::count_world_step(&s->model, s->nv, s->cfg);
+    const pz::FlopCount fc = pz::count_world_step(&s->model, s->nv, s->cfg, s->sweeps);
     if (flops) *flops = fc.flops;
     if (transcendentals) *transcendentals = fc.transcendentals;
     return PHYZB_OK;

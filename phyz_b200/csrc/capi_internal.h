@@ -95,6 +95,10 @@ struct phyzb_sim {
     cudaStream_t own_stream = nullptr, stream = nullptr, copy_stream = nullptr;
     void *q = nullptr, *v = nullptr, *ctrl = nullptr, *qdd = nullptr;
     void *targets = nullptr, *cstate = nullptr;
+    void* imp = nullptr;      // impulse mode: [imp_slots][nworld] wrenches + staged impulses
+    size_t imp_bytes = 0;
+    int sweeps = 16;          // impulse mode: contact sweeps per step (DEFAULT_CONTACT_SWEEPS)
+    double erp = 0.0;         // impulse mode: solref error reduction at this dt
     int* status = nullptr;
     // lay[0]: every record in shared memory (the objective kernel's layout
     // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the

@@ -63,6 +63,10 @@ inline Cnt pz_tanh(Cnt x) {
     g_tally.trans += 1;
     return Cnt(std::tanh(x.v));
 }
+inline Cnt pz_pow(Cnt x, Cnt y) {
+    g_tally.trans += 1;
+    return Cnt(std::pow(x.v, y.v));
+}
 inline Cnt pz_abs(Cnt x) { return Cnt(std::fabs(x.v)); }
 inline Cnt pz_min(Cnt a, Cnt b) { return Cnt(std::fmin(a.v, b.v)); }
 inline Cnt pz_max(Cnt a, Cnt b) { return Cnt(std::fmax(a.v, b.v)); }
@@ -114,7 +118,7 @@ struct HostScr {
 };
 }  // namespace
 
-FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
+FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps) {
     std::vector<unsigned char> blob;
     const PackInfo info = pack_model<double>(m, nv, cfg, blob);
     const int nb = m->nbodies, npd = (int)cfg.pd.size();
@@ -152,6 +156,8 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
     const double dtc = m->dt > 1e-9 ? m->dt : 1e-9;
     M.inv_dt_c = Cnt(1.0 / dtc);
     M.kstiff_c = Cnt(4.0 / (dtc * dtc));
+    M.im = ImpMat<Cnt>{M.ground_h, M.friction, M.dt, Cnt(0.0), Cnt(0.001), Cnt(0.0), Cnt(0.05),
+                       Cnt(0.9),   Cnt(0.95),  Cnt(0.001), Cnt(0.5), Cnt(2.0)};
 
     std::vector<Cnt> scratch(info.scratch > 0 ? info.scratch : 1, Cnt(0.0));
     HostScr S{scratch.data()};
@@ -165,11 +171,25 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg) {
     const Out<Cnt> none{nullptr, 0};
     for (int i = 0; i < nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
     constexpr int ALL = FEAT_MULTI | FEAT_CONTACT;  // runtime flags select the paths taken
-    pass1_all<ALL>(M, S);
-    // steady state: one backward sweep + one fused finish/start sweep
-    g_tally = Tally{};
-    pass2<ALL>(M, S);
-    pass3_next<ALL, false>(M, S, io, 1, none);
+    constexpr int ALLI = ALL | FEAT_IMPULSE;
+    if (cfg.contact && cfg.impulse) {
+        pass1_all<ALLI>(M, S);
+        // steady state: the leading backward sweep, `sweeps` x [forward
+        // sweep with contact, backward sweep], the fused finish/start sweep
+        g_tally = Tally{};
+        pass2<ALLI>(M, S);
+        for (int k = 0; k < sweeps; k++) {
+            sweep_forward<ALLI>(M, S);
+            pass2<ALLI>(M, S);
+        }
+        pass3_next<ALLI, false>(M, S, io, 1, none);
+    } else {
+        pass1_all<ALL>(M, S);
+        // steady state: one backward sweep + one fused finish/start sweep
+        g_tally = Tally{};
+        pass2<ALL>(M, S);
+        pass3_next<ALL, false>(M, S, io, 1, none);
+    }
     FlopCount fc;
     fc.flops = g_tally.flops;
     fc.transcendentals = g_tally.trans;

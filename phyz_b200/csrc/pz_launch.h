@@ -21,7 +21,7 @@ struct RolloutArgs {
     int model_bytes;         // multiple of 16
     int off_bi, off_pd, off_pdmap;
     int nb, nv, npd, contact;
-    int feat;              // kernel variant: FEAT_MULTI | FEAT_CONTACT | FEAT_PERM bits (pz_world.cuh)
+    int feat;              // kernel variant: Features bits (pz_world.cuh)
     double dt, gx, gy, gz, ground_h, friction;
     T* q;                  // [nv][nworld]
     T* v;                  // [nv][nworld]
@@ -34,6 +34,13 @@ struct RolloutArgs {
     long long nworld;
     int nsteps;
     int scratch;           // scratch slots per world
+    // impulse-mode contact (feat bit 16)
+    T* imp;                // [imp_slots][nworld]: per collidable body its wrench (6) and staged
+                           // impulses (3 per point), carried between steps and launches
+    int imp_slots;
+    int sweeps;            // [contact, backward sweep] pairs per step
+    double erp, margin, restitution, rest_thr;
+    double si_dmin, si_dmax, si_width, si_mid, si_power;
 };
 
 // tmem_cols > 0: configure the Tensor-Memory variant for a layout whose

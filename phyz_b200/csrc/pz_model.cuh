@@ -62,7 +62,8 @@ struct alignas(16) BodyI {
     int flags;        // BodyFlags
     int s_xj;         // joint transform data: hinge (c, s); ball/free R_J (9)
     int s_vw;         // body velocity (6) between passes 1 and 2, then W = U D^-1 (6*ndof)
-    int s_w0;         // control input of the step, then D^-1 u (ndof)
+    int s_w0;         // control input of the step (unless s_in is separate), then D^-1 u (ndof)
+    int s_in;         // control input of the step (ndof): s_w0, or its own slots in impulse mode
     int s_f;          // contact wrench, body frame (6)
     int s_acc;        // branch: accumulated child inertia (21) + bias force (6)
     int s_vold;       // branch: velocity of the step being finished (6)
@@ -71,12 +72,28 @@ struct alignas(16) BodyI {
     int gtype;        // geometry code (0 none)
     int t_rec;        // Tensor Memory column of the body's record [c, s, v|W] (-1: in s_xj/s_vw)
     int qshift;       // F_ZHINGE: parent->child relabelling (Q v)_a = v_(a+qshift mod 3)
+    // impulse-mode contact (-1 otherwise)
+    int s_up;         // collidable: world up in the body frame (3) and origin height (1)
+    int s_imp;        // collidable: staged impulses [normal, tangent u, tangent w] per point
+    int s_vf;         // branch: free velocity v + dt qdd of the sweep (6)
+    int c_imp;        // collidable: first row of the body's wrench (6) + impulses in the
+                      // persistent impulse buffer
+    int fshift;       // this body's frame relabelling: stored = P_fshift (original coordinates)
 };
 
 template <class T>
 struct alignas(16) PdT {
     T kp, kd, maxf;
     int qi, vi;
+};
+
+// Impulse-mode contact material (contact_pipeline.rs:85-95): ground height,
+// friction, dt, solref error reduction, margin, restitution and its
+// threshold, SolImp parameters.
+template <class T>
+struct ImpMat {
+    T ground_h, friction, dt, erp, margin, restitution, rest_thr;
+    T dmin, dmax, width, mid, power;
 };
 
 // Everything a world-step needs besides its own state.
@@ -92,6 +109,7 @@ struct ModelView {
     T ground_h, friction;
     T inv_dt_c;            // 1 / max(dt, 1e-9)   (phyz_kernels.cu:574-578)
     T kstiff_c;            // 4 / max(dt, 1e-9)^2
+    ImpMat<T> im;          // impulse-mode contact material
 };
 
 }  // namespace pz

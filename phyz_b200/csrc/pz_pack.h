@@ -74,8 +74,9 @@ struct PackInfo {
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
     int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges,
-                         // 8 = (with 4) every relabel is the shift-1 cycle
+                         // 8 = (with 4) every relabel is the shift-1 cycle, 16 = (with 2) impulse contact
     int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
+    int imp_slots = 0;   // impulse mode: rows per world of the persistent wrench + impulse buffer
 };
 
 inline int pad16(int b) { return (b + 15) & ~15; }
@@ -83,6 +84,7 @@ inline int pad16(int b) { return (b + 15) & ~15; }
 // Contact and PD settings that change the table.
 struct PackCfg {
     bool contact = false;
+    bool impulse = false;                // contact as the velocity-level impulse solve
     std::vector<double> gk, gd;          // per-body penalty gains (contact)
     std::vector<phyzb_pd_dof> pd;        // PD servos
 };
@@ -270,6 +272,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
                 if (unit) d.axis_k = k;
             }
         d.qshift = 0;
+        d.fshift = shift[i];
         if (tmem_kind(m->bodies[i])) {
             flags |= F_ZHINGE;
             d.qshift = (shift[i] - (b.parent >= 0 ? shift[b.parent] : 0) + 3) % 3;
@@ -295,11 +298,28 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         }
         d.s_w0 = next;
         next += nd;
-        d.s_f = -1;
+        const bool impulse = cfg.contact && cfg.impulse;
+        // impulse mode runs the backward sweep several times per step, so the
+        // control input keeps slots of its own
+        d.s_in = d.s_w0;
+        if (impulse) {
+            d.s_in = next;
+            next += nd;
+        }
+        d.s_f = d.s_up = d.s_imp = d.s_vf = d.c_imp = -1;
         if (cfg.contact && b.geom_type != 0) {
             flags |= F_CONTACT;
             d.s_f = next;
             next += 6;
+            if (impulse) {
+                const int npts = b.geom_type == 2 ? 8 : 1;
+                d.s_up = next;
+                next += 4;
+                d.s_imp = next;
+                next += 3 * npts;
+                d.c_imp = info.imp_slots;
+                info.imp_slots += 6 + 3 * npts;
+            }
         }
         d.s_acc = d.s_vold = d.s_acca = d.s_wx = -1;
         if (flags & F_BRANCH) {
@@ -312,6 +332,10 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             if (cfg.contact) {
                 d.s_wx = next;  // world up (3) and origin height (1)
                 next += 4;
+            }
+            if (impulse) {
+                d.s_vf = next;
+                next += 6;
             }
         }
         d.flags = flags;
@@ -332,6 +356,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
     for (int i = 0; i < nb; i++)
         if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;
     if (cfg.contact) info.feat |= 2;
+    if (cfg.contact && cfg.impulse) info.feat |= 16;
     bool all_one = true;
     for (int i = 0; i < nb; i++)
         if (bi[i].flags & F_ZHINGE) {
@@ -346,6 +371,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
 struct FlopCount {
     double flops = 0, transcendentals = 0;
 };
-FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg);
+// `sweeps`: contact sweeps per step when cfg.impulse.
+FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps = 0);
 
 }  // namespace pz

@@ -40,6 +40,8 @@ __device__ __forceinline__ float pz_atan2(float y, float x) { return atan2f(y, x
 __device__ __forceinline__ double pz_atan2(double y, double x) { return atan2(y, x); }
 __device__ __forceinline__ float pz_tanh(float x) { return tanhf(x); }
 __device__ __forceinline__ double pz_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float pz_pow(float x, float y) { return powf(x, y); }
+__device__ __forceinline__ double pz_pow(double x, double y) { return pow(x, y); }
 __device__ __forceinline__ float pz_abs(float x) { return fabsf(x); }
 __device__ __forceinline__ double pz_abs(double x) { return fabs(x); }
 __device__ __forceinline__ float pz_min(float a, float b) { return fminf(a, b); }

@@ -36,8 +36,9 @@ namespace pz {
 // hinge frame relabelled by a non-identity cyclic permutation, and (with
 // FEAT_PERM) every relabelled hinge relabelled by the same shift 1 -- a chain
 // whose axes cycle x, y, z -- so the relabel is a compile-time register
-// renaming instead of a run-time branch.
-enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8 };
+// renaming instead of a run-time branch; and (with FEAT_CONTACT) contact as
+// the velocity-level impulse solve instead of the penalty law.
+enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8, FEAT_IMPULSE = 16 };
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
@@ -517,7 +518,7 @@ template <class T, class Scr>
 PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S, int k, bool one_dof) {
     const int d = bi.off + k;
     const T qd = S(M.nv + d);
-    T in = S(bi.s_w0 + k);
+    T in = S(bi.s_in + k);
     if (bi.flags & F_PD) {
         const int pdi = M.pd_of_dof[d];
         if (pdi >= 0) {
@@ -844,7 +845,7 @@ PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& 
         const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
         const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
                                 : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
-        S.prefetch(bi.s_w0 + k, src);
+        S.prefetch(bi.s_in + k, src);
     }
 }
 // One-DOF form for the relabelled-hinge path.
@@ -855,7 +856,7 @@ PZ_HD void prefetch_control1(const ModelView<T>& M, const BodyI& bi, const Scr& 
     const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
     const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
                             : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
-    S.prefetch(bi.s_w0, src);
+    S.prefetch(bi.s_in, src);
 }
 
 // I c for a bias c whose K components are structurally zero (c = v x S qd
@@ -947,18 +948,69 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
             S(s + 3) = wf.pos.z;
         }
         if (bi.flags & F_CONTACT) {
-            const SV<T> f = contact_wrench_call(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, bi, &bt, wf, v,
-                                                false, i, Out<T>{nullptr, 0});
-            st_sv(S, bi.s_f, f);
+            if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+                // the impulse sweeps read the body's world up and height
+                S(bi.s_up) = wf.up.x;
+                S(bi.s_up + 1) = wf.up.y;
+                S(bi.s_up + 2) = wf.up.z;
+                S(bi.s_up + 3) = wf.pos.z;
+            } else {
+                const SV<T> f = contact_wrench_call(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, bi, &bt, wf,
+                                                    v, false, i, Out<T>{nullptr, 0});
+                st_sv(S, bi.s_f, f);
+            }
         }
     }
 }
 
+// Full world frame of body i for the state in scratch (joint transforms of
+// pass 1 in place), built by walking its ancestor chain: a body-frame vector
+// d maps into its parent as E_tree^T d (plus tree_pos for points).
+template <int FEAT, class T, class Scr>
+PZ_HD WF<T> world_frame(const ModelView<T>& M, const Scr& S, int i) {
+    // columns of the body->world rotation and the origin, built upwards
+    V3<T> cx = mk3<T>(T(1), T(0), T(0)), cy = mk3<T>(T(0), T(1), T(0)), cz = mk3<T>(T(0), T(0), T(1));
+    V3<T> o = zero3<T>();
+    for (int b = i; b >= 0; b = M.bi[b].parent) {
+        const BodyI bb = M.bi[b];
+        const BodyT<T>& tb = M.bt[b];
+        JX<T> j;
+        if (bb.t_rec >= 0) {
+            const Rec<T> r = S.rec_get(bb);
+            j.c = r.c;
+            j.s = r.s;
+        } else {
+            j = load_jx<-1, FEAT>(bb, tb, S);
+        }
+        // E_tree^T d = R_ptj^T R_J^T d
+        auto up_dir = [&](V3<T> d) {
+            switch (bb.jtype) {
+                case J_REVOLUTE: d = bb.axis_k >= 0 ? hrot_t(bb.axis_k, j.c, j.s, d) : rtmul(j.E, d); break;
+                case J_BALL:
+                case J_FREE:
+                    if constexpr ((FEAT & FEAT_MULTI) != 0) d = rtmul(j.E, d);
+                    break;
+                default: break;
+            }
+            if (bb.flags & F_PTJ_ROT) d = m3tv(tb.ptj_rot, d);
+            return d;
+        };
+        cx = up_dir(cx);
+        cy = up_dir(cy);
+        cz = up_dir(cz);
+        o = up_dir(o) + tree_pos<-1, FEAT>(bb, tb, j);
+    }
+    WF<T> wf;  // rows of the body->world rotation = components of the columns
+    wf.r0 = mk3<T>(cx.x, cy.x, cz.x);
+    wf.r1 = mk3<T>(cx.y, cy.y, cz.y);
+    wf.up = mk3<T>(cx.z, cy.z, cz.z);
+    wf.pos = o;
+    return wf;
+}
+
 // Contact state [touching, depth, point(3), force(3)] of every body for the
 // state in scratch (joint transforms and velocities of pass 1 in place),
-// written to rows 8*i.. of `cs` (layout.rs:68-80). Each collidable body's
-// full world frame is rebuilt by walking its ancestor chain: a body-frame
-// vector d maps into its parent as E_tree^T d (plus tree_pos for points).
+// written to rows 8*i.. of `cs` (layout.rs:68-80).
 template <int FEAT, class T, class Scr>
 PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>& cs) {
     for (int i = 0; i < M.nb; i++) {
@@ -967,44 +1019,189 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
             for (int k = 0; k < 8; k++) cs.put(8 * i + k, T(0));
             continue;
         }
-        // columns of the body->world rotation and the origin, built upwards
-        V3<T> cx = mk3<T>(T(1), T(0), T(0)), cy = mk3<T>(T(0), T(1), T(0)), cz = mk3<T>(T(0), T(0), T(1));
-        V3<T> o = zero3<T>();
-        for (int b = i; b >= 0; b = M.bi[b].parent) {
-            const BodyI bb = M.bi[b];
-            const BodyT<T>& tb = M.bt[b];
-            JX<T> j;
-            if (bb.t_rec >= 0) {
-                const Rec<T> r = S.rec_get(bb);
-                j.c = r.c;
-                j.s = r.s;
-            } else {
-                j = load_jx<-1, FEAT>(bb, tb, S);
-            }
-            // E_tree^T d = R_ptj^T R_J^T d
-            auto up_dir = [&](V3<T> d) {
-                switch (bb.jtype) {
-                    case J_REVOLUTE: d = bb.axis_k >= 0 ? hrot_t(bb.axis_k, j.c, j.s, d) : rtmul(j.E, d); break;
-                    case J_BALL:
-                    case J_FREE:
-                        if constexpr ((FEAT & FEAT_MULTI) != 0) d = rtmul(j.E, d);
-                        break;
-                    default: break;
-                }
-                if (bb.flags & F_PTJ_ROT) d = m3tv(tb.ptj_rot, d);
-                return d;
-            };
-            cx = up_dir(cx);
-            cy = up_dir(cy);
-            cz = up_dir(cz);
-            o = up_dir(o) + tree_pos<-1, FEAT>(bb, tb, j);
-        }
-        WF<T> wf;  // rows of the body->world rotation = components of the columns
-        wf.r0 = mk3<T>(cx.x, cy.x, cz.x);
-        wf.r1 = mk3<T>(cx.y, cy.y, cz.y);
-        wf.up = mk3<T>(cx.z, cy.z, cz.z);
-        wf.pos = o;
+        const WF<T> wf = world_frame<FEAT>(M, S, i);
         contact_wrench(M, bi, M.bt[i], wf, ld_vel<T>(S, bi), true, i, cs);
+    }
+}
+
+// ── impulse-mode ground contact (phyz_kernels.cu:581-622 helpers, :856-918
+// the impulse branch of contact_thread; flat ground) ───────────────────────
+// SolImp impedance at depth r (phyz_kernels.cu:589-601)
+template <class T>
+PZ_HD T solimp_impedance(const ImpMat<T>& m, const T& r) {
+    const T dmin = pz_min(pz_max(m.dmin, T(1e-4)), T(1) - T(1e-9));
+    const T dmax = pz_min(pz_max(m.dmax, T(1e-4)), T(1) - T(1e-9));
+    if (!(m.width > T(0))) return dmax;
+    const T x = pz_min(pz_max(pz_abs(r) / m.width, T(0)), T(1));
+    const T mid = pz_min(pz_max(m.mid, T(1e-6)), T(1) - T(1e-6));
+    const T pw = pz_max(m.power, T(1));
+    const T y = x <= mid ? pz_pow(x, pw) / pz_pow(mid, pw - T(1))
+                         : T(1) - pz_pow(T(1) - x, pw) / pz_pow(T(1) - mid, pw - T(1));
+    return dmin + y * (dmax - dmin);
+}
+// solimp when penetrating, smoothstep to zero across the margin (:604-611)
+template <class T>
+PZ_HD T impedance_at(const ImpMat<T>& m, const T& depth) {
+    if (depth >= T(0)) return solimp_impedance(m, depth);
+    const T gap = -depth;
+    if (!(m.margin > T(0)) || gap >= m.margin) return T(0);
+    const T sc = T(1) - gap / m.margin;
+    return sc * sc * (T(3) - T(2) * sc) * solimp_impedance(m, T(0));
+}
+// restitution ramp between v_rest and 2 v_rest (:613-622)
+template <class T>
+PZ_HD T effective_restitution(const ImpMat<T>& m, const T& e, const T& approach) {
+    const T vr = m.rest_thr;
+    if (!(vr > T(0))) return e;
+    const T sp = pz_abs(approach);
+    if (sp <= vr) return T(0);
+    if (sp >= T(2) * vr) return e;
+    const T t = (sp - vr) / vr;
+    return e * t * t * (T(3) - T(2) * t);
+}
+// orthonormal tangents around a unit normal (:581-586)
+template <class T>
+PZ_HD void contact_tangents(const V3<T>& n, V3<T>& u, V3<T>& w) {
+    const V3<T> a = pz_abs(n.x) > T(0.9) ? mk3<T>(T(0), T(1), T(0)) : mk3<T>(T(1), T(0), T(0));
+    const V3<T> c = cross(n, a);
+    const T l = pz_sqrt(dot(c, c));
+    u = l > T(0) ? c * (T(1) / l) : c;
+    w = cross(n, u);
+}
+
+// The tangents of contact_tangents taken in the body's original frame and
+// expressed in its stored (relabelled) one: the staged update treats the two
+// tangent directions separately, so its result depends on the basis, which
+// has to be the reference's.
+template <class T>
+PZ_HD void body_tangents(const BodyI& bi, const V3<T>& n, V3<T>& u, V3<T>& w) {
+    if (bi.fshift == 1) {
+        contact_tangents(cperm<2>(n), u, w);
+        u = cperm<1>(u);
+        w = cperm<1>(w);
+    } else if (bi.fshift == 2) {
+        contact_tangents(cperm<1>(n), u, w);
+        u = cperm<2>(u);
+        w = cperm<2>(w);
+    } else {
+        contact_tangents(n, u, w);
+    }
+}
+
+// One staged Coulomb update of every contact point of body i (normal
+// impulse first, then the tangential impulse clamped into the friction disc
+// that normal admits), at the body's free velocity `vf` (body frame) with
+// world up `up` (body frame) and origin height `z0`. The impulses of the
+// previous sweep are read from and the new ones written to the body's
+// impulse slots; returns the wrench (body frame) they apply over one step.
+template <class T, class Scr>
+PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const BodyI& bi, const BodyT<T>& bt, const V3<T>& up, const T& z0,
+                           const SV<T>& vf, const Scr& S) {
+    const int npts = bi.gtype == 2 ? 8 : 1;
+    const T dtc = pz_max(m.dt, T(1e-9));
+    // within-body load sharing: points inside the margin
+    int n_active = 0;
+    for (int c = 0; c < npts; c++) {
+        const V3<T> sup = support_pt(bi, bt, up, c);
+        if (m.ground_h - (z0 + dot(up, sup)) > -m.margin) n_active++;
+    }
+    const T na = T(n_active < 1 ? 1 : n_active);
+    SV<T> f = zerosv<T>();
+    bool any = false;
+    for (int c = 0; c < npts; c++) {
+        const int slot = bi.s_imp + 3 * c;
+        const V3<T> sup = support_pt(bi, bt, up, c);
+        const T pen = m.ground_h - (z0 + dot(up, sup));
+        if (!(pen > -m.margin)) {
+            S(slot) = T(0);
+            S(slot + 1) = T(0);
+            S(slot + 2) = T(0);
+            continue;
+        }
+        const V3<T>& n = up;
+        const V3<T> vp = vf.l + cross(vf.w, sup);
+        V3<T> tu, tw;
+        body_tangents(bi, n, tu, tw);
+        const T bn = dot(vp, n), bu = dot(vp, tu), bw = dot(vp, tw);
+        const T mn = eff_mass(bt, sup, n) / na;
+        const T ann = T(1) / pz_max(mn, T(1e-9));
+        const T bias = impedance_at(m, pen) * m.erp * pz_max(pen, T(0)) / dtc;
+        const T e = effective_restitution(m, m.restitution, pz_min(bn, T(0)));
+        const T rn = bn * (T(1) + e) - ann * S(slot);
+        const T fn = pz_max((bias - rn) / ann, T(0));
+        const T auu = na / pz_max(eff_mass(bt, sup, tu), T(1e-9));
+        const T aww = na / pz_max(eff_mass(bt, sup, tw), T(1e-9));
+        T ju = -(bu - auu * S(slot + 1)) / auu;
+        T jw = -(bw - aww * S(slot + 2)) / aww;
+        const T limit = m.friction * fn;
+        const T jt = pz_sqrt(ju * ju + jw * jw);
+        if (jt > limit) {
+            const T sc = jt > T(0) ? limit / jt : T(0);
+            ju = ju * sc;
+            jw = jw * sc;
+        }
+        S(slot) = fn;
+        S(slot + 1) = ju;
+        S(slot + 2) = jw;
+        const V3<T> fb = (n * fn + tu * ju + tw * jw) * (T(1) / dtc);
+        f.w = f.w + cross(sup, fb);
+        f.l = f.l + fb;
+        any = true;
+    }
+    if (!any)
+        for (int k = 0; k < 3 * npts; k++) S(bi.s_imp + k) = T(0);
+    return f;
+}
+
+// Out-of-line entry, everything by value: the sweep's own state stays in
+// registers.
+template <class T, class Scr>
+PZ_OUTLINE SV<T> impulse_wrench_call(ImpMat<T> m, BodyI bi, const BodyT<T>* bt, V3<T> up, T z0, SV<T> vf, Scr S) {
+    return impulse_wrench(m, bi, *bt, up, z0, vf, S);
+}
+
+// Contact state of every body in impulse mode, from the impulses the last
+// sweep left in the slots (phyz_kernels.cu:964-980 with the impulse
+// branch's point and force): [touching, depth, point(3), force(3)].
+template <int FEAT, class T, class Scr>
+PZ_HD void contact_state_impulse_pass(const ModelView<T>& M, const Scr& S, const Out<T>& cs) {
+    const T idt = T(1) / pz_max(M.im.dt, T(1e-9));
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        if (!(bi.flags & F_CONTACT)) {
+            for (int k = 0; k < 8; k++) cs.put(8 * i + k, T(0));
+            continue;
+        }
+        const BodyT<T>& bt = M.bt[i];
+        const WF<T> wf = world_frame<FEAT>(M, S, i);
+        const int npts = bi.gtype == 2 ? 8 : 1;
+        V3<T> fw = zero3<T>(), dp = zero3<T>();
+        T deepest = T(0);
+        bool any = false;
+        for (int c = 0; c < npts; c++) {
+            const V3<T> sup = support_pt(bi, bt, wf.up, c);
+            const T z = wf.pos.z + dot(wf.up, sup);
+            const T pen = M.im.ground_h - z;
+            if (!(pen > -M.im.margin)) continue;
+            V3<T> tu, tw;
+            body_tangents(bi, wf.up, tu, tw);
+            const int slot = bi.s_imp + 3 * c;
+            const V3<T> fb = (wf.up * S(slot) + tu * S(slot + 1) + tw * S(slot + 2)) * idt;
+            fw = fw + mk3<T>(dot(wf.r0, fb), dot(wf.r1, fb), dot(wf.up, fb));
+            any = true;
+            if (pen > deepest) {
+                deepest = pen;
+                dp = mk3<T>(wf.pos.x + dot(wf.r0, sup), wf.pos.y + dot(wf.r1, sup), z);
+            }
+        }
+        cs.put(8 * i + 0, any ? T(1) : T(0));
+        cs.put(8 * i + 1, any ? deepest : T(0));
+        cs.put(8 * i + 2, any ? dp.x : T(0));
+        cs.put(8 * i + 3, any ? dp.y : T(0));
+        cs.put(8 * i + 4, any ? dp.z : T(0));
+        cs.put(8 * i + 5, any ? fw.x : T(0));
+        cs.put(8 * i + 6, any ? fw.y : T(0));
+        cs.put(8 * i + 7, any ? fw.z : T(0));
     }
 }
 
@@ -1342,6 +1539,118 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
 #define PZ_P3(AX) pass3_body<AX, FEAT, LAST>(M, S, io, i, bi, next_step, qdd_out, cvo, ca, cvn, cw)
         PZ_BY_KIND(body_kind(bi), PZ_P3)
 #undef PZ_P3
+    }
+    S.fence_st();
+}
+
+// ── one impulse sweep, forward half (cuda/mod.rs:916-927; phyz_kernels.cu
+// :1322-1368 then :804-918): body i's accelerations from the backward sweep
+// just run, its body velocity put back for the next backward sweep, its free
+// velocity X v_f,parent + S (qd + dt qdd), and -- if collidable -- one
+// staged impulse update whose wrench the next backward sweep applies. The
+// free velocity carries every impulse written so far through the whole
+// articulated chain, which is what makes the iteration matrix-free.
+template <int AX, int FEAT, class T, class Scr>
+PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& cvo, SV<T>& ca,
+                      SV<T>& cvf) {
+    const BodyT<T>& bt = M.bt[i];
+    const int p = bi.parent;
+    JX<T> j;
+    SV<T> Wv;
+    if constexpr (AX >= 0) {
+        const Rec<T> rec = S.rec_get(bi);
+        j.c = rec.c;
+        j.s = rec.s;
+        Wv = rec.v;
+    } else {
+        j = load_jx<AX, FEAT>(bi, bt, S);
+    }
+    SV<T> vpo, apar, vfp;
+    if (p < 0) {
+        vpo = zerosv<T>();
+        vfp = zerosv<T>();
+        apar = mksv<T>(zero3<T>(), mk3<T>(-M.gx, -M.gy, -M.gz));
+    } else if (p == i - 1) {
+        vpo = cvo;
+        apar = ca;
+        vfp = cvf;
+    } else {
+        vpo = ld_sv<T>(S, M.bi[p].s_vold);
+        apar = ld_sv<T>(S, M.bi[p].s_acca);
+        vfp = ld_sv<T>(S, M.bi[p].s_vf);
+    }
+    SV<T> vo, c;
+    if constexpr (AX >= 0) {
+        const T qd = S(M.nv + bi.off);
+        vo = mot_X<AX, FEAT>(bi, bt, j, vpo);
+        at<AX>(vo.w) = at<AX>(vo.w) + qd;
+        c = mksv<T>(cross_axis<AX>(vo.w, qd), cross_axis<AX>(vo.l, qd));
+    } else {
+        const SV<T> vj = joint_vel<AX, FEAT>(bi, bt, S, M.nv);
+        vo = mot_X<AX, FEAT>(bi, bt, j, vpo) + vj;
+        c = crm(vo, vj);
+    }
+    SV<T> a = mot_X<AX, FEAT>(bi, bt, j, apar) + c;
+    SV<T> vf = mot_X<AX, FEAT>(bi, bt, j, vfp);
+    if (AX >= 0 || bi.ndof == 1) {
+        T qdd0;
+        if constexpr (AX >= 0)
+            qdd0 = S(bi.s_w0) - dot(Wv, a);
+        else
+            qdd0 = S(bi.s_w0) - dot(ld_sv<T>(S, bi.s_vw), a);
+        const T u = S(M.nv + bi.off) + M.dt * qdd0;
+        if constexpr (AX >= 0) {
+            at<AX>(a.w) = at<AX>(a.w) + qdd0;
+            at<AX>(vf.w) = at<AX>(vf.w) + u;
+        } else {
+            const V3<T> ax = ld3(bt.axis);
+            if (bi.jtype == J_REVOLUTE) {
+                a.w = a.w + ax * qdd0;
+                vf.w = vf.w + ax * u;
+            } else {
+                a.l = a.l + ax * qdd0;
+                vf.l = vf.l + ax * u;
+            }
+        }
+    } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
+        if (bi.ndof > 1) {
+            multi_qdd(bi, S, a);  // qdd into the w0 slots
+            const int o = M.nv + bi.off;
+            vf.w = vf.w + mk3<T>(S(o) + M.dt * S(bi.s_w0), S(o + 1) + M.dt * S(bi.s_w0 + 1),
+                                 S(o + 2) + M.dt * S(bi.s_w0 + 2));
+            if (bi.ndof == 6)
+                vf.l = vf.l + mk3<T>(S(o + 3) + M.dt * S(bi.s_w0 + 3), S(o + 4) + M.dt * S(bi.s_w0 + 4),
+                                     S(o + 5) + M.dt * S(bi.s_w0 + 5));
+        }
+    }
+    if (bi.flags & F_BRANCH) {
+        st_sv(S, bi.s_vold, vo);
+        st_sv(S, bi.s_acca, a);
+        st_sv(S, bi.s_vf, vf);
+    }
+    cvo = vo;
+    ca = a;
+    cvf = vf;
+    // the backward sweep reads the body velocity where it left W
+    if constexpr (AX >= 0)
+        S.rec_put_vw(bi, vo);
+    else
+        st_sv(S, bi.s_vw, vo);
+    if (bi.flags & F_CONTACT) {
+        const V3<T> up = mk3<T>(S(bi.s_up), S(bi.s_up + 1), S(bi.s_up + 2));
+        const SV<T> f = impulse_wrench_call(M.im, bi, &bt, up, S(bi.s_up + 3), vf, S);
+        st_sv(S, bi.s_f, f);
+    }
+}
+
+template <int FEAT, class T, class Scr>
+PZ_HD void sweep_forward(const ModelView<T>& M, const Scr& S) {
+    SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvf = zerosv<T>();
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+#define PZ_SW(AX) sweep_body<AX, FEAT>(M, S, i, bi, cvo, ca, cvf)
+        PZ_BY_KIND(body_kind(bi), PZ_SW)
+#undef PZ_SW
     }
     S.fence_st();
 }

@@ -184,6 +184,18 @@ __device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const
     const double dtc = P.dt > 1e-9 ? P.dt : 1e-9;
     M.inv_dt_c = T(1.0 / dtc);
     M.kstiff_c = T(4.0 / (dtc * dtc));
+    M.im.ground_h = T(P.ground_h);
+    M.im.friction = T(P.friction);
+    M.im.dt = T(P.dt);
+    M.im.erp = T(P.erp);
+    M.im.margin = T(P.margin);
+    M.im.restitution = T(P.restitution);
+    M.im.rest_thr = T(P.rest_thr);
+    M.im.dmin = T(P.si_dmin);
+    M.im.dmax = T(P.si_dmax);
+    M.im.width = T(P.si_width);
+    M.im.mid = T(P.si_mid);
+    M.im.power = T(P.si_power);
     return M;
 }
 
@@ -244,18 +256,37 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
         for (int i = 0; i < M.nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
         S.commit();
+        if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+            // the wrenches of the previous step's last sweep and the staged
+            // impulses that warm-start this one
+            for (int i = 0; i < M.nb; i++) {
+                const BodyI bi = M.bi[i];
+                if (bi.c_imp < 0) continue;
+                const int nimp = 3 * (bi.gtype == 2 ? 8 : 1);
+                for (int k = 0; k < 6; k++) S(bi.s_f + k) = P.imp[(long long)(bi.c_imp + k) * N + w];
+                for (int k = 0; k < nimp; k++) S(bi.s_imp + k) = P.imp[(long long)(bi.c_imp + 6 + k) * N + w];
+            }
+        }
         const Out<T> none{nullptr, 0};
         pass1_all<FEAT>(M, S);
         for (int s = 0; s < P.nsteps; s++) {
             S.wait();
             const bool last = s == P.nsteps - 1;
-            if constexpr ((FEAT & FEAT_CONTACT) != 0) {
+            if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
                 // contact state of the last step, from the state it starts from
                 // (every lane runs it, warp-wide record loads; only active lanes write)
                 if (last && P.contact && P.cstate)
                     contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
             pass2<FEAT>(M, S);
+            if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+                // sweeps x [contact at the free velocity -> backward sweep]
+                for (int k = 0; k < P.sweeps; k++) {
+                    sweep_forward<FEAT>(M, S);
+                    pass2<FEAT>(M, S);
+                }
+                if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
+            }
             if (last)
                 pass3_next<FEAT, true>(M, S, io, -1, active ? Out<T>{P.qdd + w, N} : none);
             else
@@ -263,6 +294,16 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
             S.commit();
         }
         S.wait();
+        if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+            if (active)
+                for (int i = 0; i < M.nb; i++) {
+                    const BodyI bi = M.bi[i];
+                    if (bi.c_imp < 0) continue;
+                    const int nimp = 3 * (bi.gtype == 2 ? 8 : 1);
+                    for (int k = 0; k < 6; k++) P.imp[(long long)(bi.c_imp + k) * N + w] = S(bi.s_f + k);
+                    for (int k = 0; k < nimp; k++) P.imp[(long long)(bi.c_imp + 6 + k) * N + w] = S(bi.s_imp + k);
+                }
+        }
         if (active) {
             bool finite = true;
             for (int j = 0; j < M.nv; j++) {

@@ -60,6 +60,17 @@ def free_sphere(mass=1.0, radius=0.1):
             .build())
 
 
+def free_box(pos=(0.0, 0.0, 0.5), half=(0.1, 0.1, 0.1), mass=1.0):
+    """contact_impulse_parity.rs:48-66: a free box, its joint frame at `pos`."""
+    hx, hy, hz = half
+    c = mass / 3.0
+    inertia = np.diag([c * (hy * hy + hz * hz), c * (hx * hx + hz * hz), c * (hx * hx + hy * hy)])
+    return (ModelBuilder().gravity([0.0, 0.0, -9.81]).dt(0.001)
+            .add_free_body("box", -1, Transform.from_translation(list(pos)),
+                           SpatialInertia.new(mass, np.zeros(3), inertia), geometry=Geometry.box(hx, hy, hz))
+            .build())
+
+
 def single_step_cases():
     """(label, model, q, v, tolerance in the reference's f32 suite)."""
     cases = []

@@ -75,3 +75,55 @@ def test_faster_than_the_reference_gpu_kernels(refcuda, name, nworld, steps):
     print(f"\n{name}: B200 stepper {ours:.3e} world-steps/s, reference CUDA kernels {ref:.3e} "
           f"world-steps/s on the same GPU: {ours / ref:.1f}x")
     assert ours > 2 * ref
+
+
+def impulse_inputs(n):
+    m = configs.quadruped()
+    q0, v0 = configs.initial_state("c3_quadruped", m, range(n))
+    q0[:, 5] = np.linspace(0.55, 0.62, n)  # feet on or just above the ground
+    return m, q0, v0, np.zeros((n, m.nv), np.float32)
+
+
+def test_impulse_mode_matches_the_reference_gpu_kernels(refhost, refcuda):
+    """Impulse-mode contact (16 sweeps) on the quadruped: the reference's GPU
+    sequence (35 launches per step) against the fused kernel, f32, from a
+    fresh warm start."""
+    n, steps = 256, 40
+    m, q0, v0, ctrl = impulse_inputs(n)
+    qr, vr, _, csr, _ = refcuda.rollout(m, q0, v0, ctrl, steps, contact=(0.0, 1.0), sweeps=16)
+    qh, vh, _, _, _ = refhost.rollout_impulse(m, q0, v0, ctrl, nsteps=steps, contact=(0.0, 1.0))
+    assert rel_err(qr, qh) < 1e-4
+    sim = BatchSim(m, n, precision="f32")
+    sim.enable_contact_impulse(0.0, 1.0)
+    sim.load_states(q0, v0, ctrl)
+    sim.step_many(steps)
+    qd, vd = sim.readback_states()
+    cs = sim.readback_contacts()
+    sim.close()
+    assert cs[:, :, 0].sum() > 0
+    assert rel_err(qd, qr) < 2e-3, rel_err(qd, qr)
+    assert np.array_equal(cs[:, :, 0], csr[:, :, 0])
+
+
+def test_impulse_mode_faster_than_the_reference_gpu_kernels(refcuda):
+    n, steps = 65536, 20
+    m, q0, v0, ctrl = impulse_inputs(n)
+    _, _, _, _, ms_ref = refcuda.rollout(m, q0, v0, ctrl, steps, contact=(0.0, 1.0), sweeps=16, reps=3)
+    sim = BatchSim(m, n, precision="f32")
+    sim.enable_contact_impulse(0.0, 1.0)
+    st = torch.cuda.Stream()
+    sim.set_stream(st.cuda_stream)
+    best = 1e30
+    for _ in range(4):
+        sim.load_states(q0, v0, ctrl)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        sim.step_many(steps)
+        e1.record(st)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    sim.close()
+    ours, ref = n * steps / best * 1e3, n * steps / ms_ref * 1e3
+    print(f"\nimpulse C3: B200 stepper {ours:.3e} world-steps/s, reference CUDA kernels {ref:.3e} "
+          f"world-steps/s on the same GPU: {ours / ref:.1f}x")
+    assert ours > 2 * ref
