@@ -19,6 +19,10 @@ final state read back, inside the timed region. `roofline` is the fused
 kernel against the measured FP32/FP64 FMA pipe. `cpu_baseline` is the
 reference's own kernels compiled as host C++ (oracle/_ref), on this host's
 cores. `--impl reference` times only that reference CPU path.
+
+`--config c3_quadruped_impulse` runs C3's worlds with impulse-mode contact
+(16 staged Coulomb sweeps per step) in place of the penalty law, 100 steps
+per rollout by default.
 """
 from __future__ import annotations
 
@@ -45,8 +49,22 @@ import numpy as np  # noqa: E402
 # with the per-world-step part taken from the capture after removing its
 # state bytes.
 NCU_DRAM_CAPTURES: dict = {
-    ("c2_chain32", "f32"): {"nworld": 65536, "horizon": 20, "bytes": 184.842240e6 + 12.996096e6},
+    ("c2_chain32", "f32"): {"nworld": 65536, "horizon": 20, "bytes": 184.666880e6 + 12.603904e6},
 }
+
+# Workloads beyond BASELINE.json's configs: a config's model, worlds and
+# initial state with impulse-mode contact (enable_contact_impulse, 16 sweeps
+# per step) in place of the penalty law, over a shorter default horizon
+# (every impulse step runs 17 backward sweeps).
+IMPULSE_WORKLOADS = {"c3_quadruped_impulse": ("c3_quadruped", 100)}
+
+
+def base_config(name):
+    """(config name the model / state / contact come from, impulse?, default horizon or 0)."""
+    if name in IMPULSE_WORKLOADS:
+        base, horizon = IMPULSE_WORKLOADS[name]
+        return base, True, horizon
+    return name, False, 0
 
 
 def ncu_traffic(config, prec, nv, esz, nworld, horizon):
@@ -164,18 +182,22 @@ def allreduce_max(x: float, world: int) -> float:
 
 
 # ── the reference's CPU path (oracle/_ref) ────────────────────────────────
-def reference_cpu(cfg_name, model, nworld, horizon, seconds, world_offset=0):
+def reference_cpu(workload, model, nworld, horizon, seconds, world_offset=0):
     """Time the reference's own kernels compiled as host C++ on every host
-    core, on a bounded sample of the workload: up to 16384 of its worlds for
+    core, on a bounded sample of the workload: up to 16384 of its worlds (2048
+    in impulse mode) for
     as many of its steps as fit ~`seconds` (controls from a 64-step seeded
-    schedule reused cyclically). Returns (world-steps/s, threads, sample)."""
+    schedule reused cyclically; in impulse mode the reference's sweep
+    sequence, its warm start carried between chunks). Returns (world-steps/s,
+    threads, sample)."""
     from oracle.oracle import RefHost, cpu_threads
     from phyz_b200 import configs
 
+    cfg_name, impulse, _ = base_config(workload)
     ref = RefHost()
     cfg = configs.CONFIGS[cfg_name]
     threads = cpu_threads()
-    n = min(nworld, 16384)
+    n = min(nworld, 2048 if impulse else 16384)  # an impulse step costs ~17 plain ones
     worlds = np.arange(world_offset, world_offset + n)
     q, v = configs.initial_state(cfg_name, model, worlds)
     contact = None
@@ -185,17 +207,30 @@ def reference_cpu(cfg_name, model, nworld, horizon, seconds, world_offset=0):
     rng = np.random.default_rng(configs.CTRL_SEED)
     period = 64
     sched = (rng.standard_normal((period, n, model.nv)) * cfg.ctrl_sigma * configs.actuated(model)).astype(np.float32)
+    state = [None]
+
+    def chunk(q, v, steps, ctrl):
+        if impulse:
+            q, v, _, _, state[0] = ref.rollout_impulse(model, q, v, ctrl, steps, schedule=True,
+                                                       contact=(contact[0], contact[1]), state=state[0],
+                                                       nthreads=threads)
+            return q, v
+        q, v, _, _ = ref.rollout(model, q, v, ctrl, steps, schedule=True, contact=contact, nthreads=threads)
+        return q, v
+
     # calibrate on 4 steps, then run whole 64-step chunks for ~`seconds`
     t0 = time.perf_counter()
-    ref.rollout(model, q, v, sched[:4], 4, schedule=True, contact=contact, nthreads=threads)
+    chunk(q, v, 4, sched[:4])
+    state[0] = None
     per_step = (time.perf_counter() - t0) / 4
     chunks = int(max(1, min(-(-horizon // period), seconds / max(per_step * period, 1e-9))))
     t0 = time.perf_counter()
     for _ in range(chunks):
-        q, v, _, _ = ref.rollout(model, q, v, sched, period, schedule=True, contact=contact, nthreads=threads)
+        q, v = chunk(q, v, period, sched)
     dt = time.perf_counter() - t0
     steps = chunks * period
-    return n * steps / dt, threads, (f"{n} of {nworld} worlds x {steps} of {horizon} steps, f32, "
+    mode = ", impulse contact (16 sweeps)" if impulse else ""
+    return n * steps / dt, threads, (f"{n} of {nworld} worlds x {steps} of {horizon} steps, f32{mode}, "
                                      f"{threads} threads, {dt:.1f} s")
 
 
@@ -204,10 +239,11 @@ def run_reference_impl(args, world, rank):
 
     if rank != 0:
         return
-    cfg = configs.CONFIGS[args.config]
+    cfg_name, _, h_default = base_config(args.config)
+    cfg = configs.CONFIGS[cfg_name]
     model = cfg.builder()
     nworld = args.nworld or cfg.nworld
-    horizon = args.horizon or cfg.steps
+    horizon = args.horizon or h_default or cfg.steps
     vals = []
     for i in range(args.warmup + args.steps):
         v, threads, sample = reference_cpu(args.config, model, nworld, horizon,
@@ -246,10 +282,11 @@ def main():
     from phyz_b200 import _lib as L
     from phyz_b200.parallel import Comm, share_bytes, weak_block
 
-    cfg = configs.CONFIGS[args.config]
+    cfg_name, impulse, h_default = base_config(args.config)
+    cfg = configs.CONFIGS[cfg_name]
     model = cfg.builder()
     nworld = args.nworld or cfg.nworld
-    horizon = args.horizon or cfg.steps
+    horizon = args.horizon or h_default or cfg.steps
     prec = args.precision
     tdt = torch.float32 if prec == "f32" else torch.float64
     esz = 4 if prec == "f32" else 8
@@ -257,13 +294,15 @@ def main():
     offset, _ = weak_block(nworld, rank)  # this rank's block of worlds
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
-    if cfg.contact:
+    if cfg.contact and impulse:
+        sim.enable_contact_impulse(cfg.contact[0], cfg.contact[3])
+    elif cfg.contact:
         sim.enable_ground_contact(*cfg.contact)
     stream = torch.cuda.Stream()
     sim.set_stream(stream.cuda_stream)
 
     # inputs resident in HBM: initial state (SoA) and the per-step controls
-    q0, v0 = configs.initial_state(args.config, model, np.arange(offset, offset + nworld))
+    q0, v0 = configs.initial_state(cfg_name, model, np.arange(offset, offset + nworld))
     sim.load_states(q0, v0)
     q0_dev = torch.tensor(q0.T.copy(), dtype=tdt, device="cuda")
     v0_dev = torch.tensor(v0.T.copy(), dtype=tdt, device="cuda")
@@ -397,6 +436,8 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": prec, "data": "synthetic (seeded)",
             "config": {"workload": args.config, "nworld_per_gpu": nworld, "horizon": horizon, "nbodies":
                        model.nbodies, "nv": nv, "parallelism": f"worlds sharded over {world} GPU(s)",
+                       "contact": (f"impulse, {sim.contact_sweeps} sweeps per step" if impulse
+                                   else ("penalty" if cfg.contact else None)),
                        "l2": "inputs larger than L2: the per-step control schedule "
                              f"({horizon * nv * nworld * esz / 1e9:.1f} GB) streams from HBM every rollout",
                        "launch": info},
