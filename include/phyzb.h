@@ -187,6 +187,41 @@ int phyzb_enable_ground_contact(phyzb_sim* sim, double ground_height, double sti
 int phyzb_enable_ground_contact_per_body(phyzb_sim* sim, double ground_height,
                                          double friction, const double* stiffness,
                                          const double* damping, int32_t* collidable_out);
+/* Heightfield terrain: phyz_model::Heightfield
+ * (crates/phyz-model/src/heightfield.rs:10-37). Node (ix, iy) at world
+ * (origin[0] + ix cell, origin[1] + iy cell), height origin[2] +
+ * heights[iy * nx + ix]; bilinear between nodes, clamped to the border
+ * outside the grid (phyz_kernels.cu:625-664). Copied in at the call. */
+typedef struct phyzb_heightfield {
+    double origin[3];
+    double cell;          /* > 0 */
+    int32_t nx, ny;       /* >= 1 each */
+    const float* heights; /* ny rows of nx */
+} phyzb_heightfield;
+/* A contact plane attached to a body (contact_pipeline.rs:318-355
+ * BodyPlane): the face at `offset` along the body's +z, `half_x` x `half_y`
+ * in its x/y, contacts deeper than `max_depth` ignored, `exclude` bodies
+ * never touch it. */
+typedef struct phyzb_body_plane {
+    int32_t body;
+    double offset, max_depth, half_x, half_y;
+    const int32_t* exclude;
+    int32_t n_exclude;
+} phyzb_body_plane;
+/* BatchSim::enable_contact_terrain / enable_ground_contact_with_plane
+ * (cuda/mod.rs:642-676): penalty contact with per-body gains (nbodies
+ * each) against the heightfield `hf` (NULL: the flat plane at
+ * ground_height, which a loaded heightfield overrides) and an optional
+ * body-attached plane (not available in this build: PHYZB_ERR_UNSUPPORTED).
+ * The device node buffer is sized to this first field. */
+int phyzb_enable_contact_terrain(phyzb_sim* sim, double ground_height, double friction,
+                                 const double* stiffness, const double* damping,
+                                 const phyzb_body_plane* plane, const phyzb_heightfield* hf,
+                                 int32_t* collidable_out);
+/* BatchSim::set_heightfield (cuda/mod.rs:741-759): replace the terrain in
+ * place; contact must be enabled and the field fit the node buffer sized at
+ * enable time (1 node when enabled without a heightfield). */
+int phyzb_set_heightfield(phyzb_sim* sim, const phyzb_heightfield* hf);
 /* BatchSim::enable_contact_impulse (cuda/mod.rs:680-701): contact as the
  * velocity-level convex impulse solve -- per step, the backward sweep with
  * the previous step's contact wrenches, then `sweeps` x [one staged Coulomb
@@ -195,9 +230,11 @@ int phyzb_enable_ground_contact_per_body(phyzb_sim* sim, double ground_height,
  * previous step's impulses. Material: GroundContactParams::default with
  * solref_erp_from(0.02, 1.0, dt) (contact_pipeline.rs:199-237). The
  * per-body gains (nullable; penalty-only) are kept but do not enter the
- * impulse law. Enabling resets the warm start to zero. */
+ * impulse law. `hf` and `plane` as in phyzb_enable_contact_terrain.
+ * Enabling resets the warm start to zero. */
 int phyzb_enable_contact_impulse(phyzb_sim* sim, double ground_height, double friction,
                                  const double* stiffness, const double* damping,
+                                 const phyzb_body_plane* plane, const phyzb_heightfield* hf,
                                  int32_t* collidable_out);
 /* BatchSim::contact_sweeps (cuda/mod.rs:449-451, default 16): contact sweeps
  * per step in impulse mode, 1 .. PHYZB_MAX_CONTACT_SWEEPS. (The reference

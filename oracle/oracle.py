@@ -56,6 +56,8 @@ class Oracle:
         L.oracle_penalty_contact.argtypes = [MP, C.c_int64, _D, _D, C.c_double, C.c_double, _D, _D, _D, _D]
         L.oracle_rollout.argtypes = [MP, C.c_int64, _D, _D, _D, C.c_int64, C.c_int32, C.c_int32, C.c_double,
                                      C.c_double, _D, _D, C.c_int32, _I, _D, _D, _D, _D, C.c_int32]
+        L.oracle_set_heightfield.argtypes = [C.c_int32, C.c_int32, C.c_double, C.c_double, C.c_double,
+                                             C.c_double, _F]
         L.oracle_rollout_impulse.argtypes = [MP, C.c_int64, _D, _D, _D, C.c_int64, C.c_int32, _D, C.c_int32,
                                              C.c_int32, _I, _D, _D, _D, _D, _D, C.c_int32]
         for f in ("oracle_aba", "oracle_rnea", "oracle_integrate_configuration", "oracle_forward_kinematics",
@@ -206,6 +208,31 @@ def _rollout_impulse(self, model, q, v, ctrl=None, nsteps=1, schedule=False, con
 Oracle.rollout_impulse = _rollout_impulse
 
 
+def _set_heightfield(self, hf=None):
+    """The terrain the following contact rollouts sample (a
+    phyz_b200.Heightfield; None: the flat plane at their ground height)."""
+    if hf is None:
+        self.lib.oracle_set_heightfield(0, 0, 0.0, 0.0, 0.0, 1.0, None)
+        return
+    h = np.ascontiguousarray(hf.heights, np.float32).reshape(-1)
+    self.lib.oracle_set_heightfield(hf.nx, hf.ny, *[float(x) for x in hf.origin], float(hf.cell), _f(h))
+
+
+Oracle.set_heightfield = _set_heightfield
+
+
+def _terrain_at(self, x, y):
+    """(height, unit normal) of the current terrain at world (x, y)."""
+    self.lib.oracle_terrain_at.restype = C.c_double
+    self.lib.oracle_terrain_at.argtypes = [C.c_double, C.c_double, _D]
+    n = np.zeros(3)
+    h = self.lib.oracle_terrain_at(float(x), float(y), _d(n))
+    return h, n
+
+
+Oracle.terrain_at = _terrain_at
+
+
 class RefHost:
     """The reference's f32 kernels compiled as host C++ (phyz_host_*)."""
 
@@ -223,6 +250,8 @@ class RefHost:
         L.phyzref_rollout.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
                                       C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, C.c_uint32, _F, _F,
                                       _F, _F, _F, C.c_int64, C.c_int32, _F, _F]
+        L.phyzref_set_heightfield.argtypes = [C.c_uint32, C.c_uint32, C.c_float, C.c_float, C.c_float, C.c_float,
+                                              _F]
         L.phyzref_rollout_impulse.argtypes = [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_float, C.c_float,
                                               C.c_float, C.c_float, _F, _F, C.c_float, C.c_float, _F, C.c_int32,
                                               C.c_uint32, _F, _F, _F, _F, _F, C.c_int64, C.c_int32, _F, _F, _F]
@@ -315,6 +344,15 @@ class RefHost:
                                  float(ground), float(fr), npd, _f(tbl), _f(tg), _f(qf), _f(vf), _f(cf), stride,
                                  nsteps, _f(qdd), _f(cs))
         return qf, vf, qdd, cs
+
+    def set_heightfield(self, hf=None):
+        """The terrain the following host rollouts pass to the reference's
+        contact kernel (None: the flat plane)."""
+        if hf is None:
+            self.lib.phyzref_set_heightfield(0, 0, 0.0, 0.0, 0.0, 1.0, None)
+            return
+        h = np.ascontiguousarray(hf.heights, np.float32).reshape(-1)
+        self.lib.phyzref_set_heightfield(hf.nx, hf.ny, *[float(x) for x in hf.origin], float(hf.cell), _f(h))
 
     def rollout_impulse(self, model, q, v, ctrl, nsteps=1, schedule=False, contact=(0.0, 0.0), sweeps=16,
                         pd=None, targets=None, state=None, nthreads=1):

@@ -117,6 +117,35 @@ int oracle_energy(const phyzb_model* fm, int64_t nworld, const double* q, const 
 }
 
 // Penalty contact forces only: ext = nworld x nb x 6, cstate = nworld x nb x 8.
+// The heightfield the following contact rollouts sample (nx == 0: none, the
+// flat plane at their ground height). Test-only process state.
+static Terrain g_terrain;
+
+int oracle_set_heightfield(int32_t nx, int32_t ny, double ox, double oy, double oz, double cell,
+                           const float* heights) {
+    g_terrain = Terrain{};
+    if (nx > 0) {
+        g_terrain.nx = nx;
+        g_terrain.ny = ny;
+        g_terrain.ox = ox;
+        g_terrain.oy = oy;
+        g_terrain.oz = oz;
+        g_terrain.cell = cell;
+        g_terrain.h.assign(heights, heights + (size_t)nx * ny);
+    }
+    return 0;
+}
+
+// Height and unit normal of the current terrain at world (x, y).
+double oracle_terrain_at(double x, double y, double* n_out) {
+    Vec3 n;
+    const double h = g_terrain.sample(x, y, n);
+    n_out[0] = n.x;
+    n_out[1] = n.y;
+    n_out[2] = n.z;
+    return h;
+}
+
 int oracle_penalty_contact(const phyzb_model* fm, int64_t nworld, const double* q,
                            const double* v, double ground_height, double friction,
                            const double* k, const double* d, double* ext_out,
@@ -128,6 +157,7 @@ int oracle_penalty_contact(const phyzb_model* fm, int64_t nworld, const double* 
     cp.friction = friction;
     cp.k.assign(k, k + nb);
     cp.d.assign(d, d + nb);
+    cp.terrain = g_terrain;
     for (int64_t w = 0; w < nworld; w++) {
         std::vector<SVec> ext;
         penalty_contact(m, cp, q + w * m.nq, v + w * m.nv, ext,
@@ -165,6 +195,7 @@ int oracle_rollout(const phyzb_model* fm, int64_t nworld, double* q, double* v,
         cp.friction = friction;
         cp.k.assign(k, k + nb);
         cp.d.assign(d, d + nb);
+        cp.terrain = g_terrain;
     }
     std::vector<PdEntry> pd;
     for (int i = 0; i < npd; i++)
@@ -216,6 +247,7 @@ int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, dou
     cp.mid = params[9];
     cp.power = params[10];
     cp.sweeps = sweeps;
+    cp.terrain = g_terrain;
     std::vector<PdEntry> pd;
     for (int i = 0; i < npd; i++)
         pd.push_back(PdEntry{pd_idx[2 * i], pd_idx[2 * i + 1], pd_gains[3 * i], pd_gains[3 * i + 1],

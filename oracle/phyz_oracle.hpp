@@ -830,9 +830,56 @@ inline double potential_energy(const Model& m, const double* q) {
 
 // ── penalty ground contact: the GPU law in f64 ───────────────────────────
 
+// Terrain: the flat plane at `ground` or, with nx > 0, a heightfield of
+// f32 node heights (phyz-model/src/heightfield.rs:10-37) sampled as the
+// GPU samples it (phyz_kernels.cu:625-664).
+struct Terrain {
+    double ground = 0;
+    int nx = 0, ny = 0;
+    double ox = 0, oy = 0, oz = 0, cell = 1;
+    std::vector<float> h;  // [ny][nx]
+    double node(int ix, int iy) const { return oz + (double)h[(size_t)iy * nx + ix]; }
+    void locate(double w, double o, int n, int& i, double& t) const {
+        if (n < 2) {
+            i = 0;
+            t = 0.0;
+            return;
+        }
+        double u = std::fmin(std::fmax((w - o) / cell, 0.0), (double)(n - 1));
+        int ii = (int)u;
+        if (ii > n - 2) ii = n - 2;
+        i = ii;
+        t = u - ii;
+    }
+    // height at world (px, py); unit normal out
+    double sample(double px, double py, Vec3& n_out) const {
+        if (nx == 0) {
+            n_out = v3(0, 0, 1);
+            return ground;
+        }
+        int ix, iy;
+        double tx, ty;
+        locate(px, ox, nx, ix, tx);
+        locate(py, oy, ny, iy, ty);
+        int ix1 = ix + 1 < nx - 1 ? ix + 1 : nx - 1;
+        int iy1 = iy + 1 < ny - 1 ? iy + 1 : ny - 1;
+        double h00 = node(ix, iy), h10 = node(ix1, iy), h01 = node(ix, iy1), h11 = node(ix1, iy1);
+        double h = (h00 * (1.0 - tx) + h10 * tx) * (1.0 - ty) + (h01 * (1.0 - tx) + h11 * tx) * ty;
+        double dhdx = 0.0, dhdy = 0.0;
+        double span_x = (nx - 1) * cell, span_y = (ny - 1) * cell;
+        if (nx >= 2 && px >= ox && px <= ox + span_x) dhdx = ((h10 - h00) * (1.0 - ty) + (h11 - h01) * ty) / cell;
+        if (ny >= 2 && py >= oy && py <= oy + span_y) dhdy = ((h01 - h00) * (1.0 - tx) + (h11 - h10) * tx) / cell;
+        Vec3 n = v3(-dhdx, -dhdy, 1.0);
+        double l = norm(n);
+        n_out = l > 0.0 ? n * (1.0 / l) : n;
+        return h;
+    }
+};
+
 struct ContactParams {
     double ground_height = 0, friction = 0;
     std::vector<double> k, d;  // per body gains (layout.rs:272-278)
+    Terrain terrain;           // terrain.ground mirrors ground_height
 };
 
 inline double fsign(double x) { return x > 0 ? 1.0 : (x < 0 ? -1.0 : 0.0); }
@@ -943,8 +990,9 @@ inline void penalty_contact(const Model& m, const ContactParams& cp, const doubl
         for (int c = 0; c < npts; c++) {
             Vec3 sup = b.geom.type == 2 ? box_corner(b.geom, c) : support_point(b.geom, z_body);
             Vec3 sup_w = wpos[i] + mul(wrot[i], sup);
-            Vec3 n_w = v3(0, 0, 1);
-            double terr_h = cp.ground_height;
+            Vec3 n_w;
+            double terr_h = cp.terrain.nx > 0 ? cp.terrain.sample(sup_w.x, sup_w.y, n_w)
+                                              : (n_w = v3(0, 0, 1), cp.ground_height);
             double pen = n_w.z * (terr_h - sup_w.z);
             if (!(pen > 0.0)) continue;
             Vec3 n_body = tmul(wrot[i], n_w);
@@ -991,6 +1039,7 @@ inline void penalty_contact(const Model& m, const ContactParams& cp, const doubl
 // (cuda/mod.rs:680-701) over GroundContactParams::default
 // (contact_pipeline.rs:199-218).
 struct ImpulseParams {
+    Terrain terrain;  // nx == 0: the flat plane at ground_height
     double ground_height = 0, friction = 0;
     double restitution = 0, restitution_threshold = 0.05;
     double erp = 0;  // solref_erp_from(0.02, 1.0, dt)
@@ -1104,9 +1153,16 @@ inline void impulse_contact(const Model& m, const ImpulseParams& cp, const doubl
         auto point = [&](int c) { return b.geom.type == 2 ? box_corner(b.geom, c) : support_point(b.geom, z_body); };
         // within-body load sharing: points inside the margin
         int n_active = 0;
+        auto terrain = [&](const Vec3& w, Vec3& n) {
+            if (cp.terrain.nx > 0) return cp.terrain.sample(w.x, w.y, n);
+            n = v3(0, 0, 1);
+            return cp.ground_height;
+        };
         for (int c = 0; c < npts; c++) {
             Vec3 sw = wpos[i] + mul(wrot[i], point(c));
-            if (cp.ground_height - sw.z > -cp.margin) n_active++;
+            Vec3 tn;
+            double th = terrain(sw, tn);
+            if (tn.z * (th - sw.z) > -cp.margin) n_active++;
         }
         if (n_active < 1) n_active = 1;
         Vec3 f_w_total{};
@@ -1117,12 +1173,14 @@ inline void impulse_contact(const Model& m, const ImpulseParams& cp, const doubl
             double* f_c = slots + 3 * c;
             Vec3 sup = point(c);
             Vec3 sup_w = wpos[i] + mul(wrot[i], sup);
-            double pen = cp.ground_height - sup_w.z;
+            Vec3 n_w;
+            double terr_h = terrain(sup_w, n_w);
+            double pen = n_w.z * (terr_h - sup_w.z);
             if (!(pen > -cp.margin)) {
                 f_c[0] = f_c[1] = f_c[2] = 0.0;
                 continue;
             }
-            Vec3 n_body = z_body;
+            Vec3 n_body = tmul(wrot[i], n_w);
             Vec3 v_point = vel[i].lin + cross(vel[i].ang, sup);
             Vec3 t_u, t_w;
             contact_tangents(n_body, t_u, t_w);

@@ -100,6 +100,27 @@ int phyzref_pack_geometries(const phyzb_model* m, const double* k, const double*
     return collidable;
 }
 
+// The heightfield the following rollouts pass to the contact kernel
+// (contact_pipeline.rs:79-84 header fields, node buffer as the reference
+// uploads it); nx == 0: none. Test-only process state.
+static uint32_t g_hf_nx = 0, g_hf_ny = 0;
+static float g_hf_o[3] = {0, 0, 0}, g_hf_cell = 1.0f;
+static std::vector<float> g_hf(1, 0.0f);
+
+void phyzref_set_heightfield(uint32_t nx, uint32_t ny, float ox, float oy, float oz, float cell,
+                             const float* heights) {
+    g_hf_nx = nx;
+    g_hf_ny = ny;
+    g_hf_o[0] = ox;
+    g_hf_o[1] = oy;
+    g_hf_o[2] = oz;
+    g_hf_cell = nx ? cell : 1.0f;
+    if (nx)
+        g_hf.assign(heights, heights + (size_t)nx * ny);
+    else
+        g_hf.assign(1, 0.0f);
+}
+
 // contact_pipeline.rs:60-98 ContactParams::pack (penalty, flat ground, no plane)
 void phyzref_pack_cparams(uint32_t nworld, uint32_t nb, uint32_t nv, float ground, float dt,
                           float friction, float* out) {
@@ -112,6 +133,17 @@ void phyzref_pack_cparams(uint32_t nworld, uint32_t nb, uint32_t nv, float groun
     out[5] = friction;
     out[6] = bits_i(-1);
     out[16] = 1.0f;  // hf_cell default
+}
+
+// The host rollouts' header of the heightfield set by phyzref_set_heightfield
+// (ContactParams::set_heightfield, contact_pipeline.rs:101-108).
+static void apply_heightfield(float* cp) {
+    cp[11] = bits_u(g_hf_nx);
+    cp[12] = bits_u(g_hf_ny);
+    cp[13] = g_hf_o[0];
+    cp[14] = g_hf_o[1];
+    cp[15] = g_hf_o[2];
+    cp[16] = g_hf_cell;
 }
 
 // n steps of the reference sequence over nworld worlds (AoS f32, as
@@ -133,7 +165,7 @@ int phyzref_rollout(int nthreads, uint32_t nworld, uint32_t nv, uint32_t nb, flo
         std::vector<float> qdd((size_t)n * nv, 0.0f), c((size_t)n * nv, 0.0f);
         float cp[CP_STRIDE];
         phyzref_pack_cparams(n, nb, nv, ground, dt, friction, cp);
-        float hf = 0.0f;
+        apply_heightfield(cp);
         float* qa = q + (size_t)a * nv;
         float* va = v + (size_t)a * nv;
         for (int s = 0; s < nsteps; s++) {
@@ -143,7 +175,7 @@ int phyzref_rollout(int nthreads, uint32_t nworld, uint32_t nv, uint32_t nb, flo
                 phyz_host_pd(n * npd, n, nv, nv, npd, pd_table, qa, va, targets + (size_t)a * npd,
                              c.data());
             if (geometry)
-                phyz_host_contact(n, cp, bodies, geometry, qa, va, ext.data(), cs.data(), &hf,
+                phyz_host_contact(n, cp, bodies, geometry, qa, va, ext.data(), cs.data(), g_hf.data(),
                                   qdd.data());
             phyz_host_aba(n, n, nv, dt, nb, gx, gy, gz, bodies, qa, va, c.data(), qdd.data(),
                           ext.data());
@@ -192,13 +224,13 @@ int phyzref_rollout_impulse(int nthreads, uint32_t nworld, uint32_t nv, uint32_t
         std::vector<float> qdd((size_t)n * nv, 0.0f), c((size_t)n * nv, 0.0f);
         float cp[CP_STRIDE];
         phyzref_pack_cparams(n, nb, nv, ground, dt, friction, cp);
+        apply_heightfield(cp);
         cp[17] = bits_u(1u);  // solve_mode: impulse
         cp[19] = imp[2];      // restitution
         cp[20] = imp[3];      // restitution_threshold
         cp[21] = imp[0];      // solref_erp
         cp[22] = imp[1];      // margin
         for (int k = 0; k < 5; k++) cp[23 + k] = imp[4 + k];  // solimp dmin, dmax, width, mid, power
-        float hf = 0.0f;
         float* qa = q + (size_t)a * nv;
         float* va = v + (size_t)a * nv;
         for (int s = 0; s < nsteps; s++) {
@@ -209,7 +241,7 @@ int phyzref_rollout_impulse(int nthreads, uint32_t nworld, uint32_t nv, uint32_t
                              c.data());
             phyz_host_aba(n, n, nv, dt, nb, gx, gy, gz, bodies, qa, va, c.data(), qdd.data(), ext);
             for (int k = 0; k < sweeps; k++) {
-                phyz_host_contact(n, cp, bodies, geometry, qa, va, ext, cs, &hf, qdd.data());
+                phyz_host_contact(n, cp, bodies, geometry, qa, va, ext, cs, g_hf.data(), qdd.data());
                 phyz_host_aba(n, n, nv, dt, nb, gx, gy, gz, bodies, qa, va, c.data(), qdd.data(), ext);
             }
             phyz_host_integrate(n * nb, n, nv, dt, nb, qa, va, qdd.data(), bodies);

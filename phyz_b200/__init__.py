@@ -3,7 +3,7 @@ batched-simulation API (BatchSim) over the C ABI of libphyzb200.so."""
 from ._lib import PhyzbError
 from .batch_sim import BatchSim, BodyContactGains, PdDof
 from .policy import ObsOp, PolicySpec
-from .model import Geometry, Joint, Model, ModelBuilder, SpatialInertia, Transform
+from .model import Geometry, Heightfield, Joint, Model, ModelBuilder, SpatialInertia, Transform
 
-__all__ = ["BatchSim", "BodyContactGains", "PdDof", "PhyzbError", "ObsOp", "PolicySpec", "Geometry", "Joint", "Model",
+__all__ = ["BatchSim", "BodyContactGains", "PdDof", "PhyzbError", "ObsOp", "PolicySpec", "Geometry", "Heightfield", "Joint", "Model",
            "ModelBuilder", "SpatialInertia", "Transform"]

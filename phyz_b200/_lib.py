@@ -73,6 +73,16 @@ class PhyzbModel(C.Structure):
     ]
 
 
+class PhyzbHeightfield(C.Structure):
+    _fields_ = [("origin", C.c_double * 3), ("cell", C.c_double), ("nx", C.c_int32), ("ny", C.c_int32),
+                ("heights", C.POINTER(C.c_float))]
+
+
+class PhyzbBodyPlane(C.Structure):
+    _fields_ = [("body", C.c_int32), ("offset", C.c_double), ("max_depth", C.c_double), ("half_x", C.c_double),
+                ("half_y", C.c_double), ("exclude", C.POINTER(C.c_int32)), ("n_exclude", C.c_int32)]
+
+
 class PhyzbPdDof(C.Structure):
     _fields_ = [
         ("q_index", C.c_int32),
@@ -166,7 +176,9 @@ SIGNATURES = {
     "phyzb_set_model": (C.c_int, [_P, C.POINTER(PhyzbModel)]),
     "phyzb_enable_ground_contact": (C.c_int, [_P, C.c_double, C.c_double, C.c_double, C.c_double, _I32P]),
     "phyzb_enable_ground_contact_per_body": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _I32P]),
-    "phyzb_enable_contact_impulse": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _I32P]),
+    "phyzb_enable_contact_impulse": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _P, _P, _I32P]),
+    "phyzb_enable_contact_terrain": (C.c_int, [_P, C.c_double, C.c_double, _D, _D, _P, _P, _I32P]),
+    "phyzb_set_heightfield": (C.c_int, [_P, _P]),
     "phyzb_set_contact_sweeps": (C.c_int, [_P, C.c_int32]),
     "phyzb_disable_contact": (C.c_int, [_P]),
     "phyzb_collidable_bodies": (C.c_int, [_P]),

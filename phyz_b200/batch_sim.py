@@ -134,21 +134,58 @@ class BatchSim:
                                                              C.byref(n)))
         return n.value
 
-    def enable_contact_impulse(self, ground_height: float, friction: float, gains=None) -> int:
+    def _gains(self, gains):
+        if gains is None:
+            return None, None
+        k = np.ascontiguousarray([g.stiffness for g in gains], np.float64)
+        d = np.ascontiguousarray([g.damping for g in gains], np.float64)
+        if k.size != self.nb:
+            raise PhyzbError(_lib.ERR_INVALID, f"need {self.nb} body gains, got {k.size}")
+        return k, d
+
+    @staticmethod
+    def _plane(plane):
+        if plane is None:
+            return None, None
+        ex = np.ascontiguousarray(list(plane.exclude), np.int32)
+        c = _lib.PhyzbBodyPlane(int(plane.body), float(plane.offset), float(plane.max_depth), float(plane.half_x),
+                                float(plane.half_y), ex.ctypes.data_as(C.POINTER(C.c_int32)), int(ex.size))
+        return c, ex
+
+    def enable_contact_terrain(self, ground_height: float, friction: float, gains, plane=None,
+                               heightfield=None) -> int:
+        """Penalty contact with per-body gains against a heightfield
+        (cuda/mod.rs:656-676; `ground_height` is ignored while one is
+        loaded) and an optional body-attached plane."""
+        k, d = self._gains(gains)
+        pc, keep_p = self._plane(plane)
+        hc, keep_h = heightfield.to_c() if heightfield is not None else (None, None)
+        n = C.c_int32()
+        check(self._lib.phyzb_enable_contact_terrain(self._h, ground_height, friction, dptr(k), dptr(d),
+                                                     C.byref(pc) if pc is not None else None,
+                                                     C.byref(hc) if hc is not None else None, C.byref(n)))
+        return n.value
+
+    def set_heightfield(self, heightfield) -> None:
+        """Replace the terrain in place (cuda/mod.rs:741-759)."""
+        hc, keep = heightfield.to_c()
+        check(self._lib.phyzb_set_heightfield(self._h, C.byref(hc)))
+
+    def enable_contact_impulse(self, ground_height: float, friction: float, gains=None, plane=None,
+                               heightfield=None) -> int:
         """Contact as the velocity-level impulse solve (cuda/mod.rs:680-701):
         `contact_sweeps` staged Coulomb updates per step, warm-started from
         the previous step. `gains` (BodyContactGains per body) only matter to
         a later penalty enable."""
-        k = d = None
-        if gains is not None:
-            k = np.ascontiguousarray([g.stiffness for g in gains], np.float64)
-            d = np.ascontiguousarray([g.damping for g in gains], np.float64)
-            if k.size != self.nb:
-                raise PhyzbError(_lib.ERR_INVALID, f"need {self.nb} body gains, got {k.size}")
+        k, d = self._gains(gains)
+        pc, keep_p = self._plane(plane)
+        hc, keep_h = heightfield.to_c() if heightfield is not None else (None, None)
         n = C.c_int32()
         check(self._lib.phyzb_enable_contact_impulse(self._h, ground_height, friction,
                                                      dptr(k) if k is not None else None,
-                                                     dptr(d) if d is not None else None, C.byref(n)))
+                                                     dptr(d) if d is not None else None,
+                                                     C.byref(pc) if pc is not None else None,
+                                                     C.byref(hc) if hc is not None else None, C.byref(n)))
         return n.value
 
     @property

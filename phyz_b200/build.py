@@ -25,9 +25,9 @@ OBJ = PKG / "_build"
 SOURCES = ["stepper.cu", "capi.cu", "capi_policy.cu", "capi_train.cu", "policy.cu", "train.cu", "flops.cpp",
            "peaks.cu", "capi_noalloc.cu"]
 VARIANT_SOURCE = "rollout_variants.cu"
-FEAT_COUNT = 32  # pz_variants.h; bit 8 only with bit 4, bit 16 only with bit 2 (feat_valid)
+FEAT_COUNT = 64  # pz_variants.h; bit 8 only with bit 4, bits 16 and 32 only with bit 2 (feat_valid)
 VARIANTS = [(t, f) for t in ("float", "double") for f in range(FEAT_COUNT)
-            if not (f & 8 and not f & 4) and not (f & 16 and not f & 2)]
+            if not (f & 8 and not f & 4) and not (f & 16 and not f & 2) and not (f & 32 and not f & 2)]
 HEADERS = ["pz_types.cuh", "pz_model.cuh", "pz_world.cuh", "pz_launch.h", "pz_pack.h", "pz_variants.h",
            "stepper_kernels.cuh", "pz_policy.h", "capi_internal.h", "pz_mlp.cuh", "pz_train.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -150,6 +150,13 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     a.si_width = 0.001;
     a.si_mid = 0.5;
     a.si_power = 2.0;
+    a.hf = (const float*)s->hf;
+    a.hf_nx = s->cfg.terrain ? s->hf_nx : 0;
+    a.hf_ny = s->cfg.terrain ? s->hf_ny : 0;
+    a.hf_ox = s->hf_o[0];
+    a.hf_oy = s->hf_o[1];
+    a.hf_oz = s->hf_o[2];
+    a.hf_cell = s->hf_cell;
     return a;
 }
 
@@ -233,7 +240,37 @@ int reset_impulse_state(phyzb_sim* s) {
     return PHYZB_OK;
 }
 
-int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d, bool impulse) {
+// contact_pipeline.rs:651-672 validate_heightfield (plus finite values)
+int check_heightfield(const phyzb_heightfield* hf) {
+    if (hf->nx < 1 || hf->ny < 1) return fail(PHYZB_ERR_INVALID, "heightfield needs at least one node per axis");
+    if (!hf->heights) return fail(PHYZB_ERR_INVALID, "heightfield heights are null");
+    if (!(std::isfinite(hf->cell) && hf->cell > 0.0))
+        return fail(PHYZB_ERR_INVALID, "heightfield cell must be positive, got " + std::to_string(hf->cell));
+    for (int k = 0; k < 3; k++)
+        if (!std::isfinite(hf->origin[k])) return fail(PHYZB_ERR_INVALID, "heightfield origin must be finite");
+    const size_t n = (size_t)hf->nx * hf->ny;
+    for (size_t i = 0; i < n; i++)
+        if (!std::isfinite(hf->heights[i])) return fail(PHYZB_ERR_INVALID, "heightfield heights must be finite");
+    return PHYZB_OK;
+}
+
+// Heightfield nodes into the device buffer (already large enough) and the
+// grid header into the simulator; kernels already queued finish first.
+int upload_heightfield(phyzb_sim* s, const phyzb_heightfield* hf) {
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_CUDA(cudaMemcpy(s->hf, hf->heights, (size_t)hf->nx * hf->ny * sizeof(float), cudaMemcpyHostToDevice));
+    s->hf_nx = hf->nx;
+    s->hf_ny = hf->ny;
+    for (int k = 0; k < 3; k++) s->hf_o[k] = hf->origin[k];
+    s->hf_cell = hf->cell;
+    return PHYZB_OK;
+}
+
+int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d, bool impulse,
+                const phyzb_body_plane* plane = nullptr, const phyzb_heightfield* hf = nullptr) {
+    if (plane)
+        return fail(PHYZB_ERR_UNSUPPORTED, "a body-attached contact plane is not available in this build");
+    if (hf) PZ_TRY(check_heightfield(hf));
     int collidable = 0;
     for (int i = 0; i < s->nb; i++)
         if (s->bodies[i].geom_type != PHYZB_GEOM_NONE) collidable++;
@@ -255,8 +292,18 @@ int set_contact(phyzb_sim* s, double ground, double friction, const double* k, c
         PZ_CUDA(cudaMalloc(&s->cstate, bytes > 0 ? bytes : 16));
         PZ_CUDA(cudaMemsetAsync(s->cstate, 0, bytes, s->stream));
     }
+    // the node buffer is sized to this first field (1 node without one)
+    const size_t nodes = hf ? (size_t)hf->nx * hf->ny : 1;
+    if (nodes > s->hf_cap) {
+        free_ptr(s->hf);
+        s->hf_cap = 0;
+        PZ_CUDA(cudaMalloc(&s->hf, nodes * sizeof(float)));
+        s->hf_cap = nodes;
+    }
+    if (hf) PZ_TRY(upload_heightfield(s, hf));
     s->cfg.contact = true;
     s->cfg.impulse = impulse;
+    s->cfg.terrain = hf != nullptr;
     s->cfg.gk.assign(k, k + s->nb);
     s->cfg.gd.assign(d, d + s->nb);
     s->ground_h = ground;
@@ -303,6 +350,7 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(s->targets);
     free_ptr(s->cstate);
     free_ptr(s->imp);
+    free_ptr(s->hf);
     void* st = s->status;
     free_ptr(st);
     free_ptr(s->lay[0].blob);
@@ -448,8 +496,40 @@ int phyzb_enable_ground_contact_per_body(phyzb_sim* s, double ground_height, dou
     return PHYZB_OK;
 }
 
+int phyzb_enable_contact_terrain(phyzb_sim* s, double ground_height, double friction, const double* stiffness,
+                                 const double* damping, const phyzb_body_plane* plane, const phyzb_heightfield* hf,
+                                 int32_t* collidable_out) {
+    PZ_TRY(check_sim(s));
+    if (!stiffness || !damping) return fail(PHYZB_ERR_INVALID, "per-body gains are null");
+    DeviceGuard g(s->device);
+    PZ_TRY(set_contact(s, ground_height, friction, stiffness, damping, false, plane, hf));
+    if (collidable_out) *collidable_out = s->collidable;
+    return PHYZB_OK;
+}
+
+int phyzb_set_heightfield(phyzb_sim* s, const phyzb_heightfield* hf) {
+    PZ_TRY(check_sim(s));
+    if (!hf) return fail(PHYZB_ERR_INVALID, "heightfield is null");
+    if (!s->cfg.contact)
+        return fail(PHYZB_ERR_STATE, "contact not enabled — call enable_contact_terrain first");
+    PZ_TRY(check_heightfield(hf));
+    const size_t nodes = (size_t)hf->nx * hf->ny;
+    if (nodes > s->hf_cap)
+        return fail(PHYZB_ERR_INVALID, "heightfield has " + std::to_string(nodes) +
+                                           " nodes but the buffer was sized for " + std::to_string(s->hf_cap) +
+                                           "; enable contact with the largest grid first");
+    DeviceGuard g(s->device);
+    PZ_TRY(upload_heightfield(s, hf));
+    if (!s->cfg.terrain) {  // the kernel variant changes
+        s->cfg.terrain = true;
+        PZ_TRY(repack(s));
+    }
+    return PHYZB_OK;
+}
+
 int phyzb_enable_contact_impulse(phyzb_sim* s, double ground_height, double friction, const double* stiffness,
-                                 const double* damping, int32_t* collidable_out) {
+                                 const double* damping, const phyzb_body_plane* plane, const phyzb_heightfield* hf,
+                                 int32_t* collidable_out) {
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
     // the per-body gains only enter the penalty law; they are kept (and
@@ -457,7 +537,7 @@ int phyzb_enable_contact_impulse(phyzb_sim* s, double ground_height, double fric
     std::vector<double> k(s->nb, 0.0), d(s->nb, 0.0);
     if (stiffness) k.assign(stiffness, stiffness + s->nb);
     if (damping) d.assign(damping, damping + s->nb);
-    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data(), true));
+    PZ_TRY(set_contact(s, ground_height, friction, k.data(), d.data(), true, plane, hf));
     if (collidable_out) *collidable_out = s->collidable;
     return PHYZB_OK;
 }
@@ -476,6 +556,7 @@ int phyzb_disable_contact(phyzb_sim* s) {
     DeviceGuard g(s->device);
     s->cfg.contact = false;
     s->cfg.impulse = false;
+    s->cfg.terrain = false;
     return repack(s);
 }
 

@@ -99,6 +99,10 @@ struct phyzb_sim {
     size_t imp_bytes = 0;
     int sweeps = 16;          // impulse mode: contact sweeps per step (DEFAULT_CONTACT_SWEEPS)
     double erp = 0.0;         // impulse mode: solref error reduction at this dt
+    void* hf = nullptr;       // heightfield nodes (f32), capacity hf_cap nodes
+    size_t hf_cap = 0;
+    int hf_nx = 0, hf_ny = 0;
+    double hf_o[3] = {0, 0, 0}, hf_cell = 1.0;
     int* status = nullptr;
     // lay[0]: every record in shared memory (the objective kernel's layout
     // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the

@@ -68,6 +68,7 @@ inline Cnt pz_pow(Cnt x, Cnt y) {
     return Cnt(std::pow(x.v, y.v));
 }
 inline Cnt pz_abs(Cnt x) { return Cnt(std::fabs(x.v)); }
+inline int pz_trunc_int(Cnt x) { return (int)x.v; }
 inline Cnt pz_min(Cnt a, Cnt b) { return Cnt(std::fmin(a.v, b.v)); }
 inline Cnt pz_max(Cnt a, Cnt b) { return Cnt(std::fmax(a.v, b.v)); }
 
@@ -158,6 +159,10 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     M.kstiff_c = Cnt(4.0 / (dtc * dtc));
     M.im = ImpMat<Cnt>{M.ground_h, M.friction, M.dt, Cnt(0.0), Cnt(0.001), Cnt(0.0), Cnt(0.05),
                        Cnt(0.9),   Cnt(0.95),  Cnt(0.001), Cnt(0.5), Cnt(2.0)};
+    // a 2 x 2 heightfield far below: terrain sampling is counted like
+    // detection, the force law is not
+    static const float hf_nodes[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    M.ter = Terrain<Cnt>{hf_nodes, 2, 2, Cnt(-1.0), Cnt(-1.0), Cnt(-1e9), Cnt(1.0)};
 
     std::vector<Cnt> scratch(info.scratch > 0 ? info.scratch : 1, Cnt(0.0));
     HostScr S{scratch.data()};
@@ -169,10 +174,32 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     std::vector<Cnt> ctrl(nv > 0 ? nv : 1, Cnt(0.5)), targets(npd > 0 ? npd : 1, Cnt(0.0));
     const WorldIO<Cnt> io{ctrl.data(), 0, targets.data(), 1, 0};
     const Out<Cnt> none{nullptr, 0};
-    for (int i = 0; i < nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
+    for (int i = 0; i < nb; i++) {
+        if (cfg.contact && cfg.impulse)
+            prefetch_controls<true>(M, M.bi[i], S, io, 0);
+        else
+            prefetch_controls<false>(M, M.bi[i], S, io, 0);
+    }
     constexpr int ALL = FEAT_MULTI | FEAT_CONTACT;  // runtime flags select the paths taken
     constexpr int ALLI = ALL | FEAT_IMPULSE;
-    if (cfg.contact && cfg.impulse) {
+    if (cfg.contact && cfg.terrain) {
+        constexpr int AT = ALL | FEAT_TERRAIN, ATI = ALLI | FEAT_TERRAIN;
+        if (cfg.impulse) {
+            pass1_all<ATI>(M, S);
+            g_tally = Tally{};
+            pass2<ATI>(M, S);
+            for (int k = 0; k < sweeps; k++) {
+                sweep_forward<ATI>(M, S);
+                pass2<ATI>(M, S);
+            }
+            pass3_next<ATI, false>(M, S, io, 1, none);
+        } else {
+            pass1_all<AT>(M, S);
+            g_tally = Tally{};
+            pass2<AT>(M, S);
+            pass3_next<AT, false>(M, S, io, 1, none);
+        }
+    } else if (cfg.contact && cfg.impulse) {
         pass1_all<ALLI>(M, S);
         // steady state: the leading backward sweep, `sweeps` x [forward
         // sweep with contact, backward sweep], the fused finish/start sweep

@@ -41,6 +41,10 @@ struct RolloutArgs {
     int sweeps;            // [contact, backward sweep] pairs per step
     double erp, margin, restitution, rest_thr;
     double si_dmin, si_dmax, si_width, si_mid, si_power;
+    // heightfield terrain (feat bit 32): f32 nodes [ny][nx] on the device
+    const float* hf;
+    int hf_nx, hf_ny;
+    double hf_ox, hf_oy, hf_oz, hf_cell;
 };
 
 // tmem_cols > 0: configure the Tensor-Memory variant for a layout whose

@@ -68,12 +68,14 @@ struct alignas(16) BodyI {
     int s_acc;        // branch: accumulated child inertia (21) + bias force (6)
     int s_vold;       // branch: velocity of the step being finished (6)
     int s_acca;       // branch: acceleration (6)
-    int s_wx;         // branch: world frame for contact (up 3, height 1)
+    int s_wx;         // branch: world frame for contact (up 3, height 1; with a heightfield
+                      // rows r0, r1, up and the origin: 12)
     int gtype;        // geometry code (0 none)
     int t_rec;        // Tensor Memory column of the body's record [c, s, v|W] (-1: in s_xj/s_vw)
     int qshift;       // F_ZHINGE: parent->child relabelling (Q v)_a = v_(a+qshift mod 3)
     // impulse-mode contact (-1 otherwise)
-    int s_up;         // collidable: world up in the body frame (3) and origin height (1)
+    int s_up;         // collidable: world up in the body frame (3) and origin height (1); with
+                      // a heightfield the frame of s_wx (12)
     int s_imp;        // collidable: staged impulses [normal, tangent u, tangent w] per point
     int s_vf;         // branch: free velocity v + dt qdd of the sweep (6)
     int c_imp;        // collidable: first row of the body's wrench (6) + impulses in the
@@ -85,6 +87,17 @@ template <class T>
 struct alignas(16) PdT {
     T kp, kd, maxf;
     int qi, vi;
+};
+
+// Heightfield terrain (phyz-model/src/heightfield.rs:10-37; the GPU's
+// sampling, phyz_kernels.cu:625-664): node (ix, iy) at world
+// (ox + ix cell, oy + iy cell) with height oz + h[iy * nx + ix], f32 nodes
+// as the reference stores them.
+template <class T>
+struct Terrain {
+    const float* h;
+    int nx, ny;
+    T ox, oy, oz, cell;
 };
 
 // Impulse-mode contact material (contact_pipeline.rs:85-95): ground height,
@@ -110,6 +123,7 @@ struct ModelView {
     T inv_dt_c;            // 1 / max(dt, 1e-9)   (phyz_kernels.cu:574-578)
     T kstiff_c;            // 4 / max(dt, 1e-9)^2
     ImpMat<T> im;          // impulse-mode contact material
+    Terrain<T> ter;        // heightfield (feature bit 32)
 };
 
 }  // namespace pz

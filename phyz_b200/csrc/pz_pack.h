@@ -74,7 +74,8 @@ struct PackInfo {
     int scratch = 0;     // scratch slots per world
     int collidable = 0;  // bodies with a contact shape
     int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges,
-                         // 8 = (with 4) every relabel is the shift-1 cycle, 16 = (with 2) impulse contact
+                         // 8 = (with 4) every relabel is the shift-1 cycle, 16 = (with 2) impulse contact,
+                         // 32 = (with 2) heightfield terrain
     int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
     int imp_slots = 0;   // impulse mode: rows per world of the persistent wrench + impulse buffer
 };
@@ -85,6 +86,7 @@ inline int pad16(int b) { return (b + 15) & ~15; }
 struct PackCfg {
     bool contact = false;
     bool impulse = false;                // contact as the velocity-level impulse solve
+    bool terrain = false;                // contact against a heightfield (full world frames)
     std::vector<double> gk, gd;          // per-body penalty gains (contact)
     std::vector<phyzb_pd_dof> pd;        // PD servos
 };
@@ -314,7 +316,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             if (impulse) {
                 const int npts = b.geom_type == 2 ? 8 : 1;
                 d.s_up = next;
-                next += 4;
+                next += cfg.terrain ? 12 : 4;
                 d.s_imp = next;
                 next += 3 * npts;
                 d.c_imp = info.imp_slots;
@@ -330,8 +332,8 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.s_acca = next;
             next += 6;
             if (cfg.contact) {
-                d.s_wx = next;  // world up (3) and origin height (1)
-                next += 4;
+                d.s_wx = next;  // world up (3) and origin height (1), or the full frame (12)
+                next += cfg.terrain ? 12 : 4;
             }
             if (impulse) {
                 d.s_vf = next;
@@ -357,6 +359,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         if (m->bodies[i].joint_type == J_BALL || m->bodies[i].joint_type == J_FREE) info.feat |= 1;
     if (cfg.contact) info.feat |= 2;
     if (cfg.contact && cfg.impulse) info.feat |= 16;
+    if (cfg.contact && cfg.terrain) info.feat |= 32;
     bool all_one = true;
     for (int i = 0; i < nb; i++)
         if (bi[i].flags & F_ZHINGE) {

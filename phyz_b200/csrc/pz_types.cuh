@@ -50,6 +50,8 @@ __device__ __forceinline__ float pz_max(float a, float b) { return fmaxf(a, b); 
 __device__ __forceinline__ double pz_max(double a, double b) { return fmax(a, b); }
 __device__ __forceinline__ bool pz_finite(float x) { return isfinite(x); }
 __device__ __forceinline__ bool pz_finite(double x) { return isfinite(x); }
+__device__ __forceinline__ int pz_trunc_int(float x) { return (int)x; }
+__device__ __forceinline__ int pz_trunc_int(double x) { return (int)x; }
 #endif
 
 // Small-angle threshold of the exp/log maps: f64 uses f64::EPSILON like

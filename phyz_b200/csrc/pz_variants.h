@@ -11,9 +11,11 @@ namespace pz {
 
 // Feature bits of a kernel variant (pz_world.cuh Features): 0 .. FEAT_COUNT-1;
 // the uniform-shift bit (8) only occurs with the relabel bit (4), the
-// impulse bit (16) only with the contact bit (2).
-constexpr int FEAT_COUNT = 32;
-constexpr bool feat_valid(int f) { return !((f & 8) && !(f & 4)) && !((f & 16) && !(f & 2)); }
+// impulse (16) and heightfield (32) bits only with the contact bit (2).
+constexpr int FEAT_COUNT = 64;
+constexpr bool feat_valid(int f) {
+    return !((f & 8) && !(f & 4)) && !((f & 16) && !(f & 2)) && !((f & 32) && !(f & 2));
+}
 
 struct DeviceLimits {
     int sm_count;

@@ -37,8 +37,9 @@ namespace pz {
 // FEAT_PERM) every relabelled hinge relabelled by the same shift 1 -- a chain
 // whose axes cycle x, y, z -- so the relabel is a compile-time register
 // renaming instead of a run-time branch; and (with FEAT_CONTACT) contact as
-// the velocity-level impulse solve instead of the penalty law.
-enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8, FEAT_IMPULSE = 16 };
+// the velocity-level impulse solve instead of the penalty law, and against a
+// heightfield instead of the flat plane (full world frames carried).
+enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8, FEAT_IMPULSE = 16, FEAT_TERRAIN = 32 };
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
@@ -514,11 +515,13 @@ PZ_HD void st_sv(const Scr& S, int s, const SV<T>& v) {
 
 // Generalized input force on DOF d: the control (or the PD servo output,
 // phyz_kernels.cu:464-483) plus the passive terms of joint.rs:232-247.
-template <class T, class Scr>
+// SEP: the control input has slots of its own (impulse mode), else it
+// shares the w0 slots (a compile-time choice: no extra table read).
+template <bool SEP, class T, class Scr>
 PZ_HD T dof_force(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S, int k, bool one_dof) {
     const int d = bi.off + k;
     const T qd = S(M.nv + d);
-    T in = S(bi.s_in + k);
+    T in = S((SEP ? bi.s_in : bi.s_w0) + k);
     if (bi.flags & F_PD) {
         const int pdi = M.pd_of_dof[d];
         if (pdi >= 0) {
@@ -587,7 +590,7 @@ PZ_HD void ai_sub_el(AI<T>& I, int r, int c, const T& v) {  // only r <= c for s
 // U = I S, D = S^T U + d_extra, W = U D^-1, w0 = D^-1 u, stored; when the
 // body has a parent, I <- I - W U^T and p <- p + I c + U w0. Returns false
 // when D is singular (aba.rs:291-294: the body is skipped).
-template <int ND, class T, class Scr>
+template <int ND, bool SEP, class T, class Scr>
 PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S,
                      AI<T>& I, SV<T>& p, const SV<T>& c, bool has_parent) {
     T U[6][ND];
@@ -603,7 +606,7 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
         for (int b = 0; b < ND; b++) L[a][b] = T(0);
     T u[ND];
 #pragma unroll
-    for (int k = 0; k < ND; k++) u[k] = dof_force(M, bi, bt, S, k, false) - svget(p, k);
+    for (int k = 0; k < ND; k++) u[k] = dof_force<SEP>(M, bi, bt, S, k, false) - svget(p, k);
     bool ok = true;
 #pragma unroll
     for (int a = 0; a < ND; a++) {
@@ -753,24 +756,104 @@ struct Out {
     }
 };
 
+// Heightfield sample at world (px, py) (phyz_kernels.cu:625-664): the
+// bilinear height, and the unit normal from the patch's gradient (zero
+// slope outside the grid's span, where the clamp extends the border flat).
+template <class T>
+PZ_HD T terrain_at(const Terrain<T>& t, const T& px, const T& py, V3<T>& n_out) {
+    auto locate = [&](const T& w, const T& o, int n, int& i, T& f) {
+        if (n < 2) {
+            i = 0;
+            f = T(0);
+            return;
+        }
+        const T u = pz_min(pz_max((w - o) / t.cell, T(0)), T(n - 1));
+        int ii = pz_trunc_int(u);  // u >= 0: truncation is the floor
+        if (ii > n - 2) ii = n - 2;
+        i = ii;
+        f = u - T(ii);
+    };
+    if (t.nx < 1 || t.ny < 1) {  // no grid loaded (never launched that way): the plane z = 0
+        n_out = mk3<T>(T(0), T(0), T(1));
+        return T(0);
+    }
+    int ix, iy;
+    T tx, ty;
+    locate(px, t.ox, t.nx, ix, tx);
+    locate(py, t.oy, t.ny, iy, ty);
+    const int ix1 = ix + 1 < t.nx - 1 ? ix + 1 : t.nx - 1;
+    const int iy1 = iy + 1 < t.ny - 1 ? iy + 1 : t.ny - 1;
+    const T h00 = t.oz + T(t.h[iy * t.nx + ix]), h10 = t.oz + T(t.h[iy * t.nx + ix1]);
+    const T h01 = t.oz + T(t.h[iy1 * t.nx + ix]), h11 = t.oz + T(t.h[iy1 * t.nx + ix1]);
+    const T h = (h00 * (T(1) - tx) + h10 * tx) * (T(1) - ty) + (h01 * (T(1) - tx) + h11 * tx) * ty;
+    T dhdx = T(0), dhdy = T(0);
+    const T span_x = T(t.nx - 1) * t.cell, span_y = T(t.ny - 1) * t.cell;
+    if (t.nx >= 2 && px >= t.ox && px <= t.ox + span_x)
+        dhdx = ((h10 - h00) * (T(1) - ty) + (h11 - h01) * ty) / t.cell;
+    if (t.ny >= 2 && py >= t.oy && py <= t.oy + span_y)
+        dhdy = ((h01 - h00) * (T(1) - tx) + (h11 - h10) * tx) / t.cell;
+    const V3<T> n = mk3<T>(-dhdx, -dhdy, T(1));
+    const T l = pz_sqrt(dot(n, n));
+    n_out = l > T(0) ? n * (T(1) / l) : n;
+    return h;
+}
+
+// One contact point against the ground: the penetration along the
+// terrain normal (phyz_kernels.cu:916-918), that normal in the body frame,
+// and (with a heightfield) the world point and the terrain height there.
+// The flat ground only needs the body's world up and origin height.
+template <bool TERRAIN, class T>
+struct GroundHit {
+    T pen, h;
+    V3<T> n, w;
+};
+template <bool TERRAIN, class T>
+PZ_HD GroundHit<TERRAIN, T> ground_hit(const Terrain<T>& ter, const T& ground_h, const WF<T>& wf, const V3<T>& sup) {
+    GroundHit<TERRAIN, T> g;
+    if constexpr (TERRAIN) {
+        g.w = mk3<T>(wf.pos.x + dot(wf.r0, sup), wf.pos.y + dot(wf.r1, sup), wf.pos.z + dot(wf.up, sup));
+        V3<T> nw;
+        g.h = terrain_at(ter, g.w.x, g.w.y, nw);
+        g.pen = nw.z * (g.h - g.w.z);
+        g.n = wf.r0 * nw.x + wf.r1 * nw.y + wf.up * nw.z;
+    } else {
+        g.h = ground_h;
+        g.pen = ground_h - (wf.pos.z + dot(wf.up, sup));
+        g.n = wf.up;
+    }
+    return g;
+}
+
+// ground_hit on the flat plane with the world point filled in (the contact
+// state wants it).
+template <class T>
+PZ_HD GroundHit<true, T> flat_hit(const T& ground_h, const WF<T>& wf, const V3<T>& sup) {
+    GroundHit<true, T> g;
+    g.w = mk3<T>(wf.pos.x + dot(wf.r0, sup), wf.pos.y + dot(wf.r1, sup), wf.pos.z + dot(wf.up, sup));
+    g.h = ground_h;
+    g.pen = ground_h - g.w.z;
+    g.n = wf.up;
+    return g;
+}
+
 // Contact wrench (body frame) of body i at body velocity v, and its state.
 // With `full`, the body's contact state [touching, depth, point(3),
 // force(3)] (layout.rs:68-80) goes to rows 8*i.. of `cs`.
-template <class T>
+template <bool TERRAIN, class T>
 PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const WF<T>& wf,
                            const SV<T>& v, bool full, int i, const Out<T>& cs) {
     SV<T> f = zerosv<T>();
     V3<T> fw = zero3<T>();
-    T deepest = T(0), dx = T(0), dy = T(0);
+    T deepest = T(0), dx = T(0), dy = T(0), dz = M.ground_h;
     bool any = false;
     const T pt_scale = bi.gtype == 2 ? T(0.25) : T(1);
     const int npts = bi.gtype == 2 ? 8 : 1;
     for (int c = 0; c < npts; c++) {
         const V3<T> sup = support_pt(bi, bt, wf.up, c);
-        const T z = wf.pos.z + dot(wf.up, sup);
-        const T pen = M.ground_h - z;
+        const GroundHit<TERRAIN, T> g = ground_hit<TERRAIN>(M.ter, M.ground_h, wf, sup);
+        const T pen = g.pen;
         if (!(pen > T(0))) continue;
-        const V3<T>& n = wf.up;
+        const V3<T>& n = g.n;
         const V3<T> vp = v.l + cross(v.w, sup);
         const T vn = dot(vp, n);
         const T mn = eff_mass(bt, sup, n);
@@ -793,8 +876,14 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
             fw = fw + mk3<T>(dot(wf.r0, fb), dot(wf.r1, fb), dot(wf.up, fb));
             if (pen > deepest) {
                 deepest = pen;
-                dx = wf.pos.x + dot(wf.r0, sup);
-                dy = wf.pos.y + dot(wf.r1, sup);
+                if constexpr (TERRAIN) {
+                    dx = g.w.x;
+                    dy = g.w.y;
+                    dz = g.h;
+                } else {
+                    dx = wf.pos.x + dot(wf.r0, sup);
+                    dy = wf.pos.y + dot(wf.r1, sup);
+                }
             }
         }
     }
@@ -803,7 +892,7 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
         cs.put(8 * i + 1, any ? deepest : T(0));
         cs.put(8 * i + 2, any ? dx : T(0));
         cs.put(8 * i + 3, any ? dy : T(0));
-        cs.put(8 * i + 4, any ? M.ground_h : T(0));
+        cs.put(8 * i + 4, any ? dz : T(0));
         cs.put(8 * i + 5, any ? fw.x : T(0));
         cs.put(8 * i + 6, any ? fw.y : T(0));
         cs.put(8 * i + 7, any ? fw.z : T(0));
@@ -814,15 +903,16 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
 // Out-of-line entry to contact_wrench: everything by value, so the caller's
 // sweep state stays in registers and the contact temporaries do not add to
 // the sweep's register pressure.
-template <class T>
-PZ_OUTLINE SV<T> contact_wrench_call(T ground_h, T friction, T inv_dt_c, T kstiff_c, BodyI bi, const BodyT<T>* bt,
-                                     WF<T> wf, SV<T> v, bool full, int i, Out<T> cs) {
+template <bool TERRAIN, class T>
+PZ_OUTLINE SV<T> contact_wrench_call(T ground_h, T friction, T inv_dt_c, T kstiff_c, Terrain<T> ter, BodyI bi,
+                                     const BodyT<T>* bt, WF<T> wf, SV<T> v, bool full, int i, Out<T> cs) {
     ModelView<T> M;
     M.ground_h = ground_h;
     M.friction = friction;
     M.inv_dt_c = inv_dt_c;
     M.kstiff_c = kstiff_c;
-    return contact_wrench(M, bi, *bt, wf, v, full, i, cs);
+    M.ter = ter;
+    return contact_wrench<TERRAIN>(M, bi, *bt, wf, v, full, i, cs);
 }
 
 // ── per-world I/O of a launch ──────────────────────────────────────────────
@@ -836,7 +926,7 @@ struct WorldIO {
 };
 
 // Queue the control inputs of `step` for body i into its w0 slots.
-template <class T, class Scr>
+template <bool SEP, class T, class Scr>
 PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
                              int step) {
     const int nd = bi.ndof;
@@ -845,18 +935,18 @@ PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& 
         const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
         const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
                                 : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
-        S.prefetch(bi.s_in + k, src);
+        S.prefetch((SEP ? bi.s_in : bi.s_w0) + k, src);
     }
 }
 // One-DOF form for the relabelled-hinge path.
-template <class T, class Scr>
+template <bool SEP, class T, class Scr>
 PZ_HD void prefetch_control1(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
                              int step) {
     const int d = bi.off;
     const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
     const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
                             : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
-    S.prefetch(bi.s_in, src);
+    S.prefetch(SEP ? bi.s_in : bi.s_w0, src);
 }
 
 // I c for a bias c whose K components are structurally zero (c = v x S qd
@@ -922,41 +1012,71 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     }
     cv = v;
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
-        V3<T> up_p;
-        T h_p;
+        constexpr bool TERRAIN = (FEAT & FEAT_TERRAIN) != 0;
+        constexpr int NW = TERRAIN ? 12 : 4;  // frame words kept per body
+        // the parent's world frame: up and origin height, or with a
+        // heightfield the rows r0, r1, up of its body->world rotation and its
+        // origin (a row transforms into the child frame like a vector)
+        WF<T> pf;
         if (p < 0) {
-            up_p = mk3<T>(T(0), T(0), T(1));
-            h_p = T(0);
+            pf.r0 = mk3<T>(T(1), T(0), T(0));
+            pf.r1 = mk3<T>(T(0), T(1), T(0));
+            pf.up = mk3<T>(T(0), T(0), T(1));
+            pf.pos = zero3<T>();
         } else if (p == i - 1) {
-            up_p = cw.up;
-            h_p = cw.pos.z;
+            pf = cw;
         } else {
             const int s = M.bi[p].s_wx;
-            up_p = mk3<T>(S(s), S(s + 1), S(s + 2));
-            h_p = S(s + 3);
+            if constexpr (TERRAIN) {
+                pf.r0 = mk3<T>(S(s), S(s + 1), S(s + 2));
+                pf.r1 = mk3<T>(S(s + 3), S(s + 4), S(s + 5));
+                pf.up = mk3<T>(S(s + 6), S(s + 7), S(s + 8));
+                pf.pos = mk3<T>(S(s + 9), S(s + 10), S(s + 11));
+            } else {
+                pf.up = mk3<T>(S(s), S(s + 1), S(s + 2));
+                pf.pos.z = S(s + 3);
+            }
         }
         WF<T> wf;
-        wf.up = tree_rot<AX, FEAT>(bi, bt, j, up_p);
-        wf.pos.z = h_p + dot(up_p, tree_pos<AX, FEAT>(bi, bt, j));
-        cw.up = wf.up;
-        cw.pos.z = wf.pos.z;
-        if (bi.flags & F_BRANCH) {
-            const int s = bi.s_wx;
-            S(s) = wf.up.x;
-            S(s + 1) = wf.up.y;
-            S(s + 2) = wf.up.z;
-            S(s + 3) = wf.pos.z;
+        const V3<T> tp = tree_pos<AX, FEAT>(bi, bt, j);
+        wf.up = tree_rot<AX, FEAT>(bi, bt, j, pf.up);
+        wf.pos.z = pf.pos.z + dot(pf.up, tp);
+        if constexpr (TERRAIN) {
+            wf.r0 = tree_rot<AX, FEAT>(bi, bt, j, pf.r0);
+            wf.r1 = tree_rot<AX, FEAT>(bi, bt, j, pf.r1);
+            wf.pos.x = pf.pos.x + dot(pf.r0, tp);
+            wf.pos.y = pf.pos.y + dot(pf.r1, tp);
         }
+        cw = wf;
+        auto store = [&](int s) {
+            if constexpr (TERRAIN) {
+                S(s) = wf.r0.x;
+                S(s + 1) = wf.r0.y;
+                S(s + 2) = wf.r0.z;
+                S(s + 3) = wf.r1.x;
+                S(s + 4) = wf.r1.y;
+                S(s + 5) = wf.r1.z;
+                S(s + 6) = wf.up.x;
+                S(s + 7) = wf.up.y;
+                S(s + 8) = wf.up.z;
+                S(s + 9) = wf.pos.x;
+                S(s + 10) = wf.pos.y;
+                S(s + 11) = wf.pos.z;
+            } else {
+                S(s) = wf.up.x;
+                S(s + 1) = wf.up.y;
+                S(s + 2) = wf.up.z;
+                S(s + 3) = wf.pos.z;
+            }
+        };
+        static_assert(NW == 4 || NW == 12, "frame words");
+        if (bi.flags & F_BRANCH) store(bi.s_wx);
         if (bi.flags & F_CONTACT) {
             if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
-                // the impulse sweeps read the body's world up and height
-                S(bi.s_up) = wf.up.x;
-                S(bi.s_up + 1) = wf.up.y;
-                S(bi.s_up + 2) = wf.up.z;
-                S(bi.s_up + 3) = wf.pos.z;
+                store(bi.s_up);  // the impulse sweeps read the body's frame
             } else {
-                const SV<T> f = contact_wrench_call(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, bi, &bt, wf,
-                                                    v, false, i, Out<T>{nullptr, 0});
+                const SV<T> f = contact_wrench_call<TERRAIN>(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, M.ter,
+                                                             bi, &bt, wf, v, false, i, Out<T>{nullptr, 0});
                 st_sv(S, bi.s_f, f);
             }
         }
@@ -1020,7 +1140,7 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
             continue;
         }
         const WF<T> wf = world_frame<FEAT>(M, S, i);
-        contact_wrench(M, bi, M.bt[i], wf, ld_vel<T>(S, bi), true, i, cs);
+        contact_wrench<(FEAT & FEAT_TERRAIN) != 0>(M, bi, M.bt[i], wf, ld_vel<T>(S, bi), true, i, cs);
     }
 }
 
@@ -1090,35 +1210,37 @@ PZ_HD void body_tangents(const BodyI& bi, const V3<T>& n, V3<T>& u, V3<T>& w) {
 
 // One staged Coulomb update of every contact point of body i (normal
 // impulse first, then the tangential impulse clamped into the friction disc
-// that normal admits), at the body's free velocity `vf` (body frame) with
-// world up `up` (body frame) and origin height `z0`. The impulses of the
-// previous sweep are read from and the new ones written to the body's
-// impulse slots; returns the wrench (body frame) they apply over one step.
-template <class T, class Scr>
-PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const BodyI& bi, const BodyT<T>& bt, const V3<T>& up, const T& z0,
-                           const SV<T>& vf, const Scr& S) {
+// that normal admits), at the body's free velocity `vf` (body frame), with
+// the body's world frame `wf` (up and origin height; all of it with a
+// heightfield). The impulses of the previous sweep are read from and the new
+// ones written to the body's impulse slots; returns the wrench (body frame)
+// they apply over one step.
+template <bool TERRAIN, class T, class Scr>
+PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const BodyI& bi, const BodyT<T>& bt,
+                           const WF<T>& wf, const SV<T>& vf, const Scr& S) {
     const int npts = bi.gtype == 2 ? 8 : 1;
     const T dtc = pz_max(m.dt, T(1e-9));
     // within-body load sharing: points inside the margin
     int n_active = 0;
     for (int c = 0; c < npts; c++) {
-        const V3<T> sup = support_pt(bi, bt, up, c);
-        if (m.ground_h - (z0 + dot(up, sup)) > -m.margin) n_active++;
+        const V3<T> sup = support_pt(bi, bt, wf.up, c);
+        if (ground_hit<TERRAIN>(ter, m.ground_h, wf, sup).pen > -m.margin) n_active++;
     }
     const T na = T(n_active < 1 ? 1 : n_active);
     SV<T> f = zerosv<T>();
     bool any = false;
     for (int c = 0; c < npts; c++) {
         const int slot = bi.s_imp + 3 * c;
-        const V3<T> sup = support_pt(bi, bt, up, c);
-        const T pen = m.ground_h - (z0 + dot(up, sup));
+        const V3<T> sup = support_pt(bi, bt, wf.up, c);
+        const GroundHit<TERRAIN, T> g = ground_hit<TERRAIN>(ter, m.ground_h, wf, sup);
+        const T pen = g.pen;
         if (!(pen > -m.margin)) {
             S(slot) = T(0);
             S(slot + 1) = T(0);
             S(slot + 2) = T(0);
             continue;
         }
-        const V3<T>& n = up;
+        const V3<T>& n = g.n;
         const V3<T> vp = vf.l + cross(vf.w, sup);
         V3<T> tu, tw;
         body_tangents(bi, n, tu, tw);
@@ -1155,9 +1277,10 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const BodyI& bi, const BodyT<T>& 
 
 // Out-of-line entry, everything by value: the sweep's own state stays in
 // registers.
-template <class T, class Scr>
-PZ_OUTLINE SV<T> impulse_wrench_call(ImpMat<T> m, BodyI bi, const BodyT<T>* bt, V3<T> up, T z0, SV<T> vf, Scr S) {
-    return impulse_wrench(m, bi, *bt, up, z0, vf, S);
+template <bool TERRAIN, class T, class Scr>
+PZ_OUTLINE SV<T> impulse_wrench_call(ImpMat<T> m, Terrain<T> ter, BodyI bi, const BodyT<T>* bt, WF<T> wf, SV<T> vf,
+                                     Scr S) {
+    return impulse_wrench<TERRAIN>(m, ter, bi, *bt, wf, vf, S);
 }
 
 // Contact state of every body in impulse mode, from the impulses the last
@@ -1180,18 +1303,23 @@ PZ_HD void contact_state_impulse_pass(const ModelView<T>& M, const Scr& S, const
         bool any = false;
         for (int c = 0; c < npts; c++) {
             const V3<T> sup = support_pt(bi, bt, wf.up, c);
-            const T z = wf.pos.z + dot(wf.up, sup);
-            const T pen = M.im.ground_h - z;
+            // the world frame is complete here: the world point is at hand
+            GroundHit<true, T> g;
+            if constexpr ((FEAT & FEAT_TERRAIN) != 0)
+                g = ground_hit<true>(M.ter, M.im.ground_h, wf, sup);
+            else
+                g = flat_hit(M.im.ground_h, wf, sup);
+            const T pen = g.pen;
             if (!(pen > -M.im.margin)) continue;
             V3<T> tu, tw;
-            body_tangents(bi, wf.up, tu, tw);
+            body_tangents(bi, g.n, tu, tw);
             const int slot = bi.s_imp + 3 * c;
-            const V3<T> fb = (wf.up * S(slot) + tu * S(slot + 1) + tw * S(slot + 2)) * idt;
+            const V3<T> fb = (g.n * S(slot) + tu * S(slot + 1) + tw * S(slot + 2)) * idt;
             fw = fw + mk3<T>(dot(wf.r0, fb), dot(wf.r1, fb), dot(wf.up, fb));
             any = true;
             if (pen > deepest) {
                 deepest = pen;
-                dp = mk3<T>(wf.pos.x + dot(wf.r0, sup), wf.pos.y + dot(wf.r1, sup), z);
+                dp = g.w;
             }
         }
         cs.put(8 * i + 0, any ? T(1) : T(0));
@@ -1303,7 +1431,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
             sp = hinge ? dot(a, pA.w) : dot(a, pA.l);
         }
         const T D = sU + bt.d_extra;
-        const T u = dof_force(M, bi, bt, S, 0, AX >= 0 || bi.ndof == 1) - sp;
+        const T u = dof_force<(FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, 0, AX >= 0 || bi.ndof == 1) - sp;
         // aba.rs:240-242: a singular D skips the body (W = 0, w0 = 0). The
         // record store happens once, outside any per-world branch, because
         // a Tensor-Memory store is warp-wide.
@@ -1342,9 +1470,9 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         if (bi.ndof > 1) {
             if constexpr ((FEAT & FEAT_MULTI) != 0) {
                 if (bi.ndof == 3)
-                    live = multi_dof<3>(M, bi, bt, S, I, pA, c, p >= 0);
+                    live = multi_dof<3, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0);
                 else
-                    live = multi_dof<6>(M, bi, bt, S, I, pA, c, p >= 0);
+                    live = multi_dof<6, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0);
             }
         }
     }
@@ -1520,9 +1648,9 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
     }
     if constexpr (!LAST) {
         if constexpr (AX >= 0)
-            prefetch_control1(M, bi, S, io, next_step);
+            prefetch_control1<(FEAT & FEAT_IMPULSE) != 0>(M, bi, S, io, next_step);
         else
-            prefetch_controls(M, bi, S, io, next_step);
+            prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, bi, S, io, next_step);
         pass1_body<AX, FEAT>(M, S, i, bi, cvn, cw);
     }
 }
@@ -1637,8 +1765,19 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     else
         st_sv(S, bi.s_vw, vo);
     if (bi.flags & F_CONTACT) {
-        const V3<T> up = mk3<T>(S(bi.s_up), S(bi.s_up + 1), S(bi.s_up + 2));
-        const SV<T> f = impulse_wrench_call(M.im, bi, &bt, up, S(bi.s_up + 3), vf, S);
+        constexpr bool TERRAIN = (FEAT & FEAT_TERRAIN) != 0;
+        const int s = bi.s_up;
+        WF<T> wf;
+        if constexpr (TERRAIN) {
+            wf.r0 = mk3<T>(S(s), S(s + 1), S(s + 2));
+            wf.r1 = mk3<T>(S(s + 3), S(s + 4), S(s + 5));
+            wf.up = mk3<T>(S(s + 6), S(s + 7), S(s + 8));
+            wf.pos = mk3<T>(S(s + 9), S(s + 10), S(s + 11));
+        } else {
+            wf.up = mk3<T>(S(s), S(s + 1), S(s + 2));
+            wf.pos.z = S(s + 3);
+        }
+        const SV<T> f = impulse_wrench_call<TERRAIN>(M.im, M.ter, bi, &bt, wf, vf, S);
         st_sv(S, bi.s_f, f);
     }
 }

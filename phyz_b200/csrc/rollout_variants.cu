@@ -5,7 +5,7 @@
 #include "stepper_kernels.cuh"
 
 #if !defined(PZ_VARIANT_T) || !defined(PZ_VARIANT_FEAT)
-#error "compile with -DPZ_VARIANT_T=float|double -DPZ_VARIANT_FEAT=<0..31>"
+#error "compile with -DPZ_VARIANT_T=float|double -DPZ_VARIANT_FEAT=<0..63>"
 #endif
 
 namespace pz {

@@ -196,6 +196,13 @@ __device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const
     M.im.width = T(P.si_width);
     M.im.mid = T(P.si_mid);
     M.im.power = T(P.si_power);
+    M.ter.h = P.hf;
+    M.ter.nx = P.hf_nx;
+    M.ter.ny = P.hf_ny;
+    M.ter.ox = T(P.hf_ox);
+    M.ter.oy = T(P.hf_oy);
+    M.ter.oz = T(P.hf_oz);
+    M.ter.cell = T(P.hf_cell);
     return M;
 }
 
@@ -254,7 +261,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
             S(M.nv + j) = P.v[j * N + w];
         }
         const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
-        for (int i = 0; i < M.nb; i++) prefetch_controls(M, M.bi[i], S, io, 0);
+        for (int i = 0; i < M.nb; i++) prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, M.bi[i], S, io, 0);
         S.commit();
         if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
             // the wrenches of the previous step's last sweep and the staged

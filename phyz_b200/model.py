@@ -92,6 +92,37 @@ class Geometry:
 
 
 @dataclass
+class Heightfield:
+    """Terrain as a regular grid of f32 heights: phyz_model::Heightfield
+    (crates/phyz-model/src/heightfield.rs:10-37). Node (ix, iy) sits at world
+    (origin.x + ix cell, origin.y + iy cell) with height origin.z +
+    heights[iy * nx + ix]; sampled bilinearly, clamped to the border outside."""
+    origin: tuple = (0.0, 0.0, 0.0)
+    cell: float = 1.0
+    nx: int = 1
+    ny: int = 1
+    heights: np.ndarray = field(default_factory=lambda: np.zeros(1, np.float32))
+
+    @staticmethod
+    def new(origin, cell: float, nx: int, ny: int) -> "Heightfield":
+        return Heightfield(tuple(float(x) for x in origin), float(cell), int(nx), int(ny),
+                           np.zeros(nx * ny, np.float32))
+
+    @staticmethod
+    def flat(height: float) -> "Heightfield":
+        """The infinite plane at z = height (a 1 x 1 field)."""
+        return Heightfield.new((0.0, 0.0, height), 1.0, 1, 1)
+
+    def to_c(self):
+        h = np.ascontiguousarray(self.heights, np.float32).reshape(-1)
+        if h.size != self.nx * self.ny:
+            raise ValueError(f"heightfield claims {self.nx}x{self.ny} nodes but carries {h.size} heights")
+        c = _lib.PhyzbHeightfield((C.c_double * 3)(*self.origin), float(self.cell), int(self.nx), int(self.ny),
+                                  h.ctypes.data_as(C.POINTER(C.c_float)))
+        return c, h
+
+
+@dataclass
 class Joint:
     """phyz_model::Joint (joint.rs:28-70)."""
 
