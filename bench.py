@@ -22,7 +22,8 @@ cores. `--impl reference` times only that reference CPU path.
 
 `--config c3_quadruped_impulse` runs C3's worlds with impulse-mode contact
 (16 staged Coulomb sweeps per step) in place of the penalty law, 100 steps
-per rollout by default.
+per rollout by default; `--config c3_quadruped_terrain` runs them with the
+penalty law over a seeded 64 x 64 heightfield.
 """
 from __future__ import annotations
 
@@ -55,8 +56,10 @@ NCU_DRAM_CAPTURES: dict = {
 # Workloads beyond BASELINE.json's configs: a config's model, worlds and
 # initial state with impulse-mode contact (enable_contact_impulse, 16 sweeps
 # per step) in place of the penalty law, over a shorter default horizon
-# (every impulse step runs 17 backward sweeps).
+# (every impulse step runs 17 backward sweeps); or with the penalty law over
+# a seeded heightfield (enable_contact_terrain) instead of the flat ground.
 IMPULSE_WORKLOADS = {"c3_quadruped_impulse": ("c3_quadruped", 100)}
+TERRAIN_WORKLOADS = {"c3_quadruped_terrain": "c3_quadruped"}
 
 
 def base_config(name):
@@ -64,7 +67,21 @@ def base_config(name):
     if name in IMPULSE_WORKLOADS:
         base, horizon = IMPULSE_WORKLOADS[name]
         return base, True, horizon
+    if name in TERRAIN_WORKLOADS:
+        return TERRAIN_WORKLOADS[name], False, 0
     return name, False, 0
+
+
+def bench_heightfield(name):
+    """The seeded terrain of a heightfield workload (None for the others):
+    64 x 64 nodes 0.25 m apart centred on the origin, heights N(0, 0.05) m."""
+    if name not in TERRAIN_WORKLOADS:
+        return None
+    from phyz_b200 import Heightfield
+
+    hf = Heightfield.new((-8.0, -8.0, 0.0), 0.25, 64, 64)
+    hf.heights[:] = (0.05 * np.random.default_rng(0x7E55).standard_normal(64 * 64)).astype(np.float32)
+    return hf
 
 
 def ncu_traffic(config, prec, nv, esz, nworld, horizon):
@@ -195,6 +212,7 @@ def reference_cpu(workload, model, nworld, horizon, seconds, world_offset=0):
 
     cfg_name, impulse, _ = base_config(workload)
     ref = RefHost()
+    ref.set_heightfield(bench_heightfield(workload))
     cfg = configs.CONFIGS[cfg_name]
     threads = cpu_threads()
     n = min(nworld, 2048 if impulse else 16384)  # an impulse step costs ~17 plain ones
@@ -230,6 +248,9 @@ def reference_cpu(workload, model, nworld, horizon, seconds, world_offset=0):
     dt = time.perf_counter() - t0
     steps = chunks * period
     mode = ", impulse contact (16 sweeps)" if impulse else ""
+    if workload in TERRAIN_WORKLOADS:
+        mode = ", heightfield terrain"
+        ref.set_heightfield(None)
     return n * steps / dt, threads, (f"{n} of {nworld} worlds x {steps} of {horizon} steps, f32{mode}, "
                                      f"{threads} threads, {dt:.1f} s")
 
@@ -294,8 +315,14 @@ def main():
     offset, _ = weak_block(nworld, rank)  # this rank's block of worlds
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
+    hf = bench_heightfield(args.config)
     if cfg.contact and impulse:
         sim.enable_contact_impulse(cfg.contact[0], cfg.contact[3])
+    elif cfg.contact and hf is not None:
+        from phyz_b200 import BodyContactGains
+
+        g, k, d, mu = cfg.contact
+        sim.enable_contact_terrain(g, mu, [BodyContactGains(k, d)] * model.nbodies, heightfield=hf)
     elif cfg.contact:
         sim.enable_ground_contact(*cfg.contact)
     stream = torch.cuda.Stream()
@@ -437,7 +464,8 @@ def main():
             "config": {"workload": args.config, "nworld_per_gpu": nworld, "horizon": horizon, "nbodies":
                        model.nbodies, "nv": nv, "parallelism": f"worlds sharded over {world} GPU(s)",
                        "contact": (f"impulse, {sim.contact_sweeps} sweeps per step" if impulse
-                                   else ("penalty" if cfg.contact else None)),
+                                   else ("penalty, 64 x 64 heightfield" if hf is not None
+                                         else ("penalty" if cfg.contact else None))),
                        "l2": "inputs larger than L2: the per-step control schedule "
                              f"({horizon * nv * nworld * esz / 1e9:.1f} GB) streams from HBM every rollout",
                        "launch": info},

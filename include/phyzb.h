@@ -212,8 +212,8 @@ typedef struct phyzb_body_plane {
  * (cuda/mod.rs:642-676): penalty contact with per-body gains (nbodies
  * each) against the heightfield `hf` (NULL: the flat plane at
  * ground_height, which a loaded heightfield overrides) and an optional
- * body-attached plane (not available in this build: PHYZB_ERR_UNSUPPORTED).
- * The device node buffer is sized to this first field. */
+ * body-attached plane (NULL: none; phyz_kernels.cu:983-1132). The device
+ * node buffer is sized to this first field. */
 int phyzb_enable_contact_terrain(phyzb_sim* sim, double ground_height, double friction,
                                  const double* stiffness, const double* damping,
                                  const phyzb_body_plane* plane, const phyzb_heightfield* hf,

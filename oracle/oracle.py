@@ -185,7 +185,7 @@ def _rollout_impulse(self, model, q, v, ctrl=None, nsteps=1, schedule=False, con
     if ctrl is not None:
         ctrl = np.ascontiguousarray(ctrl, np.float64)
         stride = n * nv if schedule else 0
-    per = nb * 6 + nb * IMPULSE_PTS * 3
+    per = nb * 6 + 2 * nb * IMPULSE_PTS * 3
     st = np.zeros((n, per)) if state is None else np.array(state, np.float64, copy=True, order="C")
     ground, fr = contact
     m = impulse_material(model.dt)
@@ -231,6 +231,23 @@ def _terrain_at(self, x, y):
 
 
 Oracle.terrain_at = _terrain_at
+
+
+def _set_plane(self, plane=None, nbodies=0):
+    """The body-attached plane of the following contact rollouts (a
+    phyz_b200.BodyPlane; None: no plane)."""
+    L = self.lib
+    L.oracle_set_plane.argtypes = [C.c_int32, C.c_double, C.c_double, C.c_double, C.c_double, _I, C.c_int32,
+                                   C.c_int32]
+    if plane is None:
+        L.oracle_set_plane(-1, 0.0, 0.0, 0.0, 0.0, None, 0, 0)
+        return
+    ex = np.ascontiguousarray(list(plane.exclude) or [-1], np.int32)
+    L.oracle_set_plane(int(plane.body), float(plane.offset), float(plane.max_depth), float(plane.half_x),
+                       float(plane.half_y), ex.ctypes.data_as(_I), len(plane.exclude), int(nbodies))
+
+
+Oracle.set_plane = _set_plane
 
 
 class RefHost:
@@ -344,6 +361,19 @@ class RefHost:
                                  float(ground), float(fr), npd, _f(tbl), _f(tg), _f(qf), _f(vf), _f(cf), stride,
                                  nsteps, _f(qdd), _f(cs))
         return qf, vf, qdd, cs
+
+    def set_plane(self, plane=None):
+        """The body-attached plane of the following host rollouts and
+        geometry packs (None: no plane)."""
+        self.lib.phyzref_set_plane.argtypes = [C.c_int32, C.c_float, C.c_float, C.c_float, C.c_float, _I,
+                                               C.c_int32]
+        if plane is None:
+            self.lib.phyzref_set_plane(-1, 0.0, 0.0, 0.0, 0.0, None, 0)
+            return
+        ex = np.ascontiguousarray(list(plane.exclude) or [-1], np.int32)
+        self.lib.phyzref_set_plane(int(plane.body), float(plane.offset), float(plane.max_depth),
+                                   float(plane.half_x), float(plane.half_y), ex.ctypes.data_as(_I),
+                                   len(plane.exclude))
 
     def set_heightfield(self, hf=None):
         """The terrain the following host rollouts pass to the reference's

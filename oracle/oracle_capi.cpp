@@ -120,6 +120,24 @@ int oracle_energy(const phyzb_model* fm, int64_t nworld, const double* q, const 
 // The heightfield the following contact rollouts sample (nx == 0: none, the
 // flat plane at their ground height). Test-only process state.
 static Terrain g_terrain;
+static Plane g_plane;
+
+// The body-attached plane of the following contact rollouts (body < 0:
+// none); `exclude` lists bodies that never touch it.
+int oracle_set_plane(int32_t body, double offset, double max_depth, double half_x, double half_y,
+                     const int32_t* exclude, int32_t n_exclude, int32_t nb) {
+    g_plane = Plane{};
+    g_plane.body = body;
+    g_plane.offset = offset;
+    g_plane.max_depth = max_depth;
+    g_plane.half_x = half_x;
+    g_plane.half_y = half_y;
+    g_plane.no_plane.assign(nb > 0 ? nb : 0, 0);
+    for (int k = 0; k < n_exclude; k++)
+        if (exclude[k] >= 0 && exclude[k] < nb) g_plane.no_plane[exclude[k]] = 1;
+    if (body >= 0 && body < nb) g_plane.no_plane[body] = 1;
+    return 0;
+}
 
 int oracle_set_heightfield(int32_t nx, int32_t ny, double ox, double oy, double oz, double cell,
                            const float* heights) {
@@ -158,6 +176,7 @@ int oracle_penalty_contact(const phyzb_model* fm, int64_t nworld, const double* 
     cp.k.assign(k, k + nb);
     cp.d.assign(d, d + nb);
     cp.terrain = g_terrain;
+    cp.plane = g_plane;
     for (int64_t w = 0; w < nworld; w++) {
         std::vector<SVec> ext;
         penalty_contact(m, cp, q + w * m.nq, v + w * m.nv, ext,
@@ -196,6 +215,7 @@ int oracle_rollout(const phyzb_model* fm, int64_t nworld, double* q, double* v,
         cp.k.assign(k, k + nb);
         cp.d.assign(d, d + nb);
         cp.terrain = g_terrain;
+        cp.plane = g_plane;
     }
     std::vector<PdEntry> pd;
     for (int i = 0; i < npd; i++)
@@ -223,7 +243,8 @@ int oracle_rollout(const phyzb_model* fm, int64_t nworld, double* q, double* v,
 
 // Impulse-mode rollout (step_world_impulse), nsteps times. `state` carries
 // the per-world impulse state across calls: per world, nb x 6 wrenches then
-// nb x 8 x 3 staged impulses (in/out; zeros to start).
+// nb x 8 x 3 staged impulses against the ground, then as many against the
+// body-attached plane (in/out; zeros to start).
 int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, double* v,
                            const double* ctrl, int64_t ctrl_step_stride, int32_t nsteps,
                            const double* params /* ground, friction, erp, margin, restitution,
@@ -248,11 +269,12 @@ int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, dou
     cp.power = params[10];
     cp.sweeps = sweeps;
     cp.terrain = g_terrain;
+    cp.plane = g_plane;
     std::vector<PdEntry> pd;
     for (int i = 0; i < npd; i++)
         pd.push_back(PdEntry{pd_idx[2 * i], pd_idx[2 * i + 1], pd_gains[3 * i], pd_gains[3 * i + 1],
                              pd_gains[3 * i + 2]});
-    const int64_t per = (int64_t)nb * 6 + (int64_t)nb * IMPULSE_PTS * 3;
+    const int64_t per = (int64_t)nb * 6 + 2 * (int64_t)nb * IMPULSE_PTS * 3;
     parallel_worlds(nworld, nthreads, [&](int64_t a, int64_t b) {
         std::vector<double> c(nv), qdd(nv);
         ImpulseState st;
@@ -266,6 +288,7 @@ int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, dou
                 st.ext[i].lin = v3(sw[6 * i + 3], sw[6 * i + 4], sw[6 * i + 5]);
             }
             for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) st.imp[k] = sw[nb * 6 + k];
+            for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) st.pimp[k] = sw[nb * 6 + nb * IMPULSE_PTS * 3 + k];
             for (int s = 0; s < nsteps; s++) {
                 const double* src = ctrl ? ctrl + s * ctrl_step_stride + w * nv : nullptr;
                 for (int j = 0; j < nv; j++) c[j] = src ? src[j] : 0.0;
@@ -280,6 +303,7 @@ int oracle_rollout_impulse(const phyzb_model* fm, int64_t nworld, double* q, dou
                 for (int k = 0; k < 6; k++) sw[6 * i + k] = vals[k];
             }
             for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) sw[nb * 6 + k] = st.imp[k];
+            for (int k = 0; k < nb * IMPULSE_PTS * 3; k++) sw[nb * 6 + nb * IMPULSE_PTS * 3 + k] = st.pimp[k];
             if (qdd_out)
                 for (int j = 0; j < nv; j++) qdd_out[w * nv + j] = qdd[j];
         }

@@ -876,11 +876,40 @@ struct Terrain {
     }
 };
 
+// A contact plane attached to a body (contact_pipeline.rs:318-355
+// BodyPlane): the face at `offset` along the body's +z, half_x x half_y in
+// its x/y; `no_plane[i]` marks the bodies that never touch it (the plane
+// body itself and the exclude list: pack_contact_geometry's geometry[7]).
+struct Plane {
+    int body = -1;
+    double offset = 0, max_depth = 0, half_x = 0, half_y = 0;
+    std::vector<char> no_plane;
+};
+
 struct ContactParams {
     double ground_height = 0, friction = 0;
     std::vector<double> k, d;  // per body gains (layout.rs:272-278)
     Terrain terrain;           // terrain.ground mirrors ground_height
+    Plane plane;
 };
+
+// Contact of every body with the body-attached plane, action on the body
+// and reaction on the plane's body at one shared point (phyz_kernels.cu:
+// 983-1132). `vel`: body-frame velocities (current in penalty mode, free in
+// impulse mode); penalty mode uses the gains k, d; impulse mode (imp !=
+// null: the material) updates the staged impulses `pimp` [nb][8][3].
+struct ImpulseParams;
+inline double impedance_at(const ImpulseParams& c, double depth);
+inline double effective_restitution(const ImpulseParams& c, double e, double approach);
+inline void contact_tangents(Vec3 n, Vec3& u, Vec3& w);
+inline double contact_eff_mass(const Body& b, Vec3 r, Vec3 u);
+inline Vec3 support_point(const Geom& g, Vec3 n_body);
+inline Vec3 box_corner(const Geom& g, int c);
+inline double max_damping(double me, double dt);
+inline double max_stiffness(double me, double dt);
+inline void plane_contact(const Model& m, const Plane& pl, double friction, const double* k, const double* d,
+                          const ImpulseParams* imp, const std::vector<Mat3>& wrot, const std::vector<Vec3>& wpos,
+                          const std::vector<SVec>& vel, std::vector<SVec>& ext, double* pimp);
 
 inline double fsign(double x) { return x > 0 ? 1.0 : (x < 0 ? -1.0 : 0.0); }
 
@@ -1030,6 +1059,7 @@ inline void penalty_contact(const Model& m, const ContactParams& cp, const doubl
         cs[6] = f_w_total.y;
         cs[7] = f_w_total.z;
     }
+    plane_contact(m, cp.plane, cp.friction, cp.k.data(), cp.d.data(), nullptr, wrot, wpos, vel, ext, nullptr);
 }
 
 // ── impulse-mode ground contact: the velocity-level staged Coulomb update
@@ -1040,6 +1070,7 @@ inline void penalty_contact(const Model& m, const ContactParams& cp, const doubl
 // (contact_pipeline.rs:199-218).
 struct ImpulseParams {
     Terrain terrain;  // nx == 0: the flat plane at ground_height
+    Plane plane;
     double ground_height = 0, friction = 0;
     double restitution = 0, restitution_threshold = 0.05;
     double erp = 0;  // solref_erp_from(0.02, 1.0, dt)
@@ -1101,12 +1132,120 @@ inline void contact_tangents(Vec3 n, Vec3& u, Vec3& w) {
 constexpr int IMPULSE_PTS = 8;
 struct ImpulseState {
     std::vector<SVec> ext;
-    std::vector<double> imp;  // [nb][IMPULSE_PTS][3]
+    std::vector<double> imp;   // [nb][IMPULSE_PTS][3]: against the ground
+    std::vector<double> pimp;  // [nb][IMPULSE_PTS][3]: against the body-attached plane
     void reset(int nb) {
         ext.assign(nb, SVec{});
         imp.assign((size_t)nb * IMPULSE_PTS * 3, 0.0);
+        pimp.assign((size_t)nb * IMPULSE_PTS * 3, 0.0);
     }
 };
+
+inline void plane_contact(const Model& m, const Plane& pl, double friction, const double* k, const double* d,
+                          const ImpulseParams* imp, const std::vector<Mat3>& wrot, const std::vector<Vec3>& wpos,
+                          const std::vector<SVec>& vel, std::vector<SVec>& ext, double* pimp) {
+    const int pb = pl.body, nb = m.nb();
+    if (pb < 0) return;
+    const double dt = m.dt, dtc = std::fmax(dt, 1e-9);
+    const Mat3& Rp = wrot[pb];
+    const Vec3 n_w = mul(Rp, v3(0, 0, 1));
+    const Vec3 p0_w = wpos[pb] + mul(Rp, v3(0, 0, pl.offset));
+    const Body& bp = m.bodies[pb];
+    for (int i = 0; i < nb; i++) {
+        const Body& b = m.bodies[i];
+        if (i == pb || b.geom.type == 0 || pl.no_plane[i]) continue;
+        const Mat3& Ri = wrot[i];
+        const Vec3 n_body = tmul(Ri, n_w);
+        const int npts = b.geom.type == 2 ? 8 : 1;
+        const double pt_scale = b.geom.type == 2 ? 0.25 : 1.0;
+        auto point = [&](int c) { return b.geom.type == 2 ? box_corner(b.geom, c) : support_point(b.geom, n_body); };
+        // the shape's footprint in face coordinates, intersected with the face
+        double lo_x = 1e30, lo_y = 1e30, hi_x = -1e30, hi_y = -1e30;
+        for (int c = 0; c < npts; c++) {
+            Vec3 rp = tmul(Rp, wpos[i] + mul(Ri, point(c)) - wpos[pb]);
+            lo_x = std::fmin(lo_x, rp.x);
+            lo_y = std::fmin(lo_y, rp.y);
+            hi_x = std::fmax(hi_x, rp.x);
+            hi_y = std::fmax(hi_y, rp.y);
+        }
+        const double ox0 = std::fmax(lo_x, -pl.half_x), oy0 = std::fmax(lo_y, -pl.half_y);
+        const double ox1 = std::fmin(hi_x, pl.half_x), oy1 = std::fmin(hi_y, pl.half_y);
+        if (ox0 > ox1 || oy0 > oy1) continue;
+        int active = 1;
+        if (imp) {
+            int cnt = 0;
+            for (int c = 0; c < npts; c++) {
+                double dd = -dot(wpos[i] + mul(Ri, point(c)) - p0_w, n_w);
+                if (dd > 0.0 && dd <= pl.max_depth) cnt++;
+            }
+            active = cnt > 1 ? cnt : 1;
+        }
+        for (int c = 0; c < npts; c++) {
+            double* slot = pimp ? pimp + ((size_t)i * IMPULSE_PTS + c) * 3 : nullptr;
+            const Vec3 sup = point(c);
+            const Vec3 sw0 = wpos[i] + mul(Ri, sup);
+            const double pen = -dot(sw0 - p0_w, n_w);
+            if (pen <= 0.0 || pen > pl.max_depth) {
+                if (slot) slot[0] = slot[1] = slot[2] = 0.0;
+                continue;
+            }
+            // the contact point in the face, clamped into the overlap: one
+            // world point, a lever on each body
+            Vec3 r_p = tmul(Rp, sw0 - wpos[pb]);
+            r_p.x = std::fmin(std::fmax(r_p.x, ox0), ox1);
+            r_p.y = std::fmin(std::fmax(r_p.y, oy0), oy1);
+            const Vec3 sw = wpos[pb] + mul(Rp, r_p);
+            const Vec3 sc = tmul(Ri, sw - wpos[i]);
+            const Vec3 v_rel = mul(Ri, vel[i].lin + cross(vel[i].ang, sc)) - mul(Rp, vel[pb].lin + cross(vel[pb].ang, r_p));
+            const double vn = dot(v_rel, n_w);
+            auto pair_mass = [&](Vec3 dir_w) {
+                return 1.0 / (1.0 / contact_eff_mass(b, sc, tmul(Ri, dir_w)) +
+                              1.0 / contact_eff_mass(bp, r_p, tmul(Rp, dir_w)));
+            };
+            const double m_n = pair_mass(n_w);
+            Vec3 f_w;
+            if (imp) {
+                Vec3 pu, pw;
+                contact_tangents(n_w, pu, pw);
+                const double bu = dot(v_rel, pu), bw = dot(v_rel, pw);
+                const double ann = active / std::fmax(m_n, 1e-9);
+                const double bias = impedance_at(*imp, pen) * imp->erp * std::fmax(pen, 0.0) / dtc;
+                const double e = effective_restitution(*imp, imp->restitution, std::fmin(vn, 0.0));
+                const double fn = std::fmax((bias - (vn * (1.0 + e) - ann * slot[0])) / ann, 0.0);
+                const double auu = active / std::fmax(pair_mass(pu), 1e-9);
+                const double aww = active / std::fmax(pair_mass(pw), 1e-9);
+                double ju = -(bu - auu * slot[1]) / auu, jw = -(bw - aww * slot[2]) / aww;
+                const double lim = friction * fn, jt = std::sqrt(ju * ju + jw * jw);
+                if (jt > lim) {
+                    const double scl = jt > 0.0 ? lim / jt : 0.0;
+                    ju *= scl;
+                    jw *= scl;
+                }
+                slot[0] = fn;
+                slot[1] = ju;
+                slot[2] = jw;
+                f_w = (n_w * fn + pu * ju + pw * jw) * (1.0 / dtc);
+            } else {
+                const double kb = std::fmin(pt_scale * k[i], max_stiffness(m_n, dt));
+                const double db = std::fmin(pt_scale * d[i], max_damping(m_n, dt));
+                const double fn = std::fmax(kb * pen - db * vn, 0.0);
+                const Vec3 vt3 = v_rel - n_w * vn;
+                const double vt = norm(vt3);
+                f_w = n_w * fn;
+                if (vt > 1e-6) {
+                    const Vec3 td = vt3 * (1.0 / vt);
+                    const double ft = std::fmin(friction * fn * std::fmin(1.0, vt / 1e-3), max_damping(pair_mass(td), dt) * vt);
+                    f_w = f_w - td * ft;
+                }
+            }
+            const Vec3 fi = tmul(Ri, f_w), fp = tmul(Rp, -f_w);
+            ext[i].ang = ext[i].ang + cross(sc, fi);
+            ext[i].lin = ext[i].lin + fi;
+            ext[pb].ang = ext[pb].ang + cross(r_p, fp);
+            ext[pb].lin = ext[pb].lin + fp;
+        }
+    }
+}
 
 // One contact sweep of one world: FK with the free velocity v + dt qdd, one
 // staged Coulomb update per contact point, the new wrenches into st.ext and
@@ -1216,7 +1355,12 @@ inline void impulse_contact(const Model& m, const ImpulseParams& cp, const doubl
             }
         }
         if (!any) {
+            // the reference clears the body's whole contact-state row here
+            // (phyz_kernels.cu:966-969), its plane impulses included: a body
+            // off the ground starts every sweep's plane update from zero
             for (int k = 0; k < IMPULSE_PTS * 3; k++) slots[k] = 0.0;
+            double* ps = st.pimp.data() + (size_t)i * IMPULSE_PTS * 3;
+            for (int k = 0; k < IMPULSE_PTS * 3; k++) ps[k] = 0.0;
             continue;
         }
         if (!cs) continue;
@@ -1229,6 +1373,7 @@ inline void impulse_contact(const Model& m, const ImpulseParams& cp, const doubl
         cs[6] = f_w_total.y;
         cs[7] = f_w_total.z;
     }
+    plane_contact(m, cp.plane, cp.friction, nullptr, nullptr, &cp, wrot, wpos, vel, st.ext, st.pimp.data());
 }
 
 // One step of the batched path for one world: [PD ->] [contact ->] ABA ->

@@ -82,6 +82,14 @@ int phyzref_pack_bodies(const phyzb_model* m, float* out) {
     return off;
 }
 
+// The body-attached plane of the following host rollouts (body < 0: none):
+// ContactParams fields 6-10 (contact_pipeline.rs:74-78) and the exclusion
+// flag geometry[7] that pack_contact_geometry sets (contact_pipeline.rs:
+// 637-641). Test-only process state.
+static int32_t g_plane_body = -1;
+static float g_plane[4] = {0, 0, 0, 0};  // offset, max_depth, half_x, half_y
+static std::vector<int32_t> g_plane_excl;
+
 // layout.rs:185-279 pack_geometries (primary shape, per-body gains)
 int phyzref_pack_geometries(const phyzb_model* m, const double* k, const double* dmp, float* out) {
     int collidable = 0;
@@ -97,6 +105,11 @@ int phyzref_pack_geometries(const phyzb_model* m, const double* k, const double*
         d[8] = (float)k[i];
         d[9] = (float)dmp[i];
     }
+    if (g_plane_body >= 0 && g_plane_body < m->nbodies) {
+        out[g_plane_body * GEOM_STRIDE + 7] = 1.0f;
+        for (int32_t b : g_plane_excl)
+            if (b >= 0 && b < m->nbodies) out[b * GEOM_STRIDE + 7] = 1.0f;
+    }
     return collidable;
 }
 
@@ -106,6 +119,17 @@ int phyzref_pack_geometries(const phyzb_model* m, const double* k, const double*
 static uint32_t g_hf_nx = 0, g_hf_ny = 0;
 static float g_hf_o[3] = {0, 0, 0}, g_hf_cell = 1.0f;
 static std::vector<float> g_hf(1, 0.0f);
+
+
+void phyzref_set_plane(int32_t body, float offset, float max_depth, float half_x, float half_y,
+                       const int32_t* exclude, int32_t n_exclude) {
+    g_plane_body = body;
+    g_plane[0] = offset;
+    g_plane[1] = max_depth;
+    g_plane[2] = half_x;
+    g_plane[3] = half_y;
+    g_plane_excl.assign(exclude, exclude + (n_exclude > 0 ? n_exclude : 0));
+}
 
 void phyzref_set_heightfield(uint32_t nx, uint32_t ny, float ox, float oy, float oz, float cell,
                              const float* heights) {
@@ -138,6 +162,9 @@ void phyzref_pack_cparams(uint32_t nworld, uint32_t nb, uint32_t nv, float groun
 // The host rollouts' header of the heightfield set by phyzref_set_heightfield
 // (ContactParams::set_heightfield, contact_pipeline.rs:101-108).
 static void apply_heightfield(float* cp) {
+    cp[6] = bits_i(g_plane_body);
+    if (g_plane_body >= 0)
+        for (int k = 0; k < 4; k++) cp[7 + k] = g_plane[k];
     cp[11] = bits_u(g_hf_nx);
     cp[12] = bits_u(g_hf_ny);
     cp[13] = g_hf_o[0];

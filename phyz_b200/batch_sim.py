@@ -34,6 +34,20 @@ class PdDof:
 
 
 @dataclass
+class BodyPlane:
+    """phyz_gpu::BodyPlane (contact_pipeline.rs:318-355): a contact face at
+    `offset` along body `body`'s +z, `half_x` x `half_y` in its x/y;
+    penetrations beyond `max_depth` are ignored; `exclude` never touch it."""
+
+    body: int
+    offset: float = 0.0
+    max_depth: float = 0.05
+    half_x: float = 0.5
+    half_y: float = 0.5
+    exclude: tuple = ()
+
+
+@dataclass
 class BodyContactGains:
     """phyz_gpu::BodyContactGains (contact_pipeline.rs:277-305)."""
 

@@ -157,6 +157,11 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     a.hf_oy = s->hf_o[1];
     a.hf_oz = s->hf_o[2];
     a.hf_cell = s->hf_cell;
+    a.plane_body = s->cfg.contact ? s->cfg.plane_body : -1;
+    a.plane_offset = s->plane[0];
+    a.plane_max_depth = s->plane[1];
+    a.plane_half_x = s->plane[2];
+    a.plane_half_y = s->plane[3];
     return a;
 }
 
@@ -268,8 +273,20 @@ int upload_heightfield(phyzb_sim* s, const phyzb_heightfield* hf) {
 
 int set_contact(phyzb_sim* s, double ground, double friction, const double* k, const double* d, bool impulse,
                 const phyzb_body_plane* plane = nullptr, const phyzb_heightfield* hf = nullptr) {
-    if (plane)
-        return fail(PHYZB_ERR_UNSUPPORTED, "a body-attached contact plane is not available in this build");
+    if (plane) {  // contact_pipeline.rs:614-627
+        if (plane->body < 0 || plane->body >= s->nb)
+            return fail(PHYZB_ERR_INVALID, "plane body " + std::to_string(plane->body) +
+                                               " out of range for a model with " + std::to_string(s->nb) + " bodies");
+        if (plane->n_exclude < 0 || (plane->n_exclude > 0 && !plane->exclude))
+            return fail(PHYZB_ERR_INVALID, "plane exclude list is null");
+        for (int k = 0; k < plane->n_exclude; k++)
+            if (plane->exclude[k] < 0 || plane->exclude[k] >= s->nb)
+                return fail(PHYZB_ERR_INVALID, "plane exclude body " + std::to_string(plane->exclude[k]) +
+                                                   " out of range");
+        const double pv[4] = {plane->offset, plane->max_depth, plane->half_x, plane->half_y};
+        for (double x : pv)
+            if (!std::isfinite(x)) return fail(PHYZB_ERR_INVALID, "plane parameters must be finite");
+    }
     if (hf) PZ_TRY(check_heightfield(hf));
     int collidable = 0;
     for (int i = 0; i < s->nb; i++)
@@ -304,6 +321,15 @@ int set_contact(phyzb_sim* s, double ground, double friction, const double* k, c
     s->cfg.contact = true;
     s->cfg.impulse = impulse;
     s->cfg.terrain = hf != nullptr;
+    s->cfg.plane_body = plane ? plane->body : -1;
+    s->cfg.plane_exclude.clear();
+    if (plane) {
+        s->cfg.plane_exclude.assign(plane->exclude, plane->exclude + plane->n_exclude);
+        s->plane[0] = plane->offset;
+        s->plane[1] = plane->max_depth;
+        s->plane[2] = plane->half_x;
+        s->plane[3] = plane->half_y;
+    }
     s->cfg.gk.assign(k, k + s->nb);
     s->cfg.gd.assign(d, d + s->nb);
     s->ground_h = ground;

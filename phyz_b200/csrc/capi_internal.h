@@ -103,6 +103,7 @@ struct phyzb_sim {
     size_t hf_cap = 0;
     int hf_nx = 0, hf_ny = 0;
     double hf_o[3] = {0, 0, 0}, hf_cell = 1.0;
+    double plane[4] = {0, 0, 0, 0};  // offset, max_depth, half_x, half_y (cfg.plane_body >= 0)
     int* status = nullptr;
     // lay[0]: every record in shared memory (the objective kernel's layout
     // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the

@@ -163,6 +163,7 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     // detection, the force law is not
     static const float hf_nodes[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     M.ter = Terrain<Cnt>{hf_nodes, 2, 2, Cnt(-1.0), Cnt(-1.0), Cnt(-1e9), Cnt(1.0)};
+    M.plane = PlaneT<Cnt>{-1, Cnt(0.0), Cnt(0.0), Cnt(0.0), Cnt(0.0)};  // plane contacts are not counted
 
     std::vector<Cnt> scratch(info.scratch > 0 ? info.scratch : 1, Cnt(0.0));
     HostScr S{scratch.data()};

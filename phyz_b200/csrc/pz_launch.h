@@ -45,6 +45,9 @@ struct RolloutArgs {
     const float* hf;
     int hf_nx, hf_ny;
     double hf_ox, hf_oy, hf_oz, hf_cell;
+    // body-attached contact plane (contact variants; plane_body -1: none)
+    int plane_body;
+    double plane_offset, plane_max_depth, plane_half_x, plane_half_y;
 };
 
 // tmem_cols > 0: configure the Tensor-Memory variant for a layout whose

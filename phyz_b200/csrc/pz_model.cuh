@@ -39,6 +39,8 @@ enum BodyFlags {
     F_ZHINGE = 1 << 8,    // hinge about z of its (relabelled) frame; parent->joint rotation
                           // is the cyclic relabelling `qshift` (the kernel's fast path)
     F_PD = 1 << 9,        // a DOF of this body is driven by a PD servo
+    F_PLANE = 1 << 10,    // touches the body-attached contact plane
+    F_EXTF = 1 << 11,     // receives an external wrench (s_f): collidable, or the plane's body
 };
 
 template <class T>
@@ -64,7 +66,7 @@ struct alignas(16) BodyI {
     int s_vw;         // body velocity (6) between passes 1 and 2, then W = U D^-1 (6*ndof)
     int s_w0;         // control input of the step (unless s_in is separate), then D^-1 u (ndof)
     int s_in;         // control input of the step (ndof): s_w0, or its own slots in impulse mode
-    int s_f;          // contact wrench, body frame (6)
+    int s_f;          // external (contact) wrench, body frame (6): F_EXTF bodies
     int s_acc;        // branch: accumulated child inertia (21) + bias force (6)
     int s_vold;       // branch: velocity of the step being finished (6)
     int s_acca;       // branch: acceleration (6)
@@ -77,10 +79,11 @@ struct alignas(16) BodyI {
     int s_up;         // collidable: world up in the body frame (3) and origin height (1); with
                       // a heightfield the frame of s_wx (12)
     int s_imp;        // collidable: staged impulses [normal, tangent u, tangent w] per point
-    int s_vf;         // branch: free velocity v + dt qdd of the sweep (6)
+    int s_vf;         // branch, plane participant: free velocity v + dt qdd of the sweep (6)
     int c_imp;        // collidable: first row of the body's wrench (6) + impulses in the
                       // persistent impulse buffer
     int fshift;       // this body's frame relabelling: stored = P_fshift (original coordinates)
+    int s_pimp;       // impulse mode, F_PLANE: staged impulses against the plane per point
 };
 
 template <class T>
@@ -98,6 +101,15 @@ struct Terrain {
     const float* h;
     int nx, ny;
     T ox, oy, oz, cell;
+};
+
+// A contact plane attached to a body (contact_pipeline.rs:318-355): the face
+// at `offset` along the body's own +z (original, unrelabelled frame),
+// half_x x half_y in its x/y, penetrations beyond max_depth ignored.
+template <class T>
+struct PlaneT {
+    int body;  // -1: none
+    T offset, max_depth, half_x, half_y;
 };
 
 // Impulse-mode contact material (contact_pipeline.rs:85-95): ground height,
@@ -124,6 +136,7 @@ struct ModelView {
     T kstiff_c;            // 4 / max(dt, 1e-9)^2
     ImpMat<T> im;          // impulse-mode contact material
     Terrain<T> ter;        // heightfield (feature bit 32)
+    PlaneT<T> plane;       // body-attached plane (contact variants)
 };
 
 }  // namespace pz

@@ -6,6 +6,7 @@
 // simulator's precision (f32 or f64) instead of always f32.
 #pragma once
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -87,6 +88,8 @@ struct PackCfg {
     bool contact = false;
     bool impulse = false;                // contact as the velocity-level impulse solve
     bool terrain = false;                // contact against a heightfield (full world frames)
+    int plane_body = -1;                 // body carrying a contact plane (-1: none)
+    std::vector<int> plane_exclude;      // bodies that never touch the plane
     std::vector<double> gk, gd;          // per-body penalty gains (contact)
     std::vector<phyzb_pd_dof> pd;        // PD servos
 };
@@ -308,13 +311,18 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.s_in = next;
             next += nd;
         }
-        d.s_f = d.s_up = d.s_imp = d.s_vf = d.c_imp = -1;
+        d.s_f = d.s_up = d.s_imp = d.s_vf = d.c_imp = d.s_pimp = -1;
+        const bool plane = cfg.contact && cfg.plane_body >= 0;
+        const bool on_plane = plane && b.geom_type != 0 && i != cfg.plane_body &&
+                              std::find(cfg.plane_exclude.begin(), cfg.plane_exclude.end(), i) ==
+                                  cfg.plane_exclude.end();
+        const bool is_pb = plane && i == cfg.plane_body;
+        const int npts = b.geom_type == 2 ? 8 : 1;
         if (cfg.contact && b.geom_type != 0) {
-            flags |= F_CONTACT;
+            flags |= F_CONTACT | F_EXTF;
             d.s_f = next;
             next += 6;
             if (impulse) {
-                const int npts = b.geom_type == 2 ? 8 : 1;
                 d.s_up = next;
                 next += cfg.terrain ? 12 : 4;
                 d.s_imp = next;
@@ -322,6 +330,26 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
                 d.c_imp = info.imp_slots;
                 info.imp_slots += 6 + 3 * npts;
             }
+        } else if (is_pb) {  // the plane's body takes the reaction even without a shape
+            flags |= F_EXTF;
+            d.s_f = next;
+            next += 6;
+            if (impulse) {
+                d.c_imp = info.imp_slots;
+                info.imp_slots += 6;
+            }
+        }
+        if (on_plane) {
+            flags |= F_PLANE;
+            if (impulse) {
+                d.s_pimp = next;
+                next += 3 * npts;
+                info.imp_slots += 3 * npts;  // after the ground impulses in the persistent rows
+            }
+        }
+        if (impulse && (on_plane || is_pb)) {
+            d.s_vf = next;  // the plane pass reads both bodies' free velocities
+            next += 6;
         }
         d.s_acc = d.s_vold = d.s_acca = d.s_wx = -1;
         if (flags & F_BRANCH) {
@@ -335,7 +363,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
                 d.s_wx = next;  // world up (3) and origin height (1), or the full frame (12)
                 next += cfg.terrain ? 12 : 4;
             }
-            if (impulse) {
+            if (impulse && d.s_vf < 0) {
                 d.s_vf = next;
                 next += 6;
             }

@@ -1270,8 +1270,14 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const Body
         f.l = f.l + fb;
         any = true;
     }
-    if (!any)
+    if (!any) {
         for (int k = 0; k < 3 * npts; k++) S(bi.s_imp + k) = T(0);
+        // the reference clears the body's whole contact-state row here
+        // (phyz_kernels.cu:966-969), its plane impulses included: a body off
+        // the ground starts every sweep's plane update from zero
+        if (bi.s_pimp >= 0)
+            for (int k = 0; k < 3 * npts; k++) S(bi.s_pimp + k) = T(0);
+    }
     return f;
 }
 
@@ -1333,6 +1339,164 @@ PZ_HD void contact_state_impulse_pass(const ModelView<T>& M, const Scr& S, const
     }
 }
 
+// ── body-attached contact plane (phyz_kernels.cu:983-1132) ───────────────
+// R x and R^T y for a body->world rotation held as its rows.
+template <class T>
+PZ_HD V3<T> wf_mul(const WF<T>& f, const V3<T>& x) {
+    return mk3<T>(dot(f.r0, x), dot(f.r1, x), dot(f.up, x));
+}
+template <class T>
+PZ_HD V3<T> wf_tmul(const WF<T>& f, const V3<T>& y) {
+    return f.r0 * y.x + f.r1 * y.y + f.up * y.z;
+}
+// A body-frame vector between the stored (relabelled) and the original
+// coordinates of a body with frame shift s.
+template <class T>
+PZ_HD V3<T> to_stored(int s, const V3<T>& v) {
+    return s == 1 ? cperm<1>(v) : (s == 2 ? cperm<2>(v) : v);
+}
+template <class T>
+PZ_HD V3<T> to_original(int s, const V3<T>& v) {
+    return s == 1 ? cperm<2>(v) : (s == 2 ? cperm<1>(v) : v);
+}
+
+// Every F_PLANE body against the plane: the action on the body and the
+// reaction on the plane's body at one shared point, added to both wrench
+// slots (the plane body's slot is cleared first unless its own ground
+// contact has just written it). Penalty mode (the gains of the touching
+// body, the pair's series effective mass bounding them) reads the body
+// velocities of pass 1; impulse mode the sweep's free velocities and the
+// staged impulses of the plane slots. Every lane runs every body (record
+// loads are warp-wide); per-world tests only skip arithmetic.
+template <bool IMPULSE, int FEAT, class T, class Scr>
+PZ_HD void plane_pass(const ModelView<T>& M, const Scr& S) {
+    const int pb = M.plane.body;
+    const BodyI bp = M.bi[pb];
+    const BodyT<T>& tp = M.bt[pb];
+    if (!(bp.flags & F_CONTACT))
+        for (int k = 0; k < 6; k++) S(bp.s_f + k) = T(0);
+    const WF<T> fp = world_frame<FEAT>(M, S, pb);
+    SV<T> vpb;
+    if constexpr (IMPULSE)
+        vpb = ld_sv<T>(S, bp.s_vf);
+    else
+        vpb = ld_vel<T>(S, bp);
+    const T dtc = pz_max(M.dt, T(1e-9));
+    const V3<T> ez = to_stored<T>(bp.fshift, mk3<T>(T(0), T(0), T(1)));  // the body's own +z
+    const V3<T> n_w = wf_mul(fp, ez);
+    const V3<T> p0_w = fp.pos + wf_mul(fp, ez * M.plane.offset);
+    const V3<T> n_p = wf_tmul(fp, n_w);
+    SV<T> fpb = zerosv<T>();
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        if (!(bi.flags & F_PLANE)) continue;  // a model constant: uniform over the warp
+        const BodyT<T>& bt = M.bt[i];
+        const WF<T> fi = world_frame<FEAT>(M, S, i);
+        SV<T> vi;
+        if constexpr (IMPULSE)
+            vi = ld_sv<T>(S, bi.s_vf);
+        else
+            vi = ld_vel<T>(S, bi);
+        const V3<T> n_i = wf_tmul(fi, n_w);
+        const int npts = bi.gtype == 2 ? 8 : 1;
+        const T pt_scale = bi.gtype == 2 ? T(0.25) : T(1);
+        // the shape's footprint in face coordinates (the plane body's original
+        // x, y), intersected with the face
+        T lo_x = T(1e30), lo_y = T(1e30), hi_x = T(-1e30), hi_y = T(-1e30);
+        int active = 0;
+        for (int c = 0; c < npts; c++) {
+            const V3<T> sw = fi.pos + wf_mul(fi, support_pt(bi, bt, n_i, c));
+            const V3<T> rp = to_original(bp.fshift, wf_tmul(fp, sw - fp.pos));
+            lo_x = pz_min(lo_x, rp.x);
+            lo_y = pz_min(lo_y, rp.y);
+            hi_x = pz_max(hi_x, rp.x);
+            hi_y = pz_max(hi_y, rp.y);
+            const T d = -dot(sw - p0_w, n_w);
+            if (d > T(0) && d <= M.plane.max_depth) active++;
+        }
+        const T ox0 = pz_max(lo_x, -M.plane.half_x), oy0 = pz_max(lo_y, -M.plane.half_y);
+        const T ox1 = pz_min(hi_x, M.plane.half_x), oy1 = pz_min(hi_y, M.plane.half_y);
+        // no overlap: no contact (a per-world test, so the loop below is
+        // skipped rather than the body: the next body's record loads stay
+        // converged)
+        const bool overlap = !(ox0 > ox1 || oy0 > oy1);
+        const T na = T(active > 1 ? active : 1);
+        SV<T> f = zerosv<T>();
+        for (int c = 0; c < (overlap ? npts : 0); c++) {
+            const V3<T> sup = support_pt(bi, bt, n_i, c);
+            const V3<T> sw0 = fi.pos + wf_mul(fi, sup);
+            const T pen = -dot(sw0 - p0_w, n_w);
+            if (!(pen > T(0)) || pen > M.plane.max_depth) {
+                if constexpr (IMPULSE) {
+                    S(bi.s_pimp + 3 * c) = T(0);
+                    S(bi.s_pimp + 3 * c + 1) = T(0);
+                    S(bi.s_pimp + 3 * c + 2) = T(0);
+                }
+                continue;
+            }
+            // the point in the face, clamped into the overlap: one world
+            // point, a lever on each body
+            V3<T> ro = to_original(bp.fshift, wf_tmul(fp, sw0 - fp.pos));
+            ro.x = pz_min(pz_max(ro.x, ox0), ox1);
+            ro.y = pz_min(pz_max(ro.y, oy0), oy1);
+            const V3<T> r_p = to_stored(bp.fshift, ro);
+            const V3<T> sw = fp.pos + wf_mul(fp, r_p);
+            const V3<T> sc = wf_tmul(fi, sw - fi.pos);
+            const V3<T> v_rel = wf_mul(fi, vi.l + cross(vi.w, sc)) - wf_mul(fp, vpb.l + cross(vpb.w, r_p));
+            const T vn = dot(v_rel, n_w);
+            auto pair_mass = [&](const V3<T>& dir_w) {
+                return T(1) / (T(1) / eff_mass(bt, sc, wf_tmul(fi, dir_w)) + T(1) / eff_mass(tp, r_p, wf_tmul(fp, dir_w)));
+            };
+            const T m_n = T(1) / (T(1) / eff_mass(bt, sc, n_i) + T(1) / eff_mass(tp, r_p, n_p));
+            V3<T> f_w;
+            if constexpr (IMPULSE) {
+                const int slot = bi.s_pimp + 3 * c;
+                V3<T> pu, pw;
+                contact_tangents(n_w, pu, pw);  // world frame: no relabelling enters
+                const T bu = dot(v_rel, pu), bw = dot(v_rel, pw);
+                const T ann = na / pz_max(m_n, T(1e-9));
+                const T bias = impedance_at(M.im, pen) * M.im.erp * pz_max(pen, T(0)) / dtc;
+                const T e = effective_restitution(M.im, M.im.restitution, pz_min(vn, T(0)));
+                const T fn = pz_max((bias - (vn * (T(1) + e) - ann * S(slot))) / ann, T(0));
+                const T auu = na / pz_max(pair_mass(pu), T(1e-9));
+                const T aww = na / pz_max(pair_mass(pw), T(1e-9));
+                T ju = -(bu - auu * S(slot + 1)) / auu;
+                T jw = -(bw - aww * S(slot + 2)) / aww;
+                const T lim = M.friction * fn;
+                const T jt = pz_sqrt(ju * ju + jw * jw);
+                if (jt > lim) {
+                    const T scl = jt > T(0) ? lim / jt : T(0);
+                    ju = ju * scl;
+                    jw = jw * scl;
+                }
+                S(slot) = fn;
+                S(slot + 1) = ju;
+                S(slot + 2) = jw;
+                f_w = (n_w * fn + pu * ju + pw * jw) * (T(1) / dtc);
+            } else {
+                const T kb = pz_min(pt_scale * bt.gk, M.kstiff_c * m_n);
+                const T db = pz_min(pt_scale * bt.gd, M.inv_dt_c * m_n);
+                const T fn = pz_max(kb * pen - db * vn, T(0));
+                const V3<T> vt3 = v_rel - n_w * vn;
+                const T vt = pz_sqrt(dot(vt3, vt3));
+                f_w = n_w * fn;
+                if (vt > T(1e-6)) {
+                    const V3<T> td = vt3 * (T(1) / vt);
+                    const T coul = (M.friction * fn) * pz_min(T(1), vt / T(1e-3));
+                    f_w = f_w - td * pz_min(coul, (M.inv_dt_c * pair_mass(td)) * vt);
+                }
+            }
+            const V3<T> fib = wf_tmul(fi, f_w), fpbb = wf_tmul(fp, f_w * T(-1));
+            f.w = f.w + cross(sc, fib);
+            f.l = f.l + fib;
+            fpb.w = fpb.w + cross(r_p, fpbb);
+            fpb.l = fpb.l + fpbb;
+        }
+        st_sv(S, bi.s_f, ld_sv<T>(S, bi.s_f) + f);
+    }
+    st_sv(S, bp.s_f, ld_sv<T>(S, bp.s_f) + fpb);
+}
+
 // Run f<AX>() for the body's kind.
 #define PZ_BY_KIND(kind, CALL) \
     if ((kind) == 2) {         \
@@ -1377,7 +1541,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
     SV<T> bias = crf(v, hv);
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
-        if (bi.flags & F_CONTACT) bias = bias - ld_sv<T>(S, bi.s_f);
+        if (bi.flags & F_EXTF) bias = bias - ld_sv<T>(S, bi.s_f);
     }
     pA = pA + bias;
     if (bi.flags & F_BRANCH) {
@@ -1754,8 +1918,8 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     if (bi.flags & F_BRANCH) {
         st_sv(S, bi.s_vold, vo);
         st_sv(S, bi.s_acca, a);
-        st_sv(S, bi.s_vf, vf);
     }
+    if (bi.s_vf >= 0) st_sv(S, bi.s_vf, vf);  // a branch, or a body the plane pass reads
     cvo = vo;
     ca = a;
     cvf = vf;

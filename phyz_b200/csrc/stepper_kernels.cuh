@@ -203,6 +203,11 @@ __device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const
     M.ter.oy = T(P.hf_oy);
     M.ter.oz = T(P.hf_oz);
     M.ter.cell = T(P.hf_cell);
+    M.plane.body = P.plane_body;
+    M.plane.offset = T(P.plane_offset);
+    M.plane.max_depth = T(P.plane_max_depth);
+    M.plane.half_x = T(P.plane_half_x);
+    M.plane.half_y = T(P.plane_half_y);
     return M;
 }
 
@@ -269,9 +274,14 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
             for (int i = 0; i < M.nb; i++) {
                 const BodyI bi = M.bi[i];
                 if (bi.c_imp < 0) continue;
-                const int nimp = 3 * (bi.gtype == 2 ? 8 : 1);
-                for (int k = 0; k < 6; k++) S(bi.s_f + k) = P.imp[(long long)(bi.c_imp + k) * N + w];
-                for (int k = 0; k < nimp; k++) S(bi.s_imp + k) = P.imp[(long long)(bi.c_imp + 6 + k) * N + w];
+                // rows: wrench (6), ground impulses, plane impulses (3 per point each)
+                const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
+                int r = bi.c_imp;
+                for (int k = 0; k < 6; k++) S(bi.s_f + k) = P.imp[(long long)(r++) * N + w];
+                if (bi.s_imp >= 0)
+                    for (int k = 0; k < np3; k++) S(bi.s_imp + k) = P.imp[(long long)(r++) * N + w];
+                if (bi.s_pimp >= 0)
+                    for (int k = 0; k < np3; k++) S(bi.s_pimp + k) = P.imp[(long long)(r++) * N + w];
             }
         }
         const Out<T> none{nullptr, 0};
@@ -285,11 +295,16 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
                 if (last && P.contact && P.cstate)
                     contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
+            if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
+                // the plane contacts of this step's state join the ground wrenches of pass 1
+                if (M.plane.body >= 0) plane_pass<false, FEAT>(M, S);
+            }
             pass2<FEAT>(M, S);
             if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
                 // sweeps x [contact at the free velocity -> backward sweep]
                 for (int k = 0; k < P.sweeps; k++) {
                     sweep_forward<FEAT>(M, S);
+                    if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
                     pass2<FEAT>(M, S);
                 }
                 if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
@@ -306,9 +321,13 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
                 for (int i = 0; i < M.nb; i++) {
                     const BodyI bi = M.bi[i];
                     if (bi.c_imp < 0) continue;
-                    const int nimp = 3 * (bi.gtype == 2 ? 8 : 1);
-                    for (int k = 0; k < 6; k++) P.imp[(long long)(bi.c_imp + k) * N + w] = S(bi.s_f + k);
-                    for (int k = 0; k < nimp; k++) P.imp[(long long)(bi.c_imp + 6 + k) * N + w] = S(bi.s_imp + k);
+                    const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
+                    int r = bi.c_imp;
+                    for (int k = 0; k < 6; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_f + k);
+                    if (bi.s_imp >= 0)
+                        for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_imp + k);
+                    if (bi.s_pimp >= 0)
+                        for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_pimp + k);
                 }
         }
         if (active) {

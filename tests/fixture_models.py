@@ -71,6 +71,50 @@ def free_box(pos=(0.0, 0.0, 0.5), half=(0.1, 0.1, 0.1), mass=1.0):
             .build())
 
 
+def deck_and_riders(nriders=2):
+    """A free deck (a thin box resting on the ground) with free riders dropped
+    onto its top face: the setting of a body-attached contact plane
+    (contact_pipeline.rs:318-355; the deck is body 0)."""
+    b = ModelBuilder().gravity([0.0, 0.0, -9.81]).dt(0.001)
+    hx, hy, hz, m = 0.3, 0.15, 0.02, 2.0
+    c = m / 3.0
+    b.add_free_body("deck", -1, Transform.from_translation([0.0, 0.0, 0.02]),
+                    SpatialInertia.new(m, np.zeros(3), np.diag([c * (hy * hy + hz * hz), c * (hx * hx + hz * hz),
+                                                                c * (hx * hx + hy * hy)])),
+                    geometry=Geometry.box(hx, hy, hz))
+    for k in range(nriders):
+        x = -0.15 + 0.3 * k / max(nriders - 1, 1)
+        if k % 2 == 0:
+            b.add_free_body(f"rider{k}", -1, Transform.from_translation([x, 0.0, 0.25]), iso(0.5, 0.4 * 0.5 * 0.05 ** 2),
+                            geometry=Geometry.sphere(0.05))
+        else:
+            r = 0.04
+            b.add_free_body(f"rider{k}", -1, Transform.from_translation([x, 0.02, 0.3]),
+                            SpatialInertia.new(0.4, np.zeros(3), np.eye(3) * (0.4 * 2 * r * r / 3.0)),
+                            geometry=Geometry.box(r, r, r))
+    return b.build()
+
+
+def seesaw_and_riders():
+    """A plank on a hinge about y (a body whose frame the kernel relabels)
+    carrying a contact plane on its top face, with free riders dropped off
+    centre so the plank tips."""
+    b = ModelBuilder().gravity([0.0, 0.0, -9.81]).dt(0.001)
+    hx, hy, hz, m = 0.4, 0.1, 0.02, 3.0
+    c = m / 3.0
+    b.add_revolute_body("plank", -1, Transform.from_translation([0.0, 0.0, 0.3]),
+                        SpatialInertia.new(m, np.zeros(3), np.diag([c * (hy * hy + hz * hz), c * (hx * hx + hz * hz),
+                                                                    c * (hx * hx + hy * hy)])),
+                        axis=(0.0, 1.0, 0.0), geometry=Geometry.box(hx, hy, hz))
+    b.add_free_body("ball", -1, Transform.from_translation([0.25, 0.0, 0.5]), iso(0.6, 0.4 * 0.6 * 0.05 ** 2),
+                    geometry=Geometry.sphere(0.05))
+    r = 0.04
+    b.add_free_body("cube", -1, Transform.from_translation([-0.1, 0.03, 0.45]),
+                    SpatialInertia.new(0.4, np.zeros(3), np.eye(3) * (0.4 * 2 * r * r / 3.0)),
+                    geometry=Geometry.box(r, r, r))
+    return b.build()
+
+
 def single_step_cases():
     """(label, model, q, v, tolerance in the reference's f32 suite)."""
     cases = []

@@ -139,15 +139,3 @@ def test_tensor_memory_layout_agrees(monkeypatch):
             res[(mode, impulse)] = tr[-1]
     for impulse in (False, True):
         assert rel_err(res[("1", impulse)], res[("0", impulse)]) < 1e-3
-
-
-def test_body_plane_is_reported_unsupported():
-    from types import SimpleNamespace
-
-    m, q0, v0, c = inputs("c3_quadruped", 4)
-    sim = BatchSim(m, 4)
-    plane = SimpleNamespace(body=0, offset=0.1, max_depth=0.05, half_x=0.3, half_y=0.2, exclude=[])
-    with pytest.raises(PhyzbError) as e:
-        sim.enable_contact_terrain(0.0, 1.0, gains(m), plane=plane)
-    assert e.value.code == _lib.ERR_UNSUPPORTED
-    sim.close()

@@ -83,11 +83,14 @@ def test_sweep_count_changes_the_solve_and_both_engines_agree(oracle, refhost):
 
 def as_ref_state(st, n, nb):
     """The oracle's warm-start state in the reference's buffers: ext_forces
-    [n][nb][6] and contact_state [n][nb][56] with the impulses at
-    CS_IMPULSE_OFF = 8 (phyz_kernels.cu:502-505)."""
+    [n][nb][6] and contact_state [n][nb][56] with the ground impulses at
+    CS_IMPULSE_OFF = 8 and the plane's at CS_PLANE_OFF = 32
+    (phyz_kernels.cu:502-505)."""
     ext = st[:, :nb * 6].reshape(n, nb, 6).astype(np.float32)
     cs = np.zeros((n, nb, 56), np.float32)
-    cs[:, :, 8:8 + 3 * IMPULSE_PTS] = st[:, nb * 6:].reshape(n, nb, 3 * IMPULSE_PTS)
+    g = nb * 6 + nb * 3 * IMPULSE_PTS
+    cs[:, :, 8:8 + 3 * IMPULSE_PTS] = st[:, nb * 6:g].reshape(n, nb, 3 * IMPULSE_PTS)
+    cs[:, :, 32:32 + 3 * IMPULSE_PTS] = st[:, g:].reshape(n, nb, 3 * IMPULSE_PTS)  # CS_PLANE_OFF
     return ext, cs
 
 
@@ -122,4 +125,4 @@ def test_articulated_contact_matches_the_reference_kernel(oracle, refhost, name)
     assert np.mean(dq < 2e-6) >= 0.9, np.sort(dq)[-8:]
     assert np.max(dq) < 1e-3, np.sort(dq)[-8:]
     # the warm-start state has the layout the oracle documents
-    assert st.shape == (n, nb * 6 + nb * IMPULSE_PTS * 3)
+    assert st.shape == (n, nb * 6 + 2 * nb * IMPULSE_PTS * 3)
