@@ -317,10 +317,16 @@ int set_contact(phyzb_sim* s, double ground, double friction, const double* k, c
         PZ_CUDA(cudaMalloc(&s->hf, nodes * sizeof(float)));
         s->hf_cap = nodes;
     }
-    if (hf) PZ_TRY(upload_heightfield(s, hf));
+    if (hf) {
+        PZ_TRY(upload_heightfield(s, hf));
+    } else {  // no terrain: the flat ground (a plane alone also runs the full-frame kernel)
+        s->hf_nx = s->hf_ny = 0;
+    }
     s->cfg.contact = true;
     s->cfg.impulse = impulse;
-    s->cfg.terrain = hf != nullptr;
+    // full world frames (kernel feature bit 32) serve both the heightfield
+    // and the body-attached plane
+    s->cfg.terrain = hf != nullptr || plane != nullptr;
     s->cfg.plane_body = plane ? plane->body : -1;
     s->cfg.plane_exclude.clear();
     if (plane) {

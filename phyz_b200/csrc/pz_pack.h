@@ -76,7 +76,7 @@ struct PackInfo {
     int collidable = 0;  // bodies with a contact shape
     int feat = 0;        // kernel variant: 1 = ball/free joints, 2 = contact on, 4 = relabelled hinges,
                          // 8 = (with 4) every relabel is the shift-1 cycle, 16 = (with 2) impulse contact,
-                         // 32 = (with 2) heightfield terrain
+                         // 32 = (with 2) full world frames (heightfield / body plane)
     int tmem_cols = 0;   // Tensor Memory columns per world holding body records (0: none)
     int imp_slots = 0;   // impulse mode: rows per world of the persistent wrench + impulse buffer
 };
@@ -87,7 +87,7 @@ inline int pad16(int b) { return (b + 15) & ~15; }
 struct PackCfg {
     bool contact = false;
     bool impulse = false;                // contact as the velocity-level impulse solve
-    bool terrain = false;                // contact against a heightfield (full world frames)
+    bool terrain = false;                // full world frames: a heightfield and/or a body plane
     int plane_body = -1;                 // body carrying a contact plane (-1: none)
     std::vector<int> plane_exclude;      // bodies that never touch the plane
     std::vector<double> gk, gd;          // per-body penalty gains (contact)

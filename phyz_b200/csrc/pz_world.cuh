@@ -37,8 +37,9 @@ namespace pz {
 // FEAT_PERM) every relabelled hinge relabelled by the same shift 1 -- a chain
 // whose axes cycle x, y, z -- so the relabel is a compile-time register
 // renaming instead of a run-time branch; and (with FEAT_CONTACT) contact as
-// the velocity-level impulse solve instead of the penalty law, and against a
-// heightfield instead of the flat plane (full world frames carried).
+// the velocity-level impulse solve instead of the penalty law, and with full
+// world frames carried (FEAT_TERRAIN): a heightfield in place of the flat
+// ground and/or a body-attached contact plane.
 enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8, FEAT_IMPULSE = 16, FEAT_TERRAIN = 32 };
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
@@ -812,6 +813,12 @@ PZ_HD GroundHit<TERRAIN, T> ground_hit(const Terrain<T>& ter, const T& ground_h,
     GroundHit<TERRAIN, T> g;
     if constexpr (TERRAIN) {
         g.w = mk3<T>(wf.pos.x + dot(wf.r0, sup), wf.pos.y + dot(wf.r1, sup), wf.pos.z + dot(wf.up, sup));
+        if (ter.nx < 1) {  // full frames for a body-attached plane, over the flat ground
+            g.h = ground_h;
+            g.pen = ground_h - g.w.z;
+            g.n = wf.up;
+            return g;
+        }
         V3<T> nw;
         g.h = terrain_at(ter, g.w.x, g.w.y, nw);
         g.pen = nw.z * (g.h - g.w.z);

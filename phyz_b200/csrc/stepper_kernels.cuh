@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
                 if (last && P.contact && P.cstate)
                     contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
-            if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
+            if constexpr ((FEAT & FEAT_TERRAIN) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
                 // the plane contacts of this step's state join the ground wrenches of pass 1
                 if (M.plane.body >= 0) plane_pass<false, FEAT>(M, S);
             }
@@ -304,7 +304,8 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
                 // sweeps x [contact at the free velocity -> backward sweep]
                 for (int k = 0; k < P.sweeps; k++) {
                     sweep_forward<FEAT>(M, S);
-                    if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
+                    if constexpr ((FEAT & FEAT_TERRAIN) != 0)
+                        if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
                     pass2<FEAT>(M, S);
                 }
                 if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
