@@ -177,6 +177,7 @@ class Model:
     bodies: list
     gravity: np.ndarray
     dt: float
+    actuators: list = field(default_factory=list)  # MJCF actuators (phyz_b200.mjcf.Actuator)
 
     @property
     def nbodies(self) -> int:
