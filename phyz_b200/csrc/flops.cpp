@@ -189,9 +189,10 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
             pass1_all<ATI>(M, S);
             g_tally = Tally{};
             pass2<ATI>(M, S);
+            keep_backward_state(M, S);
             for (int k = 0; k < sweeps; k++) {
                 sweep_forward<ATI>(M, S);
-                pass2<ATI>(M, S);
+                wrench_response<ATI>(M, S);
             }
             pass3_next<ATI, false>(M, S, io, 1, none);
         } else {
@@ -206,9 +207,10 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
         // sweep with contact, backward sweep], the fused finish/start sweep
         g_tally = Tally{};
         pass2<ALLI>(M, S);
+        keep_backward_state(M, S);
         for (int k = 0; k < sweeps; k++) {
             sweep_forward<ALLI>(M, S);
-            pass2<ALLI>(M, S);
+            wrench_response<ALLI>(M, S);
         }
         pass3_next<ALLI, false>(M, S, io, 1, none);
     } else {

@@ -304,12 +304,15 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
         d.s_w0 = next;
         next += nd;
         const bool impulse = cfg.contact && cfg.impulse;
-        // impulse mode runs the backward sweep several times per step, so the
-        // control input keeps slots of its own
         d.s_in = d.s_w0;
+        d.s_dinv = d.s_w0b = d.s_fp = -1;
         if (impulse) {
-            d.s_in = next;
+            // the sweeps rewrite w0 from the step's own (s_w0b) plus the
+            // response to the wrench change, through D^-1 (s_dinv)
+            d.s_w0b = next;
             next += nd;
+            d.s_dinv = next;
+            next += nd > 1 ? nd * (nd + 1) / 2 : 1;
         }
         d.s_f = d.s_up = d.s_imp = d.s_vf = d.c_imp = d.s_pimp = -1;
         const bool plane = cfg.contact && cfg.plane_body >= 0;
@@ -323,6 +326,10 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.s_f = next;
             next += 6;
             if (impulse) {
+                d.s_fp = next;
+                next += 6;
+            }
+            if (impulse) {
                 d.s_up = next;
                 next += cfg.terrain ? 12 : 4;
                 d.s_imp = next;
@@ -334,6 +341,10 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             flags |= F_EXTF;
             d.s_f = next;
             next += 6;
+            if (impulse) {
+                d.s_fp = next;
+                next += 6;
+            }
             if (impulse) {
                 d.c_imp = info.imp_slots;
                 info.imp_slots += 6;

@@ -629,6 +629,12 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
             L[b][a] = e * inv;
         }
     }
+    if (bi.s_dinv >= 0) {  // impulse mode: the factor the sweeps' wrench response solves with
+#pragma unroll
+        for (int a = 0; a < ND; a++)
+#pragma unroll
+            for (int b = 0; b <= a; b++) S(bi.s_dinv + a * (a + 1) / 2 + b) = ok ? L[a][b] : T(0);
+    }
     if (!ok) {
 #pragma unroll
         for (int k = 0; k < 6 * ND; k++) S(bi.s_vw + k) = T(0);
@@ -1608,6 +1614,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         // a Tensor-Memory store is warp-wide.
         live = !(pz_abs(D) < T(1e-20));
         const T invD = live ? T(1) / D : T(0);
+        if constexpr ((FEAT & FEAT_IMPULSE) != 0) S(bi.s_dinv) = invD;  // the sweeps' wrench response
         const V3<T> Ww = Uw * invD, Wl = Ul * invD;
         const T w0 = u * invD;
         if constexpr (AX >= 0)
@@ -1843,12 +1850,13 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
 }
 
 // ── one impulse sweep, forward half (cuda/mod.rs:916-927; phyz_kernels.cu
-// :1322-1368 then :804-918): body i's accelerations from the backward sweep
-// just run, its body velocity put back for the next backward sweep, its free
-// velocity X v_f,parent + S (qd + dt qdd), and -- if collidable -- one
-// staged impulse update whose wrench the next backward sweep applies. The
-// free velocity carries every impulse written so far through the whole
-// articulated chain, which is what makes the iteration matrix-free.
+// :1322-1368 then :804-918): body i's accelerations from the backward
+// quantities in place (W of the step's backward sweep, w0 of the last
+// wrench response), its free velocity X v_f,parent + S (qd + dt qdd), and --
+// if collidable -- one staged impulse update whose wrench the next wrench
+// response applies. The free velocity carries every impulse written so far
+// through the whole articulated chain, which is what makes the iteration
+// matrix-free.
 template <int AX, int FEAT, class T, class Scr>
 PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& cvo, SV<T>& ca,
                       SV<T>& cvf) {
@@ -1930,11 +1938,6 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     cvo = vo;
     ca = a;
     cvf = vf;
-    // the backward sweep reads the body velocity where it left W
-    if constexpr (AX >= 0)
-        S.rec_put_vw(bi, vo);
-    else
-        st_sv(S, bi.s_vw, vo);
     if (bi.flags & F_CONTACT) {
         constexpr bool TERRAIN = (FEAT & FEAT_TERRAIN) != 0;
         const int s = bi.s_up;
@@ -1950,6 +1953,113 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
         }
         const SV<T> f = impulse_wrench_call<TERRAIN>(M.im, M.ter, bi, &bt, wf, vf, S);
         st_sv(S, bi.s_f, f);
+    }
+}
+
+// ── one impulse sweep, wrench response (replaces a full backward sweep) ──
+// Between sweeps only the contact wrenches change, and the articulated-body
+// recursion is linear in them: with the step's backward quantities kept
+// (W = U D^-1 per body, D^-1 or the factor of D, w0 of the step), the change
+// dF of the external wrenches moves the bias forces by dp = -dF plus the
+// children's share, each joint's w0 by D^-1 (-S^T dp), and passes
+// X^T (dp + W (-S^T dp)) to the parent. This is exactly the difference
+// between the backward sweeps the reference reruns per sweep (aba.rs:215-320)
+// with the old and the new wrenches, without their inertia work.
+template <int AX, int FEAT, class T, class Scr>
+PZ_HD void wrench_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& dp) {
+    const BodyT<T>& bt = M.bt[i];
+    const int p = bi.parent;
+    if (!(bi.flags & F_CHAIN)) dp = zerosv<T>();
+    if (bi.flags & F_EXTF) dp = dp - (ld_sv<T>(S, bi.s_f) - ld_sv<T>(S, bi.s_fp));
+    if (bi.flags & F_BRANCH) dp = dp + ld_sv<T>(S, bi.s_acc + 21);
+    JX<T> j;
+    SV<T> Wv;
+    if constexpr (AX >= 0) {
+        const Rec<T> rec = S.rec_get(bi);
+        j.c = rec.c;
+        j.s = rec.s;
+        Wv = rec.v;
+    } else {
+        j = load_jx<AX, FEAT>(bi, bt, S);
+    }
+    bool live = true;
+    if (AX >= 0 || bi.ndof == 1) {
+        T du;
+        if constexpr (AX >= 0) {
+            du = -at<AX>(dp.w);
+        } else {
+            Wv = ld_sv<T>(S, bi.s_vw);
+            const V3<T> a = ld3(bt.axis);
+            du = -(bi.jtype == J_REVOLUTE ? dot(a, dp.w) : dot(a, dp.l));
+        }
+        const T invD = S(bi.s_dinv);
+        S(bi.s_w0) = S(bi.s_w0b) + invD * du;
+        live = pz_abs(invD) > T(0);
+        dp = dp + mksv<T>(Wv.w * du, Wv.l * du);
+    } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
+        const int nd = bi.ndof;
+        if (nd > 1) {
+            T x[6], du[6];
+#pragma unroll
+            for (int k = 0; k < 6; k++) du[k] = k < nd ? -svget(dp, k) : T(0);
+            live = pz_abs(S(bi.s_dinv)) > T(0);
+            if (live) {
+                // D dw0 = du with D = L L^T
+#pragma unroll
+                for (int a = 0; a < 6; a++) {
+                    if (a >= nd) break;
+                    T e = du[a];
+                    for (int k = 0; k < a; k++) e = e - S(bi.s_dinv + a * (a + 1) / 2 + k) * x[k];
+                    x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+                }
+                for (int a = nd - 1; a >= 0; a--) {
+                    T e = x[a];
+                    for (int k = a + 1; k < nd; k++) e = e - S(bi.s_dinv + k * (k + 1) / 2 + a) * x[k];
+                    x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < 6; k++) {
+                if (k >= nd) break;
+                S(bi.s_w0 + k) = S(bi.s_w0b + k) + (live ? x[k] : T(0));
+                const SV<T> wk = ld_sv<T>(S, bi.s_vw + 6 * k);
+                dp = dp + mksv<T>(wk.w * du[k], wk.l * du[k]);
+            }
+        }
+    }
+    if (p < 0) return;
+    dp = live ? frc_XT<AX, FEAT>(bi, bt, j, dp) : zerosv<T>();  // a skipped body passes nothing
+    if (p != i - 1) {
+        const int s = M.bi[p].s_acc + 21;
+        st_sv(S, s, ld_sv<T>(S, s) + dp);
+    }
+}
+
+template <int FEAT, class T, class Scr>
+PZ_HD void wrench_response(const ModelView<T>& M, const Scr& S) {
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        if (bi.flags & F_BRANCH)
+            for (int k = 0; k < 6; k++) S(bi.s_acc + 21 + k) = T(0);
+    }
+    SV<T> dp = zerosv<T>();
+    for (int i = M.nb - 1; i >= 0; i--) {
+        const BodyI bi = M.bi[i];
+#define PZ_WR(AX) wrench_body<AX, FEAT>(M, S, i, bi, dp)
+        PZ_BY_KIND(body_kind(bi), PZ_WR)
+#undef PZ_WR
+    }
+}
+
+// The step's backward quantities the wrench responses start from: w0 and
+// the wrenches it applied.
+template <class T, class Scr>
+PZ_HD void keep_backward_state(const ModelView<T>& M, const Scr& S) {
+    for (int i = 0; i < M.nb; i++) {
+        const BodyI bi = M.bi[i];
+        for (int k = 0; k < bi.ndof; k++) S(bi.s_w0b + k) = S(bi.s_w0 + k);
+        if (bi.flags & F_EXTF)
+            for (int k = 0; k < 6; k++) S(bi.s_fp + k) = S(bi.s_f + k);
     }
 }
 

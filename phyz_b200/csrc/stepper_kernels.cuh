@@ -301,12 +301,14 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
             }
             pass2<FEAT>(M, S);
             if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
-                // sweeps x [contact at the free velocity -> backward sweep]
+                // sweeps x [contact at the free velocity -> the response to
+                // the wrench change], from the step's backward sweep
+                keep_backward_state(M, S);
                 for (int k = 0; k < P.sweeps; k++) {
                     sweep_forward<FEAT>(M, S);
                     if constexpr ((FEAT & FEAT_TERRAIN) != 0)
                         if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
-                    pass2<FEAT>(M, S);
+                    wrench_response<FEAT>(M, S);
                 }
                 if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
             }
