@@ -1294,14 +1294,6 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const Body
     return f;
 }
 
-// Out-of-line entry, everything by value: the sweep's own state stays in
-// registers.
-template <bool TERRAIN, class T, class Scr>
-PZ_OUTLINE SV<T> impulse_wrench_call(ImpMat<T> m, Terrain<T> ter, BodyI bi, const BodyT<T>* bt, WF<T> wf, SV<T> vf,
-                                     Scr S) {
-    return impulse_wrench<TERRAIN>(m, ter, bi, *bt, wf, vf, S);
-}
-
 // Contact state of every body in impulse mode, from the impulses the last
 // sweep left in the slots (phyz_kernels.cu:964-980 with the impulse
 // branch's point and force): [touching, depth, point(3), force(3)].
@@ -1951,7 +1943,7 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
             wf.up = mk3<T>(S(s), S(s + 1), S(s + 2));
             wf.pos.z = S(s + 3);
         }
-        const SV<T> f = impulse_wrench_call<TERRAIN>(M.im, M.ter, bi, &bt, wf, vf, S);
+        const SV<T> f = impulse_wrench<TERRAIN>(M.im, M.ter, bi, bt, wf, vf, S);
         st_sv(S, bi.s_f, f);
     }
 }
@@ -1965,6 +1957,40 @@ PZ_HD void sweep_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
 // X^T (dp + W (-S^T dp)) to the parent. This is exactly the difference
 // between the backward sweeps the reference reruns per sweep (aba.rs:215-320)
 // with the old and the new wrenches, without their inertia work.
+// The wrench response of a ball (ND 3) or free (ND 6) joint: D dw0 = du with
+// D = L L^T (the factor kept by the backward sweep), w0 = w0_step + dw0, and
+// dp += W du. Returns false for a body the backward sweep skipped.
+template <int ND, class T, class Scr>
+PZ_HD bool wrench_multi(const BodyI& bi, const Scr& S, SV<T>& dp) {
+    T du[ND], x[ND];
+#pragma unroll
+    for (int k = 0; k < ND; k++) du[k] = -svget(dp, k);
+    const bool live = pz_abs(S(bi.s_dinv)) > T(0);
+    if (live) {
+#pragma unroll
+        for (int a = 0; a < ND; a++) {
+            T e = du[a];
+#pragma unroll
+            for (int k = 0; k < a; k++) e = e - S(bi.s_dinv + a * (a + 1) / 2 + k) * x[k];
+            x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+        }
+#pragma unroll
+        for (int a = ND - 1; a >= 0; a--) {
+            T e = x[a];
+#pragma unroll
+            for (int k = a + 1; k < ND; k++) e = e - S(bi.s_dinv + k * (k + 1) / 2 + a) * x[k];
+            x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < ND; k++) {
+        S(bi.s_w0 + k) = S(bi.s_w0b + k) + (live ? x[k] : T(0));
+        const SV<T> wk = ld_sv<T>(S, bi.s_vw + 6 * k);
+        dp = dp + mksv<T>(wk.w * du[k], wk.l * du[k]);
+    }
+    return live;
+}
+
 template <int AX, int FEAT, class T, class Scr>
 PZ_HD void wrench_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& bi, SV<T>& dp) {
     const BodyT<T>& bt = M.bt[i];
@@ -1997,35 +2023,10 @@ PZ_HD void wrench_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& 
         live = pz_abs(invD) > T(0);
         dp = dp + mksv<T>(Wv.w * du, Wv.l * du);
     } else if constexpr (AX < 0 && (FEAT & FEAT_MULTI) != 0) {
-        const int nd = bi.ndof;
-        if (nd > 1) {
-            T x[6], du[6];
-#pragma unroll
-            for (int k = 0; k < 6; k++) du[k] = k < nd ? -svget(dp, k) : T(0);
-            live = pz_abs(S(bi.s_dinv)) > T(0);
-            if (live) {
-                // D dw0 = du with D = L L^T
-#pragma unroll
-                for (int a = 0; a < 6; a++) {
-                    if (a >= nd) break;
-                    T e = du[a];
-                    for (int k = 0; k < a; k++) e = e - S(bi.s_dinv + a * (a + 1) / 2 + k) * x[k];
-                    x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
-                }
-                for (int a = nd - 1; a >= 0; a--) {
-                    T e = x[a];
-                    for (int k = a + 1; k < nd; k++) e = e - S(bi.s_dinv + k * (k + 1) / 2 + a) * x[k];
-                    x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
-                }
-            }
-#pragma unroll
-            for (int k = 0; k < 6; k++) {
-                if (k >= nd) break;
-                S(bi.s_w0 + k) = S(bi.s_w0b + k) + (live ? x[k] : T(0));
-                const SV<T> wk = ld_sv<T>(S, bi.s_vw + 6 * k);
-                dp = dp + mksv<T>(wk.w * du[k], wk.l * du[k]);
-            }
-        }
+        if (bi.ndof == 3)
+            live = wrench_multi<3>(bi, S, dp);
+        else if (bi.ndof == 6)
+            live = wrench_multi<6>(bi, S, dp);
     }
     if (p < 0) return;
     dp = live ? frc_XT<AX, FEAT>(bi, bt, j, dp) : zerosv<T>();  // a skipped body passes nothing
