@@ -108,6 +108,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--specialize", default="auto", choices=["auto", "0", "1"],
+                    help="rollout kernel: 1 compiled at run time for the model (tables literal, loops "
+                         "unrolled), 0 the generic variant, auto 1 for models of at most 16 bodies")
     return ap.parse_args()
 
 
@@ -315,6 +318,7 @@ def main():
     offset, _ = weak_block(nworld, rank)  # this rank's block of worlds
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
+    sim.specialize = {"auto": "auto", "0": False, "1": True}[args.specialize]
     hf = bench_heightfield(args.config)
     if cfg.contact and impulse:
         sim.enable_contact_impulse(cfg.contact[0], cfg.contact[3])
@@ -468,7 +472,9 @@ def main():
                                          else ("penalty" if cfg.contact else None))),
                        "l2": "inputs larger than L2: the per-step control schedule "
                              f"({horizon * nv * nworld * esz / 1e9:.1f} GB) streams from HBM every rollout",
-                       "launch": info},
+                       "launch": info,
+                       "kernel": ("model-specialized (compiled at run time for this model)" if sim.specialized
+                                  else "generic variant")},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
             "gpu_launches": args.steps * 2,  # per rollout: rollout_kernel + objective_kernel
             "objective": objective[0],

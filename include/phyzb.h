@@ -543,6 +543,35 @@ int phyzb_measure_fma_peak(int precision, double* tflops);
 int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
                       int32_t* smem_bytes, int32_t* scratch_per_world, int32_t* tmem_cols);
 
+/* ── model-specialized kernels (no reference counterpart) ──────────────── */
+
+/* Kernel specialization mode of a simulator:
+ *   PHYZB_SPECIALIZE_OFF  rollouts run the generic kernel variants;
+ *   PHYZB_SPECIALIZE_ON   they run a kernel compiled at run time (NVRTC) for
+ *                         the simulator's packed model: its body tables
+ *                         literal in the code and every body loop unrolled,
+ *                         the generic kernel's source and arithmetic (results
+ *                         agree to rounding: constant folding may move which
+ *                         product of a sum fuses into an FMA);
+ *   PHYZB_SPECIALIZE_AUTO ON for models of at most
+ *                         PHYZB_SPECIALIZE_AUTO_MAX_BODIES bodies, where
+ *                         unrolling pays; OFF for longer ones, whose unrolled
+ *                         code outgrows the instruction cache.
+ * The compile happens at the first launch after each table change (model,
+ * contact or PD settings, world count) and is cached per process and on
+ * disk (PHYZB_KERNEL_CACHE: a directory, or "0" for none; default
+ * $HOME/.cache/phyzb). A compile or load failure fails that launch with
+ * PHYZB_ERR_CUDA and the compiler's log in phyzb_last_error(). A new
+ * simulator starts in the mode PHYZB_SPECIALIZE names ("0", "1", "auto"),
+ * else OFF. `active` (may be null) tells whether the next launch runs the
+ * specialized kernel. */
+#define PHYZB_SPECIALIZE_OFF 0
+#define PHYZB_SPECIALIZE_ON 1
+#define PHYZB_SPECIALIZE_AUTO 2
+#define PHYZB_SPECIALIZE_AUTO_MAX_BODIES 16
+int phyzb_set_kernel_specialization(phyzb_sim* sim, int32_t mode);
+int phyzb_get_kernel_specialization(const phyzb_sim* sim, int32_t* mode, int32_t* active);
+
 #ifdef __cplusplus
 }
 #endif

@@ -201,6 +201,8 @@ SIGNATURES = {
     "phyzb_objective_device": (C.c_int, [_P, C.c_int, _P]),
     "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
     "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
+    "phyzb_set_kernel_specialization": (C.c_int, [_P, C.c_int32]),
+    "phyzb_get_kernel_specialization": (C.c_int, [_P, _I32P, _I32P]),
     "phyzb_enable_policy": (C.c_int, [_P, C.POINTER(PhyzbPolicySpec)]),
     "phyzb_set_policy_weights": (C.c_int, [_P, _D, C.c_int64]),
     "phyzb_set_policy_std": (C.c_int, [_P, _D, C.c_int32]),

@@ -414,6 +414,30 @@ class BatchSim:
         check(self._lib.phyzb_flops_per_world_step(self._h, C.byref(f), C.byref(t)))
         return f.value, t.value
 
+    @property
+    def specialize(self):
+        """Kernel specialization mode: False (generic variants), True (the
+        rollout kernel compiled at run time for this model: tables literal,
+        body loops unrolled) or "auto" (True for models of at most
+        PHYZB_SPECIALIZE_AUTO_MAX_BODIES bodies). The compile happens at the
+        next launch after any table change and is cached in-process and on
+        disk."""
+        mode = C.c_int32()
+        check(self._lib.phyzb_get_kernel_specialization(self._h, C.byref(mode), None))
+        return {0: False, 1: True, 2: "auto"}[mode.value]
+
+    @specialize.setter
+    def specialize(self, mode) -> None:
+        code = 2 if mode == "auto" else (1 if mode else 0)
+        check(self._lib.phyzb_set_kernel_specialization(self._h, code))
+
+    @property
+    def specialized(self) -> bool:
+        """Whether the next rollout launch runs the model-specialized kernel."""
+        mode, active = C.c_int32(), C.c_int32()
+        check(self._lib.phyzb_get_kernel_specialization(self._h, C.byref(mode), C.byref(active)))
+        return bool(active.value)
+
     def launch_info(self) -> dict:
         vals = [C.c_int32() for _ in range(5)]
         check(self._lib.phyzb_launch_info(self._h, *[C.byref(x) for x in vals]))

@@ -49,6 +49,8 @@ int upload_layout(phyzb_sim* s, phyzb_sim::Layout& L, const std::vector<unsigned
         L.cap = L.info.bytes;
     }
     PZ_CUDA(cudaMemcpy(L.blob, blob.data(), L.info.bytes, cudaMemcpyHostToDevice));
+    L.host = blob;
+    L.spec = nullptr;  // the table changed: specialize again at the next launch
     return PHYZB_OK;
 }
 
@@ -165,14 +167,35 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
     return a;
 }
 
-int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
-    const phyzb_sim::Layout& L = s->lay[s->use];
-    cudaError_t e = is_f64(s) ? pz::launch_rollout<double>(rollout_args<double>(s, ctrl, stride, nsteps, s->use),
-                                                           L.launch, s->stream)
-                              : pz::launch_rollout<float>(rollout_args<float>(s, ctrl, stride, nsteps, s->use),
-                                                          L.launch, s->stream);
-    PZ_CUDA(e);
+bool specialized(const phyzb_sim* s) {
+    return s->specialize == PHYZB_SPECIALIZE_ON ||
+           (s->specialize == PHYZB_SPECIALIZE_AUTO && s->nb <= PHYZB_SPECIALIZE_AUTO_MAX_BODIES);
+}
+
+template <class T>
+int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+    phyzb_sim::Layout& L = s->lay[s->use];
+    const pz::RolloutArgs<T> a = rollout_args<T>(s, ctrl, stride, nsteps, s->use);
+    if (specialized(s)) {
+        if (!L.spec) {
+            std::string err;
+            const cudaError_t e = pz::spec_prepare<T>(L.host.data(), a, L.launch.tm != 0, L.info.tmem_cols, &L.spec,
+                                                      &L.spec_launch, &err);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                L.spec = nullptr;
+                return fail(PHYZB_ERR_CUDA, err);
+            }
+        }
+        PZ_CUDA(pz::spec_launch<T>(L.spec, a, L.spec_launch, s->stream));
+        return PHYZB_OK;
+    }
+    PZ_CUDA(pz::launch_rollout<T>(a, L.launch, s->stream));
     return PHYZB_OK;
+}
+
+int launch(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+    return is_f64(s) ? launch_t<double>(s, ctrl, stride, nsteps) : launch_t<float>(s, ctrl, stride, nsteps);
 }
 
 // host rows [nworld][width] f64 -> device SoA [width][nworld] in the sim precision
@@ -447,6 +470,8 @@ int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int preci
     s->nworld = nworld;
     s->nb = model->nbodies;
     s->nv = nv;
+    if (const char* env = getenv("PHYZB_SPECIALIZE"))
+        s->specialize = env[0] == '1' ? PHYZB_SPECIALIZE_ON : (env[0] == 'a' ? PHYZB_SPECIALIZE_AUTO : PHYZB_SPECIALIZE_OFF);
     set_model_copy(s, model);
     auto bail = [&](int code) {
         destroy_sim(s);
@@ -860,13 +885,30 @@ int phyzb_flops_per_world_step(const phyzb_sim* s, double* flops, double* transc
     return PHYZB_OK;
 }
 
+int phyzb_set_kernel_specialization(phyzb_sim* s, int32_t mode) {
+    PZ_TRY(check_sim(s));
+    if (mode != PHYZB_SPECIALIZE_OFF && mode != PHYZB_SPECIALIZE_ON && mode != PHYZB_SPECIALIZE_AUTO)
+        return fail(PHYZB_ERR_INVALID, "specialization mode " + std::to_string(mode) + " is not 0, 1 or 2");
+    s->specialize = mode;
+    return PHYZB_OK;
+}
+
+int phyzb_get_kernel_specialization(const phyzb_sim* s, int32_t* mode, int32_t* active) {
+    PZ_TRY(check_sim(s));
+    if (!mode) return fail(PHYZB_ERR_INVALID, "null output");
+    *mode = s->specialize;
+    if (active) *active = specialized(s) ? 1 : 0;
+    return PHYZB_OK;
+}
+
 int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t* smem, int32_t* scratch,
                       int32_t* tmem_cols) {
     PZ_TRY(check_sim(s));
     const phyzb_sim::Layout& L = s->lay[s->use];
-    if (wpb) *wpb = L.launch.W;
-    if (blocks) *blocks = L.launch.grid;
-    if (smem) *smem = L.launch.smem;
+    const pz::LaunchCfg& c = specialized(s) && L.spec ? L.spec_launch : L.launch;
+    if (wpb) *wpb = c.W;
+    if (blocks) *blocks = c.grid;
+    if (smem) *smem = c.smem;
     if (scratch) *scratch = L.info.scratch;
     if (tmem_cols) *tmem_cols = L.launch.tm ? L.info.tmem_cols : 0;
     return PHYZB_OK;

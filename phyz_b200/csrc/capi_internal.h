@@ -113,8 +113,14 @@ struct phyzb_sim {
         void* blob = nullptr;
         size_t cap = 0;
         pz::LaunchCfg launch{};
+        std::vector<unsigned char> host;        // the table as uploaded
+        const pz::SpecKernel* spec = nullptr;   // its model-specialized kernel, once compiled
+        pz::LaunchCfg spec_launch{};
     } lay[2];
     int use = 0;
+    // PHYZB_SPECIALIZE_*: whether rollouts run the model-specialized kernel
+    // (compiled at the first launch after each repack) or the generic variants
+    int specialize = 0;
     void* staging = nullptr;  // device, AoS f64 rows for host copies
     void* hist_q = nullptr;   // state history [slot][nv][nworld] (enable_state_history)
     void* hist_v = nullptr;
@@ -137,6 +143,7 @@ struct phyzb_sim {
 namespace pzc {
 
 bool is_f64(const phyzb_sim* s);
+bool specialized(const phyzb_sim* s);  // the next rollout launch runs the specialized kernel
 int check_sim(const phyzb_sim* s);
 void free_ptr(void*& p);
 // one fused rollout launch of nsteps under `ctrl` (schedule stride or 0)

@@ -138,7 +138,7 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
         pd[k].vi = psrc[k].vi;
     }
     ModelView<Cnt> M;
-    M.bt = bt.data();
+    M.bt = M.btp = bt.data();
     M.bi = reinterpret_cast<const BodyI*>(blob.data() + info.off_bi);
     M.pd = pd.data();
     M.pd_of_dof = reinterpret_cast<const int*>(blob.data() + info.off_pdmap);

@@ -2,9 +2,17 @@
 // the C ABI (capi.cu). No kernel here has a host implementation.
 #pragma once
 
+#ifndef __CUDACC_RTC__
 #include <cuda_runtime.h>
 
+#include <string>
+#endif
+
 namespace pz {
+
+// TMEM columns allocated per block by the Tensor-Memory variant: the whole
+// array (one block per SM).
+constexpr unsigned TMEM_COLS = 512;
 
 struct LaunchCfg {
     int W;         // worlds (threads) per block
@@ -50,6 +58,7 @@ struct RolloutArgs {
     double plane_offset, plane_max_depth, plane_half_x, plane_half_y;
 };
 
+#ifndef __CUDACC_RTC__
 // tmem_cols > 0: configure the Tensor-Memory variant for a layout whose
 // body records need tmem_cols columns per world.
 template <class T>
@@ -70,5 +79,19 @@ cudaError_t launch_aos_to_soa(const Tin* aos, Tout* soa, long long nworld, int w
                               cudaStream_t s);
 template <class Tin, class Tout>
 cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int width, cudaStream_t s);
+// Model-specialized rollout kernels (spec.cu): the rollout kernel compiled
+// at run time for one packed model, its tables literal (pz_spec.h). One
+// compile per (model table, precision, feature set, layout, device) per
+// process; compiled kernels are also kept on disk (PHYZB_KERNEL_CACHE,
+// default $HOME/.cache/phyzb; "0" turns the disk cache off).
+struct SpecKernel;
+// Compile or fetch the kernel of the table in `blob` (host copy of
+// a.model_blob) and size its launch. On failure *err says why.
+template <class T>
+cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols,
+                         const SpecKernel** k, LaunchCfg* cfg, std::string* err);
+template <class T>
+cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
+#endif  // __CUDACC_RTC__
 
 }  // namespace pz

@@ -57,6 +57,10 @@ struct alignas(16) BodyT {
     T gk, gd;                 // penalty gains of this body
     T armature;
 };
+// A body row is 64 scalars, no padding (the specialized source lists them in order).
+constexpr int BODYT_WORDS = 64;
+static_assert(sizeof(BodyT<float>) == BODYT_WORDS * sizeof(float), "BodyT<float> layout");
+static_assert(sizeof(BodyT<double>) == BODYT_WORDS * sizeof(double), "BodyT<double> layout");
 
 struct alignas(16) BodyI {
     int parent, jtype, off, ndof;
@@ -90,6 +94,7 @@ struct alignas(16) BodyI {
     int s_w0b;        // D^-1 u of the step's full backward sweep (ndof)
     int s_fp;         // F_EXTF: the wrench that backward sweep applied (6)
 };
+static_assert(sizeof(BodyI) == 28 * sizeof(int), "BodyI: 27 words and one of padding");
 
 template <class T>
 struct alignas(16) PdT {
@@ -126,14 +131,58 @@ struct ImpMat {
     T dmin, dmax, width, mid, power;
 };
 
+// Words of a BodyI before its alignment padding (the model-specialized
+// source lists them in this order).
+constexpr int BODYI_WORDS = 27;
+
+#ifdef PZ_SPEC
+// Model-specialized build: the host emits one packed model's tables as
+// literal constants (the definitions below, PZ_SPEC_NB and PZ_SPEC_NV) and
+// compiles the kernel for it, so body loops unroll with every table entry
+// folded into the instruction stream. The accessors mirror the pointer
+// tables of the generic build.
+namespace spec {
+__device__ __forceinline__ BodyI body(int i);
+template <class T>
+__device__ __forceinline__ BodyT<T> bodyt(int i);
+__device__ __forceinline__ int pd_of(int d);
+template <class T>
+__device__ __forceinline__ PdT<T> pdt(int k);
+}  // namespace spec
+struct SpecBodies {
+    __device__ __forceinline__ BodyI operator[](int i) const { return spec::body(i); }
+};
+template <class T>
+struct SpecBodyT {
+    __device__ __forceinline__ BodyT<T> operator[](int i) const { return spec::bodyt<T>(i); }
+};
+struct SpecPdOf {
+    __device__ __forceinline__ int operator[](int d) const { return spec::pd_of(d); }
+};
+template <class T>
+struct SpecPd {
+    __device__ __forceinline__ PdT<T> operator[](int k) const { return spec::pdt<T>(k); }
+};
+#endif
+
 // Everything a world-step needs besides its own state.
 template <class T>
 struct ModelView {
+#ifdef PZ_SPEC
+    SpecBodyT<T> bt;
+    SpecBodies bi;
+    SpecPd<T> pd;
+    SpecPdOf pd_of_dof;
+    static constexpr int nb = PZ_SPEC_NB, nv = PZ_SPEC_NV;
+    int npd;
+#else
     const BodyT<T>* bt;
     const BodyI* bi;
     const PdT<T>* pd;
     const int* pd_of_dof;  // nv entries: PD entry driving this DOF, or -1
     int nb, nv, npd;
+#endif
+    const BodyT<T>* btp;   // the body table in memory (out-of-line calls take rows by address)
     int contact;           // 0/1
     T dt, gx, gy, gz;
     T ground_h, friction;

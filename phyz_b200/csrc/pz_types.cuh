@@ -24,7 +24,7 @@
 #define PZ_OUTLINE inline
 #endif
 
-#if defined(__CUDA_ARCH__)
+#if defined(__CUDA_ARCH__) && !defined(__CUDACC_RTC__)
 #include <cuda_runtime.h>
 #endif
 

@@ -5,6 +5,10 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
 #include "pz_launch.h"
 
 namespace pz {
@@ -21,6 +25,61 @@ struct DeviceLimits {
     int sm_count;
     int smem_optin;  // opt-in shared memory per block (static + dynamic)
 };
+
+// Pick the block width that keeps the most worlds resident per SM,
+// discounted by how full the last wave of tiles is. Shared-memory layout:
+// any even width up to the 256 of the kernel's launch bounds. Tensor-Memory
+// layout: whole warps, one block per SM, and few enough warps per TMEM lane
+// quarter that each thread's columns hold its records. `occupancy(&blocks,
+// W, smem)` asks the runtime about the kernel being configured; dyn_cap is
+// its dynamic shared-memory limit. PHYZB_WORLDS_PER_BLOCK overrides the
+// width for tuning.
+template <class Occ>
+cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, int scratch, int model_bytes,
+                        long long nworld, int tmem_cols, int tmem_total, Occ occupancy, LaunchCfg* out) {
+    const long long per_world = (long long)scratch * (long long)esz;
+    int forced = 0;
+    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
+    int best_w = 0, best_blocks = 0, best_smem = 0;
+    double best_score = -1.0;
+    const int step = tm ? 32 : 2;
+    for (int W = 32; W <= 256; W += step) {
+        if (forced > 0 && W != forced) continue;
+        if (tm) {
+            const int per_quarter = ((W + 31) / 32 + 3) / 4;
+            if (tmem_cols * per_quarter > tmem_total) break;
+        }
+        long long smem = (long long)model_bytes + per_world * W;
+        if (smem > dyn_cap) break;
+        // Tensor-Memory blocks ask for more than half an SM's shared memory so
+        // that no second block lands on the SM and waits on the allocation
+        if (tm) smem = std::max(smem, (long long)(dl.smem_optin / 2 + 16) & ~15LL);
+        int blocks = 0;
+        const cudaError_t e = occupancy(&blocks, W, (size_t)smem);
+        if (e != cudaSuccess) return e;
+        if (blocks <= 0) continue;
+        if (tm) blocks = 1;  // each block holds the whole Tensor Memory
+        const double resident = (double)blocks * W * dl.sm_count;  // worlds in flight on the GPU
+        const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
+        const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
+        const double score = (double)blocks * W * used;
+        if (score > best_score * 1.0001) {
+            best_score = score;
+            best_w = W;
+            best_blocks = blocks;
+            best_smem = (int)smem;
+        }
+    }
+    if (best_w == 0) return cudaErrorInvalidConfiguration;
+    const long long ntiles = (nworld + best_w - 1) / best_w;
+    const long long cap = (long long)dl.sm_count * best_blocks;
+    out->W = best_w;
+    out->grid = (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
+    out->smem = best_smem;
+    out->tm = tm ? 1 : 0;
+    out->score = best_score;
+    return cudaSuccess;
+}
 
 template <class T, int FEAT, bool TM>
 cudaError_t config_variant(const DeviceLimits& dl, int scratch, int model_bytes, long long nworld, int tmem_cols,

@@ -28,6 +28,14 @@
 #include "pz_model.cuh"
 #include "pz_types.cuh"
 
+// Loops over the bodies (and DOFs) of the model: fully unrolled in a
+// model-specialized build, where the table they index is literal.
+#ifdef PZ_SPEC
+#define PZ_UNROLL_BODIES _Pragma("unroll")
+#else
+#define PZ_UNROLL_BODIES
+#endif
+
 namespace pz {
 
 // Compile-time feature mask of a kernel variant: a model without ball/free
@@ -1089,7 +1097,7 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
                 store(bi.s_up);  // the impulse sweeps read the body's frame
             } else {
                 const SV<T> f = contact_wrench_call<TERRAIN>(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, M.ter,
-                                                             bi, &bt, wf, v, false, i, Out<T>{nullptr, 0});
+                                                             bi, M.btp + i, wf, v, false, i, Out<T>{nullptr, 0});
                 st_sv(S, bi.s_f, f);
             }
         }
@@ -1146,6 +1154,7 @@ PZ_HD WF<T> world_frame(const ModelView<T>& M, const Scr& S, int i) {
 // written to rows 8*i.. of `cs` (layout.rs:68-80).
 template <int FEAT, class T, class Scr>
 PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>& cs) {
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         if (!(bi.flags & F_CONTACT)) {
@@ -1300,6 +1309,7 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const Body
 template <int FEAT, class T, class Scr>
 PZ_HD void contact_state_impulse_pass(const ModelView<T>& M, const Scr& S, const Out<T>& cs) {
     const T idt = T(1) / pz_max(M.im.dt, T(1e-9));
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         if (!(bi.flags & F_CONTACT)) {
@@ -1392,6 +1402,7 @@ PZ_HD void plane_pass(const ModelView<T>& M, const Scr& S) {
     const V3<T> p0_w = fp.pos + wf_mul(fp, ez * M.plane.offset);
     const V3<T> n_p = wf_tmul(fp, n_w);
     SV<T> fpb = zerosv<T>();
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         if (!(bi.flags & F_PLANE)) continue;  // a model constant: uniform over the warp
@@ -1678,6 +1689,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
 template <int FEAT, class T, class Scr>
 PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
     // zero the stored accumulators of branch bodies
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         if (bi.flags & F_BRANCH)
@@ -1686,6 +1698,7 @@ PZ_HD void pass2(const ModelView<T>& M, const Scr& S) {
     AI<T> I;
     SV<T> pA = zerosv<T>();
     ai_zero(I);
+    PZ_UNROLL_BODIES
     for (int i = M.nb - 1; i >= 0; i--) {
         const BodyI bi = M.bi[i];
 #define PZ_P2(AX) pass2_body<AX, FEAT>(M, S, i, bi, I, pA)
@@ -1832,6 +1845,7 @@ PZ_HD void pass3_next(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
                       const Out<T>& qdd_out) {
     SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvn = zerosv<T>();
     WF<T> cw;
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
 #define PZ_P3(AX) pass3_body<AX, FEAT, LAST>(M, S, io, i, bi, next_step, qdd_out, cvo, ca, cvn, cw)
@@ -2038,12 +2052,14 @@ PZ_HD void wrench_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& 
 
 template <int FEAT, class T, class Scr>
 PZ_HD void wrench_response(const ModelView<T>& M, const Scr& S) {
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         if (bi.flags & F_BRANCH)
             for (int k = 0; k < 6; k++) S(bi.s_acc + 21 + k) = T(0);
     }
     SV<T> dp = zerosv<T>();
+    PZ_UNROLL_BODIES
     for (int i = M.nb - 1; i >= 0; i--) {
         const BodyI bi = M.bi[i];
 #define PZ_WR(AX) wrench_body<AX, FEAT>(M, S, i, bi, dp)
@@ -2056,6 +2072,7 @@ PZ_HD void wrench_response(const ModelView<T>& M, const Scr& S) {
 // the wrenches it applied.
 template <class T, class Scr>
 PZ_HD void keep_backward_state(const ModelView<T>& M, const Scr& S) {
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
         for (int k = 0; k < bi.ndof; k++) S(bi.s_w0b + k) = S(bi.s_w0 + k);
@@ -2067,6 +2084,7 @@ PZ_HD void keep_backward_state(const ModelView<T>& M, const Scr& S) {
 template <int FEAT, class T, class Scr>
 PZ_HD void sweep_forward(const ModelView<T>& M, const Scr& S) {
     SV<T> cvo = zerosv<T>(), ca = zerosv<T>(), cvf = zerosv<T>();
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
 #define PZ_SW(AX) sweep_body<AX, FEAT>(M, S, i, bi, cvo, ca, cvf)
@@ -2081,6 +2099,7 @@ template <int FEAT, class T, class Scr>
 PZ_HD void pass1_all(const ModelView<T>& M, const Scr& S) {
     SV<T> cv = zerosv<T>();
     WF<T> cw;
+    PZ_UNROLL_BODIES
     for (int i = 0; i < M.nb; i++) {
         const BodyI bi = M.bi[i];
 #define PZ_P1(AX) pass1_body<AX, FEAT>(M, S, i, bi, cv, cw)

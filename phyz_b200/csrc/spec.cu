@@ -1,0 +1,394 @@
+// Run-time compilation of model-specialized rollout kernels.
+//
+// pz_spec.h writes, for one packed model, a translation unit whose body
+// tables are literal; this file compiles it with NVRTC for the device in use,
+// loads the cubin as a module, sizes its launch like the generic variants'
+// (pick_launch) and launches it with the generic kernel's argument block.
+// The kernel source itself (stepper_kernels.cuh and its headers) is carried
+// inside the library as text (pz_spec_headers.inc, written by the build), so
+// the library needs no source tree at run time, only libnvrtc.
+//
+// NVRTC is loaded on first use (libnvrtc.so.12, or the file PHYZB_NVRTC
+// names); the driver calls come through the runtime's entry-point query, so
+// the library links neither. Compiled cubins are kept per process and, unless
+// PHYZB_KERNEL_CACHE is "0", in a cache directory keyed by a hash of the
+// compiler version, the options, the generated source and the headers.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nvrtc.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "pz_launch.h"
+#include "pz_spec.h"
+#include "pz_variants.h"
+#include "pz_spec_headers.inc"
+
+namespace pz {
+
+struct SpecKernel {
+    CUmodule mod = nullptr;
+    CUfunction fn = nullptr;
+    int static_smem = 0;
+};
+
+namespace {
+
+constexpr int kSpecHeaderCount = (int)(sizeof(kSpecHeaderNames) / sizeof(kSpecHeaderNames[0]));
+
+struct Nvrtc {
+    decltype(&::nvrtcVersion) version = nullptr;
+    decltype(&::nvrtcCreateProgram) create = nullptr;
+    decltype(&::nvrtcDestroyProgram) destroy = nullptr;
+    decltype(&::nvrtcAddNameExpression) add_name = nullptr;
+    decltype(&::nvrtcCompileProgram) compile = nullptr;
+    decltype(&::nvrtcGetProgramLogSize) log_size = nullptr;
+    decltype(&::nvrtcGetProgramLog) log = nullptr;
+    decltype(&::nvrtcGetCUBINSize) cubin_size = nullptr;
+    decltype(&::nvrtcGetCUBIN) cubin = nullptr;
+    decltype(&::nvrtcGetLoweredName) lowered = nullptr;
+    decltype(&::nvrtcGetErrorString) error_string = nullptr;
+    std::string error;  // empty: loaded
+    std::string tag;    // "nvrtc <major>.<minor>"
+};
+
+template <class F>
+bool sym(void* h, const char* name, F* f, std::string* err) {
+    *f = reinterpret_cast<F>(dlsym(h, name));
+    if (!*f) *err = std::string("libnvrtc has no ") + name;
+    return *f != nullptr;
+}
+
+Nvrtc load_nvrtc() {
+    Nvrtc n;
+    void* h = nullptr;
+    std::string tried;
+    const char* env = getenv("PHYZB_NVRTC");
+    const char* names[] = {env, "libnvrtc.so.12", "libnvrtc.so"};
+    for (const char* name : names) {
+        if (!name || !*name) continue;
+        h = dlopen(name, RTLD_NOW | RTLD_LOCAL);
+        if (h) break;
+        const char* e = dlerror();
+        tried += std::string(tried.empty() ? "" : "; ") + (e ? e : name);
+    }
+    if (!h) {
+        n.error = "model-specialized kernels need the CUDA runtime compiler (libnvrtc.so.12): " + tried;
+        return n;
+    }
+    if (!sym(h, "nvrtcVersion", &n.version, &n.error) || !sym(h, "nvrtcCreateProgram", &n.create, &n.error) ||
+        !sym(h, "nvrtcDestroyProgram", &n.destroy, &n.error) ||
+        !sym(h, "nvrtcAddNameExpression", &n.add_name, &n.error) ||
+        !sym(h, "nvrtcCompileProgram", &n.compile, &n.error) ||
+        !sym(h, "nvrtcGetProgramLogSize", &n.log_size, &n.error) ||
+        !sym(h, "nvrtcGetProgramLog", &n.log, &n.error) || !sym(h, "nvrtcGetCUBINSize", &n.cubin_size, &n.error) ||
+        !sym(h, "nvrtcGetCUBIN", &n.cubin, &n.error) || !sym(h, "nvrtcGetLoweredName", &n.lowered, &n.error) ||
+        !sym(h, "nvrtcGetErrorString", &n.error_string, &n.error))
+        return n;
+    int major = 0, minor = 0;
+    n.version(&major, &minor);
+    n.tag = "nvrtc " + std::to_string(major) + "." + std::to_string(minor);
+    return n;
+}
+
+const Nvrtc& nvrtc() {
+    static const Nvrtc n = load_nvrtc();
+    return n;
+}
+
+struct Driver {
+    decltype(&::cuModuleLoadData) load = nullptr;
+    decltype(&::cuModuleGetFunction) get = nullptr;
+    decltype(&::cuFuncGetAttribute) attr = nullptr;
+    decltype(&::cuFuncSetAttribute) set_attr = nullptr;
+    decltype(&::cuOccupancyMaxActiveBlocksPerMultiprocessor) occupancy = nullptr;
+    decltype(&::cuLaunchKernel) launch = nullptr;
+    std::string error;
+};
+
+template <class F>
+bool entry(const char* name, F* f, std::string* err) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    const cudaError_t e = cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || !p) {
+        *err = std::string("driver entry point ") + name + " unavailable (" + cudaGetErrorString(e) + ")";
+        return false;
+    }
+    *f = reinterpret_cast<F>(p);
+    return true;
+}
+
+Driver load_driver() {
+    Driver d;
+    if (!entry("cuModuleLoadData", &d.load, &d.error) || !entry("cuModuleGetFunction", &d.get, &d.error) ||
+        !entry("cuFuncGetAttribute", &d.attr, &d.error) || !entry("cuFuncSetAttribute", &d.set_attr, &d.error) ||
+        !entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", &d.occupancy, &d.error) ||
+        !entry("cuLaunchKernel", &d.launch, &d.error))
+        return d;
+    return d;
+}
+
+const Driver& driver() {
+    static const Driver d = load_driver();
+    return d;
+}
+
+std::string cu_error(const char* what, CUresult r) {
+    return std::string(what) + " failed (CUresult " + std::to_string((int)r) + ")";
+}
+
+// FNV-1a, 64 bit, over a sequence of strings (each followed by a 0 byte)
+struct Hash {
+    uint64_t h;
+    explicit Hash(uint64_t seed) : h(seed) {}
+    void add(const std::string& s) {
+        for (unsigned char c : s) h = (h ^ c) * 0x100000001b3ull;
+        h = (h ^ 0u) * 0x100000001b3ull;
+    }
+};
+
+std::string cache_dir() {
+    const char* env = getenv("PHYZB_KERNEL_CACHE");
+    if (env && std::strcmp(env, "0") == 0) return "";
+    if (env && *env) return env;
+    const char* home = getenv("HOME");
+    if (!home || !*home) return "";
+    return std::string(home) + "/.cache/phyzb";
+}
+
+void make_dirs(const std::string& dir) {
+    for (size_t i = 1; i <= dir.size(); i++)
+        if (i == dir.size() || dir[i] == '/') mkdir(dir.substr(0, i).c_str(), 0755);
+}
+
+// cache file: "PZSPEC1\n<lowered name>\n" then the cubin
+bool read_cached(const std::string& path, std::string* lowered, std::vector<char>* cubin) {
+    FILE* f = std::fopen(path.c_str(), "rb");
+    if (!f) return false;
+    std::vector<char> all;
+    char buf[1 << 16];
+    size_t n;
+    while ((n = std::fread(buf, 1, sizeof buf, f)) > 0) all.insert(all.end(), buf, buf + n);
+    std::fclose(f);
+    const std::string magic = "PZSPEC1\n";
+    if (all.size() < magic.size() || std::memcmp(all.data(), magic.data(), magic.size()) != 0) return false;
+    size_t i = magic.size();
+    while (i < all.size() && all[i] != '\n') i++;
+    if (i >= all.size()) return false;
+    lowered->assign(all.data() + magic.size(), all.data() + i);
+    cubin->assign(all.begin() + (long)i + 1, all.end());
+    return !cubin->empty();
+}
+
+void write_cached(const std::string& dir, const std::string& path, const std::string& lowered,
+                  const std::vector<char>& cubin) {
+    make_dirs(dir);
+    const std::string tmp = path + ".tmp" + std::to_string((long long)getpid());
+    FILE* f = std::fopen(tmp.c_str(), "wb");
+    if (!f) return;
+    const std::string head = "PZSPEC1\n" + lowered + "\n";
+    const bool ok = std::fwrite(head.data(), 1, head.size(), f) == head.size() &&
+                    std::fwrite(cubin.data(), 1, cubin.size(), f) == cubin.size();
+    std::fclose(f);
+    if (ok)
+        std::rename(tmp.c_str(), path.c_str());
+    else
+        std::remove(tmp.c_str());
+}
+
+cudaError_t compile(const std::string& src, const std::string& name, const std::vector<std::string>& opts,
+                    std::string* lowered, std::vector<char>* cubin, std::string* err) {
+    const Nvrtc& n = nvrtc();
+    if (!n.error.empty()) {
+        *err = n.error;
+        return cudaErrorNotSupported;
+    }
+    nvrtcProgram prog = nullptr;
+    nvrtcResult r = n.create(&prog, src.c_str(), "pz_spec_rollout.cu", kSpecHeaderCount, kSpecHeaderTexts,
+                             kSpecHeaderNames);
+    if (r != NVRTC_SUCCESS) {
+        *err = std::string("nvrtcCreateProgram: ") + n.error_string(r);
+        return cudaErrorUnknown;
+    }
+    std::vector<const char*> o;
+    for (const std::string& s : opts) o.push_back(s.c_str());
+    r = n.add_name(prog, name.c_str());
+    if (r == NVRTC_SUCCESS) r = n.compile(prog, (int)o.size(), o.data());
+    if (r != NVRTC_SUCCESS) {
+        size_t ls = 0;
+        n.log_size(prog, &ls);
+        std::string log(ls, '\0');
+        if (ls) n.log(prog, &log[0]);
+        *err = std::string("runtime compile of the specialized rollout kernel failed: ") + n.error_string(r) +
+               "\n" + log;
+        n.destroy(&prog);
+        return cudaErrorUnknown;
+    }
+    const char* low = nullptr;
+    size_t cs = 0;
+    r = n.lowered(prog, name.c_str(), &low);
+    if (r == NVRTC_SUCCESS) *lowered = low;
+    if (r == NVRTC_SUCCESS) r = n.cubin_size(prog, &cs);
+    if (r == NVRTC_SUCCESS) {
+        cubin->resize(cs);
+        r = n.cubin(prog, cubin->data());
+    }
+    n.destroy(&prog);
+    if (r != NVRTC_SUCCESS || cubin->empty()) {
+        *err = std::string("runtime compile produced no cubin: ") + n.error_string(r);
+        return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+}
+
+std::mutex g_mu;
+std::map<std::string, std::unique_ptr<SpecKernel>> g_kernels;  // key: device + source hash
+
+// The module of `src` on the current device: from this process's table,
+// else the disk cache, else a fresh compile.
+cudaError_t get_kernel(const std::string& src, const std::string& name, SpecKernel** out, std::string* err) {
+    const Driver& drv = driver();
+    if (!drv.error.empty()) {
+        *err = drv.error;
+        return cudaErrorNotSupported;
+    }
+    int dev = 0, major = 0, minor = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) {
+        *err = cudaGetErrorString(e);
+        return e;
+    }
+    // the kernel's Tensor Memory and bulk-copy instructions are sm_100a's;
+    // PHYZB_SPEC_NVRTC_OPTS appends options (space-separated) for tuning
+    std::vector<std::string> opts = {"-arch=sm_" + std::to_string(major * 10 + minor) + "a", "-std=c++17",
+                                     "-lineinfo"};
+    if (const char* extra = getenv("PHYZB_SPEC_NVRTC_OPTS")) {
+        std::string tok;
+        for (const char* c = extra;; c++) {
+            if (*c == ' ' || *c == '\0') {
+                if (!tok.empty()) opts.push_back(tok);
+                tok.clear();
+                if (*c == '\0') break;
+            } else {
+                tok += *c;
+            }
+        }
+    }
+    Hash h1(0xcbf29ce484222325ull), h2(0x84222325cbf29ce4ull);
+    for (Hash* h : {&h1, &h2}) {
+        h->add(nvrtc().tag);
+        for (const std::string& s : opts) h->add(s);
+        h->add(name);
+        h->add(src);
+        for (int k = 0; k < kSpecHeaderCount; k++) h->add(kSpecHeaderTexts[k]);
+    }
+    char hex[40];
+    std::snprintf(hex, sizeof hex, "%016llx%016llx", (unsigned long long)h1.h, (unsigned long long)h2.h);
+    const std::string key = std::to_string(dev) + ":" + hex;
+    std::lock_guard<std::mutex> lock(g_mu);
+    auto it = g_kernels.find(key);
+    if (it != g_kernels.end()) {
+        *out = it->second.get();
+        return cudaSuccess;
+    }
+    const std::string dir = cache_dir();
+    const std::string path = dir.empty() ? "" : dir + "/" + hex + ".cubin";
+    std::string lowered;
+    std::vector<char> cubin;
+    bool cached = !path.empty() && read_cached(path, &lowered, &cubin);
+    auto k = std::make_unique<SpecKernel>();
+    for (int attempt = 0; attempt < 2; attempt++) {
+        if (!cached) {
+            if ((e = compile(src, name, opts, &lowered, &cubin, err)) != cudaSuccess) return e;
+            if (!path.empty()) write_cached(dir, path, lowered, cubin);
+        }
+        CUresult r = drv.load(&k->mod, cubin.data());
+        if (r == CUDA_SUCCESS) r = drv.get(&k->fn, k->mod, lowered.c_str());
+        if (r == CUDA_SUCCESS) break;
+        if (!cached) {
+            *err = cu_error("loading the specialized rollout kernel", r);
+            return cudaErrorUnknown;
+        }
+        cached = false;  // a stale or damaged cache entry: compile afresh
+    }
+    CUresult r = drv.attr(&k->static_smem, CU_FUNC_ATTRIBUTE_SHARED_SIZE_BYTES, k->fn);
+    if (r != CUDA_SUCCESS) {
+        *err = cu_error("cuFuncGetAttribute", r);
+        return cudaErrorUnknown;
+    }
+    *out = k.get();
+    g_kernels.emplace(key, std::move(k));
+    return cudaSuccess;
+}
+
+}  // namespace
+
+template <class T>
+cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols,
+                         const SpecKernel** kout, LaunchCfg* cfg, std::string* err) {
+    const std::string src = spec_source<T>(blob, a.off_bi, a.off_pd, a.off_pdmap, a.nb, a.nv, a.npd);
+    SpecKernel* k = nullptr;
+    cudaError_t e = get_kernel(src, spec_kernel_name<T>(a.feat, tm), &k, err);
+    if (e != cudaSuccess) return e;
+    int dev = 0;
+    DeviceLimits dl{0, 0};
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+        *err = cudaGetErrorString(e);
+        return e;
+    }
+    const Driver& drv = driver();
+    const int dyn_cap = dl.smem_optin - k->static_smem;
+    CUresult r = drv.set_attr(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_cap);
+    if (r != CUDA_SUCCESS) {
+        *err = cu_error("cuFuncSetAttribute", r);
+        return cudaErrorUnknown;
+    }
+    CUfunction fn = k->fn;
+    auto occupancy = [&drv, fn](int* blocks, int W, size_t smem) {
+        return drv.occupancy(blocks, fn, W, smem) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+    };
+    e = pick_launch(dl, dyn_cap, tm, (int)sizeof(T), a.scratch, a.model_bytes, a.nworld, tmem_cols,
+                    (int)TMEM_COLS, occupancy, cfg);
+    if (e != cudaSuccess) {
+        *err = "no launch shape fits the specialized rollout kernel";
+        return e;
+    }
+    *kout = k;
+    return cudaSuccess;
+}
+
+template <class T>
+cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
+    if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
+    RolloutArgs<T> args = a;
+    void* params[] = {&args};
+    const CUresult r = driver().launch(k->fn, (unsigned)cfg.grid, 1, 1, (unsigned)cfg.W, 1, 1, (unsigned)cfg.smem,
+                                       (CUstream)s, params, nullptr);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
+}
+
+template cudaError_t spec_prepare<float>(const unsigned char*, const RolloutArgs<float>&, bool, int,
+                                         const SpecKernel**, LaunchCfg*, std::string*);
+template cudaError_t spec_prepare<double>(const unsigned char*, const RolloutArgs<double>&, bool, int,
+                                          const SpecKernel**, LaunchCfg*, std::string*);
+template cudaError_t spec_launch<float>(const SpecKernel*, const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
+template cudaError_t spec_launch<double>(const SpecKernel*, const RolloutArgs<double>&, const LaunchCfg&,
+                                         cudaStream_t);
+
+}  // namespace pz

@@ -19,15 +19,17 @@
 // (precision, feature set) pair per translation unit.
 #pragma once
 
+#ifndef __CUDACC_RTC__
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
-#include <type_traits>
 
 #include "pz_variants.h"
+#endif
+#include "pz_launch.h"
 #include "pz_world.cuh"
 
 namespace pz {
@@ -167,12 +169,15 @@ struct TmemScr : SmemScr<T> {
 template <class T>
 __device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const unsigned char* blob) {
     ModelView<T> M;
-    M.bt = reinterpret_cast<const BodyT<T>*>(blob);
+    M.btp = reinterpret_cast<const BodyT<T>*>(blob);
+#ifndef PZ_SPEC
+    M.bt = M.btp;
     M.bi = reinterpret_cast<const BodyI*>(blob + P.off_bi);
     M.pd = reinterpret_cast<const PdT<T>*>(blob + P.off_pd);
     M.pd_of_dof = reinterpret_cast<const int*>(blob + P.off_pdmap);
     M.nb = P.nb;
     M.nv = P.nv;
+#endif
     M.npd = P.npd;
     M.contact = P.contact;
     M.dt = T(P.dt);
@@ -221,9 +226,15 @@ __device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, 
     return smem;
 }
 
-// TMEM columns allocated per block by the Tensor-Memory variant: the whole
-// array (one block per SM).
-constexpr unsigned TMEM_COLS = 512;
+
+template <bool TM, class T>
+struct PickScr {
+    using type = SmemScr<T>;
+};
+template <class T>
+struct PickScr<true, T> {
+    using type = TmemScr<T>;
+};
 
 template <class T, int FEAT, bool TM>
 __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
@@ -232,7 +243,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
     const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
     const ModelView<T> M = make_view<T>(P, blob);
     const int W = blockDim.x;
-    using Scr = typename std::conditional<TM, TmemScr<T>, SmemScr<T>>::type;
+    using Scr = typename PickScr<TM, T>::type;
     Scr S;
     S.base = reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x;
     S.W = W;
@@ -261,16 +272,19 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         // every warp stays converged for the warp-wide tcgen05 operations
         const bool active = wt < N;
         const long long w = active ? wt : N - 1;
+        PZ_UNROLL_BODIES
         for (int j = 0; j < M.nv; j++) {
             S(j) = P.q[j * N + w];
             S(M.nv + j) = P.v[j * N + w];
         }
         const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
+        PZ_UNROLL_BODIES
         for (int i = 0; i < M.nb; i++) prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, M.bi[i], S, io, 0);
         S.commit();
         if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
             // the wrenches of the previous step's last sweep and the staged
             // impulses that warm-start this one
+            PZ_UNROLL_BODIES
             for (int i = 0; i < M.nb; i++) {
                 const BodyI bi = M.bi[i];
                 if (bi.c_imp < 0) continue;
@@ -321,6 +335,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         S.wait();
         if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
             if (active)
+                PZ_UNROLL_BODIES
                 for (int i = 0; i < M.nb; i++) {
                     const BodyI bi = M.bi[i];
                     if (bi.c_imp < 0) continue;
@@ -335,6 +350,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         }
         if (active) {
             bool finite = true;
+            PZ_UNROLL_BODIES
             for (int j = 0; j < M.nv; j++) {
                 const T qj = S(j), vj = S(M.nv + j);
                 finite = finite && pz_finite(qj) && pz_finite(vj);
@@ -374,15 +390,18 @@ __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ 
         const long long w = tile * W + threadIdx.x;
         if (w >= P.nworld) continue;
         const long long N = P.nworld;
+        PZ_UNROLL_BODIES
         for (int j = 0; j < M.nv; j++) {
             S(j) = P.q[j * N + w];
             S(M.nv + j) = P.v[j * N + w];
         }
         if (kind == 1) {
+            PZ_UNROLL_BODIES
             for (int j = 0; j < M.nv; j++) acc += S(j) * S(j);
             continue;
         }
         pass1_all<FEAT & (FEAT_MULTI | FEAT_PERM | FEAT_PERM1)>(M, S);
+        PZ_UNROLL_BODIES
         for (int i = 0; i < M.nb; i++) {
             const BodyI bi = M.bi[i];
             const BodyT<T>& bt = M.bt[i];
@@ -401,70 +420,27 @@ __global__ void __launch_bounds__(256) objective_kernel(const __grid_constant__ 
     if ((threadIdx.x & 31) == 0) atomicAdd(out, acc);
 }
 
+#ifndef __CUDACC_RTC__
 template <class T, int FEAT, bool TM>
 cudaError_t config_variant(const DeviceLimits& dl, int scratch, int model_bytes, long long nworld, int tmem_cols,
                            LaunchCfg* out) {
-    const int smem_optin = dl.smem_optin, sm_count = dl.sm_count;
     // the opt-in limit covers static and dynamic shared memory together
     cudaFuncAttributes fa{};
     cudaError_t e = cudaFuncGetAttributes(&fa, rollout_kernel<T, FEAT, TM>);
     if (e != cudaSuccess) return e;
-    const int dyn_cap = smem_optin - (int)fa.sharedSizeBytes;
+    const int dyn_cap = dl.smem_optin - (int)fa.sharedSizeBytes;
     e = cudaFuncSetAttribute(rollout_kernel<T, FEAT, TM>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_cap);
     if (e != cudaSuccess) return e;
     if (!TM) {
         e = cudaFuncSetAttribute(objective_kernel<T, FEAT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smem_optin);
+                                 dl.smem_optin);
         if (e != cudaSuccess) return e;
     }
-    const long long per_world = (long long)scratch * (long long)sizeof(T);
-    // Pick the block width that keeps the most worlds resident per SM,
-    // discounted by how full the last wave of tiles is. Shared-memory layout:
-    // any even width up to the 256 of __launch_bounds__. Tensor-Memory layout:
-    // whole warps, one block per SM, and few enough warps per TMEM lane
-    // quarter that each thread's columns hold its records.
-    // PHYZB_WORLDS_PER_BLOCK overrides the width for tuning.
-    int forced = 0;
-    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
-    int best_w = 0, best_blocks = 0, best_smem = 0;
-    double best_score = -1.0;
-    const int step = TM ? 32 : 2;
-    for (int W = 32; W <= 256; W += step) {
-        if (forced > 0 && W != forced) continue;
-        if (TM) {
-            const int per_quarter = ((W + 31) / 32 + 3) / 4;
-            if (tmem_cols * per_quarter > (int)TMEM_COLS) break;
-        }
-        long long smem = (long long)model_bytes + per_world * W;
-        if (smem > dyn_cap) break;
-        // Tensor-Memory blocks ask for more than half an SM's shared memory so
-        // that no second block lands on the SM and waits on the allocation
-        if (TM) smem = std::max(smem, (long long)(smem_optin / 2 + 16) & ~15LL);
-        int blocks = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, rollout_kernel<T, FEAT, TM>, W, (size_t)smem);
-        if (e != cudaSuccess) return e;
-        if (blocks <= 0) continue;
-        if (TM) blocks = 1;  // each block holds the whole Tensor Memory
-        const double resident = (double)blocks * W * sm_count;  // worlds in flight on the GPU
-        const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
-        const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
-        const double score = (double)blocks * W * used;
-        if (score > best_score * 1.0001) {
-            best_score = score;
-            best_w = W;
-            best_blocks = blocks;
-            best_smem = (int)smem;
-        }
-    }
-    if (best_w == 0) return cudaErrorInvalidConfiguration;
-    const long long ntiles = (nworld + best_w - 1) / best_w;
-    const long long cap = (long long)sm_count * best_blocks;
-    out->W = best_w;
-    out->grid = (int)(ntiles < cap ? (ntiles > 0 ? ntiles : 1) : cap);
-    out->smem = best_smem;
-    out->tm = TM ? 1 : 0;
-    out->score = best_score;
-    return cudaSuccess;
+    auto occupancy = [](int* blocks, int W, size_t smem) {
+        return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, rollout_kernel<T, FEAT, TM>, W, smem);
+    };
+    return pick_launch(dl, dyn_cap, TM, (int)sizeof(T), scratch, model_bytes, nworld, tmem_cols, (int)TMEM_COLS,
+                       occupancy, out);
 }
 
 template <class T, int FEAT, bool TM>
@@ -476,5 +452,6 @@ template <class T, int FEAT>
 void launch_objective_variant(const RolloutArgs<T>& a, const LaunchCfg& cfg, int kind, T* out, cudaStream_t s) {
     objective_kernel<T, FEAT><<<cfg.grid, cfg.W, cfg.smem, s>>>(a, kind, out);
 }
+#endif  // __CUDACC_RTC__
 
 }  // namespace pz
