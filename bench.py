@@ -110,7 +110,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--specialize", default="auto", choices=["auto", "0", "1"],
                     help="rollout kernel: 1 compiled at run time for the model (tables literal, loops "
-                         "unrolled), 0 the generic variant, auto 1 for models of at most 16 bodies")
+                         "unrolled), 0 the generic variant, auto 1 unless the model's longest chain "
+                         "exceeds 16 bodies")
     return ap.parse_args()
 
 

@@ -418,8 +418,8 @@ class BatchSim:
     def specialize(self):
         """Kernel specialization mode: False (generic variants), True (the
         rollout kernel compiled at run time for this model: tables literal,
-        body loops unrolled) or "auto" (True for models of at most
-        PHYZB_SPECIALIZE_AUTO_MAX_BODIES bodies). The compile happens at the
+        body loops unrolled) or "auto" (True for branching models whose
+        longest chain has at most 16 bodies). The compile happens at the
         next launch after any table change and is cached in-process and on
         disk."""
         mode = C.c_int32()

@@ -105,6 +105,14 @@ void set_model_copy(phyzb_sim* s, const phyzb_model* m) {
     s->bodies.assign(m->bodies, m->bodies + m->nbodies);
     s->model = *m;
     s->model.bodies = s->bodies.data();
+    // bodies on the longest root-to-leaf path (parents precede children)
+    std::vector<int> d(s->bodies.size(), 1);
+    s->depth = 0;
+    for (size_t i = 0; i < s->bodies.size(); i++) {
+        const int p = s->bodies[i].parent;
+        if (p >= 0 && (size_t)p < i) d[i] = d[p] + 1;
+        s->depth = std::max(s->depth, d[i]);
+    }
 }
 
 template <class T>
@@ -169,7 +177,8 @@ pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long 
 
 bool specialized(const phyzb_sim* s) {
     return s->specialize == PHYZB_SPECIALIZE_ON ||
-           (s->specialize == PHYZB_SPECIALIZE_AUTO && s->nb <= PHYZB_SPECIALIZE_AUTO_MAX_BODIES);
+           (s->specialize == PHYZB_SPECIALIZE_AUTO && s->depth <= PHYZB_SPECIALIZE_AUTO_MAX_DEPTH &&
+            s->nb <= PHYZB_SPECIALIZE_AUTO_MAX_BODIES);
 }
 
 template <class T>
@@ -179,8 +188,10 @@ int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
     if (specialized(s)) {
         if (!L.spec) {
             std::string err;
-            const cudaError_t e = pz::spec_prepare<T>(L.host.data(), a, L.launch.tm != 0, L.info.tmem_cols, &L.spec,
-                                                      &L.spec_launch, &err);
+            // the generic variant's block width: the specialized kernel's
+            // registers and shared memory per world are the same budget
+            const cudaError_t e = pz::spec_prepare<T>(L.host.data(), a, L.launch.tm != 0, L.info.tmem_cols,
+                                                      L.launch.W, &L.spec, &L.spec_launch, &err);
             if (e != cudaSuccess) {
                 cudaGetLastError();
                 L.spec = nullptr;

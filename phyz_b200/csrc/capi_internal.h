@@ -86,6 +86,7 @@ struct phyzb_sim {
     int device = 0, precision = PHYZB_F64;
     long long nworld = 0;
     int nb = 0, nv = 0;
+    int depth = 0;  // bodies on the model's longest root-to-leaf path
     std::vector<phyzb_body> bodies;
     phyzb_model model{};  // points into `bodies`
     pz::PackCfg cfg;

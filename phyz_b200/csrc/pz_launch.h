@@ -86,9 +86,10 @@ cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int w
 // default $HOME/.cache/phyzb; "0" turns the disk cache off).
 struct SpecKernel;
 // Compile or fetch the kernel of the table in `blob` (host copy of
-// a.model_blob) and size its launch. On failure *err says why.
+// a.model_blob) for blocks of W worlds and size its launch. On failure *err
+// says why.
 template <class T>
-cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols,
+cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols, int W,
                          const SpecKernel** k, LaunchCfg* cfg, std::string* err);
 template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);

@@ -89,8 +89,9 @@ struct alignas(16) BodyI {
     int fshift;       // this body's frame relabelling: stored = P_fshift (original coordinates)
     int s_pimp;       // impulse mode, F_PLANE: staged impulses against the plane per point
     // impulse mode: what the sweeps need to propagate a wrench change alone
-    int s_dinv;       // 1-DOF: D^-1 (0: a singular body); ball/free: the Cholesky factor of D,
-                      // row-major lower triangle (its first entry 0: singular)
+    int s_dinv;       // 1-DOF: D^-1 (0: a singular body); ball/free: the Cholesky factor L of D,
+                      // row-major lower triangle with 1 / L_aa on the diagonal (first entry 0:
+                      // singular)
     int s_w0b;        // D^-1 u of the step's full backward sweep (ndof)
     int s_fp;         // F_EXTF: the wrench that backward sweep applied (6)
 };

@@ -6,10 +6,13 @@
 // writes a translation unit that defines the same tables as literal
 // constants (namespace pz::spec, declared in pz_model.cuh) and includes the
 // unchanged kernel source with PZ_SPEC set: every body loop then unrolls,
-// the per-body kind dispatch and flag tests fold away, and table entries
-// become immediates of the instructions that use them. The arithmetic is the
-// generic kernel's, operation for operation; the runtime compiler
-// (spec.cu) turns the text into a kernel for the device in use.
+// the per-body kind dispatch and flag tests fold away, table entries become
+// immediates of the instructions that use them, and with the block width
+// fixed every scratch slot is an immediate shared-memory offset. The source
+// and its operations are the generic kernel's (the compiler may fuse a
+// different product of a sum into an FMA once constants fold, so results
+// agree to rounding); the runtime compiler (spec.cu) turns the text into a
+// kernel for the device in use.
 #pragma once
 
 #include <cmath>
@@ -60,16 +63,19 @@ std::string spec_kernel_name(int feat, bool tm) {
 }
 
 // The translation unit for the model packed in `blob` (BodyT[nb] at 0,
-// BodyI[nb] at off_bi, PdT[npd] at off_pd, int[nv] at off_pdmap).
+// BodyI[nb] at off_bi, PdT[npd] at off_pd, int[nv] at off_pdmap), launched
+// with blocks of W threads (W worlds per block).
 template <class T>
-std::string spec_source(const unsigned char* blob, int off_bi, int off_pd, int off_pdmap, int nb, int nv, int npd) {
+std::string spec_source(const unsigned char* blob, int off_bi, int off_pd, int off_pdmap, int nb, int nv, int npd,
+                        int W) {
     const char* tn = spec_type_name<T>();
     std::string o;
     o.reserve(4096 + (size_t)nb * 1536);
     o += "// model-specialized rollout kernel: " + std::to_string(nb) + " bodies, " + std::to_string(nv) +
-         " DOFs, " + tn + "\n";
+         " DOFs, " + tn + ", " + std::to_string(W) + " worlds per block\n";
     o += "#define PZ_SPEC 1\n#define PZ_SPEC_NB " + std::to_string(nb) + "\n#define PZ_SPEC_NV " +
-         std::to_string(nv) + "\n#include \"pz_model.cuh\"\n\nnamespace pz {\nnamespace spec {\n\n";
+         std::to_string(nv) + "\n#define PZ_SPEC_W " + std::to_string(W) +
+         "\n#include \"pz_model.cuh\"\n\nnamespace pz {\nnamespace spec {\n\n";
     // body integer table
     o += "__device__ __forceinline__ BodyI body(int i) {\n    switch (i) {\n";
     for (int i = 0; i < nb; i++) {

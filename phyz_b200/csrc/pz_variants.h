@@ -32,14 +32,15 @@ struct DeviceLimits {
 // layout: whole warps, one block per SM, and few enough warps per TMEM lane
 // quarter that each thread's columns hold its records. `occupancy(&blocks,
 // W, smem)` asks the runtime about the kernel being configured; dyn_cap is
-// its dynamic shared-memory limit. PHYZB_WORLDS_PER_BLOCK overrides the
-// width for tuning.
+// its dynamic shared-memory limit. `only_w` > 0 (a kernel compiled for one
+// width), else PHYZB_WORLDS_PER_BLOCK for tuning, fixes the width.
 template <class Occ>
 cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, int scratch, int model_bytes,
-                        long long nworld, int tmem_cols, int tmem_total, Occ occupancy, LaunchCfg* out) {
+                        long long nworld, int tmem_cols, int tmem_total, Occ occupancy, LaunchCfg* out,
+                        int only_w = 0) {
     const long long per_world = (long long)scratch * (long long)esz;
-    int forced = 0;
-    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK")) forced = atoi(env);
+    int forced = only_w;
+    if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK"); env && forced <= 0) forced = atoi(env);
     int best_w = 0, best_blocks = 0, best_smem = 0;
     double best_score = -1.0;
     const int step = tm ? 32 : 2;

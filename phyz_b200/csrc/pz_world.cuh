@@ -95,11 +95,12 @@ PZ_HD Q4<T> qmul(const Q4<T>& a, const Q4<T>& b) {
 template <class T>
 PZ_HD Q4<T> qnormalize(const Q4<T>& q) {
     const T n = pz_sqrt(q.w * q.w + q.x * q.x + q.y * q.y + q.z * q.z);
+    const T inv = T(1) / n;
     Q4<T> r;
-    r.w = q.w / n;
-    r.x = q.x / n;
-    r.y = q.y / n;
-    r.z = q.z / n;
+    r.w = q.w * inv;
+    r.x = q.x * inv;
+    r.y = q.y * inv;
+    r.z = q.z * inv;
     return r;
 }
 template <class T>
@@ -607,8 +608,9 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
     for (int r = 0; r < 6; r++)
 #pragma unroll
         for (int k = 0; k < ND; k++) U[r][k] = ai_el(I, r, k);
-    // Cholesky of D = U[0..ND) + d_extra 1
-    T L[ND][ND];
+    // Cholesky of D = U[0..ND) + d_extra 1; the substitutions multiply by
+    // the reciprocal diagonal (one division per row instead of one per use)
+    T L[ND][ND], Linv[ND];
 #pragma unroll
     for (int a = 0; a < ND; a++)
 #pragma unroll
@@ -629,6 +631,7 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
         const T ld = pz_sqrt(d);
         L[a][a] = ld;
         const T inv = T(1) / ld;
+        Linv[a] = inv;
 #pragma unroll
         for (int b = a + 1; b < ND; b++) {
             T e = U[b][a];
@@ -641,7 +644,8 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
 #pragma unroll
         for (int a = 0; a < ND; a++)
 #pragma unroll
-            for (int b = 0; b <= a; b++) S(bi.s_dinv + a * (a + 1) / 2 + b) = ok ? L[a][b] : T(0);
+            for (int b = 0; b <= a; b++)
+                S(bi.s_dinv + a * (a + 1) / 2 + b) = ok ? (b == a ? Linv[a] : L[a][b]) : T(0);
     }
     if (!ok) {
 #pragma unroll
@@ -657,14 +661,14 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
             T e = x[a];
 #pragma unroll
             for (int k = 0; k < a; k++) e = e - L[a][k] * x[k];
-            x[a] = e / L[a][a];
+            x[a] = e * Linv[a];
         }
 #pragma unroll
         for (int a = ND - 1; a >= 0; a--) {
             T e = x[a];
 #pragma unroll
             for (int k = a + 1; k < ND; k++) e = e - L[k][a] * x[k];
-            x[a] = e / L[a][a];
+            x[a] = e * Linv[a];
         }
     };
     // W row r = D^-1 U row r (D symmetric)
@@ -1112,9 +1116,14 @@ PZ_HD WF<T> world_frame(const ModelView<T>& M, const Scr& S, int i) {
     // columns of the body->world rotation and the origin, built upwards
     V3<T> cx = mk3<T>(T(1), T(0), T(0)), cy = mk3<T>(T(0), T(1), T(0)), cz = mk3<T>(T(0), T(0), T(1));
     V3<T> o = zero3<T>();
-    for (int b = i; b >= 0; b = M.bi[b].parent) {
+    // (at most nb ancestors: the bound lets a specialized build unroll the
+    // walk with every ancestor's table entry folded)
+    int b = i;
+    PZ_UNROLL_BODIES
+    for (int k = 0; k < M.nb && b >= 0; k++) {
         const BodyI bb = M.bi[b];
         const BodyT<T>& tb = M.bt[b];
+        b = bb.parent;
         JX<T> j;
         if (bb.t_rec >= 0) {
             const Rec<T> r = S.rec_get(bb);
@@ -1986,14 +1995,14 @@ PZ_HD bool wrench_multi(const BodyI& bi, const Scr& S, SV<T>& dp) {
             T e = du[a];
 #pragma unroll
             for (int k = 0; k < a; k++) e = e - S(bi.s_dinv + a * (a + 1) / 2 + k) * x[k];
-            x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+            x[a] = e * S(bi.s_dinv + a * (a + 1) / 2 + a);  // the stored diagonal is 1 / L_aa
         }
 #pragma unroll
         for (int a = ND - 1; a >= 0; a--) {
             T e = x[a];
 #pragma unroll
             for (int k = a + 1; k < ND; k++) e = e - S(bi.s_dinv + k * (k + 1) / 2 + a) * x[k];
-            x[a] = e / S(bi.s_dinv + a * (a + 1) / 2 + a);
+            x[a] = e * S(bi.s_dinv + a * (a + 1) / 2 + a);
         }
     }
 #pragma unroll

@@ -338,9 +338,9 @@ cudaError_t get_kernel(const std::string& src, const std::string& name, SpecKern
 }  // namespace
 
 template <class T>
-cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols,
+cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols, int W,
                          const SpecKernel** kout, LaunchCfg* cfg, std::string* err) {
-    const std::string src = spec_source<T>(blob, a.off_bi, a.off_pd, a.off_pdmap, a.nb, a.nv, a.npd);
+    const std::string src = spec_source<T>(blob, a.off_bi, a.off_pd, a.off_pdmap, a.nb, a.nv, a.npd, W);
     SpecKernel* k = nullptr;
     cudaError_t e = get_kernel(src, spec_kernel_name<T>(a.feat, tm), &k, err);
     if (e != cudaSuccess) return e;
@@ -364,9 +364,9 @@ cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, boo
         return drv.occupancy(blocks, fn, W, smem) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
     };
     e = pick_launch(dl, dyn_cap, tm, (int)sizeof(T), a.scratch, a.model_bytes, a.nworld, tmem_cols,
-                    (int)TMEM_COLS, occupancy, cfg);
+                    (int)TMEM_COLS, occupancy, cfg, W);
     if (e != cudaSuccess) {
-        *err = "no launch shape fits the specialized rollout kernel";
+        *err = "the specialized rollout kernel does not launch with " + std::to_string(W) + " worlds per block";
         return e;
     }
     *kout = k;
@@ -383,9 +383,9 @@ cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const Laun
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
 }
 
-template cudaError_t spec_prepare<float>(const unsigned char*, const RolloutArgs<float>&, bool, int,
+template cudaError_t spec_prepare<float>(const unsigned char*, const RolloutArgs<float>&, bool, int, int,
                                          const SpecKernel**, LaunchCfg*, std::string*);
-template cudaError_t spec_prepare<double>(const unsigned char*, const RolloutArgs<double>&, bool, int,
+template cudaError_t spec_prepare<double>(const unsigned char*, const RolloutArgs<double>&, bool, int, int,
                                           const SpecKernel**, LaunchCfg*, std::string*);
 template cudaError_t spec_launch<float>(const SpecKernel*, const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t spec_launch<double>(const SpecKernel*, const RolloutArgs<double>&, const LaunchCfg&,

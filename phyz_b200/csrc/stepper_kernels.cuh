@@ -36,11 +36,17 @@ namespace pz {
 
 
 // Per-thread view of the shared-memory scratch: slot s of this world lives
-// at base[s * W] (consecutive threads -> consecutive banks).
+// at base[s * W] (consecutive threads -> consecutive banks). A specialized
+// build fixes W (the block width) at compile time, so every slot access is
+// one load or store at an immediate offset from `base`.
 template <class T>
 struct SmemScr {
     T* base;
+#ifdef PZ_SPEC
+    static constexpr int W = PZ_SPEC_W;
+#else
     int W;
+#endif
     __device__ __forceinline__ T& operator()(int s) const { return base[s * W]; }
     __device__ __forceinline__ void prefetch(int s, const T* g) const {
         const unsigned sa = (unsigned)__cvta_generic_to_shared(&base[s * W]);
@@ -242,11 +248,17 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
     __shared__ unsigned tmem_slot;
     const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
     const ModelView<T> M = make_view<T>(P, blob);
+#ifdef PZ_SPEC
+    constexpr int W = PZ_SPEC_W;  // the launch's block width
+#else
     const int W = blockDim.x;
+#endif
     using Scr = typename PickScr<TM, T>::type;
     Scr S;
     S.base = reinterpret_cast<T*>(smem + P.model_bytes) + threadIdx.x;
+#ifndef PZ_SPEC
     S.W = W;
+#endif
     const int warp = threadIdx.x >> 5;
     if constexpr (TM) {
         if (warp == 0) {

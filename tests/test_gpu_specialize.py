@@ -121,13 +121,15 @@ def test_table_change_recompiles():
 
 
 def test_auto_mode_and_invalid_mode():
-    """"auto" specializes models of at most 16 bodies (C3's 13), not C2's 32;
-    a mode outside {0, 1, 2} is refused."""
+    """"auto" specializes trees whose longest chain has at most 16 bodies (the
+    quadruped, the 22-body humanoid), not the 32-body chain; a mode outside
+    {0, 1, 2} is refused."""
     from phyz_b200 import PhyzbError, _lib
 
-    for name, expect in (("c3_quadruped", True), ("c2_chain32", False)):
+    for name, expect in (("c3_quadruped", True), ("c4_humanoid", True), ("c2_chain32", False)):
         m = configs.CONFIGS[name].builder()
         sim = BatchSim(m, 64, precision="f32")
+        sim.specialize = False
         assert sim.specialize is False and not sim.specialized
         sim.specialize = "auto"
         assert sim.specialize == "auto" and sim.specialized == expect
