@@ -50,7 +50,6 @@ int upload_layout(phyzb_sim* s, phyzb_sim::Layout& L, const std::vector<unsigned
     }
     PZ_CUDA(cudaMemcpy(L.blob, blob.data(), L.info.bytes, cudaMemcpyHostToDevice));
     L.host = blob;
-    L.spec = nullptr;  // the table changed: specialize again at the next launch
     return PHYZB_OK;
 }
 
@@ -58,6 +57,7 @@ template <class T>
 int repack_t(phyzb_sim* s) {
     // kernels already queued may read the tables: drain the stream first
     PZ_CUDA(cudaStreamSynchronize(s->stream));
+    s->spec = nullptr;  // the tables change: specialize again at the next launch
     std::vector<unsigned char> blob;
     phyzb_sim::Layout& L0 = s->lay[0];
     L0.info = pz::pack_model<T>(&s->model, s->nv, s->cfg, blob, 0);
@@ -116,8 +116,8 @@ void set_model_copy(phyzb_sim* s, const phyzb_model* m) {
 }
 
 template <class T>
-pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const void* ctrl, long long stride, int nsteps, int layout) {
-    const phyzb_sim::Layout& L = s->lay[layout];
+pz::RolloutArgs<T> rollout_args(const phyzb_sim* s, const phyzb_sim::Layout& L, const void* ctrl, long long stride,
+                                int nsteps) {
     pz::RolloutArgs<T> a;
     a.model_blob = L.blob;
     a.model_bytes = L.info.bytes;
@@ -181,27 +181,67 @@ bool specialized(const phyzb_sim* s) {
             s->nb <= PHYZB_SPECIALIZE_AUTO_MAX_BODIES);
 }
 
+pz::SpecLayout spec_layout(const pz::PackInfo& i, const std::vector<unsigned char>& blob, bool tm, int w0) {
+    return pz::SpecLayout{blob.data(), i.bytes, i.off_bi, i.off_pd, i.off_pdmap, i.scratch, i.feat, i.tmem_cols, tm, w0};
+}
+
+// Compile the model-specialized kernel of the current tables: candidates
+// are the shared-memory layout and (unless PHYZB_TMEM=0; only it with
+// PHYZB_TMEM=1) a Tensor-Memory layout; the chosen table is uploaded into
+// spec_lay.
+template <class T>
+int prepare_spec(phyzb_sim* s) {
+    const phyzb_sim::Layout& L0 = s->lay[0];
+    std::vector<pz::SpecLayout> cands;
+    const char* env = getenv("PHYZB_TMEM");
+    if (!(env && env[0] == '1')) cands.push_back(spec_layout(L0.info, L0.host, false, L0.launch.W));
+    std::vector<unsigned char> tb;
+    pz::PackInfo ti{};
+    if (!(env && env[0] == '0')) {
+        for (int budget : {512, 256}) {
+            std::vector<unsigned char> b;
+            const pz::PackInfo i = pz::pack_model<T>(&s->model, s->nv, s->cfg, b, budget);
+            if (i.tmem_cols == 0) break;
+            pz::LaunchCfg c{};
+            if (pz::rollout_config<T>(i.scratch, i.bytes, s->nworld, i.feat, i.tmem_cols, &c) != cudaSuccess) {
+                cudaGetLastError();  // not launchable as a generic variant: try the smaller budget
+                continue;
+            }
+            tb.swap(b);
+            ti = i;
+            cands.push_back(spec_layout(ti, tb, true, c.W));
+            break;
+        }
+    }
+    if (cands.empty()) cands.push_back(spec_layout(L0.info, L0.host, false, L0.launch.W));
+    const pz::RolloutArgs<T> a = rollout_args<T>(s, L0, nullptr, 0, 1);
+    int chosen = 0;
+    const pz::SpecKernel* k = nullptr;
+    pz::LaunchCfg cfg{};
+    std::string err;
+    const cudaError_t e = pz::spec_prepare<T>(cands.data(), (int)cands.size(), a, &chosen, &k, &cfg, &err);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(PHYZB_ERR_CUDA, err);
+    }
+    const bool tm = cands[chosen].tm;
+    s->spec_lay.info = tm ? ti : L0.info;
+    PZ_TRY(upload_layout(s, s->spec_lay, tm ? tb : L0.host));
+    s->spec_lay.launch = cfg;
+    s->spec = k;
+    return PHYZB_OK;
+}
+
 template <class T>
 int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
-    phyzb_sim::Layout& L = s->lay[s->use];
-    const pz::RolloutArgs<T> a = rollout_args<T>(s, ctrl, stride, nsteps, s->use);
     if (specialized(s)) {
-        if (!L.spec) {
-            std::string err;
-            // the generic variant's block width: the specialized kernel's
-            // registers and shared memory per world are the same budget
-            const cudaError_t e = pz::spec_prepare<T>(L.host.data(), a, L.launch.tm != 0, L.info.tmem_cols,
-                                                      L.launch.W, &L.spec, &L.spec_launch, &err);
-            if (e != cudaSuccess) {
-                cudaGetLastError();
-                L.spec = nullptr;
-                return fail(PHYZB_ERR_CUDA, err);
-            }
-        }
-        PZ_CUDA(pz::spec_launch<T>(L.spec, a, L.spec_launch, s->stream));
+        if (!s->spec) PZ_TRY(prepare_spec<T>(s));
+        const pz::RolloutArgs<T> a = rollout_args<T>(s, s->spec_lay, ctrl, stride, nsteps);
+        PZ_CUDA(pz::spec_launch<T>(s->spec, a, s->spec_lay.launch, s->stream));
         return PHYZB_OK;
     }
-    PZ_CUDA(pz::launch_rollout<T>(a, L.launch, s->stream));
+    const phyzb_sim::Layout& L = s->lay[s->use];
+    PZ_CUDA(pz::launch_rollout<T>(rollout_args<T>(s, L, ctrl, stride, nsteps), L.launch, s->stream));
     return PHYZB_OK;
 }
 
@@ -421,6 +461,7 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(st);
     free_ptr(s->lay[0].blob);
     free_ptr(s->lay[1].blob);
+    free_ptr(s->spec_lay.blob);
     free_ptr(s->staging);
     free_ptr(s->hist_q);
     free_ptr(s->hist_v);
@@ -880,9 +921,9 @@ int phyzb_objective_device(phyzb_sim* s, int kind, void* out) {
     if (kind != 0 && kind != 1) return fail(PHYZB_ERR_INVALID, "objective kind must be 0 or 1");
     if (!out) return fail(PHYZB_ERR_INVALID, "output is null");
     DeviceGuard g(s->device);
-    cudaError_t e = is_f64(s) ? pz::launch_objective<double>(rollout_args<double>(s, s->ctrl, 0, 1, 0),
+    cudaError_t e = is_f64(s) ? pz::launch_objective<double>(rollout_args<double>(s, s->lay[0], s->ctrl, 0, 1),
                                                              s->lay[0].launch, kind, (double*)out, s->stream)
-                              : pz::launch_objective<float>(rollout_args<float>(s, s->ctrl, 0, 1, 0),
+                              : pz::launch_objective<float>(rollout_args<float>(s, s->lay[0], s->ctrl, 0, 1),
                                                             s->lay[0].launch, kind, (float*)out, s->stream);
     PZ_CUDA(e);
     return PHYZB_OK;
@@ -915,11 +956,10 @@ int phyzb_get_kernel_specialization(const phyzb_sim* s, int32_t* mode, int32_t* 
 int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t* smem, int32_t* scratch,
                       int32_t* tmem_cols) {
     PZ_TRY(check_sim(s));
-    const phyzb_sim::Layout& L = s->lay[s->use];
-    const pz::LaunchCfg& c = specialized(s) && L.spec ? L.spec_launch : L.launch;
-    if (wpb) *wpb = c.W;
-    if (blocks) *blocks = c.grid;
-    if (smem) *smem = c.smem;
+    const phyzb_sim::Layout& L = specialized(s) && s->spec ? s->spec_lay : s->lay[s->use];
+    if (wpb) *wpb = L.launch.W;
+    if (blocks) *blocks = L.launch.grid;
+    if (smem) *smem = L.launch.smem;
     if (scratch) *scratch = L.info.scratch;
     if (tmem_cols) *tmem_cols = L.launch.tm ? L.info.tmem_cols : 0;
     return PHYZB_OK;

@@ -114,11 +114,13 @@ struct phyzb_sim {
         void* blob = nullptr;
         size_t cap = 0;
         pz::LaunchCfg launch{};
-        std::vector<unsigned char> host;        // the table as uploaded
-        const pz::SpecKernel* spec = nullptr;   // its model-specialized kernel, once compiled
-        pz::LaunchCfg spec_launch{};
+        std::vector<unsigned char> host;  // the table as uploaded
     } lay[2];
     int use = 0;
+    // the model-specialized kernel (null: not compiled since the last repack),
+    // its table layout and launch
+    const pz::SpecKernel* spec = nullptr;
+    Layout spec_lay;
     // PHYZB_SPECIALIZE_*: whether rollouts run the model-specialized kernel
     // (compiled at the first launch after each repack) or the generic variants
     int specialize = 0;

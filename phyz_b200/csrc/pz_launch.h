@@ -85,11 +85,21 @@ cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int w
 // process; compiled kernels are also kept on disk (PHYZB_KERNEL_CACHE,
 // default $HOME/.cache/phyzb; "0" turns the disk cache off).
 struct SpecKernel;
-// Compile or fetch the kernel of the table in `blob` (host copy of
-// a.model_blob) for blocks of W worlds and size its launch. On failure *err
-// says why.
+// One packed table the specialized kernel may run with.
+struct SpecLayout {
+    const unsigned char* blob;  // host copy of the table
+    int bytes, off_bi, off_pd, off_pdmap;
+    int scratch, feat, tmem_cols;
+    bool tm;                    // body records in Tensor Memory
+    int w0;                     // a block width the generic variant launches it with
+};
+// Compile (or fetch) the kernel of each candidate layout -- Tensor-Memory
+// ones widened past the generic variants' 256 threads as far as the compiled
+// kernel's registers and the layout's on-chip memory allow -- and keep the
+// best-scoring launch: *chosen indexes `lays`. a supplies the model's sizes
+// and the world count. On failure *err says why.
 template <class T>
-cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols, int W,
+cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a, int* chosen,
                          const SpecKernel** k, LaunchCfg* cfg, std::string* err);
 template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);

@@ -23,7 +23,9 @@ constexpr bool feat_valid(int f) {
 
 struct DeviceLimits {
     int sm_count;
-    int smem_optin;  // opt-in shared memory per block (static + dynamic)
+    int smem_optin;         // opt-in shared memory per block (static + dynamic)
+    int regs_per_sm = 65536;
+    int max_threads = 1024;  // per block
 };
 
 // Pick the block width that keeps the most worlds resident per SM,
@@ -34,22 +36,27 @@ struct DeviceLimits {
 // W, smem)` asks the runtime about the kernel being configured; dyn_cap is
 // its dynamic shared-memory limit. `only_w` > 0 (a kernel compiled for one
 // width), else PHYZB_WORLDS_PER_BLOCK for tuning, fixes the width.
+// The TMEM columns each thread of a block of `warps` warps owns (warps
+// w, w+4, ... share lane quarter w % 4 and split its columns, whole 8-column
+// records each).
+inline int tmem_cols_per_thread(int warps, int tmem_total) {
+    const int per_quarter = (warps + 3) / 4;
+    return (tmem_total / per_quarter) & ~7;
+}
+
 template <class Occ>
 cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, int scratch, int model_bytes,
                         long long nworld, int tmem_cols, int tmem_total, Occ occupancy, LaunchCfg* out,
-                        int only_w = 0) {
+                        int only_w = 0, int max_w = 256) {
     const long long per_world = (long long)scratch * (long long)esz;
     int forced = only_w;
     if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK"); env && forced <= 0) forced = atoi(env);
     int best_w = 0, best_blocks = 0, best_smem = 0;
     double best_score = -1.0;
     const int step = tm ? 32 : 2;
-    for (int W = 32; W <= 256; W += step) {
+    for (int W = 32; W <= max_w; W += step) {
         if (forced > 0 && W != forced) continue;
-        if (tm) {
-            const int per_quarter = ((W + 31) / 32 + 3) / 4;
-            if (tmem_cols * per_quarter > tmem_total) break;
-        }
+        if (tm && tmem_cols > tmem_cols_per_thread((W + 31) / 32, tmem_total)) break;
         long long smem = (long long)model_bytes + per_world * W;
         if (smem > dyn_cap) break;
         // Tensor-Memory blocks ask for more than half an SM's shared memory so

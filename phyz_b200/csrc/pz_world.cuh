@@ -32,6 +32,9 @@
 // model-specialized build, where the table they index is literal.
 #ifdef PZ_SPEC
 #define PZ_UNROLL_BODIES _Pragma("unroll")
+#ifndef PZ_SPEC_INLINE_CONTACT
+#define PZ_SPEC_INLINE_CONTACT 1
+#endif
 #else
 #define PZ_UNROLL_BODIES
 #endif
@@ -1100,8 +1103,13 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
             if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
                 store(bi.s_up);  // the impulse sweeps read the body's frame
             } else {
+#if defined(PZ_SPEC) && PZ_SPEC_INLINE_CONTACT
+                // specialized: inline, the body's shape and gains literal
+                const SV<T> f = contact_wrench<TERRAIN>(M, bi, M.bt[i], wf, v, false, i, Out<T>{nullptr, 0});
+#else
                 const SV<T> f = contact_wrench_call<TERRAIN>(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, M.ter,
                                                              bi, M.btp + i, wf, v, false, i, Out<T>{nullptr, 0});
+#endif
                 st_sv(S, bi.s_f, f);
             }
         }

@@ -337,39 +337,126 @@ cudaError_t get_kernel(const std::string& src, const std::string& name, SpecKern
 
 }  // namespace
 
+namespace {
+
 template <class T>
-cudaError_t spec_prepare(const unsigned char* blob, const RolloutArgs<T>& a, bool tm, int tmem_cols, int W,
-                         const SpecKernel** kout, LaunchCfg* cfg, std::string* err) {
-    const std::string src = spec_source<T>(blob, a.off_bi, a.off_pd, a.off_pdmap, a.nb, a.nv, a.npd, W);
-    SpecKernel* k = nullptr;
-    cudaError_t e = get_kernel(src, spec_kernel_name<T>(a.feat, tm), &k, err);
-    if (e != cudaSuccess) return e;
-    int dev = 0;
-    DeviceLimits dl{0, 0};
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
-        (e = cudaDeviceGetAttribute(&dl.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
-        (e = cudaDeviceGetAttribute(&dl.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
-        *err = cudaGetErrorString(e);
-        return e;
-    }
-    const Driver& drv = driver();
+cudaError_t spec_compile(const SpecLayout& L, const RolloutArgs<T>& a, int W, SpecKernel** k, std::string* err) {
+    const std::string src = spec_source<T>(L.blob, L.off_bi, L.off_pd, L.off_pdmap, a.nb, a.nv, a.npd, W);
+    return get_kernel(src, spec_kernel_name<T>(L.feat, L.tm), k, err);
+}
+
+cudaError_t fn_attr(const SpecKernel* k, CUfunction_attribute at, int* v, std::string* err) {
+    const CUresult r = driver().attr(v, at, k->fn);
+    if (r == CUDA_SUCCESS) return cudaSuccess;
+    *err = cu_error("cuFuncGetAttribute", r);
+    return cudaErrorUnknown;
+}
+
+// Launch shape of kernel k (compiled for W threads) on layout L, scored like
+// the generic variants' (worlds resident per SM x fill of the last wave).
+template <class T>
+cudaError_t spec_config(const DeviceLimits& dl, const SpecKernel* k, const SpecLayout& L, const RolloutArgs<T>& a,
+                        int W, LaunchCfg* cfg, std::string* err) {
     const int dyn_cap = dl.smem_optin - k->static_smem;
+    const Driver& drv = driver();
     CUresult r = drv.set_attr(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, dyn_cap);
     if (r != CUDA_SUCCESS) {
         *err = cu_error("cuFuncSetAttribute", r);
         return cudaErrorUnknown;
     }
     CUfunction fn = k->fn;
-    auto occupancy = [&drv, fn](int* blocks, int W, size_t smem) {
-        return drv.occupancy(blocks, fn, W, smem) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
+    auto occupancy = [&drv, fn](int* blocks, int w, size_t smem) {
+        return drv.occupancy(blocks, fn, w, smem) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
     };
-    e = pick_launch(dl, dyn_cap, tm, (int)sizeof(T), a.scratch, a.model_bytes, a.nworld, tmem_cols,
-                    (int)TMEM_COLS, occupancy, cfg, W);
-    if (e != cudaSuccess) {
+    const cudaError_t e = pick_launch(dl, dyn_cap, L.tm, (int)sizeof(T), L.scratch, L.bytes, a.nworld, L.tmem_cols,
+                                      (int)TMEM_COLS, occupancy, cfg, W, W);
+    if (e != cudaSuccess)
         *err = "the specialized rollout kernel does not launch with " + std::to_string(W) + " worlds per block";
+    return e;
+}
+
+// The widest one-per-SM Tensor-Memory block that `regs` registers a thread,
+// the layout's shared memory per world and its TMEM columns per world allow.
+int tm_width_limit(const DeviceLimits& dl, int dyn_cap, int regs, int esz, const SpecLayout& L) {
+    const int regs_warp = ((regs * 32 + 255) / 256) * 256;  // the register file's allocation unit
+    int best = 0;
+    for (int W = 32; W <= dl.max_threads; W += 32) {
+        if ((W / 32) * regs_warp > dl.regs_per_sm) break;
+        if ((long long)L.bytes + (long long)L.scratch * esz * W > dyn_cap) break;
+        if (L.tmem_cols > tmem_cols_per_thread(W / 32, (int)TMEM_COLS)) break;
+        best = W;
+    }
+    return best;
+}
+
+}  // namespace
+
+template <class T>
+cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a, int* chosen,
+                         const SpecKernel** kout, LaunchCfg* cfg, std::string* err) {
+    int dev = 0;
+    DeviceLimits dl{0, 0};
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.regs_per_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev)) !=
+            cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&dl.max_threads, cudaDevAttrMaxThreadsPerBlock, dev)) != cudaSuccess) {
+        *err = cudaGetErrorString(e);
         return e;
     }
-    *kout = k;
+    double best = -1.0;
+    for (int li = 0; li < nlay; li++) {
+        const SpecLayout& L = lays[li];
+        SpecKernel* k = nullptr;
+        if ((e = spec_compile<T>(L, a, L.w0, &k, err)) != cudaSuccess) return e;
+        LaunchCfg c{};
+        int W = L.w0;
+        if (L.tm) {
+            // one block per SM: as wide as the compiled kernel's registers and
+            // the layout's on-chip memory per world allow, then compiled for it
+            int regs = 0;
+            if ((e = fn_attr(k, CU_FUNC_ATTRIBUTE_NUM_REGS, &regs, err)) != cudaSuccess) return e;
+            const int wmax = tm_width_limit(dl, dl.smem_optin - k->static_smem, regs, (int)sizeof(T), L);
+            LaunchCfg wide{};
+            auto fits = [wmax](int* blocks, int w, size_t) {
+                *blocks = w <= wmax ? 1 : 0;
+                return cudaSuccess;
+            };
+            if (wmax > 0 && pick_launch(dl, dl.smem_optin - k->static_smem, true, (int)sizeof(T), L.scratch, L.bytes,
+                                        a.nworld, L.tmem_cols, (int)TMEM_COLS, fits, &wide, 0, wmax) == cudaSuccess &&
+                wide.W != L.w0) {
+                SpecKernel* kw = nullptr;
+                std::string werr;
+                LaunchCfg cw{};
+                if (spec_compile<T>(L, a, wide.W, &kw, &werr) == cudaSuccess &&
+                    spec_config<T>(dl, kw, L, a, wide.W, &cw, &werr) == cudaSuccess) {
+                    k = kw;
+                    W = wide.W;
+                    c = cw;
+                }
+                cudaGetLastError();
+            }
+        }
+        if (c.W == 0 && (e = spec_config<T>(dl, k, L, a, W, &c, err)) != cudaSuccess) return e;
+        // A record in Tensor Memory is a tcgen05 load and wait the compiler
+        // cannot hoist, where a shared-memory slot is a load it schedules
+        // early; measured on B200, a specialized Tensor-Memory layout needs
+        // about twice the resident worlds to break even (C3 f32: 320 vs 256
+        // worlds per SM ran 16 % slower; C4 f32: 192 vs 128, 7 % slower).
+        const double score = L.tm ? c.score * 0.5 : c.score;
+        if (score > best * 1.0001) {
+            best = score;
+            *chosen = li;
+            *kout = k;
+            *cfg = c;
+        }
+    }
+    if (best < 0) {
+        *err = "no table layout to specialize";
+        return cudaErrorInvalidValue;
+    }
     return cudaSuccess;
 }
 
@@ -383,9 +470,9 @@ cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const Laun
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
 }
 
-template cudaError_t spec_prepare<float>(const unsigned char*, const RolloutArgs<float>&, bool, int, int,
+template cudaError_t spec_prepare<float>(const SpecLayout*, int, const RolloutArgs<float>&, int*,
                                          const SpecKernel**, LaunchCfg*, std::string*);
-template cudaError_t spec_prepare<double>(const unsigned char*, const RolloutArgs<double>&, bool, int, int,
+template cudaError_t spec_prepare<double>(const SpecLayout*, int, const RolloutArgs<double>&, int*,
                                           const SpecKernel**, LaunchCfg*, std::string*);
 template cudaError_t spec_launch<float>(const SpecKernel*, const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t spec_launch<double>(const SpecKernel*, const RolloutArgs<double>&, const LaunchCfg&,

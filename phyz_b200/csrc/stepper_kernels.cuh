@@ -233,6 +233,10 @@ __device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, 
 }
 
 
+#ifndef PZ_STEP_SYNC
+#define PZ_STEP_SYNC 0
+#endif
+
 template <bool TM, class T>
 struct PickScr {
     using type = SmemScr<T>;
@@ -242,8 +246,18 @@ struct PickScr<true, T> {
     using type = TmemScr<T>;
 };
 
+// Threads per block the kernel is compiled for: any width up to 256 in the
+// generic variants (up to 255 registers a thread); a specialized build is
+// compiled for its one width, which may go past 256 when its registers,
+// shared memory and Tensor Memory per world allow.
+#ifdef PZ_SPEC
+#define PZ_MAX_THREADS PZ_SPEC_W
+#else
+#define PZ_MAX_THREADS 256
+#endif
+
 template <class T, int FEAT, bool TM>
-__global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
+__global__ void __launch_bounds__(PZ_MAX_THREADS, 1) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ unsigned tmem_slot;
     const unsigned char* blob = stage_model(P.model_blob, P.model_bytes, smem);
@@ -273,7 +287,7 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         // warps w, w+4, w+8, ... share lane quarter w % 4 and split its columns
         const int nwarps = (W + 31) >> 5;
         const unsigned per_quarter = (unsigned)((nwarps + 3) >> 2);
-        const unsigned cols = TMEM_COLS / per_quarter;
+        const unsigned cols = (TMEM_COLS / per_quarter) & ~7u;  // whole 8-column records
         S.tbase = tmem_slot + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(warp >> 2) * cols;
     }
     const long long ntiles = (P.nworld + W - 1) / W;
@@ -314,6 +328,11 @@ __global__ void __launch_bounds__(256, 1) rollout_kernel(const __grid_constant__
         pass1_all<FEAT>(M, S);
         for (int s = 0; s < P.nsteps; s++) {
             S.wait();
+#if PZ_STEP_SYNC
+            // keep the block's warps on the same stretch of code (they share
+            // its instruction fetches); every thread runs every step
+            __syncthreads();
+#endif
             const bool last = s == P.nsteps - 1;
             if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
                 // contact state of the last step, from the state it starts from
