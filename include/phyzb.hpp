@@ -145,6 +145,9 @@ class BatchSim {
     void step() { check(phyzb_step(h_, 1)); }
     Result<Unit> try_step() { return status(phyzb_step(h_, 1)); }
     Result<Unit> step_many(int n) { return status(phyzb_step(h_, n)); }
+    // PHYZB_SPECIALIZE_OFF / _ON / _AUTO: the rollout kernel compiled at run
+    // time for this model (phyzb_set_kernel_specialization)
+    void set_kernel_specialization(int mode) { check(phyzb_set_kernel_specialization(h_, mode)); }
 
     // readback (cuda/mod.rs:978-996): rows of nv
     std::pair<std::vector<std::vector<double>>, std::vector<std::vector<double>>> readback_states() {

@@ -185,16 +185,101 @@ pz::SpecLayout spec_layout(const pz::PackInfo& i, const std::vector<unsigned cha
     return pz::SpecLayout{blob.data(), i.bytes, i.off_bi, i.off_pd, i.off_pdmap, i.scratch, i.feat, i.tmem_cols, tm, w0};
 }
 
+// Time each compiled candidate on scratch copies of the simulator's state
+// (one untimed launch of two steps, then one timed) and return the fastest:
+// whether more resident worlds beat the cheaper shared-memory record access
+// depends on the model, so the choice is measured, not modelled.
+template <class T>
+int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
+                      const std::vector<const std::vector<unsigned char>*>& hosts,
+                      const std::vector<pz::SpecChoice>& ch, size_t* best) {
+    struct Scratch {
+        std::vector<void*> p;
+        cudaEvent_t e0 = nullptr, e1 = nullptr;
+        ~Scratch() {
+            for (void* x : p) cudaFree(x);
+            if (e0) cudaEventDestroy(e0);
+            if (e1) cudaEventDestroy(e1);
+        }
+        void* alloc(size_t bytes) {
+            void* x = nullptr;
+            if (cudaMalloc(&x, bytes > 0 ? bytes : 16) != cudaSuccess) return nullptr;
+            p.push_back(x);
+            return x;
+        }
+    } sc;
+    const size_t sb = s->state_bytes();
+    void* q = sc.alloc(sb);
+    void* v = sc.alloc(sb);
+    void* qdd = sc.alloc(sb);
+    void* status = sc.alloc(2 * sizeof(int));
+    void* cs = s->cstate ? sc.alloc((size_t)s->nworld * s->nb * PHYZB_CONTACT_STRIDE * s->esz()) : nullptr;
+    void* imp = s->imp ? sc.alloc(s->imp_bytes) : nullptr;
+    std::vector<void*> blobs;
+    for (size_t i = 0; i < infos.size(); i++) blobs.push_back(sc.alloc(infos[i].bytes));
+    for (void* x : sc.p)
+        if (!x) return fail(PHYZB_ERR_CUDA, "cudaMalloc failed while timing the specialized kernels");
+    PZ_CUDA(cudaMemcpyAsync(q, s->q, sb, cudaMemcpyDeviceToDevice, s->stream));
+    PZ_CUDA(cudaMemcpyAsync(v, s->v, sb, cudaMemcpyDeviceToDevice, s->stream));
+    if (imp) PZ_CUDA(cudaMemcpyAsync(imp, s->imp, s->imp_bytes, cudaMemcpyDeviceToDevice, s->stream));
+    PZ_CUDA(cudaMemsetAsync(status, 0, 2 * sizeof(int), s->stream));
+    for (size_t i = 0; i < infos.size(); i++)
+        PZ_CUDA(cudaMemcpyAsync(blobs[i], hosts[i]->data(), infos[i].bytes, cudaMemcpyHostToDevice, s->stream));
+    PZ_CUDA(cudaEventCreate(&sc.e0));
+    PZ_CUDA(cudaEventCreate(&sc.e1));
+    float best_ms = -1.0f;
+    for (size_t c = 0; c < ch.size(); c++) {
+        phyzb_sim::Layout L;
+        L.info = infos[ch[c].layout];
+        L.blob = blobs[ch[c].layout];
+        pz::RolloutArgs<T> a = rollout_args<T>(s, L, s->ctrl, 0, 2);
+        a.q = (T*)q;
+        a.v = (T*)v;
+        a.qdd = (T*)qdd;
+        a.cstate = (T*)cs;
+        a.imp = (T*)imp;
+        a.status = (int*)status;
+        L.blob = nullptr;  // owned by the scratch
+        if (pz::spec_launch<T>(ch[c].k, a, ch[c].cfg, s->stream) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        PZ_CUDA(cudaEventRecord(sc.e0, s->stream));
+        if (pz::spec_launch<T>(ch[c].k, a, ch[c].cfg, s->stream) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        PZ_CUDA(cudaEventRecord(sc.e1, s->stream));
+        PZ_CUDA(cudaEventSynchronize(sc.e1));
+        float ms = 0.0f;
+        PZ_CUDA(cudaEventElapsedTime(&ms, sc.e0, sc.e1));
+        if (best_ms < 0.0f || ms < best_ms) {
+            best_ms = ms;
+            *best = c;
+        }
+    }
+    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    if (best_ms < 0.0f) return fail(PHYZB_ERR_CUDA, "no specialized kernel candidate launched");
+    return PHYZB_OK;
+}
+
 // Compile the model-specialized kernel of the current tables: candidates
 // are the shared-memory layout and (unless PHYZB_TMEM=0; only it with
-// PHYZB_TMEM=1) a Tensor-Memory layout; the chosen table is uploaded into
-// spec_lay.
+// PHYZB_TMEM=1) a Tensor-Memory layout, each at two widths; the fastest on
+// this simulator's state is kept and its table uploaded into spec_lay.
 template <class T>
 int prepare_spec(phyzb_sim* s) {
     const phyzb_sim::Layout& L0 = s->lay[0];
     std::vector<pz::SpecLayout> cands;
+    std::vector<pz::PackInfo> infos;
+    std::vector<const std::vector<unsigned char>*> hosts;
     const char* env = getenv("PHYZB_TMEM");
-    if (!(env && env[0] == '1')) cands.push_back(spec_layout(L0.info, L0.host, false, L0.launch.W));
+    auto add = [&](const pz::PackInfo& i, const std::vector<unsigned char>& b, bool tm, int w0) {
+        cands.push_back(spec_layout(i, b, tm, w0));
+        infos.push_back(i);
+        hosts.push_back(&b);
+    };
+    if (!(env && env[0] == '1')) add(L0.info, L0.host, false, L0.launch.W);
     std::vector<unsigned char> tb;
     pz::PackInfo ti{};
     if (!(env && env[0] == '0')) {
@@ -209,26 +294,25 @@ int prepare_spec(phyzb_sim* s) {
             }
             tb.swap(b);
             ti = i;
-            cands.push_back(spec_layout(ti, tb, true, c.W));
+            add(ti, tb, true, c.W);
             break;
         }
     }
-    if (cands.empty()) cands.push_back(spec_layout(L0.info, L0.host, false, L0.launch.W));
+    if (cands.empty()) add(L0.info, L0.host, false, L0.launch.W);
     const pz::RolloutArgs<T> a = rollout_args<T>(s, L0, nullptr, 0, 1);
-    int chosen = 0;
-    const pz::SpecKernel* k = nullptr;
-    pz::LaunchCfg cfg{};
+    std::vector<pz::SpecChoice> ch;
     std::string err;
-    const cudaError_t e = pz::spec_prepare<T>(cands.data(), (int)cands.size(), a, &chosen, &k, &cfg, &err);
-    if (e != cudaSuccess) {
+    if (pz::spec_candidates<T>(cands.data(), (int)cands.size(), a, &ch, &err) != cudaSuccess) {
         cudaGetLastError();
         return fail(PHYZB_ERR_CUDA, err);
     }
-    const bool tm = cands[chosen].tm;
-    s->spec_lay.info = tm ? ti : L0.info;
-    PZ_TRY(upload_layout(s, s->spec_lay, tm ? tb : L0.host));
-    s->spec_lay.launch = cfg;
-    s->spec = k;
+    size_t pick = 0;
+    if (ch.size() > 1) PZ_TRY(time_spec_choices<T>(s, infos, hosts, ch, &pick));
+    const int li = ch[pick].layout;
+    s->spec_lay.info = infos[li];
+    PZ_TRY(upload_layout(s, s->spec_lay, *hosts[li]));
+    s->spec_lay.launch = ch[pick].cfg;
+    s->spec = ch[pick].k;
     return PHYZB_OK;
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <string>
+#include <vector>
 #endif
 
 namespace pz {
@@ -93,14 +94,21 @@ struct SpecLayout {
     bool tm;                    // body records in Tensor Memory
     int w0;                     // a block width the generic variant launches it with
 };
-// Compile (or fetch) the kernel of each candidate layout -- Tensor-Memory
-// ones widened past the generic variants' 256 threads as far as the compiled
-// kernel's registers and the layout's on-chip memory allow -- and keep the
-// best-scoring launch: *chosen indexes `lays`. a supplies the model's sizes
-// and the world count. On failure *err says why.
+// A compiled candidate: layout index, kernel, launch shape.
+struct SpecChoice {
+    int layout;
+    const SpecKernel* k;
+    LaunchCfg cfg;
+};
+// Compile (or fetch) the candidate kernels of each layout: at the generic
+// variant's width, and at a second width -- a Tensor-Memory table as wide
+// as the compiled kernel's registers and the table's on-chip memory allow
+// (past the generic variants' 256 threads), a shared-memory table at whole
+// warps. a supplies the model's sizes and the world count. On failure *err
+// says why.
 template <class T>
-cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a, int* chosen,
-                         const SpecKernel** k, LaunchCfg* cfg, std::string* err);
+cudaError_t spec_candidates(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a,
+                            std::vector<SpecChoice>* out, std::string* err);
 template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
 #endif  // __CUDACC_RTC__

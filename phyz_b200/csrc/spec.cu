@@ -392,8 +392,8 @@ int tm_width_limit(const DeviceLimits& dl, int dyn_cap, int regs, int esz, const
 }  // namespace
 
 template <class T>
-cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a, int* chosen,
-                         const SpecKernel** kout, LaunchCfg* cfg, std::string* err) {
+cudaError_t spec_candidates(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a,
+                            std::vector<SpecChoice>* out, std::string* err) {
     int dev = 0;
     DeviceLimits dl{0, 0};
     cudaError_t e;
@@ -406,16 +406,19 @@ cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>&
         *err = cudaGetErrorString(e);
         return e;
     }
-    double best = -1.0;
+    out->clear();
     for (int li = 0; li < nlay; li++) {
         const SpecLayout& L = lays[li];
         SpecKernel* k = nullptr;
         if ((e = spec_compile<T>(L, a, L.w0, &k, err)) != cudaSuccess) return e;
         LaunchCfg c{};
-        int W = L.w0;
+        if ((e = spec_config<T>(dl, k, L, a, L.w0, &c, err)) != cudaSuccess) return e;
+        out->push_back(SpecChoice{li, k, c});
+        // a second width: Tensor-Memory tables as wide as the compiled
+        // kernel's registers and the table's on-chip memory per world allow
+        // (one block per SM); shared-memory tables at whole warps
+        int w2 = 0;
         if (L.tm) {
-            // one block per SM: as wide as the compiled kernel's registers and
-            // the layout's on-chip memory per world allow, then compiled for it
             int regs = 0;
             if ((e = fn_attr(k, CU_FUNC_ATTRIBUTE_NUM_REGS, &regs, err)) != cudaSuccess) return e;
             const int wmax = tm_width_limit(dl, dl.smem_optin - k->static_smem, regs, (int)sizeof(T), L);
@@ -425,35 +428,22 @@ cudaError_t spec_prepare(const SpecLayout* lays, int nlay, const RolloutArgs<T>&
                 return cudaSuccess;
             };
             if (wmax > 0 && pick_launch(dl, dl.smem_optin - k->static_smem, true, (int)sizeof(T), L.scratch, L.bytes,
-                                        a.nworld, L.tmem_cols, (int)TMEM_COLS, fits, &wide, 0, wmax) == cudaSuccess &&
-                wide.W != L.w0) {
-                SpecKernel* kw = nullptr;
-                std::string werr;
-                LaunchCfg cw{};
-                if (spec_compile<T>(L, a, wide.W, &kw, &werr) == cudaSuccess &&
-                    spec_config<T>(dl, kw, L, a, wide.W, &cw, &werr) == cudaSuccess) {
-                    k = kw;
-                    W = wide.W;
-                    c = cw;
-                }
-                cudaGetLastError();
-            }
+                                        a.nworld, L.tmem_cols, (int)TMEM_COLS, fits, &wide, 0, wmax) == cudaSuccess)
+                w2 = wide.W;
+        } else {
+            w2 = (L.w0 / 32) * 32;
         }
-        if (c.W == 0 && (e = spec_config<T>(dl, k, L, a, W, &c, err)) != cudaSuccess) return e;
-        // A record in Tensor Memory is a tcgen05 load and wait the compiler
-        // cannot hoist, where a shared-memory slot is a load it schedules
-        // early; measured on B200, a specialized Tensor-Memory layout needs
-        // about twice the resident worlds to break even (C3 f32: 320 vs 256
-        // worlds per SM ran 16 % slower; C4 f32: 192 vs 128, 7 % slower).
-        const double score = L.tm ? c.score * 0.5 : c.score;
-        if (score > best * 1.0001) {
-            best = score;
-            *chosen = li;
-            *kout = k;
-            *cfg = c;
+        if (w2 > 0 && w2 != L.w0) {
+            SpecKernel* k2 = nullptr;
+            std::string e2;
+            LaunchCfg c2{};
+            if (spec_compile<T>(L, a, w2, &k2, &e2) == cudaSuccess &&
+                spec_config<T>(dl, k2, L, a, w2, &c2, &e2) == cudaSuccess)
+                out->push_back(SpecChoice{li, k2, c2});
+            cudaGetLastError();  // a width that does not launch is simply not a candidate
         }
     }
-    if (best < 0) {
+    if (out->empty()) {
         *err = "no table layout to specialize";
         return cudaErrorInvalidValue;
     }
@@ -470,10 +460,10 @@ cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const Laun
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorLaunchFailure;
 }
 
-template cudaError_t spec_prepare<float>(const SpecLayout*, int, const RolloutArgs<float>&, int*,
-                                         const SpecKernel**, LaunchCfg*, std::string*);
-template cudaError_t spec_prepare<double>(const SpecLayout*, int, const RolloutArgs<double>&, int*,
-                                          const SpecKernel**, LaunchCfg*, std::string*);
+template cudaError_t spec_candidates<float>(const SpecLayout*, int, const RolloutArgs<float>&,
+                                            std::vector<SpecChoice>*, std::string*);
+template cudaError_t spec_candidates<double>(const SpecLayout*, int, const RolloutArgs<double>&,
+                                             std::vector<SpecChoice>*, std::string*);
 template cudaError_t spec_launch<float>(const SpecKernel*, const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t spec_launch<double>(const SpecKernel*, const RolloutArgs<double>&, const LaunchCfg&,
                                          cudaStream_t);
