@@ -186,9 +186,14 @@ pz::SpecLayout spec_layout(const pz::PackInfo& i, const std::vector<unsigned cha
 }
 
 // Time each compiled candidate on scratch copies of the simulator's state
-// (one untimed launch of two steps, then one timed) and return the fastest:
-// whether more resident worlds beat the cheaper shared-memory record access
-// depends on the model, so the choice is measured, not modelled.
+// (one untimed launch of kTrialSteps steps, then the faster of two timed
+// ones) and return the fastest, a later candidate replacing an earlier one
+// only when 3 % faster (the shared-memory table comes first): whether more
+// resident worlds beat the cheaper shared-memory record access depends on
+// the model, so the choice is measured, not modelled. The launches are long
+// enough that the per-tile load and store of the state do not decide it.
+constexpr int kTrialSteps = 16;
+
 template <class T>
 int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
                       const std::vector<const std::vector<unsigned char>*>& hosts,
@@ -232,7 +237,7 @@ int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
         phyzb_sim::Layout L;
         L.info = infos[ch[c].layout];
         L.blob = blobs[ch[c].layout];
-        pz::RolloutArgs<T> a = rollout_args<T>(s, L, s->ctrl, 0, 2);
+        pz::RolloutArgs<T> a = rollout_args<T>(s, L, s->ctrl, 0, kTrialSteps);
         a.q = (T*)q;
         a.v = (T*)v;
         a.qdd = (T*)qdd;
@@ -244,16 +249,17 @@ int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
             cudaGetLastError();
             continue;
         }
-        PZ_CUDA(cudaEventRecord(sc.e0, s->stream));
-        if (pz::spec_launch<T>(ch[c].k, a, ch[c].cfg, s->stream) != cudaSuccess) {
-            cudaGetLastError();
-            continue;
+        float ms = -1.0f;
+        for (int rep = 0; rep < 2; rep++) {
+            PZ_CUDA(cudaEventRecord(sc.e0, s->stream));
+            PZ_CUDA(pz::spec_launch<T>(ch[c].k, a, ch[c].cfg, s->stream));
+            PZ_CUDA(cudaEventRecord(sc.e1, s->stream));
+            PZ_CUDA(cudaEventSynchronize(sc.e1));
+            float t = 0.0f;
+            PZ_CUDA(cudaEventElapsedTime(&t, sc.e0, sc.e1));
+            if (ms < 0.0f || t < ms) ms = t;
         }
-        PZ_CUDA(cudaEventRecord(sc.e1, s->stream));
-        PZ_CUDA(cudaEventSynchronize(sc.e1));
-        float ms = 0.0f;
-        PZ_CUDA(cudaEventElapsedTime(&ms, sc.e0, sc.e1));
-        if (best_ms < 0.0f || ms < best_ms) {
+        if (best_ms < 0.0f || ms < 0.97f * best_ms) {
             best_ms = ms;
             *best = c;
         }

@@ -159,6 +159,7 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     M.kstiff_c = Cnt(4.0 / (dtc * dtc));
     M.im = ImpMat<Cnt>{M.ground_h, M.friction, M.dt, Cnt(0.0), Cnt(0.001), Cnt(0.0), Cnt(0.05),
                        Cnt(0.9),   Cnt(0.95),  Cnt(0.001), Cnt(0.5), Cnt(2.0)};
+    impmat_finish(M.im);  // per-launch constants, outside the counted step
     // a 2 x 2 heightfield far below: terrain sampling is counted like
     // detection, the force law is not
     static const float hf_nodes[4] = {0.0f, 0.0f, 0.0f, 0.0f};

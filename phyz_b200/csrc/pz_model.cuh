@@ -130,6 +130,10 @@ template <class T>
 struct ImpMat {
     T ground_h, friction, dt, erp, margin, restitution, rest_thr;
     T dmin, dmax, width, mid, power;
+    // derived once per launch (impmat_finish): the SolImp curve's clamped
+    // parameters and the reciprocals the per-point law multiplies by
+    T c_dmin, c_dmax, c_mid, c_pw, inv_width, mid_scale, omid_scale, inv_margin, inv_dtc, inv_vr;
+    bool pw2;  // the curve's power is 2 (the default): x^2 by one multiply
 };
 
 // Words of a BodyI before its alignment padding (the model-specialized

@@ -726,6 +726,14 @@ PZ_HD T eff_mass(const BodyT<T>& bt, const V3<T>& r, const V3<T>& u) {
     const T ang = pz_max(dot(a, symv(bt.Icinv, a)), T(0));
     return T(1) / (T(1) / bt.mass + ang);
 }
+// Its reciprocal, 1/m + (r x u) . Ic^-1 (r x u), without the division.
+template <class T>
+PZ_HD T eff_mass_inv(const BodyT<T>& bt, const V3<T>& r, const V3<T>& u) {
+    if (!(bt.mass > T(0))) return T(1e-30);
+    const V3<T> a = cross(r - ld3(bt.com), u);
+    const T ang = pz_max(dot(a, symv(bt.Icinv, a)), T(0));
+    return T(1) / bt.mass + ang;
+}
 template <class T>
 PZ_HD T fsign(const T& x) {
     return x > T(0) ? T(1) : (x < T(0) ? T(-1) : T(0));
@@ -1185,18 +1193,34 @@ PZ_HD void contact_state_pass(const ModelView<T>& M, const Scr& S, const Out<T>&
 
 // ── impulse-mode ground contact (phyz_kernels.cu:581-622 helpers, :856-918
 // the impulse branch of contact_thread; flat ground) ───────────────────────
-// SolImp impedance at depth r (phyz_kernels.cu:589-601)
+// The per-launch constants of the impulse law: the SolImp curve's clamped
+// parameters (phyz_kernels.cu:589-601 clamps them at every call) and the
+// reciprocals of the divisors that do not change within a launch.
+template <class T>
+PZ_HD void impmat_finish(ImpMat<T>& m) {
+    m.c_dmin = pz_min(pz_max(m.dmin, T(1e-4)), T(1) - T(1e-9));
+    m.c_dmax = pz_min(pz_max(m.dmax, T(1e-4)), T(1) - T(1e-9));
+    m.c_mid = pz_min(pz_max(m.mid, T(1e-6)), T(1) - T(1e-6));
+    m.c_pw = pz_max(m.power, T(1));
+    m.pw2 = !(m.c_pw < T(2)) && !(m.c_pw > T(2));
+    m.inv_width = m.width > T(0) ? T(1) / m.width : T(0);
+    m.mid_scale = T(1) / pz_pow(m.c_mid, m.c_pw - T(1));
+    m.omid_scale = T(1) / pz_pow(T(1) - m.c_mid, m.c_pw - T(1));
+    m.inv_margin = m.margin > T(0) ? T(1) / m.margin : T(0);
+    m.inv_dtc = T(1) / pz_max(m.dt, T(1e-9));
+    m.inv_vr = m.rest_thr > T(0) ? T(1) / m.rest_thr : T(0);
+}
+// SolImp impedance at depth r (phyz_kernels.cu:589-601):
+// y = x^p / mid^(p-1) below mid, 1 - (1-x)^p / (1-mid)^(p-1) above.
 template <class T>
 PZ_HD T solimp_impedance(const ImpMat<T>& m, const T& r) {
-    const T dmin = pz_min(pz_max(m.dmin, T(1e-4)), T(1) - T(1e-9));
-    const T dmax = pz_min(pz_max(m.dmax, T(1e-4)), T(1) - T(1e-9));
-    if (!(m.width > T(0))) return dmax;
-    const T x = pz_min(pz_max(pz_abs(r) / m.width, T(0)), T(1));
-    const T mid = pz_min(pz_max(m.mid, T(1e-6)), T(1) - T(1e-6));
-    const T pw = pz_max(m.power, T(1));
-    const T y = x <= mid ? pz_pow(x, pw) / pz_pow(mid, pw - T(1))
-                         : T(1) - pz_pow(T(1) - x, pw) / pz_pow(T(1) - mid, pw - T(1));
-    return dmin + y * (dmax - dmin);
+    if (!(m.width > T(0))) return m.c_dmax;
+    const T x = pz_min(pz_max(pz_abs(r) * m.inv_width, T(0)), T(1));
+    const bool lo = x <= m.c_mid;
+    const T z = lo ? x : T(1) - x;
+    const T zp = m.pw2 ? z * z : pz_pow(z, m.c_pw);
+    const T y = lo ? zp * m.mid_scale : T(1) - zp * m.omid_scale;
+    return m.c_dmin + y * (m.c_dmax - m.c_dmin);
 }
 // solimp when penetrating, smoothstep to zero across the margin (:604-611)
 template <class T>
@@ -1204,18 +1228,20 @@ PZ_HD T impedance_at(const ImpMat<T>& m, const T& depth) {
     if (depth >= T(0)) return solimp_impedance(m, depth);
     const T gap = -depth;
     if (!(m.margin > T(0)) || gap >= m.margin) return T(0);
-    const T sc = T(1) - gap / m.margin;
+    const T sc = T(1) - gap * m.inv_margin;
     return sc * sc * (T(3) - T(2) * sc) * solimp_impedance(m, T(0));
 }
-// restitution ramp between v_rest and 2 v_rest (:613-622)
+// restitution ramp between v_rest and 2 v_rest (:613-622); no restitution
+// (the default material) is zero throughout the ramp
 template <class T>
 PZ_HD T effective_restitution(const ImpMat<T>& m, const T& e, const T& approach) {
     const T vr = m.rest_thr;
     if (!(vr > T(0))) return e;
+    if (!(pz_abs(e) > T(0))) return T(0);
     const T sp = pz_abs(approach);
     if (sp <= vr) return T(0);
     if (sp >= T(2) * vr) return e;
-    const T t = (sp - vr) / vr;
+    const T t = (sp - vr) * m.inv_vr;
     return e * t * t * (T(3) - T(2) * t);
 }
 // orthonormal tangents around a unit normal (:581-586)
@@ -1258,7 +1284,6 @@ template <bool TERRAIN, class T, class Scr>
 PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const BodyI& bi, const BodyT<T>& bt,
                            const WF<T>& wf, const SV<T>& vf, const Scr& S) {
     const int npts = bi.gtype == 2 ? 8 : 1;
-    const T dtc = pz_max(m.dt, T(1e-9));
     // within-body load sharing: points inside the margin
     int n_active = 0;
     for (int c = 0; c < npts; c++) {
@@ -1284,14 +1309,16 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const Body
         V3<T> tu, tw;
         body_tangents(bi, n, tu, tw);
         const T bn = dot(vp, n), bu = dot(vp, tu), bw = dot(vp, tw);
-        const T mn = eff_mass(bt, sup, n) / na;
-        const T ann = T(1) / pz_max(mn, T(1e-9));
-        const T bias = impedance_at(m, pen) * m.erp * pz_max(pen, T(0)) / dtc;
+        // the reference's A = 1 / max(m_eff / n_active, 1e-9) along the
+        // normal and n_active / max(m_eff, 1e-9) along each tangent, taken
+        // from the inverse effective mass (no division)
+        const T ann = pz_min(na * eff_mass_inv(bt, sup, n), T(1e9));
+        const T bias = impedance_at(m, pen) * m.erp * pz_max(pen, T(0)) * m.inv_dtc;
         const T e = effective_restitution(m, m.restitution, pz_min(bn, T(0)));
         const T rn = bn * (T(1) + e) - ann * S(slot);
         const T fn = pz_max((bias - rn) / ann, T(0));
-        const T auu = na / pz_max(eff_mass(bt, sup, tu), T(1e-9));
-        const T aww = na / pz_max(eff_mass(bt, sup, tw), T(1e-9));
+        const T auu = pz_min(na * eff_mass_inv(bt, sup, tu), na * T(1e9));
+        const T aww = pz_min(na * eff_mass_inv(bt, sup, tw), na * T(1e9));
         T ju = -(bu - auu * S(slot + 1)) / auu;
         T jw = -(bw - aww * S(slot + 2)) / aww;
         const T limit = m.friction * fn;
@@ -1304,7 +1331,7 @@ PZ_HD SV<T> impulse_wrench(const ImpMat<T>& m, const Terrain<T>& ter, const Body
         S(slot) = fn;
         S(slot + 1) = ju;
         S(slot + 2) = jw;
-        const V3<T> fb = (n * fn + tu * ju + tw * jw) * (T(1) / dtc);
+        const V3<T> fb = (n * fn + tu * ju + tw * jw) * m.inv_dtc;
         f.w = f.w + cross(sup, fb);
         f.l = f.l + fb;
         any = true;
@@ -1413,7 +1440,6 @@ PZ_HD void plane_pass(const ModelView<T>& M, const Scr& S) {
         vpb = ld_sv<T>(S, bp.s_vf);
     else
         vpb = ld_vel<T>(S, bp);
-    const T dtc = pz_max(M.dt, T(1e-9));
     const V3<T> ez = to_stored<T>(bp.fshift, mk3<T>(T(0), T(0), T(1)));  // the body's own +z
     const V3<T> n_w = wf_mul(fp, ez);
     const V3<T> p0_w = fp.pos + wf_mul(fp, ez * M.plane.offset);
@@ -1488,7 +1514,7 @@ PZ_HD void plane_pass(const ModelView<T>& M, const Scr& S) {
                 contact_tangents(n_w, pu, pw);  // world frame: no relabelling enters
                 const T bu = dot(v_rel, pu), bw = dot(v_rel, pw);
                 const T ann = na / pz_max(m_n, T(1e-9));
-                const T bias = impedance_at(M.im, pen) * M.im.erp * pz_max(pen, T(0)) / dtc;
+                const T bias = impedance_at(M.im, pen) * M.im.erp * pz_max(pen, T(0)) * M.im.inv_dtc;
                 const T e = effective_restitution(M.im, M.im.restitution, pz_min(vn, T(0)));
                 const T fn = pz_max((bias - (vn * (T(1) + e) - ann * S(slot))) / ann, T(0));
                 const T auu = na / pz_max(pair_mass(pu), T(1e-9));
@@ -1505,7 +1531,7 @@ PZ_HD void plane_pass(const ModelView<T>& M, const Scr& S) {
                 S(slot) = fn;
                 S(slot + 1) = ju;
                 S(slot + 2) = jw;
-                f_w = (n_w * fn + pu * ju + pw * jw) * (T(1) / dtc);
+                f_w = (n_w * fn + pu * ju + pw * jw) * M.im.inv_dtc;
             } else {
                 const T kb = pz_min(pt_scale * bt.gk, M.kstiff_c * m_n);
                 const T db = pz_min(pt_scale * bt.gd, M.inv_dt_c * m_n);

@@ -207,6 +207,7 @@ __device__ __forceinline__ ModelView<T> make_view(const RolloutArgs<T>& P, const
     M.im.width = T(P.si_width);
     M.im.mid = T(P.si_mid);
     M.im.power = T(P.si_power);
+    impmat_finish(M.im);
     M.ter.h = P.hf;
     M.ter.nx = P.hf_nx;
     M.ter.ny = P.hf_ny;
