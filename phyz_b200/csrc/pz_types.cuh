@@ -108,6 +108,81 @@ template <class T>
 PZ_HD V3<T> cross(const V3<T>& a, const V3<T>& b) {
     return mk3<T>(a.y * b.z - a.z * b.y, a.z * b.x - a.x * b.z, a.x * b.y - a.y * b.x);
 }
+
+// ── products with model-table constants ────────────────────────────────────
+// A model table is full of exact zeros (off-diagonal inertias, offsets and
+// centres of mass along one axis). In a specialized build the table is
+// literal, and a term whose table factor is zero is left out of its sum:
+// kzero() is then a compile-time constant per term. The compiler cannot drop
+// such a term itself (0 x is not 0 for infinite or NaN x, and x + 0 is not x
+// for x = -0), so the sums below start from -0 (-0 + t = t for every t) and
+// add their terms conditionally; in the generic build every term is added.
+// Leaving a term out changes a result only in the sign of a zero or in NaN
+// propagation. PZ_KSKIP makes a host build take the same decisions at run
+// time (for checking them against the oracle).
+#if defined(PZ_SPEC) || defined(PZ_KSKIP)
+#define PZ_KSKIP_ON 1
+#else
+#define PZ_KSKIP_ON 0
+#endif
+template <class T>
+PZ_HD bool kzero(const T& k) {
+    if constexpr (PZ_KSKIP_ON != 0 && !Counting<T>::value) return !(k > T(0) || k < T(0));
+    return false;
+}
+// k x, or -0 when k is a zero table constant (a sum's first term)
+template <class T>
+PZ_HD T kmul(const T& k, const T& x) {
+    return kzero(k) ? T(-0.0) : k * x;
+}
+template <class T>
+PZ_HD T kmadd(const T& acc, const T& k, const T& x) {
+    return kzero(k) ? acc : acc + k * x;
+}
+template <class T>
+PZ_HD T kmsub(const T& acc, const T& k, const T& x) {
+    return kzero(k) ? acc : acc - k * x;
+}
+// x + k, x - k for a table constant k
+template <class T>
+PZ_HD T kadd(const T& x, const T& k) {
+    return kzero(k) ? x : x + k;
+}
+template <class T>
+PZ_HD T ksub(const T& x, const T& k) {
+    return kzero(k) ? x : x - k;
+}
+// k x b and a x k with k a table constant
+template <class T>
+PZ_HD V3<T> kcross(const V3<T>& k, const V3<T>& b) {
+    return mk3<T>(kmsub(kmul(k.y, b.z), k.z, b.y), kmsub(kmul(k.z, b.x), k.x, b.z),
+                  kmsub(kmul(k.x, b.y), k.y, b.x));
+}
+template <class T>
+PZ_HD V3<T> crossk(const V3<T>& a, const V3<T>& k) {
+    return mk3<T>(kmsub(kmul(k.z, a.y), k.y, a.z), kmsub(kmul(k.x, a.z), k.z, a.x),
+                  kmsub(kmul(k.y, a.x), k.x, a.y));
+}
+// H x and H^T x for a row-major 3x3 table matrix H
+template <class T>
+PZ_HD V3<T> km3v(const T* H, const V3<T>& x) {
+    return mk3<T>(kmadd(kmadd(kmul(H[0], x.x), H[1], x.y), H[2], x.z),
+                  kmadd(kmadd(kmul(H[3], x.x), H[4], x.y), H[5], x.z),
+                  kmadd(kmadd(kmul(H[6], x.x), H[7], x.y), H[8], x.z));
+}
+template <class T>
+PZ_HD V3<T> km3tv(const T* H, const V3<T>& x) {
+    return mk3<T>(kmadd(kmadd(kmul(H[0], x.x), H[3], x.y), H[6], x.z),
+                  kmadd(kmadd(kmul(H[1], x.x), H[4], x.y), H[7], x.z),
+                  kmadd(kmadd(kmul(H[2], x.x), H[5], x.y), H[8], x.z));
+}
+// A x for a symmetric table matrix A (xx, yy, zz, xy, xz, yz)
+template <class T>
+PZ_HD V3<T> ksymv(const T* A, const V3<T>& x) {
+    return mk3<T>(kmadd(kmadd(kmul(A[0], x.x), A[3], x.y), A[4], x.z),
+                  kmadd(kmadd(kmul(A[3], x.x), A[1], x.y), A[5], x.z),
+                  kmadd(kmadd(kmul(A[4], x.x), A[5], x.y), A[2], x.z));
+}
 template <class T>
 PZ_HD T get(const V3<T>& a, int i) {
     return i == 0 ? a.x : (i == 1 ? a.y : a.z);
@@ -249,6 +324,21 @@ template <class T>
 PZ_HD SV<T> xf_tapply_trans(const V3<T>& r, const SV<T>& f) {
     return mksv<T>(f.w + cross(r, f.l), f.l);
 }
+// The same two translations by a table constant r (a specialized build
+// forms l - r x w as l + w x r, so that left-out terms are -0 added; the
+// generic build keeps the original expression)
+template <class T>
+PZ_HD SV<T> kxm_apply_trans(const V3<T>& r, const SV<T>& m) {
+#if PZ_KSKIP_ON
+    return mksv<T>(m.w, m.l + crossk(m.w, r));
+#else
+    return xm_apply_trans(r, m);
+#endif
+}
+template <class T>
+PZ_HD SV<T> kxf_tapply_trans(const V3<T>& r, const SV<T>& f) {
+    return mksv<T>(f.w + kcross(r, f.l), f.l);
+}
 
 // Planar rotation about the coordinate axis K by the angle whose cosine
 // and sine are (c, s): E e_i = c e_i + s e_j, E e_j = -s e_i + c e_j with
@@ -387,6 +477,40 @@ PZ_HD void ai_trans(const V3<T>& r, AI<T>& I) {
             const T wij = get(w, j);
             I.a[sidx(i, j)] = I.a[sidx(i, j)] - z[i * 3 + j] - z[j * 3 + i] - wij;
         }
+    }
+#pragma unroll
+    for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + t1[k];
+}
+// ai_trans by a table constant r, every product with r through the k
+// helpers: Ia' = Ia + Y + Y^T + V with Y = -(H r^x) (rows r x H_row) and
+// V = -(T1 r^x) (rows r x T1_row), so that a left-out term is a -0 added.
+template <class T>
+PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
+#if !PZ_KSKIP_ON
+    ai_trans(r, I);  // the generic build: the original expression order
+    return;
+#endif
+    T t1[9];
+#pragma unroll
+    for (int j = 0; j < 3; j++) {
+        const V3<T> rc = kcross(r, mk3<T>(I.m[sidx(0, j)], I.m[sidx(1, j)], I.m[sidx(2, j)]));
+        t1[0 * 3 + j] = rc.x;
+        t1[1 * 3 + j] = rc.y;
+        t1[2 * 3 + j] = rc.z;
+    }
+    T y[9];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const V3<T> rr = kcross(r, mk3<T>(I.h[i * 3 + 0], I.h[i * 3 + 1], I.h[i * 3 + 2]));
+        y[i * 3 + 0] = rr.x;
+        y[i * 3 + 1] = rr.y;
+        y[i * 3 + 2] = rr.z;
+    }
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const V3<T> w = kcross(r, mk3<T>(t1[i * 3 + 0], t1[i * 3 + 1], t1[i * 3 + 2]));
+#pragma unroll
+        for (int j = i; j < 3; j++) I.a[sidx(i, j)] = I.a[sidx(i, j)] + y[i * 3 + j] + y[j * 3 + i] + get(w, j);
     }
 #pragma unroll
     for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + t1[k];

@@ -386,7 +386,7 @@ template <int AX, int FEAT, class T>
 PZ_HD SV<T> mot_X(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> m) {
     // (relabelled hinges translate unconditionally: a zero offset is exact and
     // cheaper than the branch)
-    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) m = xm_apply_trans(ld3(bt.ptj_pos), m);
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) m = kxm_apply_trans(ld3(bt.ptj_pos), m);
     if constexpr (AX >= 0) {
         return rot_fwd<AX, FEAT>(bi.qshift, j.c, j.s, m);
     } else {
@@ -441,7 +441,7 @@ PZ_HD SV<T> frc_XT(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, SV<T> f)
             f = xf_tapply_rot(P, f);
         }
     }
-    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) f = xf_tapply_trans(ld3(bt.ptj_pos), f);
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) f = kxf_tapply_trans(ld3(bt.ptj_pos), f);
     return f;
 }
 
@@ -479,7 +479,7 @@ PZ_HD void ai_XtIX(const BodyI& bi, const BodyT<T>& bt, const JX<T>& j, AI<T>& I
             ai_rot(P, I);
         }
     }
-    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) ai_trans(ld3(bt.ptj_pos), I);
+    if ((AX >= 0 && !Counting<T>::value) || (bi.flags & F_PTJ_POS)) kai_trans(ld3(bt.ptj_pos), I);
 }
 
 // S qd of body i (aba.rs:15-30).
@@ -720,18 +720,22 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
 
 // ── penalty ground contact of one body (phyz_kernels.cu:541-578, 691-725, 939-965)
 template <class T>
+PZ_HD V3<T> ksub3(const V3<T>& x, const T* k) {
+    return mk3<T>(ksub(x.x, k[0]), ksub(x.y, k[1]), ksub(x.z, k[2]));
+}
+template <class T>
 PZ_HD T eff_mass(const BodyT<T>& bt, const V3<T>& r, const V3<T>& u) {
     if (!(bt.mass > T(0))) return T(1e30);
-    const V3<T> a = cross(r - ld3(bt.com), u);
-    const T ang = pz_max(dot(a, symv(bt.Icinv, a)), T(0));
+    const V3<T> a = cross(ksub3(r, bt.com), u);
+    const T ang = pz_max(dot(a, ksymv(bt.Icinv, a)), T(0));
     return T(1) / (T(1) / bt.mass + ang);
 }
 // Its reciprocal, 1/m + (r x u) . Ic^-1 (r x u), without the division.
 template <class T>
 PZ_HD T eff_mass_inv(const BodyT<T>& bt, const V3<T>& r, const V3<T>& u) {
     if (!(bt.mass > T(0))) return T(1e-30);
-    const V3<T> a = cross(r - ld3(bt.com), u);
-    const T ang = pz_max(dot(a, symv(bt.Icinv, a)), T(0));
+    const V3<T> a = cross(ksub3(r, bt.com), u);
+    const T ang = pz_max(dot(a, ksymv(bt.Icinv, a)), T(0));
     return T(1) / bt.mass + ang;
 }
 template <class T>
@@ -740,13 +744,12 @@ PZ_HD T fsign(const T& x) {
 }
 template <class T>
 PZ_HD V3<T> support_pt(const BodyI& bi, const BodyT<T>& bt, const V3<T>& n_body, int corner) {
-    const R3<T> O = ld9(bt.grot);
     V3<T> s = zero3<T>();
     if (bi.gtype == 2) {  // box corner (phyz_kernels.cu:679-689)
         s = mk3<T>(bt.geom[0] * ((corner & 1) ? T(1) : T(-1)), bt.geom[1] * ((corner & 2) ? T(1) : T(-1)),
                    bt.geom[2] * ((corner & 4) ? T(1) : T(-1)));
     } else {
-        const V3<T> n = rmul(O, n_body);
+        const V3<T> n = km3v(bt.grot, n_body);
         if (bi.gtype == 1) {
             s = n * (-bt.geom[0]);
         } else if (bi.gtype == 3) {
@@ -763,7 +766,8 @@ PZ_HD V3<T> support_pt(const BodyI& bi, const BodyT<T>& bt, const V3<T>& n_body,
             s = mc - mk3<T>(mh.x * fsign(n.x), mh.y * fsign(n.y), mh.z * fsign(n.z));
         }
     }
-    return ld3(bt.gpos) + rtmul(O, s);
+    const V3<T> o = km3tv(bt.grot, s);
+    return mk3<T>(kadd(o.x, bt.gpos[0]), kadd(o.y, bt.gpos[1]), kadd(o.z, bt.gpos[2]));
 }
 
 // World frame of a body for contact: world up seen in the body frame (row 2
@@ -1586,18 +1590,18 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     // rigid inertia about the origin [Io, (mc)^x; -(mc)^x, m 1] and the
     // bias force v x* (I v) - f_ext
 #pragma unroll
-    for (int k = 0; k < 6; k++) I.a[k] = I.a[k] + bt.Io[k];
-    I.h[1] = I.h[1] - bt.mcom[2];
-    I.h[2] = I.h[2] + bt.mcom[1];
-    I.h[3] = I.h[3] + bt.mcom[2];
-    I.h[5] = I.h[5] - bt.mcom[0];
-    I.h[6] = I.h[6] - bt.mcom[1];
-    I.h[7] = I.h[7] + bt.mcom[0];
+    for (int k = 0; k < 6; k++) I.a[k] = kadd(I.a[k], bt.Io[k]);
+    I.h[1] = ksub(I.h[1], bt.mcom[2]);
+    I.h[2] = kadd(I.h[2], bt.mcom[1]);
+    I.h[3] = kadd(I.h[3], bt.mcom[2]);
+    I.h[5] = ksub(I.h[5], bt.mcom[0]);
+    I.h[6] = ksub(I.h[6], bt.mcom[1]);
+    I.h[7] = kadd(I.h[7], bt.mcom[0]);
     I.m[0] = I.m[0] + bt.mass;
     I.m[1] = I.m[1] + bt.mass;
     I.m[2] = I.m[2] + bt.mass;
     const V3<T> mc = ld3(bt.mcom);
-    const SV<T> hv = mksv<T>(symv(bt.Io, v.w) + cross(mc, v.l), v.l * bt.mass + cross(v.w, mc));
+    const SV<T> hv = mksv<T>(ksymv(bt.Io, v.w) + kcross(mc, v.l), v.l * bt.mass + crossk(v.w, mc));
     SV<T> bias = crf(v, hv);
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
         if (bi.flags & F_EXTF) bias = bias - ld_sv<T>(S, bi.s_f);
