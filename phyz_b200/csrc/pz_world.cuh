@@ -896,17 +896,22 @@ PZ_HD SV<T> contact_wrench(const ModelView<T>& M, const BodyI& bi, const BodyT<T
         const V3<T>& n = g.n;
         const V3<T> vp = v.l + cross(v.w, sup);
         const T vn = dot(vp, n);
-        const T mn = eff_mass(bt, sup, n);
-        const T kb = pz_min(pt_scale * bt.gk, M.kstiff_c * mn);
-        const T db = pz_min(pt_scale * bt.gd, M.inv_dt_c * mn);
+        // the gains' caps k <= 4 m_eff / dt^2, d <= m_eff / dt and the
+        // friction cap m_eff vt / dt, compared through the inverse effective
+        // mass: a division only where a cap binds
+        const T in = eff_mass_inv(bt, sup, n);
+        const T kg = pt_scale * bt.gk, dg = pt_scale * bt.gd;
+        const T kb = kg * in <= M.kstiff_c ? kg : M.kstiff_c / in;
+        const T db = dg * in <= M.inv_dt_c ? dg : M.inv_dt_c / in;
         const T fn = pz_max(kb * pen - db * vn, T(0));
         const V3<T> vt3 = vp - n * vn;
         const T vt = pz_sqrt(dot(vt3, vt3));
         V3<T> fb = n * fn;
         if (vt > T(1e-6)) {
             const V3<T> td = vt3 * (T(1) / vt);
-            const T coul = (M.friction * fn) * pz_min(T(1), vt / T(1e-3));
-            const T ft = pz_min(coul, (M.inv_dt_c * eff_mass(bt, sup, td)) * vt);
+            const T coul = (M.friction * fn) * pz_min(T(1), vt * T(1e3));
+            const T it = eff_mass_inv(bt, sup, td), cap = M.inv_dt_c * vt;
+            const T ft = coul * it <= cap ? coul : cap / it;
             fb = fb - td * ft;
         }
         f.w = f.w + cross(sup, fb);
