@@ -41,6 +41,8 @@ enum BodyFlags {
     F_PD = 1 << 9,        // a DOF of this body is driven by a PD servo
     F_PLANE = 1 << 10,    // touches the body-attached contact plane
     F_EXTF = 1 << 11,     // receives an external wrench (s_f): collidable, or the plane's body
+    F_ROOTQDD = 1 << 12,  // ball/free joint of a root body: its parent acceleration is gravity
+                          // alone, so pass 2 solves its qdd outright and W is never formed
 };
 
 template <class T>

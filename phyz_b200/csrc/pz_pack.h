@@ -283,6 +283,7 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.qshift = (shift[i] - (b.parent >= 0 ? shift[b.parent] : 0) + 3) % 3;
         }
         if (i + 1 < nb && m->bodies[i + 1].parent == i) flags |= F_CHAIN;
+        if (nd > 1 && b.parent < 0) flags |= F_ROOTQDD;
         for (int j = i + 2; j < nb; j++)
             if (m->bodies[j].parent == i) flags |= F_BRANCH;
         d.gtype = b.geom_type;

@@ -603,9 +603,14 @@ PZ_HD void ai_sub_el(AI<T>& I, int r, int c, const T& v) {  // only r <= c for s
 // U = I S, D = S^T U + d_extra, W = U D^-1, w0 = D^-1 u, stored; when the
 // body has a parent, I <- I - W U^T and p <- p + I c + U w0. Returns false
 // when D is singular (aba.rs:291-294: the body is skipped).
+// A root body (F_ROOTQDD, ag = its parent's acceleration -g in its own
+// frame) instead gets w0 = D^-1 (u - U^T ag), its qdd: the step's
+// accelerations start from the root as qdd = w0 - W^T a with a = ag (the
+// root's bias c = v x S qd vanishes, its v being S qd), and D^-1 U^T =
+// W^T, so W is neither solved for nor stored.
 template <int ND, bool SEP, class T, class Scr>
 PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt, const Scr& S,
-                     AI<T>& I, SV<T>& p, const SV<T>& c, bool has_parent) {
+                     AI<T>& I, SV<T>& p, const SV<T>& c, bool has_parent, const SV<T>* ag = nullptr) {
     T U[6][ND];
 #pragma unroll
     for (int r = 0; r < 6; r++)
@@ -674,6 +679,19 @@ PZ_HD bool multi_dof(const ModelView<T>& M, const BodyI& bi, const BodyT<T>& bt,
             x[a] = e * Linv[a];
         }
     };
+    if (ag) {
+#pragma unroll
+        for (int k = 0; k < ND; k++) {
+            T s = u[k];
+#pragma unroll
+            for (int r = 0; r < 6; r++) s = s - U[r][k] * svget(*ag, r);
+            u[k] = s;
+        }
+        solve(u);
+#pragma unroll
+        for (int k = 0; k < ND; k++) S(bi.s_w0 + k) = u[k];
+        return true;
+    }
     // W row r = D^-1 U row r (D symmetric)
     T W[6][ND];
 #pragma unroll
@@ -1702,10 +1720,18 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     } else if constexpr (AX < 0) {
         if (bi.ndof > 1) {
             if constexpr ((FEAT & FEAT_MULTI) != 0) {
+                SV<T> ag;
+                const bool root = (bi.flags & F_ROOTQDD) != 0;
+                if (root) {
+                    const JX<T> jr = load_jx<AX, FEAT>(bi, bt, S);
+                    ag = mot_X<AX, FEAT>(bi, bt, jr, mksv<T>(zero3<T>(), mk3<T>(-M.gx, -M.gy, -M.gz)));
+                }
                 if (bi.ndof == 3)
-                    live = multi_dof<3, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0);
+                    live = multi_dof<3, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0,
+                                                                    root ? &ag : nullptr);
                 else
-                    live = multi_dof<6, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0);
+                    live = multi_dof<6, (FEAT & FEAT_IMPULSE) != 0>(M, bi, bt, S, I, pA, c, p >= 0,
+                                                                    root ? &ag : nullptr);
             }
         }
     }
@@ -1770,13 +1796,16 @@ PZ_HD void integrate_1dof(const ModelView<T>& M, const BodyI& bi, const Scr& S, 
 }
 
 // Multi-DOF accelerations qdd = w0 - W^T a, written into the w0 slots (the
-// integrator reads them back), and a += S qdd.
+// integrator reads them back), and a += S qdd. A root's w0 is its qdd
+// already (F_ROOTQDD).
 template <class T, class Scr>
 PZ_HD void multi_qdd(const BodyI& bi, const Scr& S, SV<T>& a) {
     const int nd = bi.ndof;
+    const bool root = (bi.flags & F_ROOTQDD) != 0;
     T q[6];
 #pragma unroll
-    for (int k = 0; k < 6; k++) q[k] = k < nd ? S(bi.s_w0 + k) - dot(ld_sv<T>(S, bi.s_vw + 6 * k), a) : T(0);
+    for (int k = 0; k < 6; k++)
+        q[k] = k < nd ? (root ? S(bi.s_w0 + k) : S(bi.s_w0 + k) - dot(ld_sv<T>(S, bi.s_vw + 6 * k), a)) : T(0);
 #pragma unroll
     for (int k = 0; k < 6; k++)
         if (k < nd) S(bi.s_w0 + k) = q[k];
@@ -2051,8 +2080,10 @@ PZ_HD bool wrench_multi(const BodyI& bi, const Scr& S, SV<T>& dp) {
 #pragma unroll
     for (int k = 0; k < ND; k++) {
         S(bi.s_w0 + k) = S(bi.s_w0b + k) + (live ? x[k] : T(0));
-        const SV<T> wk = ld_sv<T>(S, bi.s_vw + 6 * k);
-        dp = dp + mksv<T>(wk.w * du[k], wk.l * du[k]);
+        if (!(bi.flags & F_ROOTQDD)) {  // a root passes nothing on (and has no W)
+            const SV<T> wk = ld_sv<T>(S, bi.s_vw + 6 * k);
+            dp = dp + mksv<T>(wk.w * du[k], wk.l * du[k]);
+        }
     }
     return live;
 }
