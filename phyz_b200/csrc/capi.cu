@@ -192,6 +192,8 @@ pz::SpecLayout spec_layout(const pz::PackInfo& i, const std::vector<unsigned cha
 // resident worlds beat the cheaper shared-memory record access depends on
 // the model, so the choice is measured, not modelled. The launches are long
 // enough that the per-tile load and store of the state do not decide it.
+// Without device memory for the scratch copies the first candidate is kept
+// untimed.
 constexpr int kTrialSteps = 16;
 
 template <class T>
@@ -222,8 +224,13 @@ int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
     void* imp = s->imp ? sc.alloc(s->imp_bytes) : nullptr;
     std::vector<void*> blobs;
     for (size_t i = 0; i < infos.size(); i++) blobs.push_back(sc.alloc(infos[i].bytes));
-    for (void* x : sc.p)
-        if (!x) return fail(PHYZB_ERR_CUDA, "cudaMalloc failed while timing the specialized kernels");
+    bool room = q && v && qdd && status && (!s->cstate || cs) && (!s->imp || imp);
+    for (void* b : blobs) room = room && b;
+    if (!room) {  // no device memory to time the candidates on: keep the first
+        cudaGetLastError();
+        *best = 0;
+        return PHYZB_OK;
+    }
     PZ_CUDA(cudaMemcpyAsync(q, s->q, sb, cudaMemcpyDeviceToDevice, s->stream));
     PZ_CUDA(cudaMemcpyAsync(v, s->v, sb, cudaMemcpyDeviceToDevice, s->stream));
     if (imp) PZ_CUDA(cudaMemcpyAsync(imp, s->imp, s->imp_bytes, cudaMemcpyDeviceToDevice, s->stream));
