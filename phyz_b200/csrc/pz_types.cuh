@@ -488,8 +488,7 @@ template <class T>
 PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
 #if !PZ_KSKIP_ON
     ai_trans(r, I);  // the generic build: the original expression order
-    return;
-#endif
+#else
     T t1[9];
 #pragma unroll
     for (int j = 0; j < 3; j++) {
@@ -514,6 +513,7 @@ PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
     }
 #pragma unroll
     for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + t1[k];
+#endif
 }
 
 }  // namespace pz
