@@ -539,7 +539,10 @@ int phyzb_flops_per_world_step(const phyzb_sim* sim, double* flops, double* tran
  * over every SM: the roofline denominator of the stepper's kernels. */
 int phyzb_measure_fma_peak(int precision, double* tflops);
 /* Launch configuration the fused kernel uses for this simulator; tmem_cols
- * > 0 when its body records live in Tensor Memory (columns per world). */
+ * > 0 when its body records live in Tensor Memory (columns per world). With
+ * specialization active it is the specialized kernel's once that kernel has
+ * been compiled (at the first launch after a table change), the generic
+ * variant's before. */
 int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
                       int32_t* smem_bytes, int32_t* scratch_per_world, int32_t* tmem_cols);
 
@@ -569,7 +572,8 @@ int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* 
  * PHYZB_ERR_CUDA and the compiler's log in phyzb_last_error(). A new
  * simulator starts in the mode PHYZB_SPECIALIZE names ("0", "1", "auto"),
  * else OFF. `active` (may be null) tells whether the next launch runs the
- * specialized kernel. */
+ * specialized kernel. PHYZB_SPEC_NVRTC_OPTS appends compiler options
+ * (space-separated, for tuning; part of the cache key). */
 #define PHYZB_SPECIALIZE_OFF 0
 #define PHYZB_SPECIALIZE_ON 1
 #define PHYZB_SPECIALIZE_AUTO 2
