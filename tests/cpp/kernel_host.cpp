@@ -43,36 +43,53 @@ struct HS {
         base[bi.s_vw + 3] = v.l.x; base[bi.s_vw + 4] = v.l.y; base[bi.s_vw + 5] = v.l.z;
     }
 };
+// One world, nsteps steps, the kernel's sequence: pass 1 once, then per step
+// the backward sweep, (impulse mode) the kept backward state and `sweeps` x
+// [forward sweep with the staged impulse update, wrench response], and the
+// fused finish / next-step sweep. Impulse state starts at zero.
 template <int F>
-void run(const ModelView<double>& M, const PackInfo& info, double* q, double* v, const double* ctrl, int nsteps) {
+void run(const ModelView<double>& M, const PackInfo& info, double* q, double* v, const double* ctrl, int nsteps,
+         int sweeps) {
+    constexpr bool IMP = (F & FEAT_IMPULSE) != 0;
     std::vector<double> scr(info.scratch + 1, 0.0);
     HS S{scr.data()};
     const int nv = M.nv;
     for (int j = 0; j < nv; j++) { S(j) = q[j]; S(nv + j) = v[j]; }
     const WorldIO<double> io{ctrl, 0, nullptr, 1, 0};
-    for (int i = 0; i < M.nb; i++) prefetch_controls<false>(M, M.bi[i], S, io, 0);
+    for (int i = 0; i < M.nb; i++) prefetch_controls<IMP>(M, M.bi[i], S, io, 0);
     const Out<double> none{nullptr, 0};
     pass1_all<F>(M, S);
     for (int s = 0; s < nsteps; s++) {
         pass2<F>(M, S);
+        if constexpr (IMP) {
+            keep_backward_state(M, S);
+            for (int k = 0; k < sweeps; k++) {
+                sweep_forward<F>(M, S);
+                wrench_response<F>(M, S);
+            }
+        }
         if (s == nsteps - 1) pass3_next<F, true>(M, S, io, -1, none);
         else pass3_next<F, false>(M, S, io, s + 1, none);
     }
     for (int j = 0; j < nv; j++) { q[j] = S(j); v[j] = S(nv + j); }
 }
 template <int F = 0>
-bool dispatch(int feat, const ModelView<double>& M, const PackInfo& info, double* q, double* v, const double* c, int n) {
-    if constexpr (F < 16) {
-        if (feat == F) { run<F>(M, info, q, v, c, n); return true; }
-        return dispatch<F + 1>(feat, M, info, q, v, c, n);
+bool dispatch(int feat, const ModelView<double>& M, const PackInfo& info, double* q, double* v, const double* c, int n,
+              int sweeps) {
+    if constexpr (F < 32) {
+        if constexpr (!((F & 8) && !(F & 4)) && !((F & 16) && !(F & 2)))
+            if (feat == F) { run<F>(M, info, q, v, c, n, sweeps); return true; }
+        return dispatch<F + 1>(feat, M, info, q, v, c, n, sweeps);
     }
     return false;
 }
+// contact: 0 none, 1 penalty (gains k, d), 2 impulse (`sweeps` per step,
+// enable_contact_impulse's material)
 extern "C" int host_rollout(const phyzb_model* m, int nworld, double* q, double* v, const double* ctrl, int nsteps,
-                            int contact, double ground, double friction, double k, double d) {
+                            int contact, double ground, double friction, double k, double d, int sweeps) {
     const int nv = [&] { int s = 0; for (int i = 0; i < m->nbodies; i++) { int t = m->bodies[i].joint_type;
         s += t == 3 ? 3 : (t == 4 ? 6 : (t == 2 ? 0 : 1)); } return s; }();
-    PackCfg cfg; cfg.contact = contact != 0;
+    PackCfg cfg; cfg.contact = contact != 0; cfg.impulse = contact == 2;
     cfg.gk.assign(m->nbodies, k); cfg.gd.assign(m->nbodies, d);
     std::vector<unsigned char> blob;
     PackInfo info = pack_model<double>(m, nv, cfg, blob, 0);
@@ -86,9 +103,15 @@ extern "C" int host_rollout(const phyzb_model* m, int nworld, double* q, double*
     M.ground_h = ground; M.friction = friction;
     const double dtc = m->dt > 1e-9 ? m->dt : 1e-9;
     M.inv_dt_c = 1.0 / dtc; M.kstiff_c = 4.0 / (dtc * dtc);
+    // GroundContactParams::default with solref_erp_from(0.02, 1.0, dt)
+    const double erp = m->dt > 0.0 ? m->dt / (2.0 * 0.02 + m->dt) : 0.0;
+    M.im = ImpMat<double>{ground, friction, m->dt, erp, 0.001, 0.0, 0.05, 0.9, 0.95, 0.001, 0.5, 2.0};
+    impmat_finish(M.im);
     M.ter = Terrain<double>{nullptr, 0, 0, 0, 0, 0, 1};
     M.plane = PlaneT<double>{-1, 0, 0, 0, 0};
     for (int w = 0; w < nworld; w++)
-        if (!dispatch(info.feat, M, info, q + (size_t)w * nv, v + (size_t)w * nv, ctrl + (size_t)w * nv, nsteps)) return -1;
+        if (!dispatch(info.feat, M, info, q + (size_t)w * nv, v + (size_t)w * nv, ctrl + (size_t)w * nv, nsteps,
+                      sweeps))
+            return -1;
     return info.feat;
 }

@@ -33,22 +33,26 @@ def kernels(tmp_path_factory):
                         "-o", str(so)], check=True)
         lib = C.CDLL(str(so))
         lib.host_rollout.argtypes = [C.c_void_p, C.c_int, D, D, D, C.c_int, C.c_int, C.c_double, C.c_double,
-                                     C.c_double, C.c_double]
+                                     C.c_double, C.c_double, C.c_int]
         out[tag] = lib
     return out
 
 
-def host_run(lib, name, n=16, steps=100):
+def host_run(lib, name, n=16, steps=100, impulse=False):
     cfg = configs.CONFIGS[name]
     m = cfg.builder()
     q0, v0 = configs.initial_state(name, m, range(n))
+    if impulse:  # root heights at which the feet stand on the ground through the run
+        lo, hi = {"c3_quadruped": (0.45, 0.6), "c4_humanoid": (0.9, 1.05)}[name]
+        q0[:, 5] = np.linspace(lo, hi, n)
     c = 0.5 * np.random.default_rng(1).standard_normal((n, m.nv)) * configs.actuated(m)
     cm, keep = m.to_c()
     q, v = q0.copy(), v0.copy()
     dp = lambda a: a.ctypes.data_as(D)  # noqa: E731
     contact = cfg.contact is not None
-    feat = lib.host_rollout(C.addressof(cm), n, dp(q), dp(v), dp(np.ascontiguousarray(c)), steps, int(contact),
-                            0.0, 1.0, 1e4, 100.0)
+    mode = 2 if impulse else int(contact)
+    feat = lib.host_rollout(C.addressof(cm), n, dp(q), dp(v), dp(np.ascontiguousarray(c)), steps, mode,
+                            0.0, 1.0, 1e4, 100.0, 16)
     assert feat >= 0
     return m, q0, v0, c, contact, q, v
 
@@ -64,3 +68,19 @@ def test_kernel_source_matches_oracle(kernels, oracle, name):
         np.testing.assert_allclose(q, qo, rtol=0, atol=1e-11, err_msg=tag)
         np.testing.assert_allclose(v, vo, rtol=0, atol=1e-10, err_msg=tag)
     np.testing.assert_allclose(runs["kskip"][5], runs["generic"][5], rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("name", ["c3_quadruped", "c4_humanoid"])
+def test_kernel_source_impulse_matches_oracle(kernels, oracle, name):
+    """Impulse mode (16 sweeps per step, the kept backward state and the
+    wrench responses): the kernel source against the oracle's full re-sweep
+    formulation, from a cold start, with the feet on the ground."""
+    runs = {tag: host_run(lib, name, impulse=True) for tag, lib in kernels.items()}
+    m, q0, v0, c, _, _, _ = runs["generic"]
+    qo, vo, _, _, _ = oracle.rollout_impulse(m, q0, v0, c, nsteps=100, contact=(0.0, 1.0), sweeps=16, nthreads=4)
+    for tag, (_, _, _, _, _, q, v) in runs.items():
+        assert np.all(np.isfinite(q)) and np.all(np.isfinite(v)), tag
+        # the staged law is discontinuous (friction clamp, margin): rounding
+        # may send a world down another branch, as in the GPU impulse tests
+        ok = np.max(np.abs(q - qo), axis=1) < 1e-8
+        assert ok.mean() >= 0.9, (tag, ok.mean(), np.abs(q - qo).max())
