@@ -42,8 +42,8 @@ sys.path.insert(0, str(ROOT))
 import numpy as np  # noqa: E402
 
 # DRAM traffic of one rollout_kernel launch measured by ncu on a smaller
-# case of the same workload (profiles/rollout_kernel_c2_chain32_f32.md:
-# dram__bytes_read.sum + dram__bytes_write.sum, 65536 worlds x 20 steps).
+# case of the same workload (dram__bytes_read.sum + dram__bytes_write.sum of
+# one launch at 65536 worlds).
 # A launch reads/writes each world's state once and streams one control row
 # per step, so it is scaled to the bench's launch as
 #   state bytes (q, v in and out) + per-world-step bytes x worlds x steps,
@@ -51,6 +51,11 @@ import numpy as np  # noqa: E402
 # state bytes.
 NCU_DRAM_CAPTURES: dict = {
     ("c2_chain32", "f32"): {"nworld": 65536, "horizon": 20, "bytes": 184.666880e6 + 12.603904e6},
+    # the model-specialized kernel
+    ("c3_quadruped", "f32"): {"nworld": 65536, "horizon": 20, "bytes": 80.932608e6 + 5.339904e6},
+    # the generic impulse variant: its DRAM traffic is the state and the
+    # control stream, as the specialized kernel's is
+    ("c3_quadruped_impulse", "f32"): {"nworld": 65536, "horizon": 10, "bytes": 53.736192e6 + 1.875200e6},
 }
 
 # Workloads beyond BASELINE.json's configs: a config's model, worlds and
@@ -411,8 +416,9 @@ def main():
         "hbm_gbs_measured_traffic": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9,
         "hbm_peak_gbs": hbm_peak,
         "hbm_frac": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9 / hbm_peak,
-        "traffic_note": "ncu DRAM bytes of a 20-step capture scaled to this launch (state once + "
-                        "control stream per step); None where no capture exists for this config",
+        "traffic_note": "ncu DRAM bytes of a capture at 65536 worlds (NCU_DRAM_CAPTURES) scaled to this "
+                        "launch (state once + control stream per step); None where no capture exists for "
+                        "this config",
     }
 
     # e2e through the C ABI with host buffers
