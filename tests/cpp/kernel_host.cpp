@@ -76,20 +76,35 @@ void run(const ModelView<double>& M, const PackInfo& info, double* q, double* v,
 template <int F = 0>
 bool dispatch(int feat, const ModelView<double>& M, const PackInfo& info, double* q, double* v, const double* c, int n,
               int sweeps) {
-    if constexpr (F < 32) {
-        if constexpr (!((F & 8) && !(F & 4)) && !((F & 16) && !(F & 2)))
+    if constexpr (F < 64) {
+        if constexpr (!((F & 8) && !(F & 4)) && !((F & 16) && !(F & 2)) && !((F & 32) && !(F & 2)))
             if (feat == F) { run<F>(M, info, q, v, c, n, sweeps); return true; }
         return dispatch<F + 1>(feat, M, info, q, v, c, n, sweeps);
     }
     return false;
 }
+// The heightfield of the following rollouts with contact (nx = 0: the flat
+// ground): f32 nodes [ny][nx], node (ix, iy) at (ox + ix cell, oy + iy cell).
+static std::vector<float> g_hf;
+static int g_nx = 0, g_ny = 0;
+static double g_ho[3] = {0, 0, 0}, g_cell = 1.0;
+extern "C" void host_set_heightfield(int nx, int ny, double ox, double oy, double oz, double cell, const float* h) {
+    g_nx = nx;
+    g_ny = ny;
+    g_ho[0] = ox;
+    g_ho[1] = oy;
+    g_ho[2] = oz;
+    g_cell = cell;
+    g_hf.assign(h, h + (size_t)(nx > 0 ? nx * ny : 0));
+}
+
 // contact: 0 none, 1 penalty (gains k, d), 2 impulse (`sweeps` per step,
 // enable_contact_impulse's material)
 extern "C" int host_rollout(const phyzb_model* m, int nworld, double* q, double* v, const double* ctrl, int nsteps,
                             int contact, double ground, double friction, double k, double d, int sweeps) {
     const int nv = [&] { int s = 0; for (int i = 0; i < m->nbodies; i++) { int t = m->bodies[i].joint_type;
         s += t == 3 ? 3 : (t == 4 ? 6 : (t == 2 ? 0 : 1)); } return s; }();
-    PackCfg cfg; cfg.contact = contact != 0; cfg.impulse = contact == 2;
+    PackCfg cfg; cfg.contact = contact != 0; cfg.impulse = contact == 2; cfg.terrain = contact != 0 && g_nx > 0;
     cfg.gk.assign(m->nbodies, k); cfg.gd.assign(m->nbodies, d);
     std::vector<unsigned char> blob;
     PackInfo info = pack_model<double>(m, nv, cfg, blob, 0);
@@ -107,7 +122,8 @@ extern "C" int host_rollout(const phyzb_model* m, int nworld, double* q, double*
     const double erp = m->dt > 0.0 ? m->dt / (2.0 * 0.02 + m->dt) : 0.0;
     M.im = ImpMat<double>{ground, friction, m->dt, erp, 0.001, 0.0, 0.05, 0.9, 0.95, 0.001, 0.5, 2.0};
     impmat_finish(M.im);
-    M.ter = Terrain<double>{nullptr, 0, 0, 0, 0, 0, 1};
+    M.ter = cfg.terrain ? Terrain<double>{g_hf.data(), g_nx, g_ny, g_ho[0], g_ho[1], g_ho[2], g_cell}
+                        : Terrain<double>{nullptr, 0, 0, 0, 0, 0, 1};
     M.plane = PlaneT<double>{-1, 0, 0, 0, 0};
     for (int w = 0; w < nworld; w++)
         if (!dispatch(info.feat, M, info, q + (size_t)w * nv, v + (size_t)w * nv, ctrl + (size_t)w * nv, nsteps,

@@ -34,6 +34,8 @@ def kernels(tmp_path_factory):
         lib = C.CDLL(str(so))
         lib.host_rollout.argtypes = [C.c_void_p, C.c_int, D, D, D, C.c_int, C.c_int, C.c_double, C.c_double,
                                      C.c_double, C.c_double, C.c_int]
+        lib.host_set_heightfield.argtypes = [C.c_int, C.c_int, C.c_double, C.c_double, C.c_double, C.c_double,
+                                             C.POINTER(C.c_float)]
         out[tag] = lib
     return out
 
@@ -84,3 +86,30 @@ def test_kernel_source_impulse_matches_oracle(kernels, oracle, name):
         # may send a world down another branch, as in the GPU impulse tests
         ok = np.max(np.abs(q - qo), axis=1) < 1e-8
         assert ok.mean() >= 0.9, (tag, ok.mean(), np.abs(q - qo).max())
+
+
+def test_kernel_source_terrain_matches_oracle(kernels, oracle):
+    """Penalty contact over a heightfield (full world frames, bilinear
+    terrain and its gradient normal): the kernel source against the oracle
+    on the quadruped walking over bumps."""
+    from phyz_b200 import Heightfield
+
+    rng = np.random.default_rng(3)
+    hf = Heightfield.new((-2.0, -2.0, -0.05), 0.25, 17, 17)
+    hf.heights[:] = (0.08 * rng.standard_normal(17 * 17)).astype(np.float32)
+    h = np.ascontiguousarray(hf.heights, np.float32)
+    try:
+        for lib in kernels.values():
+            lib.host_set_heightfield(17, 17, *hf.origin, hf.cell, h.ctypes.data_as(C.POINTER(C.c_float)))
+        runs = {tag: host_run(lib, "c3_quadruped") for tag, lib in kernels.items()}
+        m, q0, v0, c, _, _, _ = runs["generic"]
+        oracle.set_heightfield(hf)
+        qo, vo, _, _ = oracle.rollout(m, q0, v0, c, nsteps=100, contact=(0.0, 1.0, [1e4] * m.nbodies,
+                                                                         [100.0] * m.nbodies), nthreads=4)
+    finally:
+        oracle.set_heightfield(None)
+        for lib in kernels.values():
+            lib.host_set_heightfield(0, 0, 0.0, 0.0, 0.0, 1.0, None)
+    for tag, (_, _, _, _, _, q, v) in runs.items():
+        assert np.all(np.isfinite(q)) and np.all(np.isfinite(v)), tag
+        np.testing.assert_allclose(q, qo, rtol=0, atol=1e-10, err_msg=tag)
