@@ -492,7 +492,9 @@ int phyzb_policy_advantages(phyzb_sim* sim, phyzb_trainer* tr, struct phyzb_comm
  * loads the library until exit); a larger nworld returns
  * PHYZB_ERR_TOO_LARGE. The first call on a device looks that array's address
  * up (cudaGetSymbolAddress), so make the first call on each device before
- * any stream capture. All calls on a device share the array: calls whose
+ * any stream capture. The address is kept for the life of the process: a
+ * cudaDeviceReset of a device ends it, so do not call this entry point on a
+ * device after resetting that device. All calls on a device share the array: calls whose
  * kernels overlap on the device race, so order them on one stream or with
  * events. Runs on `stream` (a cudaStream_t, NULL = the default stream);
  * asynchronous unless `stats` (optional, host, 3 doubles: mean return per

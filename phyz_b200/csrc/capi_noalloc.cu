@@ -45,7 +45,10 @@ double* g_addr[MAX_DEVICES] = {};
 
 // The device address of g_gae_scratch on `device` (current). The host-side
 // name of a __device__ array is only a stand-in for it, so host code looks the
-// address up once per device and hands that to the kernels.
+// address up once per device and hands that to the kernels. The cached
+// address lives as long as the device's primary context: a cudaDeviceReset
+// unloads this module's copy of the array, after which the entry point must
+// not be called on that device (the header says so).
 int scratch_on(int device, double** out) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_addr[device]) {

@@ -5,6 +5,7 @@ the reference's own benchmark models (models/*.xml, tests/
 benchmark_models.rs) where its tree is present. The models then step on the
 oracle, so a loaded model is a usable model."""
 import math
+import os
 from pathlib import Path
 
 import numpy as np
@@ -13,7 +14,9 @@ import pytest
 from phyz_b200.mjcf import MjcfError, MjcfLoader, load_mjcf
 from phyz_b200.model import BALL, FIXED, FREE
 
-REF_MODELS = Path("/root/reference/models")
+# the reference tree: $PHYZ_REFERENCE, else a `reference` directory beside the
+# repository; the tests that read its models skip when neither exists
+REF_MODELS = Path(os.environ.get("PHYZ_REFERENCE", Path(__file__).resolve().parents[2] / "reference")) / "models"
 
 
 def load(xml):
