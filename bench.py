@@ -12,13 +12,20 @@ max over ranks. Multi-GPU runs are weak-scaled: each rank owns its own
 contiguous block of worlds (no per-step communication); one NCCL all-reduce
 of the per-world objective closes every rollout.
 
-`value` has the inputs (initial state, control schedule) resident in HBM.
-`e2e` is the same metric through the C ABI with host buffers: the initial
-state and every step's controls copied in from pinned host memory and the
-final state read back, inside the timed region. `roofline` is the fused
-kernel against the measured FP32/FP64 FMA pipe. `cpu_baseline` is the
-reference's own kernels compiled as host C++ (oracle/_ref), on this host's
-cores. `--impl reference` times only that reference CPU path.
+`value` has the inputs (initial state, control schedule) resident in HBM;
+where the schedule is smaller than L2, a 256 MB buffer is written between
+rollouts and value counts the rollouts' own device time. `e2e` is the same
+metric through the C ABI with host buffers: the initial state and every
+step's controls copied in from pinned host memory and the final state read
+back, inside the timed region. `roofline` is the fused kernel against the
+measured FP32/FP64 FMA pipe, counting the flops the running kernel executes
+on this rollout's states. `cpu_baseline` is the reference's own kernels
+compiled as host C++ (oracle/_ref) on this host's cores, on a fixed sample
+both arms time alike; f64 runs add the f64 oracle (`cpu_baseline_f64_oracle`).
+`reference_gpu` is the reference's own CUDA kernels on this GPU in their
+stock launch sequence. The default run also measures C1 (f64, its 4096
+worlds split over the GPUs), C3 and C4 (f32) under `per_config`.
+`--impl reference` times only the reference CPU path.
 
 `--config c3_quadruped_impulse` runs C3's worlds with impulse-mode contact
 (16 staged Coulomb sweeps per step) in place of the penalty law, 100 steps
@@ -109,10 +116,13 @@ def parse():
     ap.add_argument("--horizon", type=int, default=0, help="physics steps per bench step (0: the config's)")
     ap.add_argument("--nworld", type=int, default=0, help="worlds per GPU (0: the config's)")
     ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--e2e-horizon", type=int, default=100)
+    ap.add_argument("--e2e-horizon", type=int, default=0, help="steps of the e2e rollout (0: the full horizon)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's own CUDA kernels on this GPU")
+    ap.add_argument("--per-config", type=int, default=1,
+                    help="with the default workload, also measure C1 f64, C3 f32 and C4 f32 (0: off)")
     ap.add_argument("--specialize", default="auto", choices=["auto", "0", "1"],
                     help="rollout kernel: 1 compiled at run time for the model (tables literal, loops "
                          "unrolled), 0 the generic variant, auto 1 unless the model's longest chain "
@@ -207,61 +217,159 @@ def allreduce_max(x: float, world: int) -> float:
     return float(t.item())
 
 
-# ── the reference's CPU path (oracle/_ref) ────────────────────────────────
-def reference_cpu(workload, model, nworld, horizon, seconds, world_offset=0):
-    """Time the reference's own kernels compiled as host C++ on every host
-    core, on a bounded sample of the workload: up to 16384 of its worlds (2048
-    in impulse mode) for
-    as many of its steps as fit ~`seconds` (controls from a 64-step seeded
-    schedule reused cyclically; in impulse mode the reference's sweep
-    sequence, its warm start carried between chunks). Returns (world-steps/s,
-    threads, sample)."""
-    from oracle.oracle import RefHost, cpu_threads
+# ── shared by both arms ───────────────────────────────────────────────────
+L2_BYTES = 126 * 1024 * 1024  # B200 L2
+
+
+def schedule_bytes(model, nworld, horizon, prec):
+    return horizon * model.nv * nworld * (4 if prec == "f32" else 8)
+
+
+def l2_rule(model, nworld, horizon, prec):
+    """(flush between rollouts?, the note for `config.l2`)."""
+    b = schedule_bytes(model, nworld, horizon, prec)
+    if b > L2_BYTES:
+        return False, (f"inputs larger than L2: the per-step control schedule ({b / 1e9:.2f} GB) streams from HBM "
+                       "every rollout")
+    return True, (f"inputs smaller than L2 ({b / 1e6:.1f} MB schedule): a 256 MB buffer is written between timed "
+                  "rollouts (L2 flushed) and value counts the rollouts' own device time")
+
+
+def bench_config(workload, model, nworld, horizon, prec, n_gpus, strong=False):
+    """The `config` block, identical in both arms for the same arguments."""
+    cfg_name, impulse, _ = base_config(workload)
     from phyz_b200 import configs
 
-    cfg_name, impulse, _ = base_config(workload)
+    cfg = configs.CONFIGS[cfg_name]
+    contact = None
+    if cfg.contact:
+        contact = ("impulse, 16 sweeps per step" if impulse else
+                   ("penalty, 64 x 64 heightfield" if workload in TERRAIN_WORKLOADS else "penalty"))
+    out = {"workload": workload, "nbodies": model.nbodies, "nv": model.nv, "horizon": horizon, "precision": prec,
+           "contact": contact, "l2": l2_rule(model, nworld, horizon, prec)[1]}
+    if strong:
+        out["nworld_total"] = nworld
+        out["parallelism"] = f"{nworld} worlds split over {n_gpus} GPU(s) (strong scaling)"
+    else:
+        out["nworld_per_gpu"] = nworld
+        out["parallelism"] = f"{nworld} worlds per GPU on each of {n_gpus} GPU(s) (weak scaling)"
+    return out
+
+
+# ── the reference's CPU path (oracle/_ref) and the f64 oracle ─────────────
+CPU_CHUNK = 64  # steps per timed repetition
+
+
+def _cpu_sample(workload, model, nworld, impulse):
+    from phyz_b200 import configs
+
+    cfg_name = base_config(workload)[0]
+    cfg = configs.CONFIGS[cfg_name]
+    n = min(nworld, 2048 if impulse else 16384)  # an impulse step costs ~17 plain ones
+    q, v = configs.initial_state(cfg_name, model, np.arange(n))
+    rng = np.random.default_rng(configs.CTRL_SEED)
+    sched = (rng.standard_normal((CPU_CHUNK, n, model.nv)) * cfg.ctrl_sigma * configs.actuated(model)).astype(
+        np.float32)
+    return cfg, n, q, v, sched
+
+
+def reference_cpu(workload, model, nworld, horizon, reps, warm=1):
+    """The reference's own kernels compiled as host C++ on every host core,
+    timed on a fixed sample of the workload: min(nworld, 16384) of its worlds
+    (2048 in impulse mode) from their seeded initial states, 64 steps of
+    seeded controls per repetition, `warm` untimed then `reps` timed
+    repetitions, each from the same initial state. Both bench arms call this
+    with the same arguments. Returns (median world-steps/s, threads, sample
+    text, per-repetition values)."""
+    from oracle.oracle import RefHost, cpu_threads
+
+    _, impulse, _ = base_config(workload)
+    cfg, n, q0, v0, sched = _cpu_sample(workload, model, nworld, impulse)
     ref = RefHost()
     ref.set_heightfield(bench_heightfield(workload))
-    cfg = configs.CONFIGS[cfg_name]
     threads = cpu_threads()
-    n = min(nworld, 2048 if impulse else 16384)  # an impulse step costs ~17 plain ones
-    worlds = np.arange(world_offset, world_offset + n)
-    q, v = configs.initial_state(cfg_name, model, worlds)
     contact = None
     if cfg.contact:
         g, k, d, mu = cfg.contact
         contact = (g, mu, k, d)
-    rng = np.random.default_rng(configs.CTRL_SEED)
-    period = 64
-    sched = (rng.standard_normal((period, n, model.nv)) * cfg.ctrl_sigma * configs.actuated(model)).astype(np.float32)
-    state = [None]
 
-    def chunk(q, v, steps, ctrl):
+    def once():
+        t0 = time.perf_counter()
         if impulse:
-            q, v, _, _, state[0] = ref.rollout_impulse(model, q, v, ctrl, steps, schedule=True,
-                                                       contact=(contact[0], contact[1]), state=state[0],
-                                                       nthreads=threads)
-            return q, v
-        q, v, _, _ = ref.rollout(model, q, v, ctrl, steps, schedule=True, contact=contact, nthreads=threads)
-        return q, v
+            ref.rollout_impulse(model, q0, v0, sched, CPU_CHUNK, schedule=True, contact=(contact[0], contact[1]),
+                                nthreads=threads)
+        else:
+            ref.rollout(model, q0, v0, sched, CPU_CHUNK, schedule=True, contact=contact, nthreads=threads)
+        return n * CPU_CHUNK / (time.perf_counter() - t0)
 
-    # calibrate on 4 steps, then run whole 64-step chunks for ~`seconds`
-    t0 = time.perf_counter()
-    chunk(q, v, 4, sched[:4])
-    state[0] = None
-    per_step = (time.perf_counter() - t0) / 4
-    chunks = int(max(1, min(-(-horizon // period), seconds / max(per_step * period, 1e-9))))
-    t0 = time.perf_counter()
-    for _ in range(chunks):
-        q, v = chunk(q, v, period, sched)
-    dt = time.perf_counter() - t0
-    steps = chunks * period
-    mode = ", impulse contact (16 sweeps)" if impulse else ""
+    for _ in range(warm):
+        once()
+    vals = [once() for _ in range(reps)]
+    ref.set_heightfield(None)
+    mode = {True: ", impulse contact (16 sweeps)"}.get(impulse, "")
     if workload in TERRAIN_WORKLOADS:
         mode = ", heightfield terrain"
-        ref.set_heightfield(None)
-    return n * steps / dt, threads, (f"{n} of {nworld} worlds x {steps} of {horizon} steps, f32{mode}, "
-                                     f"{threads} threads, {dt:.1f} s")
+    sample = (f"{n} of {nworld} worlds x {CPU_CHUNK} of {horizon} steps, f32{mode}, {threads} threads, median of "
+              f"{reps} repetitions after {warm} untimed")
+    return statistics.median(vals), threads, sample, vals
+
+
+def oracle_cpu(workload, model, nworld, horizon, reps):
+    """The f64 oracle (this repository's C++ restatement of phyz-rigid's ABA
+    and integrator with the reference GPU's penalty law) on every host core,
+    on min(nworld, 2048) worlds x 64 steps per repetition, median of `reps`.
+    None for impulse and terrain workloads."""
+    from oracle.oracle import Oracle, cpu_threads
+
+    _, impulse, _ = base_config(workload)
+    if impulse or workload in TERRAIN_WORKLOADS:
+        return None
+    cfg, n, q0, v0, sched = _cpu_sample(workload, model, min(nworld, 2048), False)
+    o = Oracle()
+    threads = cpu_threads()
+    contact = None
+    if cfg.contact:
+        g, k, d, mu = cfg.contact
+        contact = (g, mu, k, d)
+    sched = sched.astype(np.float64)
+
+    def once():
+        t0 = time.perf_counter()
+        o.rollout(model, q0, v0, sched, CPU_CHUNK, schedule=True, contact=contact, nthreads=threads)
+        return n * CPU_CHUNK / (time.perf_counter() - t0)
+
+    once()
+    vals = [once() for _ in range(reps)]
+    return {"value": statistics.median(vals), "unit": "world-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{n} of {nworld} worlds x {CPU_CHUNK} of {horizon} steps, f64 oracle (phyz-rigid restated), "
+                      f"{threads} threads, median of {reps} repetitions"}
+
+
+def reference_gpu(workload, model, nworld, horizon):
+    """The reference's own CUDA kernels (crates/phyz-gpu/cuda/phyz_kernels.cu
+    built for sm_100a by oracle/Makefile) on this GPU, in its stock sequence
+    (contact -> aba -> integrate per step, 64-thread blocks, the rollout
+    replayed as one captured CUDA graph), f32, the same worlds and horizon,
+    controls held at the first step's row. Best of 3 replays."""
+    from oracle.oracle import RefCuda, RefHost
+    from phyz_b200 import configs
+
+    cfg_name, impulse, _ = base_config(workload)
+    if impulse or workload in TERRAIN_WORKLOADS:
+        return None
+    cfg = configs.CONFIGS[cfg_name]
+    q0, v0 = configs.initial_state(cfg_name, model, np.arange(nworld))
+    rng = np.random.default_rng(configs.CTRL_SEED)
+    ctrl = (rng.standard_normal((nworld, model.nv)) * cfg.ctrl_sigma * configs.actuated(model)).astype(np.float32)
+    contact = None
+    if cfg.contact:
+        g, k, d, mu = cfg.contact
+        contact = (g, mu, k, d)
+    rc = RefCuda(RefHost())
+    _, _, _, _, ms = rc.rollout(model, q0, v0, ctrl, horizon, contact=contact, reps=3)
+    return {"value": nworld * horizon / (ms * 1e-3), "unit": "world-steps/s", "ms_per_rollout": ms,
+            "path": "phyz_kernels.cu contact -> aba -> integrate, 64-thread blocks, one CUDA graph per rollout, "
+                    "f32, controls held"}
 
 
 def run_reference_impl(args, world, rank):
@@ -274,58 +382,84 @@ def run_reference_impl(args, world, rank):
     model = cfg.builder()
     nworld = args.nworld or cfg.nworld
     horizon = args.horizon or h_default or cfg.steps
-    vals = []
-    for i in range(args.warmup + args.steps):
-        v, threads, sample = reference_cpu(args.config, model, nworld, horizon,
-                                           max(2.0, args.cpu_seconds / 3), 0)
-        if i >= args.warmup:
-            vals.append(v)
-    value = statistics.median(vals)
+    value, threads, sample, _ = reference_cpu(args.config, model, nworld, horizon, reps=max(args.steps, 1),
+                                              warm=max(args.warmup, 1))
     line = {
         "impl": "reference", "metric": "world-steps/sec", "value": value, "unit": "world-steps/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": args.config, "nworld": nworld, "horizon": horizon, "precision": "f32"},
+        "config": bench_config(args.config, model, nworld, horizon, args.precision, args.gpus),
         "cpu_baseline": {"value": value, "unit": "world-steps/s", "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": "world-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own kernels (phyz_kernels.cu) compiled as host C++, f32; the reference has no "
+                "f64 or multithreaded batch stepper of its own",
     }
     print(json.dumps(line), flush=True)
 
 
 # ── our arm ────────────────────────────────────────────────────────────────
-def main():
-    args = parse()
-    if args.impl == "reference":
-        # CPU only: no process group; rank 0 runs, the other ranks exit 0
-        run_reference_impl(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
-        return
-    world, rank, local = dist_setup(args)
-    if args.config == "c5_quadruped_ppo":
-        run_c5(args, world, rank, local)
-        finish(world)
-        return
+# Configs measured beside the headline in the default run (BASELINE.json
+# configs[0], [2], [3]): (workload, precision, worlds, strong scaling?).
+# C1's 4096 worlds are split over the GPUs (the north star's target is that
+# batch on 8 GPUs); C3 and C4 keep their worlds per GPU.
+PER_CONFIG = [("c1_double_pendulum", "f64", 4096, True), ("c3_quadruped", "f32", 262144, False),
+              ("c4_humanoid", "f32", 131072, False)]
 
+
+class Ctx:
+    """Per-process state shared by the measured workloads."""
+
+    def __init__(self, args, world, rank, local):
+        import torch
+
+        from phyz_b200.parallel import Comm, share_bytes
+
+        self.args, self.world, self.rank, self.local = args, world, rank, local
+        self.stream = torch.cuda.Stream()
+        self.comm = Comm(rank, world, local, timeout=120.0,
+                         id_channel=(lambda p, r: share_bytes(p, r)) if world > 1 else (lambda p, r: p))
+        self.flush_buf = None
+
+    def flush_l2(self):
+        import torch
+
+        if self.flush_buf is None:
+            self.flush_buf = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MB
+        with torch.cuda.stream(self.stream):
+            self.flush_buf.zero_()
+
+
+def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=False, e2e=False, cpu=False,
+            ref_gpu=False, specialize="auto"):
+    """One workload on this rank: `steps` timed rollouts after `warmup`.
+    Returns the entry (rank 0's view; times are max over ranks)."""
     import torch
 
     from phyz_b200 import BatchSim, configs
     from phyz_b200 import _lib as L
-    from phyz_b200.parallel import Comm, share_bytes, weak_block
+    from phyz_b200.parallel import shard_bounds, weak_block
 
-    cfg_name, impulse, h_default = base_config(args.config)
+    args, world, rank, local, stream = ctx.args, ctx.world, ctx.rank, ctx.local, ctx.stream
+    cfg_name, impulse, h_default = base_config(workload)
     cfg = configs.CONFIGS[cfg_name]
     model = cfg.builder()
-    nworld = args.nworld or cfg.nworld
-    horizon = args.horizon or h_default or cfg.steps
-    prec = args.precision
+    total = nworld_arg or cfg.nworld
+    horizon = horizon_arg or h_default or cfg.steps
+    if strong:
+        lo, hi = shard_bounds(total, rank, world)
+        nworld, offset = hi - lo, lo
+    else:
+        nworld = total
+        offset, _ = weak_block(nworld, rank)
     tdt = torch.float32 if prec == "f32" else torch.float64
     esz = 4 if prec == "f32" else 8
     nv = model.nv
-    offset, _ = weak_block(nworld, rank)  # this rank's block of worlds
+    flush, l2_note = l2_rule(model, nworld, horizon, prec)
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
-    sim.specialize = {"auto": "auto", "0": False, "1": True}[args.specialize]
-    hf = bench_heightfield(args.config)
+    sim.specialize = {"auto": "auto", "0": False, "1": True}[specialize]
+    hf = bench_heightfield(workload)
     if cfg.contact and impulse:
         sim.enable_contact_impulse(cfg.contact[0], cfg.contact[3])
     elif cfg.contact and hf is not None:
@@ -335,7 +469,6 @@ def main():
         sim.enable_contact_terrain(g, mu, [BodyContactGains(k, d)] * model.nbodies, heightfield=hf)
     elif cfg.contact:
         sim.enable_ground_contact(*cfg.contact)
-    stream = torch.cuda.Stream()
     sim.set_stream(stream.cuda_stream)
 
     # inputs resident in HBM: initial state (SoA) and the per-step controls
@@ -349,58 +482,71 @@ def main():
     with torch.cuda.stream(stream):
         sched = torch.randn(horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
     stream.synchronize()
-    # the end-of-rollout collective: sum of the per-world objective over all
-    # ranks (NCCL through the library; one rank at N=1)
-    comm = Comm(rank, world, local, timeout=120.0,
-                id_channel=(lambda p, r: share_bytes(p, r)) if world > 1 else (lambda p, r: p))
     objective = [0.0]
 
-    def reset_state():
-        # every rollout starts from the same seeded state: same work each step
-        sim.load_states_device(q0_dev.data_ptr(), v0_dev.data_ptr())
-
     def rollout(ev=None):
-        reset_state()
         if ev is not None:
             ev[0].record(stream)
-        sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
+        sim.load_states_device(q0_dev.data_ptr(), v0_dev.data_ptr())  # same start, same work each rollout
         if ev is not None:
             ev[1].record(stream)
-        objective[0] = comm.reduce_objective(sim, 0)
+        sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
+        if ev is not None:
+            ev[2].record(stream)
+        objective[0] = ctx.comm.reduce_objective(sim, 0)
+        if ev is not None:
+            ev[3].record(stream)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         rollout()
+        if flush:
+            ctx.flush_l2()
     stream.synchronize()
     sim.sync()
 
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         t0.record(stream)
-        for k in range(args.steps):
-            rollout(kev[k])
+        for k in range(steps):
+            rollout(ev[k])
+            if flush:
+                ctx.flush_l2()
         t1.record(stream)
         stream.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     sim.sync()  # raises if any world went non-finite
-    ms = allreduce_max(t0.elapsed_time(t1), world)
-    per_launch = sorted(a.elapsed_time(b) for a, b in kev)
-    kernel_ms = allreduce_max(sum(per_launch) / args.steps, world)
+    region_ms = allreduce_max(t0.elapsed_time(t1), world)
+    rollout_ms = allreduce_max(sum(e[0].elapsed_time(e[3]) for e in ev), world)
+    per_launch = sorted(e[1].elapsed_time(e[2]) for e in ev)
+    kernel_ms = allreduce_max(sum(per_launch) / steps, world)
     kernel_ms_min = allreduce_max(per_launch[0], world)
     kernel_ms_median = allreduce_max(statistics.median(per_launch), world)
-    world_steps = nworld * horizon * world
-    value = world_steps * args.steps / (ms * 1e-3)
+    world_steps = (total if strong else nworld * world) * horizon
+    ms = rollout_ms if flush else region_ms
+    value = world_steps * steps / (ms * 1e-3)
 
-    # roofline of the fused kernel: algorithmic flops / launch time vs the
-    # measured FMA pipe of this precision
-    flops_ws, trans_ws = sim.flops_per_world_step()
+    # roofline of the fused kernel against the measured FMA pipe of this
+    # precision: the flops the running kernel executes per world-step,
+    # counted on this rank's first 16 worlds over the whole schedule (the
+    # contact force law included where a body touches; the specialized
+    # kernel without its products with zero table constants), beside the
+    # generic formulation's steady-state count
+    flops_gen, trans_ws = sim.flops_per_world_step()
+    ns = min(16, nworld)
+    ctrl_s = sched[:, :, :ns].permute(0, 2, 1).double().cpu().numpy()
+    try:
+        flops_ex, _ = sim.flops_executed(q0[:ns], v0[:ns], ctrl_s, specialized=sim.specialized)
+    except L.PhyzbError:
+        flops_ex = None  # terrain: counted on the flat ground only
+    flops_ws = flops_ex if flops_ex is not None else flops_gen
     pk = np.zeros(1)
     L.check(L.load().phyzb_measure_fma_peak(L.F32 if prec == "f32" else L.F64, L.dptr(pk)))
     achieved = flops_ws * nworld * horizon / (kernel_ms * 1e-3) / 1e12
-    traffic = ncu_traffic(args.config, prec, nv, esz, nworld, horizon)
+    traffic = ncu_traffic(workload, prec, nv, esz, nworld, horizon)
     hbm_peak = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()).get("hbm_gbs") \
         if (ROOT / "MEASURED_PEAKS.json").exists() else 6650.0
     alg_bytes = (3 + 2) * nv * esz  # read q, v, ctrl; write q, v per world-step
@@ -408,9 +554,16 @@ def main():
         "bound": "fma", "pipe": f"{'fp32' if prec == 'f32' else 'fp64'} FMA", "achieved": achieved,
         "peak": float(pk[0]), "unit": "TFLOP/s", "frac": achieved / float(pk[0]),
         "peak_source": "measured in this run (independent FMA chains over every SM, phyzb_measure_fma_peak)",
+        "flops_per_world_step": flops_ws,
+        "flops_counted": ("executed by the running kernel on this rollout's first 16 worlds (contact force law "
+                          "where bodies touch" + ("; model-specialized: products with zero table constants left "
+                                                  "out)" if sim.specialized else ")")
+                          if flops_ex is not None else "generic formulation, steady state, contact force excluded"),
+        "flops_per_world_step_generic": flops_gen,
+        "frac_generic_count": flops_gen * nworld * horizon / (kernel_ms * 1e-3) / 1e12 / float(pk[0]),
+        "transcendentals_per_world_step": trans_ws,
         "traffic": traffic, "kernel": "rollout_kernel", "kernel_ms_per_launch": kernel_ms,
         "kernel_ms_min": kernel_ms_min, "kernel_ms_median": kernel_ms_median,
-        "flops_per_world_step": flops_ws, "transcendentals_per_world_step": trans_ws,
         "algorithmic_bytes_per_world_step": alg_bytes,
         "hbm_gbs_algorithmic": alg_bytes * nworld * horizon / (kernel_ms * 1e-3) / 1e9,
         "hbm_gbs_measured_traffic": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9,
@@ -418,16 +571,19 @@ def main():
         "hbm_frac": None if traffic is None else traffic / (kernel_ms * 1e-3) / 1e9 / hbm_peak,
         "traffic_note": "ncu DRAM bytes of a capture at 65536 worlds (NCU_DRAM_CAPTURES) scaled to this "
                         "launch (state once + control stream per step); None where no capture exists for "
-                        "this config",
+                        "this workload",
     }
 
-    # e2e through the C ABI with host buffers
-    e2e = None
-    if not args.no_e2e:
-        eh = min(args.e2e_horizon, horizon)
-        host_ctrl = torch.empty((eh, nworld, nv), dtype=torch.float32 if prec == "f32" else torch.float64,
-                                pin_memory=True)
-        host_ctrl.copy_(sched[:eh].permute(0, 2, 1).cpu())
+    # e2e through the C ABI with host buffers: every step's controls copied
+    # in from pinned host memory, held as a ring of at most ~4 GB of steps
+    # that the rollout walks through (the full horizon for C2 f32 takes
+    # three passes: 476 + 476 + 48 steps)
+    e2e_out = None
+    if e2e:
+        eh = min(args.e2e_horizon or horizon, horizon)
+        ring = max(1, min(eh, (4 << 30) // (nworld * nv * esz)))
+        host_ctrl = torch.empty((ring, nworld, nv), dtype=tdt, pin_memory=True)
+        host_ctrl.copy_(sched[:ring].permute(0, 2, 1).cpu())
         # every host buffer of the e2e leg is pinned (page-locked), the form a
         # collector streaming rollouts keeps its rows in
         q0_pin = torch.from_numpy(np.ascontiguousarray(q0, np.float64)).pin_memory().numpy()
@@ -438,7 +594,11 @@ def main():
 
         def e2e_step():
             sim.load_states(q0_pin, v0_pin)
-            sim.step_with_controls_ptr(host_ctrl.data_ptr(), hdt, eh)
+            done = 0
+            while done < eh:
+                n = min(ring, eh - done)
+                sim.step_with_controls_ptr(host_ctrl.data_ptr(), hdt, n)
+                done += n
             sim.readback_states(out=(hq, hv))
 
         e2e_step()
@@ -452,44 +612,100 @@ def main():
         stream.synchronize()
         barrier(world)
         ems = allreduce_max(e0.elapsed_time(e1), world)
-        e2e = {"value": nworld * eh * world * args.e2e_steps / (ems * 1e-3), "unit": "world-steps/s",
-               "h2d_bytes_per_step": int(2 * nworld * nv * 8 + host_ctrl.numel() * host_ctrl.element_size()),
-               "d2h_bytes_per_step": int(2 * nworld * nv * 8), "horizon": eh,
-               "path": "phyzb_load_states + phyzb_step_with_controls + phyzb_readback_states, pinned host buffers"}
+        e2e_out = {"value": nworld * eh * world * args.e2e_steps / (ems * 1e-3), "unit": "world-steps/s",
+                   "h2d_bytes_per_step": int(2 * nworld * nv * 8 + eh * nworld * nv * esz),
+                   "d2h_bytes_per_step": int(2 * nworld * nv * 8), "horizon": eh,
+                   "path": f"phyzb_load_states + phyzb_step_with_controls + phyzb_readback_states, pinned host "
+                           f"buffers; controls from a {ring}-step pinned ring walked to the horizon"}
+        del host_ctrl
 
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    cpu_out = oracle_out = None
+    if cpu and rank == 0 and world == 1:
         try:
-            v, threads, sample = reference_cpu(args.config, model, nworld, horizon, args.cpu_seconds)
-            cpu = {"value": v, "unit": "world-steps/s", "cores": threads, "kind": "reference", "sample": sample}
+            v, threads, sample, _ = reference_cpu(workload, model, nworld, horizon, reps=7)
+            cpu_out = {"value": v, "unit": "world-steps/s", "cores": threads, "kind": "reference",
+                       "sample": sample}
         except Exception as ex:  # the baseline is reported, never required
-            cpu = {"value": None, "unit": "world-steps/s", "cores": None, "kind": "reference",
-                   "sample": f"unavailable: {ex}"}
+            cpu_out = {"value": None, "unit": "world-steps/s", "cores": None, "kind": "reference",
+                       "sample": f"unavailable: {ex}"}
+        if prec == "f64":
+            try:
+                oracle_out = oracle_cpu(workload, model, nworld, horizon, reps=7)
+            except Exception as ex:
+                oracle_out = {"value": None, "kind": "port", "sample": f"unavailable: {ex}"}
+    ref_gpu_out = None
+    if ref_gpu and rank == 0 and world == 1:
+        try:
+            ref_gpu_out = reference_gpu(workload, model, nworld, horizon)
+            if ref_gpu_out is not None:
+                ref_gpu_out["ratio"] = value / ref_gpu_out["value"]
+        except Exception as ex:
+            ref_gpu_out = {"value": None, "note": f"unavailable: {ex}"}
 
     info = sim.launch_info()
+    entry = {
+        "value": value, "unit": "world-steps/s", "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
+        "dtype": prec, "scaling": "strong" if strong else "weak",
+        "config": bench_config(workload, model, total, horizon, prec, world, strong=strong),
+        "launch": info,
+        "kernel": ("model-specialized (compiled at run time for this model)" if sim.specialized
+                   else "generic variant"),
+        "timed_region_ms": region_ms,
+        "roofline": roofline, "cpu_baseline": cpu_out, "e2e": e2e_out, "clocks": clk.summary(),
+        "gpu_launches": steps * 2,  # per rollout: rollout_kernel + objective_kernel
+        "objective": objective[0],
+    }
+    if oracle_out is not None:
+        entry["cpu_baseline_f64_oracle"] = oracle_out
+    if ref_gpu_out is not None:
+        entry["reference_gpu"] = ref_gpu_out
+    del sched
+    sim.close()
+    torch.cuda.empty_cache()
+    return entry
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        # CPU only: no process group; rank 0 runs, the other ranks exit 0
+        run_reference_impl(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local = dist_setup(args)
+    if args.config == "c5_quadruped_ppo":
+        run_c5(args, world, rank, local)
+        finish(world)
+        return
+    ctx = Ctx(args, world, rank, local)
+    main_entry = measure(ctx, args.config, args.precision, args.nworld, args.horizon, args.steps, args.warmup,
+                         e2e=not args.no_e2e, cpu=not args.no_cpu_baseline, ref_gpu=not args.no_reference_gpu,
+                         specialize=args.specialize)
+    per_config = {}
+    if args.per_config and args.config == "c2_chain32" and not args.nworld and not args.horizon:
+        for wl, prec, total, strong in PER_CONFIG:
+            per_config[f"{wl}_{prec}"] = measure(ctx, wl, prec, total, 0, min(args.steps, 5), 3, strong=strong,
+                                                 cpu=not args.no_cpu_baseline,
+                                                 ref_gpu=not args.no_reference_gpu and prec == "f32",
+                                                 specialize=args.specialize)
     if rank == 0:
+        e = main_entry
         line = {
-            "metric": "world-steps/sec", "value": value, "unit": "world-steps/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": prec, "data": "synthetic (seeded)",
-            "config": {"workload": args.config, "nworld_per_gpu": nworld, "horizon": horizon, "nbodies":
-                       model.nbodies, "nv": nv, "parallelism": f"worlds sharded over {world} GPU(s)",
-                       "contact": (f"impulse, {sim.contact_sweeps} sweeps per step" if impulse
-                                   else ("penalty, 64 x 64 heightfield" if hf is not None
-                                         else ("penalty" if cfg.contact else None))),
-                       "l2": "inputs larger than L2: the per-step control schedule "
-                             f"({horizon * nv * nworld * esz / 1e9:.1f} GB) streams from HBM every rollout",
-                       "launch": info,
-                       "kernel": ("model-specialized (compiled at run time for this model)" if sim.specialized
-                                  else "generic variant")},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk.summary(),
-            "gpu_launches": args.steps * 2,  # per rollout: rollout_kernel + objective_kernel
-            "objective": objective[0],
+            "metric": "world-steps/sec", "value": e["value"], "unit": "world-steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": e["ms_per_step"], "higher_is_better": True,
+            "scaling": e["scaling"], "vs_baseline": None, "dtype": args.precision, "data": "synthetic (seeded)",
+            "config": e["config"], "launch": e["launch"], "kernel": e["kernel"],
+            "timed_region_ms": e["timed_region_ms"], "roofline": e["roofline"], "cpu_baseline": e["cpu_baseline"],
+            "e2e": e["e2e"], "clocks": e["clocks"], "gpu_launches": e["gpu_launches"],
+            "objective": e["objective"],
             "objective_reduce": "phyzb_reduce_objective (NCCL all-reduce over all ranks, once per rollout)",
         }
+        for key in ("cpu_baseline_f64_oracle", "reference_gpu"):
+            if key in e:
+                line[key] = e[key]
+        if per_config:
+            line["per_config"] = per_config
         print(json.dumps(line), flush=True)
-    comm.close()
-    sim.close()
+    ctx.comm.close()
     finish(world)
 
 

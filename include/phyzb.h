@@ -536,6 +536,18 @@ int phyzb_reduce_objective(phyzb_sim* sim, phyzb_comm* comm, int kind, double ti
  * settings, as executed by the kernel's formulation (add/sub/mul = 1,
  * fma = 2, div = 1), with transcendental calls tallied separately. */
 int phyzb_flops_per_world_step(const phyzb_sim* sim, double* flops, double* transcendentals);
+/* The flops the kernel executes per world-step on given states, averaged
+ * over `nworld` worlds stepped `nsteps` steps on the host by the kernel's
+ * own step code with a counting scalar: q, v host rows [nworld][nv] (as
+ * phyzb_load_states), ctrl [nsteps][nworld][nv] (NULL: zero controls).
+ * Unlike phyzb_flops_per_world_step it counts the contact force law where a
+ * body touches the flat ground (penalty or impulse mode, this simulator's
+ * settings). specialized = 1 counts as a model-specialized kernel executes
+ * (products with zero model-table constants left out), 0 as the generic
+ * variants do. Models with a heightfield or body plane return
+ * PHYZB_ERR_INVALID. Host work only; nothing touches the device. */
+int phyzb_flops_executed(const phyzb_sim* sim, const double* q, const double* v, const double* ctrl, int64_t nworld,
+                         int32_t nsteps, int32_t specialized, double* flops, double* transcendentals);
 /* FP32 (PHYZB_F32) or FP64 (PHYZB_F64) FMA-pipe throughput of the calling
  * thread's current device in TFLOP/s, measured with independent FMA chains
  * over every SM: the roofline denominator of the stepper's kernels. */

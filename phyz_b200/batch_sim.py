@@ -414,6 +414,22 @@ class BatchSim:
         check(self._lib.phyzb_flops_per_world_step(self._h, C.byref(f), C.byref(t)))
         return f.value, t.value
 
+    def flops_executed(self, q, v, ctrl=None, specialized: bool = False):
+        """Flops per world-step the kernel executes from these states
+        (q, v [n][nv] rows; ctrl [steps][n][nv] or None for one zero-control
+        step), the contact force law included where a body touches; with
+        `specialized`, as a model-specialized kernel executes them (products
+        with zero table constants left out). Returns (flops, transcendentals)."""
+        q = np.ascontiguousarray(q, np.float64)
+        v = np.ascontiguousarray(v, np.float64)
+        n = q.shape[0]
+        steps = 1 if ctrl is None else int(np.shape(ctrl)[0])
+        c = None if ctrl is None else np.ascontiguousarray(ctrl, np.float64)
+        f, t = C.c_double(), C.c_double()
+        check(self._lib.phyzb_flops_executed(self._h, dptr(q), dptr(v), None if c is None else dptr(c), n, steps,
+                                             int(bool(specialized)), C.byref(f), C.byref(t)))
+        return f.value, t.value
+
     @property
     def specialize(self):
         """Kernel specialization mode: False (generic variants), True (the

@@ -1034,6 +1034,19 @@ int phyzb_flops_per_world_step(const phyzb_sim* s, double* flops, double* transc
     return PHYZB_OK;
 }
 
+int phyzb_flops_executed(const phyzb_sim* s, const double* q, const double* v, const double* ctrl, int64_t nworld,
+                         int32_t nsteps, int32_t specialized, double* flops, double* transcendentals) {
+    PZ_TRY(check_sim(s));
+    if (!q || !v) return fail(PHYZB_ERR_INVALID, "null state rows");
+    if (nworld < 1 || nsteps < 1) return fail(PHYZB_ERR_INVALID, "nworld and nsteps must be >= 1");
+    if (s->cfg.terrain) return fail(PHYZB_ERR_INVALID, "executed flops are counted on the flat ground only");
+    const pz::FlopCount fc = pz::count_rollout(&s->model, s->nv, s->cfg, s->sweeps, s->ground_h, s->friction,
+                                               s->erp, q, v, ctrl, nworld, nsteps, specialized != 0);
+    if (flops) *flops = fc.flops;
+    if (transcendentals) *transcendentals = fc.transcendentals;
+    return PHYZB_OK;
+}
+
 int phyzb_set_kernel_specialization(phyzb_sim* s, int32_t mode) {
     PZ_TRY(check_sim(s));
     if (mode != PHYZB_SPECIALIZE_OFF && mode != PHYZB_SPECIALIZE_ON && mode != PHYZB_SPECIALIZE_AUTO)

@@ -18,6 +18,9 @@ struct Tally {
     double flops = 0, trans = 0;
 };
 static thread_local Tally g_tally;
+// count as a model-specialized kernel executes: products with zero table
+// constants left out (pz_types.cuh kzero)
+static thread_local bool g_kskip = false;
 
 struct Cnt {
     double v;
@@ -79,6 +82,7 @@ struct Eps<Cnt> {
 template <>
 struct Counting<Cnt> {
     static constexpr bool value = true;
+    static bool kskip_on() { return g_kskip; }
 };
 
 }  // namespace pz
@@ -119,16 +123,30 @@ struct HostScr {
 };
 }  // namespace
 
-FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps) {
+namespace {
+// The packed model in the counting scalar, and a view of it whose ground
+// sits at `ground_h` (far below: detection is counted, the force law is not).
+struct CountModel {
     std::vector<unsigned char> blob;
-    const PackInfo info = pack_model<double>(m, nv, cfg, blob);
+    PackInfo info;
+    std::vector<BodyT<Cnt>> bt;
+    std::vector<PdT<Cnt>> pd;
+    ModelView<Cnt> M;
+};
+
+void make_count_model(const phyzb_model* m, int nv, const PackCfg& cfg, double ground_h, double friction, double erp,
+                      CountModel* cm) {
+    std::vector<unsigned char>& blob = cm->blob;
+    cm->info = pack_model<double>(m, nv, cfg, blob);
+    const PackInfo& info = cm->info;
     const int nb = m->nbodies, npd = (int)cfg.pd.size();
-    // the same table in the counting scalar (BodyT<double> -> BodyT<Cnt>)
-    std::vector<BodyT<Cnt>> bt(nb);
+    std::vector<BodyT<Cnt>>& bt = cm->bt;
+    bt.resize(nb);
     const BodyT<double>* src = reinterpret_cast<const BodyT<double>*>(blob.data());
     static_assert(sizeof(BodyT<double>) == sizeof(BodyT<Cnt>), "layout");
     std::memcpy((void*)bt.data(), src, sizeof(BodyT<double>) * nb);
-    std::vector<PdT<Cnt>> pd(npd > 0 ? npd : 1);
+    std::vector<PdT<Cnt>>& pd = cm->pd;
+    pd.resize(npd > 0 ? npd : 1);
     const PdT<double>* psrc = reinterpret_cast<const PdT<double>*>(blob.data() + info.off_pd);
     for (int k = 0; k < npd; k++) {
         pd[k].kp = psrc[k].kp;
@@ -137,7 +155,7 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
         pd[k].qi = psrc[k].qi;
         pd[k].vi = psrc[k].vi;
     }
-    ModelView<Cnt> M;
+    ModelView<Cnt>& M = cm->M;
     M.bt = M.btp = bt.data();
     M.bi = reinterpret_cast<const BodyI*>(blob.data() + info.off_bi);
     M.pd = pd.data();
@@ -150,14 +168,13 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     M.gx = Cnt(m->gravity[0]);
     M.gy = Cnt(m->gravity[1]);
     M.gz = Cnt(m->gravity[2]);
-    // Ground far below: contact detection is counted, the force law is not
-    // (a lower bound on the work of a contact step).
-    M.ground_h = Cnt(-1e9);
-    M.friction = Cnt(1.0);
+    M.ground_h = Cnt(ground_h);
+    M.friction = Cnt(friction);
     const double dtc = m->dt > 1e-9 ? m->dt : 1e-9;
     M.inv_dt_c = Cnt(1.0 / dtc);
     M.kstiff_c = Cnt(4.0 / (dtc * dtc));
-    M.im = ImpMat<Cnt>{M.ground_h, M.friction, M.dt, Cnt(0.0), Cnt(0.001), Cnt(0.0), Cnt(0.05),
+    // the impulse material of enable_contact_impulse (capi.cu rollout_args)
+    M.im = ImpMat<Cnt>{M.ground_h, M.friction, M.dt, Cnt(erp), Cnt(0.001), Cnt(0.0), Cnt(0.05),
                        Cnt(0.9),   Cnt(0.95),  Cnt(0.001), Cnt(0.5), Cnt(2.0)};
     impmat_finish(M.im);  // per-launch constants, outside the counted step
     // a 2 x 2 heightfield far below: terrain sampling is counted like
@@ -165,7 +182,18 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     static const float hf_nodes[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     M.ter = Terrain<Cnt>{hf_nodes, 2, 2, Cnt(-1.0), Cnt(-1.0), Cnt(-1e9), Cnt(1.0)};
     M.plane = PlaneT<Cnt>{-1, Cnt(0.0), Cnt(0.0), Cnt(0.0), Cnt(0.0)};  // plane contacts are not counted
+}
+}  // namespace
 
+FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps) {
+    g_kskip = false;
+    CountModel cm;
+    // Ground far below: contact detection is counted, the force law is not
+    // (a lower bound on the work of a contact step).
+    make_count_model(m, nv, cfg, -1e9, 1.0, 0.0, &cm);
+    const PackInfo& info = cm.info;
+    const ModelView<Cnt>& M = cm.M;
+    const int nb = m->nbodies, npd = (int)cfg.pd.size();
     std::vector<Cnt> scratch(info.scratch > 0 ? info.scratch : 1, Cnt(0.0));
     HostScr S{scratch.data()};
     // a generic state, away from the exp/log small-angle branches
@@ -224,6 +252,70 @@ FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int
     FlopCount fc;
     fc.flops = g_tally.flops;
     fc.transcendentals = g_tally.trans;
+    return fc;
+}
+
+FlopCount count_rollout(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps, double ground_h,
+                        double friction, double erp, const double* q, const double* v, const double* ctrl,
+                        long long nworld, int nsteps, bool specialized) {
+    CountModel cm;
+    make_count_model(m, nv, cfg, ground_h, friction, erp, &cm);
+    const ModelView<Cnt>& M = cm.M;
+    const int npd = (int)cfg.pd.size();
+    std::vector<Cnt> scratch(cm.info.scratch > 0 ? cm.info.scratch : 1, Cnt(0.0));
+    // one world's schedule [step][nv], its last row repeated for the
+    // prefetch of the step after the last
+    std::vector<Cnt> sched((size_t)(nsteps + 1) * (nv > 0 ? nv : 1), Cnt(0.0)), targets(npd > 0 ? npd : 1, Cnt(0.0));
+    g_kskip = specialized;
+    Tally total{};
+    for (long long w = 0; w < nworld; w++) {
+        std::fill(scratch.begin(), scratch.end(), Cnt(0.0));
+        for (int j = 0; j < nv; j++) {
+            scratch[j] = Cnt(q[w * nv + j]);
+            scratch[nv + j] = Cnt(v[w * nv + j]);
+        }
+        for (int s = 0; s <= nsteps; s++)
+            for (int j = 0; j < nv; j++) {
+                const int t = s < nsteps ? s : nsteps - 1;
+                sched[(size_t)s * nv + j] = Cnt(ctrl ? ctrl[((size_t)t * nworld + w) * nv + j] : 0.0);
+            }
+        const WorldIO<Cnt> io{sched.data(), nv, targets.data(), 1, 0};
+        HostScr S{scratch.data()};
+        // the relabelling of frames (FEAT_PERM) places the contact shapes
+        constexpr int ALL = FEAT_MULTI | FEAT_CONTACT | FEAT_PERM;
+        // the counted steps only: pass 1 of the launch's first step is not one
+        Tally base;
+        g_tally = Tally{};
+        if (cfg.contact && cfg.impulse) {
+            for (int i = 0; i < M.nb; i++) prefetch_controls<true>(M, M.bi[i], S, io, 0);
+            pass1_all<ALL | FEAT_IMPULSE>(M, S);
+            base = g_tally;
+            for (int s = 0; s < nsteps; s++) {
+                pass2<ALL | FEAT_IMPULSE>(M, S);
+                keep_backward_state(M, S);
+                for (int k = 0; k < sweeps; k++) {
+                    sweep_forward<ALL | FEAT_IMPULSE>(M, S);
+                    wrench_response<ALL | FEAT_IMPULSE>(M, S);
+                }
+                pass3_next<ALL | FEAT_IMPULSE, false>(M, S, io, s + 1, Out<Cnt>{nullptr, 0});
+            }
+        } else {
+            for (int i = 0; i < M.nb; i++) prefetch_controls<false>(M, M.bi[i], S, io, 0);
+            pass1_all<ALL>(M, S);
+            base = g_tally;
+            for (int s = 0; s < nsteps; s++) {
+                pass2<ALL>(M, S);
+                pass3_next<ALL, false>(M, S, io, s + 1, Out<Cnt>{nullptr, 0});
+            }
+        }
+        total.flops += g_tally.flops - base.flops;
+        total.trans += g_tally.trans - base.trans;
+    }
+    g_kskip = false;
+    const double n = (double)nworld * (double)nsteps;
+    FlopCount fc;
+    fc.flops = n > 0 ? total.flops / n : 0.0;
+    fc.transcendentals = n > 0 ? total.trans / n : 0.0;
     return fc;
 }
 

@@ -416,5 +416,13 @@ struct FlopCount {
 };
 // `sweeps`: contact sweeps per step when cfg.impulse.
 FlopCount count_world_step(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps = 0);
+// The flops a rollout executes per world-step, averaged over `nworld`
+// worlds (host rows q, v [nworld][nv]; ctrl [nsteps][nworld][nv] or null)
+// stepped `nsteps` steps on the flat ground at `ground_h` (the contact force
+// law counted where a body touches); `specialized`: products with zero
+// table constants left out as a model-specialized kernel leaves them out.
+FlopCount count_rollout(const phyzb_model* m, int nv, const PackCfg& cfg, int sweeps, double ground_h,
+                        double friction, double erp, const double* q, const double* v, const double* ctrl,
+                        long long nworld, int nsteps, bool specialized);
 
 }  // namespace pz

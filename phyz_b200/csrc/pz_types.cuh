@@ -119,7 +119,9 @@ PZ_HD V3<T> cross(const V3<T>& a, const V3<T>& b) {
 // add their terms conditionally; in the generic build every term is added.
 // Leaving a term out changes a result only in the sign of a zero or in NaN
 // propagation. PZ_KSKIP makes a host build take the same decisions at run
-// time (for checking them against the oracle).
+// time (for checking them against the oracle). The host flop counter's
+// scalar (Counting<T>) takes them at run time when its kskip_on() says so,
+// to count what a specialized kernel executes.
 #if defined(PZ_SPEC) || defined(PZ_KSKIP)
 #define PZ_KSKIP_ON 1
 #else
@@ -127,8 +129,12 @@ PZ_HD V3<T> cross(const V3<T>& a, const V3<T>& b) {
 #endif
 template <class T>
 PZ_HD bool kzero(const T& k) {
-    if constexpr (PZ_KSKIP_ON != 0 && !Counting<T>::value) return !(k > T(0) || k < T(0));
-    return false;
+    if constexpr (Counting<T>::value) {
+        return Counting<T>::kskip_on() && !(k > T(0) || k < T(0));
+    } else {
+        if constexpr (PZ_KSKIP_ON != 0) return !(k > T(0) || k < T(0));
+        return false;
+    }
 }
 // k x, or -0 when k is a zero table constant (a sum's first term)
 template <class T>
@@ -332,6 +338,8 @@ PZ_HD SV<T> kxm_apply_trans(const V3<T>& r, const SV<T>& m) {
 #if PZ_KSKIP_ON
     return mksv<T>(m.w, m.l + crossk(m.w, r));
 #else
+    if constexpr (Counting<T>::value)
+        if (Counting<T>::kskip_on()) return mksv<T>(m.w, m.l + crossk(m.w, r));
     return xm_apply_trans(r, m);
 #endif
 }
@@ -485,10 +493,7 @@ PZ_HD void ai_trans(const V3<T>& r, AI<T>& I) {
 // helpers: Ia' = Ia + Y + Y^T + V with Y = -(H r^x) (rows r x H_row) and
 // V = -(T1 r^x) (rows r x T1_row), so that a left-out term is a -0 added.
 template <class T>
-PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
-#if !PZ_KSKIP_ON
-    ai_trans(r, I);  // the generic build: the original expression order
-#else
+PZ_HD void kai_trans_skip(const V3<T>& r, AI<T>& I) {
     T t1[9];
 #pragma unroll
     for (int j = 0; j < 3; j++) {
@@ -513,6 +518,19 @@ PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
     }
 #pragma unroll
     for (int k = 0; k < 9; k++) I.h[k] = I.h[k] + t1[k];
+}
+template <class T>
+PZ_HD void kai_trans(const V3<T>& r, AI<T>& I) {
+#if PZ_KSKIP_ON
+    kai_trans_skip(r, I);
+#else
+    if constexpr (Counting<T>::value) {
+        if (Counting<T>::kskip_on()) {
+            kai_trans_skip(r, I);
+            return;
+        }
+    }
+    ai_trans(r, I);  // the generic build: the original expression order
 #endif
 }
 

@@ -48,9 +48,13 @@ struct SmemScr {
     int W;
 #endif
     __device__ __forceinline__ T& operator()(int s) const { return base[s * W]; }
+    // Queue an asynchronous copy of *g into slot s. The "memory" clobber keeps
+    // the compiler from moving a read of the slot's previous contents (the
+    // sweep's D^-1 u, read just before the next control is queued into the
+    // same slot) past the copy's issue, where the copy could land first.
     __device__ __forceinline__ void prefetch(int s, const T* g) const {
         const unsigned sa = (unsigned)__cvta_generic_to_shared(&base[s * W]);
-        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(sa), "l"(g), "n"(sizeof(T)));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(sa), "l"(g), "n"(sizeof(T)) : "memory");
     }
     __device__ __forceinline__ void commit() const { asm volatile("cp.async.commit_group;\n" ::); }
     __device__ __forceinline__ void wait() const { asm volatile("cp.async.wait_all;\n" ::: "memory"); }

@@ -179,15 +179,16 @@ def test_full_horizon_full_size(oracle, refhost, monkeypatch, name, precision, k
 @pytest.mark.parametrize("name", ["c2_chain32", "c3_quadruped"])
 @pytest.mark.parametrize("layout", ["0", "1"])
 def test_second_tiles_narrow_blocks(oracle, monkeypatch, name, layout):
-    """32-world blocks over 5000 worlds: more tiles than the grid's 148
-    blocks, so blocks walk to a second tile (and a Tensor-Memory block
-    reuses its columns for it). Worlds of first and second tiles match the
-    oracle over a 10-step schedule."""
+    """32-world blocks over 40000 worlds: more tiles than the grid's blocks
+    (one Tensor-Memory block or a few shared-memory blocks per SM), so blocks
+    walk to second and later tiles (and a Tensor-Memory block reuses its
+    columns for them). Worlds of first and later tiles match the oracle over
+    a 10-step schedule."""
     monkeypatch.setenv("PHYZB_WORLDS_PER_BLOCK", "32")
     monkeypatch.setenv("PHYZB_TMEM", layout)
     cfg = configs.CONFIGS[name]
     model = cfg.builder()
-    n, steps = 5000, 10
+    n, steps = 40000, 10
     q0, v0 = configs.initial_state(name, model, range(n))
     sched = configs.control_schedule(name, model, range(n), steps)
     sim = BatchSim(model, n, precision="f64")
@@ -202,8 +203,8 @@ def test_second_tiles_narrow_blocks(oracle, monkeypatch, name, layout):
     q, v = sim.readback_states()
     sim.close()
     G = info["blocks"]
-    ws = np.unique(np.concatenate([np.arange(0, 64), np.arange(G * 32, n),
-                                   np.random.default_rng(2).integers(64, G * 32, 64)]))
+    ws = np.unique(np.concatenate([np.arange(0, 64), np.arange(G * 32, G * 32 + 64), np.arange(n - 64, n),
+                                   np.random.default_rng(2).integers(64, n - 64, 64)]))
     qo, vo, _, _ = oracle.rollout(model, q0[ws], v0[ws], sched[:, ws], steps, schedule=True,
                                   contact=oracle_contact(cfg, model), nthreads=8)
     assert rel_err(q[ws], qo) <= 1e-9 and rel_err(v[ws], vo) <= 1e-9, (rel_err(q[ws], qo), rel_err(v[ws], vo))

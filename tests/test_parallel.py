@@ -100,7 +100,7 @@ def test_reference_arm_under_two_ranks(tmp_path):
     """`bench.py --impl reference` under a 2-rank launch: rank 0 times the
     reference's CPU path and prints one line; rank 1 exits 0 silently."""
     base = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--gpus", "2", "--steps", "1",
-            "--warmup", "0", "--nworld", "64", "--horizon", "8", "--cpu-seconds", "0.5"]
+            "--warmup", "0", "--nworld", "64", "--horizon", "8"]
     env = dict(os.environ, WORLD_SIZE="2", MASTER_ADDR="127.0.0.1", MASTER_PORT=str(_free_port()))
     r1 = subprocess.run(base, env=dict(env, RANK="1", LOCAL_RANK="1"), capture_output=True, text=True, timeout=300)
     assert r1.returncode == 0, r1.stderr
