@@ -481,7 +481,7 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     mask = torch.tensor(configs.actuated(model), dtype=tdt, device="cuda").view(1, nv, 1)
     with torch.cuda.stream(stream):
         sched = torch.randn(horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
-    stream.synchronize()
+    torch.cuda.synchronize()  # inputs written on torch's streams before the simulator's stream reads them
     objective = [0.0]
 
     def rollout(ev=None):

@@ -310,7 +310,12 @@ int phyzb_readback_state_history(phyzb_sim* sim, int32_t slot0, int32_t n, doubl
 int phyzb_device_view_get(phyzb_sim* sim, phyzb_device_view* out);
 /* Device-resident form of phyzb_load_states: q, v (and ctrl, NULL = keep)
  * are device arrays in the simulator's precision and SoA layout
- * ([nv][nworld]); copied on the simulator's stream, asynchronously. */
+ * ([nv][nworld]); copied on the simulator's stream, asynchronously.
+ * Device inputs of this and the calls below are read on the simulator's
+ * stream (its own non-blocking stream unless phyzb_set_stream named
+ * another): work that writes them on another stream must be ordered before
+ * the call (an event, a synchronize, or the same stream via
+ * phyzb_set_stream). */
 int phyzb_load_states_device(phyzb_sim* sim, const void* q, const void* v, const void* ctrl);
 /* Launch on a caller-provided stream (a cudaStream_t; NULL = the
  * simulator's own stream). */

@@ -75,6 +75,8 @@ class OnDevicePpo:
         self.v0 = torch.tensor(v0.T.copy(), dtype=tdt, device=f"cuda:{device}")
         self.adv = torch.zeros(T * N, dtype=torch.float32, device=f"cuda:{device}")
         self.ret = torch.zeros(T * N, dtype=torch.float32, device=f"cuda:{device}")
+        # written on torch's stream; the simulator and trainer use their own
+        torch.cuda.synchronize(device)
         self.coef = np.zeros(n_in)
         self.coef[24] = 1.0  # BodyPosZ(torso)
         self.iter = 0

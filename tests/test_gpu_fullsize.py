@@ -100,6 +100,9 @@ def device_run(name, precision, kernel, steps, monkeypatch):
     gen.manual_seed(configs.CTRL_SEED)
     mask = torch.tensor(configs.actuated(model), dtype=tdt, device="cuda").view(1, nv, 1)
     sched = torch.randn(steps, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
+    # the schedule is written on torch's stream and read on the simulator's
+    # own (non-blocking) stream: finish it first
+    torch.cuda.synchronize()
     sim.load_states(q0, v0)
     sim.step_device_controls(sched.data_ptr(), nv * nworld, steps)
     sim.sync()

@@ -253,6 +253,7 @@ def test_device_schedule_matches_host_schedule():
     sim.enable_ground_contact(*contact)
     sim.load_states(q0, v0)
     dev = torch.tensor(sched.transpose(0, 2, 1).copy(), dtype=torch.float32, device="cuda")  # [step][nv][nworld]
+    torch.cuda.synchronize()  # written on torch's stream, read on the simulator's
     sim.step_device_controls(dev.data_ptr(), 64 * model.nv, 10)
     sim.sync()
     qd, vd = sim.readback_states()
