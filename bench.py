@@ -221,12 +221,25 @@ def allreduce_max(x: float, world: int) -> float:
 L2_BYTES = 126 * 1024 * 1024  # B200 L2
 
 
+def held_controls(workload):
+    """Configs with zero control (C1) step under held zero controls: no
+    per-step control input exists to stream."""
+    from phyz_b200 import configs
+
+    return configs.CONFIGS[base_config(workload)[0]].ctrl_sigma == 0.0
+
+
 def schedule_bytes(model, nworld, horizon, prec):
     return horizon * model.nv * nworld * (4 if prec == "f32" else 8)
 
 
-def l2_rule(model, nworld, horizon, prec):
+def l2_rule(workload, model, nworld, horizon, prec):
     """(flush between rollouts?, the note for `config.l2`)."""
+    if held_controls(workload):
+        b = 4 * model.nv * nworld * (4 if prec == "f32" else 8)
+        return True, (f"zero controls held (no per-step input); inputs smaller than L2 ({b / 1e3:.0f} kB of "
+                      "state): a 256 MB buffer is written between timed rollouts (L2 flushed) and value counts "
+                      "the rollouts' own device time")
     b = schedule_bytes(model, nworld, horizon, prec)
     if b > L2_BYTES:
         return False, (f"inputs larger than L2: the per-step control schedule ({b / 1e9:.2f} GB) streams from HBM "
@@ -246,7 +259,7 @@ def bench_config(workload, model, nworld, horizon, prec, n_gpus, strong=False):
         contact = ("impulse, 16 sweeps per step" if impulse else
                    ("penalty, 64 x 64 heightfield" if workload in TERRAIN_WORKLOADS else "penalty"))
     out = {"workload": workload, "nbodies": model.nbodies, "nv": model.nv, "horizon": horizon, "precision": prec,
-           "contact": contact, "l2": l2_rule(model, nworld, horizon, prec)[1]}
+           "contact": contact, "l2": l2_rule(workload, model, nworld, horizon, prec)[1]}
     if strong:
         out["nworld_total"] = nworld
         out["parallelism"] = f"{nworld} worlds split over {n_gpus} GPU(s) (strong scaling)"
@@ -455,7 +468,8 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     tdt = torch.float32 if prec == "f32" else torch.float64
     esz = 4 if prec == "f32" else 8
     nv = model.nv
-    flush, l2_note = l2_rule(model, nworld, horizon, prec)
+    flush, l2_note = l2_rule(workload, model, nworld, horizon, prec)
+    held = held_controls(workload)
 
     sim = BatchSim(model, nworld, device=local, precision=prec)
     sim.specialize = {"auto": "auto", "0": False, "1": True}[specialize]
@@ -479,18 +493,24 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     gen = torch.Generator(device="cuda")
     gen.manual_seed(configs.CTRL_SEED + rank)
     mask = torch.tensor(configs.actuated(model), dtype=tdt, device="cuda").view(1, nv, 1)
+    c0_dev = torch.zeros(nv, nworld, dtype=tdt, device="cuda")
     with torch.cuda.stream(stream):
-        sched = torch.randn(horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (cfg.ctrl_sigma * mask)
+        sched = torch.randn(1 if held else horizon, nv, nworld, generator=gen, dtype=tdt, device="cuda") * (
+            cfg.ctrl_sigma * mask)
     torch.cuda.synchronize()  # inputs written on torch's streams before the simulator's stream reads them
     objective = [0.0]
 
     def rollout(ev=None):
         if ev is not None:
             ev[0].record(stream)
-        sim.load_states_device(q0_dev.data_ptr(), v0_dev.data_ptr())  # same start, same work each rollout
+        # same start, same work each rollout
+        sim.load_states_device(q0_dev.data_ptr(), v0_dev.data_ptr(), c0_dev.data_ptr() if held else None)
         if ev is not None:
             ev[1].record(stream)
-        sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
+        if held:
+            sim.step_many(horizon)
+        else:
+            sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
         if ev is not None:
             ev[2].record(stream)
         objective[0] = ctx.comm.reduce_objective(sim, 0)
@@ -537,7 +557,7 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     # generic formulation's steady-state count
     flops_gen, trans_ws = sim.flops_per_world_step()
     ns = min(16, nworld)
-    ctrl_s = sched[:, :, :ns].permute(0, 2, 1).double().cpu().numpy()
+    ctrl_s = (np.zeros((horizon, ns, nv)) if held else sched[:, :, :ns].permute(0, 2, 1).double().cpu().numpy())
     try:
         flops_ex, _ = sim.flops_executed(q0[:ns], v0[:ns], ctrl_s, specialized=sim.specialized)
     except L.PhyzbError:
@@ -579,7 +599,34 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     # that the rollout walks through (the full horizon for C2 f32 takes
     # three passes: 476 + 476 + 48 steps)
     e2e_out = None
-    if e2e:
+    if e2e and held:
+        q0_pin = torch.from_numpy(np.ascontiguousarray(q0, np.float64)).pin_memory().numpy()
+        v0_pin = torch.from_numpy(np.ascontiguousarray(v0, np.float64)).pin_memory().numpy()
+        c0_pin = torch.zeros((nworld, nv), dtype=torch.float64).pin_memory().numpy()
+        hq = torch.zeros((nworld, nv), dtype=torch.float64).pin_memory().numpy()
+        hv = torch.zeros((nworld, nv), dtype=torch.float64).pin_memory().numpy()
+
+        def e2e_held():
+            sim.load_states(q0_pin, v0_pin, c0_pin)
+            sim.step_many(horizon)
+            sim.readback_states(out=(hq, hv))
+
+        e2e_held()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.e2e_steps):
+            e2e_held()
+        e1.record(stream)
+        stream.synchronize()
+        barrier(world)
+        ems = allreduce_max(e0.elapsed_time(e1), world)
+        e2e_out = {"value": nworld * horizon * world * args.e2e_steps / (ems * 1e-3), "unit": "world-steps/s",
+                   "h2d_bytes_per_step": int(3 * nworld * nv * 8), "d2h_bytes_per_step": int(2 * nworld * nv * 8),
+                   "horizon": horizon, "path": "phyzb_load_states (zero controls held) + phyzb_step + "
+                                                "phyzb_readback_states, pinned host buffers"}
+    elif e2e:
         eh = min(args.e2e_horizon or horizon, horizon)
         ring = max(1, min(eh, (4 << 30) // (nworld * nv * esz)))
         host_ctrl = torch.empty((ring, nworld, nv), dtype=tdt, pin_memory=True)

@@ -57,6 +57,7 @@ template <class T>
 int repack_t(phyzb_sim* s) {
     // kernels already queued may read the tables: drain the stream first
     PZ_CUDA(cudaStreamSynchronize(s->stream));
+    pz::spec_release(s->spec);
     s->spec = nullptr;  // the tables change: specialize again at the next launch
     std::vector<unsigned char> blob;
     phyzb_sim::Layout& L0 = s->lay[0];
@@ -326,6 +327,7 @@ int prepare_spec(phyzb_sim* s) {
     PZ_TRY(upload_layout(s, s->spec_lay, *hosts[li]));
     s->spec_lay.launch = ch[pick].cfg;
     s->spec = ch[pick].k;
+    pz::spec_retain(s->spec);  // the candidates not picked may now be unloaded
     return PHYZB_OK;
 }
 
@@ -546,6 +548,8 @@ void destroy_sim(phyzb_sim* s) {
     destroy_policy(s);
     if (s->stream) cudaStreamSynchronize(s->stream);
     if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
+    pz::spec_release(s->spec);
+    s->spec = nullptr;
     free_ptr(s->q);
     free_ptr(s->v);
     free_ptr(s->ctrl);

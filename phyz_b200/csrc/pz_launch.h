@@ -111,6 +111,13 @@ cudaError_t spec_candidates(const SpecLayout* lays, int nlay, const RolloutArgs<
                             std::vector<SpecChoice>* out, std::string* err);
 template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
+// A simulator takes (retain) and gives back (release) the compiled kernel it
+// runs; modules no simulator holds are unloaded, least recently used first,
+// once more than kSpecModuleCap (or $PHYZB_SPEC_MODULE_CAP) are loaded (the
+// on-disk cache keeps them).
+constexpr int kSpecModuleCap = 32;
+void spec_retain(const SpecKernel* k);
+void spec_release(const SpecKernel* k);
 #endif  // __CUDACC_RTC__
 
 }  // namespace pz

@@ -41,6 +41,8 @@ struct SpecKernel {
     CUmodule mod = nullptr;
     CUfunction fn = nullptr;
     int static_smem = 0;
+    int users = 0;                 // simulators running it
+    unsigned long long stamp = 0;  // last lookup (least recently used goes first)
 };
 
 namespace {
@@ -114,6 +116,7 @@ struct Driver {
     decltype(&::cuFuncSetAttribute) set_attr = nullptr;
     decltype(&::cuOccupancyMaxActiveBlocksPerMultiprocessor) occupancy = nullptr;
     decltype(&::cuLaunchKernel) launch = nullptr;
+    decltype(&::cuModuleUnload) unload = nullptr;
     std::string error;
 };
 
@@ -135,7 +138,7 @@ Driver load_driver() {
     if (!entry("cuModuleLoadData", &d.load, &d.error) || !entry("cuModuleGetFunction", &d.get, &d.error) ||
         !entry("cuFuncGetAttribute", &d.attr, &d.error) || !entry("cuFuncSetAttribute", &d.set_attr, &d.error) ||
         !entry("cuOccupancyMaxActiveBlocksPerMultiprocessor", &d.occupancy, &d.error) ||
-        !entry("cuLaunchKernel", &d.launch, &d.error))
+        !entry("cuLaunchKernel", &d.launch, &d.error) || !entry("cuModuleUnload", &d.unload, &d.error))
         return d;
     return d;
 }
@@ -255,6 +258,37 @@ cudaError_t compile(const std::string& src, const std::string& name, const std::
 
 std::mutex g_mu;
 std::map<std::string, std::unique_ptr<SpecKernel>> g_kernels;  // key: device + source hash
+unsigned long long g_clock = 0;
+
+// Unload modules no simulator holds, oldest lookup first, until at most
+// kSpecModuleCap stay loaded (caller holds g_mu). A module's device is the
+// one current at its load; the key's prefix names it.
+int module_cap() {
+    static const int cap = [] {
+        const char* e = getenv("PHYZB_SPEC_MODULE_CAP");  // tests shrink it
+        const int v = e ? atoi(e) : 0;
+        return v > 0 ? v : kSpecModuleCap;
+    }();
+    return cap;
+}
+
+void trim_locked() {
+    const Driver& drv = driver();
+    while ((int)g_kernels.size() > module_cap()) {
+        auto victim = g_kernels.end();
+        for (auto it = g_kernels.begin(); it != g_kernels.end(); ++it)
+            if (it->second->users == 0 && (victim == g_kernels.end() || it->second->stamp < victim->second->stamp))
+                victim = it;
+        if (victim == g_kernels.end()) return;  // every loaded module is in use
+        int dev = 0, cur = 0;
+        dev = std::atoi(victim->first.c_str());
+        cudaGetDevice(&cur);
+        if (dev != cur) cudaSetDevice(dev);
+        if (drv.unload) drv.unload(victim->second->mod);
+        if (dev != cur) cudaSetDevice(cur);
+        g_kernels.erase(victim);
+    }
+}
 
 // The module of `src` on the current device: from this process's table,
 // else the disk cache, else a fresh compile.
@@ -302,6 +336,7 @@ cudaError_t get_kernel(const std::string& src, const std::string& name, SpecKern
     std::lock_guard<std::mutex> lock(g_mu);
     auto it = g_kernels.find(key);
     if (it != g_kernels.end()) {
+        it->second->stamp = ++g_clock;
         *out = it->second.get();
         return cudaSuccess;
     }
@@ -330,12 +365,28 @@ cudaError_t get_kernel(const std::string& src, const std::string& name, SpecKern
         *err = cu_error("cuFuncGetAttribute", r);
         return cudaErrorUnknown;
     }
+    k->stamp = ++g_clock;
     *out = k.get();
     g_kernels.emplace(key, std::move(k));
     return cudaSuccess;
 }
 
 }  // namespace
+
+void spec_retain(const SpecKernel* k) {
+    if (!k) return;
+    std::lock_guard<std::mutex> lock(g_mu);
+    const_cast<SpecKernel*>(k)->users++;
+    trim_locked();
+}
+
+void spec_release(const SpecKernel* k) {
+    if (!k) return;
+    std::lock_guard<std::mutex> lock(g_mu);
+    SpecKernel* m = const_cast<SpecKernel*>(k);
+    if (m->users > 0) m->users--;
+    trim_locked();
+}
 
 namespace {
 

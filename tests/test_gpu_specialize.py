@@ -146,3 +146,46 @@ def test_auto_mode_and_invalid_mode():
         with pytest.raises(PhyzbError):
             _lib.check(sim._lib.phyzb_set_kernel_specialization(sim._h, 7))
         sim.close()
+
+
+MODULE_CAP_SCRIPT = r"""
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+from phyz_b200 import BatchSim, configs
+name = "c3_quadruped"
+m = configs.CONFIGS[name].builder()
+n = 96
+q0, v0 = configs.initial_state(name, m, range(n))
+gen = BatchSim(m, n, precision="f32")
+sims = [BatchSim(m, n, precision="f32") for _ in range(2)]
+for s in sims:
+    s.specialize = True
+for s in [gen] + sims:
+    s.load_states(q0, v0)
+    s.step_many(5)  # no contact: one module each table
+    s.enable_ground_contact(0.0, 1e4, 100.0, 1.0)  # a table change: compile again, release the old module
+    s.step_many(30)
+sims[0].close()  # its module is now unused and may be unloaded
+for s in [gen, sims[1]]:
+    s.step_many(10)
+a, b = gen.readback_states(), sims[1].readback_states()
+for x, y in zip(a, b):
+    np.testing.assert_allclose(y, x, rtol=2e-4, atol=2e-4 * max(1.0, float(np.abs(x).max())))
+print("ok")
+"""
+
+
+def test_module_cache_unloads_unused_modules():
+    """With the cache capped at one loaded module, table changes and a closed
+    simulator unload the modules no simulator holds, and the simulator still
+    running its specialized kernel keeps stepping it correctly."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parents[1])
+    r = subprocess.run([sys.executable, "-c", MODULE_CAP_SCRIPT, root], capture_output=True, text=True, timeout=900,
+                       env=dict(os.environ, PHYZB_SPEC_MODULE_CAP="1"))
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]
