@@ -164,16 +164,36 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
     }
-    for (int rst = r0; rst < r1; rst += KS) {
-        for (int e = threadIdx.x; e < TM * KS; e += blockDim.x) {
+    // Software pipeline: the next stage's rows are loaded into registers
+    // while the current stage is multiplied out of shared memory (each
+    // thread loads TM * KS / 256 = 8 elements of each operand per stage).
+    constexpr int PER = TM * KS / 256;
+    float ra[PER], rb[PER];
+    auto load = [&](int rst) {
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int e = threadIdx.x + u * 256;
             const int mm = e / KS, kk = e % KS, r = rst + kk;
             const int m = m0 + mm, n = n0 + mm;
-            As[kk][mm] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
+            ra[u] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
             float bv = 0.0f;
             if (r < r1 && n < N) bv = gather ? col(x, idx ? (long long)idx[r] : r, n) : Bact[(long long)n * ldb + r];
-            Bs[kk][mm] = bv;
+            rb[u] = bv;
         }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int u = 0; u < PER; u++) {
+            const int e = threadIdx.x + u * 256;
+            As[e % KS][e / KS] = ra[u];
+            Bs[e % KS][e / KS] = rb[u];
+        }
+    };
+    if (r0 < r1) load(r0);
+    for (int rst = r0; rst < r1; rst += KS) {
+        store();
         __syncthreads();
+        if (rst + KS < r1) load(rst + KS);
         float fa[4][4] = {}, fr[4] = {};
 #pragma unroll 8
         for (int kk = 0; kk < KS; kk++) {
