@@ -119,6 +119,8 @@ def parse():
     ap.add_argument("--e2e-horizon", type=int, default=0, help="steps of the e2e rollout (0: the full horizon)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--lanes", type=int, default=0, choices=[0, 2, 4, 8],
+                    help="threads per world for branching trees (0: one thread per world)")
     ap.add_argument("--no-reference-gpu", action="store_true",
                     help="skip timing the reference's own CUDA kernels on this GPU")
     ap.add_argument("--per-config", type=int, default=1,
@@ -444,7 +446,7 @@ class Ctx:
 
 
 def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=False, e2e=False, cpu=False,
-            ref_gpu=False, specialize="auto"):
+            ref_gpu=False, specialize="auto", lanes=0):
     """One workload on this rank: `steps` timed rollouts after `warmup`.
     Returns the entry (rank 0's view; times are max over ranks)."""
     import torch
@@ -483,6 +485,8 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
         sim.enable_contact_terrain(g, mu, [BodyContactGains(k, d)] * model.nbodies, heightfield=hf)
     elif cfg.contact:
         sim.enable_ground_contact(*cfg.contact)
+    if lanes:
+        sim.world_lanes = lanes
     sim.set_stream(stream.cuda_stream)
 
     # inputs resident in HBM: initial state (SoA) and the per-step controls
@@ -695,8 +699,9 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
         "dtype": prec, "scaling": "strong" if strong else "weak",
         "config": bench_config(workload, model, total, horizon, prec, world, strong=strong),
         "launch": info,
-        "kernel": ("model-specialized (compiled at run time for this model)" if sim.specialized
-                   else "generic variant"),
+        "kernel": (f"one world over {lanes} lanes (all but the last step of a rollout)" if lanes and
+                   sim.lanes_active else ("model-specialized (compiled at run time for this model)"
+                                          if sim.specialized else "generic variant")),
         "timed_region_ms": region_ms,
         "roofline": roofline, "cpu_baseline": cpu_out, "e2e": e2e_out, "clocks": clk.summary(),
         "gpu_launches": steps * 2,  # per rollout: rollout_kernel + objective_kernel
@@ -726,7 +731,7 @@ def main():
     ctx = Ctx(args, world, rank, local)
     main_entry = measure(ctx, args.config, args.precision, args.nworld, args.horizon, args.steps, args.warmup,
                          e2e=not args.no_e2e, cpu=not args.no_cpu_baseline, ref_gpu=not args.no_reference_gpu,
-                         specialize=args.specialize)
+                         specialize=args.specialize, lanes=args.lanes)
     per_config = {}
     if args.per_config and args.config == "c2_chain32" and not args.nworld and not args.horizon:
         for wl, prec, total, strong in PER_CONFIG:

@@ -392,6 +392,8 @@ extern "C" {
                              smem_bytes: *mut i32, scratch_per_world: *mut i32, tmem_cols: *mut i32) -> c_int;
     pub fn phyzb_set_kernel_specialization(sim: *mut phyzb_sim, mode: i32) -> c_int;
     pub fn phyzb_get_kernel_specialization(sim: *const phyzb_sim, mode: *mut i32, active: *mut i32) -> c_int;
+    pub fn phyzb_set_world_lanes(sim: *mut phyzb_sim, lanes: i32) -> c_int;
+    pub fn phyzb_get_world_lanes(sim: *mut phyzb_sim, lanes: *mut i32, active: *mut i32) -> c_int;
 }
 
 /// The message of the calling thread's last failing call.
@@ -624,6 +626,10 @@ impl Simulator {
     /// PHYZB_SPECIALIZE_{OFF, ON, AUTO}.
     pub fn set_kernel_specialization(&mut self, mode: i32) -> Result<(), Error> {
         check(unsafe { phyzb_set_kernel_specialization(self.raw, mode) })
+    }
+    /// Threads per world for branching trees (2, 4, 8; 0: one thread).
+    pub fn set_world_lanes(&mut self, lanes: i32) -> Result<(), Error> {
+        check(unsafe { phyzb_set_world_lanes(self.raw, lanes) })
     }
 }
 

@@ -601,6 +601,28 @@ int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* 
 int phyzb_set_kernel_specialization(phyzb_sim* sim, int32_t mode);
 int phyzb_get_kernel_specialization(const phyzb_sim* sim, int32_t* mode, int32_t* active);
 
+/* One world over several threads: the north star's "one world per warp with
+ * per-body parallelism" for branching trees (no reference counterpart; the
+ * reference runs one thread per world, phyz_kernels.cu:1175-1369). `lanes`
+ * (2, 4, 8; 0 or 1: one thread per world) threads of a warp share a world:
+ * each steps the trunk (the bodies with two or more leaves below them) and
+ * its share of the limbs (the chains off the trunk), and the backward sweep
+ * sums the limbs' articulated inertias and bias forces over the lanes with
+ * warp shuffles before the trunk is swept. A world step then takes the
+ * trunk's time plus the longest share of limbs instead of every body in
+ * turn: for batches too small to fill the GPU with one thread per world,
+ * where per-world latency is the bound. Results equal the one-thread
+ * kernel's up to the order of those sums. PHYZB_ERR_UNSUPPORTED for a model
+ * that does not branch or settings the lanes kernel lacks (PD servos,
+ * impulse contact, heightfield / plane); such settings enabled later return
+ * the simulator to one thread per world. The last step of every launch runs
+ * on one thread per world (it writes qdd and contact state). $PHYZB_LANES
+ * sets a new simulator's lanes where its model splits. */
+int phyzb_set_world_lanes(phyzb_sim* sim, int32_t lanes);
+/* lanes as set; active = 1 when a launch of two or more steps runs the lanes
+ * kernel with the current settings (plans and packs the split if needed). */
+int phyzb_get_world_lanes(phyzb_sim* sim, int32_t* lanes, int32_t* active);
+
 #ifdef __cplusplus
 }
 #endif

@@ -448,6 +448,26 @@ class BatchSim:
         check(self._lib.phyzb_set_kernel_specialization(self._h, code))
 
     @property
+    def world_lanes(self) -> int:
+        """Threads per world (2, 4, 8; 0: one thread per world): for branching
+        trees, each lane steps the trunk and its share of the limbs and the
+        backward sweep sums the limbs' contributions over the lanes."""
+        n = C.c_int32()
+        check(self._lib.phyzb_get_world_lanes(self._h, C.byref(n), None))
+        return n.value
+
+    @world_lanes.setter
+    def world_lanes(self, lanes: int) -> None:
+        check(self._lib.phyzb_set_world_lanes(self._h, int(lanes)))
+
+    @property
+    def lanes_active(self) -> bool:
+        """Whether a launch of two or more steps runs the lanes kernel."""
+        n, a = C.c_int32(), C.c_int32()
+        check(self._lib.phyzb_get_world_lanes(self._h, C.byref(n), C.byref(a)))
+        return bool(a.value)
+
+    @property
     def specialized(self) -> bool:
         """Whether the next rollout launch runs the model-specialized kernel."""
         mode, active = C.c_int32(), C.c_int32()

@@ -20,6 +20,7 @@
 #include "../../include/phyzb.h"
 #include "capi_internal.h"
 #include "pz_launch.h"
+#include "pz_lanes.h"
 #include "pz_pack.h"
 
 namespace pzc {
@@ -59,6 +60,7 @@ int repack_t(phyzb_sim* s) {
     PZ_CUDA(cudaStreamSynchronize(s->stream));
     pz::spec_release(s->spec);
     s->spec = nullptr;  // the tables change: specialize again at the next launch
+    s->lanes_built = false;  // and split over lanes again
     std::vector<unsigned char> blob;
     phyzb_sim::Layout& L0 = s->lay[0];
     L0.info = pz::pack_model<T>(&s->model, s->nv, s->cfg, blob, 0);
@@ -331,8 +333,116 @@ int prepare_spec(phyzb_sim* s) {
     return PHYZB_OK;
 }
 
+// Why this simulator's settings keep one thread per world ("" when the
+// model may split over lanes).
+std::string lanes_unsupported(const phyzb_sim* s) {
+    if (!s->cfg.pd.empty()) return "PD servos are enabled";
+    if (s->cfg.contact && s->cfg.impulse) return "impulse contact is enabled";
+    if (s->cfg.contact && s->cfg.terrain) return "heightfield / plane contact is enabled";
+    return "";
+}
+
+// Plan and pack the lanes' sub-model tables (pz_lanes.h) and configure the
+// lanes kernel; on a model or settings that do not split, lanes_ok stays
+// false with the reason.
+template <class T>
+int build_lanes(phyzb_sim* s) {
+    s->lanes_built = true;
+    s->lanes_ok = false;
+    s->lanes_why = lanes_unsupported(s);
+    if (!s->lanes_why.empty()) return PHYZB_OK;
+    pz::LanePlan plan;
+    s->lanes_why = pz::plan_lanes(&s->model, s->lanes, &plan);
+    if (!s->lanes_why.empty()) return PHYZB_OK;
+    const int L = s->lanes;
+    std::vector<std::vector<unsigned char>> blobs(L);
+    std::vector<pz::PackInfo> infos(L);
+    int bytes = 0, scratch = 0, nv_max = 1, feat_or = 0;
+    bool perm1 = true;
+    pz::LanesArgs la{};
+    la.lanes = L;
+    la.nt = plan.nt;
+    la.trunk_nv = 0;
+    for (int t = 0; t < plan.nt; t++) la.trunk_nv += pz::ndof_of(plan.sub[0][t].joint_type);
+    for (int l = 0; l < L; l++) {
+        phyzb_model sub{};
+        sub.nbodies = (int)plan.sub[l].size();
+        for (int k = 0; k < 3; k++) sub.gravity[k] = s->model.gravity[k];
+        sub.dt = s->model.dt;
+        sub.bodies = plan.sub[l].data();
+        pz::PackCfg c = s->cfg;
+        c.gk.clear();
+        c.gd.clear();
+        for (int b : plan.bodies[l]) {
+            c.gk.push_back((int)s->cfg.gk.size() > b ? s->cfg.gk[b] : 0.0);
+            c.gd.push_back((int)s->cfg.gd.size() > b ? s->cfg.gd[b] : 0.0);
+        }
+        c.force_branch = plan.force_branch;
+        c.force_chain = plan.force_chain;
+        const int nv = (int)plan.dof[l].size();
+        infos[l] = pz::pack_model<T>(&sub, nv, c, blobs[l], 0);
+        bytes = std::max(bytes, infos[l].bytes);
+        scratch = std::max(scratch, infos[l].scratch);
+        nv_max = std::max(nv_max, nv);
+        feat_or |= infos[l].feat & ~8;
+        perm1 = perm1 && (infos[l].feat & 8) != 0;
+        la.nb[l] = sub.nbodies;
+        la.nv[l] = nv;
+        la.off_bi[l] = infos[l].off_bi;
+        la.off_pd[l] = infos[l].off_pd;
+        la.off_pdmap[l] = infos[l].off_pdmap;
+    }
+    const int feat = feat_or | ((perm1 && (feat_or & 4)) ? 8 : 0);
+    bytes = (bytes + 15) & ~15;
+    la.lane_bytes = bytes;
+    la.off_gdof = bytes * L;
+    la.nv_max = nv_max;
+    const int total = la.off_gdof + (((int)sizeof(int) * L * nv_max + 15) & ~15);
+    std::vector<unsigned char> host(total, 0);
+    for (int l = 0; l < L; l++) {
+        std::memcpy(host.data() + l * bytes, blobs[l].data(), blobs[l].size());
+        int* g = reinterpret_cast<int*>(host.data() + la.off_gdof) + l * nv_max;
+        for (int j = 0; j < (int)plan.dof[l].size(); j++) g[j] = plan.dof[l][j];
+    }
+    if ((size_t)total > s->lanes_cap) {
+        free_ptr(s->lanes_blob);
+        s->lanes_cap = 0;
+        PZ_CUDA(cudaMalloc(&s->lanes_blob, total));
+        s->lanes_cap = total;
+    }
+    PZ_CUDA(cudaMemcpy(s->lanes_blob, host.data(), total, cudaMemcpyHostToDevice));
+    cudaError_t e = pz::lanes_config<T>(feat, L, scratch, total, s->nworld, &s->lanes_launch);
+    if (e == cudaErrorInvalidConfiguration) {
+        cudaGetLastError();
+        s->lanes_why = "the sub-models' scratch does not fit shared memory";
+        return PHYZB_OK;
+    }
+    PZ_CUDA(e);
+    s->la = la;
+    s->lanes_bytes = total;
+    s->lanes_scratch = scratch;
+    s->lanes_feat = feat;
+    s->lanes_ok = true;
+    return PHYZB_OK;
+}
+
 template <class T>
 int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
+    if (s->lanes >= 2 && nsteps >= 2) {
+        if (!s->lanes_built) PZ_TRY(build_lanes<T>(s));
+        if (s->lanes_ok) {
+            // every step but the last on the lanes kernel; the last on the
+            // one-thread kernel, which writes its accelerations and contact state
+            pz::RolloutArgs<T> a = rollout_args<T>(s, s->lay[0], ctrl, stride, nsteps - 1);
+            a.model_blob = s->lanes_blob;
+            a.model_bytes = s->lanes_bytes;
+            a.feat = s->lanes_feat;
+            a.scratch = s->lanes_scratch;
+            PZ_CUDA(pz::launch_lanes<T>(a, s->la, s->lanes_launch, s->stream));
+            ctrl = (const char*)ctrl + (size_t)(nsteps - 1) * (size_t)stride * sizeof(T);
+            nsteps = 1;
+        }
+    }
     if (specialized(s)) {
         if (!s->spec) PZ_TRY(prepare_spec<T>(s));
         const pz::RolloutArgs<T> a = rollout_args<T>(s, s->spec_lay, ctrl, stride, nsteps);
@@ -550,6 +660,7 @@ void destroy_sim(phyzb_sim* s) {
     if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
     pz::spec_release(s->spec);
     s->spec = nullptr;
+    free_ptr(s->lanes_blob);
     free_ptr(s->q);
     free_ptr(s->v);
     free_ptr(s->ctrl);
@@ -626,6 +737,14 @@ int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int preci
     if (const char* env = getenv("PHYZB_SPECIALIZE"))
         s->specialize = env[0] == '1' ? PHYZB_SPECIALIZE_ON : (env[0] == 'a' ? PHYZB_SPECIALIZE_AUTO : PHYZB_SPECIALIZE_OFF);
     set_model_copy(s, model);
+    if (const char* env = getenv("PHYZB_LANES")) {
+        // a new simulator's lanes per world, where its model splits (the test
+        // suite runs with it to cover the lanes kernel everywhere it applies;
+        // settings that keep one thread per world are checked at each launch)
+        const int l = atoi(env);
+        pz::LanePlan plan;
+        if ((l == 2 || l == 4 || l == 8) && pz::plan_lanes(&s->model, l, &plan).empty()) s->lanes = l;
+    }
     auto bail = [&](int code) {
         destroy_sim(s);
         return code;
@@ -1048,6 +1167,37 @@ int phyzb_flops_executed(const phyzb_sim* s, const double* q, const double* v, c
                                                s->erp, q, v, ctrl, nworld, nsteps, specialized != 0);
     if (flops) *flops = fc.flops;
     if (transcendentals) *transcendentals = fc.transcendentals;
+    return PHYZB_OK;
+}
+
+int phyzb_set_world_lanes(phyzb_sim* s, int32_t lanes) {
+    PZ_TRY(check_sim(s));
+    if (lanes != 0 && lanes != 1 && lanes != 2 && lanes != 4 && lanes != 8)
+        return fail(PHYZB_ERR_INVALID, "lanes per world must be 0, 1, 2, 4 or 8, not " + std::to_string(lanes));
+    if (lanes >= 2) {
+        std::string why = lanes_unsupported(s);
+        if (why.empty()) {
+            pz::LanePlan plan;
+            why = pz::plan_lanes(&s->model, lanes, &plan);
+        }
+        if (!why.empty()) return fail(PHYZB_ERR_UNSUPPORTED, "cannot split a world over lanes: " + why);
+    }
+    s->lanes = lanes >= 2 ? lanes : 0;
+    s->lanes_built = false;
+    return PHYZB_OK;
+}
+
+int phyzb_get_world_lanes(phyzb_sim* s, int32_t* lanes, int32_t* active) {
+    PZ_TRY(check_sim(s));
+    if (lanes) *lanes = s->lanes;
+    if (active) {
+        *active = 0;
+        if (s->lanes >= 2) {
+            DeviceGuard g(s->device);
+            if (!s->lanes_built) PZ_TRY(is_f64(s) ? build_lanes<double>(s) : build_lanes<float>(s));
+            *active = s->lanes_ok ? 1 : 0;
+        }
+    }
     return PHYZB_OK;
 }
 

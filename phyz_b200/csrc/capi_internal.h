@@ -124,6 +124,18 @@ struct phyzb_sim {
     // PHYZB_SPECIALIZE_*: whether rollouts run the model-specialized kernel
     // (compiled at the first launch after each repack) or the generic variants
     int specialize = 0;
+    // one world over several threads (pz_lanes.h): requested lanes (0: off),
+    // and the packed sub-model tables (rebuilt at the first launch after a
+    // repack); lanes_ok false with lanes_why when the model or its settings
+    // keep one thread per world
+    int lanes = 0;
+    bool lanes_built = false, lanes_ok = false;
+    std::string lanes_why;
+    void* lanes_blob = nullptr;
+    size_t lanes_cap = 0;
+    int lanes_bytes = 0, lanes_scratch = 0, lanes_feat = 0;
+    pz::LanesArgs la{};
+    pz::LaunchCfg lanes_launch{};
     void* staging = nullptr;  // device, AoS f64 rows for host copies
     void* hist_q = nullptr;   // state history [slot][nv][nworld] (enable_state_history)
     void* hist_v = nullptr;

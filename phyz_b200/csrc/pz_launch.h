@@ -59,7 +59,26 @@ struct RolloutArgs {
     double plane_offset, plane_max_depth, plane_half_x, plane_half_y;
 };
 
+// The world split over lanes (stepper_lanes.cuh, planned by pz_lanes.h):
+// the staged blob holds `lanes` sub-model tables of lane_bytes each, then
+// the DOF maps.
+constexpr int LANES_MAX = 8;
+struct LanesArgs {
+    int lanes;                  // threads per world (2, 4, 8)
+    int nt;                     // trunk bodies: the first nt of every sub-model
+    int trunk_nv;               // DOFs of the trunk: the first trunk_nv of every sub-model
+    int lane_bytes;             // bytes of one lane's table in the staged blob
+    int off_gdof;               // blob offset of the DOF maps [lanes][nv_max]
+    int nv_max;
+    int nb[LANES_MAX], nv[LANES_MAX];
+    int off_bi[LANES_MAX], off_pd[LANES_MAX], off_pdmap[LANES_MAX];
+};
+
 #ifndef __CUDACC_RTC__
+template <class T>
+cudaError_t lanes_config(int feat, int lanes, int scratch, int model_bytes, long long nworld, LaunchCfg* out);
+template <class T>
+cudaError_t launch_lanes(const RolloutArgs<T>& a, const LanesArgs& la, const LaunchCfg& cfg, cudaStream_t s);
 // tmem_cols > 0: configure the Tensor-Memory variant for a layout whose
 // body records need tmem_cols columns per world.
 template <class T>

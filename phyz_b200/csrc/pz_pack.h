@@ -92,6 +92,11 @@ struct PackCfg {
     std::vector<int> plane_exclude;      // bodies that never touch the plane
     std::vector<double> gk, gd;          // per-body penalty gains (contact)
     std::vector<phyzb_pd_dof> pd;        // PD servos
+    // one lane's part of a model split over several threads per world
+    // (pz_lanes.h): bodies that keep branch slots whatever their children,
+    // and a body whose chain flag is set whatever its next body
+    std::vector<int> force_branch;
+    int force_chain = -1;
 };
 
 // A body whose per-step record [cos, sin, velocity | W] can live in Tensor
@@ -283,9 +288,12 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
             d.qshift = (shift[i] - (b.parent >= 0 ? shift[b.parent] : 0) + 3) % 3;
         }
         if (i + 1 < nb && m->bodies[i + 1].parent == i) flags |= F_CHAIN;
+        if (i == cfg.force_chain) flags |= F_CHAIN;
         if (nd > 1 && b.parent < 0) flags |= F_ROOTQDD;
         for (int j = i + 2; j < nb; j++)
             if (m->bodies[j].parent == i) flags |= F_BRANCH;
+        if (std::find(cfg.force_branch.begin(), cfg.force_branch.end(), i) != cfg.force_branch.end())
+            flags |= F_BRANCH;
         d.gtype = b.geom_type;
         if (b.geom_type != 0) info.collidable++;
 

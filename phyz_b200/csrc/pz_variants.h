@@ -92,6 +92,14 @@ cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, i
 template <class T, int FEAT, bool TM>
 cudaError_t config_variant(const DeviceLimits& dl, int scratch, int model_bytes, long long nworld, int tmem_cols,
                            LaunchCfg* out);
+// lanes kernel (stepper_lanes.cuh): feature sets of the ball / free, contact
+// and relabel bits only
+constexpr int LANES_FEAT_COUNT = 16;
+template <class T, int FEAT>
+cudaError_t config_lanes_variant(const DeviceLimits& dl, int lanes, int scratch, int model_bytes, long long nworld,
+                                 LaunchCfg* out);
+template <class T, int FEAT>
+void launch_lanes_variant(const RolloutArgs<T>& a, const LanesArgs& la, const LaunchCfg& cfg, cudaStream_t s);
 template <class T, int FEAT, bool TM>
 void launch_variant(const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
 template <class T, int FEAT>

@@ -51,7 +51,15 @@ namespace pz {
 // the velocity-level impulse solve instead of the penalty law, and with full
 // world frames carried (FEAT_TERRAIN): a heightfield in place of the flat
 // ground and/or a body-attached contact plane.
-enum Features { FEAT_MULTI = 1, FEAT_CONTACT = 2, FEAT_PERM = 4, FEAT_PERM1 = 8, FEAT_IMPULSE = 16, FEAT_TERRAIN = 32 };
+enum Features {
+    FEAT_MULTI = 1,
+    FEAT_CONTACT = 2,
+    FEAT_PERM = 4,
+    FEAT_PERM1 = 8,
+    FEAT_IMPULSE = 16,
+    FEAT_TERRAIN = 32,
+    FEAT_LANES = 64  // the world split over lanes (stepper_lanes.cuh): controls through a DOF map
+};
 
 // ── quaternions (w, x, y, z), crates/phyz-math/src/lib.rs:43-72 ───────────
 template <class T>
@@ -986,29 +994,34 @@ struct WorldIO {
     const T* targets;       // PD targets [npd][nworld]
     long long nworld;
     long long w;
+    const int* gdof = nullptr;  // FEAT_LANES: model DOF of each of the lane's DOFs
 };
 
-// Queue the control inputs of `step` for body i into its w0 slots.
-template <bool SEP, class T, class Scr>
+// Queue the control inputs of `step` for body i into its w0 slots. MAP: the
+// world is split over lanes (FEAT_LANES) and a lane's DOF d is the model's
+// DOF io.gdof[d] (PD servos do not occur there).
+template <bool SEP, class T, class Scr, bool MAP = false>
 PZ_HD void prefetch_controls(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
                              int step) {
     const int nd = bi.ndof;
     for (int k = 0; k < nd; k++) {
         const int d = bi.off + k;
         const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
+        const long long g = MAP ? (long long)io.gdof[d] : (long long)d;
         const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
-                                : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
+                                : io.ctrl + (long long)step * io.ctrl_stride + g * io.nworld + io.w;
         S.prefetch((SEP ? bi.s_in : bi.s_w0) + k, src);
     }
 }
 // One-DOF form for the relabelled-hinge path.
-template <bool SEP, class T, class Scr>
+template <bool SEP, class T, class Scr, bool MAP = false>
 PZ_HD void prefetch_control1(const ModelView<T>& M, const BodyI& bi, const Scr& S, const WorldIO<T>& io,
                              int step) {
     const int d = bi.off;
     const int pdi = (bi.flags & F_PD) ? M.pd_of_dof[d] : -1;
+    const long long g = MAP ? (long long)io.gdof[d] : (long long)d;
     const T* src = pdi >= 0 ? io.targets + (long long)pdi * io.nworld + io.w
-                            : io.ctrl + (long long)step * io.ctrl_stride + (long long)d * io.nworld + io.w;
+                            : io.ctrl + (long long)step * io.ctrl_stride + g * io.nworld + io.w;
     S.prefetch(SEP ? bi.s_in : bi.s_w0, src);
 }
 
@@ -1912,9 +1925,9 @@ PZ_HD void pass3_body(const ModelView<T>& M, const Scr& S, const WorldIO<T>& io,
     }
     if constexpr (!LAST) {
         if constexpr (AX >= 0)
-            prefetch_control1<(FEAT & FEAT_IMPULSE) != 0>(M, bi, S, io, next_step);
+            prefetch_control1<(FEAT & FEAT_IMPULSE) != 0, T, Scr, (FEAT & FEAT_LANES) != 0>(M, bi, S, io, next_step);
         else
-            prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, bi, S, io, next_step);
+            prefetch_controls<(FEAT & FEAT_IMPULSE) != 0, T, Scr, (FEAT & FEAT_LANES) != 0>(M, bi, S, io, next_step);
         pass1_body<AX, FEAT>(M, S, i, bi, cvn, cw);
     }
 }

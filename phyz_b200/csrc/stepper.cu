@@ -112,6 +112,47 @@ static cudaError_t objective_by_feat(const RolloutArgs<T>& a, const LaunchCfg& c
     }
 }
 
+template <class T, int F = 0>
+static cudaError_t lanes_config_by_feat(int feat, int lanes, int scratch, int model_bytes, long long nworld,
+                                        LaunchCfg* out) {
+    if constexpr (F < LANES_FEAT_COUNT) {
+        if constexpr (feat_valid(F))
+            if (feat == F) return config_lanes_variant<T, F>(g_limits, lanes, scratch, model_bytes, nworld, out);
+        return lanes_config_by_feat<T, F + 1>(feat, lanes, scratch, model_bytes, nworld, out);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+}
+template <class T, int F = 0>
+static cudaError_t launch_lanes_by_feat(const RolloutArgs<T>& a, const LanesArgs& la, const LaunchCfg& cfg,
+                                        cudaStream_t s) {
+    if constexpr (F < LANES_FEAT_COUNT) {
+        if constexpr (feat_valid(F))
+            if (a.feat == F) {
+                launch_lanes_variant<T, F>(a, la, cfg, s);
+                return cudaSuccess;
+            }
+        return launch_lanes_by_feat<T, F + 1>(a, la, cfg, s);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+}
+
+template <class T>
+cudaError_t lanes_config(int feat, int lanes, int scratch, int model_bytes, long long nworld, LaunchCfg* out) {
+    cudaError_t e = device_limits();
+    if (e != cudaSuccess) return e;
+    return lanes_config_by_feat<T>(feat, lanes, scratch, model_bytes, nworld, out);
+}
+
+template <class T>
+cudaError_t launch_lanes(const RolloutArgs<T>& a, const LanesArgs& la, const LaunchCfg& cfg, cudaStream_t s) {
+    if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
+    cudaError_t e = launch_lanes_by_feat<T>(a, la, cfg, s);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
 template <class T>
 cudaError_t rollout_config(int scratch, int model_bytes, long long nworld, int feat, int tmem_cols, LaunchCfg* out) {
     cudaError_t e = device_limits();
@@ -152,6 +193,11 @@ cudaError_t launch_soa_to_aos(const Tin* soa, Tout* aos, long long nworld, int w
     return cudaGetLastError();
 }
 
+template cudaError_t lanes_config<float>(int, int, int, int, long long, LaunchCfg*);
+template cudaError_t lanes_config<double>(int, int, int, int, long long, LaunchCfg*);
+template cudaError_t launch_lanes<float>(const RolloutArgs<float>&, const LanesArgs&, const LaunchCfg&, cudaStream_t);
+template cudaError_t launch_lanes<double>(const RolloutArgs<double>&, const LanesArgs&, const LaunchCfg&,
+                                          cudaStream_t);
 template cudaError_t rollout_config<float>(int, int, long long, int, int, LaunchCfg*);
 template cudaError_t rollout_config<double>(int, int, long long, int, int, LaunchCfg*);
 template cudaError_t launch_rollout<float>(const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
