@@ -10,6 +10,7 @@
 // fixed order, so results are deterministic run to run.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "pz_mlp.cuh"
@@ -142,20 +143,43 @@ __global__ void __launch_bounds__(ROW_BLOCK) bwd_kernel(const NetDev n, int b) {
 // Split-K partial sums part[split][m][n] = sum over the split's rows of
 // A[m][r] * Bv(r, n) for n < N, and part[split][m][N] = sum A[m][r] (the
 // bias column). A is SoA [M][lda]; Bv is SoA activations [N][ldb] or, with
-// gather, batch column x at sample idx[r]. 64 x 64 output tile per block,
-// 4 x 4 per thread; each 32-row stage accumulates in f32 registers and is
-// added into f64 accumulators (the reference accumulates in f64).
-constexpr int TM = 64, TN = 64, KS = 32;
+// gather, batch column x at sample idx[r]. A block's output tile is TM x TN,
+// shaped to the layer (64, 16 or 4 rows; 64, 32 or 4 columns), 4 x 4 per
+// thread; the 256 threads that the tile leaves over split each KS-row stage
+// into KG interleaved row groups, whose partials are added in group order
+// before the split is written (the reduction kernel then sums the splits in
+// a fixed order). Each stage
+// accumulates in f32 registers and is added into f64 accumulators (the
+// reference accumulates in f64); the next stage's rows are loaded into
+// registers while the current one is multiplied.
+template <int TM, int TN>
+struct GradShape {
+    static constexpr int TY = TM / 4, TX = TN / 4;
+    static constexpr int KG = 256 / (TY * TX);  // row groups per stage
+    // rows per stage: at least 32, two per row group, and enough that each
+    // operand's stage is a whole number of elements per thread
+    static constexpr int cmax(int a, int b) { return a > b ? a : b; }
+    static constexpr int KS = cmax(cmax(32, 2 * KG), cmax(256 / TM, 256 / TN));
+    static constexpr int PA = TM * KS / 256, PB = TN * KS / 256;  // elements each thread loads
+};
 
+template <int TM, int TN>
 __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int M, const float* Bact, int ldb,
                                                    BatchCol x, const uint32_t* idx, int gather, int N, int b,
                                                    int kc, double* part) {
-    __shared__ __align__(16) float As[KS][TM + 4];
-    __shared__ __align__(16) float Bs[KS][TN + 4];
+    using G = GradShape<TM, TN>;
+    constexpr int KS = G::KS, KG = G::KG;
+    // the stage operands, and after the last stage the row groups' partials
+    constexpr int ABYTES = KS * (TM + 4) * 4, BBYTES = KS * (TN + 4) * 4, RBYTES = 256 * 20 * 8;
+    constexpr int SBYTES = ABYTES + BBYTES > RBYTES ? ABYTES + BBYTES : RBYTES;
+    __shared__ __align__(16) unsigned char sbuf[SBYTES];
+    float(*As)[TM + 4] = reinterpret_cast<float(*)[TM + 4]>(sbuf);
+    float(*Bs)[TN + 4] = reinterpret_cast<float(*)[TN + 4]>(sbuf + ABYTES);
     const int m0 = blockIdx.x * TM, n0 = blockIdx.y * TN, split = blockIdx.z;
     const int r0 = split * kc;
     const int r1 = min(b, r0 + kc);
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int kg = threadIdx.x / (G::TY * G::TX), tt = threadIdx.x % (G::TY * G::TX);
+    const int tx = tt % G::TX, ty = tt / G::TX;
     const bool bias_col = blockIdx.y == 0 && tx == 0;
     double acc[4][4], rs[4];
 #pragma unroll
@@ -164,18 +188,18 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[i][j] = 0.0;
     }
-    // Software pipeline: the next stage's rows are loaded into registers
-    // while the current stage is multiplied out of shared memory (each
-    // thread loads TM * KS / 256 = 8 elements of each operand per stage).
-    constexpr int PER = TM * KS / 256;
-    float ra[PER], rb[PER];
+    float ra[G::PA], rb[G::PB];
     auto load = [&](int rst) {
 #pragma unroll
-        for (int u = 0; u < PER; u++) {
+        for (int u = 0; u < G::PA; u++) {
             const int e = threadIdx.x + u * 256;
-            const int mm = e / KS, kk = e % KS, r = rst + kk;
-            const int m = m0 + mm, n = n0 + mm;
+            const int mm = e / KS, kk = e % KS, r = rst + kk, m = m0 + mm;
             ra[u] = (m < M && r < r1) ? A[(long long)m * lda + r] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < G::PB; u++) {
+            const int e = threadIdx.x + u * 256;
+            const int nn = e / KS, kk = e % KS, r = rst + kk, n = n0 + nn;
             float bv = 0.0f;
             if (r < r1 && n < N) bv = gather ? col(x, idx ? (long long)idx[r] : r, n) : Bact[(long long)n * ldb + r];
             rb[u] = bv;
@@ -183,9 +207,13 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
     };
     auto store = [&]() {
 #pragma unroll
-        for (int u = 0; u < PER; u++) {
+        for (int u = 0; u < G::PA; u++) {
             const int e = threadIdx.x + u * 256;
             As[e % KS][e / KS] = ra[u];
+        }
+#pragma unroll
+        for (int u = 0; u < G::PB; u++) {
+            const int e = threadIdx.x + u * 256;
             Bs[e % KS][e / KS] = rb[u];
         }
     };
@@ -195,8 +223,8 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
         __syncthreads();
         if (rst + KS < r1) load(rst + KS);
         float fa[4][4] = {}, fr[4] = {};
-#pragma unroll 8
-        for (int kk = 0; kk < KS; kk++) {
+#pragma unroll 4
+        for (int kk = kg; kk < KS; kk += KG) {
             const float4 a4 = *reinterpret_cast<const float4*>(&As[kk][4 * ty]);
             const float4 b4 = *reinterpret_cast<const float4*>(&Bs[kk][4 * tx]);
             const float av[4] = {a4.x, a4.y, a4.z, a4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
@@ -214,6 +242,29 @@ __global__ void __launch_bounds__(256) grad_kernel(const float* A, int lda, int 
             for (int j = 0; j < 4; j++) acc[i][j] += (double)fa[i][j];
         }
         __syncthreads();
+    }
+    if constexpr (KG > 1) {
+        // the row groups' partials added in group order by group 0
+        constexpr int TT = G::TY * G::TX;
+        double* red = reinterpret_cast<double*>(sbuf);
+        if (kg > 0) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                red[(kg * TT + tt) * 20 + 16 + i] = rs[i];
+#pragma unroll
+                for (int j = 0; j < 4; j++) red[(kg * TT + tt) * 20 + 4 * i + j] = acc[i][j];
+            }
+        }
+        __syncthreads();
+        if (kg > 0) return;
+        for (int q = 1; q < KG; q++) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                rs[i] += red[(q * TT + tt) * 20 + 16 + i];
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] += red[(q * TT + tt) * 20 + 4 * i + j];
+            }
+        }
     }
     const int N1 = N + 1;
 #pragma unroll
@@ -303,24 +354,39 @@ cudaError_t row_block(int packed, int per_row, int* W_out, int* smem_out) {
 }
 
 // Rows per split: enough splits for about two blocks per SM over the
-// output tiles, no split shorter than GKC_MIN rows (a multiple of KS).
-int split_rows(int M, int N, int b) {
-    const int tiles = ((M + TM - 1) / TM) * (N > 0 ? (N + TN - 1) / TN : 1);
+// output tiles, no split shorter than GKC_MIN rows, a whole number of stages.
+int split_rows(int tiles, int ks, int b) {
     const int want = (2 * 148 + tiles - 1) / tiles;
     int rows = (b + want - 1) / want;
-    rows = (rows + KS - 1) / KS * KS;
-    return rows < GKC_MIN ? GKC_MIN : rows;
+    rows = rows < GKC_MIN ? GKC_MIN : rows;
+    return (rows + ks - 1) / ks * ks;
 }
 
-cudaError_t grad(const float* A, int lda, int M, const float* Bact, int ldb, BatchCol x, const uint32_t* idx,
-                 int gather, int N, int b, float* g, int off_w, int off_b, double* work, cudaStream_t s) {
-    const int kc = split_rows(M, N, b);
+template <int TM, int TN>
+cudaError_t grad_shaped(const float* A, int lda, int M, const float* Bact, int ldb, BatchCol x, const uint32_t* idx,
+                        int gather, int N, int b, float* g, int off_w, int off_b, double* work, cudaStream_t s) {
+    using G = GradShape<TM, TN>;
+    const int tiles = ((M + TM - 1) / TM) * (N > 0 ? (N + TN - 1) / TN : 1);
+    const int kc = split_rows(tiles, G::KS, b);
     const int nsplit = (b + kc - 1) / kc;
     dim3 grid((unsigned)((M + TM - 1) / TM), (unsigned)(N > 0 ? (N + TN - 1) / TN : 1), (unsigned)nsplit);
-    grad_kernel<<<grid, 256, 0, s>>>(A, lda, M, Bact, ldb, x, idx, gather, N, b, kc, work);
+    grad_kernel<TM, TN><<<grid, 256, 0, s>>>(A, lda, M, Bact, ldb, x, idx, gather, N, b, kc, work);
     const long long lanes = (long long)M * (N + 1) * 8;
     grad_reduce_kernel<<<(unsigned)((lanes + 255) / 256), 256, 0, s>>>(work, nsplit, M, N, g, off_w, off_b);
     return cudaGetLastError();
+}
+
+// The tile shape of a layer: 64, 16 or 4 output rows; 64, 32 or 4 columns.
+cudaError_t grad(const float* A, int lda, int M, const float* Bact, int ldb, BatchCol x, const uint32_t* idx,
+                 int gather, int N, int b, float* g, int off_w, int off_b, double* work, cudaStream_t s) {
+    const int rm = M > 16 ? 64 : (M > 4 ? 16 : 4), cn = N > 32 ? 64 : (N > 4 ? 32 : 4);
+#define PZ_GRAD(TM_, TN_)                                                                                        \
+    if (rm == TM_ && cn == TN_) return grad_shaped<TM_, TN_>(A, lda, M, Bact, ldb, x, idx, gather, N, b, g, off_w, \
+                                                             off_b, work, s);
+    PZ_GRAD(64, 64) PZ_GRAD(64, 32) PZ_GRAD(64, 4) PZ_GRAD(16, 64) PZ_GRAD(16, 32) PZ_GRAD(16, 4)
+    PZ_GRAD(4, 64) PZ_GRAD(4, 32) PZ_GRAD(4, 4)
+#undef PZ_GRAD
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace
