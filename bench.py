@@ -503,8 +503,9 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
             cfg.ctrl_sigma * mask)
     torch.cuda.synchronize()  # inputs written on torch's streams before the simulator's stream reads them
     objective = [0.0]
+    obj_dev = torch.zeros(max(steps, 1), dtype=tdt, device="cuda")
 
-    def rollout(ev=None):
+    def rollout(ev=None, k=None):
         if ev is not None:
             ev[0].record(stream)
         # same start, same work each rollout
@@ -517,7 +518,11 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
             sim.step_device_controls(sched.data_ptr(), nv * nworld, horizon)
         if ev is not None:
             ev[2].record(stream)
-        objective[0] = ctx.comm.reduce_objective(sim, 0)
+        if k is None:
+            objective[0] = ctx.comm.reduce_objective(sim, 0)
+        else:
+            # enqueued into a device scalar; one bounded wait after the loop
+            ctx.comm.reduce_objective_device(sim, obj_dev[k].data_ptr(), 0)
         if ev is not None:
             ev[3].record(stream)
 
@@ -535,11 +540,13 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
     with ClockSampler(local) as clk:
         t0.record(stream)
         for k in range(steps):
-            rollout(ev[k])
+            rollout(ev[k], k)
             if flush:
                 ctx.flush_l2()
         t1.record(stream)
+        ctx.comm.sync(sim)
         stream.synchronize()
+    objective[0] = float(obj_dev[steps - 1].item())
     barrier(world)
     torch.cuda.synchronize()
     sim.sync()  # raises if any world went non-finite

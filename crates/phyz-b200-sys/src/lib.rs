@@ -382,6 +382,9 @@ extern "C" {
     pub fn phyzb_comm_destroy(comm: *mut phyzb_comm) -> c_int;
     pub fn phyzb_reduce_objective(sim: *mut phyzb_sim, comm: *mut phyzb_comm, kind: c_int, timeout_s: f64,
                                   out: *mut f64) -> c_int;
+    pub fn phyzb_reduce_objective_device(sim: *mut phyzb_sim, comm: *mut phyzb_comm, kind: c_int,
+                                         out_device_scalar: *mut c_void) -> c_int;
+    pub fn phyzb_comm_sync(comm: *mut phyzb_comm, sim: *mut phyzb_sim, timeout_s: f64) -> c_int;
 
     // measurement and kernel selection
     pub fn phyzb_flops_per_world_step(sim: *const phyzb_sim, flops: *mut f64, transcendentals: *mut f64) -> c_int;

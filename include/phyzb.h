@@ -534,6 +534,17 @@ int phyzb_comm_destroy(phyzb_comm* comm);
  * part makes the others return PHYZB_ERR_COMM after timeout_s seconds; the
  * communicator is then aborted and must be rebuilt. */
 int phyzb_reduce_objective(phyzb_sim* sim, phyzb_comm* comm, int kind, double timeout_s, double* out);
+/* The same reduction enqueued on the simulator's stream into a device
+ * scalar (the simulator's precision), without waiting: a caller closing
+ * many rollouts keeps the host from stalling on each one and reads the
+ * scalars after one bounded wait (phyzb_comm_sync). A failing or stalled
+ * collective is reported by that wait (the communicator is then aborted).
+ * No reference counterpart. */
+int phyzb_reduce_objective_device(phyzb_sim* sim, phyzb_comm* comm, int kind, void* out_device_scalar);
+/* Wait, at most timeout_s, for everything enqueued on the simulator's
+ * stream, watching the communicator for errors (PHYZB_ERR_COMM on failure
+ * or timeout, the communicator aborted). */
+int phyzb_comm_sync(phyzb_comm* comm, phyzb_sim* sim, double timeout_s);
 
 /* ── measurement helpers (no reference counterpart) ───────────────────── */
 

@@ -202,6 +202,8 @@ SIGNATURES = {
     "phyzb_flops_per_world_step": (C.c_int, [_P, _D, _D]),
     "phyzb_flops_executed": (C.c_int, [_P, _D, _D, _D, C.c_int64, C.c_int32, C.c_int32, _D, _D]),
     "phyzb_set_world_lanes": (C.c_int, [_P, C.c_int32]),
+    "phyzb_reduce_objective_device": (C.c_int, [_P, _P, C.c_int, _P]),
+    "phyzb_comm_sync": (C.c_int, [_P, _P, C.c_double]),
     "phyzb_get_world_lanes": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
     "phyzb_set_kernel_specialization": (C.c_int, [_P, C.c_int32]),

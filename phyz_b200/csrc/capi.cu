@@ -1446,6 +1446,33 @@ int phyzb_comm_destroy(phyzb_comm* c) {
     return PHYZB_OK;
 }
 
+int phyzb_reduce_objective_device(phyzb_sim* s, phyzb_comm* c, int kind, void* out) {
+    PZ_TRY(check_sim(s));
+    if (!c || !out) return fail(PHYZB_ERR_INVALID, "communicator or output is null");
+    if (c->broken) return fail(PHYZB_ERR_COMM, "communicator was aborted by an earlier failure");
+    if (c->device != s->device) return fail(PHYZB_ERR_INVALID, "communicator and simulator are on different devices");
+    NcclApi& n = nccl();
+    DeviceGuard g(s->device);
+    PZ_CUDA(cudaMemsetAsync(out, 0, s->esz(), s->stream));
+    PZ_TRY(phyzb_objective_device(s, kind, out));
+    const ncclResult_t r = n.AllReduce(out, out, 1, is_f64(s) ? ncclFloat64 : ncclFloat32, ncclSum, c->comm, s->stream);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        n.CommAbort(c->comm);
+        c->broken = true;
+        return fail(PHYZB_ERR_COMM, "ncclAllReduce: " + nccl_msg(r));
+    }
+    return comm_settle(c, 60.0, "objective all-reduce (enqueue)");
+}
+
+int phyzb_comm_sync(phyzb_comm* c, phyzb_sim* s, double timeout_s) {
+    PZ_TRY(check_sim(s));
+    if (!c) return fail(PHYZB_ERR_INVALID, "communicator is null");
+    if (c->broken) return fail(PHYZB_ERR_COMM, "communicator was aborted by an earlier failure");
+    if (!(timeout_s > 0.0)) return fail(PHYZB_ERR_INVALID, "timeout must be > 0");
+    DeviceGuard g(s->device);
+    return comm_wait(c, s->stream, timeout_s);
+}
+
 int phyzb_reduce_objective(phyzb_sim* s, phyzb_comm* c, int kind, double timeout_s, double* out) {
     PZ_TRY(check_sim(s));
     if (!c || !out) return fail(PHYZB_ERR_INVALID, "communicator or output is null");

@@ -72,6 +72,15 @@ class Comm:
                                                float(timeout or self.timeout), C.byref(out)))
         return out.value
 
+    def reduce_objective_device(self, sim, out_ptr: int, kind: int = 0) -> None:
+        """Enqueue the reduction into a device scalar without waiting (read it
+        after sync)."""
+        check(self._lib.phyzb_reduce_objective_device(sim._h, self._h, int(kind), C.c_void_p(int(out_ptr))))
+
+    def sync(self, sim, timeout: Optional[float] = None) -> None:
+        """Bounded wait for everything enqueued on sim's stream."""
+        check(self._lib.phyzb_comm_sync(self._h, sim._h, float(timeout or self.timeout)))
+
     def close(self) -> None:
         if getattr(self, "_h", None):
             self._lib.phyzb_comm_destroy(self._h)

@@ -39,6 +39,13 @@ def test_reduce_objective_single_rank(oracle):
         total = comm.reduce_objective(sim, 0)
         total_again = comm.reduce_objective(sim, 0)
         sq = comm.reduce_objective(sim, 1)
+        # enqueued without waiting, read after one bounded wait
+        dev = torch.full((2,), -1.0, dtype=torch.float64, device="cuda")
+        torch.cuda.synchronize()
+        comm.reduce_objective_device(sim, dev[0].data_ptr(), 0)
+        comm.reduce_objective_device(sim, dev[1].data_ptr(), 1)
+        comm.sync(sim)
+        total_dev, sq_dev = (float(x) for x in dev.cpu())
     out = torch.zeros(1, dtype=torch.float64, device="cuda")
     sim.objective_device(0, out.data_ptr())
     torch.cuda.synchronize()
@@ -47,6 +54,7 @@ def test_reduce_objective_single_rank(oracle):
     # the per-warp partial sums are added atomically (order varies by run)
     assert abs(total - total_again) <= 1e-12 * total and abs(total - out.item()) <= 1e-12 * total
     assert abs(sq - np.sum(q * q)) <= 1e-10 * np.sum(q * q)
+    assert abs(total_dev - total) <= 1e-12 * total and abs(sq_dev - sq) <= 1e-12 * sq
     sim.close()
 
 
