@@ -17,7 +17,11 @@
  *   - nothing here allocates except phyzb_create / phyzb_enable_* (device
  *     buffers) and the staging used by the *_host bulk copies;
  *   - no call ever traps the GPU: device-side failures (non-finite state)
- *     are recorded in a status word that phyzb_status() reads.
+ *     are recorded in a status word that phyzb_status() reads;
+ *   - every wait on the device is bounded: stream waits give up after
+ *     $PHYZB_SYNC_TIMEOUT seconds (default 600; the kernels hold no spin)
+ *     with PHYZB_ERR_CUDA, collectives after the caller's timeout with
+ *     PHYZB_ERR_COMM.
  *
  * Joint, geometry and DOF conventions are phyz's:
  *   - joint types use the packed-body-table codes of layout.rs:23;

@@ -33,6 +33,26 @@ int fail(int code, const std::string& msg) {
 }
 const char* last_error() { return g_err.c_str(); }
 
+int bounded_sync(cudaStream_t stream) {
+    static const double limit = [] {
+        const char* e = getenv("PHYZB_SYNC_TIMEOUT");
+        const double v = e ? atof(e) : 0.0;
+        return v > 0.0 ? v : 600.0;
+    }();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (long k = 0;; k++) {
+        const cudaError_t q = cudaStreamQuery(stream);
+        if (q == cudaSuccess) return PHYZB_OK;
+        if (q != cudaErrorNotReady)
+            return fail(PHYZB_ERR_CUDA, std::string("stream wait: ") + cudaGetErrorString(q));
+        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (waited > limit)
+            return fail(PHYZB_ERR_CUDA, "stream wait: nothing finished within " + std::to_string(limit) + " s");
+        // poll for the first millisecond, then back off
+        if (waited > 1e-3) std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
 }  // namespace pzc
 
 using namespace pzc;
@@ -57,7 +77,7 @@ int upload_layout(phyzb_sim* s, phyzb_sim::Layout& L, const std::vector<unsigned
 template <class T>
 int repack_t(phyzb_sim* s) {
     // kernels already queued may read the tables: drain the stream first
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     pz::spec_release(s->spec);
     s->spec = nullptr;  // the tables change: specialize again at the next launch
     s->lanes_built = false;  // and split over lanes again
@@ -274,7 +294,7 @@ int time_spec_choices(phyzb_sim* s, const std::vector<pz::PackInfo>& infos,
             *best = c;
         }
     }
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     if (best_ms < 0.0f) return fail(PHYZB_ERR_CUDA, "no specialized kernel candidate launched");
     return PHYZB_OK;
 }
@@ -470,7 +490,7 @@ int upload_rows(phyzb_sim* s, const double* host, int width, void* dst) {
                                                                      s->nworld, width, 1, s->stream);
     PZ_CUDA(e);
     // the caller may reuse `host` as soon as this returns
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -484,7 +504,7 @@ int download_rows(phyzb_sim* s, const void* src, int width, double* host) {
                                                                      s->nworld, width, s->stream);
     PZ_CUDA(e);
     PZ_CUDA(cudaMemcpyAsync(host, s->staging, bytes, cudaMemcpyDeviceToHost, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -501,7 +521,7 @@ int check_sim(const phyzb_sim* s) {
 int read_status(phyzb_sim* s) {
     int st[2] = {0, 0};
     PZ_CUDA(cudaMemcpyAsync(st, s->status, sizeof(st), cudaMemcpyDeviceToHost, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     if (st[0] & 1)
         return fail(PHYZB_ERR_NONFINITE, "state went non-finite on device (first world " + std::to_string(st[1]) + ")");
     return PHYZB_OK;
@@ -545,7 +565,7 @@ int check_heightfield(const phyzb_heightfield* hf) {
 // Heightfield nodes into the device buffer (already large enough) and the
 // grid header into the simulator; kernels already queued finish first.
 int upload_heightfield(phyzb_sim* s, const phyzb_heightfield* hf) {
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     PZ_CUDA(cudaMemcpy(s->hf, hf->heights, (size_t)hf->nx * hf->ny * sizeof(float), cudaMemcpyHostToDevice));
     s->hf_nx = hf->nx;
     s->hf_ny = hf->ny;
@@ -656,8 +676,8 @@ void destroy_sim(phyzb_sim* s) {
     if (!s) return;
     DeviceGuard g(s->device);
     destroy_policy(s);
-    if (s->stream) cudaStreamSynchronize(s->stream);
-    if (s->copy_stream) cudaStreamSynchronize(s->copy_stream);
+    if (s->stream) bounded_sync(s->stream);
+    if (s->copy_stream) bounded_sync(s->copy_stream);
     pz::spec_release(s->spec);
     s->spec = nullptr;
     free_ptr(s->lanes_blob);
@@ -773,7 +793,7 @@ int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int preci
         destroy_sim(s);
         return fail(r, msg);
     }
-    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "init sync failed"));
+    if (bounded_sync(s->stream) != PHYZB_OK) return bail(PHYZB_ERR_CUDA);
     *out = s;
     return PHYZB_OK;
 }
@@ -929,7 +949,7 @@ int phyzb_load_states(phyzb_sim* s, const double* q, const double* v, const doub
     PZ_TRY(upload_rows(s, v, s->nv, s->v));
     if (ctrl) return upload_rows(s, ctrl, s->nv, s->ctrl);
     PZ_CUDA(cudaMemsetAsync(s->ctrl, 0, s->state_bytes(), s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -1011,14 +1031,14 @@ int phyzb_step_with_controls(phyzb_sim* s, const void* ctrl, int host_dtype, int
         c++;
     }
     // every host row has been read once the copy stream drains
-    PZ_CUDA(cudaStreamSynchronize(s->copy_stream));
+    PZ_TRY(bounded_sync(s->copy_stream));
     return PHYZB_OK;
 }
 
 int phyzb_sync(phyzb_sim* s) {
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return read_status(s);
 }
 
@@ -1033,7 +1053,7 @@ int phyzb_clear_status(phyzb_sim* s) {
     DeviceGuard g(s->device);
     const int init[2] = {0, 0x7fffffff};
     PZ_CUDA(cudaMemcpyAsync(s->status, init, sizeof(init), cudaMemcpyHostToDevice, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -1131,7 +1151,7 @@ int phyzb_load_states_device(phyzb_sim* s, const void* q, const void* v, const v
 int phyzb_set_stream(phyzb_sim* s, void* stream) {
     PZ_TRY(check_sim(s));
     DeviceGuard g(s->device);
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     s->stream = stream ? (cudaStream_t)stream : s->own_stream;
     return PHYZB_OK;
 }
@@ -1347,7 +1367,7 @@ int comm_allreduce_sum(phyzb_comm* c, void* buf, size_t count, bool f64, cudaStr
 
 int comm_wait(phyzb_comm* c, cudaStream_t stream, double timeout_s) {
     if (!c) {
-        PZ_CUDA(cudaStreamSynchronize(stream));
+        PZ_TRY(bounded_sync(stream));
         return PHYZB_OK;
     }
     NcclApi& n = nccl();

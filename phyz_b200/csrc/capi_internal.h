@@ -35,6 +35,11 @@ const char* last_error();
         if (r_ != PHYZB_OK) return r_; \
     } while (0)
 
+// Wait for everything enqueued on `stream`, at most $PHYZB_SYNC_TIMEOUT seconds
+// (default 600): the kernels hold no spin, so a longer wait means a lost
+// device, reported as PHYZB_ERR_CUDA instead of blocking the caller forever.
+int bounded_sync(cudaStream_t stream);
+
 // Restores the caller's current device on scope exit.
 struct DeviceGuard {
     int prev = -1;

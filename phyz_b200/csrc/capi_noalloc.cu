@@ -93,7 +93,7 @@ int phyzb_gae_noalloc(const float* rewards, const float* values, int64_t nworld,
     if (stats) {
         double hs[3] = {0, 0, 0};
         PZ_CUDA(cudaMemcpyAsync(hs, sums, sizeof(hs), cudaMemcpyDeviceToHost, s));
-        PZ_CUDA(cudaStreamSynchronize(s));
+        PZ_TRY(bounded_sync(s));
         const double mean = hs[0] / count;
         stats[0] = hs[2] / (double)nworld;
         stats[1] = mean;

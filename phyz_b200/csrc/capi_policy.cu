@@ -189,7 +189,7 @@ int download_float_rows(phyzb_sim* s, const float* src, int width, float* host) 
     const cudaError_t e = pz::launch_soa_to_aos<float, float>(src, (float*)p->d_rows, s->nworld, width, s->stream);
     PZ_CUDA(e);
     PZ_CUDA(cudaMemcpyAsync(host, p->d_rows, bytes, cudaMemcpyDeviceToHost, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -255,7 +255,7 @@ int phyzb_enable_policy(phyzb_sim* s, const phyzb_policy_spec* sp) {
     PZ_CUDA(cudaMalloc((void**)&p->d_h, (size_t)2 * p->h_pad * N * sizeof(float)));
     PZ_CUDA(cudaMalloc((void**)&p->d_obs, (size_t)p->history * p->n_in * N * sizeof(float)));
     PZ_CUDA(cudaMalloc((void**)&p->d_out, (size_t)p->history * (p->n_out + 1) * N * sizeof(float)));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return phyzb_seed_policy(s, 0);
 }
 
@@ -293,7 +293,7 @@ int phyzb_set_policy_weights(phyzb_sim* s, const double* w, int64_t n) {
     for (int k = 0; k < p->n_out; k++) o[k] = (float)b3[k];
     DeviceGuard g(s->device);
     PZ_CUDA(cudaMemcpyAsync(p->d_w, pk.data(), pk.size() * sizeof(float), cudaMemcpyHostToDevice, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     p->has_weights = true;
     return PHYZB_OK;
 }
@@ -309,7 +309,7 @@ int phyzb_set_policy_std(phyzb_sim* s, const double* sd, int32_t n) {
     for (int k = 0; k < n; k++) f[k] = (float)sd[k];
     DeviceGuard g(s->device);
     PZ_CUDA(cudaMemcpyAsync(p->d_std, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     p->has_std = true;
     return PHYZB_OK;
 }
@@ -338,7 +338,7 @@ int phyzb_seed_policy(phyzb_sim* s, uint64_t seed) {
     DeviceGuard g(s->device);
     PZ_CUDA(cudaMemcpyAsync(p->d_rng, st.data(), st.size() * sizeof(st[0]), cudaMemcpyHostToDevice, s->stream));
     PZ_CUDA(cudaMemsetAsync(p->d_z, 0, (size_t)p->n_out * s->nworld * sizeof(float), s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 
@@ -417,7 +417,7 @@ int phyzb_readback_kinematics(phyzb_sim* s, double* xf) {
                                                          width, s->stream);
     PZ_CUDA(e);
     PZ_CUDA(cudaMemcpyAsync(xf, p->d_rows, bytes, cudaMemcpyDeviceToHost, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     return PHYZB_OK;
 }
 

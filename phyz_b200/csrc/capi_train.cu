@@ -160,7 +160,7 @@ namespace {
 void destroy_trainer(phyzb_trainer* t) {
     if (!t) return;
     DeviceGuard g(t->device);
-    if (t->stream) cudaStreamSynchronize(t->stream);
+    if (t->stream) bounded_sync(t->stream);
     free_net(t->actor);
     free_net(t->critic);
     void* bufs[] = {t->obs_a, t->obs_c,   t->act,   t->logp,    t->adv,  t->ret,  t->upload_raw,
@@ -378,7 +378,7 @@ int phyzb_trainer_params(phyzb_trainer* t, int32_t which, double* flat, int64_t 
         return fail(PHYZB_ERR_INVALID, "parameter array is " + std::to_string(n) + " long, network has " +
                                            std::to_string(net->d.n_param));
     DeviceGuard g(t->device);
-    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    PZ_TRY(bounded_sync(t->stream));
     PZ_CUDA(cudaMemcpy(flat, net->d.p, (size_t)n * 8, cudaMemcpyDeviceToHost));
     return PHYZB_OK;
 }
@@ -398,7 +398,7 @@ int phyzb_trainer_upload_batch(phyzb_trainer* t, int64_t n, const float* obs_a, 
     PZ_TRY(upload_col(t, logp_old, 1, n, t->logp));
     PZ_TRY(upload_col(t, adv, 1, n, t->adv));
     PZ_TRY(upload_col(t, ret, 1, n, t->ret));
-    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    PZ_TRY(bounded_sync(t->stream));
     t->n_rows = n;
     t->c_obs_a = pz::BatchCol{t->obs_a, std::max<long long>(n, 1), t->actor.d.n_in};
     t->c_obs_c = pz::BatchCol{t->obs_c, std::max<long long>(n, 1), t->critic.d.n_in};
@@ -510,7 +510,7 @@ int phyzb_trainer_evaluate(phyzb_trainer* t, int32_t which, phyzb_batch_col x, i
             PZ_CUDA(cudaMemcpyAsync(out + (size_t)k * n_rows + r0, net->d.out + (size_t)k * t->max_b,
                                     (size_t)b * 4, cudaMemcpyDeviceToDevice, t->stream));
     }
-    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    PZ_TRY(bounded_sync(t->stream));
     return PHYZB_OK;
 }
 
@@ -574,7 +574,7 @@ int phyzb_policy_advantages(phyzb_sim* s, phyzb_trainer* t, phyzb_comm* comm, co
     PZ_CUDA(cudaMemcpyAsync(coef, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice, s->stream));
     PZ_CUDA(pz::rollout_rewards(p->d_obs, p->d_out, p->n_in, p->n_out, N, T, coef, (float)cfg->action_penalty, rew,
                                 s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     // critic values of rows 0 .. T
     const phyzb_batch_col oc{p->d_obs, N, p->n_in};
     PZ_TRY(phyzb_trainer_evaluate(t, 1, oc, (int64_t)(T + 1) * N, val));
@@ -587,7 +587,7 @@ int phyzb_policy_advantages(phyzb_sim* s, phyzb_trainer* t, phyzb_comm* comm, co
     PZ_TRY(comm_wait(comm, s->stream, 120.0));
     double hs[3] = {0, 0, 0};
     PZ_CUDA(cudaMemcpyAsync(hs, sums, sizeof(hs), cudaMemcpyDeviceToHost, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     if (stats) {
         const double mean = hs[0] / count;
         stats[0] = hs[2] / ((double)N * comm_nranks(comm));  // mean return per world
@@ -606,14 +606,14 @@ int phyzb_policy_sync_from_trainer(phyzb_sim* s, phyzb_trainer* t) {
     if (a.n_in != p->n_in || a.n_h != p->n_h || a.n_out != p->n_out || a.n_wf != p->n_wf)
         return fail(PHYZB_ERR_INVALID, "actor shape differs from the policy's");
     DeviceGuard g(s->device);
-    PZ_CUDA(cudaStreamSynchronize(t->stream));
+    PZ_TRY(bounded_sync(t->stream));
     PZ_CUDA(cudaMemcpyAsync(p->d_w, a.wf, (size_t)a.n_wf * 4, cudaMemcpyDeviceToDevice, s->stream));
     std::vector<double> logstd(a.n_out);
     PZ_CUDA(cudaMemcpy(logstd.data(), a.p + t->actor.mlp_params, (size_t)a.n_out * 8, cudaMemcpyDeviceToHost));
     std::vector<float> sd(a.n_out);
     for (int k = 0; k < a.n_out; k++) sd[k] = (float)std::exp(logstd[k]);
     PZ_CUDA(cudaMemcpyAsync(p->d_std, sd.data(), sd.size() * 4, cudaMemcpyHostToDevice, s->stream));
-    PZ_CUDA(cudaStreamSynchronize(s->stream));
+    PZ_TRY(bounded_sync(s->stream));
     p->has_weights = p->has_std = true;
     return PHYZB_OK;
 }
