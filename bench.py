@@ -700,7 +700,11 @@ def measure(ctx, workload, prec, nworld_arg, horizon_arg, steps, warmup, strong=
         except Exception as ex:
             ref_gpu_out = {"value": None, "note": f"unavailable: {ex}"}
 
-    info = sim.launch_info()
+    info = dict(sim.launch_info())
+    # how the rollout launch runs: tile mode (steps_per_run 0) or slice mode
+    # (warps take 32 worlds x steps_per_run jobs; worlds_per_block / blocks
+    # of the slice launch)
+    info["slices"] = sim.slice_plan(horizon)
     entry = {
         "value": value, "unit": "world-steps/s", "ms_per_step": ms / steps, "steps": steps, "warmup": warmup,
         "dtype": prec, "scaling": "strong" if strong else "weak",

@@ -393,6 +393,8 @@ extern "C" {
     pub fn phyzb_measure_fma_peak(precision: c_int, tflops: *mut f64) -> c_int;
     pub fn phyzb_launch_info(sim: *const phyzb_sim, worlds_per_block: *mut i32, blocks: *mut i32,
                              smem_bytes: *mut i32, scratch_per_world: *mut i32, tmem_cols: *mut i32) -> c_int;
+    pub fn phyzb_slice_plan(sim: *const phyzb_sim, nsteps: i32, steps_per_run: *mut i32, worlds_per_block: *mut i32,
+                            blocks: *mut i32) -> c_int;
     pub fn phyzb_set_kernel_specialization(sim: *mut phyzb_sim, mode: i32) -> c_int;
     pub fn phyzb_get_kernel_specialization(sim: *const phyzb_sim, mode: *mut i32, active: *mut i32) -> c_int;
     pub fn phyzb_set_world_lanes(sim: *mut phyzb_sim, lanes: i32) -> c_int;

@@ -579,6 +579,16 @@ int phyzb_measure_fma_peak(int precision, double* tflops);
  * variant's before. */
 int phyzb_launch_info(const phyzb_sim* sim, int32_t* worlds_per_block, int32_t* blocks,
                       int32_t* smem_bytes, int32_t* scratch_per_world, int32_t* tmem_cols);
+/* How a one-thread-per-world rollout launch of `nsteps` steps would run:
+ * steps_per_run = 0 in tile mode (each block takes tiles of
+ * worlds_per_block worlds for every step), else slice mode (each warp
+ * takes jobs of 32 worlds x steps_per_run steps from a device queue, so
+ * warps that finish early take the remaining worlds' runs instead of
+ * idling through a partial last wave). The library picks slice mode when
+ * its wave count says it is faster; PHYZB_SLICES=0 / 1 at creation turns
+ * it off / on for every launch of two or more steps. Host work only. */
+int phyzb_slice_plan(const phyzb_sim* sim, int32_t nsteps, int32_t* steps_per_run, int32_t* worlds_per_block,
+                     int32_t* blocks);
 
 /* ── model-specialized kernels (no reference counterpart) ──────────────── */
 

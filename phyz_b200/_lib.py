@@ -206,6 +206,7 @@ SIGNATURES = {
     "phyzb_comm_sync": (C.c_int, [_P, _P, C.c_double]),
     "phyzb_get_world_lanes": (C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "phyzb_launch_info": (C.c_int, [_P, _I32P, _I32P, _I32P, _I32P, _I32P]),
+    "phyzb_slice_plan": (C.c_int, [_P, C.c_int32, _I32P, _I32P, _I32P]),
     "phyzb_set_kernel_specialization": (C.c_int, [_P, C.c_int32]),
     "phyzb_get_kernel_specialization": (C.c_int, [_P, _I32P, _I32P]),
     "phyzb_enable_policy": (C.c_int, [_P, C.POINTER(PhyzbPolicySpec)]),

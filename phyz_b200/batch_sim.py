@@ -474,6 +474,13 @@ class BatchSim:
         check(self._lib.phyzb_get_kernel_specialization(self._h, C.byref(mode), C.byref(active)))
         return bool(active.value)
 
+    def slice_plan(self, nsteps: int) -> dict:
+        """How a rollout launch of nsteps steps runs: steps_per_run 0 = tile
+        mode, else slice mode (warps take 32 worlds x steps_per_run jobs)."""
+        vals = [C.c_int32() for _ in range(3)]
+        check(self._lib.phyzb_slice_plan(self._h, int(nsteps), *[C.byref(x) for x in vals]))
+        return dict(zip(("steps_per_run", "worlds_per_block", "blocks"), [x.value for x in vals]))
+
     def launch_info(self) -> dict:
         vals = [C.c_int32() for _ in range(5)]
         check(self._lib.phyzb_launch_info(self._h, *[C.byref(x) for x in vals]))

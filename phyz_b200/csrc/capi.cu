@@ -463,14 +463,29 @@ int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
             nsteps = 1;
         }
     }
-    if (specialized(s)) {
-        if (!s->spec) PZ_TRY(prepare_spec<T>(s));
-        const pz::RolloutArgs<T> a = rollout_args<T>(s, s->spec_lay, ctrl, stride, nsteps);
-        PZ_CUDA(pz::spec_launch<T>(s->spec, a, s->spec_lay.launch, s->stream));
-        return PHYZB_OK;
+    const bool spec = specialized(s);
+    if (spec && !s->spec) PZ_TRY(prepare_spec<T>(s));
+    const phyzb_sim::Layout& L = spec ? s->spec_lay : s->lay[s->use];
+    pz::RolloutArgs<T> a = rollout_args<T>(s, L, ctrl, stride, nsteps);
+    // tile or slice mode (pz::plan_slices)
+    pz::LaunchCfg cfg = L.launch;
+    const int chunk = s->slices ? pz::plan_slices(L.launch, s->nworld, nsteps, s->slice_force, &cfg) : 0;
+    if (chunk > 0) {
+        PZ_CUDA(cudaMemsetAsync(s->slices, 0, s->slices_bytes(), s->stream));
+        if (s->slice_stall) {
+            s->slice_stall_start = (unsigned)((s->nworld + 31) / 32);
+            PZ_CUDA(cudaMemcpyAsync(s->slices, &s->slice_stall_start, sizeof(unsigned), cudaMemcpyHostToDevice,
+                                    s->stream));
+        }
+        a.chunk = chunk;
+        a.slices = s->slices;
+    } else {
+        cfg = L.launch;
     }
-    const phyzb_sim::Layout& L = s->lay[s->use];
-    PZ_CUDA(pz::launch_rollout<T>(rollout_args<T>(s, L, ctrl, stride, nsteps), L.launch, s->stream));
+    if (spec)
+        PZ_CUDA(pz::spec_launch<T>(s->spec, a, cfg, s->stream));
+    else
+        PZ_CUDA(pz::launch_rollout<T>(a, cfg, s->stream));
     return PHYZB_OK;
 }
 
@@ -524,6 +539,7 @@ int read_status(phyzb_sim* s) {
     PZ_TRY(bounded_sync(s->stream));
     if (st[0] & 1)
         return fail(PHYZB_ERR_NONFINITE, "state went non-finite on device (first world " + std::to_string(st[1]) + ")");
+    if (st[0] & 2) return fail(PHYZB_ERR_CUDA, "a slice-mode run waited past its bound for the run before it");
     return PHYZB_OK;
 }
 
@@ -691,6 +707,8 @@ void destroy_sim(phyzb_sim* s) {
     free_ptr(s->hf);
     void* st = s->status;
     free_ptr(st);
+    void* sl = s->slices;
+    free_ptr(sl);
     free_ptr(s->lay[0].blob);
     free_ptr(s->lay[1].blob);
     free_ptr(s->spec_lay.blob);
@@ -784,6 +802,9 @@ int phyzb_create(const phyzb_model* model, int64_t nworld, int device, int preci
     s->status = (int*)st;
     const int init[2] = {0, 0x7fffffff};
     cudaMemcpy(s->status, init, sizeof(init), cudaMemcpyHostToDevice);
+    if (const char* env = getenv("PHYZB_SLICES")) s->slice_force = env[0] == '0' ? 0 : (env[0] == '1' ? 1 : -1);
+    if (const char* env = getenv("PHYZB_SLICES_STALL")) s->slice_stall = env[0] == '1';
+    if (cudaMalloc(&s->slices, s->slices_bytes()) != cudaSuccess) return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc slices"));
     s->staging_bytes = (size_t)nworld * std::max(nv, s->nb * PHYZB_CONTACT_STRIDE) * sizeof(double);
     if (cudaMalloc(&s->staging, s->staging_bytes > 0 ? s->staging_bytes : 16) != cudaSuccess)
         return bail(fail(PHYZB_ERR_CUDA, "cudaMalloc staging"));
@@ -1246,6 +1267,21 @@ int phyzb_launch_info(const phyzb_sim* s, int32_t* wpb, int32_t* blocks, int32_t
     if (smem) *smem = L.launch.smem;
     if (scratch) *scratch = L.info.scratch;
     if (tmem_cols) *tmem_cols = L.launch.tm ? L.info.tmem_cols : 0;
+    return PHYZB_OK;
+}
+
+int phyzb_slice_plan(const phyzb_sim* s, int32_t nsteps, int32_t* steps_per_run, int32_t* wpb, int32_t* blocks) {
+    PZ_TRY(check_sim(s));
+    const phyzb_sim::Layout& L = specialized(s) && s->spec ? s->spec_lay : s->lay[s->use];
+    pz::LaunchCfg cfg = L.launch;
+    int chunk = s->slices ? pz::plan_slices(L.launch, s->nworld, nsteps, s->slice_force, &cfg) : 0;
+    if (chunk <= 0) {
+        chunk = 0;
+        cfg = L.launch;
+    }
+    if (steps_per_run) *steps_per_run = chunk;
+    if (wpb) *wpb = cfg.W;
+    if (blocks) *blocks = cfg.grid;
     return PHYZB_OK;
 }
 

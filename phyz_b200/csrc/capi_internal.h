@@ -111,6 +111,17 @@ struct phyzb_sim {
     double hf_o[3] = {0, 0, 0}, hf_cell = 1.0;
     double plane[4] = {0, 0, 0, 0};  // offset, max_depth, half_x, half_y (cfg.plane_body >= 0)
     int* status = nullptr;
+    // slice-mode job queue: job counter, a spare word, runs finished per warp tile
+    // (pz::RolloutArgs::slices); slice_force: PHYZB_SLICES at creation
+    // (-1 decide per launch, 0 never, 1 whenever a launch has two steps)
+    int* slices = nullptr;
+    int slice_force = -1;
+    // PHYZB_SLICES_STALL=1 at creation (a test of the bounded wait): every
+    // slice-mode launch starts its queue past the first run of every warp
+    // tile, so each later run's wait runs out and the status reports it
+    bool slice_stall = false;
+    unsigned slice_stall_start = 0;
+    size_t slices_bytes() const { return 8 + 4 * (size_t)((nworld + 31) / 32); }
     // lay[0]: every record in shared memory (the objective kernel's layout
     // and the fallback); lay[1]: hinge records in Tensor Memory. `use` is the
     // layout the rollout kernel runs with.

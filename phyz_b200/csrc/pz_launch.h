@@ -15,12 +15,26 @@ namespace pz {
 // array (one block per SM).
 constexpr unsigned TMEM_COLS = 512;
 
+// Whether a generic rollout variant has slice mode compiled in (each mode is
+// a copy of the step's code): the Tensor-Memory variants (one block per SM,
+// whole warps: the layouts whose few resident worlds leave the widest
+// partial waves) without impulse contact (feature bit 16) or terrain (32).
+template <int FEAT, bool TM>
+struct SliceVariant {
+    static constexpr bool value = TM && (FEAT & (16 | 32)) == 0;
+};
+
 struct LaunchCfg {
     int W;         // worlds (threads) per block
     int grid;      // blocks
     int smem;      // dynamic shared memory bytes per block
     int tm;        // 1: body records in Tensor Memory (one block per SM)
     double score;  // worlds resident per SM x fill of the last wave
+    int blocks;    // blocks resident per SM at this shape
+    // Slice mode (every warp takes (32 worlds, a run of steps) jobs from a
+    // queue, plan_slices): the widest whole-warp block that puts no more warps
+    // on an SM sub-partition than the tile shape above does; slice_W 0: none.
+    int slice_W, slice_grid, slice_smem;
 };
 
 // One fused rollout launch: `nsteps` steps of every world.
@@ -57,6 +71,14 @@ struct RolloutArgs {
     // body-attached contact plane (contact variants; plane_body -1: none)
     int plane_body;
     double plane_offset, plane_max_depth, plane_half_x, plane_half_y;
+    // slice mode: chunk > 0 splits every world's steps into runs of `chunk`
+    // steps; a warp takes (warp tile of 32 worlds, run) jobs in run-major
+    // order from the queue in `slices` ([0]: job counter, [1] unused, [2 + t]:
+    // runs finished of warp tile t; zeroed before the launch) and starts a
+    // run once the tile's previous one is finished (a bounded wait). 0: each
+    // block takes its tiles of W worlds for all steps.
+    int chunk = 0;
+    int* slices = nullptr;
 };
 
 // The world split over lanes (stepper_lanes.cuh, planned by pz_lanes.h):
@@ -75,6 +97,54 @@ struct LanesArgs {
 };
 
 #ifndef __CUDACC_RTC__
+// Whether a rollout of `nsteps` steps over `nworld` worlds runs faster in
+// slice mode, and with which run length. A tile launch takes ceil(tiles /
+// grid) waves of the whole horizon, so a world count just past a multiple
+// of the resident worlds leaves most of the GPU idle in its last wave
+// (C2: 65536 worlds on 148 x 224 = 1.98 waves run as 2; at 256 worlds per
+// SM, 1.73). Slices let the warps that finish early take the remaining
+// worlds' runs, so the rollout takes about (warp tiles x steps) / warp
+// slots step-times plus one run of tail. Each run costs about one step more
+// (the state's load and store and the first step's forward sweep), counted
+// here. Returns the run length (0: tile mode) and the slice launch shape in
+// *out. force: -1 decide, 0 tile mode, 1 slices whenever the launch has two
+// or more steps (runs of a third of them; PHYZB_SLICES=1, which the tests
+// use to cover the mode at small sizes).
+inline int plan_slices(const LaunchCfg& c, long long nworld, int nsteps, int force, LaunchCfg* out) {
+    if (c.slice_W < 32 || c.slice_grid <= 0 || nsteps < 2 || nworld <= 0 || force == 0) return 0;
+    const long long ntw = (nworld + 31) / 32;
+    const int wpb = c.slice_W / 32;
+    const long long need = (ntw + wpb - 1) / wpb;
+    const long long grid = need < c.slice_grid ? need : c.slice_grid;
+    const long long slots = grid * wpb;
+    *out = c;
+    out->W = c.slice_W;
+    out->grid = (int)grid;
+    out->smem = c.slice_smem;
+    // the job counter is 32-bit: every warp's last fetch passes the job count
+    auto fits = [&](long long runs) { return ntw * runs + slots < (1LL << 31); };
+    if (force == 1) {
+        const int chunk = nsteps >= 3 ? (nsteps / 3 < 512 ? nsteps / 3 : 512) : 1;
+        return fits((nsteps + chunk - 1) / chunk) ? chunk : 0;
+    }
+    const long long tiles = (nworld + c.W - 1) / c.W;
+    const double t_tile = (double)((tiles + c.grid - 1) / c.grid) * nsteps;
+    double best = 0.97 * t_tile;
+    int pick = 0;
+    // runs of 8 to 512 steps: long enough that a run's extra step is small,
+    // short enough that a wait for the run before stays far below its bound
+    for (int chunk = 8; chunk <= 512 && chunk < nsteps; chunk += chunk < 64 ? 4 : 32) {
+        const long long runs = (nsteps + chunk - 1) / chunk;
+        if (!fits(runs)) continue;
+        const double t = (double)((ntw * runs + slots - 1) / slots) * (chunk + 1);
+        if (t < best) {
+            best = t;
+            pick = chunk;
+        }
+    }
+    return pick;
+}
+
 template <class T>
 cudaError_t lanes_config(int feat, int lanes, int scratch, int model_bytes, long long nworld, LaunchCfg* out);
 template <class T>

@@ -47,26 +47,39 @@ inline int tmem_cols_per_thread(int warps, int tmem_total) {
 template <class Occ>
 cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, int scratch, int model_bytes,
                         long long nworld, int tmem_cols, int tmem_total, Occ occupancy, LaunchCfg* out,
-                        int only_w = 0, int max_w = 256) {
+                        int only_w = 0, int max_w = 256, bool can_slice = false) {
     const long long per_world = (long long)scratch * (long long)esz;
     int forced = only_w;
     if (const char* env = getenv("PHYZB_WORLDS_PER_BLOCK"); env && forced <= 0) forced = atoi(env);
+    // shared memory and resident blocks per SM of width W: 1 = fits, 0 = past
+    // the layout's limits (wider blocks do not fit either), -1 = skip W,
+    // -2 = the occupancy query failed (occ_err)
+    cudaError_t occ_err = cudaSuccess;
+    auto shape = [&](int W, long long* smem, int* blocks) -> int {
+        if (tm && tmem_cols > tmem_cols_per_thread((W + 31) / 32, tmem_total)) return 0;
+        *smem = (long long)model_bytes + per_world * W;
+        if (*smem > dyn_cap) return 0;
+        // Tensor-Memory blocks ask for more than half an SM's shared memory so
+        // that no second block lands on the SM and waits on the allocation
+        if (tm) *smem = std::max(*smem, (long long)(dl.smem_optin / 2 + 16) & ~15LL);
+        *blocks = 0;
+        occ_err = occupancy(blocks, W, (size_t)*smem);
+        if (occ_err != cudaSuccess) return -2;
+        if (*blocks <= 0) return -1;
+        if (tm) *blocks = 1;  // each block holds the whole Tensor Memory
+        return 1;
+    };
     int best_w = 0, best_blocks = 0, best_smem = 0;
     double best_score = -1.0;
     const int step = tm ? 32 : 2;
     for (int W = 32; W <= max_w; W += step) {
         if (forced > 0 && W != forced) continue;
-        if (tm && tmem_cols > tmem_cols_per_thread((W + 31) / 32, tmem_total)) break;
-        long long smem = (long long)model_bytes + per_world * W;
-        if (smem > dyn_cap) break;
-        // Tensor-Memory blocks ask for more than half an SM's shared memory so
-        // that no second block lands on the SM and waits on the allocation
-        if (tm) smem = std::max(smem, (long long)(dl.smem_optin / 2 + 16) & ~15LL);
+        long long smem = 0;
         int blocks = 0;
-        const cudaError_t e = occupancy(&blocks, W, (size_t)smem);
-        if (e != cudaSuccess) return e;
-        if (blocks <= 0) continue;
-        if (tm) blocks = 1;  // each block holds the whole Tensor Memory
+        const int r = shape(W, &smem, &blocks);
+        if (r == -2) return occ_err;
+        if (r == 0) break;
+        if (r < 0) continue;
         const double resident = (double)blocks * W * dl.sm_count;  // worlds in flight on the GPU
         const double waves = nworld > 0 ? std::ceil((double)nworld / resident) : 1.0;
         const double used = nworld > 0 ? (double)nworld / (waves * resident) : 1.0;
@@ -86,6 +99,31 @@ cudaError_t pick_launch(const DeviceLimits& dl, int dyn_cap, bool tm, int esz, i
     out->smem = best_smem;
     out->tm = tm ? 1 : 0;
     out->score = best_score;
+    out->blocks = best_blocks;
+    // The slice-mode shape: the most resident worlds in whole-warp blocks
+    // with no more warps on the busiest SM sub-partition (warps are spread
+    // over the SM's four schedulers) than the tile shape has, so a step
+    // takes about as long in either mode.
+    out->slice_W = out->slice_grid = out->slice_smem = 0;
+    if (!can_slice) return cudaSuccess;
+    const int per_sub = (best_blocks * ((best_w + 31) / 32) + 3) / 4;
+    long long best_res = 0;
+    for (int W = 32; W <= max_w; W += 32) {
+        if (only_w > 0 && W != only_w) continue;
+        long long smem = 0;
+        int blocks = 0;
+        const int r = shape(W, &smem, &blocks);
+        if (r == -2) return occ_err;
+        if (r == 0) break;
+        if (r < 0) continue;
+        if ((blocks * (W / 32) + 3) / 4 > per_sub) continue;
+        if ((long long)blocks * W > best_res) {
+            best_res = (long long)blocks * W;
+            out->slice_W = W;
+            out->slice_grid = dl.sm_count * blocks;
+            out->slice_smem = (int)smem;
+        }
+    }
     return cudaSuccess;
 }
 

@@ -242,6 +242,50 @@ __device__ __forceinline__ unsigned char* stage_model(const void* g, int bytes, 
 #define PZ_STEP_SYNC 0
 #endif
 
+// Slice mode (RolloutArgs::chunk > 0). The warp's next job from the queue:
+// lane 0 takes it and a warp reduction (its result is the same on every
+// lane by construction) hands it to every lane.
+__device__ __forceinline__ int slice_next(int* slices) {
+    unsigned j = 0;
+    if ((threadIdx.x & 31) == 0) j = atomicAdd(reinterpret_cast<unsigned*>(slices), 1u);
+    return (int)__reduce_max_sync(0xffffffffu, j);
+}
+
+// Wait until a warp tile has finished `want` runs (*flag, published by
+// slice_done). Every lane reads the flag with acquire semantics, so the
+// state stores of the run before are visible to every lane's loads after.
+// The job order makes the wait short (the run before was taken a whole
+// round of jobs earlier) and a run is only ever held by a running warp, so
+// it ends; it is still bounded: after 4 s of device time the status word's
+// bit 1 is set and the run goes on.
+__device__ __forceinline__ void slice_wait(const int* flag, int want, int* status) {
+    int got;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(got) : "l"(flag) : "memory");
+    if (got < want) {
+        unsigned long long t0, t;
+        asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t0));
+        for (;;) {
+            __nanosleep(256);
+            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(got) : "l"(flag) : "memory");
+            if (got >= want) break;
+            asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+            if (t - t0 > 4000000000ull) {
+                atomicOr(status, 2);
+                break;
+            }
+        }
+    }
+    __syncwarp();
+}
+
+// Publish that a warp tile has finished `done` runs, after every lane's
+// state stores.
+__device__ __forceinline__ void slice_done(int* flag, int done) {
+    __threadfence();
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) asm volatile("st.release.gpu.global.s32 [%0], %1;\n" ::"l"(flag), "r"(done) : "memory");
+}
+
 template <bool TM, class T>
 struct PickScr {
     using type = SmemScr<T>;
@@ -260,6 +304,114 @@ struct PickScr<true, T> {
 #else
 #define PZ_MAX_THREADS 256
 #endif
+
+// One job of the rollout kernel: this thread's world wt from step s0 to
+// step s1 of the launch (state in from q, v and the impulse buffer, out to
+// them; accelerations and contact state when s1 is the launch's last step).
+template <class T, int FEAT, class Scr>
+__device__ __forceinline__ void run_job(const RolloutArgs<T>& P, const ModelView<T>& M, const Scr& S,
+                                        const long long wt, const int s0, const int s1) {
+    const long long N = P.nworld;
+    // lanes past the last world run world N-1 again and write nothing, so
+    // every warp stays converged for the warp-wide tcgen05 operations
+    const bool active = wt < N;
+    const long long w = active ? wt : N - 1;
+    PZ_UNROLL_BODIES
+    for (int j = 0; j < M.nv; j++) {
+        S(j) = P.q[j * N + w];
+        S(M.nv + j) = P.v[j * N + w];
+    }
+    const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
+    PZ_UNROLL_BODIES
+    for (int i = 0; i < M.nb; i++) prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, M.bi[i], S, io, s0);
+    S.commit();
+    if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+        // the wrenches of the previous step's last sweep and the staged
+        // impulses that warm-start this one
+        PZ_UNROLL_BODIES
+        for (int i = 0; i < M.nb; i++) {
+            const BodyI bi = M.bi[i];
+            if (bi.c_imp < 0) continue;
+            // rows: wrench (6), ground impulses, plane impulses (3 per point each)
+            const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
+            int r = bi.c_imp;
+            for (int k = 0; k < 6; k++) S(bi.s_f + k) = P.imp[(long long)(r++) * N + w];
+            if (bi.s_imp >= 0)
+                for (int k = 0; k < np3; k++) S(bi.s_imp + k) = P.imp[(long long)(r++) * N + w];
+            if (bi.s_pimp >= 0)
+                for (int k = 0; k < np3; k++) S(bi.s_pimp + k) = P.imp[(long long)(r++) * N + w];
+        }
+    }
+    const Out<T> none{nullptr, 0};
+    pass1_all<FEAT>(M, S);
+    for (int s = s0; s < s1; s++) {
+        S.wait();
+#if PZ_STEP_SYNC
+        // keep the block's warps on the same stretch of code (they share
+        // its instruction fetches); every thread runs every step
+        __syncthreads();
+#endif
+        const bool last = s == P.nsteps - 1;
+        if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
+            // contact state of the last step, from the state it starts from
+            // (every lane runs it, warp-wide record loads; only active lanes write)
+            if (last && P.contact && P.cstate)
+                contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
+        }
+        if constexpr ((FEAT & FEAT_TERRAIN) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
+            // the plane contacts of this step's state join the ground wrenches of pass 1
+            if (M.plane.body >= 0) plane_pass<false, FEAT>(M, S);
+        }
+        pass2<FEAT>(M, S);
+        if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+            // sweeps x [contact at the free velocity -> the response to
+            // the wrench change], from the step's backward sweep
+            keep_backward_state(M, S);
+            for (int k = 0; k < P.sweeps; k++) {
+                sweep_forward<FEAT>(M, S);
+                if constexpr ((FEAT & FEAT_TERRAIN) != 0)
+                    if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
+                wrench_response<FEAT>(M, S);
+            }
+            if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
+        }
+        if (last)
+            pass3_next<FEAT, true>(M, S, io, -1, active ? Out<T>{P.qdd + w, N} : none);
+        else
+            pass3_next<FEAT, false>(M, S, io, s + 1, none);
+        S.commit();
+    }
+    S.wait();
+    if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
+        if (active)
+            PZ_UNROLL_BODIES
+            for (int i = 0; i < M.nb; i++) {
+                const BodyI bi = M.bi[i];
+                if (bi.c_imp < 0) continue;
+                const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
+                int r = bi.c_imp;
+                for (int k = 0; k < 6; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_f + k);
+                if (bi.s_imp >= 0)
+                    for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_imp + k);
+                if (bi.s_pimp >= 0)
+                    for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_pimp + k);
+            }
+    }
+    if (active) {
+        bool finite = true;
+        PZ_UNROLL_BODIES
+        for (int j = 0; j < M.nv; j++) {
+            const T qj = S(j), vj = S(M.nv + j);
+            finite = finite && pz_finite(qj) && pz_finite(vj);
+            P.q[j * N + w] = qj;
+            P.v[j * N + w] = vj;
+        }
+        if (!finite) {
+            atomicOr(P.status, 1);
+            atomicMin(P.status + 1, (int)(w < 0x7fffffff ? w : 0x7fffffff));
+        }
+    }
+}
 
 template <class T, int FEAT, bool TM>
 __global__ void __launch_bounds__(PZ_MAX_THREADS, 1) rollout_kernel(const __grid_constant__ RolloutArgs<T> P) {
@@ -295,108 +447,36 @@ __global__ void __launch_bounds__(PZ_MAX_THREADS, 1) rollout_kernel(const __grid
         const unsigned cols = (TMEM_COLS / per_quarter) & ~7u;  // whole 8-column records
         S.tbase = tmem_slot + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(warp >> 2) * cols;
     }
-    const long long ntiles = (P.nworld + W - 1) / W;
     const long long N = P.nworld;
-    for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        const long long wt = tile * W + threadIdx.x;
-        // lanes past the last world run world N-1 again and write nothing, so
-        // every warp stays converged for the warp-wide tcgen05 operations
-        const bool active = wt < N;
-        const long long w = active ? wt : N - 1;
-        PZ_UNROLL_BODIES
-        for (int j = 0; j < M.nv; j++) {
-            S(j) = P.q[j * N + w];
-            S(M.nv + j) = P.v[j * N + w];
-        }
-        const WorldIO<T> io{P.ctrl, P.ctrl_stride, P.targets, N, w};
-        PZ_UNROLL_BODIES
-        for (int i = 0; i < M.nb; i++) prefetch_controls<(FEAT & FEAT_IMPULSE) != 0>(M, M.bi[i], S, io, 0);
-        S.commit();
-        if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
-            // the wrenches of the previous step's last sweep and the staged
-            // impulses that warm-start this one
-            PZ_UNROLL_BODIES
-            for (int i = 0; i < M.nb; i++) {
-                const BodyI bi = M.bi[i];
-                if (bi.c_imp < 0) continue;
-                // rows: wrench (6), ground impulses, plane impulses (3 per point each)
-                const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
-                int r = bi.c_imp;
-                for (int k = 0; k < 6; k++) S(bi.s_f + k) = P.imp[(long long)(r++) * N + w];
-                if (bi.s_imp >= 0)
-                    for (int k = 0; k < np3; k++) S(bi.s_imp + k) = P.imp[(long long)(r++) * N + w];
-                if (bi.s_pimp >= 0)
-                    for (int k = 0; k < np3; k++) S(bi.s_pimp + k) = P.imp[(long long)(r++) * N + w];
-            }
-        }
-        const Out<T> none{nullptr, 0};
-        pass1_all<FEAT>(M, S);
-        for (int s = 0; s < P.nsteps; s++) {
-            S.wait();
-#if PZ_STEP_SYNC
-            // keep the block's warps on the same stretch of code (they share
-            // its instruction fetches); every thread runs every step
-            __syncthreads();
+#if PZ_STEP_SYNC || defined(PZ_SPEC)
+    // (a model-specialized build runs tile mode only: a second copy of its
+    // unrolled step would double its compile time)
+    constexpr bool sliced = false;
+#else
+    constexpr bool can_slice = SliceVariant<FEAT, TM>::value;
+    const bool sliced = can_slice && P.chunk > 0;
 #endif
-            const bool last = s == P.nsteps - 1;
-            if constexpr ((FEAT & FEAT_CONTACT) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
-                // contact state of the last step, from the state it starts from
-                // (every lane runs it, warp-wide record loads; only active lanes write)
-                if (last && P.contact && P.cstate)
-                    contact_state_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
-            }
-            if constexpr ((FEAT & FEAT_TERRAIN) != 0 && (FEAT & FEAT_IMPULSE) == 0) {
-                // the plane contacts of this step's state join the ground wrenches of pass 1
-                if (M.plane.body >= 0) plane_pass<false, FEAT>(M, S);
-            }
-            pass2<FEAT>(M, S);
-            if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
-                // sweeps x [contact at the free velocity -> the response to
-                // the wrench change], from the step's backward sweep
-                keep_backward_state(M, S);
-                for (int k = 0; k < P.sweeps; k++) {
-                    sweep_forward<FEAT>(M, S);
-                    if constexpr ((FEAT & FEAT_TERRAIN) != 0)
-                        if (M.plane.body >= 0) plane_pass<true, FEAT>(M, S);
-                    wrench_response<FEAT>(M, S);
-                }
-                if (last && P.cstate) contact_state_impulse_pass<FEAT>(M, S, active ? Out<T>{P.cstate + w, N} : none);
-            }
-            if (last)
-                pass3_next<FEAT, true>(M, S, io, -1, active ? Out<T>{P.qdd + w, N} : none);
-            else
-                pass3_next<FEAT, false>(M, S, io, s + 1, none);
-            S.commit();
-        }
-        S.wait();
-        if constexpr ((FEAT & FEAT_IMPULSE) != 0) {
-            if (active)
-                PZ_UNROLL_BODIES
-                for (int i = 0; i < M.nb; i++) {
-                    const BodyI bi = M.bi[i];
-                    if (bi.c_imp < 0) continue;
-                    const int np3 = 3 * (bi.gtype == 2 ? 8 : 1);
-                    int r = bi.c_imp;
-                    for (int k = 0; k < 6; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_f + k);
-                    if (bi.s_imp >= 0)
-                        for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_imp + k);
-                    if (bi.s_pimp >= 0)
-                        for (int k = 0; k < np3; k++) P.imp[(long long)(r++) * N + w] = S(bi.s_pimp + k);
-                }
-        }
-        if (active) {
-            bool finite = true;
-            PZ_UNROLL_BODIES
-            for (int j = 0; j < M.nv; j++) {
-                const T qj = S(j), vj = S(M.nv + j);
-                finite = finite && pz_finite(qj) && pz_finite(vj);
-                P.q[j * N + w] = qj;
-                P.v[j * N + w] = vj;
-            }
-            if (!finite) {
-                atomicOr(P.status, 1);
-                atomicMin(P.status + 1, (int)(w < 0x7fffffff ? w : 0x7fffffff));
-            }
+    // Tile mode: the blocks stride over tiles of W worlds, each for every
+    // step. Slice mode: every warp takes jobs (a tile of 32 worlds, one run
+    // of P.chunk steps) from the queue in run-major order, the state going
+    // through q and v between runs. The two loops are written out apart so
+    // that tile mode's step range stays the kernel parameters (measured:
+    // one loop over either kind of job ran C2's tile launches 2 % slower).
+    if (!sliced) {
+        const long long ntiles = (N + W - 1) / W;
+        for (long long tile = blockIdx.x; tile < ntiles; tile += gridDim.x)
+            run_job<T, FEAT>(P, M, S, tile * W + threadIdx.x, 0, P.nsteps);
+    } else {
+        const long long ntiles = (N + 31) / 32;
+        const long long njobs = ntiles * ((P.nsteps + P.chunk - 1) / P.chunk);
+        for (long long job = slice_next(P.slices); job < njobs; job = slice_next(P.slices)) {
+            const long long tile = job % ntiles;
+            const int run = (int)(job / ntiles);
+            const int s0 = run * P.chunk;
+            if (run > 0) slice_wait(P.slices + 2 + tile, run, P.status);
+            run_job<T, FEAT>(P, M, S, tile * 32 + (threadIdx.x & 31), s0,
+                             s0 + P.chunk < P.nsteps ? s0 + P.chunk : P.nsteps);
+            slice_done(P.slices + 2 + tile, run + 1);
         }
     }
     if constexpr (TM) {
@@ -476,7 +556,7 @@ cudaError_t config_variant(const DeviceLimits& dl, int scratch, int model_bytes,
         return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks, rollout_kernel<T, FEAT, TM>, W, smem);
     };
     return pick_launch(dl, dyn_cap, TM, (int)sizeof(T), scratch, model_bytes, nworld, tmem_cols, (int)TMEM_COLS,
-                       occupancy, out);
+                       occupancy, out, 0, 256, SliceVariant<FEAT, TM>::value);
 }
 
 template <class T, int FEAT, bool TM>
