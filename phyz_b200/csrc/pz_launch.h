@@ -131,9 +131,13 @@ inline int plan_slices(const LaunchCfg& c, long long nworld, int nsteps, int for
     const double t_tile = (double)((tiles + c.grid - 1) / c.grid) * nsteps;
     double best = 0.97 * t_tile;
     int pick = 0;
-    // runs of 8 to 512 steps: long enough that a run's extra step is small,
-    // short enough that a wait for the run before stays far below its bound
-    for (int chunk = 8; chunk <= 512 && chunk < nsteps; chunk += chunk < 64 ? 4 : 32) {
+    // every split into 2 or more runs of 8 to 512 steps: long enough that a
+    // run's extra step is small, short enough that a wait for the run before
+    // stays far below its bound
+    for (int split = 2; split <= nsteps; split++) {
+        const int chunk = (nsteps + split - 1) / split;
+        if (chunk < 8) break;
+        if (chunk > 512) continue;
         const long long runs = (nsteps + chunk - 1) / chunk;
         if (!fits(runs)) continue;
         const double t = (double)((ntw * runs + slots - 1) / slots) * (chunk + 1);
