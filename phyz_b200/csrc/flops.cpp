@@ -112,6 +112,8 @@ struct HostScr {
         base[bi.s_xj + 1] = r.s;
         rec_put_vw(bi, r.v);
     }
+    SV<Cnt> ext_get(const BodyI& bi) const { return ld_sv<Cnt>(*this, bi.s_f); }
+    void ext_put(const BodyI& bi, const SV<Cnt>& f) const { st_sv(*this, bi.s_f, f); }
     void rec_put_vw(const BodyI& bi, const SV<Cnt>& v) const {
         base[bi.s_vw] = v.w.x;
         base[bi.s_vw + 1] = v.w.y;

@@ -96,8 +96,10 @@ struct alignas(16) BodyI {
                       // singular)
     int s_w0b;        // D^-1 u of the step's full backward sweep (ndof)
     int s_fp;         // F_EXTF: the wrench that backward sweep applied (6)
+    int t_f;          // F_EXTF: Tensor Memory column of the body's external wrench record
+                      // [f (6), 0, 0] (-1: in s_f)
 };
-static_assert(sizeof(BodyI) == 28 * sizeof(int), "BodyI: 27 words and one of padding");
+static_assert(sizeof(BodyI) == 28 * sizeof(int), "BodyI: 28 words");
 
 template <class T>
 struct alignas(16) PdT {
@@ -140,7 +142,7 @@ struct ImpMat {
 
 // Words of a BodyI before its alignment padding (the model-specialized
 // source lists them in this order).
-constexpr int BODYI_WORDS = 27;
+constexpr int BODYI_WORDS = 28;
 
 #ifdef PZ_SPEC
 // Model-specialized build: the host emits one packed model's tables as

@@ -170,7 +170,9 @@ inline std::vector<phyzb_body> relabel_frames(const phyzb_model* m, std::vector<
 // `tmem_budget` > 0: place the records of all tmem_kind bodies in Tensor
 // Memory columns (8 words per record in f32, 16 in f64) if they all fit the
 // budget (else none: info.tmem_cols = 0); their s_xj / s_vw slots are then
-// not allocated in shared memory.
+// not allocated in shared memory. The collidable bodies' contact wrenches
+// follow them there when all of them fit too (penalty contact, no body
+// plane), and then have no s_f slot.
 template <class T>
 inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std::vector<unsigned char>& blob,
                            int tmem_budget = 0) {
@@ -195,11 +197,21 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
     const std::vector<phyzb_body> rb = relabel_frames(m, shift);
     // a Tensor-Memory layout holds the records of every relabelled hinge
     // (the kernel then accesses them without a per-body test) or none
+    // and, when they fit beside those, the external wrenches of the
+    // collidable bodies (penalty contact without a body plane: each wrench is
+    // stored once per step by the forward sweep and read once by the
+    // backward sweep), all of them or none
+    bool tmem_wrench = false;
     {
-        int need = 0;
-        for (int i = 0; i < nb; i++)
-            if (tmem_kind(m->bodies[i])) need += 8 * (int)(sizeof(T) / 4);
+        const int rec = 8 * (int)(sizeof(T) / 4);
+        int need = 0, wneed = 0;
+        for (int i = 0; i < nb; i++) {
+            if (tmem_kind(m->bodies[i])) need += rec;
+            if (m->bodies[i].geom_type != 0) wneed += rec;
+        }
         if (need > tmem_budget) tmem_budget = 0;
+        tmem_wrench = tmem_budget > 0 && cfg.contact && !cfg.impulse && cfg.plane_body < 0 && wneed > 0 &&
+                      need + wneed <= tmem_budget;
     }
     int next = 2 * nv;  // q, v
     int off = 0;
@@ -330,10 +342,16 @@ inline PackInfo pack_model(const phyzb_model* m, int nv, const PackCfg& cfg, std
                                   cfg.plane_exclude.end();
         const bool is_pb = plane && i == cfg.plane_body;
         const int npts = b.geom_type == 2 ? 8 : 1;
+        d.t_f = -1;
         if (cfg.contact && b.geom_type != 0) {
             flags |= F_CONTACT | F_EXTF;
-            d.s_f = next;
-            next += 6;
+            if (tmem_wrench) {
+                d.t_f = info.tmem_cols;
+                info.tmem_cols += rec_cols;
+            } else {
+                d.s_f = next;
+                next += 6;
+            }
             if (impulse) {
                 d.s_fp = next;
                 next += 6;

@@ -1158,7 +1158,7 @@ PZ_HD void pass1_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
                 const SV<T> f = contact_wrench_call<TERRAIN>(M.ground_h, M.friction, M.inv_dt_c, M.kstiff_c, M.ter,
                                                              bi, M.btp + i, wf, v, false, i, Out<T>{nullptr, 0});
 #endif
-                st_sv(S, bi.s_f, f);
+                S.ext_put(bi, f);
             }
         }
     }
@@ -1640,7 +1640,7 @@ PZ_HD void pass2_body(const ModelView<T>& M, const Scr& S, int i, const BodyI& b
     const SV<T> hv = mksv<T>(ksymv(bt.Io, v.w) + kcross(mc, v.l), v.l * bt.mass + crossk(v.w, mc));
     SV<T> bias = crf(v, hv);
     if constexpr ((FEAT & FEAT_CONTACT) != 0) {
-        if (bi.flags & F_EXTF) bias = bias - ld_sv<T>(S, bi.s_f);
+        if (bi.flags & F_EXTF) bias = bias - S.ext_get(bi);
     }
     pA = pA + bias;
     if (bi.flags & F_BRANCH) {

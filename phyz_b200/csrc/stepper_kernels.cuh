@@ -72,6 +72,9 @@ struct SmemScr {
         st_sv(*this, bi.s_vw, r.v);
     }
     __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const { st_sv(*this, bi.s_vw, v); }
+    // the external (contact) wrench of an F_EXTF body
+    __device__ __forceinline__ SV<T> ext_get(const BodyI& bi) const { return ld_sv<T>(*this, bi.s_f); }
+    __device__ __forceinline__ void ext_put(const BodyI& bi, const SV<T>& f) const { st_sv(*this, bi.s_f, f); }
 };
 
 // Tensor Memory scratch for body records: each thread owns the TMEM lane of
@@ -171,6 +174,50 @@ struct TmemScr : SmemScr<T> {
     __device__ __forceinline__ void rec_put_vw(const BodyI& bi, const SV<T>& v) const {
         const T d[8] = {T(0), T(0), v.w.x, v.w.y, v.w.z, v.l.x, v.l.y, v.l.z};
         put_words(tbase + (unsigned)bi.t_rec, d, 6);
+    }
+    // the external (contact) wrench of an F_EXTF body: a record [f, 0, 0] at
+    // column t_f, or its shared-memory slots when the layout keeps it there
+    __device__ __forceinline__ SV<T> ext_get(const BodyI& bi) const {
+        if (bi.t_f < 0) return ld_sv<T>(*this, bi.s_f);
+        const unsigned a = tbase + (unsigned)bi.t_f;
+        T d[6];
+        if constexpr (sizeof(T) == 4) {
+            unsigned x0, x1, x2, x3, x4, x5, x6, x7;
+            asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+                         : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3), "=r"(x4), "=r"(x5), "=r"(x6), "=r"(x7)
+                         : "r"(a));
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                         : "+r"(x0), "+r"(x1), "+r"(x2), "+r"(x3), "+r"(x4), "+r"(x5), "+r"(x6), "+r"(x7)::"memory");
+            d[0] = __uint_as_float(x0);
+            d[1] = __uint_as_float(x1);
+            d[2] = __uint_as_float(x2);
+            d[3] = __uint_as_float(x3);
+            d[4] = __uint_as_float(x4);
+            d[5] = __uint_as_float(x5);
+        } else {
+            unsigned x[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+                "%14, %15}, [%16];\n"
+                : "=r"(x[0]), "=r"(x[1]), "=r"(x[2]), "=r"(x[3]), "=r"(x[4]), "=r"(x[5]), "=r"(x[6]), "=r"(x[7]),
+                  "=r"(x[8]), "=r"(x[9]), "=r"(x[10]), "=r"(x[11]), "=r"(x[12]), "=r"(x[13]), "=r"(x[14]), "=r"(x[15])
+                : "r"(a));
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                         : "+r"(x[0]), "+r"(x[1]), "+r"(x[2]), "+r"(x[3]), "+r"(x[4]), "+r"(x[5]), "+r"(x[6]),
+                           "+r"(x[7]), "+r"(x[8]), "+r"(x[9]), "+r"(x[10]), "+r"(x[11]), "+r"(x[12]), "+r"(x[13]),
+                           "+r"(x[14]), "+r"(x[15])::"memory");
+#pragma unroll
+            for (int k = 0; k < 6; k++) d[k] = T(__hiloint2double((int)x[2 * k + 1], (int)x[2 * k]));
+        }
+        return mksv<T>(mk3<T>(d[0], d[1], d[2]), mk3<T>(d[3], d[4], d[5]));
+    }
+    __device__ __forceinline__ void ext_put(const BodyI& bi, const SV<T>& f) const {
+        if (bi.t_f < 0) {
+            st_sv(*this, bi.s_f, f);
+            return;
+        }
+        const T d[8] = {f.w.x, f.w.y, f.w.z, f.l.x, f.l.y, f.l.z, T(0), T(0)};
+        put_words(tbase + (unsigned)bi.t_f, d, 8);
     }
     // stores complete before later loads of the same columns
     __device__ __forceinline__ void fence_st() const { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }

@@ -38,6 +38,8 @@ struct HS {
         return r;
     }
     void rec_put(const BodyI& bi, const Rec<double>& r) const { base[bi.s_xj] = r.c; base[bi.s_xj + 1] = r.s; rec_put_vw(bi, r.v); }
+    SV<double> ext_get(const BodyI& bi) const { return ld_sv<double>(*this, bi.s_f); }
+    void ext_put(const BodyI& bi, const SV<double>& f) const { st_sv(*this, bi.s_f, f); }
     void rec_put_vw(const BodyI& bi, const SV<double>& v) const {
         base[bi.s_vw] = v.w.x; base[bi.s_vw + 1] = v.w.y; base[bi.s_vw + 2] = v.w.z;
         base[bi.s_vw + 3] = v.l.x; base[bi.s_vw + 4] = v.l.y; base[bi.s_vw + 5] = v.l.z;
