@@ -79,7 +79,8 @@ int repack_t(phyzb_sim* s) {
     // kernels already queued may read the tables: drain the stream first
     PZ_TRY(bounded_sync(s->stream));
     pz::spec_release(s->spec);
-    s->spec = nullptr;  // the tables change: specialize again at the next launch
+    pz::spec_release(s->spec_sliced);
+    s->spec = s->spec_sliced = nullptr;  // the tables change: specialize again at the next launch
     s->lanes_built = false;  // and split over lanes again
     std::vector<unsigned char> blob;
     phyzb_sim::Layout& L0 = s->lay[0];
@@ -482,10 +483,24 @@ int launch_t(phyzb_sim* s, const void* ctrl, long long stride, int nsteps) {
     } else {
         cfg = L.launch;
     }
-    if (spec)
-        PZ_CUDA(pz::spec_launch<T>(s->spec, a, cfg, s->stream));
-    else
+    if (spec) {
+        if (chunk > 0 && !s->spec_sliced) {
+            // the slice-mode twin of the chosen kernel: same table and width
+            const phyzb_sim::Layout& SL = s->spec_lay;
+            std::string err;
+            if (pz::spec_sliced<T>(spec_layout(SL.info, SL.host, SL.launch.tm != 0, SL.launch.W),
+                                   rollout_args<T>(s, SL, nullptr, 0, 1), SL.launch.slice_W, &s->spec_sliced,
+                                   &err) != cudaSuccess) {
+                cudaGetLastError();
+                s->spec_sliced = nullptr;
+                return fail(PHYZB_ERR_CUDA, err);
+            }
+            pz::spec_retain(s->spec_sliced);
+        }
+        PZ_CUDA(pz::spec_launch<T>(chunk > 0 ? s->spec_sliced : s->spec, a, cfg, s->stream));
+    } else {
         PZ_CUDA(pz::launch_rollout<T>(a, cfg, s->stream));
+    }
     return PHYZB_OK;
 }
 
@@ -695,7 +710,8 @@ void destroy_sim(phyzb_sim* s) {
     if (s->stream) bounded_sync(s->stream);
     if (s->copy_stream) bounded_sync(s->copy_stream);
     pz::spec_release(s->spec);
-    s->spec = nullptr;
+    pz::spec_release(s->spec_sliced);
+    s->spec = s->spec_sliced = nullptr;
     free_ptr(s->lanes_blob);
     free_ptr(s->q);
     free_ptr(s->v);

@@ -136,6 +136,7 @@ struct phyzb_sim {
     // the model-specialized kernel (null: not compiled since the last repack),
     // its table layout and launch
     const pz::SpecKernel* spec = nullptr;
+    const pz::SpecKernel* spec_sliced = nullptr;  // its slice-mode twin (compiled on first use)
     Layout spec_lay;
     // PHYZB_SPECIALIZE_*: whether rollouts run the model-specialized kernel
     // (compiled at the first launch after each repack) or the generic variants

@@ -19,6 +19,8 @@ constexpr unsigned TMEM_COLS = 512;
 // a copy of the step's code): the Tensor-Memory variants (one block per SM,
 // whole warps: the layouts whose few resident worlds leave the widest
 // partial waves) without impulse contact (feature bit 16) or terrain (32).
+// A model-specialized kernel compiles a slice-mode twin of itself instead
+// (spec_sliced), at its own whole-warp width.
 template <int FEAT, bool TM>
 struct SliceVariant {
     static constexpr bool value = TM && (FEAT & (16 | 32)) == 0;
@@ -202,6 +204,13 @@ struct SpecChoice {
 template <class T>
 cudaError_t spec_candidates(const SpecLayout* lays, int nlay, const RolloutArgs<T>& a,
                             std::vector<SpecChoice>* out, std::string* err);
+// The slice-mode twin of the specialized kernel of layout L at width W
+// (compiled, or fetched from the caches, on a simulator's first slice-mode
+// launch; its launch shape is the tile kernel's slice_W / slice_grid /
+// slice_smem).
+template <class T>
+cudaError_t spec_sliced(const SpecLayout& L, const RolloutArgs<T>& a, int W, const SpecKernel** out,
+                        std::string* err);
 template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s);
 // A simulator takes (retain) and gives back (release) the compiled kernel it

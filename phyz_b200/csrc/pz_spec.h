@@ -64,18 +64,19 @@ std::string spec_kernel_name(int feat, bool tm) {
 
 // The translation unit for the model packed in `blob` (BodyT[nb] at 0,
 // BodyI[nb] at off_bi, PdT[npd] at off_pd, int[nv] at off_pdmap), launched
-// with blocks of W threads (W worlds per block).
+// with blocks of W threads (W worlds per block). `sliced`: the kernel's
+// slice-mode loop instead of its tile loop (each build holds one of them).
 template <class T>
 std::string spec_source(const unsigned char* blob, int off_bi, int off_pd, int off_pdmap, int nb, int nv, int npd,
-                        int W) {
+                        int W, bool sliced = false) {
     const char* tn = spec_type_name<T>();
     std::string o;
     o.reserve(4096 + (size_t)nb * 1536);
     o += "// model-specialized rollout kernel: " + std::to_string(nb) + " bodies, " + std::to_string(nv) +
          " DOFs, " + tn + ", " + std::to_string(W) + " worlds per block\n";
     o += "#define PZ_SPEC 1\n#define PZ_SPEC_NB " + std::to_string(nb) + "\n#define PZ_SPEC_NV " +
-         std::to_string(nv) + "\n#define PZ_SPEC_W " + std::to_string(W) +
-         "\n#include \"pz_model.cuh\"\n\nnamespace pz {\nnamespace spec {\n\n";
+         std::to_string(nv) + "\n#define PZ_SPEC_W " + std::to_string(W) + "\n#define PZ_SPEC_SLICED " +
+         (sliced ? "1" : "0") + "\n#include \"pz_model.cuh\"\n\nnamespace pz {\nnamespace spec {\n\n";
     // body integer table
     o += "__device__ __forceinline__ BodyI body(int i) {\n    switch (i) {\n";
     for (int i = 0; i < nb; i++) {

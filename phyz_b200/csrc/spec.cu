@@ -391,8 +391,9 @@ void spec_release(const SpecKernel* k) {
 namespace {
 
 template <class T>
-cudaError_t spec_compile(const SpecLayout& L, const RolloutArgs<T>& a, int W, SpecKernel** k, std::string* err) {
-    const std::string src = spec_source<T>(L.blob, L.off_bi, L.off_pd, L.off_pdmap, a.nb, a.nv, a.npd, W);
+cudaError_t spec_compile(const SpecLayout& L, const RolloutArgs<T>& a, int W, SpecKernel** k, std::string* err,
+                         bool sliced = false) {
+    const std::string src = spec_source<T>(L.blob, L.off_bi, L.off_pd, L.off_pdmap, a.nb, a.nv, a.npd, W, sliced);
     return get_kernel(src, spec_kernel_name<T>(L.feat, L.tm), k, err);
 }
 
@@ -419,8 +420,9 @@ cudaError_t spec_config(const DeviceLimits& dl, const SpecKernel* k, const SpecL
     auto occupancy = [&drv, fn](int* blocks, int w, size_t smem) {
         return drv.occupancy(blocks, fn, w, smem) == CUDA_SUCCESS ? cudaSuccess : cudaErrorUnknown;
     };
+    // the slice shape is that of the kernel's slice-mode twin (spec_sliced)
     const cudaError_t e = pick_launch(dl, dyn_cap, L.tm, (int)sizeof(T), L.scratch, L.bytes, a.nworld, L.tmem_cols,
-                                      (int)TMEM_COLS, occupancy, cfg, W, W);
+                                      (int)TMEM_COLS, occupancy, cfg, W, W, true);
     if (e != cudaSuccess)
         *err = "the specialized rollout kernel does not launch with " + std::to_string(W) + " worlds per block";
     return e;
@@ -502,6 +504,27 @@ cudaError_t spec_candidates(const SpecLayout* lays, int nlay, const RolloutArgs<
 }
 
 template <class T>
+cudaError_t spec_sliced(const SpecLayout& L, const RolloutArgs<T>& a, int W, const SpecKernel** out,
+                        std::string* err) {
+    int dev = 0, optin = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+        *err = cudaGetErrorString(e);
+        return e;
+    }
+    SpecKernel* k = nullptr;
+    if ((e = spec_compile<T>(L, a, W, &k, err, true)) != cudaSuccess) return e;
+    const CUresult r = driver().set_attr(k->fn, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, optin - k->static_smem);
+    if (r != CUDA_SUCCESS) {
+        *err = cu_error("cuFuncSetAttribute", r);
+        return cudaErrorUnknown;
+    }
+    *out = k;
+    return cudaSuccess;
+}
+
+template <class T>
 cudaError_t spec_launch(const SpecKernel* k, const RolloutArgs<T>& a, const LaunchCfg& cfg, cudaStream_t s) {
     if (a.nsteps <= 0 || a.nworld <= 0) return cudaSuccess;
     RolloutArgs<T> args = a;
@@ -515,6 +538,10 @@ template cudaError_t spec_candidates<float>(const SpecLayout*, int, const Rollou
                                             std::vector<SpecChoice>*, std::string*);
 template cudaError_t spec_candidates<double>(const SpecLayout*, int, const RolloutArgs<double>&,
                                              std::vector<SpecChoice>*, std::string*);
+template cudaError_t spec_sliced<float>(const SpecLayout&, const RolloutArgs<float>&, int, const SpecKernel**,
+                                        std::string*);
+template cudaError_t spec_sliced<double>(const SpecLayout&, const RolloutArgs<double>&, int, const SpecKernel**,
+                                         std::string*);
 template cudaError_t spec_launch<float>(const SpecKernel*, const RolloutArgs<float>&, const LaunchCfg&, cudaStream_t);
 template cudaError_t spec_launch<double>(const SpecKernel*, const RolloutArgs<double>&, const LaunchCfg&,
                                          cudaStream_t);

@@ -495,10 +495,13 @@ __global__ void __launch_bounds__(PZ_MAX_THREADS, 1) rollout_kernel(const __grid
         S.tbase = tmem_slot + ((unsigned)(32 * (warp & 3)) << 16) + (unsigned)(warp >> 2) * cols;
     }
     const long long N = P.nworld;
-#if PZ_STEP_SYNC || defined(PZ_SPEC)
-    // (a model-specialized build runs tile mode only: a second copy of its
-    // unrolled step would double its compile time)
+#if PZ_STEP_SYNC
     constexpr bool sliced = false;
+#elif defined(PZ_SPEC)
+    // a model-specialized build holds one of the two loops (a second copy of
+    // its unrolled step would double the compile): the tile kernel and its
+    // slice-mode twin are compiled apart
+    constexpr bool sliced = PZ_SPEC_SLICED != 0;
 #else
     constexpr bool can_slice = SliceVariant<FEAT, TM>::value;
     const bool sliced = can_slice && P.chunk > 0;

@@ -7,11 +7,11 @@
 #include "pz_pack.h"
 #include "pz_spec.h"
 
-// contact: 0 none, 1 penalty, 2 impulse. Writes the source (NUL-terminated)
-// and the kernel's name expression; returns the source length, or -needed
-// when a buffer is too small.
-extern "C" int spec_source_for(const phyzb_model* m, int nv, int contact, int f64, int W, char* src, int src_cap,
-                               char* name, int name_cap) {
+// contact: 0 none, 1 penalty, 2 impulse; sliced: the slice-mode twin. Writes
+// the source (NUL-terminated) and the kernel's name expression; returns the
+// source length, or -needed when a buffer is too small.
+extern "C" int spec_source_for(const phyzb_model* m, int nv, int contact, int f64, int W, int sliced, char* src,
+                               int src_cap, char* name, int name_cap) {
     pz::PackCfg cfg;
     cfg.contact = contact != 0;
     cfg.impulse = contact == 2;
@@ -21,9 +21,9 @@ extern "C" int spec_source_for(const phyzb_model* m, int nv, int contact, int f6
     const pz::PackInfo info =
         f64 ? pz::pack_model<double>(m, nv, cfg, blob, 0) : pz::pack_model<float>(m, nv, cfg, blob, 0);
     const std::string s = f64 ? pz::spec_source<double>(blob.data(), info.off_bi, info.off_pd, info.off_pdmap,
-                                                        m->nbodies, nv, 0, W)
+                                                        m->nbodies, nv, 0, W, sliced != 0)
                               : pz::spec_source<float>(blob.data(), info.off_bi, info.off_pd, info.off_pdmap,
-                                                       m->nbodies, nv, 0, W);
+                                                       m->nbodies, nv, 0, W, sliced != 0);
     const std::string k = f64 ? pz::spec_kernel_name<double>(info.feat, false)
                               : pz::spec_kernel_name<float>(info.feat, false);
     if ((int)s.size() + 1 > src_cap || (int)k.size() + 1 > name_cap) return -(int)(s.size() + k.size() + 2);

@@ -11,11 +11,12 @@ phyzb_slice_plan).
   launch of two or more steps): a run starts from q, v (and the impulse
   buffer) where the one before ended and recomputes its first forward sweep,
   so the two modes agree to rounding (f64 <= 1e-12 relative), and the f64
-  results match the oracle <= 1e-9, on the variants that have slice mode
-  (Tensor-Memory records, no impulse contact or terrain): chains and free
-  joints with penalty contact, f32 and f64. The model-specialized kernel,
-  the shared-memory layout and the impulse / terrain variants run tile mode
-  only.
+  results match the oracle <= 1e-9, on the generic variants that have
+  slice mode (Tensor-Memory records, no impulse contact or terrain): chains
+  and free joints with penalty contact, f32 and f64; and on the
+  model-specialized kernel's slice-mode twin (compiled on the first sliced
+  launch). The generic shared-memory layout and impulse / terrain variants
+  run tile mode only.
 * Many rounds of jobs: C2 f64 at 65536 worlds, where a warp takes several
   tiles' runs and waits for runs other SMs ran.
 * The bounded wait: PHYZB_SLICES_STALL=1 starts the queue past every tile's
@@ -110,6 +111,8 @@ CASES = [
     ("c3_quadruped", "f64", "1", False, False),
     ("c4_humanoid", "f64", "1", False, False),
     ("c4_humanoid", "f32", "1", False, False),
+    ("c3_quadruped", "f64", "1", True, False),
+    ("c4_humanoid", "f32", "1", True, False),
 ]
 
 
@@ -136,11 +139,11 @@ def test_slices_match_tiles(oracle, monkeypatch, name, precision, layout, spec, 
             assert rel_err(a, b) <= 1e-9, f"{nm}: slices vs oracle {rel_err(a, b):.3e}"
 
 
-@pytest.mark.parametrize("kind", ["specialized", "smem", "impulse"])
+@pytest.mark.parametrize("kind", ["smem", "impulse"])
 def test_tile_only_kernels(monkeypatch, kind):
-    """The model-specialized kernel, the shared-memory layout and the
-    impulse-contact variants are compiled for tile mode only: they report it
-    and step correctly with PHYZB_SLICES=1 set."""
+    """The generic shared-memory layout and the impulse-contact variants
+    are compiled for tile mode only: they report it and step correctly with
+    PHYZB_SLICES=1 set."""
     monkeypatch.setenv("PHYZB_SLICES", "1")
     if kind == "smem":
         monkeypatch.setenv("PHYZB_TMEM", "0")
@@ -150,10 +153,9 @@ def test_tile_only_kernels(monkeypatch, kind):
         sim.enable_contact_impulse(0.0, 1.0)
     else:
         sim.enable_ground_contact(*configs.CONFIGS["c3_quadruped"].contact)
-    sim.specialize = kind == "specialized"
+    sim.specialize = False
     sim.step_many(2)
     sim.sync()
-    assert sim.specialized == (kind == "specialized")
     assert sim.slice_plan(12)["steps_per_run"] == 0
     sim.close()
 

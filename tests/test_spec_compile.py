@@ -34,23 +34,24 @@ def helper(tmp_path_factory):
     subprocess.run(["g++", "-std=c++17", "-O1", "-shared", "-fPIC", "-I", str(CSRC),
                     str(ROOT / "tests" / "cpp" / "spec_source.cpp"), "-o", str(so)], check=True)
     lib = C.CDLL(str(so))
-    lib.spec_source_for.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int,
+    lib.spec_source_for.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_char_p, C.c_int,
                                     C.c_char_p, C.c_int]
     return lib
 
 
-@pytest.mark.parametrize("name,contact,f64,W", [
-    ("c1_double_pendulum", 0, 1, 32),
-    ("c3_quadruped", 1, 0, 128),
-    ("c3_quadruped", 2, 0, 224),
+@pytest.mark.parametrize("name,contact,f64,W,sliced", [
+    ("c1_double_pendulum", 0, 1, 32, 0),
+    ("c3_quadruped", 1, 0, 128, 0),
+    ("c3_quadruped", 1, 0, 128, 1),  # the slice-mode twin
+    ("c3_quadruped", 2, 0, 224, 0),
 ])
-def test_specialized_source_compiles(helper, name, contact, f64, W):
+def test_specialized_source_compiles(helper, name, contact, f64, W, sliced):
     nv_lib = nvrtc()
     m = configs.CONFIGS[name].builder()
     cm, keep = m.to_c()
     src = C.create_string_buffer(1 << 22)
     kname = C.create_string_buffer(256)
-    n = helper.spec_source_for(C.addressof(cm), m.nv, contact, f64, W, src, len(src), kname, len(kname))
+    n = helper.spec_source_for(C.addressof(cm), m.nv, contact, f64, W, sliced, src, len(src), kname, len(kname))
     assert n > 0
     prog = C.c_void_p()
     assert nv_lib.nvrtcCreateProgram(C.byref(prog), src.value, b"spec.cu", 0, None, None) == 0
