@@ -636,6 +636,13 @@ impl Simulator {
     pub fn set_world_lanes(&mut self, lanes: i32) -> Result<(), Error> {
         check(unsafe { phyzb_set_world_lanes(self.raw, lanes) })
     }
+    /// How a rollout launch of `nsteps` steps runs: (steps per run, worlds
+    /// per block, blocks); steps per run 0 is tile mode, else slice mode.
+    pub fn slice_plan(&self, nsteps: i32) -> Result<(i32, i32, i32), Error> {
+        let (mut run, mut wpb, mut blocks) = (0i32, 0i32, 0i32);
+        check(unsafe { phyzb_slice_plan(self.raw, nsteps, &mut run, &mut wpb, &mut blocks) })?;
+        Ok((run, wpb, blocks))
+    }
 }
 
 impl Drop for Simulator {
